@@ -1,0 +1,268 @@
+// Attention-residual depth mixing: for each token, softmax over S depth sources of
+//   logit_s = q . (RMSNorm(src_s) * w)
+// and an fp32 weighted sum of the raw sources. One warp per token; each source tensor is
+// read through its own pointer (no stacked copy), once for the logits and once for the sum.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace kimi {
+namespace {
+
+constexpr int kMaxSources = 16;
+
+template <typename T>
+struct SrcPtrs {
+  const T* p[kMaxSources];
+};
+template <typename T>
+struct DstPtrs {
+  T* p[kMaxSources];
+};
+
+int grid_tokens(int64_t tokens, int warps_per_block) {
+  int64_t g = (tokens + warps_per_block - 1) / warps_per_block;
+  if (g > 148 * 8) g = 148 * 8;
+  return (int)(g < 1 ? 1 : g);
+}
+
+template <typename T, int MAXV>
+__global__ void attnres_fwd_kernel(SrcPtrs<T> src, int S, const float* __restrict__ q, const float* __restrict__ w,
+                                   T* __restrict__ out, float* __restrict__ probs, float* __restrict__ rstd,
+                                   int64_t tokens, int dim, float eps) {
+  constexpr int VN = Vec<T>::N;
+  const int lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
+  const int nvec = dim / VN;
+  // Preload q*w for this lane's slice.
+  float qw[MAXV][VN];
+#pragma unroll
+  for (int v = 0; v < MAXV; ++v) {
+    const int vi = lane + v * 32;
+#pragma unroll
+    for (int j = 0; j < VN; ++j) qw[v][j] = vi < nvec ? q[vi * VN + j] * w[vi * VN + j] : 0.f;
+  }
+  for (int64_t tok = (int64_t)blockIdx.x * wpb + (threadIdx.x >> 5); tok < tokens; tok += (int64_t)gridDim.x * wpb) {
+    float logit[kMaxSources], rs[kMaxSources];
+    float mx = -INFINITY;
+    for (int s = 0; s < S; ++s) {
+      const T* row = src.p[s] + tok * dim;
+      float ss = 0.f, a = 0.f;
+#pragma unroll
+      for (int v = 0; v < MAXV; ++v) {
+        const int vi = lane + v * 32;
+        if (vi < nvec) {
+          Vec<T> x;
+          x.load(row + vi * VN);
+#pragma unroll
+          for (int j = 0; j < VN; ++j) {
+            const float xv = x.f(j);
+            ss += xv * xv;
+            a += qw[v][j] * xv;
+          }
+        }
+      }
+      ss = warp_sum(ss);
+      a = warp_sum(a);
+      const float r = rsqrtf(ss / dim + eps);
+      rs[s] = r;
+      logit[s] = r * a;
+      mx = fmaxf(mx, logit[s]);
+    }
+    float denom = 0.f;
+    for (int s = 0; s < S; ++s) {
+      logit[s] = expf(logit[s] - mx);
+      denom += logit[s];
+    }
+    const float inv = 1.f / denom;
+    for (int s = 0; s < S; ++s) logit[s] *= inv;
+    if (lane < S) {
+      // lane-indexed writes of the per-source statistics (S <= 16 < 32)
+      float pv = 0.f, rv = 0.f;
+      for (int s = 0; s < S; ++s)
+        if (s == lane) { pv = logit[s]; rv = rs[s]; }
+      probs[tok * S + lane] = pv;
+      rstd[tok * S + lane] = rv;
+    }
+#pragma unroll
+    for (int v = 0; v < MAXV; ++v) {
+      const int vi = lane + v * 32;
+      if (vi < nvec) {
+        float acc[VN];
+#pragma unroll
+        for (int j = 0; j < VN; ++j) acc[j] = 0.f;
+        for (int s = 0; s < S; ++s) {
+          Vec<T> x;
+          x.load(src.p[s] + tok * dim + vi * VN);
+#pragma unroll
+          for (int j = 0; j < VN; ++j) acc[j] += logit[s] * x.f(j);
+        }
+        Vec<T> o;
+#pragma unroll
+        for (int j = 0; j < VN; ++j) o.set(j, acc[j]);
+        o.store(out + tok * dim + vi * VN);
+      }
+    }
+  }
+}
+
+template <typename T, int MAXV>
+__global__ void attnres_bwd_kernel(SrcPtrs<T> src, int S, const float* __restrict__ q, const float* __restrict__ w,
+                                   const T* __restrict__ dout, const float* __restrict__ probs,
+                                   const float* __restrict__ rstd, DstPtrs<T> dsrc, float* __restrict__ dq,
+                                   float* __restrict__ dw, int64_t tokens, int dim) {
+  constexpr int VN = Vec<T>::N;
+  const int lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
+  const int nvec = dim / VN;
+  // dq_d = w_d * C_d and dw_d = q_d * C_d with C_d = sum dlogit * r * x_d: one accumulator.
+  float qw[MAXV][VN], acc[MAXV][VN];
+#pragma unroll
+  for (int v = 0; v < MAXV; ++v) {
+    const int vi = lane + v * 32;
+#pragma unroll
+    for (int j = 0; j < VN; ++j) {
+      qw[v][j] = vi < nvec ? q[vi * VN + j] * w[vi * VN + j] : 0.f;
+      acc[v][j] = 0.f;
+    }
+  }
+  const float inv_dim = 1.f / dim;
+  for (int64_t tok = (int64_t)blockIdx.x * wpb + (threadIdx.x >> 5); tok < tokens; tok += (int64_t)gridDim.x * wpb) {
+    float p[kMaxSources], r[kMaxSources], dp[kMaxSources], a[kMaxSources];
+    float pdp = 0.f;
+    for (int s = 0; s < S; ++s) {
+      p[s] = probs[tok * S + s];
+      r[s] = rstd[tok * S + s];
+      const T* row = src.p[s] + tok * dim;
+      float d0 = 0.f, a0 = 0.f;
+#pragma unroll
+      for (int v = 0; v < MAXV; ++v) {
+        const int vi = lane + v * 32;
+        if (vi < nvec) {
+          Vec<T> x, g;
+          x.load(row + vi * VN);
+          g.load(dout + tok * dim + vi * VN);
+#pragma unroll
+          for (int j = 0; j < VN; ++j) {
+            d0 += g.f(j) * x.f(j);
+            a0 += qw[v][j] * x.f(j);
+          }
+        }
+      }
+      dp[s] = warp_sum(d0);
+      a[s] = warp_sum(a0);
+      pdp += p[s] * dp[s];
+    }
+    for (int s = 0; s < S; ++s) {
+      const float dl = p[s] * (dp[s] - pdp);  // d loss / d logit_s
+      const float r3 = r[s] * r[s] * r[s] * a[s] * inv_dim;
+      const T* row = src.p[s] + tok * dim;
+      T* drow = dsrc.p[s] + tok * dim;
+#pragma unroll
+      for (int v = 0; v < MAXV; ++v) {
+        const int vi = lane + v * 32;
+        if (vi < nvec) {
+          Vec<T> x, g, o;
+          x.load(row + vi * VN);
+          g.load(dout + tok * dim + vi * VN);
+#pragma unroll
+          for (int j = 0; j < VN; ++j) {
+            const float xv = x.f(j);
+            o.set(j, p[s] * g.f(j) + dl * (r[s] * qw[v][j] - r3 * xv));
+            acc[v][j] += dl * r[s] * xv;
+          }
+          o.store(drow + vi * VN);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int v = 0; v < MAXV; ++v) {
+    const int vi = lane + v * 32;
+    if (vi < nvec)
+#pragma unroll
+      for (int j = 0; j < VN; ++j) {
+        atomicAdd(&dq[vi * VN + j], w[vi * VN + j] * acc[v][j]);
+        atomicAdd(&dw[vi * VN + j], q[vi * VN + j] * acc[v][j]);
+      }
+  }
+}
+
+template <typename T>
+int maxv_for(int dim) {
+  const int nvec = dim / Vec<T>::N;
+  const int per_lane = (nvec + 31) / 32;
+  if (per_lane <= 1) return 1;
+  if (per_lane <= 2) return 2;
+  if (per_lane <= 4) return 4;
+  if (per_lane <= 8) return 8;
+  return -1;
+}
+
+}  // namespace
+
+#define KIMI_MAXV_SWITCH(mv, MV, ...)            \
+  switch (mv) {                                  \
+    case 1: { constexpr int MV = 1; __VA_ARGS__; break; } \
+    case 2: { constexpr int MV = 2; __VA_ARGS__; break; } \
+    case 4: { constexpr int MV = 4; __VA_ARGS__; break; } \
+    case 8: { constexpr int MV = 8; __VA_ARGS__; break; } \
+    default: return cudaErrorInvalidValue;       \
+  }
+
+template <typename T>
+static cudaError_t fwd_impl(const void* const* sources, int S, const float* q, const float* w, void* out, float* probs,
+                            float* rstd, int64_t tokens, int dim, float eps, cudaStream_t s) {
+  if (S < 1 || S > kMaxSources || dim % Vec<T>::N) return cudaErrorInvalidValue;
+  SrcPtrs<T> ptrs{};
+  for (int i = 0; i < S; ++i) ptrs.p[i] = (const T*)sources[i];
+  const int threads = 256;
+  const int mv = maxv_for<T>(dim);
+  KIMI_MAXV_SWITCH(mv, MV, {
+    attnres_fwd_kernel<T, MV><<<grid_tokens(tokens, threads / 32), threads, 0, s>>>(ptrs, S, q, w, (T*)out, probs,
+                                                                                    rstd, tokens, dim, eps);
+  });
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t bwd_impl(const void* const* sources, int S, const float* q, const float* w, const void* dout,
+                            const float* probs, const float* rstd, void* const* dsources, float* dq, float* dw,
+                            int64_t tokens, int dim, cudaStream_t s) {
+  if (S < 1 || S > kMaxSources || dim % Vec<T>::N) return cudaErrorInvalidValue;
+  SrcPtrs<T> ptrs{};
+  DstPtrs<T> dptrs{};
+  for (int i = 0; i < S; ++i) {
+    ptrs.p[i] = (const T*)sources[i];
+    dptrs.p[i] = (T*)dsources[i];
+  }
+  const int threads = 256;
+  const int mv = maxv_for<T>(dim);
+  KIMI_MAXV_SWITCH(mv, MV, {
+    attnres_bwd_kernel<T, MV><<<grid_tokens(tokens, threads / 32), threads, 0, s>>>(
+        ptrs, S, q, w, (const T*)dout, probs, rstd, dptrs, dq, dw, tokens, dim);
+  });
+  return cudaGetLastError();
+}
+
+cudaError_t attnres_mix_fwd(int dtype, const void* const* sources, int S, const float* q, const float* w, void* out,
+                            float* probs, float* rstd, int64_t tokens, int dim, float eps, cudaStream_t s) {
+  switch (dtype) {
+    case 0: return fwd_impl<float>(sources, S, q, w, out, probs, rstd, tokens, dim, eps, s);
+    case 1: return fwd_impl<__nv_bfloat16>(sources, S, q, w, out, probs, rstd, tokens, dim, eps, s);
+    case 2: return fwd_impl<__half>(sources, S, q, w, out, probs, rstd, tokens, dim, eps, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t attnres_mix_bwd(int dtype, const void* const* sources, int S, const float* q, const float* w,
+                            const void* dout, const float* probs, const float* rstd, void* const* dsources, float* dq,
+                            float* dw, int64_t tokens, int dim, cudaStream_t s) {
+  switch (dtype) {
+    case 0: return bwd_impl<float>(sources, S, q, w, dout, probs, rstd, dsources, dq, dw, tokens, dim, s);
+    case 1: return bwd_impl<__nv_bfloat16>(sources, S, q, w, dout, probs, rstd, dsources, dq, dw, tokens, dim, s);
+    case 2: return bwd_impl<__half>(sources, S, q, w, dout, probs, rstd, dsources, dq, dw, tokens, dim, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace kimi

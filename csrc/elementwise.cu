@@ -1,0 +1,485 @@
+// Memory-bound fused kernels: RMSNorm (plain and head-wise), SiTU-GLU, sigmoid gate,
+// KDA lower-bounded decay, and the KDA short causal conv + SiLU (+ per-head L2 norm).
+//
+// Rows are processed by groups of `tpr` threads (a power of two <= 32) so that narrow
+// rows (head_dim 64) still keep a warp busy; 16-byte vector loads are used when the row
+// width is a multiple of the vector width. All math is fp32; storage rounding follows
+// the PyTorch reference (normalised value rounded to the activation dtype before the
+// affine multiply).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace kimi {
+namespace {
+
+int pick_tpr(int nvec) {
+  int t = 1;
+  while (t < nvec && t < 32) t <<= 1;
+  return t;
+}
+
+int grid_for(int64_t work_items, int per_block) {
+  int64_t g = (work_items + per_block - 1) / per_block;
+  const int64_t cap = 148 * 16;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return (int)g;
+}
+
+// ------------------------------------------------------------------ RMSNorm
+template <typename T>
+__global__ void rms_fwd_kernel(const T* __restrict__ x, const float* __restrict__ w, T* __restrict__ y,
+                               float* __restrict__ rstd, int64_t rows, int dim, int period, float eps, int tpr) {
+  constexpr int VN = Vec<T>::N;
+  const int nvec = dim / VN;
+  const int gid = threadIdx.x / tpr, lane = threadIdx.x % tpr;
+  const int rpb = blockDim.x / tpr;
+  const int warp_first_gid = (threadIdx.x / 32) * (32 / tpr);
+  for (int64_t base = (int64_t)blockIdx.x * rpb; base + warp_first_gid < rows; base += (int64_t)gridDim.x * rpb) {
+    const int64_t row = base + gid;
+    const bool ok = row < rows;
+    const T* xr = x + row * dim;
+    float ss = 0.f;
+    if (ok)
+      for (int i = lane; i < nvec; i += tpr) {
+        Vec<T> a;
+        a.load(xr + i * VN);
+#pragma unroll
+        for (int j = 0; j < VN; ++j) ss += a.f(j) * a.f(j);
+      }
+    ss = group_sum(ss, tpr);
+    const float r = rsqrtf(ss / dim + eps);
+    if (ok) {
+      if (lane == 0 && rstd) rstd[row] = r;
+      const float* wr = w ? w + (int64_t)(row % period) * dim : nullptr;
+      T* yr = y + row * dim;
+      for (int i = lane; i < nvec; i += tpr) {
+        Vec<T> a, o;
+        a.load(xr + i * VN);
+#pragma unroll
+        for (int j = 0; j < VN; ++j) {
+          float n = round_through<T>(a.f(j) * r);
+          if (wr) n = n * round_through<T>(wr[i * VN + j]);
+          o.set(j, n);
+        }
+        o.store(yr + i * VN);
+      }
+    }
+  }
+}
+
+// dx = r * (dn - xhat * mean(dn * xhat)),  dn = dy * w ; dw[p, d] += dy * n
+template <typename T>
+__global__ void rms_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x, const float* __restrict__ w,
+                               const float* __restrict__ rstd, T* __restrict__ dx, float* __restrict__ dw,
+                               int64_t rows, int dim, int period, int tpr) {
+  constexpr int VN = Vec<T>::N;
+  extern __shared__ float sdw[];  // period * dim accumulators
+  const int nvec = dim / VN;
+  const int gid = threadIdx.x / tpr, lane = threadIdx.x % tpr;
+  const int rpb = blockDim.x / tpr;
+  const int warp_first_gid = (threadIdx.x / 32) * (32 / tpr);
+  if (dw)
+    for (int i = threadIdx.x; i < period * dim; i += blockDim.x) sdw[i] = 0.f;
+  __syncthreads();
+  for (int64_t base = (int64_t)blockIdx.x * rpb; base + warp_first_gid < rows; base += (int64_t)gridDim.x * rpb) {
+    const int64_t row = base + gid;
+    const bool ok = row < rows;
+    const T* xr = x + row * dim;
+    const T* dyr = dy + row * dim;
+    const int p = ok ? (int)(row % period) : 0;
+    const float* wr = w ? w + (int64_t)p * dim : nullptr;
+    const float r = ok ? rstd[row] : 0.f;
+    float dot = 0.f;
+    if (ok)
+      for (int i = lane; i < nvec; i += tpr) {
+        Vec<T> a, g;
+        a.load(xr + i * VN);
+        g.load(dyr + i * VN);
+#pragma unroll
+        for (int j = 0; j < VN; ++j) {
+          const float wv = wr ? round_through<T>(wr[i * VN + j]) : 1.f;
+          dot += g.f(j) * wv * a.f(j) * r;
+        }
+      }
+    dot = group_sum(dot, tpr) / dim;
+    if (ok) {
+      T* dxr = dx + row * dim;
+      for (int i = lane; i < nvec; i += tpr) {
+        Vec<T> a, g, o;
+        a.load(xr + i * VN);
+        g.load(dyr + i * VN);
+#pragma unroll
+        for (int j = 0; j < VN; ++j) {
+          const float wv = wr ? round_through<T>(wr[i * VN + j]) : 1.f;
+          const float xh = a.f(j) * r;
+          o.set(j, r * (g.f(j) * wv - xh * dot));
+          if (dw) atomicAdd(&sdw[p * dim + i * VN + j], g.f(j) * round_through<T>(xh));
+        }
+        o.store(dxr + i * VN);
+      }
+    }
+  }
+  __syncthreads();
+  if (dw)
+    for (int i = threadIdx.x; i < period * dim; i += blockDim.x) atomicAdd(&dw[i], sdw[i]);
+}
+
+// ------------------------------------------------------------------ SiTU-GLU and sigmoid gate
+template <typename T>
+__global__ void situ_fwd_kernel(const T* __restrict__ g, const T* __restrict__ u, T* __restrict__ y, int64_t n,
+                                float bg, float bu) {
+  constexpr int VN = Vec<T>::N;
+  const int64_t nv = n / VN;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+    Vec<T> a, b, o;
+    a.load(g + i * VN);
+    b.load(u + i * VN);
+#pragma unroll
+    for (int j = 0; j < VN; ++j) {
+      const float gv = a.f(j), uv = b.f(j);
+      o.set(j, bg * tanhf(gv / bg) * sigmoidf_(gv) * bu * tanhf(uv / bu));
+    }
+    o.store(y + i * VN);
+  }
+  for (int64_t i = nv * VN + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float gv = to_f<T>(g[i]), uv = to_f<T>(u[i]);
+    y[i] = from_f<T>(bg * tanhf(gv / bg) * sigmoidf_(gv) * bu * tanhf(uv / bu));
+  }
+}
+
+template <typename T>
+KIMI_D void situ_grad(float gv, float uv, float d, float bg, float bu, float& dg, float& du) {
+  const float tg = tanhf(gv / bg), tu = tanhf(uv / bu), sg = sigmoidf_(gv);
+  const float cg = bg * tg, cu = bu * tu;
+  dg = d * cu * ((1.f - tg * tg) * sg + cg * sg * (1.f - sg));
+  du = d * cg * sg * (1.f - tu * tu);
+}
+
+template <typename T>
+__global__ void situ_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ g, const T* __restrict__ u,
+                                T* __restrict__ dg, T* __restrict__ du, int64_t n, float bg, float bu) {
+  constexpr int VN = Vec<T>::N;
+  const int64_t nv = n / VN;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+    Vec<T> a, b, d, og, ou;
+    a.load(g + i * VN);
+    b.load(u + i * VN);
+    d.load(dy + i * VN);
+#pragma unroll
+    for (int j = 0; j < VN; ++j) {
+      float x0, x1;
+      situ_grad<T>(a.f(j), b.f(j), d.f(j), bg, bu, x0, x1);
+      og.set(j, x0);
+      ou.set(j, x1);
+    }
+    og.store(dg + i * VN);
+    ou.store(du + i * VN);
+  }
+  for (int64_t i = nv * VN + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float x0, x1;
+    situ_grad<T>(to_f<T>(g[i]), to_f<T>(u[i]), to_f<T>(dy[i]), bg, bu, x0, x1);
+    dg[i] = from_f<T>(x0);
+    du[i] = from_f<T>(x1);
+  }
+}
+
+template <typename T>
+__global__ void sigmul_fwd_kernel(const T* __restrict__ z, const T* __restrict__ x, T* __restrict__ y, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = from_f<T>(round_through<T>(sigmoidf_(to_f<T>(z[i]))) * to_f<T>(x[i]));
+}
+
+template <typename T>
+__global__ void sigmul_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ z, const T* __restrict__ x,
+                                  T* __restrict__ dz, T* __restrict__ dx, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float s = sigmoidf_(to_f<T>(z[i])), d = to_f<T>(dy[i]);
+    dz[i] = from_f<T>(d * to_f<T>(x[i]) * s * (1.f - s));
+    dx[i] = from_f<T>(d * s);
+  }
+}
+
+// ------------------------------------------------------------------ KDA decay gate
+// g = g_min * clamp(sigmoid(exp(A_log[h]) * z), eps, 1-eps)  (fp32 output)
+template <typename T>
+__global__ void decay_fwd_kernel(const T* __restrict__ z, const float* __restrict__ a_log, float* __restrict__ g,
+                                 int64_t n, int heads, int kdim, float g_min, float ceps) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int h = (int)((i / kdim) % heads);
+    const float p = sigmoidf_(expf(a_log[h]) * to_f<T>(z[i]));
+    g[i] = g_min * fminf(fmaxf(p, ceps), 1.f - ceps);
+  }
+}
+
+template <typename T>
+__global__ void decay_bwd_kernel(const float* __restrict__ dg, const T* __restrict__ z,
+                                 const float* __restrict__ a_log, T* __restrict__ dz, float* __restrict__ da_log,
+                                 int64_t n, int heads, int kdim, float g_min, float ceps) {
+  extern __shared__ float sda[];
+  for (int i = threadIdx.x; i < heads; i += blockDim.x) sda[i] = 0.f;
+  __syncthreads();
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int h = (int)((i / kdim) % heads);
+    const float sc = expf(a_log[h]), zv = to_f<T>(z[i]);
+    const float p = sigmoidf_(sc * zv);
+    const bool inside = p > ceps && p < 1.f - ceps;
+    const float dpre = inside ? dg[i] * g_min * p * (1.f - p) : 0.f;  // d/d(sc*z)
+    dz[i] = from_f<T>(dpre * sc);
+    atomicAdd(&sda[h], dpre * zv * sc);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < heads; i += blockDim.x) atomicAdd(&da_log[i], sda[i]);
+}
+
+// ------------------------------------------------------------------ KDA short conv + SiLU (+ L2 per head)
+// One group of `tpr` threads per (b, t, head); each thread covers head_dim / tpr channels.
+// The conv starts from a zero history (training / full-sequence mode).
+template <typename T>
+KIMI_D float conv_at(const T* __restrict__ x, const float* __restrict__ w, int64_t bt_row, int t, int c, int channels,
+                     int ksize) {
+  float acc = 0.f;
+  for (int j = 0; j < ksize; ++j) {
+    if (t - j < 0) break;
+    acc += w[c * ksize + j] * to_f<T>(x[(bt_row - j) * channels + c]);
+  }
+  return acc;
+}
+
+template <typename T>
+__global__ void conv_fwd_kernel(const T* __restrict__ x, const float* __restrict__ w, T* __restrict__ y, int batch,
+                                int tokens, int channels, int ksize, int head_dim, float eps, bool normalize,
+                                int tpr) {
+  const int heads = channels / head_dim;
+  const int64_t groups = (int64_t)batch * tokens * heads;
+  const int gid = threadIdx.x / tpr, lane = threadIdx.x % tpr;
+  const int gpb = blockDim.x / tpr;
+  const int warp_first_gid = (threadIdx.x / 32) * (32 / tpr);
+  for (int64_t base = (int64_t)blockIdx.x * gpb; base + warp_first_gid < groups; base += (int64_t)gridDim.x * gpb) {
+    const int64_t grp = base + gid;
+    const bool ok = grp < groups;
+    const int64_t bt = ok ? grp / heads : 0;
+    const int h = ok ? (int)(grp % heads) : 0;
+    const int t = (int)(bt % tokens);
+    float ss = 0.f;
+    float vals[8];
+    int cnt = 0;
+    for (int cc = lane; cc < head_dim && cnt < 8; cc += tpr, ++cnt) {
+      const int c = h * head_dim + cc;
+      const float pre = ok ? conv_at<T>(x, w, bt, t, c, channels, ksize) : 0.f;
+      const float s = siluf_(pre);
+      vals[cnt] = s;
+      ss += s * s;
+    }
+    float inv = 1.f;
+    if (normalize) {
+      ss = group_sum(ss, tpr);
+      inv = 1.f / fmaxf(sqrtf(ss), eps);
+    }
+    if (ok) {
+      cnt = 0;
+      for (int cc = lane; cc < head_dim && cnt < 8; cc += tpr, ++cnt)
+        y[bt * channels + h * head_dim + cc] = from_f<T>(vals[cnt] * inv);
+    }
+  }
+}
+
+// Pass 1: dpre[b,t,c] = d(output)/d(pre-activation), recomputing the conv and norm stats.
+template <typename T>
+__global__ void conv_bwd_pre_kernel(const T* __restrict__ dy, const T* __restrict__ x, const float* __restrict__ w,
+                                    float* __restrict__ dpre, int batch, int tokens, int channels, int ksize,
+                                    int head_dim, float eps, bool normalize, int tpr) {
+  const int heads = channels / head_dim;
+  const int64_t groups = (int64_t)batch * tokens * heads;
+  const int gid = threadIdx.x / tpr, lane = threadIdx.x % tpr;
+  const int gpb = blockDim.x / tpr;
+  const int warp_first_gid = (threadIdx.x / 32) * (32 / tpr);
+  for (int64_t base = (int64_t)blockIdx.x * gpb; base + warp_first_gid < groups; base += (int64_t)gridDim.x * gpb) {
+    const int64_t grp = base + gid;
+    const bool ok = grp < groups;
+    const int64_t bt = ok ? grp / heads : 0;
+    const int h = ok ? (int)(grp % heads) : 0;
+    const int t = (int)(bt % tokens);
+    float pre[8], s[8], d[8];
+    float ss = 0.f, dot = 0.f;
+    int cnt = 0;
+    for (int cc = lane; cc < head_dim && cnt < 8; cc += tpr, ++cnt) {
+      const int c = h * head_dim + cc;
+      pre[cnt] = ok ? conv_at<T>(x, w, bt, t, c, channels, ksize) : 0.f;
+      s[cnt] = siluf_(pre[cnt]);
+      d[cnt] = ok ? to_f<T>(dy[bt * channels + c]) : 0.f;
+      ss += s[cnt] * s[cnt];
+      dot += s[cnt] * d[cnt];
+    }
+    float inv = 1.f, coef = 0.f;
+    if (normalize) {
+      ss = group_sum(ss, tpr);
+      dot = group_sum(dot, tpr);
+      const float nrm = sqrtf(ss);
+      if (nrm > eps) {
+        inv = 1.f / nrm;
+        coef = dot * inv * inv * inv;  // (s . d) / ||s||^3
+      } else {
+        inv = 1.f / eps;
+      }
+    }
+    if (ok) {
+      cnt = 0;
+      for (int cc = lane; cc < head_dim && cnt < 8; cc += tpr, ++cnt) {
+        const float ds = d[cnt] * inv - s[cnt] * coef;
+        const float sg = sigmoidf_(pre[cnt]);
+        dpre[bt * channels + h * head_dim + cc] = ds * sg * (1.f + pre[cnt] * (1.f - sg));
+      }
+    }
+  }
+}
+
+// Pass 2: dx[t,c] = sum_j w[c,j] dpre[t+j,c];  dw[c,j] = sum_{b,t} dpre[t,c] x[t-j,c]
+template <typename T>
+__global__ void conv_bwd_x_kernel(const float* __restrict__ dpre, const T* __restrict__ x,
+                                  const float* __restrict__ w, T* __restrict__ dx, float* __restrict__ dw, int batch,
+                                  int tokens, int channels, int ksize) {
+  extern __shared__ float sdw[];  // channels * ksize
+  for (int i = threadIdx.x; i < channels * ksize; i += blockDim.x) sdw[i] = 0.f;
+  __syncthreads();
+  const int64_t n = (int64_t)batch * tokens * channels;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % channels);
+    const int64_t bt = i / channels;
+    const int t = (int)(bt % tokens);
+    float acc = 0.f;
+    const float dp = dpre[i];
+    for (int j = 0; j < ksize; ++j) {
+      if (t + j < tokens) acc += w[c * ksize + j] * dpre[(bt + j) * channels + c];
+      if (t - j >= 0) atomicAdd(&sdw[c * ksize + j], dp * to_f<T>(x[(bt - j) * channels + c]));
+    }
+    dx[i] = from_f<T>(acc);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < channels * ksize; i += blockDim.x) atomicAdd(&dw[i], sdw[i]);
+}
+
+
+}  // namespace
+
+#define KIMI_DISPATCH(dtype, T, ...)                       \
+  switch (dtype) {                                         \
+    case 0: { using T = float; __VA_ARGS__; break; }       \
+    case 1: { using T = __nv_bfloat16; __VA_ARGS__; break; } \
+    case 2: { using T = __half; __VA_ARGS__; break; }      \
+    default: return cudaErrorInvalidValue;                 \
+  }
+
+cudaError_t rms_norm_fwd(int dtype, const void* x, const float* w, void* y, float* rstd, int64_t rows, int dim,
+                         int period, float eps, cudaStream_t s) {
+  KIMI_DISPATCH(dtype, T, {
+    if (dim % Vec<T>::N) return cudaErrorInvalidValue;
+    const int tpr = pick_tpr(dim / Vec<T>::N);
+    const int threads = 256;
+    rms_fwd_kernel<T><<<grid_for(rows, threads / tpr), threads, 0, s>>>(
+        (const T*)x, w, (T*)y, rstd, rows, dim, period < 1 ? 1 : period, eps, tpr);
+  });
+  return cudaGetLastError();
+}
+
+cudaError_t rms_norm_bwd(int dtype, const void* dy, const void* x, const float* w, const float* rstd, void* dx,
+                         float* dw, int64_t rows, int dim, int period, cudaStream_t s) {
+  KIMI_DISPATCH(dtype, T, {
+    if (dim % Vec<T>::N) return cudaErrorInvalidValue;
+    const int tpr = pick_tpr(dim / Vec<T>::N);
+    const int threads = 256;
+    const int p = period < 1 ? 1 : period;
+    const size_t smem = dw ? (size_t)p * dim * sizeof(float) : 0;
+    if (smem > 48 * 1024) return cudaErrorInvalidValue;
+    rms_bwd_kernel<T><<<grid_for(rows, threads / tpr), threads, smem, s>>>(
+        (const T*)dy, (const T*)x, w, rstd, (T*)dx, dw, rows, dim, p, tpr);
+  });
+  return cudaGetLastError();
+}
+
+cudaError_t situ_glu_fwd(int dtype, const void* g, const void* u, void* y, int64_t n, float bg, float bu,
+                         cudaStream_t s) {
+  KIMI_DISPATCH(dtype, T, {
+    situ_fwd_kernel<T><<<grid_for(n / Vec<T>::N + 1, 256), 256, 0, s>>>((const T*)g, (const T*)u, (T*)y, n, bg, bu);
+  });
+  return cudaGetLastError();
+}
+
+cudaError_t situ_glu_bwd(int dtype, const void* dy, const void* g, const void* u, void* dg, void* du, int64_t n,
+                         float bg, float bu, cudaStream_t s) {
+  KIMI_DISPATCH(dtype, T, {
+    situ_bwd_kernel<T><<<grid_for(n / Vec<T>::N + 1, 256), 256, 0, s>>>((const T*)dy, (const T*)g, (const T*)u,
+                                                                       (T*)dg, (T*)du, n, bg, bu);
+  });
+  return cudaGetLastError();
+}
+
+cudaError_t sigmoid_mul_fwd(int dtype, const void* z, const void* x, void* y, int64_t n, cudaStream_t s) {
+  KIMI_DISPATCH(dtype, T, { sigmul_fwd_kernel<T><<<grid_for(n, 256), 256, 0, s>>>((const T*)z, (const T*)x, (T*)y, n); });
+  return cudaGetLastError();
+}
+
+cudaError_t sigmoid_mul_bwd(int dtype, const void* dy, const void* z, const void* x, void* dz, void* dx, int64_t n,
+                            cudaStream_t s) {
+  KIMI_DISPATCH(dtype, T, {
+    sigmul_bwd_kernel<T><<<grid_for(n, 256), 256, 0, s>>>((const T*)dy, (const T*)z, (const T*)x, (T*)dz, (T*)dx, n);
+  });
+  return cudaGetLastError();
+}
+
+cudaError_t kda_decay_fwd(int dtype, const void* z, const float* a_log, float* g, int64_t rows, int heads, int kdim,
+                          float g_min, float ceps, cudaStream_t s) {
+  const int64_t n = rows * heads * kdim;
+  KIMI_DISPATCH(dtype, T, {
+    decay_fwd_kernel<T><<<grid_for(n, 256), 256, 0, s>>>((const T*)z, a_log, g, n, heads, kdim, g_min, ceps);
+  });
+  return cudaGetLastError();
+}
+
+cudaError_t kda_decay_bwd(int dtype, const float* dg, const void* z, const float* a_log, void* dz, float* da_log,
+                          int64_t rows, int heads, int kdim, float g_min, float ceps, cudaStream_t s) {
+  const int64_t n = rows * heads * kdim;
+  KIMI_DISPATCH(dtype, T, {
+    decay_bwd_kernel<T><<<grid_for(n, 256), 256, heads * sizeof(float), s>>>(dg, (const T*)z, a_log, (T*)dz, da_log,
+                                                                            n, heads, kdim, g_min, ceps);
+  });
+  return cudaGetLastError();
+}
+
+cudaError_t conv_silu_norm_fwd(int dtype, const void* x, const float* w, void* y, int batch, int tokens,
+                               int channels, int ksize, int head_dim, float eps, bool normalize, cudaStream_t s) {
+  if (channels % head_dim) return cudaErrorInvalidValue;
+  int tpr = 1;
+  while (tpr * 8 < head_dim && tpr < 32) tpr <<= 1;
+  if (tpr * 8 < head_dim) return cudaErrorInvalidValue;
+  const int64_t groups = (int64_t)batch * tokens * (channels / head_dim);
+  KIMI_DISPATCH(dtype, T, {
+    conv_fwd_kernel<T><<<grid_for(groups, 256 / tpr), 256, 0, s>>>((const T*)x, w, (T*)y, batch, tokens, channels,
+                                                                   ksize, head_dim, eps, normalize, tpr);
+  });
+  return cudaGetLastError();
+}
+
+cudaError_t conv_silu_norm_bwd(int dtype, const void* dy, const void* x, const float* w, float* dpre, void* dx,
+                               float* dw, int batch, int tokens, int channels, int ksize, int head_dim, float eps,
+                               bool normalize, cudaStream_t s) {
+  if (channels % head_dim) return cudaErrorInvalidValue;
+  int tpr = 1;
+  while (tpr * 8 < head_dim && tpr < 32) tpr <<= 1;
+  if (tpr * 8 < head_dim) return cudaErrorInvalidValue;
+  const int64_t groups = (int64_t)batch * tokens * (channels / head_dim);
+  const int64_t n = (int64_t)batch * tokens * channels;
+  const size_t smem = (size_t)channels * ksize * sizeof(float);
+  if (smem > 48 * 1024) return cudaErrorInvalidValue;
+  KIMI_DISPATCH(dtype, T, {
+    conv_bwd_pre_kernel<T><<<grid_for(groups, 256 / tpr), 256, 0, s>>>(
+        (const T*)dy, (const T*)x, w, dpre, batch, tokens, channels, ksize, head_dim, eps, normalize, tpr);
+    conv_bwd_x_kernel<T><<<grid_for(n, 256), 256, smem, s>>>(dpre, (const T*)x, w, (T*)dx, dw, batch, tokens,
+                                                            channels, ksize);
+  });
+  return cudaGetLastError();
+}
+
+}  // namespace kimi

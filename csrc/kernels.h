@@ -1,0 +1,78 @@
+// Host-side launch entry points of the kimi_k3_b200 CUDA kernels.
+// Each launcher takes raw device pointers and a stream and returns the launch status.
+// dtype codes: 0 = float32, 1 = bfloat16, 2 = float16.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace kimi {
+
+// ---- norms / gates / activations (elementwise.cu)
+cudaError_t rms_norm_fwd(int dtype, const void* x, const float* w, void* y, float* rstd, int64_t rows, int dim,
+                         int weight_period, float eps, cudaStream_t s);
+cudaError_t rms_norm_bwd(int dtype, const void* dy, const void* x, const float* w, const float* rstd, void* dx,
+                         float* dw, int64_t rows, int dim, int weight_period, cudaStream_t s);
+cudaError_t situ_glu_fwd(int dtype, const void* g, const void* u, void* y, int64_t n, float bg, float bu,
+                         cudaStream_t s);
+cudaError_t situ_glu_bwd(int dtype, const void* dy, const void* g, const void* u, void* dg, void* du, int64_t n,
+                         float bg, float bu, cudaStream_t s);
+cudaError_t sigmoid_mul_fwd(int dtype, const void* z, const void* x, void* y, int64_t n, cudaStream_t s);
+cudaError_t sigmoid_mul_bwd(int dtype, const void* dy, const void* z, const void* x, void* dz, void* dx, int64_t n,
+                            cudaStream_t s);
+cudaError_t kda_decay_fwd(int dtype, const void* z, const float* a_log, float* g, int64_t rows, int heads,
+                          int kdim, float g_min, float clamp_eps, cudaStream_t s);
+cudaError_t kda_decay_bwd(int dtype, const float* dg, const void* z, const float* a_log, void* dz, float* da_log,
+                          int64_t rows, int heads, int kdim, float g_min, float clamp_eps, cudaStream_t s);
+cudaError_t conv_silu_norm_fwd(int dtype, const void* x, const float* w, void* y, int batch, int tokens,
+                               int channels, int ksize, int head_dim, float eps, bool normalize, cudaStream_t s);
+cudaError_t conv_silu_norm_bwd(int dtype, const void* dy, const void* x, const float* w, float* dpre, void* dx,
+                               float* dw, int batch, int tokens, int channels, int ksize, int head_dim, float eps,
+                               bool normalize, cudaStream_t s);
+
+// ---- attention residual depth mix (attnres.cu); sources: device array of S pointers
+cudaError_t attnres_mix_fwd(int dtype, const void* const* sources, int num_sources, const float* q, const float* w,
+                            void* out, float* probs, float* rstd, int64_t tokens, int dim, float eps,
+                            cudaStream_t s);
+cudaError_t attnres_mix_bwd(int dtype, const void* const* sources, int num_sources, const float* q, const float* w,
+                            const void* dout, const float* probs, const float* rstd, void* const* dsources,
+                            float* dq, float* dw, int64_t tokens, int dim, cudaStream_t s);
+
+// ---- cross-entropy rows (ce.cu): logits rows with leading dimension ld (elements)
+cudaError_t ce_rows_fwd_bwd(int dtype, void* logits, int64_t ld, int64_t rows, int vocab, const int64_t* targets,
+                            const bool* valid, float* loss_rows, float grad_scale, cudaStream_t s);
+
+// ---- router (router.cu)
+cudaError_t router_topk(int dtype, const void* logits, const float* bias, int64_t rows, int experts, int k,
+                        bool need_cutoff, float eps, int64_t* sel, float* raw_sel, float* weights, float* cutoff,
+                        int64_t* load, float* raw_out, cudaStream_t s);
+
+// ---- KDA chunk (kda_chunk.cu); head dims 64, chunk 64, tokens padded to a multiple of 64.
+// Intermediates are fp32 [B*H, NC, 64, 64] (eGC: [B*H, NC, 64]) and are kept for backward.
+struct KdaBuffers {
+  float* W;       // M (k e^G)            rows = chunk tokens, cols = key dim
+  float* U;       // M v
+  float* P;       // lower((q e^G)(k e^-G)^T)
+  float* Qg;      // q e^G
+  float* Kend;    // k e^(G_C - G)
+  float* eGC;     // e^(G_C)
+  float* states;  // S at the start of each chunk  [K x V]
+  float* Vp;      // U - W S
+};
+cudaError_t kda_chunk_fwd(int dtype, const void* q, const void* k, const void* v, const float* g, const float* beta,
+                          const float* h0, void* o, float* ht, KdaBuffers buf, int batch, int tokens_padded,
+                          int heads, cudaStream_t s);
+cudaError_t kda_chunk_bwd(int dtype, const void* q, const void* k, const void* v, const float* g, const float* beta,
+                          KdaBuffers buf, const void* dout, const float* dht, float* dVp, float* dSn, float* dq,
+                          float* dk, float* dv, float* dg, float* dbeta, float* dh0, int batch, int tokens_padded,
+                          int heads, cudaStream_t s);
+
+// ---- flash attention (flash_attn.cu); q/k/v/o are [B,T,H,D] contiguous
+cudaError_t flash_attn_fwd(int dtype, const void* q, const void* k, const void* v, void* o, float* lse, int batch,
+                           int tq, int tk, int heads, int dqk, int dv, bool causal, const int* key_lengths,
+                           float scale, cudaStream_t s);
+cudaError_t flash_attn_bwd(int dtype, const void* q, const void* k, const void* v, const void* o, const void* dout,
+                           const float* lse, float* dq_acc, void* dk, void* dv, float* delta, int batch, int tq,
+                           int tk, int heads, int dqk, int dv_dim, bool causal, const int* key_lengths, float scale,
+                           cudaStream_t s);
+
+}  // namespace kimi

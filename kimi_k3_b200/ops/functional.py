@@ -1,0 +1,390 @@
+"""Autograd functions over the sm_100a kernels (CUDA tensors only).
+
+Numerics contract (checked by ``tests/test_kernels_gpu.py`` against fp32 PyTorch):
+activations may be bf16/fp16/fp32; all reductions and recurrences run in fp32; outputs
+are rounded to the activation dtype once.  Gradients of fp32 parameters are returned in
+fp32.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+from . import _loader
+
+
+def _C():
+    return _loader.require()
+
+
+def _act_dtype(x: torch.Tensor) -> torch.dtype:
+    if torch.is_autocast_enabled("cuda") and x.dtype == torch.float32:
+        return torch.get_autocast_dtype("cuda")
+    return x.dtype
+
+
+# --------------------------------------------------------------------------- RMSNorm
+class _RMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, eps, period):
+        xc = x.contiguous()
+        y, rstd = _C().rms_norm_fwd(xc, w, float(eps), int(period))
+        ctx.save_for_backward(xc, w, rstd)
+        ctx.period = int(period)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w, rstd = ctx.saved_tensors
+        dx, dw = _C().rms_norm_bwd(dy, x, w, rstd, ctx.period, ctx.needs_input_grad[1])
+        return dx, (dw.to(w.dtype) if dw is not None and ctx.needs_input_grad[1] else None), None, None
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, per_row_weight_period: int | None = None):
+    """RMSNorm over the last axis; ``weight`` is ``[D]`` or ``[P, D]`` applied to row ``r % P``."""
+    dim = x.shape[-1]
+    vec = 16 // x.element_size()
+    if dim % vec:
+        from ..models.primitives import rms_norm_reference
+        return rms_norm_reference(x, weight, eps)
+    period = per_row_weight_period or 1
+    shape = x.shape
+    y = _RMSNorm.apply(x.reshape(-1, dim), weight, eps, period)
+    return y.reshape(shape)
+
+
+# --------------------------------------------------------------------------- SiTU / gates
+class _SiTU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, g, u, bg, bu):
+        g, u = g.contiguous(), u.contiguous()
+        ctx.save_for_backward(g, u)
+        ctx.b = (float(bg), float(bu))
+        return _C().situ_fwd(g, u, *ctx.b)
+
+    @staticmethod
+    def backward(ctx, dy):
+        g, u = ctx.saved_tensors
+        dg, du = _C().situ_bwd(dy, g, u, *ctx.b)
+        return dg, du, None, None
+
+
+def situ_glu(gate, up, beta_gate, beta_up):
+    if up.dtype != gate.dtype:
+        up = up.to(gate.dtype)
+    return _SiTU.apply(gate, up, beta_gate, beta_up)
+
+
+class _SigMul(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, z, x):
+        z, x = z.contiguous(), x.contiguous()
+        ctx.save_for_backward(z, x)
+        return _C().sigmul_fwd(z, x)
+
+    @staticmethod
+    def backward(ctx, dy):
+        z, x = ctx.saved_tensors
+        dz, dx = _C().sigmul_bwd(dy, z, x)
+        return dz, dx
+
+
+def sigmoid_mul(logits, x):
+    """``sigmoid(logits) * x`` (both in the activation dtype)."""
+    if x.dtype != logits.dtype:
+        x = x.to(logits.dtype)
+    return _SigMul.apply(logits, x)
+
+
+# --------------------------------------------------------------------------- KDA prep
+class _KdaDecay(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, z, a_log, g_min, ceps):
+        z = z.contiguous()
+        ctx.save_for_backward(z, a_log)
+        ctx.c = (float(g_min), float(ceps))
+        return _C().decay_fwd(z, a_log, *ctx.c)
+
+    @staticmethod
+    def backward(ctx, dg):
+        z, a_log = ctx.saved_tensors
+        dz, da = _C().decay_bwd(dg, z, a_log, *ctx.c)
+        return dz, da.to(a_log.dtype), None, None
+
+
+def kda_decay(logits, a_log, g_min):
+    """``g_min * clamp(sigmoid(exp(A_log) z), eps, 1-eps)`` in fp32 (eps of the input dtype)."""
+    return _KdaDecay.apply(logits, a_log, g_min, torch.finfo(logits.dtype).eps)
+
+
+class _ConvSiluNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, head_dim, eps, normalize):
+        x = x.contiguous()
+        ctx.save_for_backward(x, w)
+        ctx.c = (int(head_dim), float(eps), bool(normalize))
+        return _C().conv_fwd(x, w, *ctx.c)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        dx, dw = _C().conv_bwd(dy, x, w, *ctx.c)
+        return dx, dw.to(w.dtype), None, None, None
+
+
+def conv_silu_norm(x, conv_weight, head_dim, eps, normalize):
+    """Causal depthwise conv (zero history) + SiLU (+ per-head L2 normalisation)."""
+    return _ConvSiluNorm.apply(x, conv_weight, head_dim, eps, normalize)
+
+
+# --------------------------------------------------------------------------- KDA chunk core
+class _KdaChunk(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, h0, want_final):
+        out = _C().kda_fwd(q, k, v, g, beta, h0, bool(want_final))
+        o, ht, saved = out[0], out[1], out[2:]
+        ctx.save_for_backward(q, k, v, g, beta, *saved)
+        ctx.has_h0 = h0 is not None
+        if want_final:
+            return o, ht
+        return o, None
+
+    @staticmethod
+    def backward(ctx, do, dht):
+        q, k, v, g, beta, *saved = ctx.saved_tensors
+        dq, dk, dv, dg, dbeta, dh0 = _C().kda_bwd(q, k, v, g, beta, list(saved), do, dht, ctx.has_h0)
+        return (dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), dg, dbeta, dh0 if ctx.has_h0 else None, None)
+
+
+def kda_chunk(q, k, v, g, beta, initial_state, output_final_state, chunk_size=64):
+    """Chunked KDA on ``[B,T,H,64]``; returns ``(o, final_state or None)``.
+
+    ``g`` and ``beta`` are promoted to fp32; the token axis is zero-padded to a multiple
+    of 64 (padded tokens have g = 0 and beta = 0, so they neither decay nor write).
+    """
+    if chunk_size != 64 or q.shape[-1] != 64 or v.shape[-1] != 64:
+        raise NotImplementedError("the sm_100a KDA kernel implements chunk 64 and head dims 64")
+    b, t, h, _ = q.shape
+    dt = _act_dtype(v)
+    q, k, v = (x.to(dt).contiguous() for x in (q, k, v))
+    g = g.float().contiguous()
+    beta = beta.float().contiguous()
+    pad = (-t) % 64
+    if pad:
+        q, k, v, g = (F.pad(x, (0, 0, 0, 0, 0, pad)) for x in (q, k, v, g))
+        beta = F.pad(beta, (0, 0, 0, pad))
+    h0 = None if initial_state is None else initial_state.float().contiguous()
+    o, ht = _KdaChunk.apply(q, k, v, g, beta, h0, bool(output_final_state))
+    if pad:
+        o = o[:, :t]
+    return o, ht
+
+
+def kda_decode_step(q, k, v, g, beta, state):
+    """One recurrent KDA token for ``[B,1,H,*]`` inputs with fp32 state ``[B,H,K,V]``."""
+    qf, kf, vf, gf, bf = (x[:, 0].float() for x in (q, k, v, g, beta))
+    s = state.float() * torch.exp(gf)[..., None]
+    err = vf - torch.einsum("bhkv,bhk->bhv", s, kf)
+    s = s + torch.einsum("bhk,bhv->bhkv", bf[..., None] * kf, err)
+    o = torch.einsum("bhkv,bhk->bhv", s, qf)
+    return o[:, None].to(v.dtype), s
+
+
+# --------------------------------------------------------------------------- attention
+class _FlashAttn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, causal, key_lengths, scale):
+        o, lse = _C().fa_fwd(q, k, v, bool(causal), key_lengths, float(scale))
+        ctx.save_for_backward(q, k, v, o, lse, key_lengths if key_lengths is not None else torch.empty(0))
+        ctx.c = (bool(causal), float(scale), key_lengths is not None)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse, kl = ctx.saved_tensors
+        causal, scale, has_kl = ctx.c
+        dq, dk, dv = _C().fa_bwd(q, k, v, o, do, lse, causal, kl if has_kl else None, scale)
+        return dq.to(q.dtype), dk, dv, None, None, None
+
+
+def flash_attention(q, k, v, causal=True, key_padding_mask=None, scale=None):
+    """Attention over ``[B,T,H,64]`` tensors (bf16/fp16 compute); returns ``[B,Tq,H,64]``.
+
+    ``key_padding_mask`` ``[B,Tk]`` (True = valid) must be right-padded; it is turned
+    into per-row key lengths.
+    """
+    dt = _act_dtype(q)
+    if dt == torch.float32:
+        dt = torch.bfloat16
+    q, k, v = (x.to(dt).contiguous() for x in (q, k, v))
+    kl = None
+    if key_padding_mask is not None:
+        kl = key_padding_mask.sum(dim=1).to(torch.int32)
+    scale = 1.0 / math.sqrt(q.shape[-1]) if scale is None else scale
+    return _FlashAttn.apply(q, k, v, causal, kl, scale)
+
+
+def mla_absorbed_decode(query, latent_cache, cache_mask, key_up_weight, value_up_weight):
+    """Weight-absorbed one-token MLA attention over the latent cache (fp32 math)."""
+    b, _, h, dq = query.shape
+    l = latent_cache.shape[-1]
+    wuk = key_up_weight.float().reshape(h, dq, l)
+    wuv = value_up_weight.float().reshape(h, -1, l)
+    q_lat = torch.einsum("bhd,hdl->bhl", query[:, 0].float(), wuk) / math.sqrt(dq)
+    scores = torch.einsum("bhl,btl->bht", q_lat, latent_cache.float())
+    if cache_mask is not None:
+        scores = scores.masked_fill(~cache_mask[:, None, :], -torch.inf)
+    p = torch.softmax(scores, dim=-1)
+    ctx = torch.einsum("bht,btl->bhl", p, latent_cache.float())
+    return torch.einsum("bhl,hvl->bhv", ctx, wuv)[:, None]
+
+
+# --------------------------------------------------------------------------- router / MoE
+class _RouterWeights(torch.autograd.Function):
+    """Forward: fused kernel. Backward: gradient of the renormalised weights to the logits."""
+
+    @staticmethod
+    def forward(ctx, logits, bias, k, need_cutoff, eps, return_raw):
+        sel, raw_sel, weights, cutoff, load, raw = _C().router(logits.contiguous(), bias, int(k), bool(need_cutoff),
+                                                               float(eps), bool(return_raw))
+        ctx.save_for_backward(sel, raw_sel, weights)
+        ctx.shape = logits.shape
+        ctx.dtype = logits.dtype
+        ctx.eps = float(eps)
+        ctx.mark_non_differentiable(sel, raw_sel, cutoff, load)
+        if raw is not None and raw.numel():
+            ctx.mark_non_differentiable(raw)
+        return sel, raw_sel, weights, cutoff, load, raw
+
+    @staticmethod
+    def backward(ctx, _dsel, _draw, dw, _dc, _dl, _dr):
+        sel, raw_sel, weights = ctx.saved_tensors
+        denom = raw_sel.sum(-1, keepdim=True).clamp_min(ctx.eps)
+        draw_sel = (dw - (dw * weights).sum(-1, keepdim=True)) / denom
+        dlogit_sel = draw_sel * raw_sel * (1.0 - raw_sel)
+        dlogits = torch.zeros(ctx.shape, dtype=torch.float32, device=dw.device)
+        dlogits.scatter_add_(1, sel, dlogit_sel)
+        return dlogits.to(ctx.dtype), None, None, None, None, None
+
+
+def router_topk(logits, bias, k, need_cutoff, eps, return_raw):
+    sel, raw_sel, weights, cutoff, load, raw = _RouterWeights.apply(logits, bias, k, need_cutoff, eps, return_raw)
+    return sel, raw_sel, weights, cutoff, load, (raw if return_raw else None)
+
+
+def qb_histogram(raw_scores, cutoffs, counts, underflow, overflow, min_margin, max_margin):
+    e, bins = counts.shape
+    margins = raw_scores.float() - cutoffs.float()[:, None]
+    underflow.add_((margins < min_margin).sum(0))
+    overflow.add_((margins >= max_margin).sum(0))
+    width = (max_margin - min_margin) / bins
+    idx = torch.floor((margins - min_margin) / width).long().clamp_(0, bins - 1)
+    flat = idx + torch.arange(e, device=margins.device)[None, :] * bins
+    counts.add_(torch.bincount(flat.reshape(-1), minlength=e * bins).reshape(e, bins))
+
+
+def moe_grouped_experts(latent, selected, weights, gate_w, up_w, down_w, beta_gate, beta_up):
+    """``sum_k w_k E_{sel_k}(latent)`` in fp32 via expert-sorted grouped GEMMs."""
+    m, l = latent.shape
+    k = selected.shape[1]
+    e_count = gate_w.shape[0]
+    dt = _act_dtype(latent)
+    x = latent.to(dt)
+    flat_e = selected.reshape(-1)
+    order = torch.argsort(flat_e, stable=True)
+    tok = order // k
+    counts = torch.bincount(flat_e, minlength=e_count).tolist()
+    xs = x.index_select(0, tok)
+    outs = []
+    start = 0
+    for e, cnt in enumerate(counts):
+        if cnt == 0:
+            continue
+        xe = xs[start:start + cnt]
+        g = xe @ gate_w[e].to(dt).t()
+        u = xe @ up_w[e].to(dt).t()
+        outs.append(situ_glu(g, u, beta_gate, beta_up) @ down_w[e].to(dt).t())
+        start += cnt
+    ys = torch.cat(outs, 0) if outs else xs.new_zeros(0, l)
+    w_sorted = weights.reshape(-1).index_select(0, order).float()
+    agg = torch.zeros(m, l, device=latent.device, dtype=torch.float32)
+    return agg.index_add(0, tok, ys.float() * w_sorted[:, None])
+
+
+# --------------------------------------------------------------------------- AttnRes
+class _AttnResMix(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, w, eps, *sources):
+        srcs = [s.contiguous() for s in sources]
+        out, probs, rstd = _C().attnres_fwd(srcs, q, w, float(eps))
+        ctx.save_for_backward(q, w, probs, rstd, *srcs)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, w, probs, rstd, *srcs = ctx.saved_tensors
+        grads = _C().attnres_bwd(list(srcs), q, w, dout, probs, rstd)
+        dsrc, dq, dw = grads[:-2], grads[-2], grads[-1]
+        return (dq.to(q.dtype), dw.to(w.dtype), None, *dsrc)
+
+
+def attnres_mix(sources, pseudo_query, key_norm_weight, eps):
+    """Depth softmax mix of ``S`` same-shape ``[B,T,D]`` sources (one fused pass)."""
+    dt = sources[0].dtype
+    srcs = [s if s.dtype == dt else s.to(dt) for s in sources]
+    return _AttnResMix.apply(pseudo_query, key_norm_weight, eps, *srcs)
+
+
+# --------------------------------------------------------------------------- LM head + CE
+class _LinearCE(torch.autograd.Function):
+    """``sum_valid CE(h @ W^T, t)``; gradients are formed chunk by chunk in forward.
+
+    Each row chunk: logits = h_c W^T (bf16, padded leading dimension), the fused row
+    kernel writes loss and (softmax - onehot) in place, then dh_c = G W and dW += G^T h_c.
+    Backward only scales by the incoming scalar gradient.
+    """
+
+    @staticmethod
+    def forward(ctx, h, w, targets, valid, chunk_rows):
+        n, d = h.shape
+        v = w.shape[0]
+        dt = h.dtype
+        wd = w.to(dt)
+        vpad = (v + 7) // 8 * 8
+        loss = torch.zeros((), device=h.device, dtype=torch.float32)
+        dh = torch.empty_like(h)
+        dw = torch.zeros(v, d, device=h.device, dtype=torch.float32)
+        buf = torch.empty(min(chunk_rows, n), vpad, device=h.device, dtype=dt)
+        for s in range(0, n, chunk_rows):
+            e = min(n, s + chunk_rows)
+            hc = h[s:e]
+            lg = buf[: e - s, :v]
+            torch.mm(hc, wd.t(), out=lg)
+            rows = _C().ce_rows(lg, v, targets[s:e], valid[s:e], 1.0)
+            loss += rows.sum()
+            torch.mm(lg, wd, out=dh[s:e])
+            dw.add_(torch.mm(lg.t(), hc).float())
+        ctx.save_for_backward(dh, dw)
+        ctx.w_dtype = w.dtype
+        return loss
+
+    @staticmethod
+    def backward(ctx, gl):
+        dh, dw = ctx.saved_tensors
+        return dh * gl.to(dh.dtype), (dw * gl).to(ctx.w_dtype), None, None, None
+
+
+def linear_cross_entropy(hidden, weight, targets, valid, chunk_rows: int = 4096):
+    """Sum of token CE losses of ``hidden @ weight^T`` over valid rows (fp32 scalar)."""
+    dt = _act_dtype(hidden)
+    h = hidden.to(dt).contiguous()
+    return _LinearCE.apply(h, weight, targets.contiguous(), valid.contiguous(), int(chunk_rows))
+
+
+__all__ = [
+    "rms_norm", "situ_glu", "sigmoid_mul", "kda_decay", "conv_silu_norm", "kda_chunk", "kda_decode_step",
+    "flash_attention", "mla_absorbed_decode", "router_topk", "qb_histogram", "moe_grouped_experts",
+    "attnres_mix", "linear_cross_entropy",
+]
