@@ -1,0 +1,354 @@
+#!/usr/bin/env python
+"""Training-throughput benchmark: t4_wikitext-shaped Kimi K3 (vocab 50,257), seq 1024, bf16.
+
+    python bench.py --gpus N --steps K --warmup W [--impl ours|reference]
+
+One optimizer step = forward (NTP + MTP losses) + backward + global-norm clip (1.0) +
+Per-Head Muon / Muon / AdamW + QK-Clip + warmup-cosine LR + Quantile-Balancing commit.
+Weak scaling: every rank trains ``--batch-per-gpu`` sequences (16 at N=1, the named
+config's global batch).  Timing: W untimed steps, then K steps bracketed by a barrier
+and ``torch.cuda.synchronize()`` on both sides and timed with CUDA events on the
+compute stream; the max over ranks is reported.  ``e2e`` repeats the measurement through
+the public ``TrainStepEngine.step`` API with inputs copied every step from pinned host
+memory and the loss read back every step.  For N > 1 launch with
+``python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+VOCAB = 50257
+SEQ = 1024
+PROFILE = "t4_wikitext"
+METRIC = "train_tokens_per_s"
+
+
+# --------------------------------------------------------------------------- helpers
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[3:7]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def init_dist(world, local):
+    torch.cuda.set_device(local)
+    if world > 1 and not torch.distributed.is_initialized():
+        from datetime import timedelta
+        torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=600),
+                                             device_id=torch.device("cuda", local))
+
+
+def max_over_ranks(value: float) -> float:
+    if torch.distributed.is_initialized():
+        t = torch.tensor([value], device="cuda", dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+    return value
+
+
+def barrier():
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+
+
+def make_batches(n, batch, seq, vocab, seed, device=None, pin=False):
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for _ in range(n):
+        ids = torch.randint(0, vocab, (batch, seq + 1), generator=g)
+        b = {"input_ids": ids[:, :-1].contiguous(), "labels": ids[:, 1:].contiguous(),
+             "attention_mask": torch.ones(batch, seq, dtype=torch.bool)}
+        if pin:
+            b = {k: v.pin_memory() for k, v in b.items()}
+        if device is not None:
+            b = {k: v.to(device) for k, v in b.items()}
+        out.append(b)
+    return out
+
+
+def optimizer_settings():
+    """t4_wikitext training.yaml optimizer/scheduler values."""
+    return dict(kind="per_head_muon_adamw", adamw_lr=3e-4, adamw_betas=(0.9, 0.95), adamw_eps=1e-8, muon_lr=3e-4,
+                muon_momentum=0.95, muon_nesterov=True, muon_ns_steps=5, muon_ns_eps=1e-7,
+                muon_update_rms_scaling=True, weight_decay=0.1, per_head_qkv=True, qk_clip_enabled=True,
+                qk_clip_threshold=100.0, qk_clip_every_steps=1)
+
+
+# --------------------------------------------------------------------------- our arm
+def run_ours(args, world, rank, local):
+    sys.path.insert(0, ROOT)
+    from kimi_k3_b200.config.profiles import profile_model_config
+    from kimi_k3_b200.models import KimiK3
+    from kimi_k3_b200.train.engine import MoEController, TrainStepEngine
+    from kimi_k3_b200.train.optimizer import KimiOptimizerConfig, build_kimi_optimizer
+    from kimi_k3_b200.train.scheduler import build_warmup_cosine_scheduler
+    from kimi_k3_b200.parallel.data_parallel import GradientAllReducer
+
+    dev = torch.device("cuda", local)
+    torch.manual_seed(1337)
+    model = KimiK3(profile_model_config(PROFILE, vocab_size=VOCAB)).to(dev)
+    reducer = GradientAllReducer(model) if world > 1 else None
+    if reducer is not None:
+        reducer.broadcast_parameters()
+    opt, _ = build_kimi_optimizer(model, KimiOptimizerConfig(**optimizer_settings()))
+    total = args.warmup + 2 * args.steps + 8
+    sched = build_warmup_cosine_scheduler(opt, total_steps=total, warmup_steps=max(1, total // 100), min_lr=3e-5,
+                                          min_muon_lr=3e-5, prepare_first_update=True)
+    engine = TrainStepEngine(model, opt, scheduler=sched, grad_clip=1.0, amp_dtype=torch.bfloat16, use_mtp=True,
+                             moe_controller=MoEController(model, reducer=reducer.qb_reducer() if reducer else None),
+                             grad_hook=reducer.all_reduce_gradients if reducer else None)
+    bpg = args.batch_per_gpu
+    dev_batches = make_batches(4, bpg, SEQ, VOCAB, seed=1000 + rank, device=dev)
+    host_batches = make_batches(4, bpg, SEQ, VOCAB, seed=2000 + rank, pin=True)
+
+    def device_loop(n, start=0):
+        for i in range(n):
+            engine.step(dev_batches[(start + i) % len(dev_batches)])
+
+    device_loop(args.warmup)
+    torch.cuda.synchronize()
+    barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    torch.cuda.synchronize()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    device_loop(args.steps)
+    ev1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+
+    # end to end through the public step API: pinned H2D copy in, loss read back, every step
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    losses = []
+    for i in range(args.steps):
+        out = engine.step(host_batches[i % len(host_batches)])
+        losses.append(float(out.loss.item()))
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1000.0 / args.steps)
+    h2d = sum(v.numel() * v.element_size() for v in host_batches[0].values())
+    launches = count_launches(engine, dev_batches[0]) if rank == 0 else None
+    return ms, e2e_ms, clocks, h2d, 4, launches, losses[-1]
+
+
+def count_launches(engine, batch):
+    """Kernels of this repository's extension launched by one training step."""
+    try:
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            engine.step(batch)
+            torch.cuda.synchronize()
+        mine = total = 0
+        for ev in prof.events():
+            if ev.device_type == torch.autograd.DeviceType.CUDA:
+                total += 1
+                name = ev.name
+                if "kimi::" in name or any(s in name for s in ("kda_", "fa_fwd", "fa_bwd", "fa_delta", "rms_fwd",
+                                                               "rms_bwd", "attnres_", "situ_", "sigmul_", "decay_",
+                                                               "conv_fwd", "conv_bwd", "router_kernel",
+                                                               "ce_rows", "gemm_", "moe_")):
+                    mine += 1
+        return {"per_step_ours": mine, "per_step_all": total}
+    except Exception as exc:  # profiler unavailable: report why
+        return {"error": repr(exc)}
+
+
+# --------------------------------------------------------------------------- reference arm
+def run_reference(args, world, rank, local):
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "src")):
+        raise FileNotFoundError("baseline/_ref is not installed")
+    sys.path.insert(0, ref)
+    from src.kimi_k3.yaml_config import build_model_config_from_mapping as ref_build
+    from src.kimi_k3_mini import KimiK3 as RefKimiK3
+    from training.moe_control import MoEController as RefMoEController
+    from training.optimizer import KimiOptimizerConfig as RefOptConfig
+    from training.optimizer import build_kimi_optimizer as ref_build_optimizer
+    from training.scheduler import build_warmup_cosine_scheduler as ref_scheduler
+    from training.train_one_epoch import train_one_epoch
+    sys.path.insert(0, ROOT)
+    from kimi_k3_b200.config.profiles import profile_model_mapping
+
+    dev = torch.device("cuda", local)
+    mapping = profile_model_mapping(PROFILE)
+    mapping["model"]["vocab_size"] = VOCAB
+    torch.manual_seed(1337)
+    model = RefKimiK3(ref_build(mapping)).to(dev)
+    context = None
+    if world > 1:
+        from training.distributed.config import DataParallelConfig, DistributedConfig
+        from training.distributed.environment import initialize_distributed
+        from training.distributed.mesh import build_device_mesh
+        from training.distributed.wrapping import broadcast_model_state, wrap_data_parallel
+        dcfg = DistributedConfig(enabled=True, backend="nccl", timeout_seconds=600,
+                                 data_parallel=DataParallelConfig(mode="ddp", size=world, find_unused_parameters=True))
+        context = build_device_mesh(initialize_distributed(dcfg), dcfg)
+        broadcast_model_state(model, context)
+        model = wrap_data_parallel(model, dcfg, context, training_precision="bf16")
+    raw = model.module if hasattr(model, "module") else model
+    opt, _ = ref_build_optimizer(raw, RefOptConfig(**optimizer_settings()))
+    total = args.warmup + args.steps + 8
+    sched = ref_scheduler(opt, total_steps=total, warmup_steps=max(1, total // 100), min_lr=3e-5, min_muon_lr=3e-5,
+                          prepare_first_update=True)
+    batches = make_batches(args.warmup + args.steps, args.batch_per_gpu, SEQ, VOCAB, seed=1000 + rank)
+    state = {"n": 0}
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    host = {}
+
+    def on_step(_metrics):
+        state["n"] += 1
+        if state["n"] == args.warmup:
+            torch.cuda.synchronize()
+            barrier()
+            sampler.start()
+            torch.cuda.synchronize()
+            barrier()
+            host["t0"] = time.perf_counter()
+            ev0.record()
+        elif state["n"] == args.warmup + args.steps:
+            ev1.record()
+            torch.cuda.synchronize()
+            host["t1"] = time.perf_counter()
+            barrier()
+
+    train_one_epoch(model, batches, opt, device=dev, scheduler=sched, amp_enabled=True, amp_dtype="bf16",
+                    grad_accum_steps=1, grad_clip=1.0, max_batches=len(batches), use_mtp=True,
+                    moe_controller=RefMoEController(model), on_optimizer_step=on_step, distributed_context=context)
+    clocks = sampler.stop()
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+    e2e_ms = max_over_ranks((host["t1"] - host["t0"]) * 1000.0 / args.steps)
+    h2d = sum(v.numel() * v.element_size() for v in batches[0].values())
+    return ms, e2e_ms, clocks, h2d, None, None, None
+
+
+# --------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--batch-per-gpu", type=int, default=16)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    world, rank, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torch.distributed.run")
+    base = {"metric": METRIC, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "dtype": "bf16",
+            "data": "synthetic uniform token ids (seeded), random-init weights",
+            "config": {"model": f"{PROFILE}-shaped Kimi K3 (vocab {VOCAB}, MTP on)",
+                       "global_batch": args.batch_per_gpu * world, "seq_len": SEQ, "parallelism": f"dp{world}",
+                       "optimizer": "per-head Muon + Muon + AdamW, QK-Clip, grad clip 1.0, QB histogram",
+                       "l2": "per-step working set (0.2B params + optimizer state + activations) >> 126 MB L2"}}
+    if args.impl == "reference":
+        base["impl"] = "reference"
+    try:
+        if not torch.cuda.is_available():
+            raise RuntimeError("no CUDA device")
+        init_dist(world, local)
+        fn = run_reference if args.impl == "reference" else run_ours
+        ms, e2e_ms, clocks, h2d, d2h, launches, last_loss = fn(args, world, rank, local)
+    except Exception as exc:
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": f"{type(exc).__name__}: {exc}"[:300]}))
+            return 0
+        raise
+    tokens = args.batch_per_gpu * SEQ * world
+    value = tokens / (ms / 1000.0)
+    line = dict(base)
+    line.update({"value": round(value, 1), "ms_per_step": round(ms, 3), "vs_baseline": None, "clocks": clocks,
+                 "e2e": {"value": round(tokens / (e2e_ms / 1000.0), 1), "unit": "tokens/s",
+                         "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d,
+                         "d2h_bytes_per_step": d2h}})
+    if launches is not None:
+        line["gpu_launches"] = (launches.get("per_step_ours", 0) * args.steps) if "per_step_ours" in launches else 0
+        line["launch_detail"] = launches
+    if last_loss is not None:
+        line["last_loss"] = round(last_loss, 4)
+    if rank == 0:
+        print(json.dumps(line))
+    if torch.distributed.is_initialized():
+        barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,722 @@
+"""Hybrid optimizer: (Per-Head) Muon for matrices + AdamW for the rest + QK-Clip.
+
+Parity targets (reference paths):
+  * ``training/optimizer/newton_schulz.py:11-74``   quintic NS (a, b, c) = (3.4445, -4.7750, 2.0315)
+  * ``training/optimizer/muon.py:17-142``           momentum, Nesterov, decoupled decay, RMS match
+  * ``training/optimizer/per_head_muon.py:14-159``  per-head orthogonalisation of q/k/v
+  * ``training/optimizer/parameter_registry.py``    family assignment + fingerprint
+  * ``training/optimizer/qk_clip.py:39-162``        rescale W_q / W_k by sqrt(tau / s)
+  * ``training/optimizer/hybrid.py:28-255``         transactional step, state dict
+  * ``training/optimizer/config.py``                KimiOptimizerConfig
+
+B200 design: every Muon matrix (a plain 2-D weight, one head block of a q/k/v
+projection, or one expert of a stacked ``[E, H, L]`` weight) is placed in a bucket
+of equal-shape matrices; each step runs one batched Newton-Schulz per bucket
+(``torch.baddbmm`` chains) instead of one small GEMM chain per matrix/head.  The
+non-finite check, the update metrics and QK-Clip all stay on the device; the host
+reads them in one transfer when a report is requested.
+"""
+from __future__ import annotations
+
+import hashlib
+import json
+import math
+from dataclasses import asdict, dataclass, field
+from typing import Literal
+
+import torch
+import torch.nn as nn
+
+NS_COEFFS = (3.4445, -4.7750, 2.0315)
+
+
+# --------------------------------------------------------------------------- config
+@dataclass(frozen=True)
+class KimiOptimizerConfig:
+    kind: Literal["adamw", "muon_adamw", "per_head_muon_adamw"] = "per_head_muon_adamw"
+    adamw_lr: float = 3e-4
+    adamw_betas: tuple = (0.9, 0.95)
+    adamw_eps: float = 1e-8
+    muon_lr: float | None = None
+    muon_momentum: float = 0.95
+    muon_nesterov: bool = True
+    muon_ns_steps: int = 5
+    muon_ns_eps: float = 1e-7
+    muon_update_rms_scaling: bool = True
+    weight_decay: float = 0.1
+    muon_weight_decay: float | None = None
+    per_head_qkv: bool = True
+    qk_clip_enabled: bool = True
+    qk_clip_threshold: float = 100.0
+    qk_clip_eps: float = 1e-6
+    qk_clip_every_steps: int = 1
+    qk_clip_kda_experimental: bool = False
+    fail_on_unclassified_matrix: bool = True
+    muon_ns_dtype: str = "auto"
+
+    def __post_init__(self) -> None:
+        object.__setattr__(self, "adamw_betas", tuple(self.adamw_betas))
+        if self.kind not in ("adamw", "muon_adamw", "per_head_muon_adamw"):
+            raise ValueError("unknown optimizer kind")
+        if self.adamw_lr <= 0 or self.adamw_eps <= 0:
+            raise ValueError("AdamW learning rate and epsilon must be positive")
+        if len(self.adamw_betas) != 2 or not all(0 <= v < 1 for v in self.adamw_betas):
+            raise ValueError("adamw_betas must contain two values in [0, 1)")
+        if self.muon_lr is not None and self.muon_lr <= 0:
+            raise ValueError("muon_lr must be None or positive")
+        if not 0 <= self.muon_momentum < 1:
+            raise ValueError("muon_momentum must be in [0, 1)")
+        if self.muon_ns_steps <= 0 or self.muon_ns_eps <= 0:
+            raise ValueError("Newton-Schulz steps and epsilon must be positive")
+        if self.weight_decay < 0 or (self.muon_weight_decay is not None and self.muon_weight_decay < 0):
+            raise ValueError("weight decay must be non-negative")
+        if self.qk_clip_threshold <= 0 or self.qk_clip_eps <= 0 or self.qk_clip_every_steps <= 0:
+            raise ValueError("invalid QK-Clip configuration")
+        if self.kind == "per_head_muon_adamw" and not self.per_head_qkv:
+            raise ValueError("canonical Per-Head Muon requires per_head_qkv=True")
+        if self.muon_ns_dtype not in ("auto", "float32", "bfloat16"):
+            raise ValueError("muon_ns_dtype must be auto, float32 or bfloat16")
+
+    @property
+    def resolved_muon_lr(self) -> float:
+        return self.adamw_lr if self.muon_lr is None else self.muon_lr
+
+    @property
+    def resolved_muon_weight_decay(self) -> float:
+        return self.weight_decay if self.muon_weight_decay is None else self.muon_weight_decay
+
+    def to_dict(self) -> dict:
+        return asdict(self)
+
+    @classmethod
+    def from_dict(cls, values: dict) -> "KimiOptimizerConfig":
+        return cls(**values)
+
+
+# --------------------------------------------------------------------------- Newton-Schulz
+@torch.no_grad()
+def zeropower_via_newton_schulz(matrix: torch.Tensor, *, steps: int = 5, eps: float = 1e-7,
+                                output_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """Single-matrix quintic Newton-Schulz orthogonalisation (fp32)."""
+    if matrix.ndim != 2:
+        raise ValueError("Newton-Schulz input must be a 2D matrix")
+    if steps <= 0 or eps <= 0:
+        raise ValueError("steps and eps must be positive")
+    out = batched_newton_schulz(matrix.detach()[None].float(), steps=steps, eps=eps, dtype=torch.float32)[0]
+    if not torch.isfinite(matrix).all():
+        raise FloatingPointError("Newton-Schulz input contains NaN or Inf")
+    return out.to(dtype=output_dtype or matrix.dtype)
+
+
+@torch.no_grad()
+def batched_newton_schulz(x: torch.Tensor, *, steps: int = 5, eps: float = 1e-7,
+                          dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """Orthogonalise a batch ``[N, m, n]`` of matrices; all-zero matrices map to zero.
+
+    Tall matrices are transposed so the Gram matrix is the small side.
+    """
+    a, b, c = NS_COEFFS
+    transposed = x.shape[-2] > x.shape[-1]
+    w = x.transpose(-2, -1) if transposed else x
+    norms = w.float().flatten(1).norm(dim=1)
+    w = (w.float() / norms.clamp_min(eps)[:, None, None]).to(dtype)
+    for _ in range(steps):
+        gram = w @ w.transpose(-2, -1)
+        poly = torch.baddbmm(gram, gram, gram, beta=b, alpha=c)  # b*G + c*G@G
+        w = torch.baddbmm(w, poly, w, beta=a, alpha=1.0)          # a*X + poly@X
+    w = w.float() * (norms > eps).to(torch.float32)[:, None, None]
+    return w.transpose(-2, -1) if transposed else w
+
+
+@torch.no_grad()
+def match_update_rms(orthogonal_update, reference=None, *, mode="shape", eps=1e-12):
+    if mode == "shape":
+        return orthogonal_update * (max(orthogonal_update.shape[-2:]) ** 0.5)
+    if mode != "reference_rms":
+        raise ValueError("unknown update RMS matching mode")
+    if reference is None or reference.shape != orthogonal_update.shape:
+        raise ValueError("reference_rms mode requires a matching reference")
+    target = reference.float().square().mean().sqrt()
+    current = orthogonal_update.float().square().mean().sqrt()
+    if float(current) <= eps:
+        return torch.zeros_like(orthogonal_update)
+    return orthogonal_update * (target / current).to(orthogonal_update.dtype)
+
+
+# --------------------------------------------------------------------------- head layouts
+@dataclass(frozen=True)
+class HeadMatrixLayout:
+    num_heads: int
+    head_dim: int
+    head_axis: int
+    input_dim: int
+    output_dim: int
+    packed_kind: str = "separate"
+    qkv_slices: tuple | None = None
+
+    def __post_init__(self) -> None:
+        if self.num_heads <= 0 or self.head_dim <= 0 or self.head_axis not in (0, 1):
+            raise ValueError("invalid head layout")
+        if self.packed_kind == "fused_qkv" and self.qkv_slices is None:
+            raise ValueError("fused_qkv layout requires explicit slices")
+
+    def validate(self, matrix: torch.Tensor) -> None:
+        if matrix.ndim != 2 or tuple(matrix.shape) != (self.output_dim, self.input_dim):
+            raise ValueError("matrix shape does not match the head layout")
+        if self.packed_kind == "separate" and matrix.shape[self.head_axis] != self.num_heads * self.head_dim:
+            raise ValueError("head axis does not equal num_heads * head_dim")
+
+    def head_blocks(self, matrix: torch.Tensor) -> torch.Tensor:
+        """``[num_heads, head_dim, in]`` (axis 0) or ``[num_heads, out, head_dim]`` (axis 1) view/copy."""
+        if self.head_axis == 0:
+            return matrix.reshape(self.num_heads, self.head_dim, matrix.shape[1])
+        return matrix.reshape(matrix.shape[0], self.num_heads, self.head_dim).permute(1, 0, 2)
+
+
+def split_head_matrix(matrix, layout: HeadMatrixLayout):
+    layout.validate(matrix)
+    blocks = layout.head_blocks(matrix)
+    return tuple(blocks[i] for i in range(layout.num_heads))
+
+
+def merge_head_matrix(blocks, layout: HeadMatrixLayout):
+    st = torch.stack(tuple(blocks))
+    if layout.head_axis == 0:
+        return st.reshape(layout.output_dim, layout.input_dim)
+    return st.permute(1, 0, 2).reshape(layout.output_dim, layout.input_dim)
+
+
+@torch.no_grad()
+def per_head_orthogonalize(matrix, layout: HeadMatrixLayout, *, steps, eps, rms_scaling=True):
+    """Orthogonalise each head block independently (batched NS); returns (update, metrics)."""
+    layout.validate(matrix)
+    blocks = layout.head_blocks(matrix).float()
+    raw = blocks.flatten(1).square().mean(1).sqrt()
+    ortho = batched_newton_schulz(blocks, steps=steps, eps=eps)
+    orms = ortho.flatten(1).square().mean(1).sqrt()
+    if rms_scaling:
+        ortho = ortho * (max(ortho.shape[-2:]) ** 0.5)
+    final = ortho.flatten(1).square().mean(1).sqrt()
+    out = merge_head_matrix(list(ortho), layout)
+
+    def summary(v, label):
+        v = v.double()
+        mean, std = float(v.mean()), float(v.std(unbiased=False))
+        return {f"per_head_muon/{label}_mean": mean, f"per_head_muon/{label}_std": std,
+                f"per_head_muon/{label}_min": float(v.min()), f"per_head_muon/{label}_max": float(v.max()),
+                f"per_head_muon/{label}_median": float(v.median()), f"per_head_muon/{label}_cv": std / max(mean, eps)}
+
+    metrics = {}
+    metrics.update(summary(raw, "raw_momentum_rms"))
+    metrics.update(summary(orms, "orthogonal_update_rms"))
+    metrics.update(summary(final, "head_update_rms"))
+    fd = final.double()
+    metrics["per_head_muon/head_update_rms_max_to_median"] = float(fd.max()) / max(float(fd.median()), eps)
+    metrics["per_head_muon/fraction_heads_near_zero_update"] = float((fd <= eps).double().mean())
+    return out.to(matrix.dtype), metrics
+
+
+# --------------------------------------------------------------------------- registry
+OptimizerFamily = Literal["adamw_decay", "adamw_no_decay", "muon", "per_head_muon"]
+
+
+@dataclass(frozen=True)
+class MatrixParameterSpec:
+    parameter_name: str
+    parameter: nn.Parameter
+    owner_module_name: str
+    role: str
+    optimizer_family: str
+    apply_weight_decay: bool
+    head_layout: HeadMatrixLayout | None = None
+
+    def fingerprint_record(self) -> dict:
+        layout = None
+        if self.head_layout is not None:
+            hl = self.head_layout
+            layout = {"num_heads": hl.num_heads, "head_dim": hl.head_dim, "head_axis": hl.head_axis,
+                      "input_dim": hl.input_dim, "output_dim": hl.output_dim, "packed_kind": hl.packed_kind}
+        return {"name": self.parameter_name, "shape": list(self.parameter.shape), "role": self.role,
+                "family": self.optimizer_family, "weight_decay": self.apply_weight_decay, "head_layout": layout}
+
+
+@dataclass(frozen=True)
+class ParameterAssignmentReport:
+    specs: tuple
+    numel_by_family: dict
+    tensor_count_by_family: dict
+    percentages_by_family: dict
+    missing: tuple
+    duplicates: tuple
+    ambiguous: tuple
+    fingerprint: str
+
+    @property
+    def total_numel(self) -> int:
+        return sum(self.numel_by_family.values())
+
+    def names_for(self, family: str) -> tuple:
+        return tuple(s.parameter_name for s in self.specs if s.optimizer_family == family)
+
+    def to_dict(self) -> dict:
+        return {"numel_by_family": dict(self.numel_by_family), "tensor_count_by_family": dict(self.tensor_count_by_family),
+                "percentages_by_family": dict(self.percentages_by_family), "missing": list(self.missing),
+                "duplicates": list(self.duplicates), "ambiguous": list(self.ambiguous),
+                "fingerprint": self.fingerprint, "specs": [s.fingerprint_record() for s in self.specs]}
+
+
+def _qkv_layout(owner_name, owner, modules):
+    from ..models.kda import KDAProjections
+    from ..models.mla import LatentKVProjection, MLAProjections
+    spec = getattr(owner, "_kimi_head_spec", None)
+    if spec is not None:
+        nh, hd = spec
+        return getattr(owner, "_kimi_role"), HeadMatrixLayout(nh, hd, 0, owner.in_features, owner.local_out_features)
+    parent_name, _, attr = owner_name.rpartition(".")
+    parent = modules.get(parent_name)
+    if isinstance(parent, KDAProjections) and attr in ("q_proj", "k_proj", "v_proj"):
+        role = {"q_proj": "attention_q", "k_proj": "attention_k", "v_proj": "attention_v"}[attr]
+        hd = parent.config.value_head_dim if attr == "v_proj" else parent.config.key_head_dim
+    elif isinstance(parent, MLAProjections) and attr == "query":
+        role, hd = "attention_q", parent.config.q_head_dim
+    elif isinstance(parent, LatentKVProjection) and attr in ("key_up", "value_up"):
+        role = "attention_k" if attr == "key_up" else "attention_v"
+        hd = parent.config.q_head_dim if attr == "key_up" else parent.config.v_head_dim
+    else:
+        return None
+    return role, HeadMatrixLayout(parent.config.num_heads, hd, 0, owner.in_features, owner.out_features)
+
+
+def _is_norm(name, owner):
+    return "norm" in name.lower() or isinstance(owner, (nn.LayerNorm, nn.BatchNorm1d, nn.BatchNorm2d, nn.GroupNorm))
+
+
+def build_parameter_registry(model: nn.Module, *, kind: str = "per_head_muon_adamw",
+                             strict: bool = True) -> ParameterAssignmentReport:
+    """Assign every trainable tensor to one optimizer family (reference rules).
+
+    Stacked routed-expert weights (``[E, H, L]``) are Muon matrices (one per expert).
+    """
+    from ..models.moe import GroupedRoutedExperts
+    modules = dict(model.named_modules())
+    owner_by_name = {}
+    for mname, module in modules.items():
+        for local, _ in module.named_parameters(recurse=False):
+            owner_by_name[f"{mname}.{local}" if mname else local] = (mname, module)
+    specs, seen, duplicates, ambiguous = [], {}, [], []
+    for name, p in model.named_parameters():
+        if not p.requires_grad:
+            continue
+        if id(p) in seen:
+            duplicates.append(name)
+            continue
+        seen[id(p)] = name
+        owner_name, owner = owner_by_name[name]
+        qkv = _qkv_layout(owner_name, owner, modules)
+        role, layout = "other", None
+        explicit = getattr(owner, "_kimi_role", None)
+        parallel_linear = bool(getattr(owner, "_kimi_parallel_linear", False))
+        no_decay = (p.ndim < 2 or name.endswith(".bias") or isinstance(owner, nn.Embedding) or _is_norm(name, owner)
+                    or "lm_head" in name or "pseudo_query" in name or explicit in ("embedding", "lm_head"))
+        stacked = isinstance(owner, GroupedRoutedExperts)
+        if qkv is not None:
+            role, layout = qkv
+        elif stacked:
+            role = "moe_routed_expert"
+        elif explicit is not None:
+            role = explicit
+        elif isinstance(owner, nn.Embedding):
+            role = "embedding"
+        elif "lm_head" in name:
+            role = "lm_head"
+        elif _is_norm(name, owner):
+            role = "norm"
+        elif isinstance(owner, nn.Linear):
+            low = name.lower()
+            if ".router." in low:
+                role = "moe_router"
+            elif "shared_experts" in low:
+                role = "moe_shared_expert"
+            elif "routed_experts" in low:
+                role = "moe_routed_expert"
+            elif "output_proj" in low:
+                role = "attention_o"
+            elif low.startswith("mtp.") or ".mtp." in low:
+                role = "mtp_matrix"
+            else:
+                role = "dense_matrix"
+        matrix_like = (isinstance(owner, nn.Linear) or parallel_linear) and p.ndim == 2
+        if kind == "adamw":
+            family = "adamw_no_decay" if no_decay else "adamw_decay"
+        elif layout is not None and kind == "per_head_muon_adamw":
+            family = "per_head_muon"
+        elif (matrix_like and not no_decay and role != "moe_router") or (stacked and p.ndim == 3):
+            family = "muon"
+        else:
+            family = "adamw_no_decay" if no_decay else "adamw_decay"
+        if strict and matrix_like and role == "other":
+            ambiguous.append(name)
+        specs.append(MatrixParameterSpec(name, p, owner_name, role, family,
+                                         family in ("adamw_decay", "muon", "per_head_muon"),
+                                         layout if family == "per_head_muon" else None))
+    trainable = {id(p): n for n, p in model.named_parameters() if p.requires_grad}
+    assigned = {id(s.parameter) for s in specs}
+    missing = tuple(n for i, n in trainable.items() if i not in assigned)
+    if strict and (missing or duplicates or ambiguous):
+        raise RuntimeError(f"invalid parameter registry: missing={missing}, duplicates={duplicates}, "
+                           f"ambiguous={ambiguous}")
+    fams = ("adamw_decay", "adamw_no_decay", "muon", "per_head_muon")
+    numel = {f: sum(s.parameter.numel() for s in specs if s.optimizer_family == f) for f in fams}
+    count = {f: sum(1 for s in specs if s.optimizer_family == f) for f in fams}
+    total = max(sum(numel.values()), 1)
+    pct = {f: 100.0 * numel[f] / total for f in fams}
+    fp = hashlib.sha256(json.dumps([s.fingerprint_record() for s in specs], sort_keys=True).encode()).hexdigest()
+    return ParameterAssignmentReport(tuple(specs), numel, count, pct, missing, tuple(duplicates), tuple(ambiguous), fp)
+
+
+# --------------------------------------------------------------------------- Muon
+@dataclass
+class _MatrixSlot:
+    param: torch.Tensor
+    count: int           # matrices contributed by this parameter
+    rows: int
+    cols: int
+    to_blocks: callable  # tensor shaped like param -> [count, rows, cols]
+    from_blocks: callable
+
+
+class KimiMuon(torch.optim.Optimizer):
+    """Muon over equal-shape matrix buckets (batched Newton-Schulz per bucket)."""
+
+    def __init__(self, params, *, lr, momentum, nesterov, ns_steps, eps, weight_decay, update_rms_scaling,
+                 spec_by_parameter: dict, ns_dtype: str = "auto"):
+        if lr <= 0 or not 0 <= momentum < 1 or ns_steps <= 0 or eps <= 0 or weight_decay < 0:
+            raise ValueError("invalid Muon configuration")
+        super().__init__(params, dict(lr=lr, momentum=momentum, nesterov=nesterov, ns_steps=ns_steps, eps=eps,
+                                      weight_decay=weight_decay, update_rms_scaling=update_rms_scaling))
+        self.spec_by_parameter = spec_by_parameter
+        self.ns_dtype = ns_dtype
+        self.last_update_metrics: dict = {}
+        self._metric_tensors: dict = {}
+        self._slots = {}
+        for group in self.param_groups:
+            for p in group["params"]:
+                if p.ndim not in (2, 3):
+                    raise ValueError("Muon parameters must be 2D (or stacked 3D experts)")
+                self._slots[id(p)] = self._make_slot(p)
+
+    def _make_slot(self, p) -> _MatrixSlot:
+        spec = self.spec_by_parameter.get(id(p))
+        if spec is not None and spec.optimizer_family == "per_head_muon" and spec.head_layout is not None \
+                and spec.head_layout.head_axis == 0 and spec.head_layout.packed_kind == "separate":
+            hl = spec.head_layout
+            return _MatrixSlot(p, hl.num_heads, hl.head_dim, p.shape[1],
+                               lambda t, hl=hl: t.reshape(hl.num_heads, hl.head_dim, t.shape[-1]),
+                               lambda b, p=p: b.reshape(p.shape))
+        if p.ndim == 3:
+            return _MatrixSlot(p, p.shape[0], p.shape[1], p.shape[2], lambda t: t, lambda b: b)
+        return _MatrixSlot(p, 1, p.shape[0], p.shape[1], lambda t: t[None], lambda b: b[0])
+
+    def _resolved_ns_dtype(self, device) -> torch.dtype:
+        if self.ns_dtype == "float32" or (self.ns_dtype == "auto" and device.type != "cuda"):
+            return torch.float32
+        return torch.bfloat16
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        if closure is not None:
+            with torch.enable_grad():
+                closure()
+        metrics = {"raw": [], "ortho": [], "scaled": [], "ratio": []}
+        for group in self.param_groups:
+            lr, mom, wd = group["lr"], group["momentum"], group["weight_decay"]
+            buckets: dict = {}
+            for p in group["params"]:
+                if p.grad is None:
+                    continue
+                st = self.state[p]
+                buf = st.get("momentum_buffer")
+                if buf is None:
+                    buf = st["momentum_buffer"] = torch.zeros_like(p.grad)
+                buf.mul_(mom).add_(p.grad)
+                raw = p.grad.add(buf, alpha=mom) if group["nesterov"] else buf
+                slot = self._slots[id(p)]
+                buckets.setdefault((slot.rows, slot.cols, p.device), []).append((p, slot, raw))
+            for (rows, cols, dev), items in buckets.items():
+                stacked = torch.cat([s.to_blocks(r).float() for _, s, r in items], 0)
+                ortho = batched_newton_schulz(stacked, steps=group["ns_steps"], eps=group["eps"],
+                                              dtype=self._resolved_ns_dtype(dev))
+                metrics["raw"].append(stacked.flatten(1).square().mean(1).sqrt())
+                metrics["ortho"].append(ortho.flatten(1).square().mean(1).sqrt())
+                if group["update_rms_scaling"]:
+                    ortho = ortho * (max(rows, cols) ** 0.5)
+                metrics["scaled"].append(ortho.flatten(1).square().mean(1).sqrt())
+                off = 0
+                for p, slot, _ in items:
+                    upd = slot.from_blocks(ortho[off:off + slot.count]).to(p.dtype)
+                    off += slot.count
+                    prms = p.float().square().mean().sqrt()
+                    metrics["ratio"].append((lr * upd.float().square().mean().sqrt() / prms.clamp_min(group["eps"]))[None])
+                    if wd:
+                        p.mul_(1.0 - lr * wd)
+                    p.add_(upd, alpha=-lr)
+        self._metric_tensors = {k: torch.cat(v) for k, v in metrics.items() if v}
+        self.last_update_metrics = {}
+        return self._metric_tensors
+
+    def update_metrics(self) -> dict:
+        """Materialise the last step's update statistics (one device-to-host copy)."""
+        if not self._metric_tensors:
+            return {}
+        keys = ("raw", "ortho", "scaled", "ratio")
+        vals = torch.stack([self._metric_tensors[k].float().mean() for k in keys]).tolist()
+        raw, ortho, scaled, ratio = vals
+        self.last_update_metrics = {"muon/raw_update_rms": raw, "muon/orthogonal_update_rms": ortho,
+                                    "muon/scaled_update_rms": scaled, "muon/ns_gain": scaled / max(raw, 1e-12),
+                                    "muon/update_to_parameter_ratio": ratio}
+        return self.last_update_metrics
+
+
+# --------------------------------------------------------------------------- QK-Clip
+@dataclass
+class QKClipReport:
+    applied: bool
+    events: int
+    fraction_layers_clipped: float
+    max_preclip_scale: float
+    max_postclip_scale: float
+    mean_rescale_factor: float
+    min_rescale_factor: float
+    consecutive_steps_active: int
+
+    def metrics(self) -> dict:
+        return {"qk_clip/applied": float(self.applied), "qk_clip/events": float(self.events),
+                "qk_clip/fraction_layers_clipped": self.fraction_layers_clipped,
+                "qk_clip/max_preclip_scale": self.max_preclip_scale,
+                "qk_clip/max_postclip_scale": self.max_postclip_scale,
+                "qk_clip/mean_rescale_factor": self.mean_rescale_factor,
+                "qk_clip/min_rescale_factor": self.min_rescale_factor,
+                "qk_clip/consecutive_steps_active": float(self.consecutive_steps_active)}
+
+
+class QKClipController:
+    """After each step: if ``s = rms(q) rms(k) sqrt(d) > tau`` scale W_q and W_k by ``sqrt(tau/s)``.
+
+    Scales of every MLA layer are stacked, reduced (MAX over the TP group) in one
+    collective and applied on the device.
+    """
+
+    def __init__(self, model, *, threshold, eps=1e-6, every_steps=1, include_kda_experimental=False):
+        from ..models.kda import KimiDeltaAttention
+        from ..models.mla import GatedMLA
+        if threshold <= 0 or eps <= 0 or every_steps <= 0:
+            raise ValueError("invalid QK-Clip configuration")
+        self.threshold, self.eps, self.every_steps = float(threshold), float(eps), int(every_steps)
+        self.layers = []
+        for name, m in model.named_modules():
+            custom = getattr(m, "_kimi_qk_weights", None)
+            if custom is not None:
+                self.layers.append((name, m, custom[0], custom[1]))
+            elif isinstance(m, GatedMLA):
+                self.layers.append((name, m, m.projections.query.weight, m.projections.latent_kv.key_up.weight))
+            elif include_kda_experimental and isinstance(m, KimiDeltaAttention):
+                self.layers.append((name, m, m.projections.q_proj.weight, m.projections.k_proj.weight))
+        self.total_events = 0
+        self.consecutive_steps_active = 0
+        self._pending = None
+
+    @torch.no_grad()
+    def apply(self, step: int, *, materialize: bool = True):
+        if step % self.every_steps:
+            return QKClipReport(False, 0, 0.0, 0.0, 0.0, 1.0, 1.0, self.consecutive_steps_active)
+        active = [(m, wq, wk) for _, m, wq, wk in self.layers if getattr(m, "_last_qk_scale", None) is not None]
+        if not active:
+            return QKClipReport(False, 0, 0.0, 0.0, 0.0, 1.0, 1.0, self.consecutive_steps_active)
+        scales = torch.stack([m._last_qk_scale.detach().float().reshape(()) for m, _, _ in active])
+        group = getattr(active[0][0], "_kimi_qk_group", None)
+        if group is not None and torch.distributed.is_initialized() and torch.distributed.get_world_size(group) > 1:
+            torch.distributed.all_reduce(scales, op=torch.distributed.ReduceOp.MAX, group=group)
+        corr = torch.where(scales > self.threshold, self.threshold / scales.clamp_min(self.eps),
+                           torch.ones_like(scales)).clamp(max=1.0)
+        sym = corr.sqrt()
+        for i, (_, wq, wk) in enumerate(active):
+            wq.mul_(sym[i].to(wq.dtype))
+            wk.mul_(sym[i].to(wk.dtype))
+        self._pending = (scales, corr, len(self.layers))
+        return self.report() if materialize else None
+
+    def report(self) -> QKClipReport:
+        if self._pending is None:
+            return QKClipReport(False, 0, 0.0, 0.0, 0.0, 1.0, 1.0, self.consecutive_steps_active)
+        scales, corr, n = self._pending
+        self._pending = None
+        s, c = scales.tolist(), corr.tolist()
+        if any(not math.isfinite(v) for v in s):
+            raise FloatingPointError("QK scale proxy is non-finite")
+        factors = [f for f, v in zip(c, s) if v > self.threshold]
+        events = len(factors)
+        self.total_events += events
+        self.consecutive_steps_active = self.consecutive_steps_active + 1 if events else 0
+        return QKClipReport(bool(events), events, events / max(n, 1), max(s, default=0.0),
+                            max([min(v, self.threshold) for v in s], default=0.0),
+                            sum(factors) / len(factors) if factors else 1.0, min(factors, default=1.0),
+                            self.consecutive_steps_active)
+
+    def state_dict(self) -> dict:
+        return {"threshold": self.threshold, "eps": self.eps, "every_steps": self.every_steps,
+                "total_events": self.total_events, "consecutive_steps_active": self.consecutive_steps_active}
+
+    def load_state_dict(self, state: dict) -> None:
+        for key in ("threshold", "eps", "every_steps"):
+            if float(state[key]) != float(getattr(self, key)):
+                raise ValueError(f"QK-Clip {key} is incompatible")
+        self.total_events = int(state["total_events"])
+        self.consecutive_steps_active = int(state["consecutive_steps_active"])
+
+
+# --------------------------------------------------------------------------- hybrid
+@dataclass
+class OptimizerStepReport:
+    executed: bool
+    adamw_lr: float
+    muon_lr: float
+    qk_clip_applied: bool
+    qk_clip_events: int
+    nonfinite_parameters: int
+    update_metrics: dict = field(default_factory=dict)
+
+
+def _all_finite(tensors) -> torch.Tensor:
+    """Single device boolean: every tensor is finite."""
+    if not tensors:
+        return torch.ones((), dtype=torch.bool)
+    norms = torch._foreach_norm([t.float() if t.dtype not in (torch.float32, torch.float64) else t
+                                 for t in tensors], 2.0)
+    return torch.isfinite(torch.stack(norms)).all()
+
+
+class KimiHybridOptimizer:
+    """Muon (matrices) + AdamW (rest) + QK-Clip; a non-finite gradient skips the whole step."""
+
+    def __init__(self, muon, adamw, report, config, qk_clip):
+        self.muon, self.adamw, self.report, self.config, self.qk_clip = muon, adamw, report, config, qk_clip
+        self.step_number = 0
+        self.last_step_report: OptimizerStepReport | None = None
+
+    @property
+    def param_groups(self):
+        return self.muon.param_groups + self.adamw.param_groups
+
+    @property
+    def defaults(self):
+        return {"muon": self.muon.defaults, "adamw": self.adamw.defaults}
+
+    def zero_grad(self, set_to_none: bool = True) -> None:
+        self.muon.zero_grad(set_to_none=set_to_none)
+        self.adamw.zero_grad(set_to_none=set_to_none)
+
+    @torch.no_grad()
+    def step(self, closure=None, *, gradients_known_finite: bool = False) -> OptimizerStepReport:
+        if closure is not None:
+            with torch.enable_grad():
+                closure()
+        params = [p for g in self.param_groups for p in g["params"] if p.grad is not None]
+        if not gradients_known_finite:
+            if not bool(_all_finite([p.grad for p in params])):
+                bad = sum(int(not torch.isfinite(p.grad).all()) for p in params)
+                rep = OptimizerStepReport(False, self.adamw.param_groups[0]["lr"], self.muon.param_groups[0]["lr"],
+                                          False, 0, bad, {})
+                self.last_step_report = rep
+                return rep
+        self.muon.step()
+        self.adamw.step()
+        self.step_number += 1
+        if self.qk_clip is not None:
+            self.qk_clip.apply(self.step_number, materialize=False)
+        rep = OptimizerStepReport(True, self.adamw.param_groups[0]["lr"], self.muon.param_groups[0]["lr"], False, 0,
+                                  0, {})
+        self.last_step_report = rep
+        return rep
+
+    def materialize_report(self) -> OptimizerStepReport:
+        """Fill the last report's metrics (Muon statistics, QK-Clip) with one host sync each."""
+        rep = self.last_step_report
+        if rep is None or not rep.executed:
+            return rep
+        metrics = dict(self.muon.update_metrics())
+        if self.qk_clip is not None:
+            clip = self.qk_clip.report()
+            metrics.update(clip.metrics())
+            rep.qk_clip_applied, rep.qk_clip_events = clip.applied, clip.events
+        rep.update_metrics = metrics
+        return rep
+
+    def set_lr(self, lr: float, muon_lr: float | None = None) -> None:
+        if lr < 0 or (muon_lr is not None and muon_lr < 0):
+            raise ValueError("learning rates must be non-negative")
+        for g in self.adamw.param_groups:
+            g["lr"] = lr
+        for g in self.muon.param_groups:
+            g["lr"] = lr if muon_lr is None else muon_lr
+
+    def set_lrs(self, *, adamw_lr: float, muon_lr: float) -> None:
+        self.set_lr(adamw_lr, muon_lr)
+
+    def get_lrs(self) -> dict:
+        return {"adamw_lr": float(self.adamw.param_groups[0]["lr"]), "muon_lr": float(self.muon.param_groups[0]["lr"])}
+
+    def parameter_assignment_report(self):
+        return self.report
+
+    def state_dict(self) -> dict:
+        return {"format_version": 1, "muon": self.muon.state_dict(), "adamw": self.adamw.state_dict(),
+                "parameter_registry_fingerprint": self.report.fingerprint, "parameter_registry": self.report.to_dict(),
+                "config": self.config.to_dict(),
+                "qk_clip": None if self.qk_clip is None else self.qk_clip.state_dict(),
+                "step_number": self.step_number}
+
+    def load_state_dict(self, state: dict, strict: bool = True) -> None:
+        if strict and state.get("parameter_registry_fingerprint") != self.report.fingerprint:
+            raise ValueError("optimizer parameter registry fingerprint mismatch")
+        self.muon.load_state_dict(state["muon"])
+        self.adamw.load_state_dict(state["adamw"])
+        if self.qk_clip is not None and state.get("qk_clip") is not None:
+            self.qk_clip.load_state_dict(state["qk_clip"])
+        self.step_number = int(state.get("step_number", 0))
+
+
+def build_kimi_optimizer(model, config: KimiOptimizerConfig | None = None):
+    """Build ``(optimizer, registry)``: AdamW only, or Muon/Per-Head Muon + AdamW (+ QK-Clip)."""
+    config = config or KimiOptimizerConfig()
+    reg = build_parameter_registry(model, kind=config.kind, strict=config.fail_on_unclassified_matrix)
+    decay = [s.parameter for s in reg.specs if s.optimizer_family == "adamw_decay"]
+    no_decay = [s.parameter for s in reg.specs if s.optimizer_family == "adamw_no_decay"]
+    fused = bool(decay + no_decay) and all(p.is_cuda for p in decay + no_decay)
+    groups = [{"params": decay, "weight_decay": config.weight_decay, "group_name": "adamw_decay"},
+              {"params": no_decay, "weight_decay": 0.0, "group_name": "adamw_no_decay"}]
+    if config.kind == "adamw":
+        return torch.optim.AdamW(groups, lr=config.adamw_lr, betas=config.adamw_betas, eps=config.adamw_eps,
+                                 fused=fused or None), reg
+    muon_specs = [s for s in reg.specs if s.optimizer_family in ("muon", "per_head_muon")]
+    if not muon_specs:
+        raise RuntimeError("Kimi optimizer found no Muon matrices")
+    muon = KimiMuon([{"params": [s.parameter for s in muon_specs]}], lr=config.resolved_muon_lr,
+                    momentum=config.muon_momentum, nesterov=config.muon_nesterov, ns_steps=config.muon_ns_steps,
+                    eps=config.muon_ns_eps, weight_decay=config.resolved_muon_weight_decay,
+                    update_rms_scaling=config.muon_update_rms_scaling,
+                    spec_by_parameter={id(s.parameter): s for s in muon_specs}, ns_dtype=config.muon_ns_dtype)
+    adamw = torch.optim.AdamW(groups, lr=config.adamw_lr, betas=config.adamw_betas, eps=config.adamw_eps,
+                              fused=fused or None)
+    qk = (QKClipController(model, threshold=config.qk_clip_threshold, eps=config.qk_clip_eps,
+                           every_steps=config.qk_clip_every_steps,
+                           include_kda_experimental=config.qk_clip_kda_experimental)
+          if config.qk_clip_enabled else None)
+    return KimiHybridOptimizer(muon, adamw, reg, config, qk), reg
+
+
+__all__ = [
+    "KimiOptimizerConfig", "zeropower_via_newton_schulz", "batched_newton_schulz", "match_update_rms",
+    "HeadMatrixLayout", "split_head_matrix", "merge_head_matrix", "per_head_orthogonalize", "MatrixParameterSpec",
+    "ParameterAssignmentReport", "build_parameter_registry", "KimiMuon", "QKClipReport", "QKClipController",
+    "OptimizerStepReport", "KimiHybridOptimizer", "build_kimi_optimizer",
+]

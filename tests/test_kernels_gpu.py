@@ -1,0 +1,285 @@
+"""Numerics of every sm_100a kernel against a plain fp32 PyTorch reference of the same op."""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+def _close(a, b, tol):
+    a, b = a.float(), b.float()
+    err = (a - b).abs().max().item()
+    scale = max(b.abs().max().item(), 1e-6)
+    assert err <= tol * scale, f"max err {err:.3e} vs scale {scale:.3e} (tol {tol})"
+
+
+def _grads(fn, inputs, gout):
+    for t in inputs:
+        t.grad = None
+    out = fn(*inputs)
+    out.backward(gout)
+    return out.detach(), [t.grad.detach().clone() for t in inputs]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("shape,period", [((64, 37, 640), 1), ((8, 50, 10, 64), 10)])
+def test_rms_norm(cuda, dtype, shape, period):
+    from kimi_k3_b200 import ops
+    from kimi_k3_b200.models.primitives import rms_norm_reference
+    torch.manual_seed(0)
+    x = torch.randn(shape, device=cuda).to(dtype).requires_grad_()
+    w = (1 + 0.1 * torch.randn((period, shape[-1]) if period > 1 else (shape[-1],), device=cuda)).requires_grad_()
+    g = torch.randn(shape, device=cuda).to(dtype)
+    if period > 1:
+        y1, (dx1, dw1) = _grads(lambda a, b: ops.rms_norm(a.reshape(-1, shape[-1]), b, 1e-6, period).reshape(shape),
+                                [x, w], g)
+        y2, (dx2, dw2) = _grads(lambda a, b: rms_norm_reference(a.float(), None, 1e-6) * b[None, None].float(),
+                                [x, w], g)
+    else:
+        y1, (dx1, dw1) = _grads(lambda a, b: ops.rms_norm(a, b, 1e-6), [x, w], g)
+        y2, (dx2, dw2) = _grads(lambda a, b: rms_norm_reference(a.float(), b, 1e-6), [x, w], g)
+    tol = 2e-2 if dtype == torch.bfloat16 else 1e-5
+    _close(y1, y2, tol)
+    _close(dx1, dx2, tol * 2)
+    _close(dw1, dw2, tol * 2)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_situ_and_sigmoid_gate(cuda, dtype):
+    from kimi_k3_b200 import ops
+    torch.manual_seed(1)
+    gt = (3 * torch.randn(1000, 333, device=cuda)).to(dtype).requires_grad_()
+    ut = (20 * torch.randn(1000, 333, device=cuda)).to(dtype).requires_grad_()
+    go = torch.randn(1000, 333, device=cuda).to(dtype)
+    ref = lambda g, u: 4 * torch.tanh(g.float() / 4) * torch.sigmoid(g.float()) * 25 * torch.tanh(u.float() / 25)
+    y1, d1 = _grads(lambda g, u: ops.situ_glu(g, u, 4.0, 25.0), [gt, ut], go)
+    y2, d2 = _grads(ref, [gt, ut], go)
+    tol = 2e-2 if dtype == torch.bfloat16 else 1e-5
+    _close(y1, y2, tol)
+    for a, b in zip(d1, d2):
+        _close(a, b, tol * 2)
+    y1, d1 = _grads(ops.sigmoid_mul, [gt, ut], go)
+    y2, d2 = _grads(lambda z, x: torch.sigmoid(z.float()) * x.float(), [gt, ut], go)
+    _close(y1, y2, tol)
+    for a, b in zip(d1, d2):
+        _close(a, b, tol * 2)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_kda_decay(cuda, dtype):
+    from kimi_k3_b200 import ops
+    torch.manual_seed(2)
+    z = (2 * torch.randn(4, 33, 10, 64, device=cuda)).to(dtype).requires_grad_()
+    a = (0.3 * torch.randn(10, device=cuda)).requires_grad_()
+    gout = torch.randn(4, 33, 10, 64, device=cuda)
+    eps = torch.finfo(dtype).eps
+
+    def ref(z_, a_):
+        p = torch.sigmoid(a_.exp()[None, None, :, None] * z_.float()).clamp(eps, 1 - eps)
+        return -5.0 * p
+
+    y1, d1 = _grads(lambda z_, a_: ops.kda_decay(z_, a_, -5.0), [z, a], gout)
+    y2, d2 = _grads(ref, [z, a], gout)
+    _close(y1, y2, 1e-5)
+    _close(d1[0], d2[0], 2e-2 if dtype == torch.bfloat16 else 1e-5)
+    _close(d1[1], d2[1], 1e-4)
+
+
+@pytest.mark.parametrize("normalize", [True, False])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_conv_silu_norm(cuda, dtype, normalize):
+    from kimi_k3_b200 import ops
+    torch.manual_seed(3)
+    b, t, c, hd = 3, 70, 640, 64
+    x = torch.randn(b, t, c, device=cuda).to(dtype).requires_grad_()
+    w = (0.3 * torch.randn(c, 4, device=cuda)).requires_grad_()
+    gout = torch.randn(b, t, c, device=cuda).to(dtype)
+
+    def ref(x_, w_):
+        y = F.conv1d(F.pad(x_.float().transpose(1, 2), (3, 0)), w_.flip(-1).unsqueeze(1), groups=c).transpose(1, 2)
+        s = F.silu(y)
+        if normalize:
+            s = F.normalize(s.reshape(b, t, c // hd, hd), dim=-1, eps=1e-6).reshape(b, t, c)
+        return s
+
+    y1, d1 = _grads(lambda x_, w_: ops.conv_silu_norm(x_, w_, hd, 1e-6, normalize), [x, w], gout)
+    y2, d2 = _grads(ref, [x, w], gout)
+    tol = 2e-2 if dtype == torch.bfloat16 else 2e-5
+    _close(y1, y2, tol)
+    _close(d1[0], d2[0], tol * 2)
+    _close(d1[1], d2[1], tol * 2)
+
+
+def _kda_inputs(cuda, b, t, h, dtype, seed=4):
+    torch.manual_seed(seed)
+    q = F.normalize(torch.randn(b, t, h, 64, device=cuda), dim=-1).to(dtype)
+    k = F.normalize(torch.randn(b, t, h, 64, device=cuda), dim=-1).to(dtype)
+    v = torch.randn(b, t, h, 64, device=cuda).to(dtype)
+    g = -5.0 * torch.sigmoid(torch.randn(b, t, h, 64, device=cuda) - 2.0)
+    beta = torch.sigmoid(torch.randn(b, t, h, device=cuda))
+    h0 = 0.1 * torch.randn(b, h, 64, 64, device=cuda)
+    return q, k, v, g, beta, h0
+
+
+@pytest.mark.parametrize("t", [64, 130, 257])
+def test_kda_chunk_forward_backward(cuda, t):
+    from kimi_k3_b200 import ops
+    from kimi_k3_b200.models.kda import chunkwise_kda
+    q, k, v, g, beta, h0 = _kda_inputs(cuda, 2, t, 3, torch.float32)
+    leaves = [x.clone().requires_grad_() for x in (q, k, v, g, beta, h0)]
+    leaves2 = [x.clone().requires_grad_() for x in (q, k, v, g, beta, h0)]
+    o1, s1 = ops.kda_chunk(*leaves[:5], leaves[5], True)
+    r = chunkwise_kda(*[x.double() for x in leaves2[:5]], leaves2[5].double(), True)
+    o2, s2 = r.hidden_states, r.final_state
+    _close(o1, o2, 1e-4)
+    _close(s1, s2, 1e-4)
+    go = torch.randn_like(o1)
+    gs = torch.randn_like(s1)
+    (o1 * go).sum().add_((s1 * gs).sum()).backward()
+    (o2 * go.double()).sum().add_((s2 * gs.double()).sum()).backward()
+    for a, b_, name in zip(leaves, leaves2, ("q", "k", "v", "g", "beta", "h0")):
+        err = (a.grad.double() - b_.grad).abs().max().item()
+        scale = b_.grad.abs().max().item()
+        assert err <= 2e-3 * max(scale, 1e-6), f"d{name}: {err} vs {scale}"
+
+
+def test_kda_chunk_bf16_matches_fp32(cuda):
+    from kimi_k3_b200 import ops
+    q, k, v, g, beta, _ = _kda_inputs(cuda, 4, 1024, 2, torch.bfloat16, seed=5)
+    o1, _ = ops.kda_chunk(q, k, v, g, beta, None, False)
+    from kimi_k3_b200.models.kda import chunkwise_kda
+    o2 = chunkwise_kda(q.float(), k.float(), v.float(), g, beta).hidden_states
+    _close(o1, o2, 3e-2)
+
+
+@pytest.mark.parametrize("causal,t,lengths", [(True, 1024, None), (True, 200, None), (False, 96, [96, 50])])
+def test_flash_attention(cuda, causal, t, lengths):
+    from kimi_k3_b200 import ops
+    torch.manual_seed(6)
+    b, h = 2, 3
+    q, k, v = (torch.randn(b, t, h, 64, device=cuda, dtype=torch.bfloat16).requires_grad_() for _ in range(3))
+    mask = None
+    if lengths is not None:
+        mask = torch.arange(t, device=cuda)[None, :] < torch.tensor(lengths, device=cuda)[:, None]
+
+    def ref(q_, k_, v_):
+        s = torch.einsum("bqhd,bkhd->bhqk", q_.float(), k_.float()) / 8.0
+        allow = torch.ones(t, t, dtype=torch.bool, device=cuda)
+        if causal:
+            allow = allow.tril()
+        allow = allow[None, None].expand(b, h, t, t)
+        if mask is not None:
+            allow = allow & mask[:, None, None, :]
+        p = torch.softmax(s.masked_fill(~allow, float("-inf")), -1)
+        return torch.einsum("bhqk,bkhd->bqhd", p, v_.float())
+
+    go = torch.randn(b, t, h, 64, device=cuda, dtype=torch.bfloat16)
+    y1, d1 = _grads(lambda a, b_, c: ops.flash_attention(a, b_, c, causal=causal, key_padding_mask=mask), [q, k, v], go)
+    y2, d2 = _grads(ref, [q, k, v], go.float())
+    _close(y1, y2, 2e-2)
+    for a, b_ in zip(d1, d2):
+        _close(a, b_, 3e-2)
+
+
+def test_router_topk(cuda):
+    from kimi_k3_b200 import ops
+    torch.manual_seed(7)
+    logits = torch.randn(500, 12, device=cuda).requires_grad_()
+    bias = 0.05 * torch.randn(12, device=cuda)
+    sel, raw_sel, w, cutoff, load, raw = ops.router_topk(logits, bias, 2, True, 1e-9, True)
+    raw_ref = torch.sigmoid(logits.float())
+    top_v, top_i = torch.topk(raw_ref + bias, 3, dim=-1)
+    assert torch.equal(sel, top_i[:, :2])
+    _close(cutoff, top_v[:, 2], 1e-6)
+    _close(raw, raw_ref, 1e-6)
+    assert torch.equal(load, torch.bincount(top_i[:, :2].reshape(-1), minlength=12))
+    gw = torch.randn_like(w)
+    (w * gw).sum().backward()
+    g1 = logits.grad.clone()
+    logits.grad = None
+    rs = raw_ref.gather(-1, top_i[:, :2])
+    wr = rs / rs.sum(-1, keepdim=True)
+    (wr * gw).sum().backward()
+    _close(g1, logits.grad, 1e-5)
+
+
+@pytest.mark.parametrize("nsrc", [1, 3, 6])
+def test_attnres_mix(cuda, nsrc):
+    from kimi_k3_b200 import ops
+    from kimi_k3_b200.models.attnres import depth_softmax_mix_reference
+    from kimi_k3_b200.models.primitives import RMSNorm
+    torch.manual_seed(8)
+    srcs = [torch.randn(2, 37, 640, device=cuda, dtype=torch.bfloat16).requires_grad_() for _ in range(nsrc)]
+    q = (0.3 * torch.randn(640, device=cuda)).requires_grad_()
+    norm = RMSNorm(640).to(cuda)
+    with torch.no_grad():
+        norm.weight.add_(0.1 * torch.randn(640, device=cuda))
+    go = torch.randn(2, 37, 640, device=cuda, dtype=torch.bfloat16)
+    y1 = ops.attnres_mix(srcs, q, norm.weight, 1e-6)
+    y1.backward(go)
+    g1 = [s.grad.clone() for s in srcs] + [q.grad.clone(), norm.weight.grad.clone()]
+    for t in srcs + [q, norm.weight]:
+        t.grad = None
+    stacked = torch.stack([s.float() for s in srcs], 2)
+    y2, _, _ = depth_softmax_mix_reference(stacked, q, norm)
+    y2.backward(go.float())
+    g2 = [s.grad for s in srcs] + [q.grad, norm.weight.grad]
+    _close(y1, y2, 2e-2)
+    for a, b_ in zip(g1, g2):
+        _close(a, b_, 3e-2)
+
+
+def test_linear_cross_entropy(cuda):
+    from kimi_k3_b200 import ops
+    torch.manual_seed(9)
+    n, d, v = 3000, 640, 50257
+    h = (0.5 * torch.randn(n, d, device=cuda)).to(torch.bfloat16).requires_grad_()
+    w = (0.02 * torch.randn(v, d, device=cuda)).requires_grad_()
+    t = torch.randint(0, v, (n,), device=cuda)
+    valid = torch.rand(n, device=cuda) > 0.1
+    loss = ops.linear_cross_entropy(h, w, t, valid, chunk_rows=1024)
+    (2.0 * loss).backward()
+    gh, gw = h.grad.clone(), w.grad.clone()
+    h.grad = w.grad = None
+    logits = h.float() @ w.t().float()
+    per = F.cross_entropy(logits, t, reduction="none")
+    ref = (per * valid.float()).sum()
+    (2.0 * ref).backward()
+    _close(loss, ref, 2e-3)
+    _close(gh, h.grad, 3e-2)
+    _close(gw, w.grad, 3e-2)
+
+
+def test_tiny_model_kernels_match_torch_path(cuda, monkeypatch):
+    """A small GPU model: the native-kernel step and the PyTorch-math step agree."""
+    from kimi_k3_b200.config.profiles import profile_model_mapping
+    from kimi_k3_b200.config.model_yaml import build_model_config_from_mapping
+    from kimi_k3_b200.models import KimiK3
+    m = profile_model_mapping("t4_wikitext")
+    m["model"].update(d_model=128, num_heads=2, num_hybrid_groups=1, vocab_size=1000)
+    m["model"]["moe"].update(latent_dim=64, shared_expert_hidden_dim=96, routed_expert_hidden_dim=64)
+    m["model"]["mla"]["kv_latent_dim"] = 128
+    cfg = build_model_config_from_mapping(m)
+    torch.manual_seed(10)
+    model = KimiK3(cfg).to(cuda)
+    ids = torch.randint(3, 1000, (2, 200), device=cuda)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        out1 = model(input_ids=ids, labels=ids, use_mtp=True, compute_logits=False)
+    out1.loss.backward()
+    g1 = {n: p.grad.clone() for n, p in model.named_parameters() if p.grad is not None}
+    model.zero_grad()
+    monkeypatch.setenv("KIMI_K3_KERNELS", "0")
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        out2 = model(input_ids=ids, labels=ids, use_mtp=True)
+    out2.loss.backward()
+    assert abs(out1.loss.item() - out2.loss.item()) < 2e-2 * out2.loss.item()
+    g2 = {n: p.grad for n, p in model.named_parameters() if p.grad is not None}
+    bad = []
+    for n in g2:
+        a, b_ = g1[n].float(), g2[n].float()
+        rel = (a - b_).norm() / b_.norm().clamp_min(1e-8)
+        if rel > 0.1:
+            bad.append((n, rel.item()))
+    assert not bad, bad[:10]
