@@ -227,7 +227,7 @@ def count_launches(engine, batch):
 
 
 # --------------------------------------------------------------------------- reference arm
-def run_reference(args, world, rank, local):
+def run_reference(args, world, rank, local, amp=True):
     ref = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref, "src")):
         raise FileNotFoundError("baseline/_ref is not installed")
@@ -285,7 +285,7 @@ def run_reference(args, world, rank, local):
             host["t1"] = time.perf_counter()
             barrier()
 
-    train_one_epoch(model, batches, opt, device=dev, scheduler=sched, amp_enabled=True, amp_dtype="bf16",
+    train_one_epoch(model, batches, opt, device=dev, scheduler=sched, amp_enabled=amp, amp_dtype="bf16",
                     grad_accum_steps=1, grad_clip=1.0, max_batches=len(batches), use_mtp=True,
                     moe_controller=RefMoEController(model), on_optimizer_step=on_step, distributed_context=context)
     clocks = sampler.stop()
@@ -322,8 +322,19 @@ def main():
         if not torch.cuda.is_available():
             raise RuntimeError("no CUDA device")
         init_dist(world, local)
-        fn = run_reference if args.impl == "reference" else run_ours
-        ms, e2e_ms, clocks, h2d, d2h, launches, last_loss = fn(args, world, rank, local)
+        if args.impl == "reference":
+            try:
+                ms, e2e_ms, clocks, h2d, d2h, launches, last_loss = run_reference(args, world, rank, local, amp=True)
+            except TypeError as exc:
+                # The reference's AttnRes stacks an fp32 embedding with bf16 sublayer outputs and
+                # rejects mixed dtypes, so its stock path cannot train this model under bf16
+                # autocast; fall back to the precision it does support.
+                base["dtype"] = "fp32"
+                base["note"] = f"reference bf16 autocast fails ({exc}); measured in fp32"
+                torch.cuda.empty_cache()
+                ms, e2e_ms, clocks, h2d, d2h, launches, last_loss = run_reference(args, world, rank, local, amp=False)
+        else:
+            ms, e2e_ms, clocks, h2d, d2h, launches, last_loss = run_ours(args, world, rank, local)
     except Exception as exc:
         if args.impl == "reference":
             if rank == 0:

@@ -8,6 +8,8 @@
 #include <vector>
 
 #include "kernels.h"
+#include "tc_gemm.h"
+#include "moe_route.h"
 
 namespace {
 
@@ -339,6 +341,190 @@ std::vector<at::Tensor> fa_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Ten
   return {dq, dk, dv};
 }
 
+
+// ---------------------------------------------------------------- tcgen05 GEMM
+// Logical C[M,N] = A[M,K] B[N,K]^T. a_mn: A given as [K, M]; b_mn: B given as [K, N] (or [G,K,N]).
+at::Tensor tc_gemm_dense(at::Tensor a, at::Tensor b, bool a_mn, bool b_mn, bool out_fp32, int64_t bn,
+                         c10::optional<at::Tensor> out_opt) {
+  CHECK_CUDA_CONTIG(a);
+  CHECK_CUDA_CONTIG(b);
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "tc_gemm takes bf16 operands");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2, "dense tc_gemm takes 2-D operands");
+  const at::cuda::CUDAGuard gd(a.device());
+  const int64_t M = a_mn ? a.size(1) : a.size(0), K = a_mn ? a.size(0) : a.size(1);
+  const int64_t N = b_mn ? b.size(1) : b.size(0);
+  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K, "inner dimensions differ");
+  TORCH_CHECK(N % 8 == 0 && K % 8 == 0 && M % 8 == 0, "tc_gemm needs M, N, K multiples of 8");
+  at::Tensor out = out_opt.has_value() && out_opt->defined() ? *out_opt
+                   : at::empty({M, N}, a.options().dtype(out_fp32 ? at::kFloat : at::kBFloat16));
+  kimi::TcGemmArgs g;
+  g.mode = 0;
+  g.bn = (int)bn;
+  g.a_mn = a_mn;
+  g.b_mn = b_mn;
+  g.a = a.data_ptr();
+  g.a_rows = a.size(0);
+  g.a_cols = a.size(1);
+  g.a_ld = a.size(1);
+  g.b = b.data_ptr();
+  g.b_groups = 1;
+  g.b_rows = b.size(0);
+  g.b_cols = b.size(1);
+  g.b_ld = b.size(1);
+  g.b_gstride = b.numel();
+  g.M = (int)M;
+  g.N = (int)N;
+  g.K = (int)K;
+  g.out = out.data_ptr();
+  g.out_fp32 = out.scalar_type() == at::kFloat;
+  g.ldc = out.stride(0);
+  int dev = a.get_device();
+  g.num_sms = at::cuda::getDeviceProperties(dev)->multiProcessorCount;
+  check(kimi::tc_gemm(g, stream()), "tc_gemm_dense");
+  return out;
+}
+
+// Grouped GEMM. mode 1: rows of `a` ([R, K] K-major) split by offsets (128-aligned); b is [G, N, K]
+// (b_mn=False) or [G, K, N] (b_mn=True); epi 0 store / 1 SiTU (b2 = up weights) / 2 scatter-add.
+// mode 2: reduction over row segments (64-aligned) of a ([R, M] MN-major) and b ([R, N] MN-major);
+// out is [G, M, N].
+std::vector<at::Tensor> tc_gemm_grouped(int64_t mode, at::Tensor a, at::Tensor b, c10::optional<at::Tensor> b2,
+                                        bool a_mn, bool b_mn, at::Tensor offsets, int64_t M, int64_t N, int64_t K,
+                                        int64_t epi, c10::optional<at::Tensor> out_opt, bool out_fp32, double bg,
+                                        double bu, c10::optional<at::Tensor> row_token,
+                                        c10::optional<at::Tensor> row_weight, int64_t b2_k_split, int64_t bn) {
+  TORCH_CHECK(a.is_cuda() && a.dim() == 2 && a.stride(1) == 1 && a.stride(0) % 8 == 0,
+              "a must be a row-major CUDA matrix with a 16-byte aligned row stride");
+  CHECK_CUDA_CONTIG(b);
+  const at::cuda::CUDAGuard gd(a.device());
+  TORCH_CHECK(offsets.scalar_type() == at::kInt && offsets.is_cuda(), "offsets must be int32 on device");
+  const int G = (int)offsets.numel() - 1;
+  kimi::TcGemmArgs g;
+  g.mode = (int)mode;
+  g.bn = (int)bn;
+  g.a_mn = a_mn;
+  g.b_mn = b_mn;
+  g.a = a.data_ptr();
+  g.a_rows = a.size(0);
+  g.a_cols = a.size(1);
+  g.a_ld = a.stride(0);
+  g.b = b.data_ptr();
+  at::Tensor b2t;
+  if (b2.has_value() && b2->defined()) {
+    b2t = b2->contiguous();
+    g.b2 = b2t.data_ptr();
+  }
+  if (b.dim() == 3) {
+    g.b_groups = b.size(0);
+    g.b_rows = b.size(1);
+    g.b_cols = b.size(2);
+    g.b_ld = b.size(2);
+    g.b_gstride = b.size(1) * b.size(2);
+  } else {
+    g.b_groups = 1;
+    g.b_rows = b.size(0);
+    g.b_cols = b.size(1);
+    g.b_ld = b.size(1);
+    g.b_gstride = b.numel();
+  }
+  g.b2_k_split = (int)b2_k_split;
+  g.M = (int)M;
+  g.N = (int)N;
+  g.K = (int)K;
+  g.G = G;
+  g.offsets = offsets.data_ptr<int>();
+  g.epi = (int)epi;
+  g.bg = (float)bg;
+  g.bu = (float)bu;
+  std::vector<at::Tensor> outs;
+  at::Tensor out;
+  if (out_opt.has_value() && out_opt->defined()) {
+    out = *out_opt;
+  } else if (mode == 2) {
+    out = at::empty({G, M, N}, a.options().dtype(out_fp32 ? at::kFloat : at::kBFloat16));
+  } else {
+    out = at::empty({a.size(0), N}, a.options().dtype(out_fp32 ? at::kFloat : at::kBFloat16));
+  }
+  g.out = out.data_ptr();
+  g.out_fp32 = out.scalar_type() == at::kFloat;
+  g.ldc = out.size(-1);
+  outs.push_back(out);
+  at::Tensor og, ou;
+  if (epi == 1) {
+    og = at::empty({a.size(0), N}, a.options());
+    ou = at::empty({a.size(0), N}, a.options());
+    g.out_g = og.data_ptr();
+    g.out_u = ou.data_ptr();
+    outs.push_back(og);
+    outs.push_back(ou);
+  }
+  at::Tensor rt, rw;
+  if (epi == 2) {
+    rt = row_token->contiguous();
+    rw = row_weight->to(at::kFloat).contiguous();
+    g.row_token = rt.data_ptr<int>();
+    g.row_weight = rw.data_ptr<float>();
+    g.ldc = out.size(-1);
+  }
+  g.num_sms = at::cuda::getDeviceProperties(a.get_device())->multiProcessorCount;
+  check(kimi::tc_gemm(g, stream()), "tc_gemm_grouped");
+  return outs;
+}
+
+
+// ---------------------------------------------------------------- MoE routing
+std::vector<at::Tensor> moe_route(at::Tensor sel, at::Tensor w, int64_t E, int64_t r_max) {
+  CHECK_CUDA_CONTIG(sel);
+  const at::cuda::CUDAGuard gd(sel.device());
+  auto i32 = sel.options().dtype(at::kInt);
+  const int64_t M = sel.size(0), k = sel.size(1);
+  auto wf = w.to(at::kFloat).contiguous();
+  auto counts = at::empty({E}, i32), offsets = at::empty({E + 1}, i32), cursor = at::empty({E}, i32);
+  auto row_token = at::empty({r_max}, i32), row_of = at::empty({M * k}, i32);
+  auto row_weight = at::zeros({r_max}, sel.options().dtype(at::kFloat));
+  check(kimi::moe_route_prep(sel.data_ptr<int64_t>(), wf.data_ptr<float>(), M, (int)k, (int)E, r_max,
+                             counts.data_ptr<int>(), offsets.data_ptr<int>(), cursor.data_ptr<int>(),
+                             row_token.data_ptr<int>(), row_weight.data_ptr<float>(), row_of.data_ptr<int>(),
+                             stream()), "moe_route_prep");
+  return {counts, offsets, row_token, row_weight, row_of};
+}
+
+at::Tensor moe_gather(at::Tensor latent, at::Tensor row_token) {
+  CHECK_CUDA_CONTIG(latent);
+  const at::cuda::CUDAGuard gd(latent.device());
+  auto xs = at::empty({row_token.size(0), latent.size(1)}, latent.options());
+  check(kimi::moe_gather(latent.data_ptr(), row_token.data_ptr<int>(), xs.data_ptr(), row_token.size(0),
+                         latent.size(1), stream()), "moe_gather");
+  return xs;
+}
+
+std::vector<at::Tensor> moe_dy(at::Tensor dagg, at::Tensor row_token, at::Tensor row_weight, at::Tensor y) {
+  const at::cuda::CUDAGuard gd(y.device());
+  dagg = dagg.to(at::kFloat).contiguous();
+  auto dy = at::empty_like(y);
+  auto dw_row = at::empty({y.size(0)}, y.options().dtype(at::kFloat));
+  check(kimi::moe_dy(dagg.data_ptr<float>(), row_token.data_ptr<int>(), row_weight.data_ptr<float>(), y.data_ptr(),
+                     dy.data_ptr(), dw_row.data_ptr<float>(), y.size(0), y.size(1), stream()), "moe_dy");
+  return {dy, dw_row};
+}
+
+at::Tensor moe_slot_sum(at::Tensor dxs, at::Tensor row_of, int64_t M, int64_t k, bool out_fp32) {
+  const at::cuda::CUDAGuard gd(dxs.device());
+  auto out = at::empty({M, dxs.size(1)}, dxs.options().dtype(out_fp32 ? at::kFloat : at::kBFloat16));
+  check(kimi::moe_slot_sum(dxs.data_ptr(), row_of.data_ptr<int>(), out.data_ptr(), out_fp32, M, (int)k,
+                           dxs.size(1), stream()), "moe_slot_sum");
+  return out;
+}
+
+at::Tensor situ_bwd_cat(at::Tensor dh, at::Tensor g, at::Tensor u, double bg, double bu) {
+  const at::cuda::CUDAGuard gd(g.device());
+  dh = dh.contiguous();
+  auto dgu = at::empty({g.size(0), 2 * g.size(1)}, g.options());
+  check(kimi::situ_bwd_cat(dh.data_ptr(), g.data_ptr(), u.data_ptr(), dgu.data_ptr(), g.size(0), g.size(1),
+                           (float)bg, (float)bu, stream()), "situ_bwd_cat");
+  return dgu;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -361,4 +547,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kda_bwd", &kda_bwd);
   m.def("fa_fwd", &fa_fwd);
   m.def("fa_bwd", &fa_bwd);
+  m.def("tc_gemm_dense", &tc_gemm_dense);
+  m.def("tc_gemm_grouped", &tc_gemm_grouped);
+  m.def("moe_route", &moe_route);
+  m.def("moe_gather", &moe_gather);
+  m.def("moe_dy", &moe_dy);
+  m.def("moe_slot_sum", &moe_slot_sum);
+  m.def("situ_bwd_cat", &situ_bwd_cat);
 }

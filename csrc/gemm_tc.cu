@@ -1,0 +1,459 @@
+// Persistent warp-specialised tcgen05 GEMM for sm_100a:  C = A * B^T  (bf16 in, fp32 accumulate).
+//
+//   warp 0      TMA producer: A and B tiles (128B-swizzled) into a STAGES-deep smem ring
+//   warp 1      MMA issuer: tcgen05.mma (M=128, N=BN, K=16) into one of two TMEM accumulators;
+//               allocates / frees TMEM
+//   warps 2..5  epilogue: tcgen05.ld of the finished accumulator (one row per thread) and a fused
+//               store, overlapping the MMAs of the next tile (double-buffered TMEM)
+//
+// Modes:  0 dense;  1 grouped over M (row segments of A, one B matrix per segment: MoE experts);
+//         2 grouped over K (reduction over row segments, one C matrix per segment: expert weight
+//           gradients).  Segment offsets are device arrays (multiples of 128 rows in mode 1 and of
+//           64 rows in mode 2), so the launch shape never depends on the routing.
+// Operands may be K-major or MN-major (``a_mn`` / ``b_mn``), which covers the forward and both
+// backward products without transposed copies.
+// Epilogues:  0 store (bf16 or fp32), 1 SiTU-GLU of a (gate | up) tile pair (stores h, gate, up),
+//             2 weighted scatter-add into fp32 rows (row_token[r] < 0 skips the row).
+// TMA loads never use cluster multicast; every mbarrier wait is bounded (status word).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "tc_common.cuh"
+#include "tc_gemm.h"
+
+namespace kimi {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+
+struct DevParams {
+  CUtensorMap map_a;
+  CUtensorMap map_b;
+  CUtensorMap map_b2;
+  int mode, M, N, K, G;
+  const int* offsets;
+  int b2_k_split;  // k-blocks at k >= split read map_b2 at (k - split); 0 = off
+  int situ;        // B tile = [gate 128 rows | up 128 rows] from map_b / map_b2
+  int epi;
+  void* out;
+  int out_fp32;
+  int64_t ldc;
+  void* out_g;
+  void* out_u;
+  float bg, bu;
+  const int* row_token;
+  const float* row_weight;
+  int* status;
+};
+
+struct TileInfo {
+  int g;        // group
+  int m0;       // A row coordinate (mode 0/1) or C row (mode 2)
+  int n0;       // C column
+  int k0;       // first reduction coordinate
+  int num_kb;   // k blocks
+  int c_row0;   // output row base (modes 0/1: m0; mode 2: m within group)
+};
+
+template <int BNT>
+__device__ __forceinline__ int tiles_n_of(const DevParams& p) {
+  return (p.N + BNT - 1) / BNT;
+}
+
+template <int BNT>
+__device__ int total_tiles(const DevParams& p) {
+  const int tn = tiles_n_of<BNT>(p);
+  if (p.mode == 0) return ((p.M + BM - 1) / BM) * tn;
+  if (p.mode == 1) {
+    int t = 0;
+    for (int g = 0; g < p.G; ++g) t += ((p.offsets[g + 1] - p.offsets[g]) / BM) * tn;
+    return t;
+  }
+  return p.G * ((p.M + BM - 1) / BM) * tn;
+}
+
+template <int BNT>
+__device__ TileInfo tile_info(const DevParams& p, int tile) {
+  const int tn = tiles_n_of<BNT>(p);
+  TileInfo ti;
+  if (p.mode == 0) {
+    const int tm = (p.M + BM - 1) / BM;
+    ti.g = 0;
+    ti.m0 = (tile % tm) * BM;
+    ti.n0 = (tile / tm) * BNT;
+    ti.k0 = 0;
+    ti.num_kb = (p.K + BK - 1) / BK;
+    ti.c_row0 = ti.m0;
+    return ti;
+  }
+  if (p.mode == 1) {
+    int g = 0, base = 0;
+    for (; g < p.G; ++g) {
+      const int tg = ((p.offsets[g + 1] - p.offsets[g]) / BM) * tn;
+      if (tile < base + tg) break;
+      base += tg;
+    }
+    const int local = tile - base;
+    const int tm = (p.offsets[g + 1] - p.offsets[g]) / BM;
+    ti.g = g;
+    ti.m0 = p.offsets[g] + (local % tm) * BM;
+    ti.n0 = (local / tm) * BNT;
+    ti.k0 = 0;
+    ti.num_kb = (p.K + BK - 1) / BK;
+    ti.c_row0 = ti.m0;
+    return ti;
+  }
+  const int tm = (p.M + BM - 1) / BM;
+  const int per = tm * tn;
+  ti.g = tile / per;
+  const int local = tile % per;
+  ti.m0 = (local % tm) * BM;
+  ti.n0 = (local / tm) * BNT;
+  ti.k0 = p.offsets[ti.g];
+  ti.num_kb = (p.offsets[ti.g + 1] - p.offsets[ti.g]) / BK;
+  ti.c_row0 = ti.m0;
+  return ti;
+}
+
+__device__ __forceinline__ float situ_fwd(float g, float u, float bg, float bu) {
+  return bg * tanhf(g / bg) * (1.f / (1.f + expf(-g))) * bu * tanhf(u / bu);
+}
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ DevParams p) {
+  constexpr int A_BYTES = BM * BK * 2;
+  constexpr int B_BYTES = BN * BK * 2;
+  constexpr int STAGE = A_BYTES + B_BYTES;
+  constexpr int STAGES = BN == 256 ? 4 : 6;
+  constexpr int TMEM_COLS = 2 * BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bnt = p.situ ? BN / 2 : BN;  // output columns per tile
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&tfull[b], 1);
+      tc::mbar_init(&tempty[b], 128);
+    }
+    tc::fence_barrier_init();
+    tc::fence_proxy_async();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tslot, TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tc::tma_prefetch(&p.map_a);
+    tc::tma_prefetch(&p.map_b);
+    if (p.situ || p.b2_k_split) tc::tma_prefetch(&p.map_b2);
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = *tslot;
+  const int total = p.situ ? total_tiles<BN / 2>(p) : total_tiles<BN>(p);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+        const TileInfo ti = p.situ ? tile_info<BN / 2>(p, tile) : tile_info<BN>(p, tile);
+        for (int kb = 0; kb < ti.num_kb; ++kb) {
+          tc::mbar_wait(&empty[s], ph ^ 1, p.status, tc::kTimeoutEmpty);
+          uint8_t* sa = smem + s * STAGE;
+          uint8_t* sb = sa + A_BYTES;
+          tc::mbar_arrive_expect_tx(&full[s], STAGE);
+          const int k = ti.k0 + kb * BK;
+          if (!A_MN) {
+            tc::tma_load_2d(sa, &p.map_a, &full[s], k, ti.m0);
+          } else {
+            tc::tma_load_2d(sa, &p.map_a, &full[s], ti.m0, k);
+            tc::tma_load_2d(sa + A_BYTES / 2, &p.map_a, &full[s], ti.m0 + 64, k);
+          }
+          const CUtensorMap* mb = &p.map_b;
+          int kb_coord = k;
+          if (p.b2_k_split && k >= p.b2_k_split) {
+            mb = &p.map_b2;
+            kb_coord = k - p.b2_k_split;
+          }
+          if (p.situ) {
+            tc::tma_load_3d(sb, &p.map_b, &full[s], kb_coord, ti.n0, ti.g);
+            tc::tma_load_3d(sb + B_BYTES / 2, &p.map_b2, &full[s], kb_coord, ti.n0, ti.g);
+          } else if (!B_MN) {
+            tc::tma_load_3d(sb, mb, &full[s], kb_coord, ti.n0, p.mode == 2 ? 0 : ti.g);
+          } else {
+#pragma unroll
+            for (int q = 0; q < BN / 64; ++q)
+              tc::tma_load_3d(sb + q * (BK * 64 * 2), mb, &full[s], ti.n0 + q * 64, kb_coord,
+                              p.mode == 2 ? 0 : ti.g);
+          }
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = tc::instr_desc_f16(BM, BN, true, A_MN, B_MN);
+      int s = 0, it = 0;
+      uint32_t ph = 0;
+      for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+        const TileInfo ti = p.situ ? tile_info<BN / 2>(p, tile) : tile_info<BN>(p, tile);
+        const int buf = it & 1;
+        const uint32_t tph = (it >> 1) & 1;
+        tc::mbar_wait(&tempty[buf], tph ^ 1, p.status, tc::kTimeoutTmemEmpty);
+        tc::tc_fence_after();
+        const uint32_t d = tmem_base + buf * BN;
+        for (int kb = 0; kb < ti.num_kb; ++kb) {
+          tc::mbar_wait(&full[s], ph, p.status, tc::kTimeoutFull);
+          tc::tc_fence_after();
+          const uint32_t base_a = tc::smem_u32(smem + s * STAGE);
+          const uint32_t base_b = base_a + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? tc::smem_desc_sw128(base_a + kk * 2048, 8192, 1024)
+                                     : tc::smem_desc_sw128(base_a + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? tc::smem_desc_sw128(base_b + kk * 2048, 8192, 1024)
+                                     : tc::smem_desc_sw128(base_b + kk * 32, 16, 1024);
+            tc::mma_f16(d, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc::mma_commit(&empty[s]);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        tc::mma_commit(&tfull[buf]);
+      }
+    }
+  } else {
+    const int sub = warp & 3;
+    const int r_local = sub * 32 + lane;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+      const TileInfo ti = p.situ ? tile_info<BN / 2>(p, tile) : tile_info<BN>(p, tile);
+      const int buf = it & 1;
+      const uint32_t tph = (it >> 1) & 1;
+      tc::mbar_wait(&tfull[buf], tph, p.status, tc::kTimeoutTmemFull);
+      tc::tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + buf * BN;
+      const int row = ti.c_row0 + r_local;
+      const bool row_ok = (p.mode == 1) ? true : row < p.M;
+      for (int c0 = 0; c0 < bnt; c0 += 32) {
+        float v[32];
+        if (ti.num_kb > 0) {
+          tc::tmem_ld_32x32b_x32(taddr + c0, v);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        }
+        const int col0 = ti.n0 + c0;
+        if (p.situ) {
+          float u[32];
+          if (ti.num_kb > 0) {
+            tc::tmem_ld_32x32b_x32(taddr + bnt + c0, u);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) u[i] = 0.f;
+          }
+          if (row_ok) {
+            __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldc;
+            __nv_bfloat16* og = reinterpret_cast<__nv_bfloat16*>(p.out_g) + (int64_t)row * p.ldc;
+            __nv_bfloat16* ou = reinterpret_cast<__nv_bfloat16*>(p.out_u) + (int64_t)row * p.ldc;
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              if (col0 + i + 8 <= p.N) {
+                Vec<__nv_bfloat16> vh, vg, vu;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const float gq = to_f<__nv_bfloat16>(from_f<__nv_bfloat16>(v[i + j]));
+                  const float uq = to_f<__nv_bfloat16>(from_f<__nv_bfloat16>(u[i + j]));
+                  vg.v[j] = from_f<__nv_bfloat16>(gq);
+                  vu.v[j] = from_f<__nv_bfloat16>(uq);
+                  vh.v[j] = from_f<__nv_bfloat16>(situ_fwd(gq, uq, p.bg, p.bu));
+                }
+                vh.store(h + col0 + i);
+                vg.store(og + col0 + i);
+                vu.store(ou + col0 + i);
+              }
+            }
+          }
+        } else if (p.epi == 2) {
+          if (row_ok) {
+            const int tok = p.row_token[row];
+            if (tok >= 0) {
+              const float w = p.row_weight[row];
+              float* o = reinterpret_cast<float*>(p.out) + (int64_t)tok * p.ldc;
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (col0 + i < p.N) atomicAdd(o + col0 + i, w * v[i]);
+            }
+          }
+        } else if (row_ok) {
+          const int64_t goff = p.mode == 2 ? (int64_t)ti.g * p.M * p.ldc : 0;
+          if (p.out_fp32) {
+            float* o = reinterpret_cast<float*>(p.out) + goff + (int64_t)row * p.ldc;
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              if (col0 + i + 4 <= p.N) *reinterpret_cast<float4*>(o + col0 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+          } else {
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + goff + (int64_t)row * p.ldc;
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              if (col0 + i + 8 <= p.N) {
+                Vec<__nv_bfloat16> vo;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) vo.v[j] = from_f<__nv_bfloat16>(v[i + j]);
+                vo.store(o + col0 + i);
+              }
+            }
+          }
+        }
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(&tempty[buf]);
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  if (warp == 1) tc::tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 3-D bf16 map: dims (d0 innermost, d1, d2), strides in bytes for d1 and d2, box (b0, b1, 1), 128B swizzle.
+bool make_map(CUtensorMap* m, const void* ptr, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1, uint64_t s2,
+              uint32_t b0, uint32_t b1) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {s1, s2};
+  cuuint32_t box[3] = {b0, b1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool make_map_2d(CUtensorMap* m, const void* ptr, uint64_t d0, uint64_t d1, uint64_t s1, uint32_t b0, uint32_t b1) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {d0, d1};
+  cuuint64_t strides[1] = {s1};
+  cuuint32_t box[2] = {b0, b1};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, bool AMN, bool BMN>
+cudaError_t launch(const DevParams& dp, int num_sms, cudaStream_t s) {
+  constexpr int STAGES = BN == 256 ? 4 : 6;
+  constexpr int STAGE = BM * BK * 2 + BN * BK * 2;
+  const size_t smem = 1024 + (size_t)STAGES * STAGE + (2 * STAGES + 4) * 8 + 16;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, AMN, BMN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  gemm_tc_kernel<BN, AMN, BMN><<<num_sms, 192, smem, s>>>(dp);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t tc_gemm(const TcGemmArgs& a, cudaStream_t stream) {
+  DevParams dp{};
+  dp.mode = a.mode;
+  dp.M = a.M;
+  dp.N = a.N;
+  dp.K = a.K;
+  dp.G = a.G;
+  dp.offsets = a.offsets;
+  dp.b2_k_split = a.b2_k_split;
+  dp.situ = a.epi == 1 ? 1 : 0;
+  dp.epi = a.epi;
+  dp.out = a.out;
+  dp.out_fp32 = a.out_fp32 ? 1 : 0;
+  dp.ldc = a.ldc;
+  dp.out_g = a.out_g;
+  dp.out_u = a.out_u;
+  dp.bg = a.bg;
+  dp.bu = a.bu;
+  dp.row_token = a.row_token;
+  dp.row_weight = a.row_weight;
+  dp.status = a.status;
+  const int bn = a.epi == 1 ? 256 : a.bn;
+  if (bn != 128 && bn != 256) return cudaErrorInvalidValue;
+  if (a.epi == 1 && (a.a_mn || a.b_mn || !a.b2)) return cudaErrorInvalidValue;
+  // A: K-major storage [a_rows, a_cols=K]; MN-major storage [a_rows=K, a_cols=M]
+  if (!a.a_mn) {
+    if (!make_map_2d(&dp.map_a, a.a, a.a_cols, a.a_rows, a.a_ld * 2, 64, 128)) return cudaErrorInvalidValue;
+  } else {
+    if (!make_map_2d(&dp.map_a, a.a, a.a_cols, a.a_rows, a.a_ld * 2, 64, 64)) return cudaErrorInvalidValue;
+  }
+  // B: K-major storage [G, N, K]; MN-major storage [G, K, N]
+  const uint32_t bbox_rows = a.epi == 1 ? 128 : (uint32_t)bn;
+  const void* bptrs[2] = {a.b, a.b2};
+  CUtensorMap* bmaps[2] = {&dp.map_b, &dp.map_b2};
+  for (int i = 0; i < 2; ++i) {
+    if (!bptrs[i]) {
+      dp.map_b2 = dp.map_b;
+      continue;
+    }
+    bool ok;
+    if (!a.b_mn)
+      ok = make_map(bmaps[i], bptrs[i], a.b_cols, a.b_rows, a.b_groups, a.b_ld * 2, a.b_gstride * 2, 64, bbox_rows);
+    else
+      ok = make_map(bmaps[i], bptrs[i], a.b_cols, a.b_rows, a.b_groups, a.b_ld * 2, a.b_gstride * 2, 64, 64);
+    if (!ok) return cudaErrorInvalidValue;
+  }
+  int sms = a.num_sms > 0 ? a.num_sms : 148;
+#define KIMI_TC_LAUNCH(BN_, AM_, BM_) return launch<BN_, AM_, BM_>(dp, sms, stream)
+  if (bn == 256) {
+    if (!a.a_mn && !a.b_mn) KIMI_TC_LAUNCH(256, false, false);
+    if (!a.a_mn && a.b_mn) KIMI_TC_LAUNCH(256, false, true);
+    if (a.a_mn && !a.b_mn) KIMI_TC_LAUNCH(256, true, false);
+    KIMI_TC_LAUNCH(256, true, true);
+  }
+  if (!a.a_mn && !a.b_mn) KIMI_TC_LAUNCH(128, false, false);
+  if (!a.a_mn && a.b_mn) KIMI_TC_LAUNCH(128, false, true);
+  if (a.a_mn && !a.b_mn) KIMI_TC_LAUNCH(128, true, false);
+  KIMI_TC_LAUNCH(128, true, true);
+#undef KIMI_TC_LAUNCH
+}
+
+}  // namespace kimi

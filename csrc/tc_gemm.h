@@ -1,0 +1,39 @@
+// Host interface of the tcgen05 GEMM (gemm_tc.cu).
+//   C = A * B^T with bf16 operands and fp32 accumulation.
+//   A storage: K-major [a_rows = M_total, a_cols = K] or MN-major [a_rows = K_total, a_cols = M] (a_ld elems).
+//   B storage: K-major [b_groups, b_rows = N, b_cols = K] or MN-major [b_groups, b_rows = K, b_cols = N]
+//              (row stride b_ld elems, group stride b_gstride elems).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace kimi {
+
+struct TcGemmArgs {
+  int mode = 0;  // 0 dense, 1 grouped over M rows, 2 grouped over K rows
+  int bn = 128;  // 128 or 256 output columns per tile (SiTU always uses 256 = 128 gate + 128 up)
+  bool a_mn = false, b_mn = false;
+  const void* a = nullptr;
+  int64_t a_rows = 0, a_cols = 0, a_ld = 0;
+  const void* b = nullptr;
+  const void* b2 = nullptr;  // SiTU "up" weights, or the second half of a concatenated K
+  int64_t b_groups = 1, b_rows = 0, b_cols = 0, b_ld = 0, b_gstride = 0;
+  int b2_k_split = 0;
+  int M = 0, N = 0, K = 0, G = 1;
+  const int* offsets = nullptr;  // device [G+1]
+  int epi = 0;                   // 0 store, 1 SiTU, 2 weighted scatter-add (fp32)
+  void* out = nullptr;
+  bool out_fp32 = false;
+  int64_t ldc = 0;
+  void* out_g = nullptr;
+  void* out_u = nullptr;
+  float bg = 4.f, bu = 25.f;
+  const int* row_token = nullptr;
+  const float* row_weight = nullptr;
+  int* status = nullptr;
+  int num_sms = 0;
+};
+
+cudaError_t tc_gemm(const TcGemmArgs& args, cudaStream_t stream);
+
+}  // namespace kimi

@@ -411,6 +411,9 @@ class KimiK3(nn.Module):
                 image_counts=image_counts, video_counts=video_counts, vision_encoder=self.vision_encoder,
                 vision_token_packer=self.vision_token_packer, vision_projector=self.vision_projector,
                 composer=self.multimodal_composer, output_hidden_states=hidden_flag, output_attentions=attn_flag)
+        if torch.is_autocast_enabled(emb.device.type) and emb.is_floating_point():
+            # Keep the whole residual stream (AttnRes sources) in the autocast dtype.
+            emb = emb.to(torch.get_autocast_dtype(emb.device.type))
         bo = self.backbone(emb, attention_mask=attention_mask, cache=cache, use_cache=use_cache, mode=mode,
                            output_hidden_states=hidden_flag, output_depth_weights=attnres_flag,
                            output_diagnostics=router_flag or attnres_flag, update_routing_bias=update_routing_bias)

@@ -395,10 +395,13 @@ class GatedMLA(nn.Module):
             return GatedMLAOutput(out, None, None, None)
         current_mask = torch.ones(b, t, dtype=torch.bool, device=dev) if attention_mask is None else attention_mask
         prev = torch.zeros(b, dtype=torch.long, device=dev) if cache is None else cache.sequence_offset
-        base = (MLACache.empty(b, c.kv_latent_dim, device=dev, dtype=hidden_states.dtype) if cache is None else cache)
+        # The cache stores latents in the dtype the compression produces (bf16 under autocast).
+        base = (MLACache.empty(b, c.kv_latent_dim, device=dev, dtype=latent.dtype) if cache is None else cache)
         if cache is not None:
-            if cache.latent_kv.shape[-1] != c.kv_latent_dim or cache.latent_kv.dtype != hidden_states.dtype:
-                raise ValueError("cache latent dimension/dtype does not match")
+            if cache.latent_kv.shape[-1] != c.kv_latent_dim:
+                raise ValueError("cache latent dimension does not match config")
+            if cache.latent_kv.dtype != latent.dtype:
+                latent = latent.to(cache.latent_kv.dtype)
         updated = base.append(latent, current_mask)
         if fast_decode:
             # Weight-absorbed decode: attend over the latent cache; K/V never rebuilt.

@@ -472,7 +472,8 @@ class StableLatentMoE(nn.Module):
 
     # ---- routed path (overridable by expert parallelism)
     def routed_aggregate(self, latent, ro: RouterOutput, accumulation_dtype):
-        if _ops.use_kernels(latent) and accumulation_dtype == torch.float32:
+        if (_ops.use_kernels(latent) and accumulation_dtype == torch.float32 and latent.shape[-1] % 64 == 0
+                and self.config.routed_expert_hidden_dim % 128 == 0):
             return _ops.moe_grouped_experts(latent, ro.selected_experts, ro.selected_weights,
                                             self.routed_experts.gate_proj, self.routed_experts.up_proj,
                                             self.routed_experts.down_proj, self.config.beta_gate, self.config.beta_up)

@@ -303,7 +303,10 @@ class KimiMTPHead(nn.Module):
                 if torch.unique(row_s[row_m]).numel() > 1:
                     raise ValueError("packed segment execution is not supported by the KDA/MLA cache")
         src = view.source_hidden.detach() if self.config.detach_backbone_hidden else view.source_hidden
-        fused = self.fusion(src, self.input_embeddings(view.future_input_ids))
+        future = self.input_embeddings(view.future_input_ids)
+        if future.dtype != src.dtype:
+            future = future.to(src.dtype)  # bf16 residual stream under autocast
+        fused = self.fusion(src, future)
         hidden, bdiag = self._run_compacted(fused, build_mtp_feature_mask(attention_mask, input_ids),
                                             output_hidden_states=return_hidden_states,
                                             output_diagnostics=return_diagnostics,
@@ -343,7 +346,8 @@ class KimiMTPHead(nn.Module):
             raise ValueError("intermediate_token_id must be an integer tensor of shape [B,1]")
         if tuple(source_hidden_t.shape) != (intermediate_token_id.shape[0], 1, self.config.d_model):
             raise ValueError("source_hidden_t must have shape [B,1,D]")
-        fused = self.fusion(source_hidden_t, self.input_embeddings(intermediate_token_id))
+        future = self.input_embeddings(intermediate_token_id)
+        fused = self.fusion(source_hidden_t, future.to(source_hidden_t.dtype))
         out = self.block(fused, cache=cache, use_cache=True, mode="prefill" if cache is None else "decode")
         h = out.last_hidden_state
         return MTPDraftOutput(self.lm_head(h), out.cache, h)

@@ -285,32 +285,67 @@ def qb_histogram(raw_scores, cutoffs, counts, underflow, overflow, min_margin, m
     counts.add_(torch.bincount(flat.reshape(-1), minlength=e * bins).reshape(e, bins))
 
 
+class _MoEGrouped(torch.autograd.Function):
+    """Routed experts as grouped tcgen05 GEMMs over 128-row aligned expert segments.
+
+    Forward: device routing -> gather -> [gate|up] GEMM with the SiTU-GLU epilogue ->
+    down GEMM with a weighted scatter-add epilogue into the fp32 aggregate.
+    Backward: recompute Y, dY / d(weight), dH = dY Wd, dWd = dY^T H, SiTU backward,
+    dX = [dG|dU] [Wg; Wu], dWg / dWu = [dG|dU]^T X, then the per-token slot sum.
+    """
+
+    @staticmethod
+    def forward(ctx, latent, weights, selected, gate_w, up_w, down_w, bg, bu):
+        C = _C()
+        m, l = latent.shape
+        k = selected.shape[1]
+        e, h, _ = gate_w.shape
+        r_max = m * k + e * 128
+        bf = torch.bfloat16
+        x = latent.to(bf).contiguous()
+        wg, wu, wd = (w.to(bf).contiguous() for w in (gate_w, up_w, down_w))
+        _, offsets, row_token, row_weight, row_of = C.moe_route(selected.contiguous(), weights.detach(), e, r_max)
+        xs = C.moe_gather(x, row_token)
+        hh, gg, uu = C.tc_gemm_grouped(1, xs, wg, wu, False, False, offsets, r_max, h, l, 1, None, False, bg, bu,
+                                       None, None, 0, 256)
+        agg = torch.zeros(m, l, device=latent.device, dtype=torch.float32)
+        C.tc_gemm_grouped(1, hh, wd, None, False, False, offsets, r_max, l, h, 2, agg, True, bg, bu, row_token,
+                          row_weight, 0, 128)
+        ctx.save_for_backward(xs, gg, uu, hh, wg, wu, wd, offsets, row_token, row_weight, row_of)
+        ctx.c = (m, k, e, h, l, r_max, float(bg), float(bu), latent.dtype, gate_w.dtype)
+        ctx.mark_non_differentiable()
+        return agg
+
+    @staticmethod
+    def backward(ctx, dagg):
+        C = _C()
+        xs, gg, uu, hh, wg, wu, wd, offsets, row_token, row_weight, row_of = ctx.saved_tensors
+        m, k, e, h, l, r_max, bg, bu, ldt, wdt = ctx.c
+        y, = C.tc_gemm_grouped(1, hh, wd, None, False, False, offsets, r_max, l, h, 0, None, False, bg, bu, None, None,
+                               0, 128)
+        dy, dw_row = C.moe_dy(dagg, row_token, row_weight, y)
+        dh, = C.tc_gemm_grouped(1, dy, wd, None, False, True, offsets, r_max, h, l, 0, None, False, bg, bu, None, None,
+                                0, 128)
+        dwd, = C.tc_gemm_grouped(2, dy, hh, None, True, True, offsets, l, h, r_max, 0, None, True, bg, bu, None, None,
+                                 0, 128)
+        dgu = C.situ_bwd_cat(dh, gg, uu, bg, bu)
+        dxs, = C.tc_gemm_grouped(1, dgu, wg, wu, False, True, offsets, r_max, l, 2 * h, 0, None, False, bg, bu, None,
+                                 None, h, 128)
+        dwg, = C.tc_gemm_grouped(2, dgu[:, :h], xs, None, True, True, offsets, h, l, r_max, 0, None, True, bg, bu,
+                                 None, None, 0, 128)
+        dwu, = C.tc_gemm_grouped(2, dgu[:, h:], xs, None, True, True, offsets, h, l, r_max, 0, None, True, bg, bu,
+                                 None, None, 0, 128)
+        dlat = C.moe_slot_sum(dxs, row_of, m, k, ldt == torch.float32)
+        dweights = dw_row.index_select(0, row_of.long().clamp_min(0)).view(m, k)
+        return dlat.to(ldt), dweights, None, dwg.to(wdt), dwu.to(wdt), dwd.to(wdt), None, None
+
+
 def moe_grouped_experts(latent, selected, weights, gate_w, up_w, down_w, beta_gate, beta_up):
-    """``sum_k w_k E_{sel_k}(latent)`` in fp32 via expert-sorted grouped GEMMs."""
-    m, l = latent.shape
-    k = selected.shape[1]
-    e_count = gate_w.shape[0]
-    dt = _act_dtype(latent)
-    x = latent.to(dt)
-    flat_e = selected.reshape(-1)
-    order = torch.argsort(flat_e, stable=True)
-    tok = order // k
-    counts = torch.bincount(flat_e, minlength=e_count).tolist()
-    xs = x.index_select(0, tok)
-    outs = []
-    start = 0
-    for e, cnt in enumerate(counts):
-        if cnt == 0:
-            continue
-        xe = xs[start:start + cnt]
-        g = xe @ gate_w[e].to(dt).t()
-        u = xe @ up_w[e].to(dt).t()
-        outs.append(situ_glu(g, u, beta_gate, beta_up) @ down_w[e].to(dt).t())
-        start += cnt
-    ys = torch.cat(outs, 0) if outs else xs.new_zeros(0, l)
-    w_sorted = weights.reshape(-1).index_select(0, order).float()
-    agg = torch.zeros(m, l, device=latent.device, dtype=torch.float32)
-    return agg.index_add(0, tok, ys.float() * w_sorted[:, None])
+    """``sum_k w_k E_{sel_k}(latent)`` in fp32 (routed experts, grouped tcgen05 GEMMs)."""
+    l, h = latent.shape[1], gate_w.shape[1]
+    if l % 64 or h % 128:
+        raise NotImplementedError("grouped expert GEMMs need latent % 64 == 0 and hidden % 128 == 0")
+    return _MoEGrouped.apply(latent, weights, selected, gate_w, up_w, down_w, float(beta_gate), float(beta_up))
 
 
 # --------------------------------------------------------------------------- AttnRes

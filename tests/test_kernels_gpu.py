@@ -259,7 +259,7 @@ def test_tiny_model_kernels_match_torch_path(cuda, monkeypatch):
     from kimi_k3_b200.models import KimiK3
     m = profile_model_mapping("t4_wikitext")
     m["model"].update(d_model=128, num_heads=2, num_hybrid_groups=1, vocab_size=1000)
-    m["model"]["moe"].update(latent_dim=64, shared_expert_hidden_dim=96, routed_expert_hidden_dim=64)
+    m["model"]["moe"].update(latent_dim=64, shared_expert_hidden_dim=96, routed_expert_hidden_dim=128)
     m["model"]["mla"]["kv_latent_dim"] = 128
     cfg = build_model_config_from_mapping(m)
     torch.manual_seed(10)
