@@ -246,7 +246,7 @@ def chunkwise_kda(q, k, v, g, beta, initial_state=None, output_final_state=False
                   chunk_size=64, secondary_tile_size=16, accumulate_state_in_fp32=True) -> KDAOperatorOutput:
     """Chunked UT/WY KDA; the per-chunk algebra is batched over all chunks and
     only the ``[K,V]`` state recurrence runs sequentially."""
-    if chunk_size <= 0 or secondary_tile_size <= 0 or secondary_tile_size > chunk_size:
+    if chunk_size <= 0 or secondary_tile_size <= 0:
         raise ValueError("invalid chunk_size / secondary_tile_size")
     b, t, h, kd, vd = _validate_core(q, k, v, g, beta, initial_state, attention_mask)
     act = v.dtype

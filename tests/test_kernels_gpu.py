@@ -253,7 +253,8 @@ def test_linear_cross_entropy(cuda):
 
 
 def test_tiny_model_kernels_match_torch_path(cuda, monkeypatch):
-    """A small GPU model: the native-kernel step and the PyTorch-math step agree."""
+    """A small GPU model: the native-kernel bf16 step is as close to the fp32 PyTorch step as the
+    PyTorch bf16 step is (bf16 rounding sets the tolerance, measured per parameter)."""
     from kimi_k3_b200.config.profiles import profile_model_mapping
     from kimi_k3_b200.config.model_yaml import build_model_config_from_mapping
     from kimi_k3_b200.models import KimiK3
@@ -264,22 +265,27 @@ def test_tiny_model_kernels_match_torch_path(cuda, monkeypatch):
     cfg = build_model_config_from_mapping(m)
     torch.manual_seed(10)
     model = KimiK3(cfg).to(cuda)
+    snapshot = {k: v.clone() for k, v in model.state_dict().items()}
     ids = torch.randint(3, 1000, (2, 200), device=cuda)
-    with torch.autocast("cuda", dtype=torch.bfloat16):
-        out1 = model(input_ids=ids, labels=ids, use_mtp=True, compute_logits=False)
-    out1.loss.backward()
-    g1 = {n: p.grad.clone() for n, p in model.named_parameters() if p.grad is not None}
-    model.zero_grad()
-    monkeypatch.setenv("KIMI_K3_KERNELS", "0")
-    with torch.autocast("cuda", dtype=torch.bfloat16):
-        out2 = model(input_ids=ids, labels=ids, use_mtp=True)
-    out2.loss.backward()
-    assert abs(out1.loss.item() - out2.loss.item()) < 2e-2 * out2.loss.item()
-    g2 = {n: p.grad for n, p in model.named_parameters() if p.grad is not None}
+
+    def run(kernels: bool, autocast: bool):
+        model.load_state_dict(snapshot)  # routing bias may move inside a training forward
+        model.zero_grad()
+        monkeypatch.setenv("KIMI_K3_KERNELS", "1" if kernels else "0")
+        with torch.autocast("cuda", dtype=torch.bfloat16, enabled=autocast):
+            out = model(input_ids=ids, labels=ids, use_mtp=True, compute_logits=False)
+        out.loss.backward()
+        return out.loss.item(), {n: p.grad.float().clone() for n, p in model.named_parameters() if p.grad is not None}
+
+    l_exact, g_exact = run(False, False)
+    l_torch, g_torch = run(False, True)
+    l_kern, g_kern = run(True, True)
+    assert abs(l_kern - l_exact) < 2e-2 * l_exact
     bad = []
-    for n in g2:
-        a, b_ = g1[n].float(), g2[n].float()
-        rel = (a - b_).norm() / b_.norm().clamp_min(1e-8)
-        if rel > 0.1:
-            bad.append((n, rel.item()))
+    for n, ge in g_exact.items():
+        scale = ge.norm().clamp_min(1e-8)
+        e_torch = ((g_torch[n] - ge).norm() / scale).item()
+        e_kern = ((g_kern[n] - ge).norm() / scale).item()
+        if e_kern > 2.0 * e_torch + 0.03:
+            bad.append((n, e_kern, e_torch))
     assert not bad, bad[:10]
