@@ -163,14 +163,16 @@ def run_ours(args, world, rank, local):
                                           min_muon_lr=3e-5, prepare_first_update=True)
     engine = TrainStepEngine(model, opt, scheduler=sched, grad_clip=1.0, amp_dtype=torch.bfloat16, use_mtp=True,
                              moe_controller=MoEController(model, reducer=reducer.qb_reducer() if reducer else None),
-                             grad_hook=reducer.all_reduce_gradients if reducer else None)
+                             grad_hook=reducer.all_reduce_gradients if reducer else None,
+                             cuda_graph=not args.no_graph and world == 1)
     bpg = args.batch_per_gpu
     dev_batches = make_batches(4, bpg, SEQ, VOCAB, seed=1000 + rank, device=dev)
     host_batches = make_batches(4, bpg, SEQ, VOCAB, seed=2000 + rank, pin=True)
 
     def device_loop(n, start=0):
         for i in range(n):
-            engine.step(dev_batches[(start + i) % len(dev_batches)])
+            # synthetic batches carry an all-True mask (no padding): tell the engine
+            engine.step(dev_batches[(start + i) % len(dev_batches)], mask_all_valid=True)
 
     device_loop(args.warmup)
     torch.cuda.synchronize()
@@ -196,6 +198,7 @@ def run_ours(args, world, rank, local):
     for i in range(args.steps):
         out = engine.step(host_batches[i % len(host_batches)])
         losses.append(float(out.loss.item()))
+    engine.finish()
     torch.cuda.synchronize()
     barrier()
     e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1000.0 / args.steps)
@@ -209,7 +212,7 @@ def count_launches(engine, batch):
     try:
         from torch.profiler import ProfilerActivity, profile
         with profile(activities=[ProfilerActivity.CUDA]) as prof:
-            engine.step(batch)
+            engine.step(batch, mask_all_valid=True)
             torch.cuda.synchronize()
         mine = total = 0
         for ev in prof.events():
@@ -303,6 +306,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--batch-per-gpu", type=int, default=16)
+    ap.add_argument("--no-graph", action="store_true", help="eager steps instead of one CUDA graph per step")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

@@ -175,15 +175,22 @@ __global__ void attnres_bwd_kernel(SrcPtrs<T> src, int S, const float* __restric
       }
     }
   }
+  // Reduce the per-warp accumulators in shared memory, then one global atomic per element
+  // per block (instead of one per warp: the grid has ~1k blocks of 8 warps).
+  extern __shared__ float sacc[];  // dim
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) sacc[i] = 0.f;
+  __syncthreads();
 #pragma unroll
   for (int v = 0; v < MAXV; ++v) {
     const int vi = lane + v * 32;
     if (vi < nvec)
 #pragma unroll
-      for (int j = 0; j < VN; ++j) {
-        atomicAdd(&dq[vi * VN + j], w[vi * VN + j] * acc[v][j]);
-        atomicAdd(&dw[vi * VN + j], q[vi * VN + j] * acc[v][j]);
-      }
+      for (int j = 0; j < VN; ++j) atomicAdd(&sacc[vi * VN + j], acc[v][j]);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+    atomicAdd(&dq[i], w[i] * sacc[i]);
+    atomicAdd(&dw[i], q[i] * sacc[i]);
   }
 }
 
@@ -238,7 +245,7 @@ static cudaError_t bwd_impl(const void* const* sources, int S, const float* q, c
   const int threads = 256;
   const int mv = maxv_for<T>(dim);
   KIMI_MAXV_SWITCH(mv, MV, {
-    attnres_bwd_kernel<T, MV><<<grid_tokens(tokens, threads / 32), threads, 0, s>>>(
+    attnres_bwd_kernel<T, MV><<<grid_tokens(tokens, threads / 32), threads, dim * sizeof(float), s>>>(
         ptrs, S, q, w, (const T*)dout, probs, rstd, dptrs, dq, dw, tokens, dim);
   });
   return cudaGetLastError();

@@ -344,19 +344,29 @@ std::vector<at::Tensor> fa_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Ten
 
 // ---------------------------------------------------------------- tcgen05 GEMM
 // Logical C[M,N] = A[M,K] B[N,K]^T. a_mn: A given as [K, M]; b_mn: B given as [K, N] (or [G,K,N]).
+static void check_tma_matrix(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.dim() == 2 && t.stride(1) == 1 && t.stride(0) % 8 == 0 && t.stride(0) >= t.size(1),
+              name, " must be a row-major CUDA matrix with a 16-byte aligned row stride");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0, name, " must start on a 16-byte boundary");
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, ": tc_gemm takes bf16 operands");
+}
+
+// Dense GEMM out[M,N] = op(a) op(b)^T on the tcgen05 kernel. Operands may be row-strided views
+// (any M, N, K; row strides multiples of 8 elements): tiles past the logical edge read zeros.
 at::Tensor tc_gemm_dense(at::Tensor a, at::Tensor b, bool a_mn, bool b_mn, bool out_fp32, int64_t bn,
                          c10::optional<at::Tensor> out_opt) {
-  CHECK_CUDA_CONTIG(a);
-  CHECK_CUDA_CONTIG(b);
-  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "tc_gemm takes bf16 operands");
-  TORCH_CHECK(a.dim() == 2 && b.dim() == 2, "dense tc_gemm takes 2-D operands");
+  check_tma_matrix(a, "a");
+  check_tma_matrix(b, "b");
   const at::cuda::CUDAGuard gd(a.device());
   const int64_t M = a_mn ? a.size(1) : a.size(0), K = a_mn ? a.size(0) : a.size(1);
   const int64_t N = b_mn ? b.size(1) : b.size(0);
   TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K, "inner dimensions differ");
-  TORCH_CHECK(N % 8 == 0 && K % 8 == 0 && M % 8 == 0, "tc_gemm needs M, N, K multiples of 8");
+  TORCH_CHECK(M > 0 && N > 0 && K > 0, "empty GEMM");
   at::Tensor out = out_opt.has_value() && out_opt->defined() ? *out_opt
                    : at::empty({M, N}, a.options().dtype(out_fp32 ? at::kFloat : at::kBFloat16));
+  TORCH_CHECK(out.is_cuda() && out.dim() == 2 && out.size(0) == M && out.size(1) == N && out.stride(1) == 1 &&
+                  out.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0,
+              "out must be an [M,N] row-major matrix with a 16-byte aligned row stride");
   kimi::TcGemmArgs g;
   g.mode = 0;
   g.bn = (int)bn;
@@ -365,13 +375,13 @@ at::Tensor tc_gemm_dense(at::Tensor a, at::Tensor b, bool a_mn, bool b_mn, bool 
   g.a = a.data_ptr();
   g.a_rows = a.size(0);
   g.a_cols = a.size(1);
-  g.a_ld = a.size(1);
+  g.a_ld = a.stride(0);
   g.b = b.data_ptr();
   g.b_groups = 1;
   g.b_rows = b.size(0);
   g.b_cols = b.size(1);
-  g.b_ld = b.size(1);
-  g.b_gstride = b.numel();
+  g.b_ld = b.stride(0);
+  g.b_gstride = b.stride(0) * b.size(0);
   g.M = (int)M;
   g.N = (int)N;
   g.K = (int)K;

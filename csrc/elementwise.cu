@@ -221,6 +221,8 @@ __global__ void decay_bwd_kernel(const float* __restrict__ dg, const T* __restri
   extern __shared__ float sda[];
   for (int i = threadIdx.x; i < heads; i += blockDim.x) sda[i] = 0.f;
   __syncthreads();
+  // With kdim % 32 == 0 (checked by the launcher, and n is then a multiple of 32), the 32
+  // consecutive elements of a warp share one head: reduce in registers, one shared atomic.
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const int h = (int)((i / kdim) % heads);
     const float sc = expf(a_log[h]), zv = to_f<T>(z[i]);
@@ -228,7 +230,8 @@ __global__ void decay_bwd_kernel(const float* __restrict__ dg, const T* __restri
     const bool inside = p > ceps && p < 1.f - ceps;
     const float dpre = inside ? dg[i] * g_min * p * (1.f - p) : 0.f;  // d/d(sc*z)
     dz[i] = from_f<T>(dpre * sc);
-    atomicAdd(&sda[h], dpre * zv * sc);
+    const float part = warp_sum(dpre * zv * sc);
+    if ((threadIdx.x & 31) == 0) atomicAdd(&sda[h], part);
   }
   __syncthreads();
   for (int i = threadIdx.x; i < heads; i += blockDim.x) atomicAdd(&da_log[i], sda[i]);
@@ -337,28 +340,41 @@ __global__ void conv_bwd_pre_kernel(const T* __restrict__ dy, const T* __restric
 }
 
 // Pass 2: dx[t,c] = sum_j w[c,j] dpre[t+j,c];  dw[c,j] = sum_{b,t} dpre[t,c] x[t-j,c]
+// One thread per channel walks a tile of kConvTile tokens (coalesced across channels), keeps
+// its dw[c,:] partial in registers and adds it to global memory once per tile.
+constexpr int kConvTile = 64;
+constexpr int kConvMaxK = 8;
 template <typename T>
-__global__ void conv_bwd_x_kernel(const float* __restrict__ dpre, const T* __restrict__ x,
-                                  const float* __restrict__ w, T* __restrict__ dx, float* __restrict__ dw, int batch,
-                                  int tokens, int channels, int ksize) {
-  extern __shared__ float sdw[];  // channels * ksize
-  for (int i = threadIdx.x; i < channels * ksize; i += blockDim.x) sdw[i] = 0.f;
-  __syncthreads();
-  const int64_t n = (int64_t)batch * tokens * channels;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int c = (int)(i % channels);
-    const int64_t bt = i / channels;
-    const int t = (int)(bt % tokens);
-    float acc = 0.f;
-    const float dp = dpre[i];
-    for (int j = 0; j < ksize; ++j) {
-      if (t + j < tokens) acc += w[c * ksize + j] * dpre[(bt + j) * channels + c];
-      if (t - j >= 0) atomicAdd(&sdw[c * ksize + j], dp * to_f<T>(x[(bt - j) * channels + c]));
-    }
-    dx[i] = from_f<T>(acc);
+__global__ void __launch_bounds__(128) conv_bwd_x_kernel(const float* __restrict__ dpre, const T* __restrict__ x,
+                                                         const float* __restrict__ w, T* __restrict__ dx,
+                                                         float* __restrict__ dw, int tokens, int channels,
+                                                         int ksize) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= channels) return;
+  const int t0 = blockIdx.y * kConvTile;
+  const int t1 = min(t0 + kConvTile, tokens);
+  const int64_t base = (int64_t)blockIdx.z * tokens;
+  float wc[kConvMaxK], acc[kConvMaxK];
+#pragma unroll
+  for (int j = 0; j < kConvMaxK; ++j) {
+    wc[j] = j < ksize ? w[c * ksize + j] : 0.f;
+    acc[j] = 0.f;
   }
-  __syncthreads();
-  for (int i = threadIdx.x; i < channels * ksize; i += blockDim.x) atomicAdd(&dw[i], sdw[i]);
+  for (int t = t0; t < t1; ++t) {
+    const float dp = dpre[(base + t) * channels + c];
+    float sx = 0.f;
+#pragma unroll
+    for (int j = 0; j < kConvMaxK; ++j) {
+      if (j < ksize) {
+        if (t + j < tokens) sx += wc[j] * dpre[(base + t + j) * channels + c];
+        if (t - j >= 0) acc[j] += dp * to_f<T>(x[(base + t - j) * channels + c]);
+      }
+    }
+    dx[(base + t) * channels + c] = from_f<T>(sx);
+  }
+#pragma unroll
+  for (int j = 0; j < kConvMaxK; ++j)
+    if (j < ksize) atomicAdd(&dw[c * ksize + j], acc[j]);
 }
 
 
@@ -393,7 +409,11 @@ cudaError_t rms_norm_bwd(int dtype, const void* dy, const void* x, const float* 
     const int p = period < 1 ? 1 : period;
     const size_t smem = dw ? (size_t)p * dim * sizeof(float) : 0;
     if (smem > 48 * 1024) return cudaErrorInvalidValue;
-    rms_bwd_kernel<T><<<grid_for(rows, threads / tpr), threads, smem, s>>>(
+    // The dw partials are flushed once per block: keep the grid near 4 blocks per SM so the
+    // global atomics per weight element stay in the hundreds.
+    int grid = grid_for(rows, threads / tpr);
+    if (dw && grid > 148 * 4) grid = 148 * 4;
+    rms_bwd_kernel<T><<<grid, threads, smem, s>>>(
         (const T*)dy, (const T*)x, w, rstd, (T*)dx, dw, rows, dim, p, tpr);
   });
   return cudaGetLastError();
@@ -441,6 +461,7 @@ cudaError_t kda_decay_fwd(int dtype, const void* z, const float* a_log, float* g
 cudaError_t kda_decay_bwd(int dtype, const float* dg, const void* z, const float* a_log, void* dz, float* da_log,
                           int64_t rows, int heads, int kdim, float g_min, float ceps, cudaStream_t s) {
   const int64_t n = rows * heads * kdim;
+  if (kdim % 32) return cudaErrorInvalidValue;
   KIMI_DISPATCH(dtype, T, {
     decay_bwd_kernel<T><<<grid_for(n, 256), 256, heads * sizeof(float), s>>>(dg, (const T*)z, a_log, (T*)dz, da_log,
                                                                             n, heads, kdim, g_min, ceps);
@@ -470,14 +491,12 @@ cudaError_t conv_silu_norm_bwd(int dtype, const void* dy, const void* x, const f
   while (tpr * 8 < head_dim && tpr < 32) tpr <<= 1;
   if (tpr * 8 < head_dim) return cudaErrorInvalidValue;
   const int64_t groups = (int64_t)batch * tokens * (channels / head_dim);
-  const int64_t n = (int64_t)batch * tokens * channels;
-  const size_t smem = (size_t)channels * ksize * sizeof(float);
-  if (smem > 48 * 1024) return cudaErrorInvalidValue;
+  if (ksize > kConvMaxK) return cudaErrorInvalidValue;
+  const dim3 gx((channels + 127) / 128, (tokens + kConvTile - 1) / kConvTile, batch);
   KIMI_DISPATCH(dtype, T, {
     conv_bwd_pre_kernel<T><<<grid_for(groups, 256 / tpr), 256, 0, s>>>(
         (const T*)dy, (const T*)x, w, dpre, batch, tokens, channels, ksize, head_dim, eps, normalize, tpr);
-    conv_bwd_x_kernel<T><<<grid_for(n, 256), 256, smem, s>>>(dpre, (const T*)x, w, (T*)dx, dw, batch, tokens,
-                                                            channels, ksize);
+    conv_bwd_x_kernel<T><<<gx, 128, 0, s>>>(dpre, (const T*)x, w, (T*)dx, dw, tokens, channels, ksize);
   });
   return cudaGetLastError();
 }

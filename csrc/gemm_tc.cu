@@ -310,8 +310,15 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
           if (p.out_fp32) {
             float* o = reinterpret_cast<float*>(p.out) + goff + (int64_t)row * p.ldc;
 #pragma unroll
-            for (int i = 0; i < 32; i += 4)
-              if (col0 + i + 4 <= p.N) *reinterpret_cast<float4*>(o + col0 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+            for (int i = 0; i < 32; i += 4) {
+              if (col0 + i + 4 <= p.N) {
+                *reinterpret_cast<float4*>(o + col0 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                  if (col0 + i + j < p.N) o[col0 + i + j] = v[i + j];
+              }
+            }
           } else {
             __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + goff + (int64_t)row * p.ldc;
 #pragma unroll
@@ -321,6 +328,10 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
 #pragma unroll
                 for (int j = 0; j < 8; ++j) vo.v[j] = from_f<__nv_bfloat16>(v[i + j]);
                 vo.store(o + col0 + i);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                  if (col0 + i + j < p.N) o[col0 + i + j] = from_f<__nv_bfloat16>(v[i + j]);
               }
             }
           }

@@ -19,6 +19,7 @@ from typing import Literal
 import torch
 import torch.nn as nn
 
+from ..runtime import host_checks, mask_all_valid
 from .attnres import (AttentionResidualBackboneOutput, AttentionResidualConfig, AttentionResidualSite,
                       BlockAttentionResidualController, DepthSiteMetadata, FullAttentionResidualController,
                       FullAttentionResidualState, padded_weight_matrix)
@@ -557,7 +558,8 @@ class HybridAttentionBackbone(nn.Module):
         b, _, mask = validate_backbone_inputs(hidden_states, attention_mask, self.config.d_model, mode)
         self._validate_cache(cache, b, mode)
         # Layers see ``None`` for an all-valid mask: mask-free fused kernels apply.
-        layer_mask = None if (not output_diagnostics and bool(mask.all())) else mask
+        all_valid = mask_all_valid() if not host_checks() else bool(mask.all())
+        layer_mask = None if (not output_diagnostics and all_valid) else mask
         if self.config.depth_mixing == "standard":
             return self._forward_standard(hidden_states, layer_mask, mask, cache, use_cache, mode,
                                           output_hidden_states, output_diagnostics, update_routing_bias)

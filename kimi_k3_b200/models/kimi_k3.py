@@ -18,6 +18,7 @@ from typing import Literal
 import torch
 import torch.nn as nn
 
+from ..runtime import host_checks
 from .attnres import AttentionResidualConfig
 from .backbone import HybridBackboneCache, KimiBlock, KimiBlockConfig
 from .kda import KDAConfig
@@ -266,6 +267,8 @@ def validate_and_build_attention_mask(input_ids, inputs_embeds, attention_mask, 
                           else torch.ones(b, t, dtype=torch.bool, device=src.device))
     if tuple(attention_mask.shape) != (b, t) or attention_mask.dtype != torch.bool:
         raise ValueError(f"attention_mask must be boolean with shape {(b, t)}")
+    if not host_checks():  # the caller validated the host copy of the mask
+        return b, t, attention_mask
     if t > 1 and torch.any((~attention_mask[:, :-1]) & attention_mask[:, 1:]):
         raise ValueError("left padding is not supported by the current hybrid backbone")
     if torch.any(attention_mask.sum(dim=1) == 0):

@@ -30,6 +30,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .. import ops as _ops
+from ..runtime import host_checks
 
 
 # --------------------------------------------------------------------------- typed outputs
@@ -153,7 +154,7 @@ def require_finite(name, values, valid):
 def validate_token_ids(labels, valid, vocab_size, *, name="labels"):
     if labels.dtype not in (torch.int32, torch.int64):
         raise TypeError(f"{name} must use int32 or int64")
-    if torch.any(valid & ((labels < 0) | (labels >= vocab_size))):
+    if host_checks() and torch.any(valid & ((labels < 0) | (labels >= vocab_size))):
         raise ValueError(f"{name} contains IDs outside [0, {vocab_size})")
 
 
@@ -318,7 +319,9 @@ class NextTokenCrossEntropyLoss(nn.Module):
                                        return_per_token=False)
         loss_sum, _ = fused_head_loss(h, head_weight, al, weighted_valid, label_smoothing=self.label_smoothing)
         normalizer = valid.sum().float()
-        if normalizer.item() == 0:
+        if not host_checks():
+            loss = loss_sum / normalizer.clamp_min(1.0)  # an empty batch gives a connected zero
+        elif normalizer.item() == 0:
             if self.zero_valid_policy == "raise":
                 raise ValueError("loss batch contains no valid tokens")
             loss = loss_sum = connected_zero(hidden)
@@ -396,7 +399,9 @@ class MultiTokenPredictionLoss(nn.Module):
         validate_token_ids(labels, valid, head_weight.shape[0], name="mtp_labels")
         loss_sum, _ = fused_head_loss(hidden, head_weight, labels, valid)
         normalizer = valid.sum().float()
-        if normalizer.item() == 0:
+        if not host_checks():
+            loss = loss_sum / normalizer.clamp_min(1.0)
+        elif normalizer.item() == 0:
             if self.zero_valid_policy == "raise":
                 raise ValueError("MTP batch contains no valid future targets")
             loss = loss_sum = connected_zero(hidden)

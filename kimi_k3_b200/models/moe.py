@@ -21,6 +21,7 @@ import torch
 import torch.nn as nn
 
 from .. import ops as _ops
+from ..runtime import host_checks
 from .primitives import RMSNorm, SiTUGLU, situ_glu_activation
 
 
@@ -152,7 +153,7 @@ class TopKRouter(nn.Module):
     def commit_next_bias(self, next_bias: torch.Tensor) -> None:
         if next_bias.shape != self.routing_bias.shape:
             raise ValueError("next routing bias has an invalid shape")
-        if not torch.isfinite(next_bias).all():
+        if host_checks() and not torch.isfinite(next_bias).all():
             raise ValueError("next routing bias must be finite")
         self.routing_bias.copy_(next_bias.to(device=self.routing_bias.device, dtype=self.routing_bias.dtype))
 
@@ -352,7 +353,7 @@ class HistogramQuantileBalancer(nn.Module):
     @torch.no_grad()
     def compute_next_bias(self, old_bias) -> QuantileBalanceUpdate:
         totals = self.counts.sum(-1)
-        if torch.any(totals == 0):
+        if host_checks() and torch.any(totals == 0):
             raise ValueError("each expert histogram requires at least one margin")
         ranks = self.target_quantile * (totals.float() - 1)
         lo_r, hi_r = ranks.floor().long(), ranks.ceil().long()
@@ -366,7 +367,7 @@ class HistogramQuantileBalancer(nn.Module):
         prov = -q
         return QuantileBalanceUpdate(prov - prov.mean(), self.target_quantile, q,
                                      torch.full_like(q, self.min_margin), torch.full_like(q, self.max_margin),
-                                     int(totals[0].item()))
+                                     int(totals[0].item()) if host_checks() else totals[0])
 
 
 # --------------------------------------------------------------------------- module
@@ -422,8 +423,12 @@ class StableLatentMoE(nn.Module):
         self._balance_accumulating = True
 
     @torch.no_grad()
-    def finalize_and_commit_balance(self, reducer=None) -> QuantileBalanceUpdate:
-        """Close the window; ``reducer`` (EP/DP) makes the statistics global first."""
+    def finalize_and_commit_balance(self, reducer=None, keep_old=None) -> QuantileBalanceUpdate:
+        """Close the window; ``reducer`` (EP/DP) makes the statistics global first.
+
+        ``keep_old`` (device bool scalar) keeps the previous bias when True: the step whose
+        window this is was skipped by a device-side finite check (no host branch needed).
+        """
         if not self._balance_accumulating:
             raise RuntimeError("balance accumulation is not active")
         if self.config.quantile_backend == "exact":
@@ -438,6 +443,9 @@ class StableLatentMoE(nn.Module):
             if reducer is not None:
                 reducer.reduce_histogram(self.histogram_balancer)
             update = self.histogram_balancer.compute_next_bias(self._balance_old_bias)
+        if keep_old is not None:
+            update.next_bias = torch.where(keep_old, self._balance_old_bias.to(update.next_bias.dtype),
+                                           update.next_bias)
         self.router.commit_next_bias(update.next_bias)
         self.discard_balance_accumulation()
         return update

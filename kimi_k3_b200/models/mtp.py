@@ -18,6 +18,7 @@ from dataclasses import asdict, dataclass
 import torch
 import torch.nn as nn
 
+from ..runtime import host_checks, mask_all_valid
 from .attnres import AttentionResidualConfig
 from .backbone import (CANONICAL_ATTENTION_PATTERN, HybridAttentionBackbone, HybridBackboneConfig,
                        HybridBackboneOutput)
@@ -267,7 +268,7 @@ class KimiMTPHead(nn.Module):
 
     def _run_compacted(self, fused, feature_mask, *, output_hidden_states, output_diagnostics, update_routing_bias):
         b, t, d = fused.shape
-        if bool(feature_mask.all()):
+        if mask_all_valid() if not host_checks() else bool(feature_mask.all()):
             out = self.block(fused, attention_mask=None, output_hidden_states=output_hidden_states,
                              output_diagnostics=output_diagnostics, update_routing_bias=update_routing_bias)
             return out.last_hidden_state, out.diagnostics

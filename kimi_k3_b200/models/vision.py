@@ -19,6 +19,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from ..runtime import host_checks
 from .primitives import RMSNorm
 
 
@@ -456,7 +457,7 @@ def prepare_multimodal_embeddings(*, config, input_ids, text_embeddings, attenti
         ids = [i for i in (config.image_token_id, config.video_token_id) if i is not None]
         if not ids:
             return text_embeddings, None, None
-        if not bool(torch.isin(input_ids, torch.tensor(ids, device=input_ids.device)).any()):
+        if not host_checks() or not bool(torch.isin(input_ids, torch.tensor(ids, device=input_ids.device)).any()):
             return text_embeddings, None, None
     if not config.enable_vision:
         raise ValueError("visual inputs cannot be used when vision is disabled")

@@ -374,33 +374,36 @@ def attnres_mix(sources, pseudo_query, key_norm_weight, eps):
 
 # --------------------------------------------------------------------------- LM head + CE
 class _LinearCE(torch.autograd.Function):
-    """``sum_valid CE(h @ W^T, t)``; gradients are formed chunk by chunk in forward.
+    """``sum_valid CE(h @ W^T, t)``; gradients are formed in forward on the tcgen05 GEMM.
 
-    Each row chunk: logits = h_c W^T (bf16, padded leading dimension), the fused row
-    kernel writes loss and (softmax - onehot) in place, then dh_c = G W and dW += G^T h_c.
-    Backward only scales by the incoming scalar gradient.
+    Per row chunk (up to ``chunk_rows``): logits = h_c W^T in bf16 with a 64-aligned row stride,
+    the fused row kernel writes the loss and (softmax - onehot) in place, then dh_c = G W and
+    dW (+)= G^T h_c in fp32. The [N, V] fp32 probability tensor never exists; backward only
+    scales by the incoming scalar gradient. Reference: ``src/loss/common/cross_entropy.py:41-46``
+    (logits materialised in fp32, CE through ``F.cross_entropy``).
     """
 
     @staticmethod
     def forward(ctx, h, w, targets, valid, chunk_rows):
         n, d = h.shape
         v = w.shape[0]
-        dt = h.dtype
-        wd = w.to(dt)
-        vpad = (v + 7) // 8 * 8
+        wd = w.to(torch.bfloat16).contiguous()
+        vpad = (v + 63) // 64 * 64
         loss = torch.zeros((), device=h.device, dtype=torch.float32)
         dh = torch.empty_like(h)
-        dw = torch.zeros(v, d, device=h.device, dtype=torch.float32)
-        buf = torch.empty(min(chunk_rows, n), vpad, device=h.device, dtype=dt)
-        for s in range(0, n, chunk_rows):
-            e = min(n, s + chunk_rows)
+        dw = None
+        rows_per = min(chunk_rows, n)
+        buf = torch.empty(rows_per, vpad, device=h.device, dtype=torch.bfloat16)
+        C = _C()
+        for s in range(0, n, rows_per):
+            e = min(n, s + rows_per)
             hc = h[s:e]
             lg = buf[: e - s, :v]
-            torch.mm(hc, wd.t(), out=lg)
-            rows = _C().ce_rows(lg, v, targets[s:e], valid[s:e], 1.0)
-            loss += rows.sum()
-            torch.mm(lg, wd, out=dh[s:e])
-            dw.add_(torch.mm(lg.t(), hc).float())
+            C.tc_gemm_dense(hc, wd, False, False, False, 256, lg)
+            loss += C.ce_rows(lg, v, targets[s:e], valid[s:e], 1.0).sum()
+            C.tc_gemm_dense(lg, wd, False, True, False, 128, dh[s:e])
+            part = C.tc_gemm_dense(lg, hc, True, True, True, 128, None)
+            dw = part if dw is None else dw.add_(part)
         ctx.save_for_backward(dh, dw)
         ctx.w_dtype = w.dtype
         return loss
@@ -411,10 +414,11 @@ class _LinearCE(torch.autograd.Function):
         return dh * gl.to(dh.dtype), (dw * gl).to(ctx.w_dtype), None, None, None
 
 
-def linear_cross_entropy(hidden, weight, targets, valid, chunk_rows: int = 4096):
+def linear_cross_entropy(hidden, weight, targets, valid, chunk_rows: int = 16384):
     """Sum of token CE losses of ``hidden @ weight^T`` over valid rows (fp32 scalar)."""
-    dt = _act_dtype(hidden)
-    h = hidden.to(dt).contiguous()
+    if hidden.shape[-1] % 8:
+        raise ValueError("linear_cross_entropy needs a hidden width that is a multiple of 8")
+    h = hidden.to(torch.bfloat16).contiguous()
     return _LinearCE.apply(h, weight, targets.contiguous(), valid.contiguous(), int(chunk_rows))
 
 

@@ -2,9 +2,17 @@
 
 A step = (optional pinned host -> device copy) -> bf16 autocast forward with the
 fused head losses (no ``[N, V]`` logits) -> backward -> global-norm clip on the
-device -> hybrid optimizer -> scheduler -> Quantile-Balancing commit.  The clip
-coefficient is applied without a host round trip; the only host syncs are the
-loss normalisers and the optimizer's single finite-gradient check.
+device -> hybrid optimizer -> scheduler -> Quantile-Balancing commit.
+
+Two execution modes:
+
+* eager: the clip coefficient is applied without a host round trip; the host syncs are
+  the loss normalisers and the optimizer's single finite-gradient check;
+* CUDA graph (``cuda_graph=True``): after ``graph_warmup`` sync-free eager steps the
+  whole step (forward, backward, clip, Muon + AdamW + QK-Clip, QB commit) is captured
+  once and replayed. Host-side validation runs on the host copy of each batch; the
+  finite check becomes a device flag (``found_inf``) that suppresses the update inside
+  the graph; the host reads it one step later (scheduler and step counters follow).
 
 Parity: the step semantics follow ``training/train_one_epoch.py:145-330`` (reference)
 for a window of one micro-batch.
@@ -50,7 +58,7 @@ class TrainStepEngine:
 
     def __init__(self, model, optimizer, *, scheduler=None, grad_clip: float | None = 1.0,
                  amp_dtype: torch.dtype | None = torch.bfloat16, use_mtp: bool = True, moe_controller=None,
-                 grad_hook=None):
+                 grad_hook=None, cuda_graph: bool = False, graph_warmup: int = 2):
         self.model = model
         self.optimizer = optimizer
         self.scheduler = scheduler
@@ -61,19 +69,33 @@ class TrainStepEngine:
         self.grad_hook = grad_hook  # called after backward (gradient reduction in data parallel)
         self.device = next(model.parameters()).device
         self._params = [p for p in model.parameters() if p.requires_grad]
+        self.cuda_graph = bool(cuda_graph) and self.device.type == "cuda"
+        self.graph_warmup = int(graph_warmup)
+        self._graph = None
+        self._static_in = None
+        self._static_out = None
+        self._graph_steps = 0
+        self._pending = None  # (pinned found_inf copy, event) of the last replayed step
 
-    def _autocast(self):
+    def _autocast(self, cache_enabled: bool = True):
         if self.amp_dtype is None or self.device.type != "cuda":
             return nullcontext()
-        return torch.autocast("cuda", dtype=self.amp_dtype)
+        return torch.autocast("cuda", dtype=self.amp_dtype, cache_enabled=cache_enabled)
 
-    def forward_loss(self, batch: dict):
-        with self._autocast():
+    def forward_loss(self, batch: dict, *, cache_enabled: bool = True):
+        with self._autocast(cache_enabled):
             out = self.model(input_ids=batch["input_ids"], attention_mask=batch.get("attention_mask"),
                              labels=batch["labels"], use_mtp=self.use_mtp, compute_logits=False)
         return out
 
-    def step(self, batch: dict) -> StepOutput:
+    # ------------------------------------------------------------------ eager
+    def step(self, batch: dict, *, mask_all_valid: bool | None = None) -> StepOutput:
+        """One optimizer step. ``mask_all_valid`` tells the CUDA-graph path that the batch's
+        attention mask is all True (otherwise it is checked, on the host copy when there is one)."""
+        if self.cuda_graph:
+            if self._graph_eligible(batch, mask_all_valid):
+                return self._graph_step(batch)
+            self._resolve_pending()
         if batch["input_ids"].device != self.device:
             batch = move_batch(batch, self.device)
         self.model.train()
@@ -104,6 +126,112 @@ class TrainStepEngine:
         return StepOutput(out.loss.detach(), lo.ntp.loss.detach(), None if lo.mtp is None else lo.mtp.loss.detach(),
                           gnorm, executed)
 
+    # ------------------------------------------------------------------ CUDA graph
+    @staticmethod
+    def _mask_is_all_valid(batch, hint):
+        if hint is not None:
+            return bool(hint)
+        mask = batch.get("attention_mask")
+        if mask is None:
+            return False  # the model would derive it from pad ids: let the eager path decide
+        return bool(mask.all())  # a host tensor is free; a device tensor costs one sync
+
+    def _graph_eligible(self, batch, hint) -> bool:
+        if self._static_in is not None:
+            for k, v in self._static_in.items():
+                if k in batch and tuple(batch[k].shape) != tuple(v.shape):
+                    return False
+        return self._mask_is_all_valid(batch, hint)
+
+    def _device_step_body(self, batch, *, cache_enabled: bool):
+        """Forward, backward, clip, optimizer and QB commit with no host synchronisation."""
+        from ..runtime import sync_free
+        with sync_free(all_valid_mask=True):
+            if self.moe_controller is not None:
+                self.moe_controller.begin()
+            out = self.forward_loss(batch, cache_enabled=cache_enabled)
+            out.loss.backward()
+            if self.grad_hook is not None:
+                self.grad_hook()
+            gnorm = clip_grad_norm_device(self._params, self.grad_clip)
+            found_inf = ~torch.isfinite(gnorm)
+            self.optimizer.step(found_inf=found_inf)
+            if self.moe_controller is not None:
+                self.moe_controller.commit(keep_old=found_inf)
+        lo = out.loss_output
+        return (out.loss.detach(), lo.ntp.loss.detach(), None if lo.mtp is None else lo.mtp.loss.detach(),
+                gnorm.detach(), found_inf)
+
+    def _resolve_pending(self) -> None:
+        """Read the previous replay's skip flag; advance the scheduler only for executed steps."""
+        if self._pending is None:
+            return
+        flag, event = self._pending
+        self._pending = None
+        event.synchronize()
+        if bool(flag.item()):
+            if hasattr(self.optimizer, "undo_step_count"):
+                self.optimizer.undo_step_count()
+        elif self.scheduler is not None:
+            self.scheduler.step()
+
+    def _load_static(self, batch) -> None:
+        for k, dst in self._static_in.items():
+            src = batch.get(k)
+            if src is None:
+                dst.fill_(True)
+            else:
+                dst.copy_(src, non_blocking=True)
+
+    def _graph_step(self, batch) -> StepOutput:
+        self._resolve_pending()
+        self.model.train()
+        if self._static_in is None:
+            if hasattr(self.optimizer, "use_device_lrs"):
+                self.optimizer.use_device_lrs()
+            ids = batch["input_ids"]
+            self._static_in = {"input_ids": torch.empty(ids.shape, dtype=ids.dtype, device=self.device),
+                               "labels": torch.empty(batch["labels"].shape, dtype=batch["labels"].dtype,
+                                                     device=self.device),
+                               "attention_mask": torch.ones(ids.shape, dtype=torch.bool, device=self.device)}
+        self._load_static(batch)
+        if self._graph_steps < self.graph_warmup:
+            # Sync-free eager steps on a side stream: they fill optimizer state and the
+            # kernels' one-time set-up, as capture requires.
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                self.optimizer.zero_grad(set_to_none=True)
+                res = self._device_step_body(self._static_in, cache_enabled=False)
+            torch.cuda.current_stream().wait_stream(side)
+        else:
+            if self._graph is None:
+                self.optimizer.zero_grad(set_to_none=True)
+                self._graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(self._graph):
+                    self._static_out = self._device_step_body(self._static_in, cache_enabled=False)
+            self._graph.replay()
+            res = self._static_out
+        self._graph_steps += 1
+        loss, ntp, mtp, gnorm, found_inf = res
+        flag = torch.empty((), dtype=torch.bool, pin_memory=True)
+        flag.copy_(found_inf, non_blocking=True)
+        event = torch.cuda.Event()
+        event.record()
+        self._pending = (flag, event)
+        return StepOutput(loss, ntp, mtp, gnorm, True)
+
+    def finish(self) -> None:
+        """Settle the bookkeeping of the last replayed step (call before reading the
+        scheduler or saving a checkpoint)."""
+        self._resolve_pending()
+
+    def release_graph(self) -> None:
+        """Drop the captured graph (required before destroying a process group it uses)."""
+        self.finish()
+        self._graph = None
+        self._static_out = None
+
 
 class MoEController:
     """Open / commit / discard Quantile-Balancing windows on every balanced MoE layer.
@@ -127,10 +255,11 @@ class MoEController:
             layer.begin_balance_accumulation()
         self.window_open = True
 
-    def commit(self):
+    def commit(self, keep_old=None):
+        """Commit every layer's next bias; ``keep_old`` (device bool) keeps the old biases."""
         if not self.window_open:
             raise RuntimeError("no Quantile Balancing window is open")
-        updates = tuple(layer.finalize_and_commit_balance(self.reducer) for layer in self.layers)
+        updates = tuple(layer.finalize_and_commit_balance(self.reducer, keep_old=keep_old) for layer in self.layers)
         self.window_open = False
         return updates
 

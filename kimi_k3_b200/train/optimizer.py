@@ -27,6 +27,8 @@ from typing import Literal
 import torch
 import torch.nn as nn
 
+from ..runtime import host_checks
+
 NS_COEFFS = (3.4445, -4.7750, 2.0315)
 
 
@@ -398,6 +400,7 @@ class KimiMuon(torch.optim.Optimizer):
         self.ns_dtype = ns_dtype
         self.last_update_metrics: dict = {}
         self._metric_tensors: dict = {}
+        self._buckets = None
         self._slots = {}
         for group in self.param_groups:
             for p in group["params"]:
@@ -422,44 +425,116 @@ class KimiMuon(torch.optim.Optimizer):
             return torch.float32
         return torch.bfloat16
 
+    # ---- bucketed state: one momentum tensor [count, rows, cols] per (group, matrix shape)
+    def _ensure_buckets(self) -> list:
+        """Per-parameter momentum buffers become views into one tensor per bucket, so a step
+        is a handful of launches per bucket instead of a dozen per parameter."""
+        if self._buckets is not None:
+            return self._buckets
+        keyed: dict = {}
+        for gi, group in enumerate(self.param_groups):
+            for p in group["params"]:
+                slot = self._slots[id(p)]
+                keyed.setdefault((gi, slot.rows, slot.cols, p.device, p.dtype), []).append(p)
+        buckets = []
+        for (gi, rows, cols, dev, dt), ps in keyed.items():
+            count = sum(self._slots[id(p)].count for p in ps)
+            mom = torch.zeros(count, rows, cols, device=dev, dtype=dt)
+            off = 0
+            for p in ps:
+                slot = self._slots[id(p)]
+                view = slot.from_blocks(mom[off:off + slot.count])
+                old = self.state[p].get("momentum_buffer")
+                if old is not None:
+                    view.copy_(old)
+                self.state[p]["momentum_buffer"] = view
+                off += slot.count
+            sqrt_numel = torch.tensor([float(p.numel()) for p in ps], device=dev).sqrt()
+            buckets.append((gi, rows, cols, ps, mom, sqrt_numel))
+        self._buckets = buckets
+        return buckets
+
+    def load_state_dict(self, state_dict):
+        super().load_state_dict(state_dict)
+        self._buckets = None  # re-view the loaded per-parameter buffers on the next step
+
     @torch.no_grad()
-    def step(self, closure=None):
+    def step(self, closure=None, *, skip: torch.Tensor | None = None):
+        """One Muon step. ``skip`` (device bool scalar) turns the step into a no-op on the
+        device (momentum, weight decay and update all suppressed) without a host branch."""
         if closure is not None:
             with torch.enable_grad():
                 closure()
+        if any(p.grad is None for g in self.param_groups for p in g["params"]):
+            if skip is not None:
+                raise RuntimeError("device-flag Muon steps need a gradient for every parameter")
+            return self._step_sparse()
+        metrics = {"raw": [], "ortho": [], "scaled": [], "ratio": []}
+        for gi, rows, cols, ps, mom_buf, numel in self._ensure_buckets():
+            group = self.param_groups[gi]
+            lr, mom, wd = group["lr"], group["momentum"], group["weight_decay"]
+            slots = [self._slots[id(p)] for p in ps]
+            g = torch.cat([s.to_blocks(p.grad).to(mom_buf.dtype) for p, s in zip(ps, slots)], 0)
+            if skip is not None:
+                g = torch.where(skip, torch.zeros((), device=g.device, dtype=g.dtype), g)
+                mom_buf.mul_(torch.where(skip, 1.0, mom).to(mom_buf.dtype)).add_(g)
+            else:
+                mom_buf.mul_(mom).add_(g)
+            raw = g.add(mom_buf, alpha=mom) if group["nesterov"] else mom_buf
+            ortho = batched_newton_schulz(raw, steps=group["ns_steps"], eps=group["eps"],
+                                          dtype=self._resolved_ns_dtype(mom_buf.device))
+            metrics["raw"].append(raw.float().flatten(1).square().mean(1).sqrt())
+            metrics["ortho"].append(ortho.flatten(1).square().mean(1).sqrt())
+            scale = max(rows, cols) ** 0.5 if group["update_rms_scaling"] else 1.0
+            metrics["scaled"].append(metrics["ortho"][-1] * scale)
+            upd = ortho.to(mom_buf.dtype).mul_(scale)
+            views, off = [], 0
+            for p, s in zip(ps, slots):
+                views.append(s.from_blocks(upd[off:off + s.count]))
+                off += s.count
+            unorm = torch.stack(torch._foreach_norm(views)).float()
+            pnorm = torch.stack(torch._foreach_norm(ps)).float()
+            metrics["ratio"].append(lr * unorm / (pnorm.clamp_min(1e-30) / numel).clamp_min(group["eps"]) / numel)
+            lr_eff = torch.where(skip, 0.0, lr) if skip is not None else lr
+            if wd:
+                torch._foreach_mul_(ps, 1.0 - lr_eff * wd)
+            if torch.is_tensor(lr_eff):
+                upd.mul_(-lr_eff)
+                torch._foreach_add_(ps, views)
+            else:
+                torch._foreach_add_(ps, views, alpha=-lr_eff)
+        self._metric_tensors = {k: torch.cat(v) for k, v in metrics.items() if v}
+        self.last_update_metrics = {}
+        return self._metric_tensors
+
+    @torch.no_grad()
+    def _step_sparse(self):
+        """Parameters without gradients this step keep their momentum untouched (reference
+        behaviour); the others are processed matrix by matrix."""
+        self._ensure_buckets()
         metrics = {"raw": [], "ortho": [], "scaled": [], "ratio": []}
         for group in self.param_groups:
             lr, mom, wd = group["lr"], group["momentum"], group["weight_decay"]
-            buckets: dict = {}
             for p in group["params"]:
                 if p.grad is None:
                     continue
-                st = self.state[p]
-                buf = st.get("momentum_buffer")
-                if buf is None:
-                    buf = st["momentum_buffer"] = torch.zeros_like(p.grad)
+                slot = self._slots[id(p)]
+                buf = self.state[p]["momentum_buffer"]
                 buf.mul_(mom).add_(p.grad)
                 raw = p.grad.add(buf, alpha=mom) if group["nesterov"] else buf
-                slot = self._slots[id(p)]
-                buckets.setdefault((slot.rows, slot.cols, p.device), []).append((p, slot, raw))
-            for (rows, cols, dev), items in buckets.items():
-                stacked = torch.cat([s.to_blocks(r).float() for _, s, r in items], 0)
-                ortho = batched_newton_schulz(stacked, steps=group["ns_steps"], eps=group["eps"],
-                                              dtype=self._resolved_ns_dtype(dev))
-                metrics["raw"].append(stacked.flatten(1).square().mean(1).sqrt())
+                ortho = batched_newton_schulz(slot.to_blocks(raw).float(), steps=group["ns_steps"], eps=group["eps"],
+                                              dtype=self._resolved_ns_dtype(p.device))
+                metrics["raw"].append(slot.to_blocks(raw).float().flatten(1).square().mean(1).sqrt())
                 metrics["ortho"].append(ortho.flatten(1).square().mean(1).sqrt())
                 if group["update_rms_scaling"]:
-                    ortho = ortho * (max(rows, cols) ** 0.5)
+                    ortho = ortho * (max(slot.rows, slot.cols) ** 0.5)
                 metrics["scaled"].append(ortho.flatten(1).square().mean(1).sqrt())
-                off = 0
-                for p, slot, _ in items:
-                    upd = slot.from_blocks(ortho[off:off + slot.count]).to(p.dtype)
-                    off += slot.count
-                    prms = p.float().square().mean().sqrt()
-                    metrics["ratio"].append((lr * upd.float().square().mean().sqrt() / prms.clamp_min(group["eps"]))[None])
-                    if wd:
-                        p.mul_(1.0 - lr * wd)
-                    p.add_(upd, alpha=-lr)
+                upd = slot.from_blocks(ortho).to(p.dtype)
+                prms = p.float().square().mean().sqrt()
+                metrics["ratio"].append((lr * upd.float().square().mean().sqrt() / prms.clamp_min(group["eps"]))[None])
+                if wd:
+                    p.mul_(1.0 - lr * wd)
+                p.add_(upd, alpha=-lr)
         self._metric_tensors = {k: torch.cat(v) for k, v in metrics.items() if v}
         self.last_update_metrics = {}
         return self._metric_tensors
@@ -526,7 +601,7 @@ class QKClipController:
         self._pending = None
 
     @torch.no_grad()
-    def apply(self, step: int, *, materialize: bool = True):
+    def apply(self, step: int, *, materialize: bool = True, skip: torch.Tensor | None = None):
         if step % self.every_steps:
             return QKClipReport(False, 0, 0.0, 0.0, 0.0, 1.0, 1.0, self.consecutive_steps_active)
         active = [(m, wq, wk) for _, m, wq, wk in self.layers if getattr(m, "_last_qk_scale", None) is not None]
@@ -538,6 +613,8 @@ class QKClipController:
             torch.distributed.all_reduce(scales, op=torch.distributed.ReduceOp.MAX, group=group)
         corr = torch.where(scales > self.threshold, self.threshold / scales.clamp_min(self.eps),
                            torch.ones_like(scales)).clamp(max=1.0)
+        if skip is not None:  # the optimizer step was suppressed on the device: no clipping either
+            corr = torch.where(skip, torch.ones_like(corr), corr)
         sym = corr.sqrt()
         for i, (_, wq, wk) in enumerate(active):
             wq.mul_(sym[i].to(wq.dtype))
@@ -602,6 +679,7 @@ class KimiHybridOptimizer:
         self.muon, self.adamw, self.report, self.config, self.qk_clip = muon, adamw, report, config, qk_clip
         self.step_number = 0
         self.last_step_report: OptimizerStepReport | None = None
+        self.last_skip: torch.Tensor | None = None
 
     @property
     def param_groups(self):
@@ -616,11 +694,38 @@ class KimiHybridOptimizer:
         self.adamw.zero_grad(set_to_none=set_to_none)
 
     @torch.no_grad()
-    def step(self, closure=None, *, gradients_known_finite: bool = False) -> OptimizerStepReport:
+    def step(self, closure=None, *, gradients_known_finite: bool = False,
+             found_inf: torch.Tensor | None = None) -> OptimizerStepReport:
+        """One hybrid step; a non-finite gradient skips it (reference: ``hybrid.py:59-112``).
+
+        Host mode: one finite check read on the host decides. Device mode (``found_inf`` given,
+        or inside :func:`kimi_k3_b200.runtime.sync_free`): the flag stays on the device and
+        suppresses Muon, AdamW (``found_inf`` of the fused kernel) and QK-Clip without a host
+        branch; ``last_skip`` holds it for the caller to read later.
+        """
         if closure is not None:
             with torch.enable_grad():
                 closure()
         params = [p for g in self.param_groups for p in g["params"] if p.grad is not None]
+        if found_inf is not None or not host_checks():
+            if found_inf is None:
+                found_inf = ~_all_finite([p.grad for p in params])
+            skip = found_inf.reshape(()).to(torch.bool)
+            self.muon.step(skip=skip)
+            self.adamw.found_inf = skip.to(torch.float32)
+            try:
+                self.adamw.step()
+            finally:
+                del self.adamw.found_inf
+            self.step_number += 1
+            if self.qk_clip is not None:
+                self.qk_clip.apply(self.step_number, materialize=False, skip=skip)
+            self.last_skip = skip
+            rep = OptimizerStepReport(True, self.adamw.param_groups[0]["lr"], self.muon.param_groups[0]["lr"], False,
+                                      0, 0, {})
+            self.last_step_report = rep
+            return rep
+        self.last_skip = None
         if not gradients_known_finite:
             if not bool(_all_finite([p.grad for p in params])):
                 bad = sum(int(not torch.isfinite(p.grad).all()) for p in params)
@@ -638,6 +743,27 @@ class KimiHybridOptimizer:
         self.last_step_report = rep
         return rep
 
+    def undo_step_count(self) -> None:
+        """A device-mode step turned out to be skipped: the host step counter steps back."""
+        self.step_number = max(0, self.step_number - 1)
+
+    def use_device_lrs(self) -> None:
+        """Move every learning rate into a device tensor (read by replayed CUDA graphs).
+
+        The scheduler then updates them in place; AdamW switches to its capturable form.
+        """
+        for opt in (self.muon, self.adamw):
+            for g in opt.param_groups:
+                dev = g["params"][0].device if g["params"] else torch.device("cpu")
+                if not torch.is_tensor(g["lr"]):
+                    g["lr"] = torch.tensor(float(g["lr"]), device=dev, dtype=torch.float32)
+        for g in self.adamw.param_groups:
+            g["capturable"] = True
+            for p in g["params"]:
+                st = self.adamw.state.get(p)
+                if st and "step" in st and st["step"].device != p.device:
+                    st["step"] = st["step"].to(p.device)
+
     def materialize_report(self) -> OptimizerStepReport:
         """Fill the last report's metrics (Muon statistics, QK-Clip) with one host sync each."""
         rep = self.last_step_report
@@ -654,10 +780,15 @@ class KimiHybridOptimizer:
     def set_lr(self, lr: float, muon_lr: float | None = None) -> None:
         if lr < 0 or (muon_lr is not None and muon_lr < 0):
             raise ValueError("learning rates must be non-negative")
+        def assign(g, v):
+            if torch.is_tensor(g["lr"]):
+                g["lr"].fill_(v)
+            else:
+                g["lr"] = v
         for g in self.adamw.param_groups:
-            g["lr"] = lr
+            assign(g, lr)
         for g in self.muon.param_groups:
-            g["lr"] = lr if muon_lr is None else muon_lr
+            assign(g, lr if muon_lr is None else muon_lr)
 
     def set_lrs(self, *, adamw_lr: float, muon_lr: float) -> None:
         self.set_lr(adamw_lr, muon_lr)

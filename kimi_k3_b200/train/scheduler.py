@@ -8,6 +8,8 @@ from __future__ import annotations
 
 import math
 
+import torch
+
 
 class WarmupCosineLR:
     def __init__(self, optimizer, total_steps: int, warmup_steps: int, min_lr: float = 0.0,
@@ -40,16 +42,24 @@ class WarmupCosineLR:
         progress = min(1.0, max(0.0, (t - self.warmup_steps) / max(1, self.total_steps - self.warmup_steps)))
         return float(min_lr + (base_lr - min_lr) * 0.5 * (1.0 + math.cos(math.pi * progress)))
 
+    @staticmethod
+    def _assign(group: dict, value: float) -> None:
+        # Device-resident learning rates (CUDA-graph replay) are updated in place.
+        if torch.is_tensor(group["lr"]):
+            group["lr"].fill_(value)
+        else:
+            group["lr"] = value
+
     def _set_lr(self, step: int) -> None:
         if self.is_hybrid:
             mmin = self.min_lr if self.min_muon_lr is None else self.min_muon_lr
             for g, b in zip(self.optimizer.adamw.param_groups, self.base_adamw_lrs):
-                g["lr"] = self._compute_lr(b, self.min_lr, step)
+                self._assign(g, self._compute_lr(b, self.min_lr, step))
             for g, b in zip(self.optimizer.muon.param_groups, self.base_muon_lrs):
-                g["lr"] = self._compute_lr(b, mmin, step)
+                self._assign(g, self._compute_lr(b, mmin, step))
         else:
             for g, b in zip(self.optimizer.param_groups, self.base_lrs):
-                g["lr"] = self._compute_lr(b, self.min_lr, step)
+                self._assign(g, self._compute_lr(b, self.min_lr, step))
 
     def step(self) -> None:
         self.step_num += 1

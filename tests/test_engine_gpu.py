@@ -1,0 +1,48 @@
+"""The CUDA-graph training step against the eager step on a small model (GPU)."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _setup(cuda, graph):
+    from kimi_k3_b200.config.model_yaml import build_model_config_from_mapping
+    from kimi_k3_b200.config.profiles import profile_model_mapping
+    from kimi_k3_b200.models import KimiK3
+    from kimi_k3_b200.train.engine import MoEController, TrainStepEngine
+    from kimi_k3_b200.train.optimizer import KimiOptimizerConfig, build_kimi_optimizer
+    from kimi_k3_b200.train.scheduler import WarmupCosineLR
+    m = profile_model_mapping("t4_wikitext")
+    m["model"].update(d_model=128, num_heads=2, num_hybrid_groups=1, vocab_size=1000)
+    m["model"]["moe"].update(latent_dim=64, shared_expert_hidden_dim=96, routed_expert_hidden_dim=128)
+    m["model"]["mla"]["kv_latent_dim"] = 128
+    torch.manual_seed(3)
+    model = KimiK3(build_model_config_from_mapping(m)).to(cuda)
+    opt, _ = build_kimi_optimizer(model, KimiOptimizerConfig(muon_lr=0.01, adamw_lr=1e-3))
+    sch = WarmupCosineLR(opt, total_steps=20, warmup_steps=2, min_lr=1e-5, prepare_first_update=True)
+    eng = TrainStepEngine(model, opt, scheduler=sch, moe_controller=MoEController(model), cuda_graph=graph,
+                          graph_warmup=2)
+    return model, eng
+
+
+def test_graph_step_matches_eager(cuda):
+    g = torch.Generator().manual_seed(0)
+    batches = []
+    for _ in range(6):
+        ids = torch.randint(3, 1000, (2, 128), generator=g)
+        batches.append({"input_ids": ids.pin_memory(), "labels": ids.clone().pin_memory(),
+                        "attention_mask": torch.ones(2, 128, dtype=torch.bool).pin_memory()})
+    m1, e1 = _setup(cuda, False)
+    m2, e2 = _setup(cuda, True)
+    l1, l2 = [], []
+    for b in batches:
+        l1.append(e1.step(b).loss.item())
+        l2.append(e2.step(b).loss.item())
+    e2.finish()
+    assert e2._graph is not None  # steps 3..6 replayed a captured graph
+    for a, b in zip(l1, l2):
+        assert abs(a - b) < 2e-2 * abs(a), (l1, l2)
+    assert e1.scheduler.step_num == e2.scheduler.step_num == len(batches)
+    worst = max(((p - q).abs().max() / q.abs().max().clamp_min(1e-6)).item()
+                for p, q in zip(m1.parameters(), m2.parameters()))
+    assert worst < 5e-2

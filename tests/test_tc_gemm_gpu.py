@@ -164,3 +164,22 @@ def test_moe_grouped_experts_vs_torch(cuda):
     _close(out1, out2, 3e-2)
     for a, b in zip(g1, g2):
         _close(a, b, 5e-2)
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True)])
+def test_dense_strided_ragged(cuda, a_mn, b_mn):
+    """Row-strided views with ragged M, N, K (the LM-head shapes: vocab 50257 padded to a 64 stride)."""
+    torch.manual_seed(11)
+    m, n, k = 300, 1001, 333
+    def view(rows, cols):
+        base = torch.randn(rows, (cols + 63) // 64 * 64, device=cuda).to(torch.bfloat16)
+        return base[:, :cols]
+    a = view(k, m) if a_mn else view(m, k)
+    b = view(k, n) if b_mn else view(n, k)
+    ref = (a.float().t() if a_mn else a.float()) @ (b.float() if b_mn else b.float().t())
+    out = torch.full((m, (n + 63) // 64 * 64), 7.0, device=cuda)
+    _C().tc_gemm_dense(a, b, a_mn, b_mn, True, 128, out[:, :n])
+    _close(out[:, :n], ref, 1e-3)
+    assert (out[:, n:] == 7.0).all()  # nothing written past the logical edge
+    out16 = _C().tc_gemm_dense(a, b, a_mn, b_mn, False, 256, None)
+    _close(out16, ref)
