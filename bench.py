@@ -344,6 +344,13 @@ def main():
             if rank == 0:
                 print(json.dumps({"impl": "reference", "unavailable": f"{type(exc).__name__}: {exc}"[:300]}))
             return 0
+        if world == 1 and not args.no_graph:
+            # A failed stream capture leaves this process's CUDA state unusable: measure the
+            # eager step in a fresh process instead, and say so in the JSON line.
+            print(f"graph capture failed ({type(exc).__name__}: {str(exc)[:200]}); re-running eager",
+                  file=sys.stderr)
+            os.environ["KIMI_BENCH_NOTE"] = f"CUDA-graph step failed ({type(exc).__name__}); eager step measured"
+            os.execv(sys.executable, [sys.executable, os.path.abspath(__file__)] + sys.argv[1:] + ["--no-graph"])
         raise
     tokens = args.batch_per_gpu * SEQ * world
     value = tokens / (ms / 1000.0)
@@ -357,6 +364,10 @@ def main():
         line["launch_detail"] = launches
     if last_loss is not None:
         line["last_loss"] = round(last_loss, 4)
+    if args.impl == "ours":
+        line["config"]["step_mode"] = "eager" if args.no_graph or world > 1 else "cuda_graph"
+        if os.environ.get("KIMI_BENCH_NOTE"):
+            line["note"] = os.environ["KIMI_BENCH_NOTE"]
     if rank == 0:
         print(json.dumps(line))
     if torch.distributed.is_initialized():

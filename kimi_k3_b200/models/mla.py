@@ -393,6 +393,15 @@ class GatedMLA(nn.Module):
             raw = _ops.flash_attention(query, key, value, causal=True)
             out, gate = self._postprocess(raw, hidden_states)
             return GatedMLAOutput(out, None, None, None)
+        if cache is None and not use_cache and not need_probs and attention_mask is None and not output_diagnostics:
+            # Full causal sequence without padding and without a cache to build: no mask at all.
+            key, value = self.projections.reconstruct_kv(latent)
+            self._record_qk_scale(query, key)
+            raw = mla_attention(query, key, value, None, is_causal=True, dropout_p=c.attention_dropout,
+                                keep_output_fp32=c.keep_attention_output_fp32, backend=c.resolved_backend,
+                                training=self.training)
+            out, gate = self._postprocess(raw, hidden_states)
+            return GatedMLAOutput(out, None, None, None)
         current_mask = torch.ones(b, t, dtype=torch.bool, device=dev) if attention_mask is None else attention_mask
         prev = torch.zeros(b, dtype=torch.long, device=dev) if cache is None else cache.sequence_offset
         # The cache stores latents in the dtype the compression produces (bf16 under autocast).

@@ -282,7 +282,8 @@ def qb_histogram(raw_scores, cutoffs, counts, underflow, overflow, min_margin, m
     width = (max_margin - min_margin) / bins
     idx = torch.floor((margins - min_margin) / width).long().clamp_(0, bins - 1)
     flat = idx + torch.arange(e, device=margins.device)[None, :] * bins
-    counts.add_(torch.bincount(flat.reshape(-1), minlength=e * bins).reshape(e, bins))
+    # scatter_add (atomics) rather than bincount: bincount reads the max index on the host
+    counts.view(-1).scatter_add_(0, flat.reshape(-1), torch.ones_like(flat.reshape(-1), dtype=counts.dtype))
 
 
 class _MoEGrouped(torch.autograd.Function):

@@ -1,8 +1,17 @@
-"""The CUDA-graph training step against the eager step on a small model (GPU)."""
+"""The CUDA-graph training step against the eager step on a small model (GPU).
+
+The comparison runs in a child process: a failed stream capture leaves the CUDA context of
+its process unusable, which must not take the rest of the GPU suite down with it.
+"""
+import os
+import subprocess
+import sys
+
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def _setup(cuda, graph):
@@ -26,6 +35,14 @@ def _setup(cuda, graph):
 
 
 def test_graph_step_matches_eager(cuda):
+    env = dict(os.environ, PYTHONPATH=ROOT + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    r = subprocess.run([sys.executable, os.path.abspath(__file__)], env=env, capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "graph-vs-eager ok" in r.stdout
+
+
+def _child(cuda):
     g = torch.Generator().manual_seed(0)
     batches = []
     for _ in range(6):
@@ -46,3 +63,8 @@ def test_graph_step_matches_eager(cuda):
     worst = max(((p - q).abs().max() / q.abs().max().clamp_min(1e-6)).item()
                 for p, q in zip(m1.parameters(), m2.parameters()))
     assert worst < 5e-2
+
+
+if __name__ == "__main__":
+    _child(torch.device("cuda"))
+    print("graph-vs-eager ok")
