@@ -247,7 +247,7 @@ def truncate_batch_to_context(batch: Mapping, max_seq_len: int, *, ignore_index:
                               image_token_id: int | None = None, video_token_id: int | None = None,
                               length_multiple: int = 1):
     """Clip every sequence field to the active context, then to the longest valid row
-    (rounded up to ``length_multiple``). Returns ``(batch, stats)``."""
+    (rounded up to ``length_multiple`` when the batch is that wide). Returns ``(batch, stats)``."""
     if max_seq_len <= 0:
         raise ValueError("max_seq_len must be positive")
     ids = batch.get("input_ids")
@@ -334,6 +334,23 @@ def dynamic_collate(samples: Sequence[Mapping], pad_token_id: int, ignore_index:
     return out
 
 
+def pad_batch_to(batch: dict, width: int, pad_token_id: int, ignore_index: int) -> dict:
+    """Right-pad every ``[B, T, ...]`` sequence field of a collated batch to ``width``."""
+    out = dict(batch)
+    t = batch["input_ids"].shape[1]
+    if width <= t:
+        return out
+    pads = dict(PAD_VALUES, input_ids=pad_token_id, labels=ignore_index)
+    if "attention_mask" not in out:
+        out["attention_mask"] = torch.ones_like(batch["input_ids"], dtype=torch.bool)
+    for name in SEQUENCE_KEYS:
+        v = out.get(name)
+        if torch.is_tensor(v) and v.ndim >= 2 and v.shape[1] == t:
+            fill = v.new_full((v.shape[0], width - t) + tuple(v.shape[2:]), pads.get(name, 0))
+            out[name] = torch.cat((v, fill), dim=1)
+    return out
+
+
 class ProgressiveContextCollator:
     """Clip samples to the active context, collate (dynamic padding by default), trim."""
 
@@ -364,6 +381,10 @@ class ProgressiveContextCollator:
             clipped.append(s)
         batch = (self.base_collator(clipped) if self.base_collator is not None
                  else dynamic_collate(clipped, self.pad_token_id, self.ignore_index))
+        if self.length_multiple > 1:
+            width = batch["input_ids"].shape[1]
+            batch = pad_batch_to(batch, min(self.max_seq_len, -(-width // self.length_multiple) * self.length_multiple),
+                                 self.pad_token_id, self.ignore_index)
         return truncate_batch_to_context(batch, self.max_seq_len, ignore_index=self.ignore_index,
                                          image_token_id=self.image_token_id, video_token_id=self.video_token_id,
                                          length_multiple=self.length_multiple)[0]
@@ -383,5 +404,5 @@ def build_context_loader(factory, max_seq_len: int):
 
 
 __all__ = ["ContextStage", "ContextCurriculumConfig", "ContextCurriculumState", "ContextTransition",
-           "ProgressiveContextCurriculum", "truncate_batch_to_context", "dynamic_collate",
+           "ProgressiveContextCurriculum", "truncate_batch_to_context", "dynamic_collate", "pad_batch_to",
            "ProgressiveContextCollator", "build_context_loader", "default_stages", "SEQUENCE_KEYS"]
