@@ -362,8 +362,11 @@ at::Tensor tc_gemm_dense(at::Tensor a, at::Tensor b, bool a_mn, bool b_mn, bool 
   const int64_t N = b_mn ? b.size(1) : b.size(0);
   TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K, "inner dimensions differ");
   TORCH_CHECK(M > 0 && N > 0 && K > 0, "empty GEMM");
-  at::Tensor out = out_opt.has_value() && out_opt->defined() ? *out_opt
-                   : at::empty({M, N}, a.options().dtype(out_fp32 ? at::kFloat : at::kBFloat16));
+  // A fresh output gets a row stride padded to 8 elements (16 bytes); the result is a view.
+  at::Tensor out = out_opt.has_value() && out_opt->defined()
+                       ? *out_opt
+                       : at::empty({M, (N + 7) / 8 * 8}, a.options().dtype(out_fp32 ? at::kFloat : at::kBFloat16))
+                             .narrow(1, 0, N);
   TORCH_CHECK(out.is_cuda() && out.dim() == 2 && out.size(0) == M && out.size(1) == N && out.stride(1) == 1 &&
                   out.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0,
               "out must be an [M,N] row-major matrix with a 16-byte aligned row stride");

@@ -452,6 +452,36 @@ class KimiK3(nn.Module):
         return out if use_dict else out.to_tuple()
 
     @torch.no_grad()
+    def loss_normalizers(self, input_ids, labels=None, attention_mask=None, loss_mask=None, boundary_mask=None,
+                         token_weights=None, use_mtp: bool = True) -> tuple:
+        """``(ntp_normalizer, mtp_normalizer)`` the pretraining loss of this batch divides by.
+
+        They depend only on ids, labels and masks, so a trainer computes them on the host copy
+        of each micro-batch before the forward: accumulation windows can then backpropagate
+        every micro-batch immediately with the window's global normalisers (token-exact, no
+        retained graphs).
+        """
+        from .losses import align_token_inputs
+        from .mtp import build_mtp_training_view
+        labels = input_ids if labels is None else labels
+        b, t = input_ids.shape
+        if attention_mask is None:
+            pad = self.config.pad_token_id
+            attention_mask = input_ids.ne(pad) if pad is not None else torch.ones_like(input_ids, dtype=torch.bool)
+        ntp = self.pretraining_loss.ntp_loss
+        _, _, valid, w = align_token_inputs(labels, labels, alignment=ntp.label_alignment,
+                                            attention_mask=attention_mask, loss_mask=loss_mask,
+                                            boundary_mask=boundary_mask, token_weights=token_weights,
+                                            ignore_index=ntp.ignore_index)
+        ntp_n = float((w.float() * valid.float()).sum()) if token_weights is not None else float(valid.sum())
+        mtp_n = 0.0
+        if use_mtp and self.mtp is not None and self.config.enable_mtp and t > 2:
+            view = build_mtp_training_view(input_ids.new_zeros(b, t, 1, dtype=torch.float32), input_ids,
+                                           attention_mask, labels, ignore_index=self.pretraining_loss.mtp_loss.ignore_index)
+            mtp_n = float((view.valid_mask & view.target_ids.ne(self.pretraining_loss.mtp_loss.ignore_index)).sum())
+        return ntp_n, mtp_n
+
+    @torch.no_grad()
     def prefill(self, input_ids, attention_mask=None, **kwargs):
         """Encode a prompt and build its cache with the same forward."""
         return self(input_ids=input_ids, attention_mask=attention_mask, use_cache=True, **kwargs)

@@ -60,9 +60,11 @@ def _child(cuda):
     for a, b in zip(l1, l2):
         assert abs(a - b) < 2e-2 * abs(a), (l1, l2)
     assert e1.scheduler.step_num == e2.scheduler.step_num == len(batches)
-    worst = max(((p - q).abs().max() / q.abs().max().clamp_min(1e-6)).item()
-                for p, q in zip(m1.parameters(), m2.parameters()))
-    assert worst < 5e-2
+    # bf16 kernels with atomic reductions are not bitwise deterministic: compare by norms
+    errs = sorted((((p - q).norm() / q.norm().clamp_min(1e-6)).item(), n)
+                  for (n, p), (_, q) in zip(m1.named_parameters(), m2.named_parameters()))
+    print("worst parameters", errs[-5:])
+    assert errs[-1][0] < 5e-2, errs[-5:]
 
 
 if __name__ == "__main__":

@@ -1,0 +1,61 @@
+"""Token-exact accumulation windows against the reference trainer (float64, CPU)."""
+import dataclasses
+
+import pytest
+import torch
+
+from _oracle import expand_expert_grads, max_diff, needs_reference, ref
+from kimi_k3_b200 import KimiK3, kimi_k3_cpu_tiny_config
+from kimi_k3_b200.train.engine import MoEController
+from kimi_k3_b200.train.loop import eval_one_epoch, next_token_preview, train_one_epoch
+from kimi_k3_b200.train.optimizer import KimiOptimizerConfig, build_kimi_optimizer
+
+
+def _batches(n=6, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for i in range(n):
+        ids = torch.randint(5, 128, (2, 26), generator=g)
+        mask = torch.ones(2, 26, dtype=torch.bool)
+        mask[1, 18 + i:] = False  # ragged valid counts: window normalisers matter
+        out.append({"input_ids": ids, "labels": ids.clone(), "attention_mask": mask})
+    return out
+
+
+@needs_reference
+@pytest.mark.reference
+def test_streaming_windows_match_reference_trainer():
+    ref()
+    from src.kimi_k3.config import kimi_k3_cpu_tiny_config as ref_cfg
+    from src.kimi_k3_mini import KimiK3 as RefK3
+    from training.moe_control import MoEController as RefMoE
+    from training.optimizer.config import KimiOptimizerConfig as RefCfg
+    from training.optimizer.hybrid import build_kimi_optimizer as ref_build
+    from training.train_one_epoch import train_one_epoch as ref_train
+    torch.manual_seed(0)
+    theirs = RefK3(dataclasses.replace(ref_cfg(), enable_vision=False)).double()
+    ours = KimiK3(kimi_k3_cpu_tiny_config(enable_vision=False)).double()
+    ours.load_state_dict(theirs.state_dict())
+    kw = dict(adamw_lr=1e-3, muon_lr=1e-2)
+    o1, _ = ref_build(theirs, RefCfg(**kw))
+    o2, _ = build_kimi_optimizer(ours, KimiOptimizerConfig(**kw))
+    data = _batches()
+    r1 = ref_train(theirs, data, o1, grad_accum_steps=3, grad_clip=1.0, use_mtp=True, moe_controller=RefMoE(theirs))
+    r2 = train_one_epoch(ours, data, o2, grad_accum_steps=3, grad_clip=1.0, use_mtp=True,
+                         moe_controller=MoEController(ours))
+    assert r2["optimizer_steps"] == r1["optimizer_steps"] == 2
+    assert abs(r1["loss"] - r2["loss"]) < 1e-9 and r1["ntp_tokens"] == r2["ntp_tokens"]
+    p1 = dict(theirs.named_parameters())
+    p2 = expand_expert_grads((n, p.detach()) for n, p in ours.named_parameters())
+    # fp32 Newton-Schulz (batched here, per matrix there) rounds differently: ~1e-6 per step
+    assert max(max_diff(p1[n], p2[n]) for n in p1) < 2e-5
+
+
+def test_eval_and_preview():
+    torch.manual_seed(1)
+    m = KimiK3(kimi_k3_cpu_tiny_config(enable_vision=False))
+    data = _batches(3)
+    stats = eval_one_epoch(m, data, use_mtp=True)
+    assert stats["num_batches"] == 3 and stats["perplexity"] > 1 and m.training
+    prev = next_token_preview(m, data[0], sample_index=1, max_tokens=8)
+    assert prev["position"] == 17 and len(prev["predicted_ids"]) == 8
