@@ -445,7 +445,7 @@ class KimiDeltaAttention(nn.Module):
         self.decay = LowerBoundedDecay(config.num_heads, config.g_min)
         self.output_norm = HeadwiseRMSNorm(config.num_heads, config.value_head_dim, eps=config.eps)
         self.output_gate = FullRankOutputGate(config.d_model, bias=config.output_gate_bias,
-                                              output_bias=config.output_bias, init_std=config.init_std)
+                                              output_bias=config.output_bias, init_std=config.init_std, value_width=config.value_width)
 
     def _validate_state(self, x, state):
         if state is None:

@@ -213,15 +213,29 @@ def reduce_token_losses(per_token, valid, weights, *, source, zero_valid_policy,
                                    valid.sum(-1).detach())
 
 
+def head_vocab_size(weight) -> int:
+    """Full vocabulary of an LM-head weight (a tensor-parallel shard records the full size)."""
+    meta = getattr(weight, "_kimi_vocab_parallel", None)
+    return int(meta[2]) if meta is not None else int(weight.shape[0])
+
+
 def fused_head_loss(hidden, weight, labels, valid, *, label_smoothing=0.0):
     """Per-row CE of ``hidden @ weight^T`` against ``labels`` for valid rows.
 
     Returns ``(loss_sum, per_row)``; on CUDA the projection + log-sum-exp run
-    fused and ``per_row`` is ``None``.
+    fused and ``per_row`` is ``None``. A vocabulary-sharded head weight (tensor parallel)
+    goes through the fused vocabulary-parallel CE: logits are never gathered.
     """
     flat_h = hidden.reshape(-1, hidden.shape[-1])
     flat_t = labels.reshape(-1).long()
     flat_v = valid.reshape(-1)
+    meta = getattr(weight, "_kimi_vocab_parallel", None)
+    if meta is not None:
+        if label_smoothing:
+            raise ValueError("label smoothing is not supported with a vocabulary-parallel head")
+        from ..parallel.tensor_parallel import vocab_parallel_linear_cross_entropy
+        return vocab_parallel_linear_cross_entropy(flat_h, weight, flat_t, flat_v, vocab_start=meta[0],
+                                                   group=meta[3]), None
     if _ops.use_kernels(hidden) and label_smoothing == 0.0:
         return _ops.linear_cross_entropy(flat_h, weight, flat_t, flat_v), None
     logits = F.linear(flat_h, weight).float()
@@ -306,7 +320,7 @@ class NextTokenCrossEntropyLoss(nn.Module):
                                               attention_mask=attention_mask, loss_mask=loss_mask,
                                               boundary_mask=boundary_mask, token_weights=token_weights,
                                               ignore_index=self.ignore_index)
-        validate_token_ids(al, valid, head_weight.shape[0])
+        validate_token_ids(al, valid, head_vocab_size(head_weight))
         weighted_valid = valid if token_weights is None else valid & (w > 0)
         h = hidden[:, sl]
         if token_weights is not None:
@@ -396,7 +410,7 @@ class MultiTokenPredictionLoss(nn.Module):
     def forward_hidden(self, hidden, head_weight, labels, valid_mask, future_offsets=None) -> MTPLossOutput:
         """Single-depth MTP loss from the MTP hidden state (fused head on CUDA)."""
         valid = valid_mask & labels.ne(self.ignore_index)
-        validate_token_ids(labels, valid, head_weight.shape[0], name="mtp_labels")
+        validate_token_ids(labels, valid, head_vocab_size(head_weight), name="mtp_labels")
         loss_sum, _ = fused_head_loss(hidden, head_weight, labels, valid)
         normalizer = valid.sum().float()
         if not host_checks():

@@ -348,7 +348,7 @@ class GatedMLA(nn.Module):
         self.config = config
         self.projections = MLAProjections(config)
         self.output_gate = FullRankOutputGate(config.d_model, bias=config.output_gate_bias,
-                                              output_bias=config.output_bias, init_std=config.init_std)
+                                              output_bias=config.output_bias, init_std=config.init_std, value_width=config.value_width)
         self.output_dropout = nn.Dropout(config.output_dropout)
         self.absorbed_decode = True
 

@@ -228,14 +228,16 @@ class FullRankOutputGate(nn.Module):
     """``output_proj(sigmoid(gate_proj(residual_input)) * attention_output)``."""
 
     def __init__(self, d_model: int, bias: bool = False, output_bias: bool = False, init_std: float = 0.02,
-                 *, device=None, dtype=None):
+                 *, device=None, dtype=None, value_width: int | None = None):
         super().__init__()
-        if d_model <= 0 or init_std <= 0:
+        value_width = d_model if value_width is None else int(value_width)
+        if d_model <= 0 or init_std <= 0 or value_width <= 0:
             raise ValueError("invalid output gate configuration")
-        self.d_model, self.init_std = d_model, float(init_std)
+        # value_width < d_model only for a tensor-parallel shard owning a subset of the heads
+        self.d_model, self.value_width, self.init_std = d_model, value_width, float(init_std)
         kw = {"device": device, "dtype": dtype}
-        self.gate_proj = nn.Linear(d_model, d_model, bias=bias, **kw)
-        self.output_proj = nn.Linear(d_model, d_model, bias=output_bias, **kw)
+        self.gate_proj = nn.Linear(d_model, value_width, bias=bias, **kw)
+        self.output_proj = nn.Linear(value_width, d_model, bias=output_bias, **kw)
         self.reset_parameters()
 
     def reset_parameters(self) -> None:
@@ -250,10 +252,10 @@ class FullRankOutputGate(nn.Module):
         return torch.sigmoid(self.gate_proj(residual_input))
 
     def forward(self, attention_output: torch.Tensor, residual_input: torch.Tensor, *, return_gate: bool = False):
-        if attention_output.ndim != 3 or attention_output.shape[-1] != self.d_model:
-            raise ValueError(f"attention_output must have shape [B,T,{self.d_model}]")
-        if attention_output.shape != residual_input.shape:
-            raise ValueError("attention_output and residual_input must have identical shapes")
+        if attention_output.ndim != 3 or attention_output.shape[-1] != self.value_width:
+            raise ValueError(f"attention_output must have shape [B,T,{self.value_width}]")
+        if attention_output.shape[:2] != residual_input.shape[:2] or residual_input.shape[-1] != self.d_model:
+            raise ValueError("attention_output and residual_input must share [B,T] (residual width d_model)")
         logits = self.gate_proj(residual_input)
         if _ops.use_kernels(logits):
             gated = _ops.sigmoid_mul(logits, attention_output)

@@ -41,22 +41,51 @@ class QBReducer:
 
 
 class GradientAllReducer:
-    def __init__(self, model: torch.nn.Module, group=None, bucket_bytes: int = 256 << 20):
+    """Average gradients over a data-replica group in flat, dtype-homogeneous buckets.
+
+    With ``overlap=True`` each bucket's all-reduce is launched from a post-accumulate-grad
+    hook as soon as the last gradient of the bucket has been produced, so communication runs
+    under the rest of the backward pass (buckets are filled in reverse parameter order,
+    roughly the order backward produces them; with gradient accumulation only the window's last
+    backward runs ``armed``). ``all_reduce_gradients()`` then launches any
+    bucket that did not complete (parameters without gradients contribute zeros) and waits.
+    ``params`` restricts the reducer to a subset (expert-parallel layouts reduce expert and
+    replicated parameters over different groups).
+    """
+
+    def __init__(self, model: torch.nn.Module, group=None, bucket_bytes: int = 256 << 20, *, params=None,
+                 overlap: bool = False, scale: float | None = None):
         self.model = model
         self.group = group
-        self.bucket_bytes = bucket_bytes
-        self.params = [p for p in model.parameters() if p.requires_grad]
+        self.bucket_bytes = int(bucket_bytes)
+        self._all_params = params is None
+        self.params = [p for p in (params if params is not None else model.parameters()) if p.requires_grad]
+        self.scale = scale
         self._buckets = self._plan()
+        self.overlap = bool(overlap) and self.world_size > 1
+        self._ready = [0] * len(self._buckets)
+        self._pending = {}
+        self._hooks = []
+        self.armed = True  # trainers disarm for all but the last backward of an accumulation window
+        if self.overlap:
+            where = {}
+            for bi, bucket in enumerate(self._buckets):
+                for p in bucket:
+                    where[id(p)] = bi
+            for p in self.params:
+                self._hooks.append(p.register_post_accumulate_grad_hook(
+                    lambda param, bi=where[id(p)]: self._grad_ready(bi)))
 
     def _plan(self):
-        buckets, cur, size, cur_dtype = [], [], 0, None
-        for p in self.params:
+        buckets, cur, size, cur_key = [], [], 0, None
+        for p in reversed(self.params):
             nbytes = p.numel() * p.element_size()
-            if cur and (p.dtype != cur_dtype or size + nbytes > self.bucket_bytes):
+            key = (p.dtype, p.device)
+            if cur and (key != cur_key or size + nbytes > self.bucket_bytes):
                 buckets.append(cur)
                 cur, size = [], 0
             cur.append(p)
-            cur_dtype = p.dtype
+            cur_key = key
             size += nbytes
         if cur:
             buckets.append(cur)
@@ -66,39 +95,68 @@ class GradientAllReducer:
     def world_size(self) -> int:
         return dist.get_world_size(self.group) if dist.is_initialized() else 1
 
+    def _src(self) -> int:
+        return dist.get_global_rank(self.group, 0) if self.group is not None else 0
+
     @torch.no_grad()
-    def broadcast_parameters(self, src: int = 0) -> None:
+    def broadcast_parameters(self, src: int | None = None) -> None:
+        """Make every replica start from the group's first rank's parameters and buffers."""
         if self.world_size == 1:
             return
-        tensors = list(self.model.parameters()) + list(self.model.buffers())
-        by_dtype: dict = {}
+        src = self._src() if src is None else src
+        seen, tensors = set(), []
+        # a reducer over a parameter subset only owns (and broadcasts) that subset
+        owned = list(self.model.parameters()) + list(self.model.buffers()) if self._all_params else list(self.params)
+        for t in owned:
+            if id(t) not in seen:
+                seen.add(id(t))
+                tensors.append(t)
+        by_key: dict = {}
         for t in tensors:
-            by_dtype.setdefault((t.dtype, t.device), []).append(t)
-        for ts in by_dtype.values():
+            by_key.setdefault((t.dtype, t.device), []).append(t)
+        for ts in by_key.values():
             flat = _flatten_dense_tensors([t.data for t in ts])
             dist.broadcast(flat, src=src, group=self.group)
-            for t, s in zip(ts, _unflatten_dense_tensors(flat, [t.data for t in ts])):
-                t.data.copy_(s)
+            for t, v in zip(ts, _unflatten_dense_tensors(flat, [t.data for t in ts])):
+                t.data.copy_(v)
+
+    @torch.no_grad()
+    def _launch(self, bi: int) -> None:
+        if bi in self._pending:
+            return
+        bucket = self._buckets[bi]
+        grads = [p.grad if p.grad is not None else torch.zeros_like(p) for p in bucket]
+        flat = _flatten_dense_tensors(grads)
+        flat.mul_(self.scale if self.scale is not None else 1.0 / self.world_size)
+        self._pending[bi] = (grads, flat, dist.all_reduce(flat, group=self.group, async_op=True))
+
+    def _grad_ready(self, bi: int) -> None:
+        if not self.armed:  # an earlier micro-batch of an accumulation window
+            return
+        self._ready[bi] += 1
+        if self._ready[bi] == len(self._buckets[bi]):
+            self._launch(bi)
 
     @torch.no_grad()
     def all_reduce_gradients(self) -> None:
-        world = self.world_size
-        if world == 1:
+        if self.world_size == 1:
             return
-        pending = []
-        for bucket in self._buckets:
-            grads = [p.grad if p.grad is not None else torch.zeros_like(p) for p in bucket]
-            flat = _flatten_dense_tensors(grads)
-            flat.div_(world)
-            work = dist.all_reduce(flat, group=self.group, async_op=True)
-            pending.append((bucket, grads, flat, work))
-        for bucket, grads, flat, work in pending:
+        for bi in range(len(self._buckets)):
+            self._launch(bi)
+        for bi, (grads, flat, work) in sorted(self._pending.items()):
             work.wait()
-            for p, g in zip(bucket, _unflatten_dense_tensors(flat, grads)):
+            for p, v in zip(self._buckets[bi], _unflatten_dense_tensors(flat, grads)):
                 if p.grad is None:
-                    p.grad = g.clone()
+                    p.grad = v.clone()
                 else:
-                    p.grad.copy_(g)
+                    p.grad.copy_(v)
+        self._pending.clear()
+        self._ready = [0] * len(self._buckets)
+
+    def remove_hooks(self) -> None:
+        for h in self._hooks:
+            h.remove()
+        self._hooks = []
 
     def qb_reducer(self) -> QBReducer:
         return QBReducer(self.group)

@@ -92,11 +92,17 @@ def _dist_sum(values: list, context) -> list:
     if context is None or not getattr(context, "initialized", False):
         return list(values)
     t = torch.tensor(values, dtype=torch.float64, device=context.device)
-    for group, size in ((getattr(context, "dp_group", None), getattr(context, "dp_size", 1)),
-                        (getattr(context, "ep_group", None), getattr(context, "ep_size", 1))):
+    for group, size in _replica_axes(context):
         if size > 1:
             torch.distributed.all_reduce(t, group=group)
     return t.tolist()
+
+
+def _replica_axes(context) -> tuple:
+    if hasattr(context, "data_replica_groups"):
+        return context.data_replica_groups
+    return ((getattr(context, "dp_group", None), getattr(context, "dp_size", 1)),
+            (getattr(context, "ep_group", None), getattr(context, "ep_size", 1)))
 
 
 def _dist_all_true(flag: bool, context) -> bool:
@@ -130,8 +136,9 @@ def train_one_epoch(model, dataloader, optimizer, *, device="cpu", scheduler=Non
                     max_seq_len: int | None = None, context_ignore_index: int = -100,
                     image_token_id: int | None = None, video_token_id: int | None = None,
                     stop_on_context_transition: bool = True, distributed_context=None, grad_reducer=None,
-                    engine=None) -> dict:
-    """Train one epoch (reference signature plus ``grad_reducer``/``engine``)."""
+                    grad_norm_fn=None, engine=None) -> dict:
+    """Train one epoch (reference signature plus ``grad_reducer`` / ``grad_norm_fn``: the
+    gradient synchronisation and global norm of a parallel plan)."""
     from .curriculum import truncate_batch_to_context
     if grad_accum_steps <= 0:
         raise ValueError("grad_accum_steps must be positive")
@@ -145,8 +152,10 @@ def train_one_epoch(model, dataloader, optimizer, *, device="cpu", scheduler=Non
     raw = _unwrap(model)
     streaming = hasattr(raw, "loss_normalizers")
     params = [p for p in model.parameters() if p.requires_grad]
-    replicas = (getattr(distributed_context, "dp_size", 1) * getattr(distributed_context, "ep_size", 1)
-                if distributed_context is not None and getattr(distributed_context, "initialized", False) else 1)
+    replicas = 1
+    if distributed_context is not None and getattr(distributed_context, "initialized", False):
+        for _, size in _replica_axes(distributed_context):
+            replicas *= size
     optimizer.zero_grad(set_to_none=True)
     totals = {"contribs": [], "steps": 0, "skipped": 0, "pre": 0.0, "post": 0.0, "n_norm": 0, "samples": 0}
     started = time.perf_counter()
@@ -224,6 +233,9 @@ def train_one_epoch(model, dataloader, optimizer, *, device="cpu", scheduler=Non
                 fwd_s += time.perf_counter() - f0
                 if diagnostics is not None and i == 0:
                     diag_metrics = diagnostics.collect_output(out, step=step_no)
+                reducer = getattr(grad_reducer, "__self__", None)
+                if reducer is not None and hasattr(reducer, "armed"):
+                    reducer.armed = i == len(window) - 1 or not streaming
                 if streaming:
                     obj = c.ntp_loss_sum * (replicas / counts[0])
                     if c.mtp_loss_sum is not None and counts[1] > 0:
@@ -260,7 +272,7 @@ def train_one_epoch(model, dataloader, optimizer, *, device="cpu", scheduler=Non
                 grad_reducer()
             if scaler is not None:
                 scaler.unscale_(optimizer)
-            pre_t = global_grad_norm(params, distributed_context)
+            pre_t = grad_norm_fn() if grad_norm_fn is not None else global_grad_norm(params, distributed_context)
             pre = None if pre_t is None else float(pre_t)
             finite = _dist_all_true(pre is None or math.isfinite(pre), distributed_context)
             if finite and grad_clip is not None and pre is not None:

@@ -146,13 +146,17 @@ def combine_distributed_window_loss(contribs: list, context) -> tuple[torch.Tens
                                                      else torch.zeros((), dtype=torch.float64,
                                                                       device=ntp_sum.device))])
     packed = torch.cat([local, sums])
-    for group in (getattr(context, "dp_group", None), getattr(context, "ep_group", None)):
-        if group is not None and dist.get_world_size(group) > 1:
+    axes = (context.data_replica_groups if hasattr(context, "data_replica_groups") else
+            ((getattr(context, "dp_group", None), getattr(context, "dp_size", 1)),
+             (getattr(context, "ep_group", None), getattr(context, "ep_size", 1))))
+    replicas = 1
+    for group, size in axes:
+        replicas *= size
+        if group is not None and size > 1:
             dist.all_reduce(packed, group=group)
     ntp_n, mtp_n, tokens, g_ntp, g_mtp = packed.tolist()
     if ntp_n <= 0:
         raise ValueError("accumulation window contains no valid NTP tokens")
-    replicas = getattr(context, "dp_size", 1) * getattr(context, "ep_size", 1)
     obj = ntp_sum * replicas / ntp_n
     mtp_loss = None
     if mtp_items:
