@@ -154,7 +154,8 @@ def run_ours(args, world, rank, local):
     dev = torch.device("cuda", local)
     torch.manual_seed(1337)
     model = KimiK3(profile_model_config(PROFILE, vocab_size=VOCAB)).to(dev)
-    reducer = GradientAllReducer(model) if world > 1 else None
+    # bucketed all-reduce launched from backward hooks: communication overlaps the backward pass
+    reducer = GradientAllReducer(model, bucket_bytes=64 << 20, overlap=True) if world > 1 else None
     if reducer is not None:
         reducer.broadcast_parameters()
     opt, _ = build_kimi_optimizer(model, KimiOptimizerConfig(**optimizer_settings()))

@@ -109,6 +109,7 @@ class ExpertParallelMoE(StableLatentMoE):
             local.up_proj.copy_(full.up_proj[s:e])
             local.down_proj.copy_(full.down_proj[s:e])
         local._kimi_expert_parallel = (s, e, c.num_routed_experts)
+        local._kimi_ep_group = group
         self.routed_experts = local
         for p in local.parameters():
             p._kimi_local_expert = True

@@ -93,6 +93,14 @@ class TensorParallelKDA(nn.Module):
         mark_tp_partial(dst.alpha_down.weight)
         if module.output_norm.weight is not None and not module.output_norm.per_head_affine:
             mark_tp_partial(self.inner.output_norm.weight)
+        # dimension along which each inner parameter is a shard of the full one (None: replicated)
+        self.shard_dims = {"projections.q_proj.weight": 0, "projections.k_proj.weight": 0,
+                           "projections.v_proj.weight": 0, "projections.q_conv.weight": 0,
+                           "projections.k_conv.weight": 0, "projections.v_conv.weight": 0,
+                           "projections.beta_proj.weight": 0, "projections.alpha_down.weight": None,
+                           "projections.alpha_up.weight": 0, "projections.b_alpha": 0, "decay.A_log": 0,
+                           "output_norm.weight": 0 if module.output_norm.per_head_affine else None,
+                           "output_gate.gate_proj.weight": 0, "output_gate.output_proj.weight": 1}
 
     def forward(self, hidden_states, attention_mask=None, state=None, mode="chunkwise", output_final_state=False,
                 output_diagnostics=False):
@@ -126,6 +134,9 @@ class TensorParallelMLA(nn.Module):
         _copy(self.inner.output_gate.gate_proj.weight, module.output_gate.gate_proj.weight[s * dv:e * dv])
         _copy(self.inner.output_gate.output_proj.weight, module.output_gate.output_proj.weight[:, s * dv:e * dv])
         mark_tp_partial(dst.latent_kv.compression.weight)
+        self.shard_dims = {"projections.query.weight": 0, "projections.latent_kv.compression.weight": None,
+                           "projections.latent_kv.key_up.weight": 0, "projections.latent_kv.value_up.weight": 0,
+                           "output_gate.gate_proj.weight": 0, "output_gate.output_proj.weight": 1}
         self.inner._kimi_qk_group = group  # QK-Clip takes the MAX scale over the heads of all ranks
         for attr in ("absorbed_decode",):
             if hasattr(module, attr):

@@ -425,6 +425,16 @@ class KimiMuon(torch.optim.Optimizer):
             return torch.float32
         return torch.bfloat16
 
+    def restrict_to(self, param_ids) -> None:
+        """Sharded data parallelism: this rank updates (and keeps state for) only these
+        parameters; the others are broadcast by their owners after the step."""
+        self._owned = set(param_ids)
+        self._buckets = None
+
+    def _mine(self, p) -> bool:
+        owned = getattr(self, "_owned", None)
+        return owned is None or id(p) in owned
+
     # ---- bucketed state: one momentum tensor [count, rows, cols] per (group, matrix shape)
     def _ensure_buckets(self) -> list:
         """Per-parameter momentum buffers become views into one tensor per bucket, so a step
@@ -434,6 +444,8 @@ class KimiMuon(torch.optim.Optimizer):
         keyed: dict = {}
         for gi, group in enumerate(self.param_groups):
             for p in group["params"]:
+                if not self._mine(p):
+                    continue
                 slot = self._slots[id(p)]
                 keyed.setdefault((gi, slot.rows, slot.cols, p.device, p.dtype), []).append(p)
         buckets = []
@@ -465,7 +477,7 @@ class KimiMuon(torch.optim.Optimizer):
         if closure is not None:
             with torch.enable_grad():
                 closure()
-        if any(p.grad is None for g in self.param_groups for p in g["params"]):
+        if any(p.grad is None for g in self.param_groups for p in g["params"] if self._mine(p)):
             if skip is not None:
                 raise RuntimeError("device-flag Muon steps need a gradient for every parameter")
             return self._step_sparse()
@@ -516,7 +528,7 @@ class KimiMuon(torch.optim.Optimizer):
         for group in self.param_groups:
             lr, mom, wd = group["lr"], group["momentum"], group["weight_decay"]
             for p in group["params"]:
-                if p.grad is None:
+                if p.grad is None or not self._mine(p):
                     continue
                 slot = self._slots[id(p)]
                 buf = self.state[p]["momentum_buffer"]
@@ -742,6 +754,21 @@ class KimiHybridOptimizer:
                                   0, {})
         self.last_step_report = rep
         return rep
+
+    def restrict_to(self, param_ids) -> None:
+        """Update only ``param_ids`` (sharded data parallelism): Muon keeps state for its owned
+        matrices; AdamW skips the others because their gradients are dropped before its step."""
+        self._owned = set(param_ids)
+        self.muon.restrict_to(self._owned)
+
+    def drop_foreign_gradients(self) -> None:
+        owned = getattr(self, "_owned", None)
+        if owned is None:
+            return
+        for g in self.param_groups:
+            for p in g["params"]:
+                if id(p) not in owned:
+                    p.grad = None
 
     def undo_step_count(self) -> None:
         """A device-mode step turned out to be skipped: the host step counter steps back."""

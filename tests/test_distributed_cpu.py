@@ -31,19 +31,28 @@ def _model(qb="exact"):
     return KimiK3(cfg).double()
 
 
-def _train(model, batch, kind, *, context=None, plan=None, steps=1):
+def _train(model, batch, kind, *, context=None, plan=None, steps=1, zero=False):
     from kimi_k3_b200.train.engine import MoEController
     from kimi_k3_b200.train.loop import train_one_epoch
     from kimi_k3_b200.train.optimizer import KimiOptimizerConfig, build_kimi_optimizer
     # a large AdamW epsilon keeps the update linear in tiny gradients, whose float32 rounding
     # (the vocabulary-parallel logits) would otherwise be amplified to full-size updates
     opt, _ = build_kimi_optimizer(model, KimiOptimizerConfig(kind=kind, adamw_lr=1e-3, muon_lr=1e-2, adamw_eps=1e-2))
-    ctl = MoEController(model, reducer=None if plan is None else plan.qb_reducer())
+    if zero:
+        from kimi_k3_b200.parallel.data_parallel import QBReducer
+        from kimi_k3_b200.parallel.zero import ZeroDataParallel
+        zdp = ZeroDataParallel(model, opt, context.dp_group)
+        zdp.broadcast_parameters()
+        ctl = MoEController(model, reducer=QBReducer(context.dp_group))
+        opt, sync, norm = zdp, zdp.reduce_gradients, zdp.grad_norm
+    else:
+        ctl = MoEController(model, reducer=None if plan is None else plan.qb_reducer())
+        sync = None if plan is None else plan.sync_gradients
+        norm = None if plan is None else plan.grad_norm
     res = None
     for _ in range(steps):
         res = train_one_epoch(model, [batch], opt, grad_clip=0.5, use_mtp=True, moe_controller=ctl,
-                              distributed_context=context, grad_reducer=None if plan is None else plan.sync_gradients,
-                              grad_norm_fn=None if plan is None else plan.grad_norm)
+                              distributed_context=context, grad_reducer=sync, grad_norm_fn=norm)
     return res
 
 
@@ -60,6 +69,8 @@ def _rank(rank, world, layout, kind, qb):
     cfg = {"enabled": True, "backend": "gloo", "timeout_seconds": 120}
     if layout == "dp":
         cfg["data_parallel"] = {"mode": "ddp", "size": world}
+    elif layout == "fsdp":
+        cfg["data_parallel"] = {"mode": "fsdp", "size": world}
     elif layout == "tp":
         cfg["tensor_parallel"] = {"enabled": True, "size": world}
     elif layout == "ep":
@@ -70,15 +81,17 @@ def _rank(rank, world, layout, kind, qb):
     dcfg = distributed_config_from_dict(cfg)
     ctx = setup_distributed(dcfg)
     model = _model(qb)
-    plan = parallelize_kimi_model(model, dcfg, ctx)
-    plan.broadcast_parameters()
+    plan = None
+    if layout != "fsdp":
+        plan = parallelize_kimi_model(model, dcfg, ctx)
+        plan.broadcast_parameters()
     full = _global_batch(world)
-    data_replicas = world if layout in ("dp", "ep") else 1
+    data_replicas = world if layout in ("dp", "ep", "fsdp") else 1
     if data_replicas > 1:
         batch = {k: v[2 * ctx.global_rank: 2 * ctx.global_rank + 2] for k, v in full.items()}
     else:
         batch = full
-    res = _train(model, batch, kind, context=ctx, plan=plan, steps=2)
+    res = _train(model, batch, kind, context=ctx, plan=plan, steps=2, zero=layout == "fsdp")
     out = {n: p.detach().clone() for n, p in model.named_parameters()
            if not getattr(p, "_kimi_tp_shard", False) and not getattr(p, "_kimi_local_expert", False)}
     experts = {n: p.detach().clone() for n, p in model.named_parameters() if getattr(p, "_kimi_local_expert", False)}
@@ -96,7 +109,7 @@ def _compare(ref_params, got, tol):
 
 
 @pytest.mark.parametrize("layout,kind", [("dp", "per_head_muon_adamw"), ("tp", "adamw"), ("ep", "per_head_muon_adamw"),
-                                         ("tp_ep_overlay", "adamw")])
+                                         ("tp_ep_overlay", "adamw"), ("fsdp", "per_head_muon_adamw")])
 def test_parallel_layout_matches_single_process(layout, kind):
     world = 2
     # Muon's Newton-Schulz runs in float32: float64 summation-order differences between the
@@ -114,3 +127,48 @@ def test_parallel_layout_matches_single_process(layout, kind):
             for n, v in experts.items():
                 per = v.shape[0]
                 assert (ref_params[n][rank * per:(rank + 1) * per] - v).abs().max().item() < tol, n
+
+
+def _ckpt_rank(rank, world, path):
+    import os
+    from kimi_k3_b200.parallel.checkpoint import (export_rank0_full_checkpoint, load_distributed_checkpoint,
+                                                  save_distributed_checkpoint)
+    from kimi_k3_b200.parallel.config import distributed_config_from_dict
+    from kimi_k3_b200.parallel.environment import setup_distributed
+    from kimi_k3_b200.parallel.parallelize import parallelize_kimi_model
+    dcfg = distributed_config_from_dict({"enabled": True, "backend": "gloo",
+                                         "tensor_parallel": {"enabled": True, "size": world},
+                                         "expert_parallel": {"enabled": True, "size": world,
+                                                             "overlay_tensor_parallel": True}})
+    ctx = setup_distributed(dcfg)
+    b = _global_batch(world)
+    m = _model()
+    parallelize_kimi_model(m, dcfg, ctx)
+    with torch.no_grad():
+        for p in m.parameters():  # make the state differ from the seeded init
+            p.add_(0.01 * torch.randn_like(p))
+    m.eval()
+    ref = m(input_ids=b["input_ids"], attention_mask=b["attention_mask"]).logits
+    save_distributed_checkpoint(os.path.join(path, "step_1"), model=m, context=ctx, step=1)
+    m2 = _model()
+    parallelize_kimi_model(m2, dcfg, ctx)
+    load_distributed_checkpoint(os.path.join(path, "step_1"), model=m2, context=ctx)
+    m2.eval()
+    got = m2(input_ids=b["input_ids"], attention_mask=b["attention_mask"]).logits
+    export_rank0_full_checkpoint(os.path.join(path, "full.pt"), model=m, context=ctx)
+    ctx.close()
+    return (ref - got).abs().max().item(), ref
+
+
+def test_distributed_checkpoint_roundtrip_and_full_export(tmp_path):
+    from kimi_k3_b200.train.checkpoints import load_checkpoint
+    res = run_ranks(_ckpt_rank, 2, str(tmp_path))
+    assert all(r[0] == 0.0 for r in res)
+    assert (tmp_path / "step_1" / "SUCCESS").is_file() and (tmp_path / "step_1" / "rank_00001.pt").is_file()
+    single = _model()
+    info = load_checkpoint(tmp_path / "full.pt", single)
+    assert not info["missing_keys"] and not info["unexpected_keys"]
+    single.eval()
+    b = _global_batch(2)
+    logits = single(input_ids=b["input_ids"], attention_mask=b["attention_mask"]).logits
+    assert (logits - res[0][1]).abs().max().item() < 1e-6  # the export reassembles the sharded model
