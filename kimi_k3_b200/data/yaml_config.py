@@ -140,15 +140,18 @@ def _loader(dataset, cfg: LoaderConfig, *, train: bool, max_seq_len: int, pad_to
             distributed_context=None, length_multiple: int = 1) -> DataLoader:
     collate = ProgressiveContextCollator(max_seq_len, pad_token_id=pad_token_id, ignore_index=ignore_index,
                                          length_multiple=length_multiple)
+    # The training loader always samples through the resumable sampler: its shuffle is seeded by
+    # (seed, epoch), so a run resumed at epoch e sees exactly the batches it would have seen.
     sampler = None
     ctx = distributed_context
+    replicas, rank = 1, 0
     if ctx is not None and getattr(ctx, "initialized", False):
         replicas = ctx.data_replicas if hasattr(ctx, "data_replicas") else ctx.dp_size * ctx.ep_size
-        if replicas > 1:
-            rank = ctx.dp_rank if getattr(ctx, "ep_overlays_tp", False) else ctx.dp_rank * ctx.ep_size + ctx.ep_rank
-            sampler = StatefulDistributedSampler(dataset, num_replicas=replicas, rank=rank,
-                                                 shuffle=cfg.shuffle_train if train else False, seed=cfg.seed,
-                                                 drop_last=cfg.drop_last if train else False)
+        rank = ctx.dp_rank if getattr(ctx, "ep_overlays_tp", False) else ctx.dp_rank * ctx.ep_size + ctx.ep_rank
+    if train or replicas > 1:
+        sampler = StatefulDistributedSampler(dataset, num_replicas=replicas, rank=rank,
+                                             shuffle=cfg.shuffle_train if train else False, seed=cfg.seed,
+                                             drop_last=cfg.drop_last if train else False)
     kw = {} if cfg.num_workers == 0 or cfg.prefetch_factor is None else {"prefetch_factor": cfg.prefetch_factor}
     return DataLoader(dataset, batch_size=cfg.batch_size if train else cfg.eval_batch_size,
                       shuffle=cfg.shuffle_train if train and sampler is None else False, sampler=sampler,

@@ -65,8 +65,6 @@ def validate_distributed_model_config(config: DistributedConfig, model_config) -
             raise ConfigError(f"routed experts={moe.num_routed_experts} must be divisible by EP size={ep.size}")
         if moe.top_k > moe.num_routed_experts:
             raise ConfigError("MoE top-k exceeds routed expert count")
-    if config.data_parallel.mode == "fsdp" and not torch.cuda.is_available() and config.backend != "gloo":
-        raise ConfigError("FSDP requires CUDA (or an explicit gloo backend for CPU tests)")
 
 
 def _tag(params, **flags) -> None:

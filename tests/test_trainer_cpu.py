@@ -59,3 +59,36 @@ def test_eval_and_preview():
     assert stats["num_batches"] == 3 and stats["perplexity"] > 1 and m.training
     prev = next_token_preview(m, data[0], sample_index=1, max_tokens=8)
     assert prev["position"] == 17 and len(prev["predicted_ids"]) == 8
+
+
+def test_yaml_trainer_end_to_end_and_resume(tmp_path):
+    """The cpu_smoke pipeline trains through ``train_kimi_from_yaml``, checkpoints, and resumes."""
+    import yaml
+    from kimi_k3_b200.config.model_yaml import build_model_from_yaml
+    from kimi_k3_b200.config.profiles import write_pipeline
+    from kimi_k3_b200.data import build_dataloaders_from_yaml
+    from kimi_k3_b200.train.trainer import train_kimi_from_yaml
+    d = write_pipeline("cpu_smoke", tmp_path / "prof")
+    tr = yaml.safe_load((d / "training.yaml").read_text())
+    tr["checkpoint"]["output_dir"] = str(tmp_path / "ckpt")
+    tr["training"]["epochs"] = 2
+    tr["runtime"]["verbose"] = False
+    tr["runtime"]["use_ema"] = True
+    (d / "training.yaml").write_text(yaml.safe_dump(tr))
+    data = build_dataloaders_from_yaml(d / "data.yaml")
+    torch.manual_seed(0)
+    model = build_model_from_yaml(d / "model.yaml", data_bundle=data)
+    res = train_kimi_from_yaml(d / "training.yaml", model=model, data=data)
+    assert res["state"].optimizer_step == 16 and res["state"].epoch == 2
+    assert len(res["history"]["validation"]) == 2 and res["last_checkpoint"].is_file()
+    assert (tmp_path / "ckpt" / "latest").is_file()
+    # resume from the epoch-0 checkpoint and finish epoch 1 again: same final weights
+    tr["checkpoint"]["resume_from"] = str(tmp_path / "ckpt" / "kimi_k3_cpu_smoke_epoch_0000.pt")
+    tr["checkpoint"]["output_dir"] = str(tmp_path / "ckpt2")
+    (d / "training.yaml").write_text(yaml.safe_dump(tr))
+    data2 = build_dataloaders_from_yaml(d / "data.yaml")
+    model2 = build_model_from_yaml(d / "model.yaml", data_bundle=data2)
+    res2 = train_kimi_from_yaml(d / "training.yaml", model=model2, data=data2)
+    assert res2["state"].optimizer_step == 16
+    for (n, p), (_, q) in zip(res["model"].named_parameters(), res2["model"].named_parameters()):
+        assert torch.equal(p, q), n
