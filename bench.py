@@ -204,7 +204,10 @@ def run_ours(args, world, rank, local):
     barrier()
     e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1000.0 / args.steps)
     h2d = sum(v.numel() * v.element_size() for v in host_batches[0].values())
-    launches = count_launches(engine, dev_batches[0]) if rank == 0 else None
+    # every rank runs the profiled step (it contains collectives); rank 0 reports it
+    launches = count_launches(engine, dev_batches[0])
+    if rank != 0:
+        launches = None
     return ms, e2e_ms, clocks, h2d, 4, launches, losses[-1]
 
 
