@@ -1,0 +1,239 @@
+"""Device microbenchmarks of the hand-written sm_100a kernels, with roofline fractions.
+
+Each case times one op (forward, or forward + backward) with CUDA events after
+warm-up, flushing L2 between repeats, and prints one JSON line with the median
+and the achieved FLOP/s or bytes/s as fractions of the measured peaks. The same
+entry points are the small, self-terminating workloads used for Nsight Compute
+captures of one kernel, e.g.::
+
+    python -m kimi_k3_b200.bench kernels kda --batch 2 --tokens 1024 --heads 10 --repeats 3
+
+Cases: ``gemm`` (tcgen05 dense GEMM vs cuBLAS), ``kda`` (chunked KDA forward /
+backward), ``moe`` (grouped routed experts), ``linear_ce`` (LM head + CE),
+``attention`` (causal flash attention), ``attnres`` (depth softmax mix).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+import torch.nn.functional as F
+
+from .timing import roofline, time_fn
+
+
+def _emit(row: dict) -> dict:
+    print(json.dumps(row), flush=True)
+    return row
+
+
+def _require_cuda():
+    if not torch.cuda.is_available():
+        raise SystemExit("kernel benchmarks need a CUDA device")
+    from ..ops import _loader
+    return _loader.require(), torch.device("cuda")
+
+
+def kda_flops_per_chunk_head(c: int = 64, dk: int = 64, dv: int = 64) -> float:
+    """Chunked KDA forward FLOPs for one 64-token chunk of one head: the two intra-chunk
+    score products, the unit-triangular solve, the two UT products, the state read
+    (``w S``, ``q S``), the intra output and the state update."""
+    return 2.0 * (2 * c * c * dk + c ** 3 / 3 + c * c * dk + c * c * dv + 2 * c * dk * dv + c * c * dv + c * dk * dv)
+
+
+def bench_gemm(args) -> list:
+    C, dev = _require_cuda()
+    torch.manual_seed(0)
+    m, n, k = args.m, args.n, args.k
+    a = torch.randn(m, k, device=dev).bfloat16()
+    b = torch.randn(n, k, device=dev).bfloat16()
+    out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    rows = []
+    flops = 2.0 * m * n * k
+    for bn in (128, 256):
+        t = time_fn(lambda: C.tc_gemm_dense(a, b, False, False, False, bn, out), device=dev,
+                    warmup=args.warmup, repeats=args.repeats)
+        rows.append(_emit({"case": "gemm", "impl": f"tcgen05_bn{bn}", "m": m, "n": n, "k": k, **t.as_dict(),
+                           **roofline(t.median_ms, flops=flops)}))
+    ref = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    t = time_fn(lambda: torch.mm(a, b.t(), out=ref), device=dev, warmup=args.warmup, repeats=args.repeats)
+    rows.append(_emit({"case": "gemm", "impl": "cublas", "m": m, "n": n, "k": k, **t.as_dict(),
+                       **roofline(t.median_ms, flops=flops)}))
+    err = ((out.float() - ref.float()).norm() / ref.float().norm()).item()
+    rows.append(_emit({"case": "gemm", "check": "rel_err_vs_cublas", "value": err}))
+    return rows
+
+
+def bench_kda(args) -> list:
+    from ..ops import kda_chunk
+    _, dev = _require_cuda()
+    torch.manual_seed(0)
+    b, t, h = args.batch, args.tokens, args.heads
+    q = F.normalize(torch.randn(b, t, h, 64, device=dev), dim=-1).bfloat16().requires_grad_()
+    k = F.normalize(torch.randn(b, t, h, 64, device=dev), dim=-1).bfloat16().requires_grad_()
+    v = torch.randn(b, t, h, 64, device=dev).bfloat16().requires_grad_()
+    g = (-5 * torch.sigmoid(torch.randn(b, t, h, 64, device=dev) - 2)).requires_grad_()
+    beta = torch.sigmoid(torch.randn(b, t, h, device=dev)).requires_grad_()
+    do = torch.randn(b, t, h, 64, device=dev).bfloat16()
+    chunks = b * h * math.ceil(t / 64)
+    fwd_flops = chunks * kda_flops_per_chunk_head()
+    io_bytes = b * t * h * (64 * 2 * 4 + 64 * 4 + 4)  # q k v o bf16, g fp32, beta fp32
+
+    def fwd():
+        with torch.no_grad():
+            kda_chunk(q, k, v, g, beta, None, False)
+
+    def fwd_bwd():
+        o, _ = kda_chunk(q, k, v, g, beta, None, False)
+        o.backward(do)
+
+    rows = []
+    tf = time_fn(fwd, device=dev, warmup=args.warmup, repeats=args.repeats)
+    rows.append(_emit({"case": "kda", "pass": "forward", "batch": b, "tokens": t, "heads": h, **tf.as_dict(),
+                       **roofline(tf.median_ms, flops=fwd_flops, bytes_moved=io_bytes)}))
+    tb = time_fn(fwd_bwd, device=dev, warmup=args.warmup, repeats=args.repeats)
+    # backward ~ 2x the forward products plus the recomputed forward
+    rows.append(_emit({"case": "kda", "pass": "forward+backward", "batch": b, "tokens": t, "heads": h,
+                       **tb.as_dict(), **roofline(tb.median_ms, flops=3 * fwd_flops, bytes_moved=3 * io_bytes)}))
+    return rows
+
+
+def bench_moe(args) -> list:
+    from ..ops import moe_grouped_experts
+    _, dev = _require_cuda()
+    torch.manual_seed(0)
+    m, lat, hid, e, topk = args.tokens, args.latent, args.hidden, args.experts, args.topk
+    x = torch.randn(m, lat, device=dev).bfloat16().requires_grad_()
+    wg = (torch.randn(e, hid, lat, device=dev) / lat ** 0.5).bfloat16().requires_grad_()
+    wu = (torch.randn(e, hid, lat, device=dev) / lat ** 0.5).bfloat16().requires_grad_()
+    wd = (torch.randn(e, lat, hid, device=dev) / hid ** 0.5).bfloat16().requires_grad_()
+    scores = torch.randn(m, e, device=dev)
+    w, sel = scores.sigmoid().topk(topk, dim=-1)
+    w = (w / w.sum(-1, keepdim=True)).requires_grad_()
+    sel = sel.to(torch.int32)
+    flops = 2.0 * m * topk * (2 * hid * lat + hid * lat)
+
+    def fwd():
+        with torch.no_grad():
+            moe_grouped_experts(x, sel, w, wg, wu, wd, 4.0, 25.0)
+
+    def fwd_bwd():
+        moe_grouped_experts(x, sel, w, wg, wu, wd, 4.0, 25.0).sum().backward()
+
+    rows = []
+    tf = time_fn(fwd, device=dev, warmup=args.warmup, repeats=args.repeats)
+    rows.append(_emit({"case": "moe", "pass": "forward", "tokens": m, "latent": lat, "hidden": hid, "experts": e,
+                       "top_k": topk, **tf.as_dict(), **roofline(tf.median_ms, flops=flops)}))
+    tb = time_fn(fwd_bwd, device=dev, warmup=args.warmup, repeats=args.repeats)
+    rows.append(_emit({"case": "moe", "pass": "forward+backward", "tokens": m, "latent": lat, "hidden": hid,
+                       "experts": e, "top_k": topk, **tb.as_dict(), **roofline(tb.median_ms, flops=4 * flops)}))
+    return rows
+
+
+def bench_linear_ce(args) -> list:
+    from ..ops import linear_cross_entropy
+    _, dev = _require_cuda()
+    torch.manual_seed(0)
+    n, d, v = args.rows, args.dim, args.vocab
+    hdn = torch.randn(n, d, device=dev).bfloat16().requires_grad_()
+    wt = (torch.randn(v, d, device=dev) / d ** 0.5).requires_grad_()
+    tgt = torch.randint(0, v, (n,), device=dev)
+    valid = torch.ones(n, dtype=torch.bool, device=dev)
+
+    def fwd_bwd():
+        linear_cross_entropy(hdn, wt, tgt, valid).backward()
+
+    t = time_fn(fwd_bwd, device=dev, warmup=args.warmup, repeats=args.repeats)
+    return [_emit({"case": "linear_ce", "pass": "forward+backward", "rows": n, "dim": d, "vocab": v, **t.as_dict(),
+                   **roofline(t.median_ms, flops=6.0 * n * d * v)})]
+
+
+def bench_attention(args) -> list:
+    from ..ops import flash_attention
+    _, dev = _require_cuda()
+    torch.manual_seed(0)
+    b, t, h = args.batch, args.tokens, args.heads
+    q, k, v = (torch.randn(b, t, h, 64, device=dev).bfloat16().requires_grad_() for _ in range(3))
+    flops = 4.0 * b * h * t * t * 64 / 2  # causal
+
+    def fwd():
+        with torch.no_grad():
+            flash_attention(q, k, v, causal=True)
+
+    def fwd_bwd():
+        flash_attention(q, k, v, causal=True).sum().backward()
+
+    rows = []
+    tf = time_fn(fwd, device=dev, warmup=args.warmup, repeats=args.repeats)
+    rows.append(_emit({"case": "attention", "pass": "forward", "batch": b, "tokens": t, "heads": h, **tf.as_dict(),
+                       **roofline(tf.median_ms, flops=flops)}))
+    tb = time_fn(fwd_bwd, device=dev, warmup=args.warmup, repeats=args.repeats)
+    rows.append(_emit({"case": "attention", "pass": "forward+backward", "batch": b, "tokens": t, "heads": h,
+                       **tb.as_dict(), **roofline(tb.median_ms, flops=3.5 * flops)}))
+    return rows
+
+
+def bench_attnres(args) -> list:
+    from ..ops import attnres_mix
+    _, dev = _require_cuda()
+    torch.manual_seed(0)
+    srcs = [torch.randn(args.batch, args.tokens, args.dim, device=dev).bfloat16().requires_grad_()
+            for _ in range(args.sources)]
+    q = torch.randn(args.dim, device=dev).requires_grad_()
+    w = torch.ones(args.dim, device=dev).requires_grad_()
+    per = args.batch * args.tokens * args.dim * 2
+
+    def fwd():
+        with torch.no_grad():
+            attnres_mix(srcs, q, w, 1e-6)
+
+    def fwd_bwd():
+        attnres_mix(srcs, q, w, 1e-6).float().sum().backward()
+
+    rows = []
+    tf = time_fn(fwd, device=dev, warmup=args.warmup, repeats=args.repeats)
+    rows.append(_emit({"case": "attnres", "pass": "forward", "sources": args.sources, **tf.as_dict(),
+                       **roofline(tf.median_ms, bytes_moved=(args.sources + 1) * per)}))
+    tb = time_fn(fwd_bwd, device=dev, warmup=args.warmup, repeats=args.repeats)
+    rows.append(_emit({"case": "attnres", "pass": "forward+backward", "sources": args.sources, **tb.as_dict(),
+                       **roofline(tb.median_ms, bytes_moved=(3 * args.sources + 2) * per)}))
+    return rows
+
+
+CASES = {"gemm": bench_gemm, "kda": bench_kda, "moe": bench_moe, "linear_ce": bench_linear_ce,
+         "attention": bench_attention, "attnres": bench_attnres}
+
+
+def build_parser(parser: argparse.ArgumentParser | None = None) -> argparse.ArgumentParser:
+    p = parser or argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("case", choices=sorted(CASES))
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--repeats", type=int, default=10)
+    p.add_argument("--m", type=int, default=4096)
+    p.add_argument("--n", type=int, default=4096)
+    p.add_argument("--k", type=int, default=4096)
+    p.add_argument("--batch", type=int, default=16)
+    p.add_argument("--tokens", type=int, default=1024)
+    p.add_argument("--heads", type=int, default=10)
+    p.add_argument("--dim", type=int, default=640)
+    p.add_argument("--sources", type=int, default=4)
+    p.add_argument("--latent", type=int, default=320)
+    p.add_argument("--hidden", type=int, default=640)
+    p.add_argument("--experts", type=int, default=12)
+    p.add_argument("--topk", type=int, default=2)
+    p.add_argument("--rows", type=int, default=16384)
+    p.add_argument("--vocab", type=int, default=50257)
+    return p
+
+
+def main(argv=None) -> list:
+    args = build_parser().parse_args(argv)
+    if args.case == "moe" and args.tokens == 1024:
+        args.tokens = 16384  # one micro-batch of the flagship config
+    return CASES[args.case](args)
+
+
+if __name__ == "__main__":
+    main()

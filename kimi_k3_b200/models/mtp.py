@@ -354,7 +354,37 @@ class KimiMTPHead(nn.Module):
         return MTPDraftOutput(self.lm_head(h), out.cache, h)
 
 
+
+def _unique_numel(*modules) -> int:
+    seen, total = set(), 0
+    for m in modules:
+        if m is None:
+            continue
+        for prm in m.parameters():
+            if id(prm) not in seen:
+                seen.add(id(prm))
+                total += prm.numel()
+    return total
+
+
+def mtp_parameter_counts(head: KimiMTPHead) -> dict:
+    """Parameter counts of an MTP head with shared (aliased) tensors counted once.
+
+    ``unique_mtp_total`` is what the head adds to the model (fusion + block); the
+    embedding and LM head are shared with the main model. Parity:
+    ``src/mtp/parameter_count.py:20-46`` (reference).
+    """
+    fusion = _unique_numel(head.fusion)
+    block = _unique_numel(head.block)
+    emb = _unique_numel(head.input_embeddings)
+    lm = _unique_numel(head.lm_head)
+    return {"fusion": fusion, "block": block, "unique_mtp_output": 0, "unique_mtp_total": fusion + block,
+            "shared_input_embeddings": emb, "shared_lm_head": lm,
+            "shared_embedding_lm_overlap": emb + lm - _unique_numel(head.input_embeddings, head.lm_head),
+            "all_referenced_unique": _unique_numel(head.fusion, head.block, head.input_embeddings, head.lm_head)}
+
 __all__ = [
     "KimiMTPConfig", "MTPTrainingView", "MTPDiagnostics", "KimiMTPOutput", "MTPDraftOutput",
     "build_mtp_training_view", "build_mtp_feature_mask", "KimiMTPFusion", "KimiMTPBlock", "KimiMTPHead",
+    "mtp_parameter_counts",
 ]
