@@ -112,7 +112,6 @@ def bench_moe(args) -> list:
     scores = torch.randn(m, e, device=dev)
     w, sel = scores.sigmoid().topk(topk, dim=-1)
     w = (w / w.sum(-1, keepdim=True)).requires_grad_()
-    sel = sel.to(torch.int32)
     flops = 2.0 * m * topk * (2 * hid * lat + hid * lat)
 
     def fwd():

