@@ -268,16 +268,18 @@ std::vector<at::Tensor> kda_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Te
   auto W = at::empty({B * H, NC, 64, 64}, f), U = at::empty_like(W), P = at::empty_like(W), Qg = at::empty_like(W),
        Kend = at::empty_like(W), states = at::empty_like(W), Vp = at::empty_like(W);
   auto eGC = at::empty({B * H, NC, 64}, f);
+  auto Araw = at::empty_like(W);
   auto o = at::empty_like(v);
   at::Tensor ht = want_final ? at::empty({B, H, 64, 64}, f) : at::Tensor();
   at::Tensor h0c;
   if (h0.has_value() && h0->defined()) h0c = h0->to(at::kFloat).contiguous();
   kimi::KdaBuffers buf{W.data_ptr<float>(), U.data_ptr<float>(), P.data_ptr<float>(), Qg.data_ptr<float>(),
-                       Kend.data_ptr<float>(), eGC.data_ptr<float>(), states.data_ptr<float>(), Vp.data_ptr<float>()};
+                       Kend.data_ptr<float>(), eGC.data_ptr<float>(), states.data_ptr<float>(), Vp.data_ptr<float>(),
+                       Araw.data_ptr<float>()};
   check(kimi::kda_chunk_fwd(dtype_code(q), q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr<float>(),
                             beta.data_ptr<float>(), h0c.defined() ? h0c.data_ptr<float>() : nullptr, o.data_ptr(),
                             want_final ? ht.data_ptr<float>() : nullptr, buf, B, Tp, H, stream()), "kda_chunk_fwd");
-  return {o, ht, W, U, P, Qg, Kend, eGC, states, Vp};
+  return {o, ht, W, U, P, Qg, Kend, eGC, states, Vp, Araw};
 }
 
 std::vector<at::Tensor> kda_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor g, at::Tensor beta,
@@ -290,7 +292,7 @@ std::vector<at::Tensor> kda_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Te
   auto& W = saved.at(0);
   kimi::KdaBuffers buf{saved[0].data_ptr<float>(), saved[1].data_ptr<float>(), saved[2].data_ptr<float>(),
                        saved[3].data_ptr<float>(), saved[4].data_ptr<float>(), saved[5].data_ptr<float>(),
-                       saved[6].data_ptr<float>(), saved[7].data_ptr<float>()};
+                       saved[6].data_ptr<float>(), saved[7].data_ptr<float>(), saved.at(8).data_ptr<float>()};
   auto dVp = at::empty_like(W), dSn = at::empty_like(W);
   auto dq = at::empty(q.sizes(), f), dk = at::empty(k.sizes(), f), dv = at::empty(v.sizes(), f),
        dg = at::empty(g.sizes(), f), dbeta = at::empty(beta.sizes(), f);
@@ -302,8 +304,24 @@ std::vector<at::Tensor> kda_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Te
                             dhtc.defined() ? dhtc.data_ptr<float>() : nullptr, dVp.data_ptr<float>(),
                             dSn.data_ptr<float>(), dq.data_ptr<float>(), dk.data_ptr<float>(), dv.data_ptr<float>(),
                             dg.data_ptr<float>(), dbeta.data_ptr<float>(),
-                            want_dh0 ? dh0.data_ptr<float>() : nullptr, B, Tp, H, stream()), "kda_chunk_bwd");
+                            want_dh0 ? dh0.data_ptr<float>() : nullptr, B, Tp, H, nullptr, stream()),
+        "kda_chunk_bwd");
   return {dq, dk, dv, dg, dbeta, dh0};
+}
+
+// ---------------------------------------------------------------- tcgen05 small-matrix self-test
+std::vector<at::Tensor> tcs_selftest(at::Tensor a, at::Tensor b, int64_t n, int64_t mode) {
+  CHECK_CUDA_CONTIG(a);
+  CHECK_CUDA_CONTIG(b);
+  TORCH_CHECK(a.scalar_type() == at::kFloat && b.scalar_type() == at::kFloat, "fp32 operands");
+  const at::cuda::CUDAGuard gd(a.device());
+  const int K = a.size(1);
+  const int ncols = mode == 0 ? n : (mode == 1 ? 256 : 64);
+  auto out = at::empty({128, ncols}, a.options());
+  auto status = at::zeros({1}, a.options().dtype(at::kInt));
+  check(kimi::tcs_selftest(a.data_ptr<float>(), b.data_ptr<float>(), out.data_ptr<float>(), K, (int)n, (int)mode,
+                           status.data_ptr<int>(), stream()), "tcs_selftest");
+  return {out, status};
 }
 
 // ---------------------------------------------------------------- flash attention
@@ -556,6 +574,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attnres_bwd", &attnres_bwd);
   m.def("ce_rows", &ce_rows);
   m.def("router", &router);
+  m.def("tcs_selftest", &tcs_selftest);
+  m.def("kda_tc_status", [](bool clear) { return kimi::kda_tc_status(clear); });
   m.def("kda_fwd", &kda_fwd);
   m.def("kda_bwd", &kda_bwd);
   m.def("fa_fwd", &fa_fwd);

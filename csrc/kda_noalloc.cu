@@ -1,7 +1,7 @@
 // Allocation-free C entry point for the KDA chunked forward (declared in kda_noalloc.h).
 //
 // The two forward kernels (intra-chunk WY transform, then the chunk-to-chunk state scan)
-// are the ones in kda_chunk.cu; only where their intermediates live differs: here they
+// are the tcgen05 ones of kda_tc.cu; only where their intermediates live differs: here they
 // are carved out of one file-scope device array instead of freshly allocated tensors.
 #include <mutex>
 
@@ -12,10 +12,10 @@ namespace {
 
 constexpr int kChunk = 64;                        // tokens per chunk (== head dim)
 constexpr size_t kTile = 64 * 64;                 // floats in one per-chunk 64 x 64 tile
-constexpr size_t kFloatsPerChunkHead = 7 * kTile + 64;  // W, U, P, Qg, Kend, states, Vp tiles + eGC row
+constexpr size_t kFloatsPerChunkHead = 8 * kTile + 64;  // W, U, P, Qg, Kend, states, Vp, A tiles + eGC row
 constexpr size_t kScratchFloats = (size_t)KIMI_KDA_NOALLOC_MAX_CHUNK_HEADS * kFloatsPerChunkHead;
 
-// The scratch array: 128 chunk-heads x 114,944 bytes = 14,712,832 bytes per device.
+// The scratch array: 128 chunk-heads x 131,328 bytes = 16,809,984 bytes per device.
 static __device__ __align__(256) float g_kda_scratch[kScratchFloats];
 
 constexpr int kMaxDevices = 64;
@@ -53,7 +53,7 @@ extern "C" __attribute__((visibility("default"))) int kimi_kda_chunk_fwd_noalloc
   if (st != KIMI_KDA_NOALLOC_OK) return st;
   const size_t tiles = (size_t)chunk_heads * kTile;
   kimi::KdaBuffers buf{base,             base + 1 * tiles, base + 2 * tiles, base + 3 * tiles,
-                       base + 4 * tiles, base + 7 * tiles, base + 5 * tiles, base + 6 * tiles};
+                       base + 4 * tiles, base + 8 * tiles, base + 5 * tiles, base + 6 * tiles, base + 7 * tiles};
   return (int)kimi::kda_chunk_fwd(dtype, q, k, v, g, beta, h0, o, ht, buf, batch, tokens_padded, heads, stream);
 }
 

@@ -11,7 +11,7 @@
 // The ordinary Python path (kimi_k3_b200.ops.kda_chunk) allocates its eight per-chunk
 // intermediates through PyTorch's caching allocator.  This entry point instead keeps
 // them in one fixed device array compiled into the library (KIMI_KDA_NOALLOC_MAX_CHUNK_HEADS
-// chunk-heads, about 14 MiB), so a call only launches the two forward kernels.
+// chunk-heads, about 16 MiB), so a call only launches the two forward kernels.
 #pragma once
 
 #include <cuda_runtime.h>

@@ -57,6 +57,7 @@ struct KdaBuffers {
   float* eGC;     // e^(G_C)
   float* states;  // S at the start of each chunk  [K x V]
   float* Vp;      // U - W S
+  float* Araw = nullptr;  // strict_lower(sum_d k_i k_j e^(G_i - G_j)), kept for the backward
 };
 cudaError_t kda_chunk_fwd(int dtype, const void* q, const void* k, const void* v, const float* g, const float* beta,
                           const float* h0, void* o, float* ht, KdaBuffers buf, int batch, int tokens_padded,
@@ -64,7 +65,26 @@ cudaError_t kda_chunk_fwd(int dtype, const void* q, const void* k, const void* v
 cudaError_t kda_chunk_bwd(int dtype, const void* q, const void* k, const void* v, const float* g, const float* beta,
                           KdaBuffers buf, const void* dout, const float* dht, float* dVp, float* dSn, float* dq,
                           float* dk, float* dv, float* dg, float* dbeta, float* dh0, int batch, int tokens_padded,
-                          int heads, cudaStream_t s);
+                          int heads, int* status, cudaStream_t s);
+
+// Intra-chunk backward on tcgen05 (kda_tc.cu); needs buf.Araw from the forward and dV', dS_next
+// from the state backward.  Mbarrier timeouts are reported through `status` (0 = ok).
+cudaError_t kda_intra_bwd_tc(int dtype, const void* q, const void* k, const void* v, const float* g,
+                             const float* beta, KdaBuffers buf, const float* araw, const void* dout, const float* dVp,
+                             const float* dSn, float* dq, float* dk, float* dv, float* dg, float* dbeta, int batch,
+                             int tokens_padded, int heads, int* status, cudaStream_t s);
+// Intra-chunk forward on tcgen05 (kda_tc.cu): W, U, P, Qg, Kend, eGC and Araw of every chunk.
+cudaError_t kda_intra_fwd_tc(int dtype, const void* q, const void* k, const void* v, const float* g,
+                             const float* beta, KdaBuffers buf, int batch, int tokens_padded, int heads, int* status,
+                             cudaStream_t s);
+// Sequential state passes on tcgen05 (kda_tc.cu): forward fills buf.states / buf.Vp and writes o
+// (and ht); backward writes dV' and dS_next per chunk (and dh0).
+cudaError_t kda_state_fwd_tc(int dtype, KdaBuffers buf, const float* h0, void* o, float* ht, int batch,
+                             int tokens_padded, int heads, int* status, cudaStream_t s);
+cudaError_t kda_state_bwd_tc(int dtype, KdaBuffers buf, const void* dout, const float* dht, float* dVp, float* dSn,
+                             float* dh0, int batch, int tokens_padded, int heads, int* status, cudaStream_t s);
+// Device status word shared by the tcgen05 KDA kernels (read and cleared by the host).
+int kda_tc_status(bool clear);
 
 // ---- flash attention (flash_attn.cu); q/k/v/o are [B,T,H,D] contiguous
 cudaError_t flash_attn_fwd(int dtype, const void* q, const void* k, const void* v, void* o, float* lse, int batch,
@@ -74,5 +94,9 @@ cudaError_t flash_attn_bwd(int dtype, const void* q, const void* k, const void* 
                            const float* lse, float* dq_acc, void* dk, void* dv, float* delta, int batch, int tq,
                            int tk, int heads, int dqk, int dv_dim, bool causal, const int* key_lengths, float scale,
                            cudaStream_t s);
+
+// ---- self-test of the small-matrix tcgen05 path (tc_small_selftest.cu)
+cudaError_t tcs_selftest(const float* A, const float* B, float* out, int K, int n, int mode, int* status,
+                         cudaStream_t s);
 
 }  // namespace kimi
