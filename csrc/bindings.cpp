@@ -155,11 +155,11 @@ std::vector<at::Tensor> conv_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, int6
   dy = dy.contiguous();
   const at::cuda::CUDAGuard gd(x.device());
   auto wf = w.to(at::kFloat).contiguous();
-  auto dpre = at::empty(x.sizes(), x.options().dtype(at::kFloat));
   auto dx = at::empty_like(x);
-  auto dw = at::zeros(wf.sizes(), wf.options());
+  auto dw = at::empty(wf.sizes(), wf.options());
+  auto part = at::empty({kimi::conv_bwd_partial_rows(x.size(0), x.size(1)), wf.numel()}, wf.options());
   check(kimi::conv_silu_norm_bwd(dtype_code(x), dy.data_ptr(), x.data_ptr(), wf.data_ptr<float>(),
-                                 dpre.data_ptr<float>(), dx.data_ptr(), dw.data_ptr<float>(), x.size(0), x.size(1),
+                                 dx.data_ptr(), dw.data_ptr<float>(), part.data_ptr<float>(), x.size(0), x.size(1),
                                  x.size(2), wf.size(1), (int)head_dim, (float)eps, normalize, stream()),
         "conv_silu_norm_bwd");
   return {dx, dw};
@@ -415,6 +415,71 @@ at::Tensor tc_gemm_dense(at::Tensor a, at::Tensor b, bool a_mn, bool b_mn, bool 
   return out;
 }
 
+// Fused GEMM + cross-rank reduction (tensor parallelism): every rank computes its partial
+// a @ op(b)^T into `part` (its [M, N] slice of a symmetric buffer) and the comm warps of the same
+// kernel reduce it over the group (mode 1 all-reduce into out [M, N]; mode 2 reduce-scatter into
+// out [M / world, N]).  part_peers / flag_peers are the device addresses of every rank's partial
+// buffer and flag words; part_mc is the multicast address of the partial buffer or 0.
+at::Tensor tc_gemm_comm(at::Tensor a, at::Tensor b, bool b_mn, int64_t bn, int64_t mode, int64_t rank, int64_t world,
+                        at::Tensor part, std::vector<int64_t> part_peers, int64_t part_mc,
+                        std::vector<int64_t> flag_peers, int64_t tiles_cap, at::Tensor out, at::Tensor status,
+                        int64_t timeout_ns) {
+  check_tma_matrix(a, "a");
+  check_tma_matrix(b, "b");
+  const at::cuda::CUDAGuard gd(a.device());
+  const int64_t M = a.size(0), K = a.size(1), N = b_mn ? b.size(1) : b.size(0);
+  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K, "inner dimensions differ");
+  TORCH_CHECK(N % 8 == 0, "the reduced width must be a multiple of 8");
+  TORCH_CHECK(part.is_cuda() && part.scalar_type() == at::kBFloat16 && part.is_contiguous() && part.size(0) == M &&
+                  part.size(1) == N,
+              "part must be this rank's contiguous bf16 [M, N] symmetric buffer slice");
+  TORCH_CHECK(world >= 1 && world <= 8 && (int64_t)part_peers.size() == world && (int64_t)flag_peers.size() == world,
+              "one partial and one flag address per rank (world <= 8)");
+  TORCH_CHECK(part_peers[rank] == (int64_t)reinterpret_cast<uintptr_t>(part.data_ptr()),
+              "part must be this rank's entry of part_peers");
+  const int64_t out_rows = mode == 2 ? M / world : M;
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kBFloat16 && out.dim() == 2 && out.size(0) == out_rows &&
+                  out.size(1) == N && out.stride(1) == 1 && out.stride(0) % 8 == 0,
+              "out has the wrong shape or layout");
+  TORCH_CHECK(status.is_cuda() && status.scalar_type() == at::kInt, "status must be an int32 CUDA tensor");
+  kimi::TcGemmArgs g;
+  g.mode = 0;
+  g.bn = (int)bn;
+  g.b_mn = b_mn;
+  g.a = a.data_ptr();
+  g.a_rows = M;
+  g.a_cols = K;
+  g.a_ld = a.stride(0);
+  g.b = b.data_ptr();
+  g.b_groups = 1;
+  g.b_rows = b.size(0);
+  g.b_cols = b.size(1);
+  g.b_ld = b.stride(0);
+  g.b_gstride = b.stride(0) * b.size(0);
+  g.M = (int)M;
+  g.N = (int)N;
+  g.K = (int)K;
+  g.out = part.data_ptr();
+  g.ldc = N;
+  g.status = status.data_ptr<int>();
+  g.comm_mode = (int)mode;
+  g.comm_rank = (int)rank;
+  g.comm_world = (int)world;
+  g.comm_rows_per_rank = (int)(M / world);
+  for (int64_t q = 0; q < world; ++q) {
+    g.part_peer[q] = (uint64_t)part_peers[q];
+    g.flags_peer[q] = (uint64_t)flag_peers[q];
+  }
+  g.part_mc = (uint64_t)part_mc;
+  g.tiles_cap = (int)tiles_cap;
+  g.comm_out = out.data_ptr();
+  g.comm_ldo = out.stride(0);
+  g.timeout_ns = timeout_ns;
+  g.num_sms = at::cuda::getDeviceProperties(a.get_device())->multiProcessorCount;
+  check(kimi::tc_gemm(g, stream()), "tc_gemm_comm");
+  return out;
+}
+
 // Grouped GEMM. mode 1: rows of `a` ([R, K] K-major) split by offsets (128-aligned); b is [G, N, K]
 // (b_mn=False) or [G, K, N] (b_mn=True); epi 0 store / 1 SiTU (b2 = up weights) / 2 scatter-add.
 // mode 2: reduction over row segments (64-aligned) of a ([R, M] MN-major) and b ([R, N] MN-major);
@@ -582,6 +647,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fa_bwd", &fa_bwd);
   m.def("tc_gemm_dense", &tc_gemm_dense);
   m.def("tc_gemm_grouped", &tc_gemm_grouped);
+  m.def("tc_gemm_comm", &tc_gemm_comm);
+  m.def("tc_gemm_tiles", [](int64_t m, int64_t n, int64_t bn) { return kimi::tc_gemm_tiles((int)m, (int)n, (int)bn); });
   m.def("moe_route", &moe_route);
   m.def("moe_gather", &moe_gather);
   m.def("moe_dy", &moe_dy);

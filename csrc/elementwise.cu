@@ -1,5 +1,5 @@
 // Memory-bound fused kernels: RMSNorm (plain and head-wise), SiTU-GLU, sigmoid gate,
-// KDA lower-bounded decay, and the KDA short causal conv + SiLU (+ per-head L2 norm).
+// KDA lower-bounded decay (the short causal conv + SiLU + head norm lives in conv.cu).
 //
 // Rows are processed by groups of `tpr` threads (a power of two <= 32) so that narrow
 // rows (head_dim 64) still keep a warp busy; 16-byte vector loads are used when the row
@@ -237,146 +237,6 @@ __global__ void decay_bwd_kernel(const float* __restrict__ dg, const T* __restri
   for (int i = threadIdx.x; i < heads; i += blockDim.x) atomicAdd(&da_log[i], sda[i]);
 }
 
-// ------------------------------------------------------------------ KDA short conv + SiLU (+ L2 per head)
-// One group of `tpr` threads per (b, t, head); each thread covers head_dim / tpr channels.
-// The conv starts from a zero history (training / full-sequence mode).
-template <typename T>
-KIMI_D float conv_at(const T* __restrict__ x, const float* __restrict__ w, int64_t bt_row, int t, int c, int channels,
-                     int ksize) {
-  float acc = 0.f;
-  for (int j = 0; j < ksize; ++j) {
-    if (t - j < 0) break;
-    acc += w[c * ksize + j] * to_f<T>(x[(bt_row - j) * channels + c]);
-  }
-  return acc;
-}
-
-template <typename T>
-__global__ void conv_fwd_kernel(const T* __restrict__ x, const float* __restrict__ w, T* __restrict__ y, int batch,
-                                int tokens, int channels, int ksize, int head_dim, float eps, bool normalize,
-                                int tpr) {
-  const int heads = channels / head_dim;
-  const int64_t groups = (int64_t)batch * tokens * heads;
-  const int gid = threadIdx.x / tpr, lane = threadIdx.x % tpr;
-  const int gpb = blockDim.x / tpr;
-  const int warp_first_gid = (threadIdx.x / 32) * (32 / tpr);
-  for (int64_t base = (int64_t)blockIdx.x * gpb; base + warp_first_gid < groups; base += (int64_t)gridDim.x * gpb) {
-    const int64_t grp = base + gid;
-    const bool ok = grp < groups;
-    const int64_t bt = ok ? grp / heads : 0;
-    const int h = ok ? (int)(grp % heads) : 0;
-    const int t = (int)(bt % tokens);
-    float ss = 0.f;
-    float vals[8];
-    int cnt = 0;
-    for (int cc = lane; cc < head_dim && cnt < 8; cc += tpr, ++cnt) {
-      const int c = h * head_dim + cc;
-      const float pre = ok ? conv_at<T>(x, w, bt, t, c, channels, ksize) : 0.f;
-      const float s = siluf_(pre);
-      vals[cnt] = s;
-      ss += s * s;
-    }
-    float inv = 1.f;
-    if (normalize) {
-      ss = group_sum(ss, tpr);
-      inv = 1.f / fmaxf(sqrtf(ss), eps);
-    }
-    if (ok) {
-      cnt = 0;
-      for (int cc = lane; cc < head_dim && cnt < 8; cc += tpr, ++cnt)
-        y[bt * channels + h * head_dim + cc] = from_f<T>(vals[cnt] * inv);
-    }
-  }
-}
-
-// Pass 1: dpre[b,t,c] = d(output)/d(pre-activation), recomputing the conv and norm stats.
-template <typename T>
-__global__ void conv_bwd_pre_kernel(const T* __restrict__ dy, const T* __restrict__ x, const float* __restrict__ w,
-                                    float* __restrict__ dpre, int batch, int tokens, int channels, int ksize,
-                                    int head_dim, float eps, bool normalize, int tpr) {
-  const int heads = channels / head_dim;
-  const int64_t groups = (int64_t)batch * tokens * heads;
-  const int gid = threadIdx.x / tpr, lane = threadIdx.x % tpr;
-  const int gpb = blockDim.x / tpr;
-  const int warp_first_gid = (threadIdx.x / 32) * (32 / tpr);
-  for (int64_t base = (int64_t)blockIdx.x * gpb; base + warp_first_gid < groups; base += (int64_t)gridDim.x * gpb) {
-    const int64_t grp = base + gid;
-    const bool ok = grp < groups;
-    const int64_t bt = ok ? grp / heads : 0;
-    const int h = ok ? (int)(grp % heads) : 0;
-    const int t = (int)(bt % tokens);
-    float pre[8], s[8], d[8];
-    float ss = 0.f, dot = 0.f;
-    int cnt = 0;
-    for (int cc = lane; cc < head_dim && cnt < 8; cc += tpr, ++cnt) {
-      const int c = h * head_dim + cc;
-      pre[cnt] = ok ? conv_at<T>(x, w, bt, t, c, channels, ksize) : 0.f;
-      s[cnt] = siluf_(pre[cnt]);
-      d[cnt] = ok ? to_f<T>(dy[bt * channels + c]) : 0.f;
-      ss += s[cnt] * s[cnt];
-      dot += s[cnt] * d[cnt];
-    }
-    float inv = 1.f, coef = 0.f;
-    if (normalize) {
-      ss = group_sum(ss, tpr);
-      dot = group_sum(dot, tpr);
-      const float nrm = sqrtf(ss);
-      if (nrm > eps) {
-        inv = 1.f / nrm;
-        coef = dot * inv * inv * inv;  // (s . d) / ||s||^3
-      } else {
-        inv = 1.f / eps;
-      }
-    }
-    if (ok) {
-      cnt = 0;
-      for (int cc = lane; cc < head_dim && cnt < 8; cc += tpr, ++cnt) {
-        const float ds = d[cnt] * inv - s[cnt] * coef;
-        const float sg = sigmoidf_(pre[cnt]);
-        dpre[bt * channels + h * head_dim + cc] = ds * sg * (1.f + pre[cnt] * (1.f - sg));
-      }
-    }
-  }
-}
-
-// Pass 2: dx[t,c] = sum_j w[c,j] dpre[t+j,c];  dw[c,j] = sum_{b,t} dpre[t,c] x[t-j,c]
-// One thread per channel walks a tile of kConvTile tokens (coalesced across channels), keeps
-// its dw[c,:] partial in registers and adds it to global memory once per tile.
-constexpr int kConvTile = 64;
-constexpr int kConvMaxK = 8;
-template <typename T>
-__global__ void __launch_bounds__(128) conv_bwd_x_kernel(const float* __restrict__ dpre, const T* __restrict__ x,
-                                                         const float* __restrict__ w, T* __restrict__ dx,
-                                                         float* __restrict__ dw, int tokens, int channels,
-                                                         int ksize) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= channels) return;
-  const int t0 = blockIdx.y * kConvTile;
-  const int t1 = min(t0 + kConvTile, tokens);
-  const int64_t base = (int64_t)blockIdx.z * tokens;
-  float wc[kConvMaxK], acc[kConvMaxK];
-#pragma unroll
-  for (int j = 0; j < kConvMaxK; ++j) {
-    wc[j] = j < ksize ? w[c * ksize + j] : 0.f;
-    acc[j] = 0.f;
-  }
-  for (int t = t0; t < t1; ++t) {
-    const float dp = dpre[(base + t) * channels + c];
-    float sx = 0.f;
-#pragma unroll
-    for (int j = 0; j < kConvMaxK; ++j) {
-      if (j < ksize) {
-        if (t + j < tokens) sx += wc[j] * dpre[(base + t + j) * channels + c];
-        if (t - j >= 0) acc[j] += dp * to_f<T>(x[(base + t - j) * channels + c]);
-      }
-    }
-    dx[(base + t) * channels + c] = from_f<T>(sx);
-  }
-#pragma unroll
-  for (int j = 0; j < kConvMaxK; ++j)
-    if (j < ksize) atomicAdd(&dw[c * ksize + j], acc[j]);
-}
-
 
 }  // namespace
 
@@ -465,38 +325,6 @@ cudaError_t kda_decay_bwd(int dtype, const float* dg, const void* z, const float
   KIMI_DISPATCH(dtype, T, {
     decay_bwd_kernel<T><<<grid_for(n, 256), 256, heads * sizeof(float), s>>>(dg, (const T*)z, a_log, (T*)dz, da_log,
                                                                             n, heads, kdim, g_min, ceps);
-  });
-  return cudaGetLastError();
-}
-
-cudaError_t conv_silu_norm_fwd(int dtype, const void* x, const float* w, void* y, int batch, int tokens,
-                               int channels, int ksize, int head_dim, float eps, bool normalize, cudaStream_t s) {
-  if (channels % head_dim) return cudaErrorInvalidValue;
-  int tpr = 1;
-  while (tpr * 8 < head_dim && tpr < 32) tpr <<= 1;
-  if (tpr * 8 < head_dim) return cudaErrorInvalidValue;
-  const int64_t groups = (int64_t)batch * tokens * (channels / head_dim);
-  KIMI_DISPATCH(dtype, T, {
-    conv_fwd_kernel<T><<<grid_for(groups, 256 / tpr), 256, 0, s>>>((const T*)x, w, (T*)y, batch, tokens, channels,
-                                                                   ksize, head_dim, eps, normalize, tpr);
-  });
-  return cudaGetLastError();
-}
-
-cudaError_t conv_silu_norm_bwd(int dtype, const void* dy, const void* x, const float* w, float* dpre, void* dx,
-                               float* dw, int batch, int tokens, int channels, int ksize, int head_dim, float eps,
-                               bool normalize, cudaStream_t s) {
-  if (channels % head_dim) return cudaErrorInvalidValue;
-  int tpr = 1;
-  while (tpr * 8 < head_dim && tpr < 32) tpr <<= 1;
-  if (tpr * 8 < head_dim) return cudaErrorInvalidValue;
-  const int64_t groups = (int64_t)batch * tokens * (channels / head_dim);
-  if (ksize > kConvMaxK) return cudaErrorInvalidValue;
-  const dim3 gx((channels + 127) / 128, (tokens + kConvTile - 1) / kConvTile, batch);
-  KIMI_DISPATCH(dtype, T, {
-    conv_bwd_pre_kernel<T><<<grid_for(groups, 256 / tpr), 256, 0, s>>>(
-        (const T*)dy, (const T*)x, w, dpre, batch, tokens, channels, ksize, head_dim, eps, normalize, tpr);
-    conv_bwd_x_kernel<T><<<gx, 128, 0, s>>>(dpre, (const T*)x, w, (T*)dx, dw, tokens, channels, ksize);
   });
   return cudaGetLastError();
 }

@@ -14,6 +14,16 @@
 // backward products without transposed copies.
 // Epilogues:  0 store (bf16 or fp32), 1 SiTU-GLU of a (gate | up) tile pair (stores h, gate, up),
 //             2 weighted scatter-add into fp32 rows (row_token[r] < 0 skips the row).
+// Comm modes (dense mode, bf16 output): the epilogue stores each tile's partial product into a
+// symmetric buffer shared with the other ranks of a tensor-parallel group and signals the tile's
+// owner; four extra "comm" warps reduce the tiles this rank owns across all ranks while the
+// MMAs of later tiles proceed:  all-reduce (every rank ends with the sum, copied out of the
+// buffer tile by tile) or reduce-scatter (the owner of a row block writes the sum into its own
+// output).  The reduction reads the ranks' partials with one NVLink-multicast multimem.ld_reduce
+// per 16 bytes and writes the sum back with multimem.st (NVLS), or with peer loads and stores
+// when the group has no multicast object.  Flags are counting semaphores in the same buffer, so
+// consecutive calls (and CUDA-graph replays) need no host-side epoch.  Every wait on a peer is
+// bounded by a time limit and reports through the status word.
 // TMA loads never use cluster multicast; every mbarrier wait is bounded (status word).
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -28,6 +38,21 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
+
+constexpr int kMaxRanks = 8;
+
+struct CommParams {
+  int mode;                     // 0 off, 1 all-reduce, 2 reduce-scatter
+  int rank, world;
+  int rows_per_rank;            // reduce-scatter: output rows owned by each rank
+  uint64_t part_peer[kMaxRanks];   // partial buffer [M, N] bf16 on every rank (this rank's included)
+  uint64_t part_mc;             // multicast address of the partial buffer (0: peer loads / stores)
+  uint64_t flags_peer[kMaxRanks];  // flag words on every rank: ready[tiles] then done[tiles]
+  int tiles_cap;                // flag capacity (tiles)
+  void* out;                    // all-reduce: [M, N] result; reduce-scatter: [rows_per_rank, N]
+  int64_t ldo;
+  int64_t timeout_ns;
+};
 
 struct DevParams {
   CUtensorMap map_a;
@@ -47,6 +72,7 @@ struct DevParams {
   const int* row_token;
   const float* row_weight;
   int* status;
+  CommParams cm;
 };
 
 struct TileInfo {
@@ -118,12 +144,99 @@ __device__ TileInfo tile_info(const DevParams& p, int tile) {
   return ti;
 }
 
+
+// ---------------------------------------------------------------- cross-rank helpers (comm modes)
+constexpr int kCommTimeout = 5;
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ uint4 ld_sys16(const void* p) {
+  uint4 v;
+  asm volatile("ld.relaxed.sys.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_sys16(void* p, uint4 v) {
+  asm volatile("st.relaxed.sys.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+// Sum of the eight bf16 values at `addr` over every rank of the multicast group (fp32 accumulation).
+__device__ __forceinline__ uint4 mc_ld_reduce_bf16x8(uint64_t addr) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(addr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void mc_st16(uint64_t addr, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+// Bounded wait for *flag >= target; on timeout (or an error already raised) returns false.
+__device__ bool wait_geq(const uint32_t* flag, uint32_t target, int64_t timeout_ns, int* status) {
+  const uint64_t t0 = global_ns();
+  while (ld_acquire_sys(flag) < target) {
+    if (*reinterpret_cast<volatile int*>(status) != 0) return false;
+    if ((int64_t)(global_ns() - t0) > timeout_ns) {
+      atomicCAS(status, 0, kCommTimeout);
+      return false;
+    }
+    __nanosleep(100);
+  }
+  return true;
+}
+__device__ __forceinline__ void comm_bar() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__device__ __forceinline__ void add_bf16x8(float* acc, uint4 v) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = __bfloat1622float2(h[j]);
+    acc[2 * j] += f.x;
+    acc[2 * j + 1] += f.y;
+  }
+}
+__device__ __forceinline__ uint4 pack_bf16x8(const float* acc) {
+  uint4 v;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+  return v;
+}
+
+// Rank that reduces a tile: spread over CTAs and over a CTA's successive tiles (all-reduce), or
+// the rank owning the tile's rows (reduce-scatter).
+__device__ __forceinline__ int tile_owner(const CommParams& c, int tile, int m0) {
+  if (c.mode == 2) return m0 / c.rows_per_rank;
+  return (int)((tile % gridDim.x + tile / gridDim.x) % c.world);
+}
+
 __device__ __forceinline__ float situ_fwd(float g, float u, float bg, float bu) {
   return bg * tanhf(g / bg) * (1.f / (1.f + expf(-g))) * bu * tanhf(u / bu);
 }
 
-template <int BN, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ DevParams p) {
+template <int BN>
+__device__ void comm_loop(const DevParams& p, int total);
+
+template <int BN, bool A_MN, bool B_MN, int CM>
+__global__ void __launch_bounds__(CM ? 320 : 192, 1) gemm_tc_kernel(const __grid_constant__ DevParams p) {
   constexpr int A_BYTES = BM * BK * 2;
   constexpr int B_BYTES = BN * BK * 2;
   constexpr int STAGE = A_BYTES + B_BYTES;
@@ -242,7 +355,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
         tc::mma_commit(&tfull[buf]);
       }
     }
-  } else {
+  } else if (warp < 6) {
     const int sub = warp & 3;
     const int r_local = sub * 32 + lane;
     int it = 0;
@@ -339,12 +452,93 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
       }
       tc::tc_fence_before();
       tc::mbar_arrive(&tempty[buf]);
+      if constexpr (CM != 0) {
+        // this rank's partial tile is in the symmetric buffer: tell the tile's owner
+        fence_sys();
+        epi_bar();
+        if (threadIdx.x == 64) {
+          const int owner = tile_owner(p.cm, tile, ti.m0);
+          red_release_sys(reinterpret_cast<uint32_t*>(p.cm.flags_peer[owner]) + tile, 1u);
+        }
+      }
     }
+  } else {
+    if constexpr (CM != 0) comm_loop<BN>(p, total);
   }
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
   if (warp == 1) tc::tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+
+// Comm warps (threads 192..319): reduce the tiles this rank owns, then hand every tile's sum out.
+template <int BN>
+__device__ void comm_loop(const DevParams& p, int total) {
+  __shared__ int s_ok;
+  const CommParams& c = p.cm;
+  const int ct = threadIdx.x - 192;
+  uint32_t* my_flags = reinterpret_cast<uint32_t*>(c.flags_peer[c.rank]);
+  for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+    const TileInfo ti = tile_info<BN>(p, tile);
+    const int rows = min(BM, p.M - ti.m0), cols = min(BN, p.N - ti.n0);
+    const int cpr = cols / 8;  // 16-byte chunks per row
+    const int n = rows * cpr;
+    if (tile_owner(c, tile, ti.m0) == c.rank) {
+      if (ct == 0) {
+        const bool ok = wait_geq(my_flags + tile, (uint32_t)c.world, c.timeout_ns, p.status);
+        if (ok) atomicSub(my_flags + tile, (uint32_t)c.world);
+        s_ok = ok;
+      }
+      comm_bar();
+      if (s_ok) {
+        for (int idx = ct; idx < n; idx += 128) {
+          const int r = idx / cpr, c8 = idx - r * cpr;
+          const int64_t off = ((int64_t)(ti.m0 + r) * p.N + ti.n0 + c8 * 8) * 2;  // bytes
+          uint4 v;
+          if (c.part_mc) {
+            v = mc_ld_reduce_bf16x8(c.part_mc + off);
+          } else {
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            for (int q = 0; q < c.world; ++q)
+              add_bf16x8(acc, ld_sys16(reinterpret_cast<const void*>(c.part_peer[q] + off)));
+            v = pack_bf16x8(acc);
+          }
+          if (c.mode == 2) {
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(c.out) +
+                               (int64_t)(ti.m0 + r - c.rank * c.rows_per_rank) * c.ldo + ti.n0 + c8 * 8;
+            *reinterpret_cast<uint4*>(o) = v;
+          } else if (c.part_mc) {
+            mc_st16(c.part_mc + off, v);
+          } else {
+            for (int q = 0; q < c.world; ++q) st_sys16(reinterpret_cast<void*>(c.part_peer[q] + off), v);
+          }
+        }
+        fence_sys();
+      }
+      comm_bar();
+      if (ct == 0 && s_ok)
+        for (int q = 0; q < c.world; ++q)
+          red_release_sys(reinterpret_cast<uint32_t*>(c.flags_peer[q]) + c.tiles_cap + tile, 1u);
+    }
+    // every rank: wait for the owner's sum, then (all-reduce) copy it out of the buffer
+    if (ct == 0) {
+      const bool ok = wait_geq(my_flags + c.tiles_cap + tile, 1u, c.timeout_ns, p.status);
+      if (ok) atomicSub(my_flags + c.tiles_cap + tile, 1u);
+      s_ok = ok;
+    }
+    comm_bar();
+    if (s_ok && c.mode == 1) {
+      const char* part = reinterpret_cast<const char*>(c.part_peer[c.rank]);
+      for (int idx = ct; idx < n; idx += 128) {
+        const int r = idx / cpr, c8 = idx - r * cpr;
+        const int64_t e = (int64_t)(ti.m0 + r) * p.N + ti.n0 + c8 * 8;
+        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(c.out) + (int64_t)(ti.m0 + r) * c.ldo + ti.n0 +
+                                  c8 * 8) = ld_sys16(part + e * 2);
+      }
+    }
+    comm_bar();
+  }
 }
 
 // ---------------------------------------------------------------- host side
@@ -388,19 +582,19 @@ bool make_map_2d(CUtensorMap* m, const void* ptr, uint64_t d0, uint64_t d1, uint
   return r == CUDA_SUCCESS;
 }
 
-template <int BN, bool AMN, bool BMN>
+template <int BN, bool AMN, bool BMN, int CM = 0>
 cudaError_t launch(const DevParams& dp, int num_sms, cudaStream_t s) {
   constexpr int STAGES = BN == 256 ? 4 : 6;
   constexpr int STAGE = BM * BK * 2 + BN * BK * 2;
   const size_t smem = 1024 + (size_t)STAGES * STAGE + (2 * STAGES + 4) * 8 + 16;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, AMN, BMN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, AMN, BMN, CM>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  gemm_tc_kernel<BN, AMN, BMN><<<num_sms, 192, smem, s>>>(dp);
+  gemm_tc_kernel<BN, AMN, BMN, CM><<<num_sms, CM ? 320 : 192, smem, s>>>(dp);
   return cudaGetLastError();
 }
 
@@ -453,6 +647,36 @@ cudaError_t tc_gemm(const TcGemmArgs& a, cudaStream_t stream) {
     if (!ok) return cudaErrorInvalidValue;
   }
   int sms = a.num_sms > 0 ? a.num_sms : 148;
+  if (a.comm_mode != 0) {
+    CommParams& c = dp.cm;
+    c.mode = a.comm_mode;
+    c.rank = a.comm_rank;
+    c.world = a.comm_world;
+    c.rows_per_rank = a.comm_rows_per_rank;
+    for (int q = 0; q < kMaxRanks; ++q) {
+      c.part_peer[q] = a.part_peer[q];
+      c.flags_peer[q] = a.flags_peer[q];
+    }
+    c.part_mc = a.part_mc;
+    c.tiles_cap = a.tiles_cap;
+    c.out = a.comm_out;
+    c.ldo = a.comm_ldo;
+    c.timeout_ns = a.timeout_ns;
+    const bool ok = a.mode == 0 && a.epi == 0 && !a.out_fp32 && !a.a_mn && a.N % 8 == 0 && a.ldc == a.N &&
+                    c.world >= 1 && c.world <= kMaxRanks && c.rank >= 0 && c.rank < c.world && a.status &&
+                    a.comm_out && tc_gemm_tiles(a.M, a.N, bn) <= c.tiles_cap && a.out == (void*)c.part_peer[c.rank] &&
+                    (c.mode == 1 || (c.mode == 2 && c.rows_per_rank > 0 && c.rows_per_rank % 128 == 0 &&
+                                     c.rows_per_rank * c.world == a.M));
+    if (!ok) return cudaErrorInvalidValue;
+    if (bn == 256) {
+      if (c.mode == 1) return a.b_mn ? launch<256, false, true, 1>(dp, sms, stream)
+                                     : launch<256, false, false, 1>(dp, sms, stream);
+      return a.b_mn ? launch<256, false, true, 2>(dp, sms, stream) : launch<256, false, false, 2>(dp, sms, stream);
+    }
+    if (c.mode == 1) return a.b_mn ? launch<128, false, true, 1>(dp, sms, stream)
+                                   : launch<128, false, false, 1>(dp, sms, stream);
+    return a.b_mn ? launch<128, false, true, 2>(dp, sms, stream) : launch<128, false, false, 2>(dp, sms, stream);
+  }
 #define KIMI_TC_LAUNCH(BN_, AM_, BM_) return launch<BN_, AM_, BM_>(dp, sms, stream)
   if (bn == 256) {
     if (!a.a_mn && !a.b_mn) KIMI_TC_LAUNCH(256, false, false);

@@ -695,9 +695,16 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_fwd_tc_kernel(const __grid_c
     }
     tcs::mma_done(bar, phase, a.status, 31);
     {  // row i: A (strict lower) from the k rows, P (lower) from the q rows; column block I(i)
-      const int i = row & 63, I = i >> 4;
-      float val[32];
-      tcs::tmem_row32(tm, warp, 64 * I + c0, val);
+      // tcgen05.ld takes one column address per warp: a warp's 32 rows span two 16-row tiles,
+      // so load both column blocks and keep the one of this row's tile.
+      const int i = row & 63, I = i >> 4, Ia = 2 * ((warp & 3) & 1);
+      float val[32], alt[32];
+      tcs::tmem_row32(tm, warp, 64 * Ia + c0, val);
+      tcs::tmem_row32(tm, warp, 64 * (Ia + 1) + c0, alt);
+      if (I != Ia) {
+#pragma unroll
+        for (int u = 0; u < 32; ++u) val[u] = alt[u];
+      }
       float* dst = (row < 64 ? a.buf.Araw : a.buf.P) + bo + i * 64 + c0;
       const int lim = row < 64 ? i : i + 1;  // columns j < lim are kept
 #pragma unroll

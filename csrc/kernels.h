@@ -25,9 +25,11 @@ cudaError_t kda_decay_bwd(int dtype, const float* dg, const void* z, const float
                           int64_t rows, int heads, int kdim, float g_min, float clamp_eps, cudaStream_t s);
 cudaError_t conv_silu_norm_fwd(int dtype, const void* x, const float* w, void* y, int batch, int tokens,
                                int channels, int ksize, int head_dim, float eps, bool normalize, cudaStream_t s);
-cudaError_t conv_silu_norm_bwd(int dtype, const void* dy, const void* x, const float* w, float* dpre, void* dx,
-                               float* dw, int batch, int tokens, int channels, int ksize, int head_dim, float eps,
+cudaError_t conv_silu_norm_bwd(int dtype, const void* dy, const void* x, const float* w, void* dx, float* dw,
+                               float* dw_part, int batch, int tokens, int channels, int ksize, int head_dim, float eps,
                                bool normalize, cudaStream_t s);
+// Rows of the dw scratch conv_silu_norm_bwd needs ([rows, channels * ksize] fp32).
+int conv_bwd_partial_rows(int batch, int tokens);
 
 // ---- attention residual depth mix (attnres.cu); sources: device array of S pointers
 cudaError_t attnres_mix_fwd(int dtype, const void* const* sources, int num_sources, const float* q, const float* w,

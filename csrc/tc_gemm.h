@@ -32,7 +32,21 @@ struct TcGemmArgs {
   const float* row_weight = nullptr;
   int* status = nullptr;
   int num_sms = 0;
+  // Comm modes (dense, bf16 output, A K-major, N % 8 == 0): `out` / `ldc` must be this rank's
+  // symmetric partial buffer [M, N] (ldc == N); the summed result goes to comm_out.
+  int comm_mode = 0;  // 0 off, 1 all-reduce, 2 reduce-scatter
+  int comm_rank = 0, comm_world = 1, comm_rows_per_rank = 0;
+  uint64_t part_peer[8] = {};
+  uint64_t part_mc = 0;
+  uint64_t flags_peer[8] = {};
+  int tiles_cap = 0;
+  void* comm_out = nullptr;
+  int64_t comm_ldo = 0;
+  int64_t timeout_ns = 10000000000LL;
 };
+
+// Output tiles of a dense launch (for sizing the comm flag region).
+inline int tc_gemm_tiles(int M, int N, int bn) { return ((M + 127) / 128) * ((N + bn - 1) / bn); }
 
 cudaError_t tc_gemm(const TcGemmArgs& args, cudaStream_t stream);
 

@@ -362,7 +362,10 @@ class GatedMLA(nn.Module):
             return out.to(hidden_states.dtype), None
         gate = torch.sigmoid(logits)
         cd = combined.dtype
-        out = F.linear(combined * gate.to(cd), gp.weight.to(cd), None if gp.bias is None else gp.bias.to(cd))
+        if not isinstance(gp, nn.Linear):  # a tensor-parallel projection that also reduces its output
+            out = gp(combined * gate.to(cd))
+        else:
+            out = F.linear(combined * gate.to(cd), gp.weight.to(cd), None if gp.bias is None else gp.bias.to(cd))
         return self.output_dropout(out).to(hidden_states.dtype), gate
 
     def _record_qk_scale(self, query, key):

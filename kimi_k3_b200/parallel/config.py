@@ -69,6 +69,9 @@ class TensorParallelConfig:
     shard_mla_heads: bool = True
     shard_moe_latent_projections: bool = False
     mla_cache_layout: Literal["replicated", "latent_sharded"] = "replicated"
+    # Run each attention shard's output projection and its all-reduce as one kernel (tcgen05 GEMM
+    # + NVLink reduction over symmetric memory) on CUDA; CPU ranks keep the separate all-reduce.
+    fused_output_reduce: bool = False
 
     def __post_init__(self) -> None:
         if self.size <= 0:

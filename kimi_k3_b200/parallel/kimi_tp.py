@@ -57,10 +57,21 @@ def _copy(dst: torch.Tensor, src: torch.Tensor) -> None:
     dst.copy_(src)
 
 
+def _install_fused_output(inner: nn.Module, group, enabled: bool) -> bool:
+    """Swap the shard's output projection for the fused GEMM + all-reduce (one tcgen05 kernel
+    over symmetric memory, ``parallel/symmetric.py``); the wrapper then skips its own reduce."""
+    if not enabled:
+        return False
+    from .symmetric import FusedRowParallelOutput
+    gate = inner.output_gate
+    gate.output_proj = FusedRowParallelOutput(gate.output_proj, group)
+    return True
+
+
 class TensorParallelKDA(nn.Module):
     """KDA with complete recurrent heads per TP rank (local state ``[B, H/TP, K, V]``)."""
 
-    def __init__(self, module: KimiDeltaAttention, *, group=None):
+    def __init__(self, module: KimiDeltaAttention, *, group=None, fused_output: bool = False):
         super().__init__()
         c = module.config
         if c.output_bias or c.projection_bias or c.beta_bias or c.output_gate_bias or c.short_conv_bias:
@@ -101,20 +112,22 @@ class TensorParallelKDA(nn.Module):
                            "projections.alpha_up.weight": 0, "projections.b_alpha": 0, "decay.A_log": 0,
                            "output_norm.weight": 0 if module.output_norm.per_head_affine else None,
                            "output_gate.gate_proj.weight": 0, "output_gate.output_proj.weight": 1}
+        self.fused_output = _install_fused_output(self.inner, group, fused_output)
 
     def forward(self, hidden_states, attention_mask=None, state=None, mode="chunkwise", output_final_state=False,
                 output_diagnostics=False):
         x = copy_to_tensor_parallel_region(hidden_states, self.group)
         out = self.inner(x, attention_mask=attention_mask, state=state, mode=mode,
                          output_final_state=output_final_state, output_diagnostics=output_diagnostics)
-        out.hidden_states = reduce_from_tensor_parallel_region(out.hidden_states, self.group)
+        if not self.fused_output:
+            out.hidden_states = reduce_from_tensor_parallel_region(out.hidden_states, self.group)
         return out
 
 
 class TensorParallelMLA(nn.Module):
     """Gated MLA with complete heads per TP rank and a replicated latent cache."""
 
-    def __init__(self, module: GatedMLA, *, group=None):
+    def __init__(self, module: GatedMLA, *, group=None, fused_output: bool = False):
         super().__init__()
         c = module.config
         if c.projection_bias or c.output_bias or c.output_gate_bias:
@@ -137,6 +150,7 @@ class TensorParallelMLA(nn.Module):
         self.shard_dims = {"projections.query.weight": 0, "projections.latent_kv.compression.weight": None,
                            "projections.latent_kv.key_up.weight": 0, "projections.latent_kv.value_up.weight": 0,
                            "output_gate.gate_proj.weight": 0, "output_gate.output_proj.weight": 1}
+        self.fused_output = _install_fused_output(self.inner, group, fused_output)
         self.inner._kimi_qk_group = group  # QK-Clip takes the MAX scale over the heads of all ranks
         for attr in ("absorbed_decode",):
             if hasattr(module, attr):
@@ -147,12 +161,15 @@ class TensorParallelMLA(nn.Module):
         x = copy_to_tensor_parallel_region(hidden_states, self.group)
         out = self.inner(x, attention_mask=attention_mask, cache=cache, use_cache=use_cache,
                          output_attentions=output_attentions, output_diagnostics=output_diagnostics, **kw)
-        out.hidden_states = reduce_from_tensor_parallel_region(out.hidden_states, self.group)
+        if not self.fused_output:
+            out.hidden_states = reduce_from_tensor_parallel_region(out.hidden_states, self.group)
         return out
 
 
-def shard_kimi_attention(model: nn.Module, *, group=None, shard_kda: bool = True, shard_mla: bool = True) -> int:
-    """Replace every KDA / gated-MLA attention of every hybrid layer in place; returns the count."""
+def shard_kimi_attention(model: nn.Module, *, group=None, shard_kda: bool = True, shard_mla: bool = True,
+                         fused_output: bool = False) -> int:
+    """Replace every KDA / gated-MLA attention of every hybrid layer in place; returns the count.
+    ``fused_output`` runs each shard's output projection and its all-reduce as one kernel."""
     from ..models.backbone import HybridAttentionLayer
     raw = model.module if hasattr(model, "module") else model
     n = 0
@@ -161,10 +178,10 @@ def shard_kimi_attention(model: nn.Module, *, group=None, shard_kda: bool = True
             continue
         att = layer.attention
         if isinstance(att, KimiDeltaAttention) and shard_kda:
-            layer.attention = TensorParallelKDA(att, group=group)
+            layer.attention = TensorParallelKDA(att, group=group, fused_output=fused_output)
             n += 1
         elif isinstance(att, GatedMLA) and shard_mla:
-            layer.attention = TensorParallelMLA(att, group=group)
+            layer.attention = TensorParallelMLA(att, group=group, fused_output=fused_output)
             n += 1
     return n
 

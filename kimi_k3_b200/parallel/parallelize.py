@@ -195,7 +195,8 @@ def parallelize_kimi_model(model: nn.Module, config: DistributedConfig, context)
     vocab = None
     if config.enabled and config.tensor_parallel.enabled:
         tp_layers = shard_kimi_attention(raw, group=context.tp_group, shard_kda=config.tensor_parallel.shard_kda_heads,
-                                         shard_mla=config.tensor_parallel.shard_mla_heads)
+                                         shard_mla=config.tensor_parallel.shard_mla_heads,
+                                         fused_output=config.tensor_parallel.fused_output_reduce)
         for m in raw.modules():
             if isinstance(m, (TensorParallelKDA, TensorParallelMLA)):
                 _tag([p for p in m.parameters() if not getattr(p, "_kimi_tp_partial", False)], _kimi_tp_shard=True)

@@ -73,6 +73,8 @@ def _rank(rank, world, layout, kind, qb):
         cfg["data_parallel"] = {"mode": "fsdp", "size": world}
     elif layout == "tp":
         cfg["tensor_parallel"] = {"enabled": True, "size": world}
+    elif layout == "tp_fused_output":  # the fused output projection (CPU ranks take its all-reduce path)
+        cfg["tensor_parallel"] = {"enabled": True, "size": world, "fused_output_reduce": True}
     elif layout == "ep":
         cfg["expert_parallel"] = {"enabled": True, "size": world}
     elif layout == "tp_ep_overlay":
@@ -108,7 +110,8 @@ def _compare(ref_params, got, tol):
     return worst
 
 
-@pytest.mark.parametrize("layout,kind", [("dp", "per_head_muon_adamw"), ("tp", "adamw"), ("ep", "per_head_muon_adamw"),
+@pytest.mark.parametrize("layout,kind", [("dp", "per_head_muon_adamw"), ("tp", "adamw"), ("tp_fused_output", "adamw"),
+                                         ("ep", "per_head_muon_adamw"),
                                          ("tp_ep_overlay", "adamw"), ("fsdp", "per_head_muon_adamw")])
 def test_parallel_layout_matches_single_process(layout, kind):
     world = 2
