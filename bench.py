@@ -165,7 +165,7 @@ def run_ours(args, world, rank, local):
     engine = TrainStepEngine(model, opt, scheduler=sched, grad_clip=1.0, amp_dtype=torch.bfloat16, use_mtp=True,
                              moe_controller=MoEController(model, reducer=reducer.qb_reducer() if reducer else None),
                              grad_hook=reducer.all_reduce_gradients if reducer else None,
-                             cuda_graph=not args.no_graph and world == 1)
+                             cuda_graph=not args.no_graph)
     bpg = args.batch_per_gpu
     dev_batches = make_batches(4, bpg, SEQ, VOCAB, seed=1000 + rank, device=dev)
     host_batches = make_batches(4, bpg, SEQ, VOCAB, seed=2000 + rank, pin=True)
@@ -208,6 +208,7 @@ def run_ours(args, world, rank, local):
     launches = count_launches(engine, dev_batches[0])
     if rank != 0:
         launches = None
+    engine.release_graph()  # a captured graph holding NCCL calls must go before the process group
     return ms, e2e_ms, clocks, h2d, 4, launches, losses[-1]
 
 
@@ -369,7 +370,7 @@ def main():
     if last_loss is not None:
         line["last_loss"] = round(last_loss, 4)
     if args.impl == "ours":
-        line["config"]["step_mode"] = "eager" if args.no_graph or world > 1 else "cuda_graph"
+        line["config"]["step_mode"] = "eager" if args.no_graph else "cuda_graph"
         if os.environ.get("KIMI_BENCH_NOTE"):
             line["note"] = os.environ["KIMI_BENCH_NOTE"]
     if rank == 0:

@@ -3,8 +3,9 @@
 //   warp 0      TMA producer: A and B tiles (128B-swizzled) into a STAGES-deep smem ring
 //   warp 1      MMA issuer: tcgen05.mma (M=128, N=BN, K=16) into one of two TMEM accumulators;
 //               allocates / frees TMEM
-//   warps 2..5  epilogue: tcgen05.ld of the finished accumulator (one row per thread) and a fused
-//               store, overlapping the MMAs of the next tile (double-buffered TMEM)
+//   warps 2..9  epilogue: tcgen05.ld of the finished accumulator (one row per thread; warps 2..5 and
+//               6..9 take the two column halves of the tile) and a fused store, overlapping the
+//               MMAs of the next tile (double-buffered TMEM)
 //
 // Modes:  0 dense;  1 grouped over M (row segments of A, one B matrix per segment: MoE experts);
 //         2 grouped over K (reduction over row segments, one C matrix per segment: expert weight
@@ -202,7 +203,7 @@ __device__ bool wait_geq(const uint32_t* flag, uint32_t target, int64_t timeout_
   return true;
 }
 __device__ __forceinline__ void comm_bar() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 __device__ __forceinline__ void add_bf16x8(float* acc, uint4 v) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
@@ -236,7 +237,7 @@ template <int BN>
 __device__ void comm_loop(const DevParams& p, int total);
 
 template <int BN, bool A_MN, bool B_MN, int CM>
-__global__ void __launch_bounds__(CM ? 320 : 192, 1) gemm_tc_kernel(const __grid_constant__ DevParams p) {
+__global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid_constant__ DevParams p) {
   constexpr int A_BYTES = BM * BK * 2;
   constexpr int B_BYTES = BN * BK * 2;
   constexpr int STAGE = A_BYTES + B_BYTES;
@@ -259,7 +260,7 @@ __global__ void __launch_bounds__(CM ? 320 : 192, 1) gemm_tc_kernel(const __grid
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&tfull[b], 1);
-      tc::mbar_init(&tempty[b], 128);
+      tc::mbar_init(&tempty[b], 256);
     }
     tc::fence_barrier_init();
     tc::fence_proxy_async();
@@ -355,9 +356,10 @@ __global__ void __launch_bounds__(CM ? 320 : 192, 1) gemm_tc_kernel(const __grid
         tc::mma_commit(&tfull[buf]);
       }
     }
-  } else if (warp < 6) {
+  } else if (warp < 10) {
     const int sub = warp & 3;
     const int r_local = sub * 32 + lane;
+    const int chalf = (warp - 2) >> 2;  // column half of the tile handled by this warpgroup
     int it = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
       const TileInfo ti = p.situ ? tile_info<BN / 2>(p, tile) : tile_info<BN>(p, tile);
@@ -368,7 +370,7 @@ __global__ void __launch_bounds__(CM ? 320 : 192, 1) gemm_tc_kernel(const __grid
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + buf * BN;
       const int row = ti.c_row0 + r_local;
       const bool row_ok = (p.mode == 1) ? true : row < p.M;
-      for (int c0 = 0; c0 < bnt; c0 += 32) {
+      for (int c0 = chalf * (bnt / 2); c0 < (chalf + 1) * (bnt / 2); c0 += 32) {
         float v[32];
         if (ti.num_kb > 0) {
           tc::tmem_ld_32x32b_x32(taddr + c0, v);
@@ -472,12 +474,12 @@ __global__ void __launch_bounds__(CM ? 320 : 192, 1) gemm_tc_kernel(const __grid
 }
 
 
-// Comm warps (threads 192..319): reduce the tiles this rank owns, then hand every tile's sum out.
+// Comm warps (threads 320..447): reduce the tiles this rank owns, then hand every tile's sum out.
 template <int BN>
 __device__ void comm_loop(const DevParams& p, int total) {
   __shared__ int s_ok;
   const CommParams& c = p.cm;
-  const int ct = threadIdx.x - 192;
+  const int ct = threadIdx.x - 320;
   uint32_t* my_flags = reinterpret_cast<uint32_t*>(c.flags_peer[c.rank]);
   for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
     const TileInfo ti = tile_info<BN>(p, tile);
@@ -594,7 +596,7 @@ cudaError_t launch(const DevParams& dp, int num_sms, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  gemm_tc_kernel<BN, AMN, BMN, CM><<<num_sms, CM ? 320 : 192, smem, s>>>(dp);
+  gemm_tc_kernel<BN, AMN, BMN, CM><<<num_sms, CM ? 448 : 320, smem, s>>>(dp);
   return cudaGetLastError();
 }
 
