@@ -563,7 +563,10 @@ std::vector<at::Tensor> tc_gemm_grouped(int64_t mode, at::Tensor a, at::Tensor b
     g.ldc = out.size(-1);
   }
   g.num_sms = at::cuda::getDeviceProperties(a.get_device())->multiProcessorCount;
-  check(kimi::tc_gemm(g, stream()), "tc_gemm_grouped");
+  const cudaError_t err = kimi::tc_gemm(g, stream());
+  TORCH_CHECK(err == cudaSuccess, "tc_gemm_grouped failed: ", cudaGetErrorString(err), " (mode ", mode, ", epi ", epi,
+              ", bn ", bn, ", M ", M, ", N ", N, ", K ", K, ", G ", G, ", a ", a.size(0), "x", a.size(1), " ld ",
+              a.stride(0), ", b ", b.sizes(), ", a_mn ", a_mn, ", b_mn ", b_mn, ")");
   return outs;
 }
 
@@ -640,6 +643,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_rows", &ce_rows);
   m.def("router", &router);
   m.def("tcs_selftest", &tcs_selftest);
+  m.def("kda_phase_profile", &kimi::kda_phase_profile);
   m.def("kda_tc_status", [](bool clear) { return kimi::kda_tc_status(clear); });
   m.def("kda_fwd", &kda_fwd);
   m.def("kda_bwd", &kda_bwd);

@@ -586,6 +586,8 @@ bool make_map_2d(CUtensorMap* m, const void* ptr, uint64_t d0, uint64_t d1, uint
 
 template <int BN, bool AMN, bool BMN, int CM = 0>
 cudaError_t launch(const DevParams& dp, int num_sms, cudaStream_t s) {
+  // an error left by an unrelated earlier call on this host thread is not this launch's
+  (void)cudaGetLastError();
   constexpr int STAGES = BN == 256 ? 4 : 6;
   constexpr int STAGE = BM * BK * 2 + BN * BK * 2;
   const size_t smem = 1024 + (size_t)STAGES * STAGE + (2 * STAGES + 4) * 8 + 16;

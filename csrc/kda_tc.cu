@@ -21,6 +21,8 @@
 // Gradients of q and k accumulate in global fp32 (one writer per element per stage); dG
 // accumulates in shared memory and becomes dg by a reverse cumulative sum.  Every mbarrier wait
 // is bounded and reports through the status word.
+#include <vector>
+
 #include "kernels.h"
 #include "tc_small.cuh"
 
@@ -40,6 +42,15 @@ constexpr int OFF_5A = 80 * KB;          // [dA^T | dP^T] R64 K128
 constexpr int OFF_3A = 112 * KB;         // [Y_K | Y_V]   R64 K128   | later [Kq | Qq] R64 K128
 constexpr int ARENA = 152 * KB;          // M = 128 reads of R64 tiles reach 8 KB past their last atom
 constexpr int LDT = 68;                  // A^T row stride (16-byte aligned rows)
+
+// Optional phase timing of the intra backward (block 0, its first chunk, thread 0): clock64() at
+// each phase boundary, enabled from the host for profiling runs only.
+__device__ long long g_kda_phase[16];
+__device__ int g_kda_phase_on = 0;
+#define KIMI_PHASE(k)                                                          \
+  do {                                                                          \
+    if (phase_on && blockIdx.x == 0 && ci == 0 && tid == 0) g_kda_phase[k] = clock64(); \
+  } while (0)
 
 struct BwdArgs {
   const void* q;
@@ -197,6 +208,7 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
   tc::tc_fence_after();
   const uint32_t tm = *slot;
   uint32_t phase = 0;
+  const int phase_on = g_kda_phase_on;
   const int H = a.H, Tp = a.Tp, NC = a.NC;
   const int total = a.B * H * NC;
 
@@ -217,6 +229,7 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
     for (int u = 0; u < 32; ++u) gacc[u] = 0.f;
     const int ri = row & 63;
 
+    KIMI_PHASE(0);
     // ---------------------------------------------------------------- loads (all issued before any use)
     {
       float gv[16], av[16];
@@ -266,6 +279,7 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
       }
     }
     __syncthreads();
+    KIMI_PHASE(1);
     {  // G = cumsum over rows: four 16-row segments per channel, then the segment offsets
       const int d = tid & 63, part = tid >> 6;
       float run = 0.f;
@@ -284,12 +298,14 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
       }
     }
     tcs::operands_ready();
+    KIMI_PHASE(2);
     if (tid == 0) {
       tcs::mma_rows128(tm, opx, 128, opy, 128, 0, 128, 0, 64, false);      // MMA-1 -> cols [0,128)
       tcs::mma_rows128(tm + 128, opy, 128, opz, 64, 0, 64, 0, 64, false);  // MMA-2 -> cols [128,192)
       tc::mma_commit(bar);
     }
     tcs::mma_done(bar, phase, a.status, 11);
+    KIMI_PHASE(3);
 
     // ---------------------------------------------------------------- read MMA-1 / MMA-2
     {
@@ -350,6 +366,7 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
       }
     }
     __syncthreads();
+    KIMI_PHASE(4);
 
     // ---------------------------------------------------------------- solve (threads 128..255) | W, U, Kown (0..127)
     if (tid >= 128) {
@@ -406,11 +423,13 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
       }
     }
     tcs::operands_ready();
+    KIMI_PHASE(5);
     if (tid == 0) {
       tcs::mma_rows128(tm, op3a, 64, op3b, 64, 0, 64, 0, 128, false);  // MMA-3 -> cols [0,64)
       tc::mma_commit(bar);
     }
     tcs::mma_done(bar, phase, a.status, 12);
+    KIMI_PHASE(6);
 
     // ---------------------------------------------------------------- dL -> dA, dbeta, Y terms | Kown
     if (row < 64) {
@@ -456,6 +475,7 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
       }
     }
     __syncthreads();
+    KIMI_PHASE(7);
     // [dA^T | dP^T]
     for (int idx = tid; idx < 64 * 64; idx += NTH) {
       const int i = idx >> 6, j = idx & 63;
@@ -463,6 +483,7 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
       tcs::st(op5a, 64, j, 64 + i, tcs::ld(op4a, 128, 64 + i, j));
     }
     tcs::operands_ready();
+    KIMI_PHASE(8);
     if (tid == 0) {
 #pragma unroll
       for (int J = 0; J < 4; ++J)  // MMA-4: row side, K tile J -> cols [64J, 64J+64)
@@ -475,6 +496,7 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
       tc::mma_commit(bar);
     }
     tcs::mma_done(bar, phase, a.status, 13);
+    KIMI_PHASE(9);
 
     // ---------------------------------------------------------------- row side (dk rows: dA, dq rows: dP)
     {
@@ -531,6 +553,7 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
 #pragma unroll
     for (int u = 0; u < 32; ++u) stage[(row >= 64 ? C * LDP : 0) + ri * LDP + c0 + u] = gacc[u];
     __syncthreads();
+    KIMI_PHASE(10);
     {
       float* dq = a.dq + tok0;
       float* dk = a.dk + tok0;
@@ -553,6 +576,7 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
     }
     tc::tc_fence_before();
     __syncthreads();
+    KIMI_PHASE(11);
     tc::tc_fence_after();
   }
   if (warp == 0) tc::tmem_dealloc(tm, 512);
@@ -1048,6 +1072,14 @@ int* status_ptr(int* status) {
 }
 
 }  // namespace
+
+std::vector<long long> kda_phase_profile(bool enable) {
+  std::vector<long long> v(16, 0);
+  cudaMemcpyFromSymbol(v.data(), g_kda_phase, sizeof(long long) * 16);
+  const int on = enable ? 1 : 0;
+  cudaMemcpyToSymbol(g_kda_phase_on, &on, sizeof(int));
+  return v;
+}
 
 int kda_tc_status(bool clear) {
   int v = 0;

@@ -2,6 +2,7 @@
 // Each launcher takes raw device pointers and a stream and returns the launch status.
 // dtype codes: 0 = float32, 1 = bfloat16, 2 = float16.
 #pragma once
+#include <vector>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -85,6 +86,9 @@ cudaError_t kda_state_fwd_tc(int dtype, KdaBuffers buf, const float* h0, void* o
                              int tokens_padded, int heads, int* status, cudaStream_t s);
 cudaError_t kda_state_bwd_tc(int dtype, KdaBuffers buf, const void* dout, const float* dht, float* dVp, float* dSn,
                              float* dh0, int batch, int tokens_padded, int heads, int* status, cudaStream_t s);
+// Phase timestamps (clock64) of the intra backward's first chunk on block 0 from the last launch
+// made while enabled; enable / disable recording for later launches.
+std::vector<long long> kda_phase_profile(bool enable);
 // Device status word shared by the tcgen05 KDA kernels (read and cleared by the host).
 int kda_tc_status(bool clear);
 
