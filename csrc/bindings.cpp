@@ -309,6 +309,49 @@ std::vector<at::Tensor> kda_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Te
   return {dq, dk, dv, dg, dbeta, dh0};
 }
 
+// ---------------------------------------------------------------- fused Muon passes
+void muon_momentum(at::Tensor g, at::Tensor mom, at::Tensor x, at::Tensor sumsq, double momentum, bool nesterov,
+                   c10::optional<at::Tensor> skip) {
+  CHECK_CUDA_CONTIG(g);
+  CHECK_CUDA_CONTIG(mom);
+  CHECK_CUDA_CONTIG(x);
+  CHECK_CUDA_CONTIG(sumsq);
+  TORCH_CHECK(g.scalar_type() == at::kFloat && mom.scalar_type() == at::kFloat && x.scalar_type() == at::kBFloat16 &&
+                  sumsq.scalar_type() == at::kFloat && g.dim() == 3 && g.sizes() == mom.sizes() &&
+                  g.sizes() == x.sizes() && sumsq.numel() == g.size(0),
+              "muon_momentum: g, mom fp32 [count, m, n], x bf16 of the same shape, sumsq fp32 [count]");
+  const at::cuda::CUDAGuard gd(g.device());
+  const bool* sk = (skip.has_value() && skip->defined()) ? skip->data_ptr<bool>() : nullptr;
+  check(kimi::muon_momentum(g.data_ptr<float>(), mom.data_ptr<float>(), x.data_ptr(), sumsq.data_ptr<float>(),
+                            (int)g.size(0), g.size(1) * g.size(2), (float)momentum, nesterov, sk, stream()),
+        "muon_momentum");
+}
+
+void muon_normalize(at::Tensor x, at::Tensor sumsq, double eps) {
+  CHECK_CUDA_CONTIG(x);
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 3 && sumsq.numel() == x.size(0), "muon_normalize");
+  const at::cuda::CUDAGuard gd(x.device());
+  check(kimi::muon_normalize(x.data_ptr(), sumsq.data_ptr<float>(), (int)x.size(0), x.size(1) * x.size(2),
+                             (float)eps, stream()),
+        "muon_normalize");
+}
+
+void muon_apply(at::Tensor o, at::Tensor param_ptrs, at::Tensor sumsq, at::Tensor lr, double wd, double scale,
+                double eps, c10::optional<at::Tensor> skip, at::Tensor stats) {
+  CHECK_CUDA_CONTIG(o);
+  TORCH_CHECK(o.scalar_type() == at::kBFloat16 && o.dim() == 3 && param_ptrs.scalar_type() == at::kLong &&
+                  param_ptrs.is_cuda() && param_ptrs.numel() == o.size(0) && sumsq.numel() == o.size(0) &&
+                  lr.is_cuda() && lr.scalar_type() == at::kFloat && stats.numel() == 3 * o.size(0) &&
+                  stats.scalar_type() == at::kFloat,
+              "muon_apply: o bf16 [count, m, n], one fp32 parameter pointer per matrix, device lr, stats [count, 3]");
+  const at::cuda::CUDAGuard gd(o.device());
+  const bool* sk = (skip.has_value() && skip->defined()) ? skip->data_ptr<bool>() : nullptr;
+  check(kimi::muon_apply(o.data_ptr(), reinterpret_cast<float* const*>(param_ptrs.data_ptr<int64_t>()),
+                         sumsq.data_ptr<float>(), (int)o.size(0), o.size(1) * o.size(2), lr.data_ptr<float>(),
+                         (float)wd, (float)scale, (float)eps, sk, stats.data_ptr<float>(), stream()),
+        "muon_apply");
+}
+
 // ---------------------------------------------------------------- tcgen05 small-matrix self-test
 std::vector<at::Tensor> tcs_selftest(at::Tensor a, at::Tensor b, int64_t n, int64_t mode) {
   CHECK_CUDA_CONTIG(a);
@@ -643,6 +686,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_rows", &ce_rows);
   m.def("router", &router);
   m.def("tcs_selftest", &tcs_selftest);
+  m.def("muon_momentum", &muon_momentum);
+  m.def("muon_normalize", &muon_normalize);
+  m.def("muon_apply", &muon_apply);
   m.def("kda_phase_profile", &kimi::kda_phase_profile);
   m.def("kda_tc_status", [](bool clear) { return kimi::kda_tc_status(clear); });
   m.def("kda_fwd", &kda_fwd);

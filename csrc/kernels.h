@@ -101,6 +101,15 @@ cudaError_t flash_attn_bwd(int dtype, const void* q, const void* k, const void* 
                            int tk, int heads, int dqk, int dv_dim, bool causal, const int* key_lengths, float scale,
                            cudaStream_t s);
 
+// ---- fused Muon passes around the Newton-Schulz GEMMs (optim.cu); one bucket of `count`
+// equal-shape matrices of `mn` elements, contiguous
+cudaError_t muon_momentum(const float* g, float* mom, void* x_bf16, float* sumsq, int count, int64_t mn,
+                          float momentum, bool nesterov, const bool* skip, cudaStream_t s);
+cudaError_t muon_normalize(void* x_bf16, const float* sumsq, int count, int64_t mn, float eps, cudaStream_t s);
+cudaError_t muon_apply(const void* o_bf16, float* const* params, const float* sumsq, int count, int64_t mn,
+                       const float* lr, float wd, float scale, float eps, const bool* skip, float* stats,
+                       cudaStream_t s);
+
 // ---- self-test of the small-matrix tcgen05 path (tc_small_selftest.cu)
 cudaError_t tcs_selftest(const float* A, const float* B, float* out, int K, int n, int mode, int* status,
                          cudaStream_t s);

@@ -117,17 +117,23 @@ def batched_newton_schulz(x: torch.Tensor, *, steps: int = 5, eps: float = 1e-7,
 
     Tall matrices are transposed so the Gram matrix is the small side.
     """
-    a, b, c = NS_COEFFS
     transposed = x.shape[-2] > x.shape[-1]
     w = x.transpose(-2, -1) if transposed else x
     norms = w.float().flatten(1).norm(dim=1)
     w = (w.float() / norms.clamp_min(eps)[:, None, None]).to(dtype)
+    w = newton_schulz_iterations(w, steps)
+    w = w.float() * (norms > eps).to(torch.float32)[:, None, None]
+    return w.transpose(-2, -1) if transposed else w
+
+
+def newton_schulz_iterations(w: torch.Tensor, steps: int) -> torch.Tensor:
+    """The quintic iterations on an already normalised batch ``[N, m, n]`` with ``m <= n``."""
+    a, b, c = NS_COEFFS
     for _ in range(steps):
         gram = w @ w.transpose(-2, -1)
         poly = torch.baddbmm(gram, gram, gram, beta=b, alpha=c)  # b*G + c*G@G
         w = torch.baddbmm(w, poly, w, beta=a, alpha=1.0)          # a*X + poly@X
-    w = w.float() * (norms > eps).to(torch.float32)[:, None, None]
-    return w.transpose(-2, -1) if transposed else w
+    return w
 
 
 @torch.no_grad()
@@ -482,10 +488,13 @@ class KimiMuon(torch.optim.Optimizer):
                 raise RuntimeError("device-flag Muon steps need a gradient for every parameter")
             return self._step_sparse()
         metrics = {"raw": [], "ortho": [], "scaled": [], "ratio": []}
-        for gi, rows, cols, ps, mom_buf, numel in self._ensure_buckets():
+        for bi, (gi, rows, cols, ps, mom_buf, numel) in enumerate(self._ensure_buckets()):
             group = self.param_groups[gi]
             lr, mom, wd = group["lr"], group["momentum"], group["weight_decay"]
             slots = [self._slots[id(p)] for p in ps]
+            if self._fused_ok(mom_buf, rows, cols):
+                self._fused_bucket_step(bi, group, rows, cols, ps, slots, mom_buf, numel, skip, metrics)
+                continue
             g = torch.cat([s.to_blocks(p.grad).to(mom_buf.dtype) for p, s in zip(ps, slots)], 0)
             if skip is not None:
                 g = torch.where(skip, torch.zeros((), device=g.device, dtype=g.dtype), g)
@@ -518,6 +527,61 @@ class KimiMuon(torch.optim.Optimizer):
         self._metric_tensors = {k: torch.cat(v) for k, v in metrics.items() if v}
         self.last_update_metrics = {}
         return self._metric_tensors
+
+    # ---- fused CUDA path: two passes over the bucket around the Newton-Schulz GEMMs
+    @staticmethod
+    def _fused_ok(mom_buf, rows, cols) -> bool:
+        if not mom_buf.is_cuda or mom_buf.dtype != torch.float32 or (rows * cols) % 4:
+            return False
+        from .. import ops
+        return ops.use_kernels(mom_buf)
+
+    def _bucket_tables(self, bi, ps, slots, device):
+        """Per-matrix parameter pointers and the matrix -> parameter map of bucket ``bi`` (cached;
+        parameters never move)."""
+        tables = getattr(self, "_fused_tables", None)
+        if tables is None:
+            tables = self._fused_tables = {}
+        key = (bi, tuple(p.data_ptr() for p in ps))
+        hit = tables.get(bi)
+        if hit is not None and hit[0] == key:
+            return hit[1], hit[2]
+        ptrs, owner = [], []
+        for j, (p, s) in enumerate(zip(ps, slots)):
+            step = s.rows * s.cols * p.element_size()
+            ptrs.extend(p.data_ptr() + m * step for m in range(s.count))
+            owner.extend([j] * s.count)
+        ptr_t = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        own_t = torch.tensor(owner, dtype=torch.int64, device=device)
+        tables[bi] = (key, ptr_t, own_t)
+        return ptr_t, own_t
+
+    def _fused_bucket_step(self, bi, group, rows, cols, ps, slots, mom_buf, numel, skip, metrics):
+        from ..ops import _loader
+        C = _loader.require()
+        dev = mom_buf.device
+        count, mn = mom_buf.shape[0], rows * cols
+        lr, wd = group["lr"], group["weight_decay"]
+        g = torch.cat([s.to_blocks(p.grad).to(torch.float32) for p, s in zip(ps, slots)], 0)
+        x = torch.empty(count, rows, cols, dtype=torch.bfloat16, device=dev)
+        sumsq = torch.zeros(count, dtype=torch.float32, device=dev)
+        C.muon_momentum(g, mom_buf, x, sumsq, float(group["momentum"]), bool(group["nesterov"]), skip)
+        C.muon_normalize(x, sumsq, float(group["eps"]))
+        transposed = rows > cols
+        w = newton_schulz_iterations(x.transpose(-2, -1) if transposed else x, group["ns_steps"])
+        o = (w.transpose(-2, -1) if transposed else w).contiguous()
+        scale = max(rows, cols) ** 0.5 if group["update_rms_scaling"] else 1.0
+        lr_t = lr.reshape(()).float() if torch.is_tensor(lr) else torch.full((), float(lr), device=dev)
+        ptr_t, own_t = self._bucket_tables(bi, ps, slots, dev)
+        stats = torch.zeros(count, 3, dtype=torch.float32, device=dev)
+        C.muon_apply(o, ptr_t, sumsq, lr_t, float(wd), float(scale), float(group["eps"]), skip, stats)
+        metrics["raw"].append((sumsq / mn).sqrt())
+        ortho = (stats[:, 0] / mn).sqrt()
+        metrics["ortho"].append(ortho)
+        metrics["scaled"].append(ortho * scale)
+        per = torch.zeros(len(ps), 2, dtype=torch.float32, device=dev).index_add_(0, own_t, stats[:, 1:])
+        unorm, pnorm = per[:, 0].sqrt(), per[:, 1].sqrt()
+        metrics["ratio"].append(lr_t * unorm / (pnorm.clamp_min(1e-30) / numel).clamp_min(group["eps"]) / numel)
 
     @torch.no_grad()
     def _step_sparse(self):

@@ -53,6 +53,7 @@ def test_fused_reduce_two_ranks():
                 "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={_free_port()}", HERE, "multi"],
                timeout=300)
     assert "multi-rank ok" in out
+    print([line for line in out.splitlines() if line.startswith("paths:")])
 
 
 # ---------------------------------------------------------------------------- children
@@ -128,6 +129,7 @@ def child_multi():
     world = int(os.environ["WORLD_SIZE"])
     dist = _init(rank, world)
     from kimi_k3_b200.parallel.symmetric import SymmetricWorkspace, fused_matmul_reduce
+    paths = []
     for use_mc in (True, False):
         ws = SymmetricWorkspace(None, f"cuda:{rank}", 1 << 24, use_multicast=use_mc)
         if use_mc and not ws.has_multicast:
@@ -146,11 +148,13 @@ def child_multi():
                 rs = fused_matmul_reduce(x, w, ws, reduce="reduce_scatter")
                 _close(rs, ref[rank * (m // world):(rank + 1) * (m // world)], 2e-2)
         ws.check()
+        paths.append("nvls-multimem" if use_mc else "peer")
         del ws
     torch.cuda.synchronize()
     dist.barrier()
     dist.destroy_process_group()
     if rank == 0:
+        print("paths: " + "+".join(paths))
         print("multi-rank ok")
 
 
