@@ -201,7 +201,37 @@ def bench_attnres(args) -> list:
     return rows
 
 
-CASES = {"gemm": bench_gemm, "kda": bench_kda, "moe": bench_moe, "linear_ce": bench_linear_ce,
+def bench_kda_phases(args) -> list:
+    """Per-phase cycles of the tcgen05 KDA intra backward (block 0, its first chunk) from the
+    kernel's optional clock64 probes."""
+    C, dev = _require_cuda()
+    from ..ops import kda_chunk
+    torch.manual_seed(0)
+    b, t, h = args.batch, args.tokens, args.heads
+    q = F.normalize(torch.randn(b, t, h, 64, device=dev), dim=-1).bfloat16().requires_grad_()
+    k = F.normalize(torch.randn(b, t, h, 64, device=dev), dim=-1).bfloat16().requires_grad_()
+    v = torch.randn(b, t, h, 64, device=dev).bfloat16().requires_grad_()
+    g = (-5 * torch.sigmoid(torch.randn(b, t, h, 64, device=dev) - 2)).requires_grad_()
+    beta = torch.sigmoid(torch.randn(b, t, h, device=dev)).requires_grad_()
+    for it in range(3):
+        C.kda_phase_profile(it == 2)
+        o, _ = kda_chunk(q, k, v, g, beta, None, False)
+        o.float().sum().backward()
+        torch.cuda.synchronize()
+    ph = C.kda_phase_profile(False)
+    names = ["loads", "cumsum+operands", "MMA-1/2 wait", "read MMA-1/2", "solve | W,U,Kown", "MMA-3 wait",
+             "dL->dA | Kq,Qq", "dA^T|dP^T transpose", "MMA-4/5 wait", "row+column side", "stores+dg"]
+    clock_khz = torch.cuda.get_device_properties(dev).clock_rate
+    total = ph[11] - ph[0]
+    rows = []
+    for i, n in enumerate(names):
+        cyc = ph[i + 1] - ph[i]
+        rows.append(_emit({"case": "kda_phases", "phase": n, "cycles": cyc, "us": round(cyc / clock_khz * 1e3, 2),
+                           "share": round(cyc / max(total, 1), 3)}))
+    return rows
+
+
+CASES = {"kda_phases": bench_kda_phases, "gemm": bench_gemm, "kda": bench_kda, "moe": bench_moe, "linear_ce": bench_linear_ce,
          "attention": bench_attention, "attnres": bench_attnres}
 
 
