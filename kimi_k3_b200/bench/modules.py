@@ -486,6 +486,7 @@ def bench_step_profile(argv=None) -> str:
     p.add_argument("--seq-len", type=int, default=1024)
     p.add_argument("--vocab", type=int, default=50257)
     p.add_argument("--top", type=int, default=40)
+    p.add_argument("--shapes", action="store_true", help="group the table by input shapes")
     args = p.parse_args(argv)
     dev = torch.device("cuda", 0)
     torch.manual_seed(0)
@@ -499,12 +500,14 @@ def bench_step_profile(argv=None) -> str:
     for _ in range(3):
         eng.step(batch, mask_all_valid=True)
     torch.cuda.synchronize()
-    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA], record_shapes=args.shapes) as prof:
         t0 = time.perf_counter()
         eng.step(batch, mask_all_valid=True)
         torch.cuda.synchronize()
         wall = (time.perf_counter() - t0) * 1e3
-    table = prof.key_averages().table(sort_by="cuda_time_total", row_limit=args.top, max_name_column_width=60)
+    table = prof.key_averages(group_by_input_shape=args.shapes).table(
+        sort_by="self_cuda_time_total" if args.shapes else "cuda_time_total", row_limit=args.top,
+        max_name_column_width=60, max_shapes_column_width=90)
     print(f"step wall ms {wall:.1f}")
     print(table)
     return table

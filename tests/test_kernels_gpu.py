@@ -326,6 +326,7 @@ def test_fused_muon_step_matches_unfused(cuda, monkeypatch):
     kw = dict(lr=0.02, momentum=0.95, nesterov=True, ns_steps=5, eps=1e-7, weight_decay=0.1, update_rms_scaling=True,
               spec_by_parameter={})
     o1, o2 = KimiMuon(params, **kw), KimiMuon(params2, **kw)
+    start = [p.detach().clone() for p in params]
     for step in range(3):
         grads = [torch.randn_like(p) for p in params]
         for p, q, g in zip(params, params2, grads):
@@ -334,8 +335,11 @@ def test_fused_muon_step_matches_unfused(cuda, monkeypatch):
         monkeypatch.setenv("KIMI_K3_KERNELS", "0")
         o2.step()
         monkeypatch.delenv("KIMI_K3_KERNELS")
-    for p, q in zip(params, params2):
-        _close(p, q, 2e-3)
+    # both run the Newton-Schulz GEMMs in bf16; the fused path rounds the input to bf16 before
+    # normalising it, so the updates agree to bf16 Newton-Schulz accuracy
+    for p, q, p0 in zip(params, params2, start):
+        d1, d2 = (p - p0).float(), (q - p0).float()
+        assert (d1 - d2).norm() <= 3e-2 * d2.norm(), ((d1 - d2).norm().item(), d2.norm().item())
     m1, m2 = o1.update_metrics(), o2.update_metrics()
     for key in m1:
         assert abs(m1[key] - m2[key]) <= 2e-2 * max(abs(m2[key]), 1e-6), (key, m1[key], m2[key])
