@@ -75,12 +75,16 @@ __global__ void __launch_bounds__(256) conv_fwd_v_kernel(const T* __restrict__ x
 #pragma unroll
       for (int e = 0; e < 8; ++e) hist[j][e] = 0.f;
   }
-  for (int t = t0; t < t1; ++t) {
-    if (active)
-      load8<T>(x + (rowbase + t) * channels + c0, hist[0]);
-    else
+  float xnext[8];  // the next token's x, loaded one step ahead
+  if (active && t0 < t1)
+    load8<T>(x + (rowbase + t0) * channels + c0, xnext);
+  else
 #pragma unroll
-      for (int e = 0; e < 8; ++e) hist[0][e] = 0.f;
+    for (int e = 0; e < 8; ++e) xnext[e] = 0.f;
+  for (int t = t0; t < t1; ++t) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) hist[0][e] = xnext[e];
+    if (active && t + 1 < t1) load8<T>(x + (rowbase + t + 1) * channels + c0, xnext);
     float s[8], ss = 0.f;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
@@ -136,13 +140,23 @@ __global__ void __launch_bounds__(256) conv_bwd_v_kernel(const T* __restrict__ d
 #pragma unroll
     for (int e = 0; e < 8; ++e) dph[j][e] = 0.f;
   }
+  float dnext[8], xnext[8];  // dy[t] and x[t - K] of the next step, loaded one step ahead
+  if (active)
+    load8<T>(dy + (rowbase + tstart) * channels + c0, dnext);
+  else
+#pragma unroll
+    for (int e = 0; e < 8; ++e) dnext[e] = 0.f;
   for (int t = tstart; t >= t0; --t) {
     float d[8];
-    if (active)
-      load8<T>(dy + (rowbase + t) * channels + c0, d);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) d[e] = dnext[e];
+    if (active && t - 1 >= t0) load8<T>(dy + (rowbase + t - 1) * channels + c0, dnext);
+    const int tn = t - K;
+    if (active && tn >= 0)
+      load8<T>(x + (rowbase + tn) * channels + c0, xnext);
     else
 #pragma unroll
-      for (int e = 0; e < 8; ++e) d[e] = 0.f;
+      for (int e = 0; e < 8; ++e) xnext[e] = 0.f;
     float pre[8], s[8], ss = 0.f, dot = 0.f;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
@@ -194,12 +208,8 @@ __global__ void __launch_bounds__(256) conv_bwd_v_kernel(const T* __restrict__ d
     for (int j = 0; j < K - 1; ++j)
 #pragma unroll
       for (int e = 0; e < 8; ++e) xw[j][e] = xw[j + 1][e];
-    const int tn = t - K;
-    if (active && tn >= 0)
-      load8<T>(x + (rowbase + tn) * channels + c0, xw[K - 1]);
-    else
 #pragma unroll
-      for (int e = 0; e < 8; ++e) xw[K - 1][e] = 0.f;
+    for (int e = 0; e < 8; ++e) xw[K - 1][e] = xnext[e];
   }
   // this block's dw partial: row (blockIdx.y, blockIdx.x) of the [blocks, C * K] scratch
   if (active) {
@@ -211,13 +221,26 @@ __global__ void __launch_bounds__(256) conv_bwd_v_kernel(const T* __restrict__ d
   }
 }
 
-// dw[i] = sum over blocks of part[block][i]
-__global__ void dw_reduce_kernel(const float* __restrict__ part, float* __restrict__ dw, int blocks, int n) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
+// dw[i] = sum over blocks of part[block][i]: a block owns 32 consecutive columns; its 8 warps read
+// interleaved rows (one 128-byte line per warp and row), then combine through shared memory.
+__global__ void __launch_bounds__(256) dw_reduce_kernel(const float* __restrict__ part, float* __restrict__ dw,
+                                                        int blocks, int n) {
+  __shared__ float red[8][33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int i = blockIdx.x * 32 + lane;
   float acc = 0.f;
-  for (int b = 0; b < blocks; ++b) acc += part[(int64_t)b * n + i];
-  dw[i] = acc;
+  if (i < n) {
+#pragma unroll 8
+    for (int b = blockIdx.y * 8 + warp; b < blocks; b += 8 * gridDim.y) acc += part[(int64_t)b * n + i];
+  }
+  red[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && i < n) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) s += red[w][lane];
+    atomicAdd(&dw[i], s);  // gridDim.y partial sums per weight; dw starts at zero
+  }
 }
 
 template <typename T>
@@ -291,7 +314,10 @@ cudaError_t conv_silu_norm_bwd(int dtype, const void* dy, const void* x, const f
   }
   if (e != cudaSuccess) return e;
   const int n = channels * ksize;
-  dw_reduce_kernel<<<(n + 255) / 256, 256, 0, s>>>(dw_part, dw, conv_bwd_partial_rows(batch, tokens), n);
+  const int rows = conv_bwd_partial_rows(batch, tokens);
+  const dim3 rgrid((n + 31) / 32, rows >= 64 * 8 ? 8 : 1);
+  if (cudaMemsetAsync(dw, 0, sizeof(float) * n, s) != cudaSuccess) return cudaGetLastError();
+  dw_reduce_kernel<<<rgrid, 256, 0, s>>>(dw_part, dw, rows, n);
   return cudaGetLastError();
 }
 

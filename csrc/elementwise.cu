@@ -6,6 +6,8 @@
 // width is a multiple of the vector width. All math is fp32; storage rounding follows
 // the PyTorch reference (normalised value rounded to the activation dtype before the
 // affine multiply).
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -123,6 +125,75 @@ __global__ void rms_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x
   __syncthreads();
   if (dw)
     for (int i = threadIdx.x; i < period * dim; i += blockDim.x) atomicAdd(&dw[i], sdw[i]);
+}
+
+// Per-channel weight (period 1) and rows of at most 32 * MAXV vectors: one warp per row keeps x and dy
+// in registers for both passes, and each lane accumulates its channels' dw partials in registers
+// over all the rows it visits (no shared-memory atomics); one block-level reduction at the end.
+template <typename T, int MAXV>
+__global__ void __launch_bounds__(256) rms_bwd_warp_kernel(const T* __restrict__ dy, const T* __restrict__ x,
+                                                           const float* __restrict__ w,
+                                                           const float* __restrict__ rstd, T* __restrict__ dx,
+                                                           float* __restrict__ dw, int64_t rows, int dim) {
+  constexpr int VN = Vec<T>::N;
+  extern __shared__ float sdw[];  // dim
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, wpb = blockDim.x >> 5;
+  const int nvec = dim / VN;
+  float wv[MAXV][VN], acc[MAXV][VN];
+#pragma unroll
+  for (int v = 0; v < MAXV; ++v) {
+    const int vi = lane + 32 * v;
+#pragma unroll
+    for (int j = 0; j < VN; ++j) {
+      wv[v][j] = (w && vi < nvec) ? round_through<T>(w[vi * VN + j]) : 1.f;
+      acc[v][j] = 0.f;
+    }
+  }
+  for (int64_t row = (int64_t)blockIdx.x * wpb + warp; row < rows; row += (int64_t)gridDim.x * wpb) {
+    const T* xr = x + row * dim;
+    const T* dyr = dy + row * dim;
+    const float r = rstd[row];
+    Vec<T> xa[MAXV], ga[MAXV];
+    float dot = 0.f;
+#pragma unroll
+    for (int v = 0; v < MAXV; ++v) {
+      const int vi = lane + 32 * v;
+      if (vi < nvec) {
+        xa[v].load(xr + vi * VN);
+        ga[v].load(dyr + vi * VN);
+#pragma unroll
+        for (int j = 0; j < VN; ++j) dot += ga[v].f(j) * wv[v][j] * xa[v].f(j) * r;
+      }
+    }
+    dot = warp_sum(dot) / dim;
+    T* dxr = dx + row * dim;
+#pragma unroll
+    for (int v = 0; v < MAXV; ++v) {
+      const int vi = lane + 32 * v;
+      if (vi < nvec) {
+        Vec<T> o;
+#pragma unroll
+        for (int j = 0; j < VN; ++j) {
+          const float xh = xa[v].f(j) * r;
+          o.set(j, r * (ga[v].f(j) * wv[v][j] - xh * dot));
+          acc[v][j] += ga[v].f(j) * round_through<T>(xh);
+        }
+        o.store(dxr + vi * VN);
+      }
+    }
+  }
+  if (!dw) return;
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) sdw[i] = 0.f;
+  __syncthreads();
+#pragma unroll
+  for (int v = 0; v < MAXV; ++v) {
+    const int vi = lane + 32 * v;
+    if (vi < nvec)
+#pragma unroll
+      for (int j = 0; j < VN; ++j) atomicAdd(&sdw[vi * VN + j], acc[v][j]);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) atomicAdd(&dw[i], sdw[i]);
 }
 
 // ------------------------------------------------------------------ SiTU-GLU and sigmoid gate
@@ -273,6 +344,18 @@ cudaError_t rms_norm_bwd(int dtype, const void* dy, const void* x, const float* 
     // global atomics per weight element stay in the hundreds.
     int grid = grid_for(rows, threads / tpr);
     if (dw && grid > 148 * 4) grid = 148 * 4;
+    const int nvec = dim / Vec<T>::N;
+    if (p == 1 && nvec <= 32 * 4) {
+      const int wgrid = (int)std::min<int64_t>((rows + 7) / 8, 148 * 8);
+      const size_t wsmem = dw ? (size_t)dim * sizeof(float) : 0;
+      if (nvec <= 32)
+        rms_bwd_warp_kernel<T, 1><<<wgrid, 256, wsmem, s>>>((const T*)dy, (const T*)x, w, rstd, (T*)dx, dw, rows, dim);
+      else if (nvec <= 64)
+        rms_bwd_warp_kernel<T, 2><<<wgrid, 256, wsmem, s>>>((const T*)dy, (const T*)x, w, rstd, (T*)dx, dw, rows, dim);
+      else
+        rms_bwd_warp_kernel<T, 4><<<wgrid, 256, wsmem, s>>>((const T*)dy, (const T*)x, w, rstd, (T*)dx, dw, rows, dim);
+      break;
+    }
     rms_bwd_kernel<T><<<grid, threads, smem, s>>>(
         (const T*)dy, (const T*)x, w, rstd, (T*)dx, dw, rows, dim, p, tpr);
   });

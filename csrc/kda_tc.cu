@@ -142,9 +142,9 @@ struct QKRows {
   int64_t rs;
   T* sq;
   T* sk;
-  KIMI_D void stage(int tid) {
+  KIMI_D void stage(int tid, int nthreads) {
     if constexpr (kStaged) {
-      for (int idx = tid; idx < 64 * 8; idx += NTH) {
+      for (int idx = tid; idx < 64 * 8; idx += nthreads) {
         const int i = idx >> 3, c8 = (idx & 7) * 8;
         *reinterpret_cast<uint4*>(sq + i * LD + c8) = *reinterpret_cast<const uint4*>(gq + i * rs + c8);
         *reinterpret_cast<uint4*>(sk + i * LD + c8) = *reinterpret_cast<const uint4*>(gk + i * rs + c8);
@@ -165,8 +165,12 @@ struct QKRows {
   }
 };
 
+// 16 warps: thread (TMEM row `row`, column quarter cq) owns columns [16 cq, 16 cq + 16) of each
+// 64-wide block of its row, so twice as many warps share each phase's per-row work.
+constexpr int NTB = 512;
+
 template <typename T>
-__global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_constant__ BwdArgs a) {
+__global__ void __launch_bounds__(NTB, 1) kda_intra_bwd_tc_kernel(const __grid_constant__ BwdArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* arena = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* op4a = reinterpret_cast<float*>(arena + OFF_4A);
@@ -193,8 +197,8 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int row = (warp & 3) * 32 + lane;  // TMEM lane of this thread
-  const int half = warp >> 2;              // column half handled by this thread
-  const int c0 = 32 * half;
+  const int cq = warp >> 2;                // column quarter handled by this thread
+  const int c0 = 16 * cq;
   if (tid == 0) {
     tc::mbar_init(bar, 1);
     tc::fence_barrier_init();
@@ -222,21 +226,20 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
     const float* g = a.g + tok0;
     QKRows<T> qk{reinterpret_cast<const T*>(a.q) + tok0, reinterpret_cast<const T*>(a.k) + tok0, rs, sQK,
                  sQK + 64 * QKRows<T>::LD};
-    // Gradient rows owned by this thread: dk for lanes 0..63 (rows of dV', V', dA),
-    // dq for lanes 64..127 (rows of dO, dP); channels [c0, c0 + 32).
-    float gacc[32];
+    // dk for TMEM lanes 0..63 (rows of dV', V', dA), dq for lanes 64..127 (rows of dO, dP)
+    float gacc[16];
 #pragma unroll
-    for (int u = 0; u < 32; ++u) gacc[u] = 0.f;
+    for (int u = 0; u < 16; ++u) gacc[u] = 0.f;
     const int ri = row & 63;
 
     KIMI_PHASE(0);
     // ---------------------------------------------------------------- loads (all issued before any use)
     {
-      float gv[16], av[16];
-      float4 t4[5][4];
+      float gv[8], av[8];
+      float4 t4[5][2];
 #pragma unroll
-      for (int n = 0; n < 16; ++n) {
-        const int idx = tid + n * NTH, i = idx >> 6, d = idx & 63;
+      for (int n = 0; n < 8; ++n) {
+        const int idx = tid + n * NTB, i = idx >> 6, d = idx & 63;
         gv[n] = g[i * rs + d];
         av[n] = a.Araw[bo + idx];
       }
@@ -244,28 +247,28 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
 #pragma unroll
       for (int m = 0; m < 4; ++m)
 #pragma unroll
-        for (int n = 0; n < 4; ++n) {
-          const int idx = tid + n * NTH, r = idx >> 4, k4 = (idx & 15) * 4;
+        for (int n = 0; n < 2; ++n) {
+          const int idx = tid + n * NTB, r = idx >> 4, k4 = (idx & 15) * 4;
           t4[m][n] = *reinterpret_cast<const float4*>(srcs[m] + r * 64 + k4);
         }
 #pragma unroll
-      for (int n = 0; n < 4; ++n) {
-        const int idx = tid + n * NTH, r = idx >> 4, k4 = (idx & 15) * 4;
+      for (int n = 0; n < 2; ++n) {
+        const int idx = tid + n * NTB, r = idx >> 4, k4 = (idx & 15) * 4;
         const T* p = dout + (int64_t)r * rs + k4;
         t4[4][n] = make_float4(to_f<T>(p[0]), to_f<T>(p[1]), to_f<T>(p[2]), to_f<T>(p[3]));
       }
       const float bt = tid < C ? a.beta[((int64_t)b * Tp + t0 + tid) * H + h] : 0.f;
-      qk.stage(tid);
+      qk.stage(tid, NTB);
 #pragma unroll
-      for (int n = 0; n < 16; ++n) {
-        const int idx = tid + n * NTH, i = idx >> 6, d = idx & 63;
+      for (int n = 0; n < 8; ++n) {
+        const int idx = tid + n * NTB, i = idx >> 6, d = idx & 63;
         sG[i * LDP + d] = gv[n];
         sDG[i * LDP + d] = 0.f;
         sAT[d * LDT + i] = av[n];
       }
 #pragma unroll
-      for (int n = 0; n < 4; ++n) {
-        const int idx = tid + n * NTH, r = idx >> 4, k4 = (idx & 15) * 4;
+      for (int n = 0; n < 2; ++n) {
+        const int idx = tid + n * NTB, r = idx >> 4, k4 = (idx & 15) * 4;
         tcs::st4(opx, 128, r, k4, t4[0][n]);        // dV'
         tcs::st4(opx, 128, 64 + r, k4, t4[4][n]);   // dO
         tcs::st4(opy, 128, r, k4, t4[1][n]);        // V'
@@ -280,21 +283,21 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
     }
     __syncthreads();
     KIMI_PHASE(1);
-    {  // G = cumsum over rows: four 16-row segments per channel, then the segment offsets
+    {  // G = cumsum over rows: eight 8-row segments per channel, then the segment offsets
       const int d = tid & 63, part = tid >> 6;
       float run = 0.f;
 #pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        run += sG[(16 * part + r) * LDP + d];
-        sG[(16 * part + r) * LDP + d] = run;
+      for (int r = 0; r < 8; ++r) {
+        run += sG[(8 * part + r) * LDP + d];
+        sG[(8 * part + r) * LDP + d] = run;
       }
       __syncthreads();
       float off = 0.f;
-      for (int p2 = 0; p2 < part; ++p2) off += sG[(16 * p2 + 15) * LDP + d];
+      for (int p2 = 0; p2 < part; ++p2) off += sG[(8 * p2 + 7) * LDP + d];
       __syncthreads();
       if (part > 0) {
 #pragma unroll
-        for (int r = 0; r < 16; ++r) sG[(16 * part + r) * LDP + d] += off;
+        for (int r = 0; r < 8; ++r) sG[(8 * part + r) * LDP + d] += off;
       }
     }
     tcs::operands_ready();
@@ -309,24 +312,23 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
 
     // ---------------------------------------------------------------- read MMA-1 / MMA-2
     {
-      float val[32];
+      float val[16];
       if (row < 64) {
         const int j = ri;
         // dW = -(dV' S^T) -> left half of the solve's right-hand side; dU = dV' -> right half
-        tcs::tmem_row32(tm, warp, 64 + c0, val);
+        tcs::tmem_row16(tm, warp, 64 + c0, val);
 #pragma unroll
-        for (int u = 0; u < 32; u += 4)
+        for (int u = 0; u < 16; u += 4)
           *reinterpret_cast<float4*>(rhs + j * 128 + c0 + u) = make_float4(-val[u], -val[u + 1], -val[u + 2], -val[u + 3]);
-        for (int u = 0; u < 32; ++u) rhs[j * 128 + 64 + c0 + u] = tcs::ld(opx, 128, j, c0 + u);
-        // dKend = V' dSn^T: dk = dKend e^{G_C - G}, dG -= dKend Kend, dG_C += sum_j dKend Kend
-        tcs::tmem_row32(tm + 128, warp, c0, val);
-        float kv[32];
-        qk.row32(false, j, c0, kv);
 #pragma unroll
-        for (int u = 0; u < 32; ++u) {
+        for (int u = 0; u < 16; ++u) rhs[j * 128 + 64 + c0 + u] = tcs::ld(opx, 128, j, c0 + u);
+        // dKend = V' dSn^T: dk = dKend e^{G_C - G}, dG -= dKend Kend, dG_C += sum_j dKend Kend
+        tcs::tmem_row16(tm + 128, warp, c0, val);
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
           const int d = c0 + u;
           const float f = expf(sG[63 * LDP + d] - sG[j * LDP + d]);
-          const float kend = kv[u] * f;
+          const float kend = qk.at(false, j, d) * f;
           gacc[u] = val[u] * f;
           atomicAdd(&sDG[j * LDP + d], -val[u] * kend);
           const float sum = warp_sum(val[u] * kend);
@@ -335,32 +337,30 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
       } else {
         const int i = ri;
         // dP = lower(dO V'^T) -> rows 64.. of [dA; dP]
-        tcs::tmem_row32(tm, warp, c0, val);
+        tcs::tmem_row16(tm, warp, c0, val);
 #pragma unroll
-        for (int u = 0; u < 32; u += 4) {
+        for (int u = 0; u < 16; u += 4) {
           const int j = c0 + u;
           tcs::st4(op4a, 128, 64 + i, j,
                    make_float4(j <= i ? val[u] : 0.f, j + 1 <= i ? val[u + 1] : 0.f, j + 2 <= i ? val[u + 2] : 0.f,
                                j + 3 <= i ? val[u + 3] : 0.f));
         }
         // dQg = dO S^T: dq = dQg e^G, dG += dQg q e^G
-        tcs::tmem_row32(tm, warp, 64 + c0, val);
-        float qv[32];
-        qk.row32(true, i, c0, qv);
+        tcs::tmem_row16(tm, warp, 64 + c0, val);
 #pragma unroll
-        for (int u = 0; u < 32; ++u) {
+        for (int u = 0; u < 16; ++u) {
           const int d = c0 + u;
           const float e = expf(sG[i * LDP + d]);
           gacc[u] = val[u] * e;
-          atomicAdd(&sDG[i * LDP + d], val[u] * qv[u] * e);
+          atomicAdd(&sDG[i * LDP + d], val[u] * qk.at(true, i, d) * e);
         }
-        // diag(S dSn^T): the e^{G_C} term of dG_C (rows 64.. of MMA-2 are the channels of S)
-        if ((i >> 5) == half) {
-          tcs::tmem_row32(tm + 128, warp, c0, val);
+        // diag(S dSn^T): the e^{G_C} term of dG_C; the warp of column quarter cq holds channels 16 cq..
+        tcs::tmem_row16(tm + 128, warp, c0, val);
+        if ((i >> 4) == cq) {
           float mine = 0.f;
 #pragma unroll
-          for (int u = 0; u < 32; ++u)
-            if (u == lane) mine = val[u];
+          for (int u = 0; u < 16; ++u)
+            if (u == (i & 15)) mine = val[u];
           atomicAdd(&sDGC[i], expf(sG[63 * LDP + i]) * mine);
         }
       }
@@ -368,11 +368,10 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
     __syncthreads();
     KIMI_PHASE(4);
 
-    // ---------------------------------------------------------------- solve (threads 128..255) | W, U, Kown (0..127)
-    if (tid >= 128) {
-      // L^T Y = R with L = I + diag(beta) A, one column per thread, 16-row blocks from the bottom:
-      // solve the block in registers, then remove it from every earlier row.
-      const int col = tid - 128;
+    // ---------------------------------------------------------------- solve (threads 384..511) | W, U, Kown
+    if (tid >= 384) {
+      // L^T Y = R with L = I + diag(beta) A, one column per thread, 16-row blocks from the bottom
+      const int col = tid - 384;
       for (int J = 3; J >= 0; --J) {
         const int j0 = 16 * J;
         float yb[16], zb[16];
@@ -403,21 +402,15 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
         }
       }
     } else {
-      float4 w4[8], u4[8];
-#pragma unroll
-      for (int n = 0; n < 8; ++n) {
-        const int idx = tid + n * 128, r = idx >> 4, k4 = (idx & 15) * 4;
-        w4[n] = *reinterpret_cast<const float4*>(a.W + bo + r * 64 + k4);
-        u4[n] = *reinterpret_cast<const float4*>(a.U + bo + r * 64 + k4);
-      }
-#pragma unroll
-      for (int n = 0; n < 8; ++n) {
-        const int idx = tid + n * 128, r = idx >> 4, k4 = (idx & 15) * 4;
-        tcs::st4(op3b, 64, r, k4, w4[n]);
-        tcs::st4(op3b, 64, r, 64 + k4, u4[n]);
+      for (int idx = tid; idx < 64 * 16; idx += 384) {
+        const int r = idx >> 4, k4 = (idx & 15) * 4;
+        const float4 w4 = *reinterpret_cast<const float4*>(a.W + bo + r * 64 + k4);
+        const float4 u4 = *reinterpret_cast<const float4*>(a.U + bo + r * 64 + k4);
+        tcs::st4(op3b, 64, r, k4, w4);
+        tcs::st4(op3b, 64, r, 64 + k4, u4);
       }
       // Kown^T: B[d][j] = k_jd e^{r_J(j),d - G_jd}
-      for (int idx = tid; idx < 64 * 64; idx += 128) {
+      for (int idx = tid; idx < 64 * 64; idx += 384) {
         const int jt = idx >> 6, d = idx & 63;
         tcs::st(op4b, 64, d, jt, qk.at(false, jt, d) * expf(sG[(jt & ~15) * LDP + d] - sG[jt * LDP + d]));
       }
@@ -431,43 +424,41 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
     tcs::mma_done(bar, phase, a.status, 12);
     KIMI_PHASE(6);
 
-    // ---------------------------------------------------------------- dL -> dA, dbeta, Y terms | Kown
+    // ---------------------------------------------------------------- dL -> dA, dbeta, Y terms | [Kq | Qq]
     if (row < 64) {
       const int i = ri;
-      float val[32], kv[32], vv[32];
-      tcs::tmem_row32(tm, warp, c0, val);
+      float val[16];
+      tcs::tmem_row16(tm, warp, c0, val);
       float part = 0.f;
+      const float bi = sBeta[i];
 #pragma unroll
-      for (int u = 0; u < 32; u += 4) {
+      for (int u = 0; u < 16; u += 4) {
         float da[4];
 #pragma unroll
         for (int w4 = 0; w4 < 4; ++w4) {
           const int j = c0 + u + w4;
           const float dl = j < i ? -val[u + w4] : 0.f;
           part += sAT[j * LDT + i] * dl;
-          da[w4] = sBeta[i] * dl;
+          da[w4] = bi * dl;
         }
         tcs::st4(op4a, 128, i, c0 + u, make_float4(da[0], da[1], da[2], da[3]));
       }
       // d(k e^G) = beta Y_K: dk += beta Y_K e^G, dG += beta Y_K k e^G; dbeta += k e^G . Y_K + v . Y_V
-      qk.row32(false, i, c0, kv);
-      load32<T>(v + i * rs + c0, vv);
-      const float bi = sBeta[i];
 #pragma unroll
-      for (int u = 0; u < 32; ++u) {
+      for (int u = 0; u < 16; ++u) {
         const int d = c0 + u;
         const float yk = tcs::ld(op3a, 64, i, d), yv = tcs::ld(op3a, 64, i, 64 + d);
         const float e = expf(sG[i * LDP + d]);
-        const float kg = kv[u] * e;
+        const float kg = qk.at(false, i, d) * e;
         gacc[u] += bi * yk * e;
         atomicAdd(&sDG[i * LDP + d], bi * yk * kg);
-        part += kg * yk + vv[u] * yv;
+        part += kg * yk + to_f<T>(v[i * rs + d]) * yv;
       }
       atomicAdd(&sDB[i], part);
     } else {
       // [Kq | Qq]^T: B[d][i] = k_id e^{G_id - r_I(i),d}, B[d][64 + i] = q_id e^{G_id - r_I(i),d}
-      const int t2 = (warp & 1) * 32 + half * 64 + (tid & 31);  // 0..127 over warps 2,3,6,7
-      for (int idx = t2; idx < 64 * 64; idx += 128) {
+      const int t2 = (warp & 1) * 32 + (warp >> 2) * 64 + lane;  // 0..255 over the warps of lanes 64..127
+      for (int idx = t2; idx < 64 * 64; idx += 256) {
         const int t = idx >> 6, d = idx & 63;
         const float e = expf(sG[t * LDP + d] - sG[(t & ~15) * LDP + d]);
         tcs::st(op5b, 64, d, t, qk.at(false, t, d) * e);
@@ -477,7 +468,7 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
     __syncthreads();
     KIMI_PHASE(7);
     // [dA^T | dP^T]
-    for (int idx = tid; idx < 64 * 64; idx += NTH) {
+    for (int idx = tid; idx < 64 * 64; idx += NTB) {
       const int i = idx >> 6, j = idx & 63;
       tcs::st(op5a, 64, j, i, tcs::ld(op4a, 128, i, j));
       tcs::st(op5a, 64, j, 64 + i, tcs::ld(op4a, 128, 64 + i, j));
@@ -502,77 +493,78 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_bwd_tc_kernel(const __grid_c
     {
       const bool is_p = row >= 64;
       const int i = ri, I = i >> 4;
-      float acc[32], val[32], xv[32];
+      float acc[16], val[16];
 #pragma unroll
-      for (int u = 0; u < 32; ++u) acc[u] = 0.f;
+      for (int u = 0; u < 16; ++u) acc[u] = 0.f;
 #pragma unroll
       for (int J = 0; J < 4; ++J) {
-        tcs::tmem_row32(tm + 64 * J, warp, c0, val);
+        tcs::tmem_row16(tm + 64 * J, warp, c0, val);
         if (J <= I) {
 #pragma unroll
-          for (int u = 0; u < 32; ++u) {
+          for (int u = 0; u < 16; ++u) {
             const int d = c0 + u;
             acc[u] += expf(sG[16 * I * LDP + d] - sG[16 * J * LDP + d]) * val[u];
           }
         }
       }
-      qk.row32(is_p, i, c0, xv);
 #pragma unroll
-      for (int u = 0; u < 32; ++u) {
+      for (int u = 0; u < 16; ++u) {
         const int d = c0 + u;
         const float e = expf(sG[i * LDP + d] - sG[16 * I * LDP + d]);
         gacc[u] += acc[u] * e;
-        atomicAdd(&sDG[i * LDP + d], acc[u] * xv[u] * e);
+        atomicAdd(&sDG[i * LDP + d], acc[u] * qk.at(is_p, i, d) * e);
       }
       // column side (lanes 0..63): dk_j += sum_I e^{r_I - G_j} gc_I, dG_j -= k_j (same)
       if (!is_p) {
         const int j = i;
-        float kv[32];
-        qk.row32(false, j, c0, kv);
 #pragma unroll
-        for (int u = 0; u < 32; ++u) acc[u] = 0.f;
+        for (int u = 0; u < 16; ++u) acc[u] = 0.f;
 #pragma unroll
         for (int I2 = 0; I2 < 4; ++I2) {
-          tcs::tmem_row32(tm + 256 + 64 * I2, warp, c0, val);
+          tcs::tmem_row16(tm + 256 + 64 * I2, warp, c0, val);
           if (j <= 16 * I2 + 15) {
 #pragma unroll
-            for (int u = 0; u < 32; ++u) {
+            for (int u = 0; u < 16; ++u) {
               const int d = c0 + u;
               acc[u] += val[u] * expf(sG[16 * I2 * LDP + d] - sG[j * LDP + d]);
             }
           }
         }
 #pragma unroll
-        for (int u = 0; u < 32; ++u) {
+        for (int u = 0; u < 16; ++u) {
           gacc[u] += acc[u];
-          atomicAdd(&sDG[j * LDP + c0 + u], -acc[u] * kv[u]);
+          atomicAdd(&sDG[j * LDP + c0 + u], -acc[u] * qk.at(false, j, c0 + u));
         }
       }
     }
     // dk / dq rows -> staging tile -> coalesced stores
 #pragma unroll
-    for (int u = 0; u < 32; ++u) stage[(row >= 64 ? C * LDP : 0) + ri * LDP + c0 + u] = gacc[u];
+    for (int u = 0; u < 16; ++u) stage[(row >= 64 ? C * LDP : 0) + ri * LDP + c0 + u] = gacc[u];
     __syncthreads();
     KIMI_PHASE(10);
     {
       float* dq = a.dq + tok0;
       float* dk = a.dk + tok0;
-      float* dg = a.dg + tok0;
-      for (int idx = tid; idx < C * 64; idx += NTH) {
+      for (int idx = tid; idx < C * 64; idx += NTB) {
         const int i = idx >> 6, d = idx & 63;
         dk[i * rs + d] = stage[i * LDP + d];
         dq[i * rs + d] = stage[C * LDP + i * LDP + d];
       }
-      if (tid < 64) {
-        float acc = sDGC[tid];
-        for (int i = C - 1; i >= 0; --i) {
-          acc += sDG[i * LDP + tid];
-          dg[i * rs + tid] = acc;
-        }
-      } else if (tid < 128) {
-        const int i = tid - 64;
-        a.dbeta[((int64_t)b * Tp + t0 + i) * H + h] = sDB[i];
+      // dg = reverse cumsum of dG (+ dG_C): eight 8-row segments per channel, then the offsets
+      const int d = tid & 63, part = tid >> 6;
+      float run = 0.f;
+#pragma unroll
+      for (int r = 7; r >= 0; --r) {
+        run += sDG[(8 * part + r) * LDP + d];
+        sDG[(8 * part + r) * LDP + d] = run;
       }
+      __syncthreads();
+      float off = sDGC[d];
+      for (int p2 = part + 1; p2 < 8; ++p2) off += sDG[(8 * p2) * LDP + d];
+      float* dg = a.dg + tok0;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) dg[(8 * part + r) * rs + d] = sDG[(8 * part + r) * LDP + d] + off;
+      if (tid < C) a.dbeta[((int64_t)b * Tp + t0 + tid) * H + h] = sDB[tid];
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -600,7 +592,7 @@ cudaError_t launch_bwd(const BwdArgs& args, cudaStream_t s) {
   const int total = args.B * args.H * args.NC;
   int sms = 148;
   const int grid = total < sms ? total : sms;
-  kda_intra_bwd_tc_kernel<T><<<grid, NTH, bwd_smem<T>(), s>>>(args);
+  kda_intra_bwd_tc_kernel<T><<<grid, NTB, bwd_smem<T>(), s>>>(args);
   return cudaGetLastError();
 }
 

@@ -76,6 +76,11 @@ KIMI_D void tmem_row32(uint32_t tmem_base, int warp, int col, float* v) {
   tc::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)col, v);
 }
 
+// Row `lane` of the accumulator at columns [col, col + 16).
+KIMI_D void tmem_row16(uint32_t tmem_base, int warp, int col, float* v) {
+  tc::tmem_ld_32x32b_x16(tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)col, v);
+}
+
 KIMI_D void bar_sync(int id, int threads) { asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(threads) : "memory"); }
 
 // Publish thread-written operand tiles to the tensor core and order earlier TMEM reads
