@@ -129,6 +129,13 @@ __global__ void attnres_bwd_kernel(SrcPtrs<T> src, int S, const float* __restric
   for (int64_t tok = (int64_t)blockIdx.x * wpb + (threadIdx.x >> 5); tok < tokens; tok += (int64_t)gridDim.x * wpb) {
     float p[kMaxSources], r[kMaxSources], dp[kMaxSources], a[kMaxSources];
     float pdp = 0.f;
+    // the output gradient row, read once for all sources and both passes
+    Vec<T> gv[MAXV];
+#pragma unroll
+    for (int v = 0; v < MAXV; ++v) {
+      const int vi = lane + v * 32;
+      if (vi < nvec) gv[v].load(dout + tok * dim + vi * VN);
+    }
     for (int s = 0; s < S; ++s) {
       p[s] = probs[tok * S + s];
       r[s] = rstd[tok * S + s];
@@ -138,12 +145,11 @@ __global__ void attnres_bwd_kernel(SrcPtrs<T> src, int S, const float* __restric
       for (int v = 0; v < MAXV; ++v) {
         const int vi = lane + v * 32;
         if (vi < nvec) {
-          Vec<T> x, g;
+          Vec<T> x;
           x.load(row + vi * VN);
-          g.load(dout + tok * dim + vi * VN);
 #pragma unroll
           for (int j = 0; j < VN; ++j) {
-            d0 += g.f(j) * x.f(j);
+            d0 += gv[v].f(j) * x.f(j);
             a0 += qw[v][j] * x.f(j);
           }
         }
@@ -161,13 +167,12 @@ __global__ void attnres_bwd_kernel(SrcPtrs<T> src, int S, const float* __restric
       for (int v = 0; v < MAXV; ++v) {
         const int vi = lane + v * 32;
         if (vi < nvec) {
-          Vec<T> x, g, o;
+          Vec<T> x, o;
           x.load(row + vi * VN);
-          g.load(dout + tok * dim + vi * VN);
 #pragma unroll
           for (int j = 0; j < VN; ++j) {
             const float xv = x.f(j);
-            o.set(j, p[s] * g.f(j) + dl * (r[s] * qw[v][j] - r3 * xv));
+            o.set(j, p[s] * gv[v].f(j) + dl * (r[s] * qw[v][j] - r3 * xv));
             acc[v][j] += dl * r[s] * xv;
           }
           o.store(drow + vi * VN);

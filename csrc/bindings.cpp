@@ -27,7 +27,18 @@ void check(cudaError_t e, const char* what) {
   TORCH_CHECK(e == cudaSuccess, what, " failed: ", cudaGetErrorString(e));
 }
 
-#define CHECK_CUDA_CONTIG(x) TORCH_CHECK((x).is_cuda() && (x).is_contiguous(), #x " must be a contiguous CUDA tensor")
+// Kernels read and write with 16-byte vector accesses and bulk copies: every tensor they take is
+// contiguous and starts on a 16-byte boundary (a misaligned view fails here, loudly).
+#define CHECK_CUDA_CONTIG(x)                                                                           \
+  TORCH_CHECK((x).is_cuda() && (x).is_contiguous() && (reinterpret_cast<uintptr_t>((x).data_ptr()) & 15) == 0, \
+              #x " must be a contiguous CUDA tensor starting on a 16-byte boundary")
+
+// A contiguous copy-if-needed of `t` that starts on a 16-byte boundary.
+at::Tensor dense(const at::Tensor& t) {
+  at::Tensor c = t.contiguous();
+  if (reinterpret_cast<uintptr_t>(c.data_ptr()) & 15) c = c.clone(at::MemoryFormat::Contiguous);
+  return c;
+}
 
 cudaStream_t stream() { return at::cuda::getCurrentCUDAStream(); }
 
@@ -42,7 +53,7 @@ std::vector<at::Tensor> rms_norm_fwd(at::Tensor x, at::Tensor w, double eps, int
   const float* wp = nullptr;
   at::Tensor wf;
   if (w.defined() && w.numel()) {
-    wf = w.to(at::kFloat).contiguous();
+    wf = dense(w.to(at::kFloat));
     wp = wf.data_ptr<float>();
   }
   check(kimi::rms_norm_fwd(dtype_code(x), x.data_ptr(), wp, y.data_ptr(), rstd.data_ptr<float>(), rows, dim,
@@ -53,7 +64,7 @@ std::vector<at::Tensor> rms_norm_fwd(at::Tensor x, at::Tensor w, double eps, int
 std::vector<at::Tensor> rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd, int64_t period,
                                      bool need_dw) {
   CHECK_CUDA_CONTIG(x);
-  dy = dy.contiguous();
+  dy = dense(dy);
   const at::cuda::CUDAGuard g(x.device());
   const int dim = x.size(-1);
   const int64_t rows = x.numel() / dim;
@@ -62,7 +73,7 @@ std::vector<at::Tensor> rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, 
   const float* wp = nullptr;
   float* dwp = nullptr;
   if (w.defined() && w.numel()) {
-    wf = w.to(at::kFloat).contiguous();
+    wf = dense(w.to(at::kFloat));
     wp = wf.data_ptr<float>();
     if (need_dw) {
       dw = at::zeros({wf.numel()}, x.options().dtype(at::kFloat));
@@ -86,7 +97,7 @@ at::Tensor situ_fwd(at::Tensor g, at::Tensor u, double bg, double bu) {
 }
 
 std::vector<at::Tensor> situ_bwd(at::Tensor dy, at::Tensor g, at::Tensor u, double bg, double bu) {
-  dy = dy.contiguous();
+  dy = dense(dy);
   const at::cuda::CUDAGuard gd(g.device());
   auto dg = at::empty_like(g), du = at::empty_like(u);
   check(kimi::situ_glu_bwd(dtype_code(g), dy.data_ptr(), g.data_ptr(), u.data_ptr(), dg.data_ptr(), du.data_ptr(),
@@ -105,7 +116,7 @@ at::Tensor sigmul_fwd(at::Tensor z, at::Tensor x) {
 }
 
 std::vector<at::Tensor> sigmul_bwd(at::Tensor dy, at::Tensor z, at::Tensor x) {
-  dy = dy.contiguous();
+  dy = dense(dy);
   const at::cuda::CUDAGuard gd(z.device());
   auto dz = at::empty_like(z), dx = at::empty_like(x);
   check(kimi::sigmoid_mul_bwd(dtype_code(x), dy.data_ptr(), z.data_ptr(), x.data_ptr(), dz.data_ptr(), dx.data_ptr(),
@@ -119,19 +130,19 @@ at::Tensor decay_fwd(at::Tensor z, at::Tensor a_log, double g_min, double ceps) 
   const int heads = z.size(-2), kdim = z.size(-1);
   const int64_t rows = z.numel() / (heads * kdim);
   auto g = at::empty(z.sizes(), z.options().dtype(at::kFloat));
-  auto af = a_log.to(at::kFloat).contiguous();
+  auto af = dense(a_log.to(at::kFloat));
   check(kimi::kda_decay_fwd(dtype_code(z), z.data_ptr(), af.data_ptr<float>(), g.data_ptr<float>(), rows, heads, kdim,
                             (float)g_min, (float)ceps, stream()), "kda_decay_fwd");
   return g;
 }
 
 std::vector<at::Tensor> decay_bwd(at::Tensor dg, at::Tensor z, at::Tensor a_log, double g_min, double ceps) {
-  dg = dg.to(at::kFloat).contiguous();
+  dg = dense(dg.to(at::kFloat));
   const at::cuda::CUDAGuard gd(z.device());
   const int heads = z.size(-2), kdim = z.size(-1);
   const int64_t rows = z.numel() / (heads * kdim);
   auto dz = at::empty_like(z);
-  auto af = a_log.to(at::kFloat).contiguous();
+  auto af = dense(a_log.to(at::kFloat));
   auto da = at::zeros({heads}, z.options().dtype(at::kFloat));
   check(kimi::kda_decay_bwd(dtype_code(z), dg.data_ptr<float>(), z.data_ptr(), af.data_ptr<float>(), dz.data_ptr(),
                             da.data_ptr<float>(), rows, heads, kdim, (float)g_min, (float)ceps, stream()),
@@ -140,9 +151,10 @@ std::vector<at::Tensor> decay_bwd(at::Tensor dg, at::Tensor z, at::Tensor a_log,
 }
 
 at::Tensor conv_fwd(at::Tensor x, at::Tensor w, int64_t head_dim, double eps, bool normalize) {
+  x = dense(x);
   CHECK_CUDA_CONTIG(x);
   const at::cuda::CUDAGuard gd(x.device());
-  auto wf = w.to(at::kFloat).contiguous();
+  auto wf = dense(w.to(at::kFloat));
   auto y = at::empty_like(x);
   check(kimi::conv_silu_norm_fwd(dtype_code(x), x.data_ptr(), wf.data_ptr<float>(), y.data_ptr(), x.size(0),
                                  x.size(1), x.size(2), wf.size(1), (int)head_dim, (float)eps, normalize, stream()),
@@ -152,9 +164,10 @@ at::Tensor conv_fwd(at::Tensor x, at::Tensor w, int64_t head_dim, double eps, bo
 
 std::vector<at::Tensor> conv_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, int64_t head_dim, double eps,
                                  bool normalize) {
-  dy = dy.contiguous();
+  dy = dense(dy);
+  x = dense(x);  // the forward's input as autograd saved it: possibly a misaligned view
   const at::cuda::CUDAGuard gd(x.device());
-  auto wf = w.to(at::kFloat).contiguous();
+  auto wf = dense(w.to(at::kFloat));
   auto dx = at::empty_like(x);
   auto dw = at::empty(wf.sizes(), wf.options());
   auto part = at::empty({kimi::conv_bwd_partial_rows(x.size(0), x.size(1)), wf.numel()}, wf.options());
@@ -181,7 +194,7 @@ std::vector<at::Tensor> attnres_fwd(std::vector<at::Tensor> sources, at::Tensor 
   auto out = at::empty_like(s0);
   auto probs = at::empty({tokens, S}, s0.options().dtype(at::kFloat));
   auto rstd = at::empty({tokens, S}, s0.options().dtype(at::kFloat));
-  auto qf = q.to(at::kFloat).contiguous(), wf = w.to(at::kFloat).contiguous();
+  auto qf = dense(q.to(at::kFloat)), wf = dense(w.to(at::kFloat));
   check(kimi::attnres_mix_fwd(dtype_code(s0), ptrs.data(), S, qf.data_ptr<float>(), wf.data_ptr<float>(),
                               out.data_ptr(), probs.data_ptr<float>(), rstd.data_ptr<float>(), tokens, dim,
                               (float)eps, stream()), "attnres_mix_fwd");
@@ -192,7 +205,7 @@ std::vector<at::Tensor> attnres_bwd(std::vector<at::Tensor> sources, at::Tensor 
                                     at::Tensor probs, at::Tensor rstd) {
   const auto& s0 = sources.at(0);
   const at::cuda::CUDAGuard gd(s0.device());
-  dout = dout.contiguous();
+  dout = dense(dout);
   std::vector<const void*> ptrs;
   std::vector<void*> dptrs;
   std::vector<at::Tensor> grads;
@@ -203,7 +216,7 @@ std::vector<at::Tensor> attnres_bwd(std::vector<at::Tensor> sources, at::Tensor 
   }
   const int dim = s0.size(-1);
   const int64_t tokens = s0.numel() / dim;
-  auto qf = q.to(at::kFloat).contiguous(), wf = w.to(at::kFloat).contiguous();
+  auto qf = dense(q.to(at::kFloat)), wf = dense(w.to(at::kFloat));
   auto dq = at::zeros({dim}, s0.options().dtype(at::kFloat));
   auto dw = at::zeros({dim}, s0.options().dtype(at::kFloat));
   check(kimi::attnres_mix_bwd(dtype_code(s0), ptrs.data(), (int)sources.size(), qf.data_ptr<float>(),
@@ -221,8 +234,8 @@ at::Tensor ce_rows(at::Tensor logits, int64_t vocab, at::Tensor targets, at::Ten
   const at::cuda::CUDAGuard gd(logits.device());
   const int64_t rows = logits.size(0);
   auto loss = at::empty({rows}, logits.options().dtype(at::kFloat));
-  auto t = targets.to(at::kLong).contiguous();
-  auto v = valid.to(at::kBool).contiguous();
+  auto t = dense(targets.to(at::kLong));
+  auto v = dense(valid.to(at::kBool));
   check(kimi::ce_rows_fwd_bwd(dtype_code(logits), logits.data_ptr(), logits.stride(0), rows, (int)vocab,
                               t.data_ptr<int64_t>(), v.data_ptr<bool>(), loss.data_ptr<float>(), (float)grad_scale,
                               stream()), "ce_rows_fwd_bwd");
@@ -242,7 +255,7 @@ std::vector<at::Tensor> router(at::Tensor logits, at::Tensor bias, int64_t k, bo
   auto cutoff = at::empty({rows}, f);
   auto load = at::zeros({experts}, logits.options().dtype(at::kLong));
   at::Tensor raw = return_raw ? at::empty({rows, experts}, f) : at::Tensor();
-  auto bf = bias.to(at::kFloat).contiguous();
+  auto bf = dense(bias.to(at::kFloat));
   check(kimi::router_topk(dtype_code(logits), logits.data_ptr(), bf.data_ptr<float>(), rows, experts, (int)k,
                           need_cutoff, (float)eps, sel.data_ptr<int64_t>(), raw_sel.data_ptr<float>(),
                           weights.data_ptr<float>(), cutoff.data_ptr<float>(), load.data_ptr<int64_t>(),
@@ -272,7 +285,7 @@ std::vector<at::Tensor> kda_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Te
   auto o = at::empty_like(v);
   at::Tensor ht = want_final ? at::empty({B, H, 64, 64}, f) : at::Tensor();
   at::Tensor h0c;
-  if (h0.has_value() && h0->defined()) h0c = h0->to(at::kFloat).contiguous();
+  if (h0.has_value() && h0->defined()) h0c = dense(h0->to(at::kFloat));
   kimi::KdaBuffers buf{W.data_ptr<float>(), U.data_ptr<float>(), P.data_ptr<float>(), Qg.data_ptr<float>(),
                        Kend.data_ptr<float>(), eGC.data_ptr<float>(), states.data_ptr<float>(), Vp.data_ptr<float>(),
                        Araw.data_ptr<float>()};
@@ -286,7 +299,7 @@ std::vector<at::Tensor> kda_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Te
                                 std::vector<at::Tensor> saved, at::Tensor dout, c10::optional<at::Tensor> dht,
                                 bool want_dh0) {
   const at::cuda::CUDAGuard gd(q.device());
-  dout = dout.contiguous();
+  dout = dense(dout);
   const int B = q.size(0), Tp = q.size(1), H = q.size(2);
   auto f = q.options().dtype(at::kFloat);
   auto& W = saved.at(0);
@@ -298,7 +311,7 @@ std::vector<at::Tensor> kda_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Te
        dg = at::empty(g.sizes(), f), dbeta = at::empty(beta.sizes(), f);
   at::Tensor dh0 = want_dh0 ? at::empty({B, H, 64, 64}, f) : at::Tensor();
   at::Tensor dhtc;
-  if (dht.has_value() && dht->defined()) dhtc = dht->to(at::kFloat).contiguous();
+  if (dht.has_value() && dht->defined()) dhtc = dense(dht->to(at::kFloat));
   check(kimi::kda_chunk_bwd(dtype_code(q), q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr<float>(),
                             beta.data_ptr<float>(), buf, dout.data_ptr(),
                             dhtc.defined() ? dhtc.data_ptr<float>() : nullptr, dVp.data_ptr<float>(),
@@ -378,7 +391,7 @@ std::vector<at::Tensor> fa_fwd(at::Tensor q, at::Tensor k, at::Tensor v, bool ca
   auto o = at::empty({B, tq, H, v.size(3)}, q.options());
   auto lse = at::empty({B, H, tq}, q.options().dtype(at::kFloat));
   at::Tensor kl;
-  if (key_lengths.has_value() && key_lengths->defined()) kl = key_lengths->to(at::kInt).contiguous();
+  if (key_lengths.has_value() && key_lengths->defined()) kl = dense(key_lengths->to(at::kInt));
   check(kimi::flash_attn_fwd(dtype_code(q), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
                              lse.data_ptr<float>(), B, tq, tk, H, q.size(3), v.size(3), causal,
                              kl.defined() ? kl.data_ptr<int>() : nullptr, (float)scale, stream()), "flash_attn_fwd");
@@ -388,13 +401,13 @@ std::vector<at::Tensor> fa_fwd(at::Tensor q, at::Tensor k, at::Tensor v, bool ca
 std::vector<at::Tensor> fa_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor dout, at::Tensor lse,
                                bool causal, c10::optional<at::Tensor> key_lengths, double scale) {
   const at::cuda::CUDAGuard gd(q.device());
-  dout = dout.contiguous();
+  dout = dense(dout);
   const int B = q.size(0), tq = q.size(1), H = q.size(2), tk = k.size(1);
   auto dq = at::zeros(q.sizes(), q.options().dtype(at::kFloat));
   auto dk = at::empty_like(k), dv = at::empty_like(v);
   auto delta = at::empty({B, H, tq}, q.options().dtype(at::kFloat));
   at::Tensor kl;
-  if (key_lengths.has_value() && key_lengths->defined()) kl = key_lengths->to(at::kInt).contiguous();
+  if (key_lengths.has_value() && key_lengths->defined()) kl = dense(key_lengths->to(at::kInt));
   check(kimi::flash_attn_bwd(dtype_code(q), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), dout.data_ptr(),
                              lse.data_ptr<float>(), dq.data_ptr<float>(), dk.data_ptr(), dv.data_ptr(),
                              delta.data_ptr<float>(), B, tq, tk, H, q.size(3), v.size(3), causal,
@@ -550,7 +563,7 @@ std::vector<at::Tensor> tc_gemm_grouped(int64_t mode, at::Tensor a, at::Tensor b
   g.b = b.data_ptr();
   at::Tensor b2t;
   if (b2.has_value() && b2->defined()) {
-    b2t = b2->contiguous();
+    b2t = dense(*b2);
     g.b2 = b2t.data_ptr();
   }
   if (b.dim() == 3) {
@@ -599,8 +612,8 @@ std::vector<at::Tensor> tc_gemm_grouped(int64_t mode, at::Tensor a, at::Tensor b
   }
   at::Tensor rt, rw;
   if (epi == 2) {
-    rt = row_token->contiguous();
-    rw = row_weight->to(at::kFloat).contiguous();
+    rt = dense(*row_token);
+    rw = dense(row_weight->to(at::kFloat));
     g.row_token = rt.data_ptr<int>();
     g.row_weight = rw.data_ptr<float>();
     g.ldc = out.size(-1);
@@ -620,7 +633,7 @@ std::vector<at::Tensor> moe_route(at::Tensor sel, at::Tensor w, int64_t E, int64
   const at::cuda::CUDAGuard gd(sel.device());
   auto i32 = sel.options().dtype(at::kInt);
   const int64_t M = sel.size(0), k = sel.size(1);
-  auto wf = w.to(at::kFloat).contiguous();
+  auto wf = dense(w.to(at::kFloat));
   auto counts = at::empty({E}, i32), offsets = at::empty({E + 1}, i32), cursor = at::empty({E}, i32);
   auto row_token = at::empty({r_max}, i32), row_of = at::empty({M * k}, i32);
   auto row_weight = at::zeros({r_max}, sel.options().dtype(at::kFloat));
@@ -642,7 +655,7 @@ at::Tensor moe_gather(at::Tensor latent, at::Tensor row_token) {
 
 std::vector<at::Tensor> moe_dy(at::Tensor dagg, at::Tensor row_token, at::Tensor row_weight, at::Tensor y) {
   const at::cuda::CUDAGuard gd(y.device());
-  dagg = dagg.to(at::kFloat).contiguous();
+  dagg = dense(dagg.to(at::kFloat));
   auto dy = at::empty_like(y);
   auto dw_row = at::empty({y.size(0)}, y.options().dtype(at::kFloat));
   check(kimi::moe_dy(dagg.data_ptr<float>(), row_token.data_ptr<int>(), row_weight.data_ptr<float>(), y.data_ptr(),
@@ -660,7 +673,7 @@ at::Tensor moe_slot_sum(at::Tensor dxs, at::Tensor row_of, int64_t M, int64_t k,
 
 at::Tensor situ_bwd_cat(at::Tensor dh, at::Tensor g, at::Tensor u, double bg, double bu) {
   const at::cuda::CUDAGuard gd(g.device());
-  dh = dh.contiguous();
+  dh = dense(dh);
   auto dgu = at::empty({g.size(0), 2 * g.size(1)}, g.options());
   check(kimi::situ_bwd_cat(dh.data_ptr(), g.data_ptr(), u.data_ptr(), dgu.data_ptr(), g.size(0), g.size(1),
                            (float)bg, (float)bu, stream()), "situ_bwd_cat");

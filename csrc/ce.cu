@@ -3,8 +3,14 @@
 // the logits buffer is overwritten in place with d(loss)/d(logits) * grad_scale
 // = (softmax - onehot) * grad_scale (zero for invalid rows). The caller then runs the two
 // backward GEMMs on that buffer, so the fp32 [N,V] probability tensor never exists.
+//
+// 16-bit rows up to 96K entries take the staged path: one persistent CTA per SM double-buffers
+// whole rows in shared memory with a TMA bulk copy (cp.async.bulk global -> shared, completion on
+// an mbarrier; no multicast), so the max / sum / gradient passes read shared memory and HBM sees
+// each logit read once and written once.  Other rows use the two-pass kernel below.
 #include "common.cuh"
 #include "kernels.h"
+#include "tc_common.cuh"
 
 namespace kimi {
 namespace {
@@ -77,10 +83,122 @@ __global__ void ce_rows_kernel(T* __restrict__ logits, int64_t ld, int64_t rows,
   }
 }
 
+constexpr int kStagedThreads = 512;
+constexpr int kMaxStagedBytes = 100 * 1024;  // per buffer; two buffers per CTA
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                   tc::smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(tc::smem_u32(bar))
+               : "memory");
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kStagedThreads, 1) ce_rows_staged_kernel(T* __restrict__ logits, int64_t ld,
+                                                                           int64_t rows, int vocab,
+                                                                           const int64_t* __restrict__ targets,
+                                                                           const bool* __restrict__ valid,
+                                                                           float* __restrict__ loss_rows,
+                                                                           float grad_scale, uint32_t row_bytes) {
+  extern __shared__ __align__(128) uint8_t sbuf[];
+  __shared__ uint64_t bars[2];
+  __shared__ float scratch[32];
+  constexpr int VN = Vec<T>::N;
+  T* buf[2] = {reinterpret_cast<T*>(sbuf), reinterpret_cast<T*>(sbuf + row_bytes)};
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    tc::mbar_init(&bars[0], 1);
+    tc::mbar_init(&bars[1], 1);
+    tc::fence_barrier_init();
+  }
+  __syncthreads();
+  int64_t row = blockIdx.x;
+  if (tid == 0 && row < rows) {
+    tc::mbar_arrive_expect_tx(&bars[0], row_bytes);
+    bulk_g2s(buf[0], logits + row * ld, row_bytes, &bars[0]);
+  }
+  const int nv = vocab / VN;
+  for (int it = 0; row < rows; row += gridDim.x, ++it) {
+    const int b = it & 1;
+    const int64_t next = row + gridDim.x;
+    if (tid == 0 && next < rows) {  // the other buffer was released by the barrier ending the last row
+      tc::fence_proxy_async();
+      tc::mbar_arrive_expect_tx(&bars[b ^ 1], row_bytes);
+      bulk_g2s(buf[b ^ 1], logits + next * ld, row_bytes, &bars[b ^ 1]);
+    }
+    tc::mbar_wait(&bars[b], (uint32_t)((it >> 1) & 1), nullptr, 0);
+    const T* sr = buf[b];
+    float m = -INFINITY;
+    for (int i = tid; i < nv; i += kStagedThreads) {
+      Vec<T> a;
+      a.load(sr + i * VN);
+#pragma unroll
+      for (int j = 0; j < VN; ++j) m = fmaxf(m, a.f(j));
+    }
+    for (int i = nv * VN + tid; i < vocab; i += kStagedThreads) m = fmaxf(m, to_f<T>(sr[i]));
+    const float gm = block_max(m, scratch);
+    float se = 0.f;
+    for (int i = tid; i < nv; i += kStagedThreads) {
+      Vec<T> a;
+      a.load(sr + i * VN);
+#pragma unroll
+      for (int j = 0; j < VN; ++j) se += expf(a.f(j) - gm);
+    }
+    for (int i = nv * VN + tid; i < vocab; i += kStagedThreads) se += expf(to_f<T>(sr[i]) - gm);
+    const float lse = gm + logf(block_sum(se, scratch));
+    const bool ok = valid == nullptr || valid[row];
+    const int64_t tgt = ok ? targets[row] : -1;
+    if (tid == 0) loss_rows[row] = (ok && tgt >= 0 && tgt < vocab) ? lse - to_f<T>(sr[tgt]) : 0.f;
+    const float sc = ok ? grad_scale : 0.f;
+    T* gr = logits + row * ld;
+    for (int i = tid; i < nv; i += kStagedThreads) {
+      Vec<T> a;
+      a.load(sr + i * VN);
+#pragma unroll
+      for (int j = 0; j < VN; ++j) {
+        const int64_t col = (int64_t)i * VN + j;
+        a.set(j, sc * (expf(a.f(j) - lse) - (col == tgt ? 1.f : 0.f)));
+      }
+      a.store(gr + i * VN);
+    }
+    for (int i = nv * VN + tid; i < vocab; i += kStagedThreads)
+      gr[i] = from_f<T>(sc * (expf(to_f<T>(sr[i]) - lse) - (i == tgt ? 1.f : 0.f)));
+    __syncthreads();  // every thread is done with buf[b] before it is refilled two rows later
+  }
+}
+
 }  // namespace
 
 cudaError_t ce_rows_fwd_bwd(int dtype, void* logits, int64_t ld, int64_t rows, int vocab, const int64_t* targets,
                             const bool* valid, float* loss_rows, float grad_scale, cudaStream_t s) {
+  if (dtype == 1 || dtype == 2) {
+    const uint32_t row_bytes = (uint32_t)(((int64_t)vocab * 2 + 15) / 16 * 16);
+    const bool aligned = (reinterpret_cast<uintptr_t>(logits) & 15) == 0 && (ld * 2) % 16 == 0 &&
+                         (int64_t)row_bytes <= ld * 2;
+    if (aligned && row_bytes <= (uint32_t)kMaxStagedBytes && rows > 0) {
+      const size_t smem = 2 * (size_t)row_bytes;
+      const int grid = (int)(rows < 148 ? rows : 148);
+      static bool configured[2] = {false, false};
+      if (!configured[dtype - 1]) {  // the attribute covers the largest staged row
+        const cudaError_t e = dtype == 1 ? cudaFuncSetAttribute(ce_rows_staged_kernel<__nv_bfloat16>,
+                                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                                2 * kMaxStagedBytes)
+                                         : cudaFuncSetAttribute(ce_rows_staged_kernel<__half>,
+                                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                                2 * kMaxStagedBytes);
+        if (e != cudaSuccess) return e;
+        configured[dtype - 1] = true;
+      }
+      if (dtype == 1) {
+        ce_rows_staged_kernel<__nv_bfloat16><<<grid, kStagedThreads, smem, s>>>(
+            (__nv_bfloat16*)logits, ld, rows, vocab, targets, valid, loss_rows, grad_scale, row_bytes);
+      } else {
+        ce_rows_staged_kernel<__half><<<grid, kStagedThreads, smem, s>>>((__half*)logits, ld, rows, vocab, targets,
+                                                                        valid, loss_rows, grad_scale, row_bytes);
+      }
+      return cudaGetLastError();
+    }
+  }
   int64_t grid = rows < 148 * 8 ? rows : 148 * 8;
   if (grid < 1) grid = 1;
   switch (dtype) {

@@ -19,6 +19,7 @@
 // `src/kda/projections.py:188-200` (reference).
 #include "common.cuh"
 #include "kernels.h"
+#include "tc_common.cuh"
 
 namespace kimi {
 namespace {
@@ -75,16 +76,12 @@ __global__ void __launch_bounds__(256) conv_fwd_v_kernel(const T* __restrict__ x
 #pragma unroll
       for (int e = 0; e < 8; ++e) hist[j][e] = 0.f;
   }
-  float xnext[8];  // the next token's x, loaded one step ahead
-  if (active && t0 < t1)
-    load8<T>(x + (rowbase + t0) * channels + c0, xnext);
-  else
-#pragma unroll
-    for (int e = 0; e < 8; ++e) xnext[e] = 0.f;
   for (int t = t0; t < t1; ++t) {
+    if (active)
+      load8<T>(x + (rowbase + t) * channels + c0, hist[0]);
+    else
 #pragma unroll
-    for (int e = 0; e < 8; ++e) hist[0][e] = xnext[e];
-    if (active && t + 1 < t1) load8<T>(x + (rowbase + t + 1) * channels + c0, xnext);
+      for (int e = 0; e < 8; ++e) hist[0][e] = 0.f;
     float s[8], ss = 0.f;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
@@ -140,23 +137,13 @@ __global__ void __launch_bounds__(256) conv_bwd_v_kernel(const T* __restrict__ d
 #pragma unroll
     for (int e = 0; e < 8; ++e) dph[j][e] = 0.f;
   }
-  float dnext[8], xnext[8];  // dy[t] and x[t - K] of the next step, loaded one step ahead
-  if (active)
-    load8<T>(dy + (rowbase + tstart) * channels + c0, dnext);
-  else
-#pragma unroll
-    for (int e = 0; e < 8; ++e) dnext[e] = 0.f;
   for (int t = tstart; t >= t0; --t) {
     float d[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) d[e] = dnext[e];
-    if (active && t - 1 >= t0) load8<T>(dy + (rowbase + t - 1) * channels + c0, dnext);
-    const int tn = t - K;
-    if (active && tn >= 0)
-      load8<T>(x + (rowbase + tn) * channels + c0, xnext);
+    if (active)
+      load8<T>(dy + (rowbase + t) * channels + c0, d);
     else
 #pragma unroll
-      for (int e = 0; e < 8; ++e) xnext[e] = 0.f;
+      for (int e = 0; e < 8; ++e) d[e] = 0.f;
     float pre[8], s[8], ss = 0.f, dot = 0.f;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
@@ -208,8 +195,12 @@ __global__ void __launch_bounds__(256) conv_bwd_v_kernel(const T* __restrict__ d
     for (int j = 0; j < K - 1; ++j)
 #pragma unroll
       for (int e = 0; e < 8; ++e) xw[j][e] = xw[j + 1][e];
+    const int tn = t - K;
+    if (active && tn >= 0)
+      load8<T>(x + (rowbase + tn) * channels + c0, xw[K - 1]);
+    else
 #pragma unroll
-    for (int e = 0; e < 8; ++e) xw[K - 1][e] = xnext[e];
+      for (int e = 0; e < 8; ++e) xw[K - 1][e] = 0.f;
   }
   // this block's dw partial: row (blockIdx.y, blockIdx.x) of the [blocks, C * K] scratch
   if (active) {
@@ -243,6 +234,202 @@ __global__ void __launch_bounds__(256) dw_reduce_kernel(const float* __restrict_
   }
 }
 
+// ---------------------------------------------------------------- shared-memory staged variants
+// The block's token rows (and their K - 1 halo rows) are contiguous in [B, T, C]: one TMA bulk
+// copy per tensor brings them into shared memory (mbarrier completion), then each thread walks
+// its 8 channels over the tile reading shared memory, so DRAM latency is paid once per block.
+constexpr int kSTile = 32;
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                   tc::smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(tc::smem_u32(bar))
+               : "memory");
+}
+
+// Rows [r0, r1) of one batch: zero the rows outside the sequence (generic stores to addresses the
+// bulk copy does not touch) and return the byte count of the rows inside it.
+template <typename T>
+__device__ uint32_t zero_outside(T* dst, int r0, int r1, int tokens, int channels) {
+  for (int r = r0; r < r1; ++r) {
+    if (r >= 0 && r < tokens) continue;
+    T* row = dst + (int64_t)(r - r0) * channels;
+    for (int c = threadIdx.x; c < channels; c += blockDim.x) row[c] = from_f<T>(0.f);
+  }
+  const int v0 = max(r0, 0), v1 = min(r1, tokens);
+  return v1 > v0 ? (uint32_t)((int64_t)(v1 - v0) * channels * sizeof(T)) : 0u;
+}
+template <typename T>
+__device__ void copy_inside(T* dst, const T* src_batch, int r0, int r1, int tokens, int channels, uint64_t* bar) {
+  const int v0 = max(r0, 0), v1 = min(r1, tokens);
+  if (v1 > v0)
+    bulk_g2s(dst + (int64_t)(v0 - r0) * channels, src_batch + (int64_t)v0 * channels,
+             (uint32_t)((int64_t)(v1 - v0) * channels * sizeof(T)), bar);
+}
+
+template <typename T, int K>
+__global__ void __launch_bounds__(256) conv_fwd_s_kernel(const T* __restrict__ x, const float* __restrict__ w,
+                                                         T* __restrict__ y, int tokens, int channels, int head_lanes,
+                                                         float eps, bool normalize) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint64_t bar;
+  T* sx = reinterpret_cast<T*>(smem);
+  const int ch = threadIdx.x;
+  const bool active = ch * 8 < channels;
+  const int c0 = active ? ch * 8 : 0;
+  const int b = blockIdx.y, t0 = blockIdx.x * kSTile, t1 = min(t0 + kSTile, tokens);
+  const int r0 = t0 - (K - 1);
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar, 1);
+    tc::fence_barrier_init();
+  }
+  __syncthreads();
+  const uint32_t bytes = zero_outside<T>(sx, r0, t1, tokens, channels);
+  if (threadIdx.x == 0) {
+    tc::mbar_arrive_expect_tx(&bar, bytes);
+    copy_inside<T>(sx, x + (int64_t)b * tokens * channels, r0, t1, tokens, channels, &bar);
+  }
+  float wr[8][K];
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+#pragma unroll
+    for (int j = 0; j < K; ++j) wr[e][j] = active ? w[(c0 + e) * K + j] : 0.f;
+  __syncthreads();  // zero rows written
+  tc::mbar_wait(&bar, 0, nullptr, 0);
+  const int64_t rowbase = (int64_t)b * tokens;
+  for (int t = t0; t < t1; ++t) {
+    float s[8], ss = 0.f;
+    float xv[K][8];
+#pragma unroll
+    for (int j = 0; j < K; ++j) load8<T>(sx + (int64_t)(t - j - r0) * channels + c0, xv[j]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float pre = 0.f;
+#pragma unroll
+      for (int j = 0; j < K; ++j) pre += wr[e][j] * xv[j][e];
+      s[e] = siluf_(pre);
+      ss += s[e] * s[e];
+    }
+    if (normalize) {
+      ss = group_sum(ss, head_lanes);
+      const float inv = 1.f / fmaxf(sqrtf(ss), eps);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s[e] *= inv;
+    }
+    if (active) store8<T>(y + (rowbase + t) * channels + c0, s);
+  }
+}
+
+template <typename T, int K>
+__global__ void __launch_bounds__(256) conv_bwd_s_kernel(const T* __restrict__ dy, const T* __restrict__ x,
+                                                         const float* __restrict__ w, T* __restrict__ dx,
+                                                         float* __restrict__ dw, int tokens, int channels,
+                                                         int head_lanes, float eps, bool normalize) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint64_t bar;
+  const int ch = threadIdx.x;
+  const bool active = ch * 8 < channels;
+  const int c0 = active ? ch * 8 : 0;
+  const int b = blockIdx.y, t0 = blockIdx.x * kSTile, t1 = min(t0 + kSTile, tokens);
+  const int tstart = min(t1 + K - 2, tokens - 1);
+  const int xr0 = t0 - (K - 1), xr1 = tstart + 1;  // x rows needed
+  const int dr0 = t0, dr1 = tstart + 1;            // dy rows needed
+  T* sx = reinterpret_cast<T*>(smem);
+  T* sd = sx + (int64_t)(kSTile + 2 * K - 2) * channels;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar, 1);
+    tc::fence_barrier_init();
+  }
+  __syncthreads();
+  const uint32_t bytes = zero_outside<T>(sx, xr0, xr1, tokens, channels) + zero_outside<T>(sd, dr0, dr1, tokens, channels);
+  if (threadIdx.x == 0) {
+    tc::mbar_arrive_expect_tx(&bar, bytes);
+    copy_inside<T>(sx, x + (int64_t)b * tokens * channels, xr0, xr1, tokens, channels, &bar);
+    copy_inside<T>(sd, dy + (int64_t)b * tokens * channels, dr0, dr1, tokens, channels, &bar);
+  }
+  float wr[8][K], dwacc[8][K];
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      wr[e][j] = active ? w[(c0 + e) * K + j] : 0.f;
+      dwacc[e][j] = 0.f;
+    }
+  __syncthreads();
+  tc::mbar_wait(&bar, 0, nullptr, 0);
+  const int64_t rowbase = (int64_t)b * tokens;
+  float dph[K][8];  // dph[j] = dpre[t + j]; slot 0 is this step's
+#pragma unroll
+  for (int j = 0; j < K; ++j)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) dph[j][e] = 0.f;
+  for (int t = tstart; t >= t0; --t) {
+    float d[8], xw[K][8];
+    load8<T>(sd + (int64_t)(t - dr0) * channels + c0, d);
+#pragma unroll
+    for (int j = 0; j < K; ++j) load8<T>(sx + (int64_t)(t - j - xr0) * channels + c0, xw[j]);
+    float pre[8], s[8], ss = 0.f, dot = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float p = 0.f;
+#pragma unroll
+      for (int j = 0; j < K; ++j) p += wr[e][j] * xw[j][e];
+      pre[e] = p;
+      s[e] = siluf_(p);
+      ss += s[e] * s[e];
+      dot += s[e] * d[e];
+    }
+    float inv = 1.f, coef = 0.f;
+    if (normalize) {
+      ss = group_sum(ss, head_lanes);
+      dot = group_sum(dot, head_lanes);
+      const float n = sqrtf(ss);
+      if (n > eps) {
+        inv = 1.f / n;
+        coef = dot * inv * inv * inv;
+      } else {
+        inv = 1.f / eps;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float ds = d[e] * inv - s[e] * coef;
+      const float sg = sigmoidf_(pre[e]);
+      dph[0][e] = ds * sg * (1.f + pre[e] * (1.f - sg));
+    }
+    if (t < t1) {
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < K; ++j) acc += wr[e][j] * dph[j][e];
+        o[e] = acc;
+#pragma unroll
+        for (int j = 0; j < K; ++j) dwacc[e][j] += dph[0][e] * xw[j][e];
+      }
+      if (active) store8<T>(dx + (rowbase + t) * channels + c0, o);
+    }
+#pragma unroll
+    for (int j = K - 1; j > 0; --j)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) dph[j][e] = dph[j - 1][e];
+  }
+  if (active) {
+    float* part = dw + ((int64_t)blockIdx.y * gridDim.x + blockIdx.x) * channels * K;
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+#pragma unroll
+      for (int j = 0; j < K; ++j) part[(c0 + e) * K + j] = dwacc[e][j];
+  }
+}
+
+size_t conv_fwd_s_smem(int channels, int ksize, size_t es) { return (size_t)(kSTile + ksize - 1) * channels * es; }
+size_t conv_bwd_s_smem(int channels, int ksize, size_t es) {
+  return (size_t)((kSTile + 2 * ksize - 2) + (kSTile + ksize - 1)) * channels * es;
+}
+constexpr size_t kConvSmemCap = 200 * 1024;
+
 template <typename T>
 cudaError_t launch_conv(bool fwd, const void* dy, const void* x, const float* w, void* out, float* dw_part, int batch,
                         int tokens, int channels, int ksize, int head_dim, float eps, bool normalize,
@@ -252,16 +439,39 @@ cudaError_t launch_conv(bool fwd, const void* dy, const void* x, const float* w,
     return cudaErrorInvalidValue;
   const int threads = ((channels / 8 + 31) / 32) * 32;
   if (threads > 256) return cudaErrorInvalidValue;
-  const dim3 grid((tokens + kTile - 1) / kTile, batch);
+  // 16-byte vector accesses and bulk copies of whole rows (channels % 64 == 0 keeps every row
+  // offset aligned once the base pointers are)
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dy) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return cudaErrorInvalidValue;
+  const bool staged = (fwd ? conv_fwd_s_smem(channels, ksize, sizeof(T))
+                           : conv_bwd_s_smem(channels, ksize, sizeof(T))) <= kConvSmemCap;
+  const int tile = staged ? kSTile : kTile;
+  const dim3 grid((tokens + tile - 1) / tile, batch);
   const int hl = head_dim / 8;
+  const size_t ssm = fwd ? conv_fwd_s_smem(channels, ksize, sizeof(T)) : conv_bwd_s_smem(channels, ksize, sizeof(T));
 #define KIMI_CONV_CASE(KK)                                                                                          \
   case KK:                                                                                                          \
-    if (fwd)                                                                                                        \
+    if (staged) {                                                                                                   \
+      if (ssm > 48 * 1024) {                                                                                        \
+        cudaError_t e = fwd ? cudaFuncSetAttribute(conv_fwd_s_kernel<T, KK>,                                        \
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kConvSmemCap)  \
+                            : cudaFuncSetAttribute(conv_bwd_s_kernel<T, KK>,                                        \
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kConvSmemCap); \
+        if (e != cudaSuccess) return e;                                                                             \
+      }                                                                                                             \
+      if (fwd)                                                                                                      \
+        conv_fwd_s_kernel<T, KK><<<grid, threads, ssm, s>>>((const T*)x, w, (T*)out, tokens, channels, hl, eps,     \
+                                                            normalize);                                             \
+      else                                                                                                          \
+        conv_bwd_s_kernel<T, KK><<<grid, threads, ssm, s>>>((const T*)dy, (const T*)x, w, (T*)out, dw, tokens,      \
+                                                            channels, hl, eps, normalize);                          \
+    } else if (fwd) {                                                                                               \
       conv_fwd_v_kernel<T, KK><<<grid, threads, 0, s>>>((const T*)x, w, (T*)out, tokens, channels, hl, eps,         \
                                                         normalize);                                                 \
-    else                                                                                                            \
+    } else {                                                                                                        \
       conv_bwd_v_kernel<T, KK><<<grid, threads, 0, s>>>((const T*)dy, (const T*)x, w, (T*)out, dw, tokens,          \
                                                         channels, hl, eps, normalize);                              \
+    }                                                                                                               \
     break;
   switch (ksize) {
     KIMI_CONV_CASE(1)
@@ -281,11 +491,7 @@ cudaError_t launch_conv(bool fwd, const void* dy, const void* x, const float* w,
 
 }  // namespace
 
-int conv_bwd_partial_rows(int batch, int tokens) { return batch * ((tokens + kTile - 1) / kTile); }
-
-namespace {
-
-}  // namespace
+int conv_bwd_partial_rows(int batch, int tokens) { return batch * ((tokens + kTile - 1) / kTile); }  // >= staged rows
 
 cudaError_t conv_silu_norm_fwd(int dtype, const void* x, const float* w, void* y, int batch, int tokens,
                                int channels, int ksize, int head_dim, float eps, bool normalize, cudaStream_t s) {
@@ -314,7 +520,9 @@ cudaError_t conv_silu_norm_bwd(int dtype, const void* dy, const void* x, const f
   }
   if (e != cudaSuccess) return e;
   const int n = channels * ksize;
-  const int rows = conv_bwd_partial_rows(batch, tokens);
+  const size_t es = dtype == 0 ? 4 : 2;
+  const int tile = conv_bwd_s_smem(channels, ksize, es) <= kConvSmemCap ? kSTile : kTile;
+  const int rows = batch * ((tokens + tile - 1) / tile);
   const dim3 rgrid((n + 31) / 32, rows >= 64 * 8 ? 8 : 1);
   if (cudaMemsetAsync(dw, 0, sizeof(float) * n, s) != cudaSuccess) return cudaGetLastError();
   dw_reduce_kernel<<<rgrid, 256, 0, s>>>(dw_part, dw, rows, n);

@@ -286,28 +286,63 @@ __global__ void decay_fwd_kernel(const T* __restrict__ z, const float* __restric
 }
 
 template <typename T>
-__global__ void decay_bwd_kernel(const float* __restrict__ dg, const T* __restrict__ z,
-                                 const float* __restrict__ a_log, T* __restrict__ dz, float* __restrict__ da_log,
-                                 int64_t n, int heads, int kdim, float g_min, float ceps) {
+__global__ void __launch_bounds__(256) decay_bwd_kernel(const float* __restrict__ dg, const T* __restrict__ z,
+                                                        const float* __restrict__ a_log, T* __restrict__ dz,
+                                                        float* __restrict__ da_log, int64_t n, int heads, int kdim,
+                                                        float g_min, float ceps) {
+  // 8 consecutive elements per thread (kdim % 64 == 0: they share one head); the lanes of a head
+  // (kdim / 8 of them, contiguous) reduce with shuffles, one shared atomic per head segment, and
+  // the grid is capped so each block flushes its per-head partials once.
   extern __shared__ float sda[];
   for (int i = threadIdx.x; i < heads; i += blockDim.x) sda[i] = 0.f;
   __syncthreads();
-  // With kdim % 32 == 0 (checked by the launcher, and n is then a multiple of 32), the 32
-  // consecutive elements of a warp share one head: reduce in registers, one shared atomic.
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int h = (int)((i / kdim) % heads);
-    const float sc = expf(a_log[h]), zv = to_f<T>(z[i]);
-    const float p = sigmoidf_(sc * zv);
-    const bool inside = p > ceps && p < 1.f - ceps;
-    const float dpre = inside ? dg[i] * g_min * p * (1.f - p) : 0.f;  // d/d(sc*z)
-    dz[i] = from_f<T>(dpre * sc);
-    const float part = warp_sum(dpre * zv * sc);
-    if ((threadIdx.x & 31) == 0) atomicAdd(&sda[h], part);
+  const int seg = kdim / 8 < 32 ? kdim / 8 : 32;  // lanes per head segment inside a warp
+  const int64_t nv = n / 8;
+  for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < nv; base += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t v = base + threadIdx.x;
+    float part = 0.f;
+    int h = 0;
+    if (v < nv) {
+      const int64_t i0 = v * 8;
+      h = (int)((i0 / kdim) % heads);
+      const float sc = expf(a_log[h]);
+      float zv[8], gv[8];
+      if constexpr (sizeof(T) == 4) {
+        const float4 z0 = reinterpret_cast<const float4*>(z)[2 * v], z1 = reinterpret_cast<const float4*>(z)[2 * v + 1];
+        zv[0] = z0.x; zv[1] = z0.y; zv[2] = z0.z; zv[3] = z0.w; zv[4] = z1.x; zv[5] = z1.y; zv[6] = z1.z; zv[7] = z1.w;
+      } else {
+        Vec<T> zz;
+        zz.load(z + i0);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) zv[j] = zz.f(j);
+      }
+      const float4 g0 = reinterpret_cast<const float4*>(dg)[2 * v], g1 = reinterpret_cast<const float4*>(dg)[2 * v + 1];
+      gv[0] = g0.x; gv[1] = g0.y; gv[2] = g0.z; gv[3] = g0.w; gv[4] = g1.x; gv[5] = g1.y; gv[6] = g1.z; gv[7] = g1.w;
+      float out[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float p = sigmoidf_(sc * zv[j]);
+        const bool inside = p > ceps && p < 1.f - ceps;
+        const float dpre = inside ? gv[j] * g_min * p * (1.f - p) : 0.f;  // d/d(sc*z)
+        out[j] = dpre * sc;
+        part += dpre * zv[j] * sc;
+      }
+      if constexpr (sizeof(T) == 4) {
+        reinterpret_cast<float4*>(dz)[2 * v] = make_float4(out[0], out[1], out[2], out[3]);
+        reinterpret_cast<float4*>(dz)[2 * v + 1] = make_float4(out[4], out[5], out[6], out[7]);
+      } else {
+        Vec<T> o;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o.set(j, out[j]);
+        o.store(dz + i0);
+      }
+    }
+    part = group_sum(part, seg);
+    if (v < nv && (threadIdx.x % seg) == 0) atomicAdd(&sda[h], part);
   }
   __syncthreads();
   for (int i = threadIdx.x; i < heads; i += blockDim.x) atomicAdd(&da_log[i], sda[i]);
 }
-
 
 }  // namespace
 
@@ -404,10 +439,11 @@ cudaError_t kda_decay_fwd(int dtype, const void* z, const float* a_log, float* g
 cudaError_t kda_decay_bwd(int dtype, const float* dg, const void* z, const float* a_log, void* dz, float* da_log,
                           int64_t rows, int heads, int kdim, float g_min, float ceps, cudaStream_t s) {
   const int64_t n = rows * heads * kdim;
-  if (kdim % 32) return cudaErrorInvalidValue;
+  if (kdim % 64) return cudaErrorInvalidValue;
   KIMI_DISPATCH(dtype, T, {
-    decay_bwd_kernel<T><<<grid_for(n, 256), 256, heads * sizeof(float), s>>>(dg, (const T*)z, a_log, (T*)dz, da_log,
-                                                                            n, heads, kdim, g_min, ceps);
+    const int grid = (int)std::min<int64_t>(grid_for(n / 8, 256), 148 * 4);
+    decay_bwd_kernel<T><<<grid, 256, heads * sizeof(float), s>>>(dg, (const T*)z, a_log, (T*)dz, da_log, n, heads,
+                                                                 kdim, g_min, ceps);
   });
   return cudaGetLastError();
 }

@@ -87,13 +87,21 @@ def test_kda_decay(cuda, dtype):
     _close(d1[1], d2[1], 1e-4)
 
 
+# (3, 70, 640, 64) runs the shared-memory staged kernels; (2, 37, 2048, 128) in fp32 does not fit
+# shared memory and runs the register-tiled ones; "offset" hands in a view whose base is not
+# 16-byte aligned, which the binding realigns before any vector load or bulk copy sees it.
 @pytest.mark.parametrize("normalize", [True, False])
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_conv_silu_norm(cuda, dtype, normalize):
+@pytest.mark.parametrize("dtype,shape", [(torch.float32, (3, 70, 640, 64)), (torch.bfloat16, (3, 70, 640, 64)),
+                                         (torch.float32, (2, 37, 2048, 128)), (torch.bfloat16, "offset")])
+def test_conv_silu_norm(cuda, dtype, shape, normalize):
     from kimi_k3_b200 import ops
     torch.manual_seed(3)
-    b, t, c, hd = 3, 70, 640, 64
-    x = torch.randn(b, t, c, device=cuda).to(dtype).requires_grad_()
+    offset = shape == "offset"
+    b, t, c, hd = (3, 70, 640, 64) if offset else shape
+    if offset:
+        x = torch.randn(b * t * c + 1, device=cuda).to(dtype)[1:].view(b, t, c).requires_grad_()
+    else:
+        x = torch.randn(b, t, c, device=cuda).to(dtype).requires_grad_()
     w = (0.3 * torch.randn(c, 4, device=cuda)).requires_grad_()
     gout = torch.randn(b, t, c, device=cuda).to(dtype)
 
