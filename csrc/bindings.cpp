@@ -680,11 +680,141 @@ at::Tensor situ_bwd_cat(at::Tensor dh, at::Tensor g, at::Tensor u, double bg, do
   return dgu;
 }
 
+// ---------------------------------------------------------------- decode step
+std::vector<at::Tensor> conv_step(std::vector<at::Tensor> xs, std::vector<at::Tensor> hists,
+                                  std::vector<at::Tensor> ws, std::vector<c10::optional<at::Tensor>> biases,
+                                  std::vector<int64_t> head_dims, double eps) {
+  const size_t n = xs.size();
+  TORCH_CHECK(n >= 1 && n <= 3 && hists.size() == n && ws.size() == n && biases.size() == n && head_dims.size() == n,
+              "conv_step takes one to three streams");
+  const at::cuda::CUDAGuard gd(xs[0].device());
+  kimi::ConvStepArgs a{};
+  std::vector<at::Tensor> ys, keep;
+  const int64_t batch = xs[0].size(0);
+  const int64_t ksize = ws[0].size(1);
+  for (size_t i = 0; i < n; ++i) {
+    auto x = dense(xs[i]);
+    CHECK_CUDA_CONTIG(hists[i]);
+    TORCH_CHECK(x.scalar_type() == xs[0].scalar_type() && hists[i].scalar_type() == x.scalar_type(),
+                "conv_step streams share one dtype");
+    const int64_t c = x.size(-1);
+    TORCH_CHECK(x.numel() == batch * c && hists[i].size(0) == batch && hists[i].size(1) == ksize - 1 &&
+                    hists[i].size(2) == c && ws[i].size(0) == c && ws[i].size(1) == ksize,
+                "conv_step shapes: x [B, C], history [B, K-1, C], weight [C, K]");
+    auto w = dense(ws[i].to(at::kFloat));
+    at::Tensor bias;
+    if (biases[i].has_value() && biases[i]->defined()) bias = dense(biases[i]->to(at::kFloat));
+    auto y = at::empty_like(x);
+    a.x[i] = x.data_ptr();
+    a.hist[i] = hists[i].data_ptr();
+    a.w[i] = w.data_ptr<float>();
+    a.bias[i] = bias.defined() ? bias.data_ptr<float>() : nullptr;
+    a.y[i] = y.data_ptr();
+    a.channels[i] = (int)c;
+    a.head_lanes[i] = (int)(head_dims[i] / 8);
+    TORCH_CHECK(head_dims[i] == 0 || (head_dims[i] % 8 == 0 && c % head_dims[i] == 0), "conv_step head_dim");
+    keep.insert(keep.end(), {x, w, bias});
+    ys.push_back(y);
+  }
+  check(kimi::conv_step(dtype_code(xs[0]), a, (int)n, (int)batch, (int)ksize, (float)eps, stream()), "conv_step");
+  return ys;
+}
+
+std::vector<at::Tensor> kda_decode(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor g, at::Tensor beta,
+                                   at::Tensor state, c10::optional<at::Tensor> state_out) {
+  q = dense(q);
+  k = dense(k);
+  v = dense(v);
+  g = dense(g.to(at::kFloat));
+  beta = dense(beta.to(at::kFloat));
+  CHECK_CUDA_CONTIG(state);
+  TORCH_CHECK(state.scalar_type() == at::kFloat && state.dim() == 4 && state.size(2) == 64 && state.size(3) == 64,
+              "kda_decode takes an fp32 state [B, H, 64, 64]");
+  const int64_t b = state.size(0), h = state.size(1);
+  TORCH_CHECK(q.numel() == b * h * 64 && k.numel() == b * h * 64 && v.numel() == b * h * 64 &&
+                  g.numel() == b * h * 64 && beta.numel() == b * h,
+              "kda_decode shapes: q/k/v/g [B, H, 64], beta [B, H]");
+  const at::cuda::CUDAGuard gd(q.device());
+  at::Tensor out_state = state_out.has_value() && state_out->defined() ? *state_out : at::empty_like(state);
+  CHECK_CUDA_CONTIG(out_state);
+  TORCH_CHECK(out_state.sizes() == state.sizes() && out_state.scalar_type() == at::kFloat, "state_out shape");
+  auto o = at::empty({b, h, 64}, q.options());
+  check(kimi::kda_decode(dtype_code(q), q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr<float>(),
+                         beta.data_ptr<float>(), state.data_ptr<float>(), out_state.data_ptr<float>(), o.data_ptr(),
+                         (int)b, (int)h, stream()),
+        "kda_decode");
+  return {o, out_state};
+}
+
+bool mla_decode_supported(int64_t heads, int64_t ldim) { return kimi::mla_decode_supported((int)heads, (int)ldim); }
+
+at::Tensor mla_decode(at::Tensor qlat, at::Tensor latent, at::Tensor lengths) {
+  qlat = dense(qlat.to(at::kFloat));
+  CHECK_CUDA_CONTIG(latent);
+  auto len = dense(lengths.to(at::kInt));
+  TORCH_CHECK(latent.dim() == 3 && qlat.dim() == 3 && qlat.size(0) == latent.size(0) && qlat.size(2) == latent.size(2),
+              "mla_decode shapes: qlat [B, H, L], latent [B, T, L]");
+  const int64_t b = latent.size(0), tmax = latent.size(1), l = latent.size(2), h = qlat.size(1);
+  const at::cuda::CUDAGuard gd(latent.device());
+  int rps = 0;
+  const int splits = kimi::mla_decode_splits((int)b, tmax, &rps);
+  auto opts = qlat.options();
+  auto part = at::empty({b, splits, h, l}, opts);
+  auto ml = at::empty({b, splits, h, 2}, opts);
+  auto ctx = at::empty({b, h, l}, opts);
+  check(kimi::mla_decode(dtype_code(latent), qlat.data_ptr<float>(), latent.data_ptr(), len.data_ptr<int32_t>(),
+                         (int)b, (int)h, (int)l, tmax, part.data_ptr<float>(), ml.data_ptr<float>(), splits, rps,
+                         ctx.data_ptr<float>(), stream()),
+        "mla_decode");
+  return ctx;
+}
+
+at::Tensor sample_tokens(at::Tensor logits, c10::optional<at::Tensor> seen, double penalty, double temperature,
+                         int64_t top_k, double top_p, bool do_sample, at::Tensor seed_offset) {
+  logits = dense(logits);
+  TORCH_CHECK(logits.dim() == 2, "logits must be [B, V]");
+  TORCH_CHECK(seed_offset.is_cuda() && seed_offset.scalar_type() == at::kLong && seed_offset.numel() >= 2,
+              "seed_offset must be a CUDA int64 tensor {seed, offset}");
+  const int64_t b = logits.size(0), vocab = logits.size(1);
+  const at::cuda::CUDAGuard gd(logits.device());
+  const uint32_t* sp = nullptr;
+  int words = 0;
+  if (seen.has_value() && seen->defined()) {
+    CHECK_CUDA_CONTIG((*seen));
+    TORCH_CHECK(seen->scalar_type() == at::kInt && seen->size(0) == b && seen->size(1) * 32 >= vocab,
+                "seen must be an int32 bitmap [B, ceil(V / 32)]");
+    sp = reinterpret_cast<const uint32_t*>(seen->data_ptr());
+    words = (int)seen->size(1);
+  }
+  auto out = at::empty({b}, logits.options().dtype(at::kLong));
+  check(kimi::sample_tokens(dtype_code(logits), logits.data_ptr(), (int)b, (int)vocab, sp, words, (float)penalty,
+                            (float)temperature, (int)top_k, (float)top_p, do_sample,
+                            seed_offset.data_ptr<int64_t>(), out.data_ptr<int64_t>(), stream()),
+        "sample_tokens");
+  return out;
+}
+
+void seen_mark(at::Tensor seen, at::Tensor ids, int64_t vocab) {
+  CHECK_CUDA_CONTIG(seen);
+  TORCH_CHECK(seen.scalar_type() == at::kInt && ids.dim() == 2 && ids.size(0) == seen.size(0), "seen_mark shapes");
+  auto idc = dense(ids.to(at::kLong));
+  const at::cuda::CUDAGuard gd(seen.device());
+  check(kimi::seen_mark(reinterpret_cast<uint32_t*>(seen.data_ptr()), (int)seen.size(1), idc.data_ptr<int64_t>(),
+                        idc.size(0), idc.size(1), idc.size(1), (int)vocab, stream()),
+        "seen_mark");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "kimi_k3_b200 sm_100a kernels";
   m.def("rms_norm_fwd", &rms_norm_fwd);
+  m.def("conv_step", &conv_step);
+  m.def("kda_decode", &kda_decode);
+  m.def("mla_decode_supported", &mla_decode_supported);
+  m.def("mla_decode", &mla_decode);
+  m.def("sample_tokens", &sample_tokens);
+  m.def("seen_mark", &seen_mark);
   m.def("rms_norm_bwd", &rms_norm_bwd);
   m.def("situ_fwd", &situ_fwd);
   m.def("situ_bwd", &situ_bwd);

@@ -114,4 +114,31 @@ cudaError_t muon_apply(const void* o_bf16, float* const* params, const float* su
 cudaError_t tcs_selftest(const float* A, const float* B, float* out, int K, int n, int mode, int* status,
                          cudaStream_t s);
 
+// ---------------------------------------------------------------- decode step (decode.cu)
+// Up to three short-conv streams advanced by one token in one launch; head_lanes = head_dim / 8
+// for a per-head L2 norm after the SiLU, 0 for none.  bias[i] may be nullptr.
+struct ConvStepArgs {
+  const void* x[3];
+  void* hist[3];
+  const float* w[3];
+  const float* bias[3];
+  void* y[3];
+  int channels[3];
+  int head_lanes[3];
+};
+cudaError_t conv_step(int dtype, const ConvStepArgs& args, int streams, int batch, int ksize, float eps,
+                      cudaStream_t s);
+cudaError_t kda_decode(int dtype, const void* q, const void* k, const void* v, const float* g, const float* beta,
+                       const float* state_in, float* state_out, void* o, int batch, int heads, cudaStream_t s);
+bool mla_decode_supported(int heads, int ldim);
+int mla_decode_splits(int batch, int64_t tmax, int* rows_per_split);
+cudaError_t mla_decode(int dtype, const float* qlat, const void* latent, const int32_t* lengths, int batch,
+                       int heads, int ldim, int64_t tmax, float* part_acc, float* part_ml, int splits,
+                       int rows_per_split, float* ctx, cudaStream_t s);
+cudaError_t sample_tokens(int dtype, const void* logits, int batch, int vocab, const uint32_t* seen, int seen_words,
+                          float penalty, float temperature, int top_k, float top_p, bool do_sample,
+                          const int64_t* seed_offset, int64_t* out, cudaStream_t s);
+cudaError_t seen_mark(uint32_t* seen, int seen_words, const int64_t* ids, int64_t rows, int64_t cols, int64_t ld,
+                      int vocab, cudaStream_t s);
+
 }  // namespace kimi

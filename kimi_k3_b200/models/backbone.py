@@ -566,7 +566,10 @@ class HybridAttentionBackbone(nn.Module):
         return self._forward_attnres(hidden_states, layer_mask, mask, cache, use_cache, mode, output_hidden_states,
                                      output_depth_weights, output_diagnostics, update_routing_bias)
 
-    def _make_cache(self, caches):
+    def _make_cache(self, caches, prev=None, tokens: int = 0):
+        if not host_checks():
+            # sync-free (decode-graph capture): every row advanced by `tokens` valid tokens
+            return HybridBackboneCache(tuple(caches), (prev.sequence_length if prev is not None else 0) + tokens)
         offsets = caches[0].sequence_offsets
         return HybridBackboneCache(tuple(caches), int(offsets.max().item()))
 
@@ -601,7 +604,7 @@ class HybridAttentionBackbone(nn.Module):
         out = self.final_norm(out)
         if output_hidden_states:
             states.append(out)
-        bc = self._make_cache(caches) if use_cache else None
+        bc = self._make_cache(caches, cache, x.shape[1]) if use_cache else None
         diagnostics = None
         if output_diagnostics:
             from .diagnostics import build_backbone_diagnostics
@@ -640,7 +643,7 @@ class HybridAttentionBackbone(nn.Module):
         out = self.final_norm(fmix.mixed_state)
         if output_hidden_states:
             legacy.extend((fmix.mixed_state, out))
-        bc = self._make_cache(caches) if use_cache else None
+        bc = self._make_cache(caches, cache, x.shape[1]) if use_cache else None
         depth = None
         if rs:
             depth = self._depth_outputs(tuple(site_stats), fmix.stats, state, rw)

@@ -108,6 +108,9 @@ class KDAState:
     k_conv_state: ShortConvState
     v_conv_state: ShortConvState
     sequence_offset: torch.Tensor
+    # A serving cache owned by one decoder: decode kernels advance its tensors in place instead
+    # of returning new ones (the previous step's state is not kept).
+    inplace: bool = False
 
     def __post_init__(self) -> None:
         if self.recurrent_state.ndim != 4:
@@ -379,7 +382,7 @@ class KDAProjections(nn.Module):
         return torch.cat(outs, 0), (ShortConvState(torch.cat(bufs, 0)) if return_state else None)
 
     def forward(self, hidden_states, *, q_conv_state=None, k_conv_state=None, v_conv_state=None,
-                attention_mask=None, output_final_state=False) -> KDAProjectionResult:
+                attention_mask=None, output_final_state=False, inplace_state=False) -> KDAProjectionResult:
         c = self.config
         if hidden_states.ndim != 3 or hidden_states.shape[-1] != c.d_model:
             raise ValueError(f"hidden_states must have shape [B,T,{c.d_model}]")
@@ -395,6 +398,24 @@ class KDAProjections(nn.Module):
         beta = beta.clamp(be, 1.0 - be)
         decay_logits = self.alpha_up(self.alpha_down(hidden_states)).reshape(b, t, c.num_heads, c.key_head_dim)
         decay_logits = decay_logits + self.b_alpha[None, None]
+        states = (q_conv_state, k_conv_state, v_conv_state)
+        hl = c.key_head_dim // 8
+        step = (_ops.use_kernels(hidden_states) and t == 1 and attention_mask is None
+                and 1 <= c.short_conv_kernel_size <= 8 and c.key_head_dim % 8 == 0 and 0 < hl <= 32
+                and hl & (hl - 1) == 0 and c.value_width % 8 == 0
+                and all(st is not None and st.buffer.dtype == ql.dtype
+                        and st.buffer.shape[1] == c.short_conv_kernel_size - 1 for st in states))
+        if step:
+            # One decode token: the three conv streams advance in one launch (history shifted in
+            # place -- on copies unless the state belongs to a serving cache).
+            hists = [st.buffer if inplace_state else st.buffer.clone() for st in states]
+            convs = (self.q_conv, self.k_conv, self.v_conv)
+            q, k, v = _ops.conv_silu_norm_step([ql, kl, vl], hists, [m.weight for m in convs], [m.bias for m in convs],
+                                               [c.key_head_dim, c.key_head_dim, 0], c.eps)
+            return KDAProjectionResult(q.view(b, t, c.num_heads, c.key_head_dim),
+                                       k.view(b, t, c.num_heads, c.key_head_dim),
+                                       v.view(b, t, c.num_heads, c.value_head_dim), beta, decay_logits,
+                                       ShortConvState(hists[0]), ShortConvState(hists[1]), ShortConvState(hists[2]))
         if fused:
             # One kernel per stream: causal conv (zero history) + SiLU (+ per-head L2 norm).
             q = _ops.conv_silu_norm(ql, self.q_conv.weight, c.key_head_dim, c.eps, True)
@@ -475,17 +496,21 @@ class KimiDeltaAttention(nn.Module):
         validate_attention_mask(attention_mask, b, t)
         self._validate_state(hidden_states, state)
         return_state = output_final_state or mode == "decode"
+        inplace = state is not None and state.inplace and mode == "decode"
         proj = self.projections(hidden_states, q_conv_state=state.q_conv_state if state else None,
                                 k_conv_state=state.k_conv_state if state else None,
                                 v_conv_state=state.v_conv_state if state else None,
-                                attention_mask=attention_mask, output_final_state=return_state)
+                                attention_mask=attention_mask, output_final_state=return_state,
+                                inplace_state=inplace)
         g, alpha = self.decay(proj.decay_logits)
         init = state.recurrent_state if state is not None else None
         kw = dict(initial_state=init, output_final_state=return_state or output_diagnostics,
                   attention_mask=attention_mask, accumulate_state_in_fp32=c.accumulate_state_in_fp32)
         if mode in ("recurrent", "decode"):
-            if mode == "decode" and _ops.use_kernels(hidden_states) and init is not None and attention_mask is None:
-                o, fs = _ops.kda_decode_step(proj.q, proj.k, proj.v, g, proj.beta, init)
+            if (mode == "decode" and _ops.use_kernels(hidden_states) and init is not None and attention_mask is None
+                    and c.key_head_dim == 64 and c.value_head_dim == 64):
+                o, fs = _ops.kda_decode_step(proj.q, proj.k, proj.v, g, proj.beta, init,
+                                             out_state=init if inplace else None)
                 core = KDAOperatorOutput(o, fs)
             else:
                 core = recurrent_kda(proj.q, proj.k, proj.v, g, proj.beta, **kw)
@@ -501,7 +526,10 @@ class KimiDeltaAttention(nn.Module):
             lengths = (torch.full((b,), t, dtype=torch.long, device=hidden_states.device) if attention_mask is None
                        else attention_mask.sum(dim=1).to(torch.long))
             offset = lengths if state is None else state.sequence_offset.to(hidden_states.device) + lengths
-            nxt = KDAState(core.final_state, proj.q_conv_state, proj.k_conv_state, proj.v_conv_state, offset)
+            if inplace:
+                offset = state.sequence_offset.copy_(offset)
+            nxt = KDAState(core.final_state, proj.q_conv_state, proj.k_conv_state, proj.v_conv_state, offset,
+                           inplace=inplace)
         diagnostics = None
         if output_diagnostics:
             from .diagnostics import build_kda_diagnostics

@@ -174,6 +174,54 @@ class MLACache:
         return MLACache(packed, packed_mask, lengths)
 
 
+class StaticMLACache(MLACache):
+    """A serving cache: a preallocated latent buffer ``[B, Tmax, L]`` whose valid rows are the
+    prefix ``[0, sequence_offset[b])``.  :meth:`append` writes one decode token per row in place
+    (no reallocation, no host synchronisation), so a decode step can be captured in a CUDA graph
+    and replayed; rows that reach ``Tmax`` keep overwriting their last slot.  Built from a
+    prefill cache with :meth:`from_cache`."""
+
+    def __init__(self, latent_kv: torch.Tensor, sequence_offset: torch.Tensor):
+        super().__init__(latent_kv, None, sequence_offset)
+
+    @classmethod
+    def from_cache(cls, cache: MLACache, max_length: int) -> "StaticMLACache":
+        b, t, l = cache.latent_kv.shape
+        if max_length < t:
+            raise ValueError(f"max_length {max_length} is shorter than the prefilled cache ({t})")
+        buf = cache.latent_kv.new_zeros(b, max_length, l)
+        buf[:, :t] = cache.latent_kv
+        if cache.attention_mask is not None:
+            buf[:, :t] *= cache.attention_mask[..., None].to(buf.dtype)
+        return cls(buf, cache.sequence_offset.clone())
+
+    @property
+    def valid_lengths(self) -> torch.Tensor:
+        return self.sequence_offset
+
+    def valid_mask(self) -> torch.Tensor:
+        return torch.arange(self.latent_kv.shape[1], device=self.latent_kv.device)[None, :] < self.sequence_offset[:, None]
+
+    def clone(self) -> "StaticMLACache":
+        return StaticMLACache(self.latent_kv.clone(), self.sequence_offset.clone())
+
+    def reorder(self, indices: torch.Tensor) -> "StaticMLACache":
+        return StaticMLACache(self.latent_kv.index_select(0, indices), self.sequence_offset.index_select(0, indices))
+
+    def append(self, latent_kv: torch.Tensor, attention_mask: torch.Tensor | None = None) -> "StaticMLACache":
+        b, t, l = latent_kv.shape
+        if t != 1 or attention_mask is not None and attention_mask.shape != (b, 1):
+            raise ValueError("a static MLA cache appends exactly one token per row")
+        if latent_kv.dtype != self.latent_kv.dtype:
+            latent_kv = latent_kv.to(self.latent_kv.dtype)
+        slot = self.sequence_offset.clamp(max=self.latent_kv.shape[1] - 1)
+        rows = torch.arange(b, device=latent_kv.device)
+        self.latent_kv.index_put_((rows, slot), latent_kv[:, 0])
+        step = 1 if attention_mask is None else attention_mask[:, 0].to(torch.long)
+        self.sequence_offset.add_(step)
+        return self
+
+
 # --------------------------------------------------------------------------- projections
 @dataclass
 class LatentKVOutput:
@@ -303,17 +351,22 @@ def mla_attention(q, k, v, attention_mask=None, is_causal=True, dropout_p=0.0, k
     return out
 
 
-def absorbed_latent_decode(query, latent_cache, cache_mask, key_up_weight, value_up_weight, num_heads):
+def absorbed_latent_decode(query, latent_cache, cache_mask, key_up_weight, value_up_weight, num_heads, *,
+                           lengths=None):
     """One-token decode attending over the latent cache directly.
 
     ``score_t = q_h . (W_uk,h c_t) = (W_uk,h^T q_h) . c_t`` and
     ``o_h = W_uv,h (sum_t p_t c_t)``; K/V are never materialised.
-    query ``[B,1,H,Dq]``, latent_cache ``[B,T,L]`` -> ``[B,1,H,Dv]`` (fp32).
+    query ``[B,1,H,Dq]``, latent_cache ``[B,T,L]`` -> ``[B,1,H,Dv]`` (fp32).  ``lengths`` [B]
+    (valid prefix per row) replaces ``cache_mask`` for a preallocated cache.
     """
     b, _, h, dq = query.shape
     l = latent_cache.shape[-1]
     if _ops.use_kernels(query):
-        return _ops.mla_absorbed_decode(query, latent_cache, cache_mask, key_up_weight, value_up_weight)
+        return _ops.mla_absorbed_decode(query, latent_cache, cache_mask, key_up_weight, value_up_weight,
+                                        lengths=lengths)
+    if lengths is not None:
+        cache_mask = torch.arange(latent_cache.shape[1], device=query.device)[None, :] < lengths[:, None]
     wd = torch.promote_types(query.dtype, torch.float32)
     wuk = key_up_weight.to(wd).reshape(h, dq, l)
     wuv = value_up_weight.to(wd).reshape(h, -1, l)
@@ -419,7 +472,8 @@ class GatedMLA(nn.Module):
             # Weight-absorbed decode: attend over the latent cache; K/V never rebuilt.
             raw = absorbed_latent_decode(query, updated.latent_kv, updated.attention_mask,
                                          self.projections.latent_kv.key_up.weight,
-                                         self.projections.latent_kv.value_up.weight, c.num_heads)
+                                         self.projections.latent_kv.value_up.weight, c.num_heads,
+                                         lengths=getattr(updated, "valid_lengths", None))
             if not c.keep_attention_output_fp32:
                 raw = raw.to(hidden_states.dtype)
             out, gate = self._postprocess(raw, hidden_states)
@@ -427,7 +481,8 @@ class GatedMLA(nn.Module):
         key, value = self.projections.reconstruct_kv(updated.latent_kv)
         self._record_qk_scale(query, key)
         qpos = prev[:, None] + torch.arange(t, device=dev)[None, :]
-        result = mla_attention(query, key, value, updated.attention_mask, is_causal=True,
+        cache_mask = updated.valid_mask() if isinstance(updated, StaticMLACache) else updated.attention_mask
+        result = mla_attention(query, key, value, cache_mask, is_causal=True,
                                dropout_p=c.attention_dropout, keep_output_fp32=c.keep_attention_output_fp32,
                                backend=c.resolved_backend, query_mask=current_mask, query_positions=qpos,
                                training=self.training, return_attentions=need_probs)
@@ -440,12 +495,12 @@ class GatedMLA(nn.Module):
             if gate is None:
                 gate = self.output_gate.gate_values(hidden_states)
             diagnostics = build_mla_diagnostics(query, key, value, updated.latent_kv, gate, probs,
-                                                updated.attention_mask, current_mask, updated.cache_elements,
+                                                cache_mask, current_mask, updated.cache_elements,
                                                 c.full_kv_width, raw, out, self._last_qk_scale)
         return GatedMLAOutput(out, updated if use_cache else None, probs if output_attentions else None, diagnostics)
 
 
 __all__ = [
-    "GatedMLAConfig", "MLACache", "LatentKVProjection", "LatentKVOutput", "MLAProjections", "MLAProjectionOutput",
+    "GatedMLAConfig", "MLACache", "StaticMLACache", "LatentKVProjection", "LatentKVOutput", "MLAProjections", "MLAProjectionOutput",
     "manual_causal_attention", "mla_attention", "absorbed_latent_decode", "GatedMLA", "GatedMLAOutput",
 ]

@@ -14,9 +14,10 @@ import os
 import torch
 
 from . import _loader
-from .functional import (attnres_mix, conv_silu_norm, flash_attention, kda_chunk, kda_decay, kda_decode_step,
-                         linear_cross_entropy, mla_absorbed_decode, moe_grouped_experts, qb_histogram, rms_norm,
-                         router_topk, sigmoid_mul, situ_glu)
+from .functional import (attnres_mix, conv_silu_norm, conv_silu_norm_step, flash_attention, kda_chunk, kda_decay,
+                         kda_decode_step, linear_cross_entropy, mark_seen, mla_absorbed_decode, mla_decode_supported,
+                         moe_grouped_experts, qb_histogram, rms_norm, router_topk, sample_tokens, sigmoid_mul,
+                         situ_glu)
 
 
 def kernels_enabled() -> bool:
@@ -34,5 +35,6 @@ def use_kernels(x: torch.Tensor) -> bool:
 __all__ = [
     "kernels_enabled", "use_kernels", "rms_norm", "situ_glu", "sigmoid_mul", "kda_chunk", "kda_decode_step",
     "conv_silu_norm", "kda_decay", "flash_attention", "mla_absorbed_decode", "router_topk", "qb_histogram",
-    "moe_grouped_experts", "attnres_mix", "linear_cross_entropy",
+    "moe_grouped_experts", "attnres_mix", "linear_cross_entropy", "conv_silu_norm_step", "mla_decode_supported",
+    "sample_tokens", "mark_seen",
 ]

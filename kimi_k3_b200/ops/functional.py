@@ -182,14 +182,26 @@ def kda_chunk(q, k, v, g, beta, initial_state, output_final_state, chunk_size=64
     return o, ht
 
 
-def kda_decode_step(q, k, v, g, beta, state):
-    """One recurrent KDA token for ``[B,1,H,*]`` inputs with fp32 state ``[B,H,K,V]``."""
-    qf, kf, vf, gf, bf = (x[:, 0].float() for x in (q, k, v, g, beta))
-    s = state.float() * torch.exp(gf)[..., None]
-    err = vf - torch.einsum("bhkv,bhk->bhv", s, kf)
-    s = s + torch.einsum("bhk,bhv->bhkv", bf[..., None] * kf, err)
-    o = torch.einsum("bhkv,bhk->bhv", s, qf)
-    return o[:, None].to(v.dtype), s
+def kda_decode_step(q, k, v, g, beta, state, out_state=None):
+    """One recurrent KDA token for ``[B,1,H,64]`` inputs with fp32 state ``[B,H,64,64]``.
+
+    The kernel reads ``state`` and writes the updated state to ``out_state`` (a new tensor when
+    None; ``out_state=state`` advances a serving cache in place).  Returns ``(o [B,1,H,64], state')``."""
+    b, _, h, _ = q.shape
+    o, ns = _C().kda_decode(q.reshape(b, h, 64), k.reshape(b, h, 64), v.reshape(b, h, 64),
+                            g.reshape(b, h, 64), beta.reshape(b, h), state.float().contiguous(), out_state)
+    return o.view(b, 1, h, 64), ns
+
+
+def conv_silu_norm_step(xs, histories, weights, biases, head_dims, eps):
+    """Advance up to three short-conv streams by one token (one launch).
+
+    ``xs[i]`` ``[B,1,C_i]`` or ``[B,C_i]``; ``histories[i]`` ``[B,K-1,C_i]`` is shifted IN PLACE
+    (oldest row first, the new input appended); ``head_dims[i]`` > 0 applies the per-head L2
+    norm after the SiLU.  Returns the outputs shaped like ``xs``."""
+    ys = _C().conv_step([x.reshape(x.shape[0], -1) for x in xs], list(histories), list(weights), list(biases),
+                        [int(d) for d in head_dims], float(eps))
+    return [y.view(x.shape) for x, y in zip(xs, ys)]
 
 
 # --------------------------------------------------------------------------- attention
@@ -226,19 +238,54 @@ def flash_attention(q, k, v, causal=True, key_padding_mask=None, scale=None):
     return _FlashAttn.apply(q, k, v, causal, kl, scale)
 
 
-def mla_absorbed_decode(query, latent_cache, cache_mask, key_up_weight, value_up_weight):
-    """Weight-absorbed one-token MLA attention over the latent cache (fp32 math)."""
+def mla_decode_supported(num_heads: int, latent_dim: int) -> bool:
+    return bool(_C().mla_decode_supported(int(num_heads), int(latent_dim)))
+
+
+def mla_absorbed_decode(query, latent_cache, cache_mask, key_up_weight, value_up_weight, lengths=None):
+    """Weight-absorbed one-token MLA attention over the latent cache (fp32 math).
+
+    ``query`` ``[B,1,H,Dq]``, ``latent_cache`` ``[B,T,L]`` whose valid rows form a prefix of
+    length ``lengths[b]`` (from ``cache_mask`` when not given) -> ``[B,1,H,Dv]`` fp32.  The
+    attention over the cache is the split-T flash-decode kernel; the two small per-head
+    projections into and out of the latent space are batched GEMMs."""
     b, _, h, dq = query.shape
     l = latent_cache.shape[-1]
     wuk = key_up_weight.float().reshape(h, dq, l)
     wuv = value_up_weight.float().reshape(h, -1, l)
-    q_lat = torch.einsum("bhd,hdl->bhl", query[:, 0].float(), wuk) / math.sqrt(dq)
-    scores = torch.einsum("bhl,btl->bht", q_lat, latent_cache.float())
-    if cache_mask is not None:
-        scores = scores.masked_fill(~cache_mask[:, None, :], -torch.inf)
-    p = torch.softmax(scores, dim=-1)
-    ctx = torch.einsum("bht,btl->bhl", p, latent_cache.float())
-    return torch.einsum("bhl,hvl->bhv", ctx, wuv)[:, None]
+    q_lat = torch.bmm(query[:, 0].float().transpose(0, 1), wuk).transpose(0, 1) / math.sqrt(dq)  # [B,H,L]
+    if latent_cache.dtype in (torch.float32, torch.bfloat16, torch.float16) and mla_decode_supported(h, l):
+        if lengths is None:
+            lengths = (torch.full((b,), latent_cache.shape[1], dtype=torch.int32, device=query.device)
+                       if cache_mask is None else cache_mask.sum(dim=1, dtype=torch.int32))
+        ctx = _C().mla_decode(q_lat.contiguous(), latent_cache.contiguous(), lengths)
+    else:
+        scores = torch.einsum("bhl,btl->bht", q_lat, latent_cache.float())
+        if lengths is not None:
+            cache_mask = torch.arange(latent_cache.shape[1], device=query.device)[None, :] < lengths[:, None]
+        if cache_mask is not None:
+            scores = scores.masked_fill(~cache_mask[:, None, :], -torch.inf)
+        ctx = torch.einsum("bht,btl->bhl", torch.softmax(scores, dim=-1), latent_cache.float())
+    out = torch.bmm(ctx.transpose(0, 1), wuv.transpose(1, 2)).transpose(0, 1)  # [B,H,Dv]
+    return out[:, None]
+
+
+# --------------------------------------------------------------------------- sampling
+def sample_tokens(logits, seen_bits, config, seed_offset):
+    """Fused next-token choice for ``[B,V]`` logits -> ``[B]`` int64 (one launch).
+
+    ``seen_bits`` is an int32 ``[B, ceil(V/32)]`` bitmap of tokens that take the repetition
+    penalty (None: no penalty); ``seed_offset`` an int64 CUDA tensor ``{seed, draw counter}``."""
+    pen = config.repetition_penalty
+    return _C().sample_tokens(logits, seen_bits if pen not in (None, 1) else None, float(pen or 1.0),
+                              float(config.temperature), int(config.top_k or 0),
+                              float(config.top_p if config.top_p is not None else 1.0), bool(config.do_sample),
+                              seed_offset)
+
+
+def mark_seen(seen_bits, token_ids, vocab):
+    """Set the bits of ``token_ids`` ``[B,T]`` in the ``[B, ceil(V/32)]`` bitmap (in place)."""
+    _C().seen_mark(seen_bits, token_ids, int(vocab))
 
 
 # --------------------------------------------------------------------------- router / MoE
@@ -425,6 +472,7 @@ def linear_cross_entropy(hidden, weight, targets, valid, chunk_rows: int = 16384
 
 __all__ = [
     "rms_norm", "situ_glu", "sigmoid_mul", "kda_decay", "conv_silu_norm", "kda_chunk", "kda_decode_step",
+    "conv_silu_norm_step", "mla_decode_supported", "sample_tokens", "mark_seen",
     "flash_attention", "mla_absorbed_decode", "router_topk", "qb_histogram", "moe_grouped_experts",
     "attnres_mix", "linear_cross_entropy",
 ]

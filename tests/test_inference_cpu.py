@@ -86,3 +86,49 @@ def test_sampling_helpers_match_reference():
     assert torch.equal(apply_repetition_penalty(logits, prev, 1.3), rrp(logits, prev, 1.3))
     assert torch.equal(top_k_filter(logits, 4), rtk(logits, 4))
     assert torch.equal(top_p_filter(logits, 0.8), rtp(logits, 0.8))
+
+
+# ------------------------------------------------------------------ serving decoder (eager on CPU)
+def test_graph_decoder_matches_generate_tokens():
+    from kimi_k3_b200.infer import GraphDecoder
+    m = _model()
+    ids = torch.randint(5, 128, (2, 9))
+    for cfg in (GenerationConfig(max_new_tokens=6),
+                GenerationConfig(max_new_tokens=5, do_sample=True, top_k=20, top_p=0.9, temperature=0.8,
+                                 repetition_penalty=1.3, seed=7)):
+        ref_out = generate_tokens(m, ids, generation_config=cfg)
+        out = GraphDecoder(m, max_length=32, generation_config=cfg).generate(ids)
+        assert torch.equal(out.sequences, ref_out.sequences), (out.sequences, ref_out.sequences)
+        assert out.cache_stats["sequence_lengths"] == [9 + cfg.max_new_tokens - 1] * 2
+
+
+def test_graph_decoder_ragged_prompts_and_eos():
+    from kimi_k3_b200.infer import GraphDecoder
+    m = _model()
+    ids = torch.randint(5, 128, (2, 9))
+    mask = torch.ones(2, 9, dtype=torch.bool)
+    mask[1, 5:] = False
+    cfg = GenerationConfig(max_new_tokens=4)
+    ref_out = generate_tokens(m, ids, generation_config=cfg, attention_mask=mask)
+    out = GraphDecoder(m, max_length=16, generation_config=cfg).generate(ids, mask)
+    assert torch.equal(out.generated_ids, ref_out.generated_ids)
+    first = int(ref_out.generated_ids[0, 0])
+    cfg = GenerationConfig(max_new_tokens=6, eos_token_id=first, pad_token_id=0)
+    ref_out = generate_tokens(m, ids[:1], generation_config=cfg)
+    out = GraphDecoder(m, max_length=16, generation_config=cfg).generate(ids[:1])
+    assert out.finish_reason == ref_out.finish_reason == "eos"
+    assert torch.equal(out.generated_ids, ref_out.generated_ids)
+
+
+def test_static_mla_cache_appends_in_place():
+    from kimi_k3_b200.models.mla import MLACache, StaticMLACache
+    lat = torch.randn(2, 3, 4)
+    mask = torch.tensor([[True, True, True], [True, True, False]])
+    c = MLACache(lat, mask, mask.sum(1))
+    s = StaticMLACache.from_cache(c, 6)
+    buf = s.latent_kv
+    new = torch.randn(2, 1, 4)
+    assert s.append(new) is s and s.latent_kv is buf
+    assert s.sequence_offset.tolist() == [4, 3]
+    assert torch.equal(buf[0, 3], new[0, 0]) and torch.equal(buf[1, 2], new[1, 0])
+    assert s.valid_mask().tolist() == [[True] * 4 + [False] * 2, [True] * 3 + [False] * 3]
