@@ -159,7 +159,13 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(const float* __
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int len = (int)min((int64_t)lengths[b], tmax);
   const int r0 = split * rows_per_split, r1 = min(r0 + rows_per_split, len);
-  for (int i = tid; i < heads * ldim; i += kMlaThreads) sq[i] = qlat[(int64_t)b * heads * ldim + i];
+  {  // 16-byte loads, several in flight per thread (ldim % 8 == 0)
+    const float4* src = reinterpret_cast<const float4*>(qlat + (int64_t)b * heads * ldim);
+    float4* dst = reinterpret_cast<float4*>(sq);
+    const int n4 = heads * ldim / 4;
+#pragma unroll 4
+    for (int i = tid; i < n4; i += kMlaThreads) dst[i] = src[i];
+  }
   if (tid < HMAX) {
     sstat[tid] = -INFINITY;
     sstat[HMAX + tid] = 0.f;
@@ -173,7 +179,18 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(const float* __
   for (int c0 = r0; c0 < r1; c0 += kMlaRows) {
     const int nr = min(kMlaRows, r1 - c0);
     __syncthreads();  // previous sub-chunk fully consumed
-    for (int i = tid; i < nr * ldim; i += kMlaThreads) sx[i] = to_f<T>(xb[(int64_t)c0 * ldim + i]);
+    {
+      constexpr int VN = 16 / sizeof(T);
+      const T* src = xb + (int64_t)c0 * ldim;
+      const int nv = nr * ldim / VN;
+#pragma unroll 4
+      for (int i = tid; i < nv; i += kMlaThreads) {
+        Vec<T> v;
+        v.load(src + i * VN);
+#pragma unroll
+        for (int e = 0; e < VN; ++e) sx[i * VN + e] = v.f(e);
+      }
+    }
     __syncthreads();
     // scores of rows warp*4 .. +4
     {
@@ -258,6 +275,7 @@ __global__ void __launch_bounds__(256) mla_decode_combine_kernel(const float* __
   float m = -INFINITY;
   for (int s = 0; s < nsplit; ++s) m = fmaxf(m, part_ml[(((int64_t)b * nsplit + s) * heads + h) * 2]);
   float den = 0.f;
+#pragma unroll 4
   for (int s = 0; s < nsplit; ++s) {
     const int64_t i = ((int64_t)b * nsplit + s) * heads + h;
     if (part_ml[i * 2] > -INFINITY) den += expf(part_ml[i * 2] - m) * part_ml[i * 2 + 1];
@@ -265,6 +283,7 @@ __global__ void __launch_bounds__(256) mla_decode_combine_kernel(const float* __
   const float inv = den > 0.f ? 1.f / den : 0.f;  // an empty row attends to nothing
   for (int l = threadIdx.x; l < ldim; l += blockDim.x) {
     float acc = 0.f;
+#pragma unroll 4
     for (int s = 0; s < nsplit; ++s) {
       const int64_t i = ((int64_t)b * nsplit + s) * heads + h;
       const float ms = part_ml[i * 2];
@@ -612,7 +631,7 @@ size_t mla_smem(int heads, int ldim, int hmax) {
 }  // namespace
 
 bool mla_decode_supported(int heads, int ldim) {
-  if (ldim % 4) return false;
+  if (ldim % 8) return false;
   const int hmax = heads <= 16 ? 16 : heads <= 32 ? 32 : 0;
   if (!hmax || !(hmax == 16 ? mla_fits<16, 4>(heads, ldim) : mla_fits<32, 2>(heads, ldim))) return false;
   return mla_smem(heads, ldim, hmax) <= 200 * 1024;

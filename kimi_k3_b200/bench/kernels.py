@@ -231,8 +231,39 @@ def bench_kda_phases(args) -> list:
     return rows
 
 
+def bench_decode(args) -> list:
+    """One decode step's device kernels at serving shapes: MLA latent flash-decode over a
+    ``[batch, tokens, dim]`` cache (``--heads`` query heads), KDA recurrent token, fused sampling."""
+    C, dev = _require_cuda()
+    torch.manual_seed(0)
+    b, t, l, h = args.batch, args.tokens, args.dim, args.heads
+    rows = []
+    qlat = torch.randn(b, h, l, device=dev)
+    latent = torch.randn(b, t, l, device=dev).bfloat16()
+    lengths = torch.full((b,), t, dtype=torch.int32, device=dev)
+    tm = time_fn(lambda: C.mla_decode(qlat, latent, lengths), device=dev, warmup=args.warmup, repeats=args.repeats)
+    rows.append(_emit({"case": "decode", "kernel": "mla_decode", "batch": b, "cache_tokens": t, "latent": l,
+                       "heads": h, **tm.as_dict(), **roofline(tm.median_ms, bytes_moved=latent.numel() * 2)}))
+    q = torch.randn(b, h, 64, device=dev).bfloat16()
+    g = -torch.rand(b, h, 64, device=dev)
+    beta = torch.rand(b, h, device=dev)
+    st = torch.randn(b, h, 64, 64, device=dev)
+    tk = time_fn(lambda: C.kda_decode(q, q, q, g, beta, st, st), device=dev, warmup=args.warmup,
+                 repeats=args.repeats)
+    rows.append(_emit({"case": "decode", "kernel": "kda_decode", "batch": b, "heads": h, **tk.as_dict(),
+                       **roofline(tk.median_ms, bytes_moved=2 * st.numel() * 4)}))
+    logits = torch.randn(b, args.vocab, device=dev).bfloat16()
+    so = torch.tensor([0, 0], dtype=torch.long, device=dev)
+    for name, kw in (("greedy", (1.0, 1.0, 0, 1.0, False)), ("top_k_top_p", (1.0, 0.8, 50, 0.9, True))):
+        ts = time_fn(lambda: C.sample_tokens(logits, None, *kw, so), device=dev, warmup=args.warmup,
+                     repeats=args.repeats)
+        rows.append(_emit({"case": "decode", "kernel": f"sample_{name}", "batch": b, "vocab": args.vocab,
+                           **ts.as_dict(), **roofline(ts.median_ms, bytes_moved=logits.numel() * 2)}))
+    return rows
+
+
 CASES = {"kda_phases": bench_kda_phases, "gemm": bench_gemm, "kda": bench_kda, "moe": bench_moe, "linear_ce": bench_linear_ce,
-         "attention": bench_attention, "attnres": bench_attnres}
+         "attention": bench_attention, "attnres": bench_attnres, "decode": bench_decode}
 
 
 def build_parser(parser: argparse.ArgumentParser | None = None) -> argparse.ArgumentParser:

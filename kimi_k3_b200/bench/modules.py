@@ -514,3 +514,74 @@ def bench_step_profile(argv=None) -> str:
 
 
 BENCHMARKS["step"] = bench_step_profile
+
+
+def bench_decode(argv=None) -> list:
+    """Serving decode throughput of the flagship architecture (``t4_wikitext``, vocab 50,257,
+    random-init weights): prefill a batch of prompts, then generate ``--new-tokens`` per row.
+    Rows: the CUDA-graph decoder (:class:`GraphDecoder`, bf16, one graph replay per token) and the
+    reference-style loop (:func:`generate_tokens` under the same bf16 autocast: a new cache per
+    token and every kernel launched from Python).  Decode time is the host time between two device
+    synchronisations around the token loop."""
+    import contextlib
+    from ..config.profiles import profile_model_config
+    from ..infer import GenerationConfig, GraphDecoder, generate_tokens
+    from ..models import KimiK3
+    p = argparse.ArgumentParser(description="decode throughput")
+    p.add_argument("--batch", type=int, default=16)
+    p.add_argument("--prompt", type=int, default=512)
+    p.add_argument("--new-tokens", type=int, default=128)
+    p.add_argument("--vocab", type=int, default=50257)
+    p.add_argument("--sample", action="store_true", help="top-k 50 / top-p 0.9 sampling instead of greedy")
+    p.add_argument("--skip-eager", action="store_true")
+    p.add_argument("--profile", action="store_true", help="print the per-kernel table of eager decode steps")
+    args = p.parse_args(argv)
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    model = KimiK3(profile_model_config("t4_wikitext", vocab_size=args.vocab)).to(dev).eval()
+    ids = torch.randint(3, args.vocab, (args.batch, args.prompt), device=dev)
+    cfg = GenerationConfig(max_new_tokens=args.new_tokens, do_sample=args.sample, top_k=50 if args.sample else None,
+                           top_p=0.9 if args.sample else None, seed=0)
+    rows = []
+
+    def run(name, fn, new_tokens):
+        fn()  # warm-up (and graph capture)
+        torch.cuda.synchronize()
+        out = fn()
+        torch.cuda.synchronize()
+        rows.append({"impl": name, "batch": args.batch, "prompt": args.prompt, "new_tokens": new_tokens,
+                     "prefill_ms": round(out.prefill_seconds * 1e3, 3),
+                     "decode_ms_per_token": round(out.decode_seconds * 1e3 / max(out.generated_tokens, 1), 4),
+                     "decode_tokens_per_s": round(out.batch_tokens_per_second, 1)})
+        print(json.dumps(rows[-1]))
+
+    dec = GraphDecoder(model, max_length=args.prompt + args.new_tokens, generation_config=cfg)
+    if args.profile:
+        from torch.profiler import ProfilerActivity, profile
+        eager_dec = GraphDecoder(model, max_length=args.prompt + 16, use_graph=False,
+                                 generation_config=GenerationConfig(max_new_tokens=2))
+        eager_dec.generate(ids)
+        with torch.inference_mode():
+            eager_dec._decode_step()
+            torch.cuda.synchronize()
+            with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA], record_shapes=True) as prof:
+                for _ in range(4):
+                    eager_dec._decode_step()
+                torch.cuda.synchronize()
+        print("four eager decode steps")
+        print(prof.key_averages(group_by_input_shape=True).table(sort_by="self_cuda_time_total", row_limit=30,
+                                                                 max_name_column_width=60,
+                                                                 max_shapes_column_width=80))
+    run("cuda_graph_decoder", lambda: dec.generate(ids), args.new_tokens)
+    if not args.skip_eager:
+        n = min(args.new_tokens, 32)
+        ecfg = GenerationConfig(max_new_tokens=n, do_sample=args.sample, top_k=cfg.top_k, top_p=cfg.top_p, seed=0)
+
+        def eager():
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                return generate_tokens(model, ids, generation_config=ecfg)
+        run("eager_reference_loop", eager, n)
+    return rows
+
+
+BENCHMARKS["decode"] = bench_decode

@@ -22,9 +22,11 @@ Off CUDA (or with ``use_graph=False``) the same step runs eagerly through the Py
 from __future__ import annotations
 
 import contextlib
+import copy
 import time
 
 import torch
+import torch.nn as nn
 
 from ..models.backbone import HybridBackboneCache, HybridLayerCache
 from ..models.kda import KDAState
@@ -35,6 +37,22 @@ from .cache import cache_summary
 from .config import GenerationConfig
 from .generation import GenerationOutput, last_prompt_logits
 from .sampling import sample_next_token
+
+
+def serving_copy(model: nn.Module, dtype: torch.dtype) -> nn.Module:
+    """A copy of ``model`` whose projection matrices (every ``nn.Linear`` weight and the stacked
+    routed-expert weights) are stored in ``dtype``, so decode steps under autocast read them
+    without a per-step cast.  Embeddings, norms, conv and decay parameters keep their dtype; a
+    LM head tied to the embedding gets its own ``dtype`` copy."""
+    from ..models.moe import GroupedRoutedExperts
+    m = copy.deepcopy(model)
+    for mod in m.modules():
+        if isinstance(mod, nn.Linear):
+            mod.weight = nn.Parameter(mod.weight.detach().to(dtype), requires_grad=False)
+        elif isinstance(mod, GroupedRoutedExperts):
+            for name in ("gate_proj", "up_proj", "down_proj"):
+                setattr(mod, name, nn.Parameter(getattr(mod, name).detach().to(dtype), requires_grad=False))
+    return m.eval()
 
 
 def _static_layer(lc: HybridLayerCache, max_length: int) -> HybridLayerCache:
@@ -67,17 +85,18 @@ class GraphDecoder:
 
     ``max_length`` bounds prompt + generated tokens (the MLA latent buffers are sized for it).
     ``autocast_dtype`` (bf16 by default on CUDA, None to disable) is the compute dtype of the
-    prefill and of every decode step."""
+    prefill and of every decode step; with it the decoder serves from :func:`serving_copy` of the
+    model (projection matrices stored in that dtype)."""
 
     def __init__(self, model, *, max_length: int, generation_config: GenerationConfig | None = None,
                  use_graph: bool | None = None, autocast_dtype: torch.dtype | None = torch.bfloat16):
-        self.model = model
         self.max_length = int(max_length)
         self.cfg = generation_config or GenerationConfig()
         dev = next(model.parameters()).device
         self.device = dev
         self.use_graph = (dev.type == "cuda") if use_graph is None else bool(use_graph and dev.type == "cuda")
         self.autocast_dtype = autocast_dtype if dev.type == "cuda" else None
+        self.model = serving_copy(model, self.autocast_dtype) if self.autocast_dtype is not None else model
         self.graph = None
         self.replays = 0
 
@@ -103,7 +122,9 @@ class GraphDecoder:
         pad = cfg.pad_token_id if cfg.pad_token_id is not None else cfg.eos_token_id
         if pad is not None:
             nxt = torch.where(self.finished, torch.full_like(nxt, int(pad)), nxt)
-        self.out.scatter_(1, self.step.view(1, 1).expand(nxt.shape[0], 1), nxt[:, None])
+        # the output column never leaves the buffer, however many steps a caller runs
+        col = self.step.clamp(max=self.out.shape[1] - 1)
+        self.out.scatter_(1, col.view(1, 1).expand(nxt.shape[0], 1), nxt[:, None])
         self.step.add_(1)
         if cfg.eos_token_id is not None:
             self.finished |= nxt.eq(int(cfg.eos_token_id))
@@ -242,4 +263,4 @@ def graph_generate(model, input_ids, *, max_length: int | None = None,
         input_ids, attention_mask)
 
 
-__all__ = ["GraphDecoder", "graph_generate"]
+__all__ = ["GraphDecoder", "graph_generate", "serving_copy"]

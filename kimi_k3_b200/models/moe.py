@@ -206,6 +206,27 @@ class SharedExpert(nn.Module):
 RoutedExpert = SharedExpert
 
 
+# Decode batches route at most this many (token, slot) rows: every expert is then applied to
+# every token with batched GEMMs and the unselected results get weight zero.  Reading all the
+# expert weights once is what the sparse path costs too at this size (almost every expert is
+# hit), and it needs no routing tables, no padding of expert segments and no host sync.
+_DENSE_DECODE_ROWS = 128
+
+
+def dense_small_batch_experts(latent, experts, selected, weights, accumulation_dtype):
+    """``sum_slot w[t, slot] * expert_{e[t, slot]}(x_t)`` for a small token batch (inference)."""
+    m = latent.shape[0]
+    e = experts.gate_proj.shape[0]
+    dense_w = torch.zeros(m, e, device=latent.device, dtype=accumulation_dtype)
+    dense_w.scatter_add_(1, selected.long(), weights.to(accumulation_dtype))
+    x = latent.unsqueeze(0).expand(e, m, latent.shape[1])
+    g = torch.bmm(x, experts.gate_proj.transpose(1, 2))
+    u = torch.bmm(x, experts.up_proj.transpose(1, 2))
+    h = situ_glu_activation(g, u, experts.beta_gate, experts.beta_up)
+    y = torch.bmm(h, experts.down_proj.transpose(1, 2))  # [E, m, L]
+    return torch.einsum("me,eml->ml", dense_w, y.to(accumulation_dtype))
+
+
 class GroupedRoutedExperts(nn.Module):
     """All routed SiTU-GLU experts as stacked weights for grouped GEMMs."""
 
@@ -480,6 +501,10 @@ class StableLatentMoE(nn.Module):
 
     # ---- routed path (overridable by expert parallelism)
     def routed_aggregate(self, latent, ro: RouterOutput, accumulation_dtype):
+        m, k = ro.selected_experts.shape
+        if latent.is_cuda and not torch.is_grad_enabled() and m * k <= _DENSE_DECODE_ROWS:
+            return dense_small_batch_experts(latent, self.routed_experts, ro.selected_experts, ro.selected_weights,
+                                             accumulation_dtype)
         if (_ops.use_kernels(latent) and accumulation_dtype == torch.float32 and latent.shape[-1] % 64 == 0
                 and self.config.routed_expert_hidden_dim % 128 == 0):
             return _ops.moe_grouped_experts(latent, ro.selected_experts, ro.selected_weights,
