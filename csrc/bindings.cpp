@@ -7,6 +7,13 @@
 
 #include <vector>
 
+#include <cstdio>
+#include <stdexcept>
+#include <string>
+#include <execinfo.h>
+#include <signal.h>
+#include <unistd.h>
+
 #include "kernels.h"
 #include "tc_gemm.h"
 #include "moe_route.h"
@@ -23,8 +30,16 @@ int dtype_code(const at::Tensor& t) {
   return -1;
 }
 
+// Failures are reported with plain std::string concatenation (no stream formatting) and also
+// written to stderr before the exception unwinds.
+[[noreturn]] void fail(const std::string& msg) {
+  fprintf(stderr, "kimi_k3_b200: %s\n", msg.c_str());
+  fflush(stderr);
+  throw std::runtime_error(msg);
+}
+
 void check(cudaError_t e, const char* what) {
-  TORCH_CHECK(e == cudaSuccess, what, " failed: ", cudaGetErrorString(e));
+  if (e != cudaSuccess) fail(std::string(what) + " failed: " + cudaGetErrorString(e));
 }
 
 // Kernels read and write with 16-byte vector accesses and bulk copies: every tensor they take is
@@ -620,9 +635,14 @@ std::vector<at::Tensor> tc_gemm_grouped(int64_t mode, at::Tensor a, at::Tensor b
   }
   g.num_sms = at::cuda::getDeviceProperties(a.get_device())->multiProcessorCount;
   const cudaError_t err = kimi::tc_gemm(g, stream());
-  TORCH_CHECK(err == cudaSuccess, "tc_gemm_grouped failed: ", cudaGetErrorString(err), " (mode ", mode, ", epi ", epi,
-              ", bn ", bn, ", M ", M, ", N ", N, ", K ", K, ", G ", G, ", a ", a.size(0), "x", a.size(1), " ld ",
-              a.stride(0), ", b ", b.sizes(), ", a_mn ", a_mn, ", b_mn ", b_mn, ")");
+  if (err != cudaSuccess) {
+    using std::to_string;
+    fail(std::string("tc_gemm_grouped failed: ") + cudaGetErrorString(err) + " (mode " + to_string(mode) + ", epi " +
+         to_string(epi) + ", bn " + to_string(bn) + ", M " + to_string(M) + ", N " + to_string(N) + ", K " +
+         to_string(K) + ", G " + to_string(G) + ", a " + to_string(a.size(0)) + "x" + to_string(a.size(1)) +
+         " ld " + to_string(a.stride(0)) + ", b dim " + to_string(b.dim()) + ", a_mn " + to_string(a_mn) +
+         ", b_mn " + to_string(b_mn) + ")");
+  }
   return outs;
 }
 
@@ -804,12 +824,178 @@ void seen_mark(at::Tensor seen, at::Tensor ids, int64_t vocab) {
         "seen_mark");
 }
 
+// ---------------------------------------------------------------- expert-parallel comm
+// `ptrs`: nine regions x world peer addresses, region-major (flags, counts, xs, row_token,
+// row_weight, agg, dagg, dxs, dw_row).
+kimi::EpPeers make_peers(const std::vector<int64_t>& ptrs, int64_t rank, int64_t world, at::Tensor status,
+                         int64_t timeout_ns) {
+  TORCH_CHECK(world >= 1 && world <= 8 && (int64_t)ptrs.size() == 9 * world && rank >= 0 && rank < world,
+              "expert-parallel peers: 9 regions x world (<= 8) pointers");
+  TORCH_CHECK(status.is_cuda() && status.scalar_type() == at::kInt, "status must be an int32 CUDA tensor");
+  kimi::EpPeers p;
+  p.rank = (int)rank;
+  p.world = (int)world;
+  for (int r = 0; r < world; ++r) {
+    p.flags[r] = reinterpret_cast<int*>(ptrs[0 * world + r]);
+    p.counts[r] = reinterpret_cast<int*>(ptrs[1 * world + r]);
+    p.xs[r] = reinterpret_cast<void*>(ptrs[2 * world + r]);
+    p.row_token[r] = reinterpret_cast<int*>(ptrs[3 * world + r]);
+    p.row_weight[r] = reinterpret_cast<float*>(ptrs[4 * world + r]);
+    p.agg[r] = reinterpret_cast<float*>(ptrs[5 * world + r]);
+    p.dagg[r] = reinterpret_cast<float*>(ptrs[6 * world + r]);
+    p.dxs[r] = reinterpret_cast<void*>(ptrs[7 * world + r]);
+    p.dw_row[r] = reinterpret_cast<float*>(ptrs[8 * world + r]);
+  }
+  p.status = status.data_ptr<int>();
+  p.timeout_ns = timeout_ns;
+  return p;
+}
+
+#define EP_PEER_ARGS std::vector<int64_t> ptrs, int64_t rank, int64_t world, at::Tensor status, int64_t timeout_ns
+#define EP_PEERS make_peers(ptrs, rank, world, status, timeout_ns)
+
+void ep_count(at::Tensor sel, int64_t E, at::Tensor cnt, at::Tensor agg) {
+  CHECK_CUDA_CONTIG(sel);
+  CHECK_CUDA_CONTIG(cnt);
+  CHECK_CUDA_CONTIG(agg);
+  TORCH_CHECK(sel.scalar_type() == at::kLong && cnt.scalar_type() == at::kInt && cnt.numel() >= E &&
+                  agg.scalar_type() == at::kFloat,
+              "ep_count: int64 selections, int32 counts, fp32 aggregate");
+  const at::cuda::CUDAGuard gd(sel.device());
+  check(kimi::ep_count(sel.data_ptr<int64_t>(), sel.numel(), (int)E, cnt.data_ptr<int>(), agg.data_ptr<float>(),
+                       agg.numel(), stream()),
+        "ep_count");
+}
+
+void ep_exchange(EP_PEER_ARGS, at::Tensor cnt, int64_t E, int64_t per, int64_t L, at::Tensor offsets_local,
+                 at::Tensor base, at::Tensor cursor) {
+  const at::cuda::CUDAGuard gd(cnt.device());
+  TORCH_CHECK(offsets_local.numel() == per + 1 && base.numel() >= E && cursor.numel() >= E, "ep_exchange shapes");
+  check(kimi::ep_exchange(EP_PEERS, cnt.data_ptr<int>(), (int)E, (int)per, (int)L, offsets_local.data_ptr<int>(),
+                          base.data_ptr<int>(), cursor.data_ptr<int>(), stream()),
+        "ep_exchange");
+}
+
+void ep_dispatch(EP_PEER_ARGS, at::Tensor latent, at::Tensor sel, at::Tensor w, int64_t E, int64_t per,
+                 at::Tensor base, at::Tensor cursor, at::Tensor slot_pos) {
+  latent = dense(latent);
+  auto wf = dense(w.to(at::kFloat));
+  CHECK_CUDA_CONTIG(sel);
+  TORCH_CHECK(latent.scalar_type() == at::kBFloat16 && latent.dim() == 2 && sel.scalar_type() == at::kLong &&
+                  sel.dim() == 2 && sel.size(0) == latent.size(0) && slot_pos.numel() == sel.numel(),
+              "ep_dispatch: bf16 latent [M, L], int64 selections [M, k]");
+  const at::cuda::CUDAGuard gd(latent.device());
+  check(kimi::ep_dispatch(EP_PEERS, latent.data_ptr(), sel.data_ptr<int64_t>(), wf.data_ptr<float>(),
+                          (int)latent.size(0), (int)sel.size(1), (int)E, (int)per, (int)latent.size(1),
+                          base.data_ptr<int>(), cursor.data_ptr<int>(), slot_pos.data_ptr<int>(), stream()),
+        "ep_dispatch");
+}
+
+int64_t ep_dispatch_grid(int64_t slots) { return kimi::ep_dispatch_grid(slots); }
+
+void ep_wait(EP_PEER_ARGS, int64_t kind, int64_t target) {
+  const at::cuda::CUDAGuard gd(status.device());
+  check(kimi::ep_wait(EP_PEERS, (int)kind, (uint32_t)target, stream()), "ep_wait");
+}
+
+void ep_signal_wait(EP_PEER_ARGS, int64_t kind) {
+  const at::cuda::CUDAGuard gd(status.device());
+  check(kimi::ep_signal_wait(EP_PEERS, (int)kind, stream()), "ep_signal_wait");
+}
+
+at::Tensor ep_dy(EP_PEER_ARGS, at::Tensor offsets_local, int64_t M, at::Tensor y) {
+  CHECK_CUDA_CONTIG(y);
+  TORCH_CHECK(y.scalar_type() == at::kBFloat16 && y.dim() == 2, "ep_dy: bf16 y [r_max, L]");
+  const at::cuda::CUDAGuard gd(y.device());
+  auto dy = at::empty_like(y);
+  const int per = (int)offsets_local.numel() - 1;
+  check(kimi::ep_dy(EP_PEERS, offsets_local.data_ptr<int>() + per, y.size(0), (int)M, (int)y.size(1), y.data_ptr(),
+                    dy.data_ptr(), stream()),
+        "ep_dy");
+  return dy;
+}
+
+std::vector<at::Tensor> ep_slot_sum(EP_PEER_ARGS, at::Tensor sel, at::Tensor slot_pos, int64_t E, int64_t per,
+                                    int64_t L, bool out_fp32) {
+  CHECK_CUDA_CONTIG(sel);
+  const at::cuda::CUDAGuard gd(sel.device());
+  const int64_t M = sel.size(0), k = sel.size(1);
+  auto dlat = at::empty({M, L}, sel.options().dtype(out_fp32 ? at::kFloat : at::kBFloat16));
+  auto dweights = at::empty({M, k}, sel.options().dtype(at::kFloat));
+  check(kimi::ep_slot_sum(EP_PEERS, sel.data_ptr<int64_t>(), slot_pos.data_ptr<int>(), (int)M, (int)k, (int)E,
+                          (int)per, (int)L, dlat.data_ptr(), out_fp32, dweights.data_ptr<float>(), stream()),
+        "ep_slot_sum");
+  return {dlat, dweights};
+}
+
+// Down-projection of the routed experts with the combine fused into the epilogue: row r adds
+// row_weight[r] * (a[r] @ b[g]^T) into agg_peers[row_token[r] / tokens_per_rank] at token
+// row_token[r] % tokens_per_rank (a peer's fp32 [tokens, N] aggregate, over NVLink).
+void tc_gemm_grouped_remote(at::Tensor a, at::Tensor b, at::Tensor offsets, int64_t M, int64_t N, int64_t K,
+                            at::Tensor row_token, at::Tensor row_weight, std::vector<int64_t> agg_peers,
+                            int64_t tokens_per_rank, int64_t bn) {
+  TORCH_CHECK(a.is_cuda() && a.dim() == 2 && a.stride(1) == 1 && a.stride(0) % 8 == 0, "a must be row-major");
+  CHECK_CUDA_CONTIG(b);
+  CHECK_CUDA_CONTIG(row_token);
+  CHECK_CUDA_CONTIG(row_weight);
+  TORCH_CHECK(!agg_peers.empty() && agg_peers.size() <= 8 && tokens_per_rank > 0, "agg_peers: 1..8 pointers");
+  const at::cuda::CUDAGuard gd(a.device());
+  kimi::TcGemmArgs g;
+  g.mode = 1;
+  g.bn = (int)bn;
+  g.a = a.data_ptr();
+  g.a_rows = a.size(0);
+  g.a_cols = a.size(1);
+  g.a_ld = a.stride(0);
+  g.b = b.data_ptr();
+  g.b_groups = b.size(0);
+  g.b_rows = b.size(1);
+  g.b_cols = b.size(2);
+  g.b_ld = b.size(2);
+  g.b_gstride = b.size(1) * b.size(2);
+  g.M = (int)M;
+  g.N = (int)N;
+  g.K = (int)K;
+  g.G = (int)offsets.numel() - 1;
+  g.offsets = offsets.data_ptr<int>();
+  g.epi = 2;
+  g.out = reinterpret_cast<void*>(agg_peers[0]);
+  g.out_fp32 = true;
+  g.ldc = N;
+  g.row_token = row_token.data_ptr<int>();
+  g.row_weight = row_weight.data_ptr<float>();
+  for (size_t r = 0; r < agg_peers.size(); ++r) g.agg_peer[r] = (uint64_t)agg_peers[r];
+  g.agg_tokens = (int)tokens_per_rank;
+  check(kimi::tc_gemm(g, stream()), "tc_gemm_grouped_remote");
+}
+
+}  // namespace
+
+namespace {
+// KIMI_K3_SEGV_TRACE=1: print the native stack of a segmentation fault (diagnostics only).
+void segv_trace(int sig) {
+  void* frames[64];
+  const int n = backtrace(frames, 64);
+  backtrace_symbols_fd(frames, n, 2);
+  signal(sig, SIG_DFL);
+  raise(sig);
+}
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "kimi_k3_b200 sm_100a kernels";
+  if (getenv("KIMI_K3_SEGV_TRACE")) signal(SIGSEGV, segv_trace);
   m.def("rms_norm_fwd", &rms_norm_fwd);
   m.def("conv_step", &conv_step);
+  m.def("ep_count", &ep_count);
+  m.def("ep_exchange", &ep_exchange);
+  m.def("ep_dispatch", &ep_dispatch);
+  m.def("ep_dispatch_grid", &ep_dispatch_grid);
+  m.def("ep_wait", &ep_wait);
+  m.def("ep_signal_wait", &ep_signal_wait);
+  m.def("ep_dy", &ep_dy);
+  m.def("ep_slot_sum", &ep_slot_sum);
+  m.def("tc_gemm_grouped_remote", &tc_gemm_grouped_remote);
   m.def("kda_decode", &kda_decode);
   m.def("mla_decode_supported", &mla_decode_supported);
   m.def("mla_decode", &mla_decode);

@@ -27,6 +27,8 @@
 // bounded by a time limit and reports through the status word.
 // TMA loads never use cluster multicast; every mbarrier wait is bounded (status word).
 #include <cuda.h>
+#include <cstdio>
+#include <cstdlib>
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
 
@@ -72,6 +74,10 @@ struct DevParams {
   float bg, bu;
   const int* row_token;
   const float* row_weight;
+  // Remote combine (epi 2): row_token = rank * agg_tokens + token selects rank's aggregate
+  // agg_peer[rank] (a peer's memory over NVLink); agg_tokens == 0 keeps the local `out`.
+  float* agg_peer[8];
+  int agg_tokens;
   int* status;
   CommParams cm;
 };
@@ -414,10 +420,19 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
             const int tok = p.row_token[row];
             if (tok >= 0) {
               const float w = p.row_weight[row];
-              float* o = reinterpret_cast<float*>(p.out) + (int64_t)tok * p.ldc;
+              if (p.agg_tokens > 0) {
+                // expert-parallel combine: add into the source rank's aggregate over NVLink;
+                // system-scope atomics, since experts on several ranks add into one row
+                float* o = p.agg_peer[tok / p.agg_tokens] + (int64_t)(tok % p.agg_tokens) * p.ldc;
 #pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (col0 + i < p.N) atomicAdd(o + col0 + i, w * v[i]);
+                for (int i = 0; i < 32; ++i)
+                  if (col0 + i < p.N) atomicAdd_system(o + col0 + i, w * v[i]);
+              } else {
+                float* o = reinterpret_cast<float*>(p.out) + (int64_t)tok * p.ldc;
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                  if (col0 + i < p.N) atomicAdd(o + col0 + i, w * v[i]);
+              }
             }
           }
         } else if (row_ok) {
@@ -584,10 +599,16 @@ bool make_map_2d(CUtensorMap* m, const void* ptr, uint64_t d0, uint64_t d1, uint
   return r == CUDA_SUCCESS;
 }
 
+bool debug_on() {
+  static const bool on = getenv("KIMI_K3_DEBUG") != nullptr;
+  return on;
+}
+
 template <int BN, bool AMN, bool BMN, int CM = 0>
 cudaError_t launch(const DevParams& dp, int num_sms, cudaStream_t s) {
   // an error left by an unrelated earlier call on this host thread is not this launch's
-  (void)cudaGetLastError();
+  const cudaError_t stale = cudaGetLastError();
+  if (debug_on() && stale != cudaSuccess) fprintf(stderr, "tc_gemm: stale error before launch: %s\n", cudaGetErrorString(stale));
   constexpr int STAGES = BN == 256 ? 4 : 6;
   constexpr int STAGE = BM * BK * 2 + BN * BK * 2;
   const size_t smem = 1024 + (size_t)STAGES * STAGE + (2 * STAGES + 4) * 8 + 16;
@@ -595,16 +616,35 @@ cudaError_t launch(const DevParams& dp, int num_sms, cudaStream_t s) {
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, AMN, BMN, CM>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (debug_on() && e != cudaSuccess) fprintf(stderr, "tc_gemm: smem attribute failed: %s\n", cudaGetErrorString(e));
     if (e != cudaSuccess) return e;
     configured = true;
   }
   gemm_tc_kernel<BN, AMN, BMN, CM><<<num_sms, CM ? 448 : 320, smem, s>>>(dp);
-  return cudaGetLastError();
+  const cudaError_t e = cudaGetLastError();
+  if (debug_on() && e != cudaSuccess) {
+    int dev = -1, maxs = -1;
+    cudaGetDevice(&dev);
+    cudaFuncAttributes fa{};
+    cudaFuncGetAttributes(&fa, gemm_tc_kernel<BN, AMN, BMN, CM>);
+    maxs = fa.maxDynamicSharedSizeBytes;
+    fprintf(stderr, "tc_gemm: launch failed: %s (device %d, grid %d, smem %zu, max dynamic smem %d, params %zu)\n",
+            cudaGetErrorString(e), dev, num_sms, smem, maxs, sizeof(DevParams));
+  }
+  return e;
 }
 
 }  // namespace
 
 cudaError_t tc_gemm(const TcGemmArgs& a, cudaStream_t stream) {
+  // The driver's tensor-map encoder needs the device's context current on this host thread; a
+  // thread whose first CUDA work is this call (an autograd worker entering a backward) has not
+  // bound it yet.  cudaFree(nullptr) binds it (once per thread).
+  static thread_local bool bound = false;
+  if (!bound) {
+    (void)cudaFree(nullptr);
+    bound = true;
+  }
   DevParams dp{};
   dp.mode = a.mode;
   dp.M = a.M;
@@ -624,13 +664,19 @@ cudaError_t tc_gemm(const TcGemmArgs& a, cudaStream_t stream) {
   dp.bu = a.bu;
   dp.row_token = a.row_token;
   dp.row_weight = a.row_weight;
+  dp.agg_tokens = a.agg_tokens;
+  for (int r = 0; r < 8; ++r) dp.agg_peer[r] = reinterpret_cast<float*>(a.agg_peer[r]);
+  if (a.agg_tokens > 0 && (a.epi != 2 || !a.agg_peer[0])) return cudaErrorInvalidValue;
   dp.status = a.status;
   const int bn = a.epi == 1 ? 256 : a.bn;
   if (bn != 128 && bn != 256) return cudaErrorInvalidValue;
   if (a.epi == 1 && (a.a_mn || a.b_mn || !a.b2)) return cudaErrorInvalidValue;
   // A: K-major storage [a_rows, a_cols=K]; MN-major storage [a_rows=K, a_cols=M]
   if (!a.a_mn) {
-    if (!make_map_2d(&dp.map_a, a.a, a.a_cols, a.a_rows, a.a_ld * 2, 64, 128)) return cudaErrorInvalidValue;
+    if (!make_map_2d(&dp.map_a, a.a, a.a_cols, a.a_rows, a.a_ld * 2, 64, 128)) {
+      if (debug_on()) fprintf(stderr, "tc_gemm: A tensor map failed\n");
+      return cudaErrorInvalidValue;
+    }
   } else {
     if (!make_map_2d(&dp.map_a, a.a, a.a_cols, a.a_rows, a.a_ld * 2, 64, 64)) return cudaErrorInvalidValue;
   }
@@ -648,7 +694,10 @@ cudaError_t tc_gemm(const TcGemmArgs& a, cudaStream_t stream) {
       ok = make_map(bmaps[i], bptrs[i], a.b_cols, a.b_rows, a.b_groups, a.b_ld * 2, a.b_gstride * 2, 64, bbox_rows);
     else
       ok = make_map(bmaps[i], bptrs[i], a.b_cols, a.b_rows, a.b_groups, a.b_ld * 2, a.b_gstride * 2, 64, 64);
-    if (!ok) return cudaErrorInvalidValue;
+    if (!ok) {
+      if (debug_on()) fprintf(stderr, "tc_gemm: B tensor map %d failed\n", i);
+      return cudaErrorInvalidValue;
+    }
   }
   int sms = a.num_sms > 0 ? a.num_sms : 148;
   if (a.comm_mode != 0) {

@@ -141,4 +141,33 @@ cudaError_t sample_tokens(int dtype, const void* logits, int batch, int vocab, c
 cudaError_t seen_mark(uint32_t* seen, int seen_words, const int64_t* ids, int64_t rows, int64_t cols, int64_t ld,
                       int vocab, cudaStream_t s);
 
+// ---------------------------------------------------------------- expert-parallel comm (ep_comm.cu)
+// Pointers into every rank's symmetric buffer (index = rank in the expert group).
+struct EpPeers {
+  int rank = 0, world = 1;
+  int* flags[8] = {};       // [kinds][8] counting semaphores
+  int* counts[8] = {};      // [world, E]
+  void* xs[8] = {};         // [r_max, L] bf16 expert-input rows
+  int* row_token[8] = {};   // [r_max]
+  float* row_weight[8] = {};
+  float* agg[8] = {};       // [M, L] fp32
+  float* dagg[8] = {};      // [M, L] fp32
+  void* dxs[8] = {};        // [r_max, L] bf16
+  float* dw_row[8] = {};    // [r_max]
+  int* status = nullptr;    // local
+  int64_t timeout_ns = 10000000000LL;
+};
+int ep_dispatch_grid(int64_t slots);
+cudaError_t ep_count(const int64_t* sel, int64_t n, int E, int* cnt, float* agg, int64_t agg_elems, cudaStream_t s);
+cudaError_t ep_exchange(const EpPeers& p, const int* cnt, int E, int per, int L, int* offsets_local, int* base,
+                        int* cursor, cudaStream_t s);
+cudaError_t ep_dispatch(const EpPeers& p, const void* latent, const int64_t* sel, const float* w, int M, int k, int E,
+                        int per, int L, const int* base, int* cursor, int* slot_pos, cudaStream_t s);
+cudaError_t ep_wait(const EpPeers& p, int kind, uint32_t target, cudaStream_t s);
+cudaError_t ep_signal_wait(const EpPeers& p, int kind, cudaStream_t s);
+cudaError_t ep_dy(const EpPeers& p, const int* offsets_total, int64_t r_max, int M, int L, const void* y, void* dy,
+                  cudaStream_t s);
+cudaError_t ep_slot_sum(const EpPeers& p, const int64_t* sel, const int* slot_pos, int M, int k, int E, int per, int L,
+                        void* dlat, bool out_fp32, float* dweights, cudaStream_t s);
+
 }  // namespace kimi

@@ -30,6 +30,9 @@ struct TcGemmArgs {
   float bg = 4.f, bu = 25.f;
   const int* row_token = nullptr;
   const float* row_weight = nullptr;
+  // epi 2 only: row_token = rank * agg_tokens + token adds into agg_peer[rank] (row stride ldc)
+  uint64_t agg_peer[8] = {};
+  int agg_tokens = 0;
   int* status = nullptr;
   int num_sms = 0;
   // Comm modes (dense, bf16 output, A K-major, N % 8 == 0): `out` / `ldc` must be this rank's

@@ -89,7 +89,10 @@ class TensorParallelConfig:
 class ExpertParallelConfig:
     enabled: bool = False
     size: int = 1
-    dispatch: Literal["all_to_all"] = "all_to_all"
+    # "all_to_all": NCCL all-to-alls (the reference's exchange); "nvlink_fused": device-initiated
+    # dispatch into the owners' grouped expert inputs and the combine fused into the expert
+    # down-GEMM epilogue, over symmetric memory (CUDA ranks of one NVLink domain)
+    dispatch: Literal["all_to_all", "nvlink_fused"] = "all_to_all"
     expert_placement: Literal["contiguous"] = "contiguous"
     shared_experts: Literal["replicated"] = "replicated"
     drop_tokens: bool = False

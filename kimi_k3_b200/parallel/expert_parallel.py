@@ -90,7 +90,7 @@ def exchange_counts(send_counts: torch.Tensor, group) -> list:
 class ExpertParallelMoE(StableLatentMoE):
     """A ``StableLatentMoE`` whose routed experts are split over an expert-parallel group."""
 
-    def __init__(self, module: StableLatentMoE, *, group=None, token_split: bool = False):
+    def __init__(self, module: StableLatentMoE, *, group=None, token_split: bool = False, fused_comm: bool = False):
         nn.Module.__init__(self)
         self.__dict__.update({k: v for k, v in module.__dict__.items() if k not in ("_modules", "_parameters",
                                                                                       "_buffers")})
@@ -114,6 +114,9 @@ class ExpertParallelMoE(StableLatentMoE):
         for p in local.parameters():
             p._kimi_local_expert = True
         self._qb_reducer = QBReducer(group)
+        # CUDA ranks: device-initiated NVLink exchange (``ep_fused``) instead of NCCL all-to-alls
+        self.fused_comm = bool(fused_comm)
+        self._ep_workspace = None
         # EP overlaid on TP: the group shares one token stream, so each rank takes a block of
         # the tokens, and the replicated MoE weights see only that block (sum over the group).
         self.token_split = bool(token_split)
@@ -157,9 +160,26 @@ class ExpertParallelMoE(StableLatentMoE):
                 return scores, cutoffs
         return super().finalize_and_commit_balance(_Chain(self._qb_reducer, reducer), keep_old=keep_old)
 
+    def _fused_workspace(self, tokens: int, top_k: int, latent: int):
+        from .ep_fused import EPWorkspace
+        ws = self._ep_workspace
+        if ws is None or ws.tokens != tokens or ws.top_k != top_k or ws.latent != latent:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("the expert-parallel workspace must exist before CUDA-graph capture")
+            ws = EPWorkspace(self.group, torch.device("cuda", torch.cuda.current_device()), tokens=tokens, top_k=top_k,
+                             latent=latent, num_experts=self.config.num_routed_experts)
+            self._ep_workspace = ws
+        return ws
+
     def routed_aggregate(self, latent, ro, accumulation_dtype):
         m, l = latent.shape
         k = ro.selected_experts.shape[1]
+        if (self.fused_comm and _ops.use_kernels(latent) and accumulation_dtype == torch.float32 and l % 64 == 0
+                and self.config.routed_expert_hidden_dim % 128 == 0):
+            from .ep_fused import fused_ep_experts
+            ws = self._fused_workspace(m, k, l)
+            return fused_ep_experts(latent, ro.selected_experts, ro.selected_weights, self.routed_experts, ws,
+                                    self.config.beta_gate, self.config.beta_up)
         group, world = self.group, group_size(self.group)
         per = self.expert_end - self.expert_start
         flat_e = ro.selected_experts.reshape(-1).long()
@@ -192,14 +212,15 @@ class ExpertParallelMoE(StableLatentMoE):
         return agg.index_add(0, flat_t[order], back)
 
 
-def shard_kimi_experts(model: nn.Module, *, group=None, token_split: bool = False) -> int:
+def shard_kimi_experts(model: nn.Module, *, group=None, token_split: bool = False, fused_comm: bool = False) -> int:
     """Replace every balanced StableLatentMoE by its expert-parallel form; returns the count."""
     raw = model.module if hasattr(model, "module") else model
     count = 0
     for parent in list(raw.modules()):
         for name, child in list(parent.named_children()):
             if isinstance(child, StableLatentMoE) and not isinstance(child, ExpertParallelMoE):
-                setattr(parent, name, ExpertParallelMoE(child, group=group, token_split=token_split))
+                setattr(parent, name, ExpertParallelMoE(child, group=group, token_split=token_split,
+                                                        fused_comm=fused_comm))
                 count += 1
     return count
 

@@ -205,7 +205,8 @@ def parallelize_kimi_model(model: nn.Module, config: DistributedConfig, context)
             _tag([raw.get_input_embeddings().weight, raw.get_output_embeddings().weight], _kimi_tp_shard=True)
     if config.enabled and config.expert_parallel.enabled:
         ep_layers = shard_kimi_experts(raw, group=context.ep_group,
-                                       token_split=config.expert_parallel.overlay_tensor_parallel)
+                                       token_split=config.expert_parallel.overlay_tensor_parallel,
+                                       fused_comm=config.expert_parallel.dispatch == "nvlink_fused")
     plan = ParallelPlan(raw, context, config, tp_layers, ep_layers, vocab)
     return plan
 
