@@ -585,3 +585,101 @@ def bench_decode(argv=None) -> list:
 
 
 BENCHMARKS["decode"] = bench_decode
+
+
+def bench_ep(argv=None) -> list:
+    """Expert-parallel routed experts, forward + backward, per rank ``--tokens`` tokens of width
+    ``--latent`` routed top-``--topk`` over ``--experts`` SiTU-GLU experts (hidden ``--hidden``)
+    split over all ranks.  Compares the device-initiated NVLink exchange (``ep_fused``: dispatch
+    into the owners' grouped inputs, combine in the down-GEMM epilogue) with the NCCL
+    all-to-all path of :class:`ExpertParallelMoE`.  Run under torchrun (one rank per GPU); times
+    are CUDA events on each rank, the max over ranks is reported."""
+    import datetime
+    import os
+    from types import SimpleNamespace
+    import torch.distributed as dist
+    from ..models.moe import GroupedRoutedExperts, StableLatentMoE  # noqa: F401
+    from ..parallel.ep_fused import EPWorkspace, fused_ep_experts
+    from ..parallel.expert_parallel import exchange_counts, _a2a
+    from .. import ops
+    p = argparse.ArgumentParser(description="expert-parallel exchange")
+    p.add_argument("--tokens", type=int, default=16384)
+    p.add_argument("--latent", type=int, default=320)
+    p.add_argument("--hidden", type=int, default=640)
+    p.add_argument("--experts", type=int, default=12)
+    p.add_argument("--topk", type=int, default=2)
+    p.add_argument("--repeats", type=int, default=20)
+    args = p.parse_args(argv)
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
+    dev = torch.device("cuda", torch.cuda.current_device())
+    if not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29533")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev,
+                                rank=rank, world_size=world)
+    m, l, h, e, k = args.tokens, args.latent, args.hidden, args.experts, args.topk
+    per = e // world
+    g = torch.Generator(device=dev).manual_seed(1 + rank)
+    x = torch.randn(m, l, device=dev, generator=g).bfloat16()
+    sel = torch.stack([torch.randperm(e, device=dev, generator=g)[:k] for _ in range(m)]) if m <= 4096 else \
+        torch.topk(torch.rand(m, e, device=dev, generator=g), k, -1).indices
+    w = torch.softmax(torch.randn(m, k, device=dev, generator=g), -1)
+    gw = torch.Generator(device=dev).manual_seed(0)
+    wg, wu, wd = (torch.randn(*s, device=dev, generator=gw) * 0.05 for s in ((per, h, l), (per, h, l), (per, l, h)))
+    dout = torch.randn(m, l, device=dev, generator=g)
+    ex = SimpleNamespace(gate_proj=wg.requires_grad_(), up_proj=wu.requires_grad_(), down_proj=wd.requires_grad_())
+    ws = EPWorkspace(None, dev, tokens=m, top_k=k, latent=l, num_experts=e)
+    xr, wr = x.clone().requires_grad_(), w.clone().requires_grad_()
+
+    def fused():
+        y = fused_ep_experts(xr, sel, wr, ex, ws, 4.0, 25.0)
+        y.backward(dout)
+
+    def nccl():
+        flat_e = sel.reshape(-1)
+        flat_t = torch.arange(m, device=dev).repeat_interleave(k)
+        owner = torch.div(flat_e, per, rounding_mode="floor")
+        order = torch.argsort(owner, stable=True)
+        send = torch.bincount(owner, minlength=world).to(torch.int64)
+        ins = send.tolist()
+        outs = exchange_counts(send, None)
+        rows = xr.index_select(0, flat_t[order])
+        meta = torch.stack(((flat_e[order] - owner[order] * per).float(), wr.reshape(-1)[order]), 1)
+        r_lat = _a2a(rows, outs, ins, None)
+        r_meta = _a2a(meta, outs, ins, None)
+        out = ops.moe_grouped_experts(r_lat, r_meta[:, 0].round().long()[:, None], r_meta[:, 1:2], ex.gate_proj,
+                                      ex.up_proj, ex.down_proj, 4.0, 25.0)
+        back = _a2a(out, ins, outs, None)
+        y = torch.zeros(m, l, device=dev).index_add(0, flat_t[order], back)
+        y.backward(dout)
+
+    rows_out = []
+    for name, fn in (("nvlink_fused", fused), ("nccl_all_to_all", nccl)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.repeats):
+            fn()
+        t1.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([t0.elapsed_time(t1) / args.repeats], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        dist.barrier()
+        rows_out.append({"bench": "ep", "impl": name, "ranks": world, "tokens_per_rank": m, "latent": l,
+                         "hidden": h, "experts": e, "top_k": k, "fwd_bwd_ms_max_over_ranks": round(ms.item(), 4),
+                         "bytes_crossing_nvlink_per_rank_fwd": int(m * k * (world - 1) / world * (l * 2 + l * 4))})
+        if rank == 0:
+            print(json.dumps(rows_out[-1]), flush=True)
+    ws.check()
+    del ws
+    dist.barrier()
+    dist.destroy_process_group()
+    return rows_out
+
+
+BENCHMARKS["ep"] = bench_ep
