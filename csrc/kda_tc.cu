@@ -686,11 +686,23 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_fwd_tc_kernel(const __grid_c
       }
     }
     __syncthreads();
-    // operands, elementwise outputs and the solve's right-hand side [k e^G | v]
-    for (int idx = tid; idx < 64 * 64; idx += NTH) {
+    // operands, elementwise outputs and the solve's right-hand side [k e^G | v]; every load of the
+    // chunk is issued before the first store, so the loads overlap instead of paying one
+    // round trip per element group
+    float kr[16], qr[16], vr[16];
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      const int idx = tid + n * NTH, i = idx >> 6, d = idx & 63;
+      kr[n] = to_f<T>(k[i * rs + d]);
+      qr[n] = to_f<T>(q[i * rs + d]);
+      vr[n] = to_f<T>(v[i * rs + d]);
+    }
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      const int idx = tid + n * NTH;
       const int i = idx >> 6, d = idx & 63;
       const float G = sG[i * LDP + d], r = sG[(i & ~15) * LDP + d], GC = sG[63 * LDP + d];
-      const float kv = to_f<T>(k[i * rs + d]), qv = to_f<T>(q[i * rs + d]);
+      const float kv = kr[n], qv = qr[n];
       const float e = expf(G - r);
       tcs::st(tQK, 128, i, d, kv * e);
       tcs::st(tQK, 128, 64 + i, d, qv * e);
@@ -701,7 +713,7 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_fwd_tc_kernel(const __grid_c
       a.buf.Qg[bo + idx] = qv * eG;
       a.buf.Kend[bo + idx] = kv * expf(GC - G);
       rhs[i * 128 + d] = kv * eG;
-      rhs[i * 128 + 64 + d] = to_f<T>(v[i * rs + d]);
+      rhs[i * 128 + 64 + d] = vr[n];
       if (i == 0) a.buf.eGC[((int64_t)bh * NC + c) * 64 + d] = expf(GC);
     }
     tcs::operands_ready();
@@ -785,32 +797,6 @@ constexpr size_t kFwdSmem = 1024 + 128 * KB + (size_t)(C * LDP + C * LDT + C) * 
 //                                                          MMA-b  [Qg^T | -W^T] x [dO^T | dV'^T]^T
 constexpr int ST_TILE = 64 * KB;  // R128 x K128 fp32 operand
 
-// rows [row0, row0+64) x k [k0, k0+64) of a K-major tile <- scale * src^T (src: 64 x 64, row stride ld)
-template <typename S>
-KIMI_D void tile_T(float* tile, int R, int row0, int k0, const S* src, int64_t ld, float scale, bool valid) {
-#pragma unroll 4
-  for (int idx = threadIdx.x; idx < 64 * 16; idx += NTH) {
-    const int r = idx >> 4, c4 = (idx & 15) * 4;
-    float x[4] = {0.f, 0.f, 0.f, 0.f};
-    if (valid) {
-      const S* p = src + r * ld + c4;
-#pragma unroll
-      for (int u = 0; u < 4; ++u) x[u] = scale * to_f<S>(p[u]);
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) tcs::st(tile, R, row0 + c4 + u, k0 + r, x[u]);
-  }
-}
-// rows [row0, row0+64) x k [k0, k0+64) <- src (64 x 64 fp32, contiguous)
-KIMI_D void tile_N(float* tile, int R, int row0, int k0, const float* src, bool valid) {
-#pragma unroll 4
-  for (int idx = threadIdx.x; idx < 64 * 16; idx += NTH) {
-    const int r = idx >> 4, c4 = (idx & 15) * 4;
-    const float4 x = valid ? *reinterpret_cast<const float4*>(src + r * 64 + c4) : make_float4(0.f, 0.f, 0.f, 0.f);
-    tcs::st4(tile, R, row0 + r, k0 + c4, x);
-  }
-}
-
 struct StateArgs {
   KdaBuffers buf;
   const void* x;      // forward: h0 (fp32, may be null); backward: dout (T)
@@ -868,13 +854,35 @@ __global__ void __launch_bounds__(NTH, 1) kda_state_fwd_tc_kernel(const __grid_c
     }
 #pragma unroll
     for (int u = 0; u < 32; ++u) tcs::st(tSV, 128, 64 * sq + c0 + u, r, S[u]);
+    {  // W, Qg, P, Kend of both sequences: 32 float4 loads in flight per thread, then the stores
+      float4 ld[2][4][4];
 #pragma unroll
-    for (int s2 = 0; s2 < 2; ++s2) {
-      const int64_t bo = ((int64_t)(bh0 + s2) * NC + c) * 4096;
-      tile_N(tW, 128, 64 * s2, 0, a.buf.W + bo, valid[s2]);
-      tile_N(tQP, 128, 64 * s2, 0, a.buf.Qg + bo, valid[s2]);
-      tile_N(tQP, 128, 64 * s2, 64, a.buf.P + bo, valid[s2]);
-      tile_T<float>(tKT, 128, 64 * s2, 0, a.buf.Kend + bo, 64, 1.f, valid[s2]);
+      for (int s2 = 0; s2 < 2; ++s2) {
+        const int64_t bo = ((int64_t)(bh0 + s2) * NC + c) * 4096;
+        const float* srcs[4] = {a.buf.W + bo, a.buf.Qg + bo, a.buf.P + bo, a.buf.Kend + bo};
+#pragma unroll
+        for (int t4 = 0; t4 < 4; ++t4)
+#pragma unroll
+          for (int n = 0; n < 4; ++n) {
+            const int idx = tid + n * NTH, rr = idx >> 4, cc = (idx & 15) * 4;
+            ld[s2][t4][n] = valid[s2] ? *reinterpret_cast<const float4*>(srcs[t4] + rr * 64 + cc)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+      }
+#pragma unroll
+      for (int s2 = 0; s2 < 2; ++s2)
+#pragma unroll
+        for (int n = 0; n < 4; ++n) {
+          const int idx = tid + n * NTH, rr = idx >> 4, cc = (idx & 15) * 4;
+          tcs::st4(tW, 128, 64 * s2 + rr, cc, ld[s2][0][n]);
+          tcs::st4(tQP, 128, 64 * s2 + rr, cc, ld[s2][1][n]);
+          tcs::st4(tQP, 128, 64 * s2 + rr, 64 + cc, ld[s2][2][n]);
+          const float4 kt = ld[s2][3][n];  // Kend row rr, columns cc..cc+3 -> transposed rows
+          tcs::st(tKT, 128, 64 * s2 + cc, rr, kt.x);
+          tcs::st(tKT, 128, 64 * s2 + cc + 1, rr, kt.y);
+          tcs::st(tKT, 128, 64 * s2 + cc + 2, rr, kt.z);
+          tcs::st(tKT, 128, 64 * s2 + cc + 3, rr, kt.w);
+        }
     }
     tcs::operands_ready();
     if (tid == 0) {
@@ -885,10 +893,14 @@ __global__ void __launch_bounds__(NTH, 1) kda_state_fwd_tc_kernel(const __grid_c
     const int64_t bo = ((int64_t)my_bh * NC + c) * 4096;
     {  // V' = U - W S  (row i = r of sequence sq)
       float val[32];
+      float4 ur[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        ur[u] = mine ? *reinterpret_cast<const float4*>(a.buf.U + bo + r * 64 + c0 + 4 * u) : make_float4(0, 0, 0, 0);
       tcs::tmem_row32(tm, warp, 64 * sq + c0, val);
 #pragma unroll
       for (int u = 0; u < 32; u += 4) {
-        float4 uu = mine ? *reinterpret_cast<const float4*>(a.buf.U + bo + r * 64 + c0 + u) : make_float4(0, 0, 0, 0);
+        const float4 uu = ur[u / 4];
         const float4 vp = make_float4(uu.x - val[u], uu.y - val[u + 1], uu.z - val[u + 2], uu.w - val[u + 3]);
         if (mine) *reinterpret_cast<float4*>(a.buf.Vp + bo + r * 64 + c0 + u) = vp;
         tcs::st(tSV, 128, 64 * sq + c0 + u, 64 + r, vp.x);
@@ -980,11 +992,39 @@ __global__ void __launch_bounds__(NTH, 1) kda_state_bwd_tc_kernel(const __grid_c
       const int64_t bo = ((int64_t)bh * NC + c) * 4096;
       const int bb = valid[s2] ? bh / a.H : 0, hh = valid[s2] ? bh % a.H : 0;
       const T* dO = dout + (((int64_t)bb * a.Tp + c * 64) * a.H + hh) * 64;
-      tile_T<float>(tA, 128, 64 * s2, 0, a.buf.P + bo, 64, 1.f, valid[s2]);
-      tile_N(tA, 128, 64 * s2, 64, a.buf.Kend + bo, valid[s2]);
-      tile_T<T>(tB, 128, 64 * s2, 0, dO, rs, 1.f, valid[s2]);
-      tile_T<float>(tC, 128, 64 * s2, 0, a.buf.Qg + bo, 64, 1.f, valid[s2]);
-      tile_T<float>(tC, 128, 64 * s2, 64, a.buf.W + bo, 64, -1.f, valid[s2]);
+      // the five operand tiles of this sequence: 20 loads in flight per thread, then the stores
+      float4 ld[5][4];
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        const int idx = tid + n * NTH, rr = idx >> 4, cc = (idx & 15) * 4;
+        const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+        ld[0][n] = valid[s2] ? *reinterpret_cast<const float4*>(a.buf.P + bo + rr * 64 + cc) : z;
+        ld[1][n] = valid[s2] ? *reinterpret_cast<const float4*>(a.buf.Kend + bo + rr * 64 + cc) : z;
+        if (valid[s2]) {
+          const T* pd = dO + rr * rs + cc;
+          ld[2][n] = make_float4(to_f<T>(pd[0]), to_f<T>(pd[1]), to_f<T>(pd[2]), to_f<T>(pd[3]));
+        } else {
+          ld[2][n] = z;
+        }
+        ld[3][n] = valid[s2] ? *reinterpret_cast<const float4*>(a.buf.Qg + bo + rr * 64 + cc) : z;
+        ld[4][n] = valid[s2] ? *reinterpret_cast<const float4*>(a.buf.W + bo + rr * 64 + cc) : z;
+      }
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        const int idx = tid + n * NTH, rr = idx >> 4, cc = (idx & 15) * 4;
+        tcs::st4(tA, 128, 64 * s2 + rr, 64 + cc, ld[1][n]);  // Kend
+        const float vP[4] = {ld[0][n].x, ld[0][n].y, ld[0][n].z, ld[0][n].w};
+        const float vD[4] = {ld[2][n].x, ld[2][n].y, ld[2][n].z, ld[2][n].w};
+        const float vQ[4] = {ld[3][n].x, ld[3][n].y, ld[3][n].z, ld[3][n].w};
+        const float vW[4] = {ld[4][n].x, ld[4][n].y, ld[4][n].z, ld[4][n].w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {  // transposed tiles: source column cc + u -> tile row
+          tcs::st(tA, 128, 64 * s2 + cc + u, rr, vP[u]);
+          tcs::st(tB, 128, 64 * s2 + cc + u, rr, vD[u]);
+          tcs::st(tC, 128, 64 * s2 + cc + u, rr, vQ[u]);
+          tcs::st(tC, 128, 64 * s2 + cc + u, 64 + rr, -vW[u]);
+        }
+      }
     }
     tcs::operands_ready();
     if (tid == 0) {
