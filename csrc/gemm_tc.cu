@@ -420,18 +420,25 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
             const int tok = p.row_token[row];
             if (tok >= 0) {
               const float w = p.row_weight[row];
+              // four columns per vector reduction (ldc and N are multiples of 4)
               if (p.agg_tokens > 0) {
                 // expert-parallel combine: add into the source rank's aggregate over NVLink;
-                // system-scope atomics, since experts on several ranks add into one row
+                // system scope, since experts on several ranks add into one row
                 float* o = p.agg_peer[tok / p.agg_tokens] + (int64_t)(tok % p.agg_tokens) * p.ldc;
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                  if (col0 + i < p.N) atomicAdd_system(o + col0 + i, w * v[i]);
+                for (int i = 0; i < 32; i += 4)
+                  if (col0 + i < p.N)
+                    asm volatile("red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(o + col0 + i),
+                                 "f"(w * v[i]), "f"(w * v[i + 1]), "f"(w * v[i + 2]), "f"(w * v[i + 3])
+                                 : "memory");
               } else {
                 float* o = reinterpret_cast<float*>(p.out) + (int64_t)tok * p.ldc;
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                  if (col0 + i < p.N) atomicAdd(o + col0 + i, w * v[i]);
+                for (int i = 0; i < 32; i += 4)
+                  if (col0 + i < p.N)
+                    asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(o + col0 + i),
+                                 "f"(w * v[i]), "f"(w * v[i + 1]), "f"(w * v[i + 2]), "f"(w * v[i + 3])
+                                 : "memory");
               }
             }
           }
@@ -667,6 +674,7 @@ cudaError_t tc_gemm(const TcGemmArgs& a, cudaStream_t stream) {
   dp.agg_tokens = a.agg_tokens;
   for (int r = 0; r < 8; ++r) dp.agg_peer[r] = reinterpret_cast<float*>(a.agg_peer[r]);
   if (a.agg_tokens > 0 && (a.epi != 2 || !a.agg_peer[0])) return cudaErrorInvalidValue;
+  if (a.epi == 2 && (a.N % 4 || a.ldc % 4 || (reinterpret_cast<uintptr_t>(a.out) & 15))) return cudaErrorInvalidValue;
   dp.status = a.status;
   const int bn = a.epi == 1 ? 256 : a.bn;
   if (bn != 128 && bn != 256) return cudaErrorInvalidValue;

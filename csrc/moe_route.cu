@@ -91,7 +91,8 @@ __global__ void gather_kernel(const T* __restrict__ latent, const int* __restric
   }
 }
 
-// One warp per row.
+// One warp per row; each lane handles 8 consecutive columns per step (two float4 of dagg, one
+// 16-byte vector of y and of dy).
 template <typename T>
 __global__ void dy_kernel(const float* __restrict__ dagg, const int* __restrict__ row_token,
                           const float* __restrict__ row_weight, const T* __restrict__ y, T* __restrict__ dy,
@@ -101,47 +102,86 @@ __global__ void dy_kernel(const float* __restrict__ dagg, const int* __restrict_
        r += (int64_t)gridDim.x * (blockDim.x >> 5)) {
     const int t = row_token[r];
     float acc = 0.f;
-    if (t >= 0) {
-      const float w = row_weight[r];
-      for (int c = lane; c < L; c += 32) {
-        const float g = dagg[(int64_t)t * L + c];
-        acc += g * to_f<T>(y[r * L + c]);
-        dy[r * L + c] = from_f<T>(w * g);
+    const float w = t >= 0 ? row_weight[r] : 0.f;
+    for (int c = lane * 8; c < L; c += 256) {
+      Vec<T> out;
+      if (t >= 0) {
+        const float4 g0 = *reinterpret_cast<const float4*>(dagg + (int64_t)t * L + c);
+        const float4 g1 = *reinterpret_cast<const float4*>(dagg + (int64_t)t * L + c + 4);
+        Vec<T> yv;
+        yv.load(y + r * L + c);
+        const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          acc += gv[e] * yv.f(e);
+          out.set(e, w * gv[e]);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) out.set(e, 0.f);
       }
-    } else {
-      for (int c = lane; c < L; c += 32) dy[r * L + c] = from_f<T>(0.f);
+      out.store(dy + r * L + c);
     }
     acc = warp_sum(acc);
     if (lane == 0) dw_row[r] = t >= 0 ? acc : 0.f;
   }
 }
 
+// 8 columns of one token per thread: sum of its k slot rows.
 template <typename T, typename TO>
 __global__ void slot_sum_kernel(const T* __restrict__ dxs, const int* __restrict__ row_of, TO* __restrict__ out,
                                 int64_t M, int k, int L) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < M * L; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t t = i / L;
-    const int c = (int)(i % L);
-    float acc = 0.f;
+  const int nv = L / 8;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < M * nv; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / nv;
+    const int c = (int)(i % nv) * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int j = 0; j < k; ++j) {
       const int r = row_of[t * k + j];
-      if (r >= 0) acc += to_f<T>(dxs[(int64_t)r * L + c]);
+      if (r < 0) continue;
+      Vec<T> v;
+      v.load(dxs + (int64_t)r * L + c);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += v.f(e);
     }
-    out[i] = from_f<TO>(acc);
+    TO* o = out + t * L + c;
+    if constexpr (sizeof(TO) == 4) {
+      reinterpret_cast<float4*>(o)[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      reinterpret_cast<float4*>(o)[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    } else {
+      Vec<TO> v;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v.set(e, acc[e]);
+      v.store(o);
+    }
   }
 }
 
+// 8 consecutive hidden units per thread (H % 8 == 0): one 16-byte load of each input and one
+// 16-byte store into each half of the [dGate | dUp] row.
 template <typename T>
 __global__ void situ_bwd_cat_kernel(const T* __restrict__ dh, const T* __restrict__ g, const T* __restrict__ u,
                                     T* __restrict__ dgu, int64_t rows, int H, float bg, float bu) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < rows * H; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / H;
-    const int c = (int)(i % H);
-    const float gv = to_f<T>(g[i]), uv = to_f<T>(u[i]), d = to_f<T>(dh[i]);
-    const float tg = tanhf(gv / bg), tu = tanhf(uv / bu), sg = sigmoidf_(gv);
-    const float cg = bg * tg, cu = bu * tu;
-    dgu[r * 2 * H + c] = from_f<T>(d * cu * ((1.f - tg * tg) * sg + cg * sg * (1.f - sg)));
-    dgu[r * 2 * H + H + c] = from_f<T>(d * cg * sg * (1.f - tu * tu));
+  const int nv = H / 8;
+  const float ibg = 1.f / bg, ibu = 1.f / bu;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < rows * nv; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / nv;
+    const int c = (int)(i % nv) * 8;
+    const int64_t src = r * H + c;
+    Vec<T> gv, uv, dv, og, ou;
+    gv.load(g + src);
+    uv.load(u + src);
+    dv.load(dh + src);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float gg = gv.f(e), uu = uv.f(e), d = dv.f(e);
+      const float tg = tanhf(gg * ibg), tu = tanhf(uu * ibu), sg = sigmoidf_(gg);
+      const float cg = bg * tg, cu = bu * tu;
+      og.set(e, d * cu * ((1.f - tg * tg) * sg + cg * sg * (1.f - sg)));
+      ou.set(e, d * cg * sg * (1.f - tu * tu));
+    }
+    og.store(dgu + r * 2 * H + c);
+    ou.store(dgu + r * 2 * H + H + c);
   }
 }
 
@@ -173,6 +213,7 @@ cudaError_t moe_gather(const void* latent, const int* row_token, void* xs, int64
 
 cudaError_t moe_dy(const float* dagg, const int* row_token, const float* row_weight, const void* y, void* dy,
                    float* dw_row, int64_t r_max, int L, cudaStream_t s) {
+  if (L % 8) return cudaErrorInvalidValue;
   dy_kernel<__nv_bfloat16><<<grid_of(r_max * 32, 256), 256, 0, s>>>(dagg, row_token, row_weight,
                                                                     (const __nv_bfloat16*)y, (__nv_bfloat16*)dy,
                                                                     dw_row, r_max, L);
@@ -181,18 +222,20 @@ cudaError_t moe_dy(const float* dagg, const int* row_token, const float* row_wei
 
 cudaError_t moe_slot_sum(const void* dxs, const int* row_of, void* out, bool out_fp32, int64_t M, int k, int L,
                          cudaStream_t s) {
+  if (L % 8) return cudaErrorInvalidValue;
   if (out_fp32)
-    slot_sum_kernel<__nv_bfloat16, float><<<grid_of(M * L, 256), 256, 0, s>>>((const __nv_bfloat16*)dxs, row_of,
+    slot_sum_kernel<__nv_bfloat16, float><<<grid_of(M * L / 8, 256), 256, 0, s>>>((const __nv_bfloat16*)dxs, row_of,
                                                                              (float*)out, M, k, L);
   else
-    slot_sum_kernel<__nv_bfloat16, __nv_bfloat16><<<grid_of(M * L, 256), 256, 0, s>>>(
+    slot_sum_kernel<__nv_bfloat16, __nv_bfloat16><<<grid_of(M * L / 8, 256), 256, 0, s>>>(
         (const __nv_bfloat16*)dxs, row_of, (__nv_bfloat16*)out, M, k, L);
   return cudaGetLastError();
 }
 
 cudaError_t situ_bwd_cat(const void* dh, const void* g, const void* u, void* dgu, int64_t rows, int H, float bg,
                          float bu, cudaStream_t s) {
-  situ_bwd_cat_kernel<__nv_bfloat16><<<grid_of(rows * H, 256), 256, 0, s>>>(
+  if (H % 8) return cudaErrorInvalidValue;
+  situ_bwd_cat_kernel<__nv_bfloat16><<<grid_of(rows * H / 8, 256), 256, 0, s>>>(
       (const __nv_bfloat16*)dh, (const __nv_bfloat16*)g, (const __nv_bfloat16*)u, (__nv_bfloat16*)dgu, rows, H, bg,
       bu);
   return cudaGetLastError();

@@ -370,19 +370,19 @@ class _MoEGrouped(torch.autograd.Function):
         xs, gg, uu, hh, wg, wu, wd, offsets, row_token, row_weight, row_of = ctx.saved_tensors
         m, k, e, h, l, r_max, bg, bu, ldt, wdt = ctx.c
         y, = C.tc_gemm_grouped(1, hh, wd, None, False, False, offsets, r_max, l, h, 0, None, False, bg, bu, None, None,
-                               0, 128)
+                               0, 256)
         dy, dw_row = C.moe_dy(dagg, row_token, row_weight, y)
         dh, = C.tc_gemm_grouped(1, dy, wd, None, False, True, offsets, r_max, h, l, 0, None, False, bg, bu, None, None,
-                                0, 128)
+                                0, 256)
         dwd, = C.tc_gemm_grouped(2, dy, hh, None, True, True, offsets, l, h, r_max, 0, None, True, bg, bu, None, None,
-                                 0, 128)
+                                 0, 256)
         dgu = C.situ_bwd_cat(dh, gg, uu, bg, bu)
         dxs, = C.tc_gemm_grouped(1, dgu, wg, wu, False, True, offsets, r_max, l, 2 * h, 0, None, False, bg, bu, None,
-                                 None, h, 128)
+                                 None, h, 256)
         dwg, = C.tc_gemm_grouped(2, dgu[:, :h], xs, None, True, True, offsets, h, l, r_max, 0, None, True, bg, bu,
-                                 None, None, 0, 128)
+                                 None, None, 0, 256)
         dwu, = C.tc_gemm_grouped(2, dgu[:, h:], xs, None, True, True, offsets, h, l, r_max, 0, None, True, bg, bu,
-                                 None, None, 0, 128)
+                                 None, None, 0, 256)
         dlat = C.moe_slot_sum(dxs, row_of, m, k, ldt == torch.float32)
         dweights = dw_row.index_select(0, row_of.long().clamp_min(0)).view(m, k)
         return dlat.to(ldt), dweights, None, dwg.to(wdt), dwu.to(wdt), dwd.to(wdt), None, None
@@ -449,8 +449,10 @@ class _LinearCE(torch.autograd.Function):
             lg = buf[: e - s, :v]
             C.tc_gemm_dense(hc, wd, False, False, False, 256, lg)
             loss += C.ce_rows(lg, v, targets[s:e], valid[s:e], 1.0).sum()
-            C.tc_gemm_dense(lg, wd, False, True, False, 128, dh[s:e])
-            part = C.tc_gemm_dense(lg, hc, True, True, True, 128, None)
+            # BN = 256 for all three products: 1.08 / 1.05 ms vs 1.52 / 1.46 ms with BN = 128 for dh / dW
+            # at 16384 x 50257 x 640 on B200
+            C.tc_gemm_dense(lg, wd, False, True, False, 256, dh[s:e])
+            part = C.tc_gemm_dense(lg, hc, True, True, True, 256, None)
             dw = part if dw is None else dw.add_(part)
         ctx.save_for_backward(dh, dw)
         ctx.w_dtype = w.dtype

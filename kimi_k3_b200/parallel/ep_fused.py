@@ -146,19 +146,19 @@ class _EPFusedExperts(torch.autograd.Function):
         ws.dagg.copy_(dagg)
         C.ep_signal_wait(*pa, 3)
         y, = C.tc_gemm_grouped(1, hh, wd, None, False, False, offs, ws.r_max, l, h, 0, None, False, bg, bu, None,
-                               None, 0, 128)
+                               None, 0, 256)
         dy = C.ep_dy(*pa, offs, m, y)
         dh, = C.tc_gemm_grouped(1, dy, wd, None, False, True, offs, ws.r_max, h, l, 0, None, False, bg, bu, None,
-                                None, 0, 128)
+                                None, 0, 256)
         dwd, = C.tc_gemm_grouped(2, dy, hh, None, True, True, offs, l, h, ws.r_max, 0, None, True, bg, bu, None,
-                                 None, 0, 128)
+                                 None, 0, 256)
         dgu = C.situ_bwd_cat(dh, gg, uu, bg, bu)
         C.tc_gemm_grouped(1, dgu, wg, wu, False, True, offs, ws.r_max, l, 2 * h, 0, ws.dxs, False, bg, bu, None,
-                          None, h, 128)
+                          None, h, 256)
         dwg, = C.tc_gemm_grouped(2, dgu[:, :h], ws.xs, None, True, True, offs, h, l, ws.r_max, 0, None, True, bg,
-                                 bu, None, None, 0, 128)
+                                 bu, None, None, 0, 256)
         dwu, = C.tc_gemm_grouped(2, dgu[:, h:], ws.xs, None, True, True, offs, h, l, ws.r_max, 0, None, True, bg,
-                                 bu, None, None, 0, 128)
+                                 bu, None, None, 0, 256)
         C.ep_signal_wait(*pa, 4)
         dlat, dweights = C.ep_slot_sum(*pa, sel, slot_pos, ws.num_experts, ws.per, l, ldt == torch.float32)
         return (dlat.to(ldt), dweights, None, dwg.to(wdt), dwu.to(wdt), dwd.to(wdt), None, None, None)
