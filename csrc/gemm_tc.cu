@@ -235,8 +235,22 @@ __device__ __forceinline__ int tile_owner(const CommParams& c, int tile, int m0)
   return (int)((tile % gridDim.x + tile / gridDim.x) % c.world);
 }
 
-__device__ __forceinline__ float situ_fwd(float g, float u, float bg, float bu) {
-  return bg * tanhf(g / bg) * (1.f / (1.f + expf(-g))) * bu * tanhf(u / bu);
+// SiTU-GLU in the GEMM epilogue, with the hardware approximations of tanh and 2^x (MUFU; relative
+// error near 2^-11, below the bf16 rounding of the stored result).  The epilogue evaluates this
+// once per output element and is otherwise the bottleneck of the short-K expert GEMM; the
+// backward recomputes the derivative from the stored bf16 gate / up values.
+__device__ __forceinline__ float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float sigmoid_approx(float x) {
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-1.4426950408889634f * x));  // e^{-x} = 2^{-x log2 e}
+  return __frcp_rn(1.f + e);
+}
+__device__ __forceinline__ float situ_fwd(float g, float u, float bg, float bu, float ibg, float ibu) {
+  return bg * tanh_approx(g * ibg) * sigmoid_approx(g) * bu * tanh_approx(u * ibu);
 }
 
 template <int BN>
@@ -366,6 +380,7 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
     const int sub = warp & 3;
     const int r_local = sub * 32 + lane;
     const int chalf = (warp - 2) >> 2;  // column half of the tile handled by this warpgroup
+    const float ibg = 1.f / p.bg, ibu = 1.f / p.bu;
     int it = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
       const TileInfo ti = p.situ ? tile_info<BN / 2>(p, tile) : tile_info<BN>(p, tile);
@@ -407,7 +422,7 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
                   const float uq = to_f<__nv_bfloat16>(from_f<__nv_bfloat16>(u[i + j]));
                   vg.v[j] = from_f<__nv_bfloat16>(gq);
                   vu.v[j] = from_f<__nv_bfloat16>(uq);
-                  vh.v[j] = from_f<__nv_bfloat16>(situ_fwd(gq, uq, p.bg, p.bu));
+                  vh.v[j] = from_f<__nv_bfloat16>(situ_fwd(gq, uq, p.bg, p.bu, ibg, ibu));
                 }
                 vh.store(h + col0 + i);
                 vg.store(og + col0 + i);
