@@ -969,6 +969,48 @@ void tc_gemm_grouped_remote(at::Tensor a, at::Tensor b, at::Tensor offsets, int6
   check(kimi::tc_gemm(g, stream()), "tc_gemm_grouped_remote");
 }
 
+// Y [world * rows, N] = all-gather(x shards) @ w^T in one kernel: the A tiles of rank r's rows
+// are TMA-loaded from rank r's shard (a peer's symmetric memory) over NVLink.
+at::Tensor tc_gemm_allgather(at::Tensor x_local, at::Tensor w, std::vector<int64_t> shard_peers, int64_t rows,
+                             at::Tensor out, int64_t bn) {
+  TORCH_CHECK(x_local.is_cuda() && x_local.scalar_type() == at::kBFloat16 && x_local.dim() == 2 &&
+                  x_local.stride(1) == 1 && x_local.stride(0) % 8 == 0,
+              "x_local must be a bf16 row-major shard");
+  CHECK_CUDA_CONTIG(w);
+  CHECK_CUDA_CONTIG(out);
+  const int64_t world = (int64_t)shard_peers.size();
+  TORCH_CHECK(world >= 1 && world <= 8 && w.scalar_type() == at::kBFloat16 && w.size(1) == x_local.size(1) &&
+                  out.size(0) == world * rows && out.size(1) == w.size(0) && out.scalar_type() == at::kBFloat16,
+              "tc_gemm_allgather shapes");
+  const at::cuda::CUDAGuard gd(x_local.device());
+  kimi::TcGemmArgs g;
+  g.mode = 0;
+  g.bn = (int)bn;
+  g.a = x_local.data_ptr();
+  g.a_rows = rows;
+  g.a_cols = x_local.size(1);
+  g.a_ld = x_local.stride(0);
+  g.b = w.data_ptr();
+  g.b_groups = 1;
+  g.b_rows = w.size(0);
+  g.b_cols = w.size(1);
+  g.b_ld = w.size(1);
+  g.b_gstride = w.numel();
+  g.M = (int)(world * rows);
+  g.N = (int)w.size(0);
+  g.K = (int)w.size(1);
+  g.G = 1;
+  g.out = out.data_ptr();
+  g.out_fp32 = false;
+  g.ldc = out.size(1);
+  g.ag_world = (int)world;
+  g.ag_rows = (int)rows;
+  for (int64_t r = 0; r < world; ++r) g.ag_peer[r] = (uint64_t)shard_peers[r];
+  g.num_sms = at::cuda::getDeviceProperties(x_local.get_device())->multiProcessorCount;
+  check(kimi::tc_gemm(g, stream()), "tc_gemm_allgather");
+  return out;
+}
+
 }  // namespace
 
 namespace {
@@ -996,6 +1038,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_dy", &ep_dy);
   m.def("ep_slot_sum", &ep_slot_sum);
   m.def("tc_gemm_grouped_remote", &tc_gemm_grouped_remote);
+  m.def("tc_gemm_allgather", &tc_gemm_allgather);
   m.def("kda_decode", &kda_decode);
   m.def("mla_decode_supported", &mla_decode_supported);
   m.def("mla_decode", &mla_decode);

@@ -61,6 +61,10 @@ struct DevParams {
   CUtensorMap map_a;
   CUtensorMap map_b;
   CUtensorMap map_b2;
+  // All-gather fused into the A operand (dense mode, A K-major): rows [r * ag_rows, (r+1) * ag_rows)
+  // of A are rank r's shard, loaded by TMA straight from that rank's memory over NVLink.
+  CUtensorMap map_a_peer[8];
+  int ag_world, ag_rows;
   int mode, M, N, K, G;
   const int* offsets;
   int b2_k_split;  // k-blocks at k >= split read map_b2 at (k - split); 0 = off
@@ -313,7 +317,12 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
           tc::mbar_arrive_expect_tx(&full[s], STAGE);
           const int k = ti.k0 + kb * BK;
           if (!A_MN) {
-            tc::tma_load_2d(sa, &p.map_a, &full[s], k, ti.m0);
+            if (p.ag_world > 0) {
+              const int owner = ti.m0 / p.ag_rows;
+              tc::tma_load_2d(sa, &p.map_a_peer[owner], &full[s], k, ti.m0 - owner * p.ag_rows);
+            } else {
+              tc::tma_load_2d(sa, &p.map_a, &full[s], k, ti.m0);
+            }
           } else {
             tc::tma_load_2d(sa, &p.map_a, &full[s], ti.m0, k);
             tc::tma_load_2d(sa + A_BYTES / 2, &p.map_a, &full[s], ti.m0 + 64, k);
@@ -690,6 +699,17 @@ cudaError_t tc_gemm(const TcGemmArgs& a, cudaStream_t stream) {
   for (int r = 0; r < 8; ++r) dp.agg_peer[r] = reinterpret_cast<float*>(a.agg_peer[r]);
   if (a.agg_tokens > 0 && (a.epi != 2 || !a.agg_peer[0])) return cudaErrorInvalidValue;
   if (a.epi == 2 && (a.N % 4 || a.ldc % 4 || (reinterpret_cast<uintptr_t>(a.out) & 15))) return cudaErrorInvalidValue;
+  dp.ag_world = a.ag_world;
+  dp.ag_rows = a.ag_rows;
+  if (a.ag_world > 0) {
+    if (a.ag_world > 8 || a.a_mn || a.mode != 0 || a.epi != 0 || a.comm_mode != 0 || a.ag_rows <= 0 ||
+        a.ag_rows % 128 || a.M != a.ag_world * a.ag_rows)
+      return cudaErrorInvalidValue;
+    for (int r = 0; r < a.ag_world; ++r)
+      if (!make_map_2d(&dp.map_a_peer[r], reinterpret_cast<const void*>(a.ag_peer[r]), a.a_cols, a.ag_rows,
+                       a.a_ld * 2, 64, 128))
+        return cudaErrorInvalidValue;
+  }
   dp.status = a.status;
   const int bn = a.epi == 1 ? 256 : a.bn;
   if (bn != 128 && bn != 256) return cudaErrorInvalidValue;

@@ -186,5 +186,81 @@ class FusedRowParallelOutput(torch.nn.Module):
         return reduce_from_tensor_parallel_region(torch.nn.functional.linear(x, self.weight.to(x.dtype)), self.group)
 
 
+class AllGatherWorkspace:
+    """Symmetric ``[row shard | flags]`` buffer for :func:`fused_allgather_matmul` (collective
+    construction): each rank's bf16 shard ``[rows, cols]`` is read by every rank's GEMM."""
+
+    _FLAGS = 1 << 12
+
+    def __init__(self, group=None, device=None, *, rows: int, cols: int, timeout_s: float = 10.0):
+        import torch.distributed._symmetric_memory as symm_mem
+        self.group = group if group is not None else dist.group.WORLD
+        self.rank, self.world = dist.get_rank(self.group), dist.get_world_size(self.group)
+        if self.world > 8 or rows % 128 or cols % 8:
+            raise ValueError("fused all-gather GEMM: at most 8 ranks, rows % 128 == 0, cols % 8 == 0")
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.rows, self.cols = rows, cols
+        shard_bytes = _align(rows * cols * 2)
+        buf = symm_mem.empty(shard_bytes + self._FLAGS, dtype=torch.uint8, device=self.device)
+        buf.zero_()
+        torch.cuda.synchronize(self.device)
+        self.handle = symm_mem.rendezvous(buf, self.group)
+        self.buffer = buf
+        ptrs = [int(p) for p in self.handle.buffer_ptrs]
+        self.shard_peers = ptrs
+        self.shard = buf[: rows * cols * 2].view(torch.bfloat16).view(rows, cols)
+        flags = [p + shard_bytes for p in ptrs]
+        # the flag-barrier kernels take the expert-parallel peer table; only its flag region is used
+        self.peer_list = flags + [0] * (8 * self.world)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.timeout_ns = int(timeout_s * 1e9)
+        self.shard_bytes = shard_bytes
+        dist.barrier(group=self.group)
+
+    def barrier(self, kind: int) -> None:
+        from ..ops import _loader
+        _loader.require().ep_signal_wait(self.peer_list, self.rank, self.world, self.status, self.timeout_ns, kind)
+
+    def check(self) -> None:
+        code = int(self.status.item())
+        if code:
+            raise RuntimeError(f"fused all-gather GEMM failed (status {code}): a peer did not arrive in time")
+
+    def reset(self) -> None:
+        torch.cuda.synchronize(self.device)
+        self.buffer[self.shard_bytes:].zero_()
+        self.status.zero_()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+
+
+def fused_allgather_matmul(x_shard: torch.Tensor, weight: torch.Tensor, workspace: AllGatherWorkspace, *,
+                           out: torch.Tensor | None = None) -> torch.Tensor:
+    """``all_gather(x_shard over the group) @ weight^T`` with the gather inside the GEMM.
+
+    ``x_shard`` [rows, K] is this rank's block of rows (rank order); ``weight`` [N, K].  The shard
+    is published in the workspace, a device-side flag barrier makes every shard visible, and the
+    tcgen05 GEMM loads each 128-row A tile by TMA directly from the owning rank's memory; a second
+    barrier keeps a rank from overwriting its shard while peers still read it.  Returns
+    [world * rows, N] (bf16).
+
+    Parity: replaces the all-gather before a sequence-parallel column-parallel projection (the
+    reference's ``_CopyToRegion`` / all-gather path, ``training/distributed/tensor_parallel.py:25-60``)."""
+    from ..ops import _loader
+    C = _loader.require()
+    ws = workspace
+    rows, k = x_shard.shape
+    if rows != ws.rows or k != ws.cols:
+        raise ValueError("x_shard must match the workspace's [rows, cols]")
+    w = weight.to(torch.bfloat16).contiguous()
+    if out is None:
+        out = torch.empty(ws.world * rows, w.shape[0], dtype=torch.bfloat16, device=x_shard.device)
+    ws.shard.copy_(x_shard)
+    ws.barrier(5)
+    C.tc_gemm_allgather(ws.shard, w, ws.shard_peers, rows, out, 256 if w.shape[0] >= 256 else 128)
+    ws.barrier(6)
+    return out
+
+
 __all__ = ["SymmetricWorkspace", "workspace_for", "release_workspaces", "fused_matmul_reduce",
-           "FusedRowParallelOutput"]
+           "FusedRowParallelOutput", "AllGatherWorkspace", "fused_allgather_matmul"]

@@ -4,7 +4,9 @@
 * one rank, a fake second rank whose flags nobody sets: every wait runs out (bounded), the kernel
   returns with the timeout status, and the workspace is usable again after ``reset()``;
 * two ranks (needs 2 GPUs): all-reduce and reduce-scatter, multicast and peer paths, against
-  NCCL's all-reduce of the fp32 partial products, over repeated calls.
+  NCCL's all-reduce of the fp32 partial products, over repeated calls;
+* the all-gather fused into a GEMM's A operand (one rank and two ranks) against NCCL's
+  all-gather followed by the product.
 
 Each case runs in child processes (process groups and symmetric memory stay out of the pytest
 process); the multi-rank case uses torchrun on 127.0.0.1 with a hard timeout.
@@ -88,6 +90,14 @@ def child_one(port):
         if m % 128 == 0:
             _close(fused_matmul_reduce(x, w, ws, reduce="reduce_scatter"), ref, 1e-2)
     ws.check()
+    # all-gather fused into the GEMM's A operand (one rank: the gather is the local shard)
+    from kimi_k3_b200.parallel.symmetric import AllGatherWorkspace, fused_allgather_matmul
+    ag = AllGatherWorkspace(None, "cuda:0", rows=256, cols=320)
+    for it in range(3):
+        x = torch.randn(256, 320, device="cuda").bfloat16()
+        w = (torch.randn(640, 320, device="cuda") / 320 ** 0.5).bfloat16()
+        _close(fused_allgather_matmul(x, w, ag), x.float() @ w.float().t(), 1e-2)
+    ag.check()
     dist.destroy_process_group()
     print("one-rank ok")
 
@@ -150,6 +160,21 @@ def child_multi():
         ws.check()
         paths.append("nvls-multimem" if use_mc else "peer")
         del ws
+    # all-gather fused into the GEMM: A tiles of rank r's rows come from rank r's shard over NVLink
+    from kimi_k3_b200.parallel.symmetric import AllGatherWorkspace, fused_allgather_matmul
+    ag = AllGatherWorkspace(None, f"cuda:{rank}", rows=384, cols=320)
+    for it in range(3):
+        torch.manual_seed(200 + 10 * it + rank)
+        x = torch.randn(384, 320, device="cuda").bfloat16()
+        torch.manual_seed(7 + it)
+        w = (torch.randn(768, 320, device="cuda") / 320 ** 0.5).bfloat16()
+        parts = [torch.empty_like(x) for _ in range(world)]
+        dist.all_gather(parts, x)
+        ref = torch.cat(parts).float() @ w.float().t()
+        _close(fused_allgather_matmul(x, w, ag), ref, 1e-2)
+    ag.check()
+    paths.append("allgather-gemm")
+    del ag
     torch.cuda.synchronize()
     dist.barrier()
     dist.destroy_process_group()
