@@ -969,34 +969,38 @@ void tc_gemm_grouped_remote(at::Tensor a, at::Tensor b, at::Tensor offsets, int6
   check(kimi::tc_gemm(g, stream()), "tc_gemm_grouped_remote");
 }
 
-// Y [world * rows, N] = all-gather(x shards) @ w^T in one kernel: the A tiles of rank r's rows
-// are TMA-loaded from rank r's shard (a peer's symmetric memory) over NVLink.
-at::Tensor tc_gemm_allgather(at::Tensor x_local, at::Tensor w, std::vector<int64_t> shard_peers, int64_t rows,
-                             at::Tensor out, int64_t bn) {
-  TORCH_CHECK(x_local.is_cuda() && x_local.scalar_type() == at::kBFloat16 && x_local.dim() == 2 &&
-                  x_local.stride(1) == 1 && x_local.stride(0) % 8 == 0,
-              "x_local must be a bf16 row-major shard");
+// Y [world * rows, N] = all-gather(x shards) @ w^T in one kernel.  `buf` is this rank's [M, K]
+// symmetric gather buffer (its own shard already in rows [rank * rows, ...)); `peers` every rank's
+// buffer base.  The kernel's comm warps copy each remote block once over NVLink into `buf`.
+at::Tensor tc_gemm_allgather(at::Tensor buf, at::Tensor w, std::vector<int64_t> peers, int64_t rank, int64_t rows,
+                             at::Tensor flags, at::Tensor epoch, at::Tensor status, at::Tensor out, int64_t bn) {
+  TORCH_CHECK(buf.is_cuda() && buf.scalar_type() == at::kBFloat16 && buf.dim() == 2 && buf.is_contiguous(),
+              "buf must be a contiguous bf16 [M, K] gather buffer");
   CHECK_CUDA_CONTIG(w);
   CHECK_CUDA_CONTIG(out);
-  const int64_t world = (int64_t)shard_peers.size();
-  TORCH_CHECK(world >= 1 && world <= 8 && w.scalar_type() == at::kBFloat16 && w.size(1) == x_local.size(1) &&
-                  out.size(0) == world * rows && out.size(1) == w.size(0) && out.scalar_type() == at::kBFloat16,
+  CHECK_CUDA_CONTIG(flags);
+  const int64_t world = (int64_t)peers.size();
+  TORCH_CHECK(world >= 1 && world <= 8 && buf.size(0) == world * rows && w.scalar_type() == at::kBFloat16 &&
+                  w.size(1) == buf.size(1) && out.size(0) == buf.size(0) && out.size(1) == w.size(0) &&
+                  out.scalar_type() == at::kBFloat16 && flags.scalar_type() == at::kInt &&
+                  flags.numel() >= buf.size(0) / 128 && epoch.scalar_type() == at::kInt &&
+                  status.scalar_type() == at::kInt,
               "tc_gemm_allgather shapes");
-  const at::cuda::CUDAGuard gd(x_local.device());
+  const at::cuda::CUDAGuard gd(buf.device());
   kimi::TcGemmArgs g;
   g.mode = 0;
   g.bn = (int)bn;
-  g.a = x_local.data_ptr();
-  g.a_rows = rows;
-  g.a_cols = x_local.size(1);
-  g.a_ld = x_local.stride(0);
+  g.a = buf.data_ptr();
+  g.a_rows = buf.size(0);
+  g.a_cols = buf.size(1);
+  g.a_ld = buf.size(1);
   g.b = w.data_ptr();
   g.b_groups = 1;
   g.b_rows = w.size(0);
   g.b_cols = w.size(1);
   g.b_ld = w.size(1);
   g.b_gstride = w.numel();
-  g.M = (int)(world * rows);
+  g.M = (int)buf.size(0);
   g.N = (int)w.size(0);
   g.K = (int)w.size(1);
   g.G = 1;
@@ -1005,8 +1009,12 @@ at::Tensor tc_gemm_allgather(at::Tensor x_local, at::Tensor w, std::vector<int64
   g.ldc = out.size(1);
   g.ag_world = (int)world;
   g.ag_rows = (int)rows;
-  for (int64_t r = 0; r < world; ++r) g.ag_peer[r] = (uint64_t)shard_peers[r];
-  g.num_sms = at::cuda::getDeviceProperties(x_local.get_device())->multiProcessorCount;
+  g.ag_rank = (int)rank;
+  g.ag_flags = reinterpret_cast<uint32_t*>(flags.data_ptr());
+  g.ag_epoch = reinterpret_cast<const uint32_t*>(epoch.data_ptr());
+  g.status = status.data_ptr<int>();
+  for (int64_t r = 0; r < world; ++r) g.ag_peer[r] = (uint64_t)peers[r];
+  g.num_sms = at::cuda::getDeviceProperties(buf.get_device())->multiProcessorCount;
   check(kimi::tc_gemm(g, stream()), "tc_gemm_allgather");
   return out;
 }

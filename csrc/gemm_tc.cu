@@ -61,10 +61,17 @@ struct DevParams {
   CUtensorMap map_a;
   CUtensorMap map_b;
   CUtensorMap map_b2;
-  // All-gather fused into the A operand (dense mode, A K-major): rows [r * ag_rows, (r+1) * ag_rows)
-  // of A are rank r's shard, loaded by TMA straight from that rank's memory over NVLink.
-  CUtensorMap map_a_peer[8];
-  int ag_world, ag_rows;
+  // All-gather fused into the A operand (dense mode, A K-major, comm warps): every rank holds an
+  // [M, K] gather buffer (symmetric) whose rows [r * ag_rows, (r + 1) * ag_rows) rank r fills with its
+  // shard.  The comm warps copy each remote 128-row block from its owner's buffer into this rank's
+  // buffer (each byte crosses NVLink once) and release a per-block flag; tiles of local rows run
+  // first, and the producer waits for a remote block's flag before its first TMA load of it.
+  int ag_world, ag_rows, ag_rank;
+  const uint8_t* ag_peer[8];
+  uint8_t* ag_local;
+  uint32_t* ag_flags;        // local, one per 128-row block, monotonic (value = call number + 1)
+  const uint32_t* ag_epoch;  // call number, advanced by the host wrapper after each call
+  int64_t ag_ld;             // row stride of the gather buffers in bytes
   int mode, M, N, K, G;
   const int* offsets;
   int b2_k_split;  // k-blocks at k >= split read map_b2 at (k - split); 0 = off
@@ -119,8 +126,20 @@ __device__ TileInfo tile_info(const DevParams& p, int tile) {
   if (p.mode == 0) {
     const int tm = (p.M + BM - 1) / BM;
     ti.g = 0;
-    ti.m0 = (tile % tm) * BM;
-    ti.n0 = (tile / tm) * BNT;
+    if (p.ag_world > 0) {  // this rank's row blocks first (every column tile), then the remote ones
+      const int bpr = p.ag_rows / BM, first = p.ag_rank * bpr, local = bpr * tn;
+      if (tile < local) {
+        ti.m0 = (first + tile % bpr) * BM;
+        ti.n0 = (tile / bpr) * BNT;
+      } else {
+        const int t2 = tile - local, rem = tm - bpr;
+        ti.m0 = ((first + bpr + t2 % rem) % tm) * BM;
+        ti.n0 = (t2 / rem) * BNT;
+      }
+    } else {
+      ti.m0 = (tile % tm) * BM;
+      ti.n0 = (tile / tm) * BNT;
+    }
     ti.k0 = 0;
     ti.num_kb = (p.K + BK - 1) / BK;
     ti.c_row0 = ti.m0;
@@ -259,6 +278,7 @@ __device__ __forceinline__ float situ_fwd(float g, float u, float bg, float bu, 
 
 template <int BN>
 __device__ void comm_loop(const DevParams& p, int total);
+__device__ void ag_copy_loop(const DevParams& p);
 
 template <int BN, bool A_MN, bool B_MN, int CM>
 __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid_constant__ DevParams p) {
@@ -308,6 +328,7 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0;
+      const uint32_t ag_target = CM == 3 ? *p.ag_epoch + 1u : 0u;
       for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
         const TileInfo ti = p.situ ? tile_info<BN / 2>(p, tile) : tile_info<BN>(p, tile);
         for (int kb = 0; kb < ti.num_kb; ++kb) {
@@ -317,12 +338,24 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
           tc::mbar_arrive_expect_tx(&full[s], STAGE);
           const int k = ti.k0 + kb * BK;
           if (!A_MN) {
-            if (p.ag_world > 0) {
-              const int owner = ti.m0 / p.ag_rows;
-              tc::tma_load_2d(sa, &p.map_a_peer[owner], &full[s], k, ti.m0 - owner * p.ag_rows);
-            } else {
-              tc::tma_load_2d(sa, &p.map_a, &full[s], k, ti.m0);
+            if (CM == 3 && kb == 0 && ti.m0 / p.ag_rows != p.ag_rank) {
+              // remote rows: wait until a comm warp has copied this block into the local buffer
+              const uint32_t* f = p.ag_flags + ti.m0 / BM;
+              const uint32_t target = ag_target;
+              const uint64_t t0 = global_ns();
+              uint32_t v;
+              while (true) {
+                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+                if (v >= target) break;
+                if ((int64_t)(global_ns() - t0) > (int64_t)10000000000LL) {
+                  atomicCAS(p.status, 0, kCommTimeout);
+                  break;
+                }
+                __nanosleep(64);
+              }
+              asm volatile("fence.proxy.async.global;" ::: "memory");
             }
+            tc::tma_load_2d(sa, &p.map_a, &full[s], k, ti.m0);
           } else {
             tc::tma_load_2d(sa, &p.map_a, &full[s], ti.m0, k);
             tc::tma_load_2d(sa + A_BYTES / 2, &p.map_a, &full[s], ti.m0 + 64, k);
@@ -500,7 +533,7 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
       }
       tc::tc_fence_before();
       tc::mbar_arrive(&tempty[buf]);
-      if constexpr (CM != 0) {
+      if constexpr (CM == 1 || CM == 2) {
         // this rank's partial tile is in the symmetric buffer: tell the tile's owner
         fence_sys();
         epi_bar();
@@ -511,7 +544,10 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
       }
     }
   } else {
-    if constexpr (CM != 0) comm_loop<BN>(p, total);
+    if constexpr (CM == 3)
+      ag_copy_loop(p);
+    else if constexpr (CM != 0)
+      comm_loop<BN>(p, total);
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -519,6 +555,40 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
   if (warp == 1) tc::tmem_dealloc(tmem_base, TMEM_COLS);
 }
 
+
+// All-gather comm warps (threads 320..447): copy remote 128-row blocks of A into the local gather
+// buffer in the order the tiles consume them, eight 16-byte loads in flight per thread, then
+// release the block's flag.
+__device__ void ag_copy_loop(const DevParams& p) {
+  const int ct = threadIdx.x - 320;
+  const int tm = p.M / BM, bpr = p.ag_rows / BM, rem = tm - bpr;
+  const uint32_t target = *p.ag_epoch + 1u;
+  const int chunks = (int)(p.ag_ld / 16);  // 16-byte chunks per row (K * 2 / 16)
+  const int per_block = BM * chunks;
+  for (int j = blockIdx.x; j < rem; j += gridDim.x) {
+    const int mb = (p.ag_rank * bpr + bpr + j) % tm;
+    const int owner = mb / bpr;
+    const int64_t base = (int64_t)mb * BM * p.ag_ld;
+    const uint4* src = reinterpret_cast<const uint4*>(p.ag_peer[owner] + base);
+    uint4* dst = reinterpret_cast<uint4*>(p.ag_local + base);
+    for (int i0 = ct; i0 < per_block; i0 += 128 * 8) {
+      uint4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * 128;
+        if (i < per_block) v[u] = src[i];
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * 128;
+        if (i < per_block) dst[i] = v[u];
+      }
+    }
+    __threadfence();
+    comm_bar();
+    if (ct == 0) asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p.ag_flags + mb), "r"(target) : "memory");
+  }
+}
 
 // Comm warps (threads 320..447): reduce the tiles this rank owns, then hand every tile's sum out.
 template <int BN>
@@ -701,15 +771,17 @@ cudaError_t tc_gemm(const TcGemmArgs& a, cudaStream_t stream) {
   if (a.epi == 2 && (a.N % 4 || a.ldc % 4 || (reinterpret_cast<uintptr_t>(a.out) & 15))) return cudaErrorInvalidValue;
   dp.ag_world = a.ag_world;
   dp.ag_rows = a.ag_rows;
-  if (a.ag_world > 0) {
-    if (a.ag_world > 8 || a.a_mn || a.mode != 0 || a.epi != 0 || a.comm_mode != 0 || a.ag_rows <= 0 ||
-        a.ag_rows % 128 || a.M != a.ag_world * a.ag_rows)
-      return cudaErrorInvalidValue;
-    for (int r = 0; r < a.ag_world; ++r)
-      if (!make_map_2d(&dp.map_a_peer[r], reinterpret_cast<const void*>(a.ag_peer[r]), a.a_cols, a.ag_rows,
-                       a.a_ld * 2, 64, 128))
-        return cudaErrorInvalidValue;
-  }
+  dp.ag_rank = a.ag_rank;
+  dp.ag_local = reinterpret_cast<uint8_t*>(const_cast<void*>(a.a));
+  dp.ag_flags = a.ag_flags;
+  dp.ag_epoch = a.ag_epoch;
+  dp.ag_ld = a.a_ld * 2;
+  for (int r = 0; r < 8; ++r) dp.ag_peer[r] = reinterpret_cast<const uint8_t*>(a.ag_peer[r]);
+  if (a.ag_world > 0 && (a.ag_world > 8 || a.a_mn || a.mode != 0 || a.epi != 0 || a.comm_mode != 0 ||
+                         a.ag_rows <= 0 || a.ag_rows % 128 || a.M != a.ag_world * a.ag_rows || a.a_rows != a.M ||
+                         a.ag_rank < 0 || a.ag_rank >= a.ag_world || !a.ag_flags || !a.ag_epoch || !a.status ||
+                         (a.a_ld * 2) % 16))
+    return cudaErrorInvalidValue;
   dp.status = a.status;
   const int bn = a.epi == 1 ? 256 : a.bn;
   if (bn != 128 && bn != 256) return cudaErrorInvalidValue;
@@ -773,6 +845,9 @@ cudaError_t tc_gemm(const TcGemmArgs& a, cudaStream_t stream) {
                                    : launch<128, false, false, 1>(dp, sms, stream);
     return a.b_mn ? launch<128, false, true, 2>(dp, sms, stream) : launch<128, false, false, 2>(dp, sms, stream);
   }
+  if (a.ag_world > 0)
+    return (bn == 256 ? (a.b_mn ? launch<256, false, true, 3>(dp, sms, stream) : launch<256, false, false, 3>(dp, sms, stream))
+                      : (a.b_mn ? launch<128, false, true, 3>(dp, sms, stream) : launch<128, false, false, 3>(dp, sms, stream)));
 #define KIMI_TC_LAUNCH(BN_, AM_, BM_) return launch<BN_, AM_, BM_>(dp, sms, stream)
   if (bn == 256) {
     if (!a.a_mn && !a.b_mn) KIMI_TC_LAUNCH(256, false, false);

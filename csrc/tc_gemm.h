@@ -33,10 +33,13 @@ struct TcGemmArgs {
   // epi 2 only: row_token = rank * agg_tokens + token adds into agg_peer[rank] (row stride ldc)
   uint64_t agg_peer[8] = {};
   int agg_tokens = 0;
-  // all-gather fused into A (dense, K-major A): ag_peer[r] holds rank r's [ag_rows, K] shard
-  // (row stride a_ld); M must be ag_world * ag_rows
+  // all-gather fused into A (dense, K-major A): `a` is this rank's [M, K] gather buffer (rows
+  // [ag_rank * ag_rows, ...) hold its own shard), ag_peer[r] rank r's buffer; M = ag_world * ag_rows;
+  // ag_flags: local [M / 128] block flags; ag_epoch: device call counter
   uint64_t ag_peer[8] = {};
-  int ag_world = 0, ag_rows = 0;
+  int ag_world = 0, ag_rows = 0, ag_rank = 0;
+  uint32_t* ag_flags = nullptr;
+  const uint32_t* ag_epoch = nullptr;
   int* status = nullptr;
   int num_sms = 0;
   // Comm modes (dense, bf16 output, A K-major, N % 8 == 0): `out` / `ldc` must be this rank's

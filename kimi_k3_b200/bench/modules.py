@@ -683,3 +683,68 @@ def bench_ep(argv=None) -> list:
 
 
 BENCHMARKS["ep"] = bench_ep
+
+
+def bench_allgather_gemm(argv=None) -> list:
+    """Sequence-parallel column projection ``all_gather(x) @ W^T``: the fused kernel (A tiles
+    TMA-loaded from the owners' shards over NVLink) against NCCL all-gather + the same GEMM.
+    Run under torchrun; CUDA-event time per call, max over ranks."""
+    import datetime
+    import os
+    import torch.distributed as dist
+    from ..parallel.symmetric import AllGatherWorkspace, fused_allgather_matmul
+    from ..ops import _loader
+    p = argparse.ArgumentParser(description="fused all-gather GEMM")
+    p.add_argument("--shard-rows", type=int, default=8192, help="rows per rank")
+    p.add_argument("--k", type=int, default=640)
+    p.add_argument("--cols-out", type=int, default=1920)
+    p.add_argument("--repeats", type=int, default=50)
+    args = p.parse_args(argv)
+    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
+    dev = torch.device("cuda", torch.cuda.current_device())
+    if not dist.is_initialized():
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    C = _loader.require()
+    x = torch.randn(args.shard_rows, args.k, device=dev).bfloat16()
+    w = torch.randn(args.cols_out, args.k, device=dev).bfloat16()
+    ws = AllGatherWorkspace(None, dev, rows=args.shard_rows, cols=args.k)
+    full = torch.empty(world * args.shard_rows, args.k, device=dev, dtype=torch.bfloat16)
+    out = torch.empty(world * args.shard_rows, args.cols_out, device=dev, dtype=torch.bfloat16)
+    bn = 256 if args.cols_out >= 256 else 128
+
+    def fused():
+        fused_allgather_matmul(x, w, ws, out=out)
+
+    def nccl():
+        dist.all_gather_into_tensor(full, x)
+        C.tc_gemm_dense(full, w, False, False, False, bn, out)
+
+    rows_out = []
+    for name, fn in (("fused_allgather_gemm", fused), ("nccl_allgather_then_gemm", nccl)):
+        for _ in range(5):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.repeats):
+            fn()
+        t1.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([t0.elapsed_time(t1) / args.repeats], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        flops = 2.0 * world * args.shard_rows * args.k * args.cols_out
+        rows_out.append({"bench": "allgather_gemm", "impl": name, "ranks": world, "rows_per_rank": args.shard_rows,
+                         "k": args.k, "n": args.cols_out, "ms_max_over_ranks": round(ms.item(), 4),
+                         "tflops": round(flops / ms.item() / 1e9, 1)})
+        if rank == 0:
+            print(json.dumps(rows_out[-1]), flush=True)
+    ws.check()
+    del ws
+    dist.barrier()
+    dist.destroy_process_group()
+    return rows_out
+
+
+BENCHMARKS["allgather_gemm"] = bench_allgather_gemm

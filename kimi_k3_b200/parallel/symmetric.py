@@ -200,15 +200,20 @@ class AllGatherWorkspace:
             raise ValueError("fused all-gather GEMM: at most 8 ranks, rows % 128 == 0, cols % 8 == 0")
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.rows, self.cols = rows, cols
-        shard_bytes = _align(rows * cols * 2)
+        full_rows = self.world * rows
+        shard_bytes = _align(full_rows * cols * 2)
         buf = symm_mem.empty(shard_bytes + self._FLAGS, dtype=torch.uint8, device=self.device)
         buf.zero_()
         torch.cuda.synchronize(self.device)
         self.handle = symm_mem.rendezvous(buf, self.group)
         self.buffer = buf
         ptrs = [int(p) for p in self.handle.buffer_ptrs]
-        self.shard_peers = ptrs
-        self.shard = buf[: rows * cols * 2].view(torch.bfloat16).view(rows, cols)
+        self.buffer_peers = ptrs
+        # [world * rows, cols] gather buffer; this rank's shard is its row block
+        self.gather = buf[: full_rows * cols * 2].view(torch.bfloat16).view(full_rows, cols)
+        self.shard = self.gather[self.rank * rows: (self.rank + 1) * rows]
+        self.block_flags = torch.zeros(full_rows // 128, dtype=torch.int32, device=self.device)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=self.device)
         flags = [p + shard_bytes for p in ptrs]
         # the flag-barrier kernels take the expert-parallel peer table; only its flag region is used
         self.peer_list = flags + [0] * (8 * self.world)
@@ -239,10 +244,12 @@ def fused_allgather_matmul(x_shard: torch.Tensor, weight: torch.Tensor, workspac
     """``all_gather(x_shard over the group) @ weight^T`` with the gather inside the GEMM.
 
     ``x_shard`` [rows, K] is this rank's block of rows (rank order); ``weight`` [N, K].  The shard
-    is published in the workspace, a device-side flag barrier makes every shard visible, and the
-    tcgen05 GEMM loads each 128-row A tile by TMA directly from the owning rank's memory; a second
-    barrier keeps a rank from overwriting its shard while peers still read it.  Returns
-    [world * rows, N] (bf16).
+    is published in its row block of the workspace's gather buffer and a device-side flag barrier
+    makes every shard visible; then ONE kernel computes the local rows' tiles first while its
+    comm warps copy each remote 128-row block over NVLink into the local gather buffer (every
+    byte crosses once) and release a per-block flag that the TMA producer waits on before the
+    remote rows' tiles.  A second barrier keeps a rank from overwriting its shard while peers
+    still read it.  Returns [world * rows, N] (bf16).
 
     Parity: replaces the all-gather before a sequence-parallel column-parallel projection (the
     reference's ``_CopyToRegion`` / all-gather path, ``training/distributed/tensor_parallel.py:25-60``)."""
@@ -257,7 +264,9 @@ def fused_allgather_matmul(x_shard: torch.Tensor, weight: torch.Tensor, workspac
         out = torch.empty(ws.world * rows, w.shape[0], dtype=torch.bfloat16, device=x_shard.device)
     ws.shard.copy_(x_shard)
     ws.barrier(5)
-    C.tc_gemm_allgather(ws.shard, w, ws.shard_peers, rows, out, 256 if w.shape[0] >= 256 else 128)
+    C.tc_gemm_allgather(ws.gather, w, ws.buffer_peers, ws.rank, rows, ws.block_flags, ws.epoch, ws.status, out,
+                        256 if w.shape[0] >= 256 else 128)
+    ws.epoch.add_(1)
     ws.barrier(6)
     return out
 
