@@ -1,7 +1,8 @@
 // Attention-residual depth mixing: for each token, softmax over S depth sources of
 //   logit_s = q . (RMSNorm(src_s) * w)
 // and an fp32 weighted sum of the raw sources. One warp per token; each source tensor is
-// read through its own pointer (no stacked copy), once for the logits and once for the sum.
+// read through its own pointer (no stacked copy), once for the logits and once for the sum
+// (once in all when there are at most four sources).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -25,15 +26,42 @@ int grid_tokens(int64_t tokens, int warps_per_block) {
   return (int)(g < 1 ? 1 : g);
 }
 
+// Sources are processed in groups (four rows, two for very wide rows): the rows of a group are
+// loaded together (several loads in flight per lane), and the per-source scalars (logit, rstd,
+// probability, partial dots) live in lane s of the warp (S <= 16 < 32) and are broadcast with
+// shuffles -- no per-thread arrays indexed by a runtime source number.  With at most one group of
+// sources, the rows loaded for the logits are reused for the weighted sum.
+template <int MAXV>
+struct Group {
+  static constexpr int n = MAXV >= 8 ? 2 : 4;  // fewer rows in flight for wide rows (register budget)
+};
+
+template <typename T, int MAXV>
+KIMI_D void load_group(Vec<T> (&xb)[Group<MAXV>::n][MAXV], const SrcPtrs<T>& src, int s0, int S, int64_t tok,
+                       int dim, int lane, int nvec) {
+  constexpr int VN = Vec<T>::N;
+#pragma unroll
+  for (int u = 0; u < Group<MAXV>::n; ++u) {
+    if (s0 + u < S) {
+      const T* row = src.p[s0 + u] + tok * dim;
+#pragma unroll
+      for (int v = 0; v < MAXV; ++v) {
+        const int vi = lane + v * 32;
+        if (vi < nvec) xb[u][v].load(row + vi * VN);
+      }
+    }
+  }
+}
+
 template <typename T, int MAXV>
 __global__ void attnres_fwd_kernel(SrcPtrs<T> src, int S, const float* __restrict__ q, const float* __restrict__ w,
                                    T* __restrict__ out, float* __restrict__ probs, float* __restrict__ rstd,
                                    int64_t tokens, int dim, float eps) {
   constexpr int VN = Vec<T>::N;
+  constexpr int kGroup = Group<MAXV>::n;
   const int lane = threadIdx.x & 31;
   const int wpb = blockDim.x >> 5;
   const int nvec = dim / VN;
-  // Preload q*w for this lane's slice.
   float qw[MAXV][VN];
 #pragma unroll
   for (int v = 0; v < MAXV; ++v) {
@@ -41,64 +69,68 @@ __global__ void attnres_fwd_kernel(SrcPtrs<T> src, int S, const float* __restric
 #pragma unroll
     for (int j = 0; j < VN; ++j) qw[v][j] = vi < nvec ? q[vi * VN + j] * w[vi * VN + j] : 0.f;
   }
+  const float inv_dim = 1.f / dim;
   for (int64_t tok = (int64_t)blockIdx.x * wpb + (threadIdx.x >> 5); tok < tokens; tok += (int64_t)gridDim.x * wpb) {
-    float logit[kMaxSources], rs[kMaxSources];
-    float mx = -INFINITY;
-    for (int s = 0; s < S; ++s) {
-      const T* row = src.p[s] + tok * dim;
-      float ss = 0.f, a = 0.f;
+    float my_logit = -INFINITY, my_r = 0.f;  // lane s: source s
+    Vec<T> xb[kGroup][MAXV];
+    for (int s0 = 0; s0 < S; s0 += kGroup) {
+      load_group<T, MAXV>(xb, src, s0, S, tok, dim, lane, nvec);
 #pragma unroll
-      for (int v = 0; v < MAXV; ++v) {
-        const int vi = lane + v * 32;
-        if (vi < nvec) {
-          Vec<T> x;
-          x.load(row + vi * VN);
+      for (int u = 0; u < kGroup; ++u) {
+        float ss = 0.f, a = 0.f;
+        if (s0 + u < S) {
 #pragma unroll
-          for (int j = 0; j < VN; ++j) {
-            const float xv = x.f(j);
-            ss += xv * xv;
-            a += qw[v][j] * xv;
+          for (int v = 0; v < MAXV; ++v) {
+            if (lane + v * 32 < nvec) {
+#pragma unroll
+              for (int j = 0; j < VN; ++j) {
+                const float xv = xb[u][v].f(j);
+                ss += xv * xv;
+                a += qw[v][j] * xv;
+              }
+            }
           }
         }
+        ss = warp_sum(ss);
+        a = warp_sum(a);
+        if (lane == s0 + u) {
+          my_r = rsqrtf(ss * inv_dim + eps);
+          my_logit = my_r * a;
+        }
       }
-      ss = warp_sum(ss);
-      a = warp_sum(a);
-      const float r = rsqrtf(ss / dim + eps);
-      rs[s] = r;
-      logit[s] = r * a;
-      mx = fmaxf(mx, logit[s]);
     }
-    float denom = 0.f;
-    for (int s = 0; s < S; ++s) {
-      logit[s] = expf(logit[s] - mx);
-      denom += logit[s];
-    }
-    const float inv = 1.f / denom;
-    for (int s = 0; s < S; ++s) logit[s] *= inv;
+    const float mx = warp_max(lane < S ? my_logit : -INFINITY);
+    const float e = lane < S ? expf(my_logit - mx) : 0.f;
+    const float my_p = e / warp_sum(e);
     if (lane < S) {
-      // lane-indexed writes of the per-source statistics (S <= 16 < 32)
-      float pv = 0.f, rv = 0.f;
-      for (int s = 0; s < S; ++s)
-        if (s == lane) { pv = logit[s]; rv = rs[s]; }
-      probs[tok * S + lane] = pv;
-      rstd[tok * S + lane] = rv;
+      probs[tok * S + lane] = my_p;
+      rstd[tok * S + lane] = my_r;
+    }
+    float acc[MAXV][VN];
+#pragma unroll
+    for (int v = 0; v < MAXV; ++v)
+#pragma unroll
+      for (int j = 0; j < VN; ++j) acc[v][j] = 0.f;
+    for (int s0 = 0; s0 < S; s0 += kGroup) {
+      if (S > kGroup) load_group<T, MAXV>(xb, src, s0, S, tok, dim, lane, nvec);
+#pragma unroll
+      for (int u = 0; u < kGroup; ++u) {
+        if (s0 + u < S) {
+          const float pu = __shfl_sync(0xffffffffu, my_p, s0 + u);
+#pragma unroll
+          for (int v = 0; v < MAXV; ++v)
+#pragma unroll
+            for (int j = 0; j < VN; ++j) acc[v][j] += pu * xb[u][v].f(j);
+        }
+      }
     }
 #pragma unroll
     for (int v = 0; v < MAXV; ++v) {
       const int vi = lane + v * 32;
       if (vi < nvec) {
-        float acc[VN];
-#pragma unroll
-        for (int j = 0; j < VN; ++j) acc[j] = 0.f;
-        for (int s = 0; s < S; ++s) {
-          Vec<T> x;
-          x.load(src.p[s] + tok * dim + vi * VN);
-#pragma unroll
-          for (int j = 0; j < VN; ++j) acc[j] += logit[s] * x.f(j);
-        }
         Vec<T> o;
 #pragma unroll
-        for (int j = 0; j < VN; ++j) o.set(j, acc[j]);
+        for (int j = 0; j < VN; ++j) o.set(j, acc[v][j]);
         o.store(out + tok * dim + vi * VN);
       }
     }
@@ -111,6 +143,7 @@ __global__ void attnres_bwd_kernel(SrcPtrs<T> src, int S, const float* __restric
                                    const float* __restrict__ rstd, DstPtrs<T> dsrc, float* __restrict__ dq,
                                    float* __restrict__ dw, int64_t tokens, int dim) {
   constexpr int VN = Vec<T>::N;
+  constexpr int kGroup = Group<MAXV>::n;
   const int lane = threadIdx.x & 31;
   const int wpb = blockDim.x >> 5;
   const int nvec = dim / VN;
@@ -127,8 +160,6 @@ __global__ void attnres_bwd_kernel(SrcPtrs<T> src, int S, const float* __restric
   }
   const float inv_dim = 1.f / dim;
   for (int64_t tok = (int64_t)blockIdx.x * wpb + (threadIdx.x >> 5); tok < tokens; tok += (int64_t)gridDim.x * wpb) {
-    float p[kMaxSources], r[kMaxSources], dp[kMaxSources], a[kMaxSources];
-    float pdp = 0.f;
     // the output gradient row, read once for all sources and both passes
     Vec<T> gv[MAXV];
 #pragma unroll
@@ -136,46 +167,61 @@ __global__ void attnres_bwd_kernel(SrcPtrs<T> src, int S, const float* __restric
       const int vi = lane + v * 32;
       if (vi < nvec) gv[v].load(dout + tok * dim + vi * VN);
     }
-    for (int s = 0; s < S; ++s) {
-      p[s] = probs[tok * S + s];
-      r[s] = rstd[tok * S + s];
-      const T* row = src.p[s] + tok * dim;
-      float d0 = 0.f, a0 = 0.f;
+    const float my_p = lane < S ? probs[tok * S + lane] : 0.f;
+    const float my_r = lane < S ? rstd[tok * S + lane] : 0.f;
+    float my_dp = 0.f, my_a = 0.f;
+    Vec<T> xb[kGroup][MAXV];
+    for (int s0 = 0; s0 < S; s0 += kGroup) {
+      load_group<T, MAXV>(xb, src, s0, S, tok, dim, lane, nvec);
 #pragma unroll
-      for (int v = 0; v < MAXV; ++v) {
-        const int vi = lane + v * 32;
-        if (vi < nvec) {
-          Vec<T> x;
-          x.load(row + vi * VN);
+      for (int u = 0; u < kGroup; ++u) {
+        float d0 = 0.f, a0 = 0.f;
+        if (s0 + u < S) {
 #pragma unroll
-          for (int j = 0; j < VN; ++j) {
-            d0 += gv[v].f(j) * x.f(j);
-            a0 += qw[v][j] * x.f(j);
+          for (int v = 0; v < MAXV; ++v) {
+            if (lane + v * 32 < nvec) {
+#pragma unroll
+              for (int j = 0; j < VN; ++j) {
+                const float xv = xb[u][v].f(j);
+                d0 += gv[v].f(j) * xv;
+                a0 += qw[v][j] * xv;
+              }
+            }
           }
         }
+        d0 = warp_sum(d0);
+        a0 = warp_sum(a0);
+        if (lane == s0 + u) {
+          my_dp = d0;
+          my_a = a0;
+        }
       }
-      dp[s] = warp_sum(d0);
-      a[s] = warp_sum(a0);
-      pdp += p[s] * dp[s];
     }
-    for (int s = 0; s < S; ++s) {
-      const float dl = p[s] * (dp[s] - pdp);  // d loss / d logit_s
-      const float r3 = r[s] * r[s] * r[s] * a[s] * inv_dim;
-      const T* row = src.p[s] + tok * dim;
-      T* drow = dsrc.p[s] + tok * dim;
+    const float pdp = warp_sum(lane < S ? my_p * my_dp : 0.f);
+    for (int s0 = 0; s0 < S; s0 += kGroup) {
+      if (S > kGroup) load_group<T, MAXV>(xb, src, s0, S, tok, dim, lane, nvec);
 #pragma unroll
-      for (int v = 0; v < MAXV; ++v) {
-        const int vi = lane + v * 32;
-        if (vi < nvec) {
-          Vec<T> x, o;
-          x.load(row + vi * VN);
+      for (int u = 0; u < kGroup; ++u) {
+        if (s0 + u < S) {
+          const int sidx = s0 + u;
+          const float p = __shfl_sync(0xffffffffu, my_p, sidx), r = __shfl_sync(0xffffffffu, my_r, sidx);
+          const float dl = p * (__shfl_sync(0xffffffffu, my_dp, sidx) - pdp);  // d loss / d logit_s
+          const float r3 = r * r * r * __shfl_sync(0xffffffffu, my_a, sidx) * inv_dim;
+          T* drow = dsrc.p[sidx] + tok * dim;
 #pragma unroll
-          for (int j = 0; j < VN; ++j) {
-            const float xv = x.f(j);
-            o.set(j, p[s] * gv[v].f(j) + dl * (r[s] * qw[v][j] - r3 * xv));
-            acc[v][j] += dl * r[s] * xv;
+          for (int v = 0; v < MAXV; ++v) {
+            const int vi = lane + v * 32;
+            if (vi < nvec) {
+              Vec<T> o;
+#pragma unroll
+              for (int j = 0; j < VN; ++j) {
+                const float xv = xb[u][v].f(j);
+                o.set(j, p * gv[v].f(j) + dl * (r * qw[v][j] - r3 * xv));
+                acc[v][j] += dl * r * xv;
+              }
+              o.store(drow + vi * VN);
+            }
           }
-          o.store(drow + vi * VN);
         }
       }
     }
