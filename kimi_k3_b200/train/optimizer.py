@@ -126,14 +126,22 @@ def batched_newton_schulz(x: torch.Tensor, *, steps: int = 5, eps: float = 1e-7,
     return w.transpose(-2, -1) if transposed else w
 
 
-def newton_schulz_iterations(w: torch.Tensor, steps: int) -> torch.Tensor:
-    """The quintic iterations on an already normalised batch ``[N, m, n]`` with ``m <= n``."""
+def newton_schulz_iterations(w: torch.Tensor, steps: int, *, transpose_out: bool = False) -> torch.Tensor:
+    """The quintic iterations on an already normalised batch ``[N, m, n]`` with ``m <= n``.
+
+    Each step is ``X <- (a I + b G + c G^2) X`` with ``G = X X^T``: the small ``[m, m]`` polynomial
+    takes the ``a I`` term on its diagonal, so the big product is a plain batched GEMM (no copy of
+    X into the output as ``a X + P X`` would need).  ``transpose_out`` returns ``X^T`` [N, n, m]
+    contiguous, computed by the last step as ``X^T P`` (P is symmetric) instead of a transpose copy."""
     a, b, c = NS_COEFFS
-    for _ in range(steps):
+    for i in range(steps):
         gram = w @ w.transpose(-2, -1)
         poly = torch.baddbmm(gram, gram, gram, beta=b, alpha=c)  # b*G + c*G@G
-        w = torch.baddbmm(w, poly, w, beta=a, alpha=1.0)          # a*X + poly@X
-    return w
+        poly.diagonal(dim1=-2, dim2=-1).add_(a)                   # + a*I
+        if transpose_out and i == steps - 1:
+            return torch.bmm(w.transpose(-2, -1), poly)
+        w = torch.bmm(poly, w)
+    return w.transpose(-2, -1).contiguous() if transpose_out else w
 
 
 @torch.no_grad()
@@ -568,8 +576,8 @@ class KimiMuon(torch.optim.Optimizer):
         C.muon_momentum(g, mom_buf, x, sumsq, float(group["momentum"]), bool(group["nesterov"]), skip)
         C.muon_normalize(x, sumsq, float(group["eps"]))
         transposed = rows > cols
-        w = newton_schulz_iterations(x.transpose(-2, -1) if transposed else x, group["ns_steps"])
-        o = (w.transpose(-2, -1) if transposed else w).contiguous()
+        o = newton_schulz_iterations(x.transpose(-2, -1) if transposed else x, group["ns_steps"],
+                                     transpose_out=transposed).contiguous()
         scale = max(rows, cols) ** 0.5 if group["update_rms_scaling"] else 1.0
         lr_t = lr.reshape(()).float() if torch.is_tensor(lr) else torch.full((), float(lr), device=dev)
         ptr_t, own_t = self._bucket_tables(bi, ps, slots, dev)
