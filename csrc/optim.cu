@@ -84,7 +84,21 @@ __global__ void __launch_bounds__(kThreads) muon_normalize_kernel(__nv_bfloat16*
   const float inv = 1.f / fmaxf(sqrtf(sumsq[m]), eps);
   __nv_bfloat162* xm = reinterpret_cast<__nv_bfloat162*>(x + (int64_t)m * mn);
   const int64_t n2 = mn / 2;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n2; i += (int64_t)gridDim.x * blockDim.x) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  // eight values (16 bytes) per step when the matrix starts on a 16-byte boundary
+  const bool vec = (mn & 7) == 0 && (reinterpret_cast<uintptr_t>(xm) & 15) == 0;
+  const int64_t n8 = vec ? mn / 8 : 0;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += stride) {
+    uint4 raw = reinterpret_cast<uint4*>(xm)[i];
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float2 f = __bfloat1622float2(h[u]);
+      h[u] = __floats2bfloat162_rn(f.x * inv, f.y * inv);
+    }
+    reinterpret_cast<uint4*>(xm)[i] = raw;
+  }
+  for (int64_t i = n8 * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n2; i += stride) {
     float2 f = __bfloat1622float2(xm[i]);
     xm[i] = __floats2bfloat162_rn(f.x * inv, f.y * inv);
   }
@@ -111,7 +125,30 @@ __global__ void __launch_bounds__(kThreads) muon_apply_kernel(const __nv_bfloat1
   const __nv_bfloat16* om = o + (int64_t)m * mn;
   float* pm = params[m];
   float so = 0.f, su = 0.f, sp = 0.f;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < mn; i += (int64_t)gridDim.x * blockDim.x) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t t0 = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  // four elements per step (16-byte parameter and 8-byte update accesses) when aligned
+  const bool vec = (mn & 3) == 0 && (reinterpret_cast<uintptr_t>(pm) & 15) == 0;
+  const int64_t nv = vec ? mn / 4 : 0;
+  for (int64_t i = t0; i < nv; i += stride) {
+    const uint2 raw = reinterpret_cast<const uint2*>(om)[i];
+    const float2 o01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+    const float2 o23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+    const float ov[4] = {o01.x, o01.y, o23.x, o23.y};
+    float4 pv = reinterpret_cast<float4*>(pm)[i];
+    float pa[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float o = ov[u] * keep;
+      so += o * o;
+      sp += pa[u] * pa[u];
+      const float up = o * scale;
+      su += up * up;
+      pa[u] = pa[u] * decay + coef * ov[u];
+    }
+    reinterpret_cast<float4*>(pm)[i] = make_float4(pa[0], pa[1], pa[2], pa[3]);
+  }
+  for (int64_t i = nv * 4 + t0; i < mn; i += stride) {
     const float ov = __bfloat162float(om[i]) * keep;
     const float pv = pm[i];
     so += ov * ov;
