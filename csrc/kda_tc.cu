@@ -809,29 +809,34 @@ struct StateArgs {
   int* status;
 };
 
+// Forward pass: ONE sequence per CTA (grid = B * H), operand tiles of 64 rows (96 KB of shared
+// memory, 256 TMEM columns), so two CTAs share an SM and every SM has work.  The M = 128 MMAs read
+// 64 rows past each 64-row A tile (the next tile's memory); those accumulator lanes are ignored.
+// Threads of warps 0, 1, 4, 5 own rows 0..63 (column halves); warps 2, 3, 6, 7 help with loads.
+constexpr size_t kStateFwdSmem = 1024 + 96 * KB + 16;
+
 template <typename T>
-__global__ void __launch_bounds__(NTH, 1) kda_state_fwd_tc_kernel(const __grid_constant__ StateArgs a) {
+__global__ void __launch_bounds__(NTH, 2) kda_state_fwd_tc_kernel(const __grid_constant__ StateArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* tW = reinterpret_cast<float*>(base);                  // R128 K64  [W]
-  float* tKT = reinterpret_cast<float*>(base + 32 * KB);       // R128 K64  [Kend^T]
-  float* tQP = reinterpret_cast<float*>(base + 64 * KB);       // R128 K128 [Qg | P]
-  float* tSV = reinterpret_cast<float*>(base + 128 * KB);      // R128 K128 [S^T | V'^T]
-  uint64_t* bar = reinterpret_cast<uint64_t*>(base + 192 * KB);
+  float* tW = reinterpret_cast<float*>(base);                  // R64 K64  [W]
+  float* tKT = reinterpret_cast<float*>(base + 16 * KB);       // R64 K64  [Kend^T]
+  float* tQP = reinterpret_cast<float*>(base + 32 * KB);       // R64 K128 [Qg | P]
+  float* tSV = reinterpret_cast<float*>(base + 64 * KB);       // R64 K128 [S^T | V'^T]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(base + 96 * KB);
   uint32_t* slot = reinterpret_cast<uint32_t*>(bar + 1);
   const int tid = threadIdx.x, warp = tid >> 5;
-  const int row = (warp & 3) * 32 + (tid & 31), sq = row >> 6, r = row & 63, half = warp >> 2, c0 = 32 * half;
+  const int row = (warp & 3) * 32 + (tid & 31), r = row & 63, half = warp >> 2, c0 = 32 * half;
   const int BH = a.B * a.H, NC = a.NC;
-  const int bh0 = 2 * blockIdx.x;
-  const bool valid[2] = {bh0 < BH, bh0 + 1 < BH};
-  const int my_bh = bh0 + sq;
-  const bool mine = my_bh < BH;
+  const int my_bh = blockIdx.x;
+  const bool valid = my_bh < BH;
+  const bool mine = valid && row < 64;
   if (tid == 0) {
     tc::mbar_init(bar, 1);
     tc::fence_barrier_init();
   }
   if (warp == 0) {
-    tc::tmem_alloc(slot, 512);
+    tc::tmem_alloc(slot, 256);
     tc::tmem_relinquish();
   }
   tc::tc_fence_before();
@@ -843,93 +848,96 @@ __global__ void __launch_bounds__(NTH, 1) kda_state_fwd_tc_kernel(const __grid_c
 #pragma unroll
   for (int u = 0; u < 32; ++u)
     S[u] = (mine && a.init) ? a.init[(int64_t)my_bh * 4096 + r * 64 + c0 + u] : 0.f;
-  const int b = my_bh / a.H, h = my_bh % a.H;
-  const int64_t rs = (int64_t)a.H * 64;
+  const int b = valid ? my_bh / a.H : 0, h = valid ? my_bh % a.H : 0;
   for (int c = 0; c < NC; ++c) {
+    const int64_t bo = ((int64_t)my_bh * NC + c) * 4096;
     // states[c] = S; S^T -> tSV[k 0..63]
     if (mine) {
-      float* dst = a.buf.states + ((int64_t)my_bh * NC + c) * 4096 + r * 64 + c0;
+      float* dst = a.buf.states + bo + r * 64 + c0;
 #pragma unroll
       for (int u = 0; u < 32; u += 4) *reinterpret_cast<float4*>(dst + u) = make_float4(S[u], S[u + 1], S[u + 2], S[u + 3]);
+#pragma unroll
+      for (int u = 0; u < 32; ++u) tcs::st(tSV, 64, c0 + u, r, S[u]);
     }
+    {  // W, Qg, P, Kend: 16 float4 loads in flight per thread, then the stores
+      float4 ld[4][4];
+      const float* srcs[4] = {a.buf.W + bo, a.buf.Qg + bo, a.buf.P + bo, a.buf.Kend + bo};
 #pragma unroll
-    for (int u = 0; u < 32; ++u) tcs::st(tSV, 128, 64 * sq + c0 + u, r, S[u]);
-    {  // W, Qg, P, Kend of both sequences: 32 float4 loads in flight per thread, then the stores
-      float4 ld[2][4][4];
-#pragma unroll
-      for (int s2 = 0; s2 < 2; ++s2) {
-        const int64_t bo = ((int64_t)(bh0 + s2) * NC + c) * 4096;
-        const float* srcs[4] = {a.buf.W + bo, a.buf.Qg + bo, a.buf.P + bo, a.buf.Kend + bo};
-#pragma unroll
-        for (int t4 = 0; t4 < 4; ++t4)
-#pragma unroll
-          for (int n = 0; n < 4; ++n) {
-            const int idx = tid + n * NTH, rr = idx >> 4, cc = (idx & 15) * 4;
-            ld[s2][t4][n] = valid[s2] ? *reinterpret_cast<const float4*>(srcs[t4] + rr * 64 + cc)
-                                      : make_float4(0.f, 0.f, 0.f, 0.f);
-          }
-      }
-#pragma unroll
-      for (int s2 = 0; s2 < 2; ++s2)
+      for (int t4 = 0; t4 < 4; ++t4)
 #pragma unroll
         for (int n = 0; n < 4; ++n) {
           const int idx = tid + n * NTH, rr = idx >> 4, cc = (idx & 15) * 4;
-          tcs::st4(tW, 128, 64 * s2 + rr, cc, ld[s2][0][n]);
-          tcs::st4(tQP, 128, 64 * s2 + rr, cc, ld[s2][1][n]);
-          tcs::st4(tQP, 128, 64 * s2 + rr, 64 + cc, ld[s2][2][n]);
-          const float4 kt = ld[s2][3][n];  // Kend row rr, columns cc..cc+3 -> transposed rows
-          tcs::st(tKT, 128, 64 * s2 + cc, rr, kt.x);
-          tcs::st(tKT, 128, 64 * s2 + cc + 1, rr, kt.y);
-          tcs::st(tKT, 128, 64 * s2 + cc + 2, rr, kt.z);
-          tcs::st(tKT, 128, 64 * s2 + cc + 3, rr, kt.w);
+          ld[t4][n] = valid ? *reinterpret_cast<const float4*>(srcs[t4] + rr * 64 + cc) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        const int idx = tid + n * NTH, rr = idx >> 4, cc = (idx & 15) * 4;
+        tcs::st4(tW, 64, rr, cc, ld[0][n]);
+        tcs::st4(tQP, 64, rr, cc, ld[1][n]);
+        tcs::st4(tQP, 64, rr, 64 + cc, ld[2][n]);
+        const float4 kt = ld[3][n];  // Kend row rr, columns cc..cc+3 -> transposed rows
+        tcs::st(tKT, 64, cc, rr, kt.x);
+        tcs::st(tKT, 64, cc + 1, rr, kt.y);
+        tcs::st(tKT, 64, cc + 2, rr, kt.z);
+        tcs::st(tKT, 64, cc + 3, rr, kt.w);
+      }
     }
     tcs::operands_ready();
     if (tid == 0) {
-      tcs::mma_rows128(tm, tW, 128, tSV, 128, 0, 128, 0, 64, false);  // W S  -> cols [0,128)
+      tcs::mma_rows128(tm, tW, 64, tSV, 64, 0, 64, 0, 64, false);  // W S -> cols [0, 64)
       tc::mma_commit(bar);
     }
     tcs::mma_done(bar, phase, a.status, 21);
-    const int64_t bo = ((int64_t)my_bh * NC + c) * 4096;
-    {  // V' = U - W S  (row i = r of sequence sq)
+    {  // V' = U - W S  (row r)
       float val[32];
       float4 ur[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u)
         ur[u] = mine ? *reinterpret_cast<const float4*>(a.buf.U + bo + r * 64 + c0 + 4 * u) : make_float4(0, 0, 0, 0);
-      tcs::tmem_row32(tm, warp, 64 * sq + c0, val);
+      tcs::tmem_row32(tm, warp, c0, val);
+      if (mine) {
 #pragma unroll
-      for (int u = 0; u < 32; u += 4) {
-        const float4 uu = ur[u / 4];
-        const float4 vp = make_float4(uu.x - val[u], uu.y - val[u + 1], uu.z - val[u + 2], uu.w - val[u + 3]);
-        if (mine) *reinterpret_cast<float4*>(a.buf.Vp + bo + r * 64 + c0 + u) = vp;
-        tcs::st(tSV, 128, 64 * sq + c0 + u, 64 + r, vp.x);
-        tcs::st(tSV, 128, 64 * sq + c0 + u + 1, 64 + r, vp.y);
-        tcs::st(tSV, 128, 64 * sq + c0 + u + 2, 64 + r, vp.z);
-        tcs::st(tSV, 128, 64 * sq + c0 + u + 3, 64 + r, vp.w);
+        for (int u = 0; u < 32; u += 4) {
+          const float4 uu = ur[u / 4];
+          const float4 vp = make_float4(uu.x - val[u], uu.y - val[u + 1], uu.z - val[u + 2], uu.w - val[u + 3]);
+          *reinterpret_cast<float4*>(a.buf.Vp + bo + r * 64 + c0 + u) = vp;
+          tcs::st(tSV, 64, c0 + u, 64 + r, vp.x);
+          tcs::st(tSV, 64, c0 + u + 1, 64 + r, vp.y);
+          tcs::st(tSV, 64, c0 + u + 2, 64 + r, vp.z);
+          tcs::st(tSV, 64, c0 + u + 3, 64 + r, vp.w);
+        }
       }
     }
     tcs::operands_ready();
     if (tid == 0) {
-      tcs::mma_rows128(tm + 128, tQP, 128, tSV, 128, 0, 128, 0, 128, false);  // Qg S + P V' -> [128,256)
-      tcs::mma_rows128_ab(tm + 256, tKT, 128, 0, tSV, 128, 0, 64, 128, 64, false);  // Kend^T V' -> [256,384)
+      tcs::mma_rows128(tm + 64, tQP, 64, tSV, 64, 0, 64, 0, 128, false);           // Qg S + P V' -> [64, 128)
+      tcs::mma_rows128_ab(tm + 128, tKT, 64, 0, tSV, 64, 0, 64, 64, 64, false);  // Kend^T V' -> [128, 192)
       tc::mma_commit(bar);
     }
     tcs::mma_done(bar, phase, a.status, 22);
     {
       float val[32];
-      tcs::tmem_row32(tm + 128, warp, 64 * sq + c0, val);
+      tcs::tmem_row32(tm + 64, warp, c0, val);
       if (mine) {
         T* o = reinterpret_cast<T*>(a.y) + (((int64_t)b * a.Tp + c * 64 + r) * a.H + h) * 64 + c0;
+        if constexpr (sizeof(T) == 2) {
 #pragma unroll
-        for (int u = 0; u < 32; ++u) o[u] = from_f<T>(val[u]);
+          for (int u = 0; u < 32; u += 8) {
+            Vec<T> v8;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v8.set(e, val[u + e]);
+            v8.store(o + u);
+          }
+        } else {
+#pragma unroll
+          for (int u = 0; u < 32; ++u) o[u] = from_f<T>(val[u]);
+        }
       }
-      tcs::tmem_row32(tm + 256, warp, 64 * sq + c0, val);
+      tcs::tmem_row32(tm + 128, warp, c0, val);
       const float e = mine ? a.buf.eGC[((int64_t)my_bh * NC + c) * 64 + r] : 0.f;
 #pragma unroll
       for (int u = 0; u < 32; ++u) S[u] = e * S[u] + val[u];
     }
-    (void)rs;
   }
   if (mine && a.fin) {
     float* dst = a.fin + (int64_t)my_bh * 4096 + r * 64 + c0;
@@ -939,7 +947,7 @@ __global__ void __launch_bounds__(NTH, 1) kda_state_fwd_tc_kernel(const __grid_c
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
-  if (warp == 0) tc::tmem_dealloc(tm, 512);
+  if (warp == 0) tc::tmem_dealloc(tm, 256);
 }
 
 template <typename T>
@@ -1077,18 +1085,17 @@ cudaError_t launch_state(bool fwd, const StateArgs& args, cudaStream_t s) {
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kda_state_fwd_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)kStateSmem);
+                                         (int)kStateFwdSmem);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(kda_state_bwd_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)kStateSmem);
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  const int grid = (args.B * args.H + 1) / 2;
   if (fwd)
-    kda_state_fwd_tc_kernel<T><<<grid, NTH, kStateSmem, s>>>(args);
+    kda_state_fwd_tc_kernel<T><<<args.B * args.H, NTH, kStateFwdSmem, s>>>(args);
   else
-    kda_state_bwd_tc_kernel<T><<<grid, NTH, kStateSmem, s>>>(args);
+    kda_state_bwd_tc_kernel<T><<<(args.B * args.H + 1) / 2, NTH, kStateSmem, s>>>(args);
   return cudaGetLastError();
 }
 
