@@ -951,27 +951,27 @@ __global__ void __launch_bounds__(NTH, 2) kda_state_fwd_tc_kernel(const __grid_c
 }
 
 template <typename T>
-__global__ void __launch_bounds__(NTH, 1) kda_state_bwd_tc_kernel(const __grid_constant__ StateArgs a) {
+__global__ void __launch_bounds__(NTH, 2) kda_state_bwd_tc_kernel(const __grid_constant__ StateArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* tA = reinterpret_cast<float*>(base);                // R128 K128 [P^T | Kend]   rows j
-  float* tB = reinterpret_cast<float*>(base + 64 * KB);      // R128 K128 [dO^T | dS^T -> dV'^T]  rows v
-  float* tC = reinterpret_cast<float*>(base + 128 * KB);     // R128 K128 [Qg^T | -W^T]  rows kk
-  uint64_t* bar = reinterpret_cast<uint64_t*>(base + 192 * KB);
+  float* tA = reinterpret_cast<float*>(base);                // R64 K128 [P^T | Kend]   rows j
+  float* tB = reinterpret_cast<float*>(base + 32 * KB);      // R64 K128 [dO^T | dS^T -> dV'^T]  rows v
+  float* tC = reinterpret_cast<float*>(base + 64 * KB);      // R64 K128 [Qg^T | -W^T]  rows kk
+  // 8 KB after tC: the M = 128 MMA over tC's last atom reads 64 rows past it
+  uint64_t* bar = reinterpret_cast<uint64_t*>(base + 104 * KB);
   uint32_t* slot = reinterpret_cast<uint32_t*>(bar + 1);
   const int tid = threadIdx.x, warp = tid >> 5;
-  const int row = (warp & 3) * 32 + (tid & 31), sq = row >> 6, r = row & 63, half = warp >> 2, c0 = 32 * half;
+  const int row = (warp & 3) * 32 + (tid & 31), r = row & 63, half = warp >> 2, c0 = 32 * half;
   const int BH = a.B * a.H, NC = a.NC;
-  const int bh0 = 2 * blockIdx.x;
-  const bool valid[2] = {bh0 < BH, bh0 + 1 < BH};
-  const int my_bh = bh0 + sq;
-  const bool mine = my_bh < BH;
+  const int my_bh = blockIdx.x;
+  const bool valid = my_bh < BH;
+  const bool mine = valid && row < 64;
   if (tid == 0) {
     tc::mbar_init(bar, 1);
     tc::fence_barrier_init();
   }
   if (warp == 0) {
-    tc::tmem_alloc(slot, 512);
+    tc::tmem_alloc(slot, 128);
     tc::tmem_relinquish();
   }
   tc::tc_fence_before();
@@ -992,13 +992,14 @@ __global__ void __launch_bounds__(NTH, 1) kda_state_bwd_tc_kernel(const __grid_c
       for (int u = 0; u < 32; u += 4)
         *reinterpret_cast<float4*>(dst + u) = make_float4(dS[u], dS[u + 1], dS[u + 2], dS[u + 3]);
     }
+    if (mine) {
 #pragma unroll
-    for (int u = 0; u < 32; ++u) tcs::st(tB, 128, 64 * sq + c0 + u, 64 + r, dS[u]);
-#pragma unroll
-    for (int s2 = 0; s2 < 2; ++s2) {
-      const int bh = bh0 + s2;
+      for (int u = 0; u < 32; ++u) tcs::st(tB, 64, c0 + u, 64 + r, dS[u]);
+    }
+    {
+      const int bh = my_bh;
       const int64_t bo = ((int64_t)bh * NC + c) * 4096;
-      const int bb = valid[s2] ? bh / a.H : 0, hh = valid[s2] ? bh % a.H : 0;
+      const int bb = valid ? bh / a.H : 0, hh = valid ? bh % a.H : 0;
       const T* dO = dout + (((int64_t)bb * a.Tp + c * 64) * a.H + hh) * 64;
       // the five operand tiles of this sequence: 20 loads in flight per thread, then the stores
       float4 ld[5][4];
@@ -1006,44 +1007,44 @@ __global__ void __launch_bounds__(NTH, 1) kda_state_bwd_tc_kernel(const __grid_c
       for (int n = 0; n < 4; ++n) {
         const int idx = tid + n * NTH, rr = idx >> 4, cc = (idx & 15) * 4;
         const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-        ld[0][n] = valid[s2] ? *reinterpret_cast<const float4*>(a.buf.P + bo + rr * 64 + cc) : z;
-        ld[1][n] = valid[s2] ? *reinterpret_cast<const float4*>(a.buf.Kend + bo + rr * 64 + cc) : z;
-        if (valid[s2]) {
+        ld[0][n] = valid ? *reinterpret_cast<const float4*>(a.buf.P + bo + rr * 64 + cc) : z;
+        ld[1][n] = valid ? *reinterpret_cast<const float4*>(a.buf.Kend + bo + rr * 64 + cc) : z;
+        if (valid) {
           const T* pd = dO + rr * rs + cc;
           ld[2][n] = make_float4(to_f<T>(pd[0]), to_f<T>(pd[1]), to_f<T>(pd[2]), to_f<T>(pd[3]));
         } else {
           ld[2][n] = z;
         }
-        ld[3][n] = valid[s2] ? *reinterpret_cast<const float4*>(a.buf.Qg + bo + rr * 64 + cc) : z;
-        ld[4][n] = valid[s2] ? *reinterpret_cast<const float4*>(a.buf.W + bo + rr * 64 + cc) : z;
+        ld[3][n] = valid ? *reinterpret_cast<const float4*>(a.buf.Qg + bo + rr * 64 + cc) : z;
+        ld[4][n] = valid ? *reinterpret_cast<const float4*>(a.buf.W + bo + rr * 64 + cc) : z;
       }
 #pragma unroll
       for (int n = 0; n < 4; ++n) {
         const int idx = tid + n * NTH, rr = idx >> 4, cc = (idx & 15) * 4;
-        tcs::st4(tA, 128, 64 * s2 + rr, 64 + cc, ld[1][n]);  // Kend
+        tcs::st4(tA, 64, rr, 64 + cc, ld[1][n]);  // Kend
         const float vP[4] = {ld[0][n].x, ld[0][n].y, ld[0][n].z, ld[0][n].w};
         const float vD[4] = {ld[2][n].x, ld[2][n].y, ld[2][n].z, ld[2][n].w};
         const float vQ[4] = {ld[3][n].x, ld[3][n].y, ld[3][n].z, ld[3][n].w};
         const float vW[4] = {ld[4][n].x, ld[4][n].y, ld[4][n].z, ld[4][n].w};
 #pragma unroll
         for (int u = 0; u < 4; ++u) {  // transposed tiles: source column cc + u -> tile row
-          tcs::st(tA, 128, 64 * s2 + cc + u, rr, vP[u]);
-          tcs::st(tB, 128, 64 * s2 + cc + u, rr, vD[u]);
-          tcs::st(tC, 128, 64 * s2 + cc + u, rr, vQ[u]);
-          tcs::st(tC, 128, 64 * s2 + cc + u, 64 + rr, -vW[u]);
+          tcs::st(tA, 64, cc + u, rr, vP[u]);
+          tcs::st(tB, 64, cc + u, rr, vD[u]);
+          tcs::st(tC, 64, cc + u, rr, vQ[u]);
+          tcs::st(tC, 64, cc + u, 64 + rr, -vW[u]);
         }
       }
     }
     tcs::operands_ready();
     if (tid == 0) {
-      tcs::mma_rows128(tm, tA, 128, tB, 128, 0, 128, 0, 128, false);  // dV' -> cols [0,128)
+      tcs::mma_rows128(tm, tA, 64, tB, 64, 0, 64, 0, 128, false);  // dV' -> cols [0, 64)
       tc::mma_commit(bar);
     }
     tcs::mma_done(bar, phase, a.status, 23);
     const int64_t bo = ((int64_t)my_bh * NC + c) * 4096;
     {
       float val[32];
-      tcs::tmem_row32(tm, warp, 64 * sq + c0, val);
+      tcs::tmem_row32(tm, warp, c0, val);
       if (mine) {
         float* dst = a.dVp + bo + r * 64 + c0;
 #pragma unroll
@@ -1051,17 +1052,18 @@ __global__ void __launch_bounds__(NTH, 1) kda_state_bwd_tc_kernel(const __grid_c
           *reinterpret_cast<float4*>(dst + u) = make_float4(val[u], val[u + 1], val[u + 2], val[u + 3]);
       }
 #pragma unroll
-      for (int u = 0; u < 32; ++u) tcs::st(tB, 128, 64 * sq + c0 + u, 64 + r, val[u]);  // dV'^T
+      for (int u = 0; u < 32; ++u)
+        if (mine) tcs::st(tB, 64, c0 + u, 64 + r, val[u]);  // dV'^T
     }
     tcs::operands_ready();
     if (tid == 0) {
-      tcs::mma_rows128(tm + 128, tC, 128, tB, 128, 0, 128, 0, 128, false);  // Qg^T dO - W^T dV'
+      tcs::mma_rows128(tm + 64, tC, 64, tB, 64, 0, 64, 0, 128, false);  // Qg^T dO - W^T dV'
       tc::mma_commit(bar);
     }
     tcs::mma_done(bar, phase, a.status, 24);
     {
       float val[32];
-      tcs::tmem_row32(tm + 128, warp, 64 * sq + c0, val);
+      tcs::tmem_row32(tm + 64, warp, c0, val);
       const float e = mine ? a.buf.eGC[((int64_t)my_bh * NC + c) * 64 + r] : 0.f;
 #pragma unroll
       for (int u = 0; u < 32; ++u) dS[u] = e * dS[u] + val[u];
@@ -1075,10 +1077,10 @@ __global__ void __launch_bounds__(NTH, 1) kda_state_bwd_tc_kernel(const __grid_c
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
-  if (warp == 0) tc::tmem_dealloc(tm, 512);
+  if (warp == 0) tc::tmem_dealloc(tm, 128);
 }
 
-constexpr size_t kStateSmem = 1024 + 192 * KB + 16;
+constexpr size_t kStateSmem = 1024 + 104 * KB + 16;  // backward: three R64 K128 tiles + 8 KB of read-past room
 
 template <typename T>
 cudaError_t launch_state(bool fwd, const StateArgs& args, cudaStream_t s) {
@@ -1095,7 +1097,7 @@ cudaError_t launch_state(bool fwd, const StateArgs& args, cudaStream_t s) {
   if (fwd)
     kda_state_fwd_tc_kernel<T><<<args.B * args.H, NTH, kStateFwdSmem, s>>>(args);
   else
-    kda_state_bwd_tc_kernel<T><<<(args.B * args.H + 1) / 2, NTH, kStateSmem, s>>>(args);
+    kda_state_bwd_tc_kernel<T><<<args.B * args.H, NTH, kStateSmem, s>>>(args);
   return cudaGetLastError();
 }
 
