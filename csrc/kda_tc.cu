@@ -644,22 +644,31 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_fwd_tc_kernel(const __grid_c
   const int H = a.H, Tp = a.Tp, NC = a.NC;
   const int total = a.B * H * NC;
   const int64_t rs = (int64_t)H * 64;
-  for (int ci = blockIdx.x; ci < total; ci += gridDim.x) {
-    const int bh = ci / NC, c = ci % NC, b = bh / H, h = bh % H, t0 = c * C;
-    const int64_t bo = ((int64_t)bh * NC + c) * C * 64;
-    const int64_t tok0 = tok_off(b, t0, h, Tp, H);
-    const T* q = reinterpret_cast<const T*>(a.q) + tok0;
-    const T* k = reinterpret_cast<const T*>(a.k) + tok0;
-    const T* v = reinterpret_cast<const T*>(a.v) + tok0;
-    const float* g = a.g + tok0;
-    {
-      float gv[16];
+  // The global inputs of a chunk (g, beta, q, k, v) are loaded into registers one chunk ahead:
+  // the loads of chunk ci + gridDim.x are issued before chunk ci's solve and land while it runs.
+  float gv[16], kr[16], qr[16], vr[16], bt = 0.f;
+  auto load_chunk = [&](int cj) {
+    const int bhj = cj / NC, cc = cj % NC, bj = bhj / H, hj = bhj % H;
+    const int64_t tj = tok_off(bj, cc * C, hj, Tp, H);
+    const float* gj = a.g + tj;
+    const T* qj = reinterpret_cast<const T*>(a.q) + tj;
+    const T* kj = reinterpret_cast<const T*>(a.k) + tj;
+    const T* vj = reinterpret_cast<const T*>(a.v) + tj;
 #pragma unroll
-      for (int n = 0; n < 16; ++n) {
-        const int idx = tid + n * NTH;
-        gv[n] = g[(idx >> 6) * rs + (idx & 63)];
-      }
-      const float bt = tid < C ? a.beta[((int64_t)b * Tp + t0 + tid) * H + h] : 0.f;
+    for (int n = 0; n < 16; ++n) {
+      const int idx = tid + n * NTH, i = idx >> 6, d = idx & 63;
+      gv[n] = gj[i * rs + d];
+      kr[n] = to_f<T>(kj[i * rs + d]);
+      qr[n] = to_f<T>(qj[i * rs + d]);
+      vr[n] = to_f<T>(vj[i * rs + d]);
+    }
+    bt = tid < C ? a.beta[((int64_t)bj * Tp + cc * C + tid) * H + hj] : 0.f;
+  };
+  if (blockIdx.x < total) load_chunk(blockIdx.x);
+  for (int ci = blockIdx.x; ci < total; ci += gridDim.x) {
+    const int bh = ci / NC, c = ci % NC;
+    const int64_t bo = ((int64_t)bh * NC + c) * C * 64;
+    {
 #pragma unroll
       for (int n = 0; n < 16; ++n) {
         const int idx = tid + n * NTH;
@@ -689,14 +698,6 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_fwd_tc_kernel(const __grid_c
     // operands, elementwise outputs and the solve's right-hand side [k e^G | v]; every load of the
     // chunk is issued before the first store, so the loads overlap instead of paying one
     // round trip per element group
-    float kr[16], qr[16], vr[16];
-#pragma unroll
-    for (int n = 0; n < 16; ++n) {
-      const int idx = tid + n * NTH, i = idx >> 6, d = idx & 63;
-      kr[n] = to_f<T>(k[i * rs + d]);
-      qr[n] = to_f<T>(q[i * rs + d]);
-      vr[n] = to_f<T>(v[i * rs + d]);
-    }
 #pragma unroll
     for (int n = 0; n < 16; ++n) {
       const int idx = tid + n * NTH;
@@ -745,6 +746,7 @@ __global__ void __launch_bounds__(NTH, 1) kda_intra_fwd_tc_kernel(const __grid_c
       }
     }
     __syncthreads();
+    if (ci + (int)gridDim.x < total) load_chunk(ci + gridDim.x);  // lands during the solve
     // forward substitution: X_i = beta_i (R_i - sum_{j<i} A_ij X_j), 16-row blocks from the top
     if (tid < 128) {
       const int col = tid;
