@@ -155,3 +155,19 @@ def test_depth_softmax_mix_matches_reference():
     ra = ra if torch.is_tensor(ra) else ra[0]
     oa = oa if torch.is_tensor(oa) else oa[0]
     assert max_diff(ra, oa) < 1e-12
+
+
+def test_dense_small_batch_experts_matches_sparse_dispatch():
+    """The decode-size expert path (every expert on every token, unselected weights zero) equals
+    the routed dispatch (fp64)."""
+    import torch
+    from kimi_k3_b200.models.moe import GroupedRoutedExperts, dense_small_batch_experts, vectorized_sparse_dispatch
+    torch.manual_seed(0)
+    ex = GroupedRoutedExperts(6, 32, 48, 4.0, 25.0, 0.2).double()
+    x = torch.randn(5, 32, dtype=torch.float64)
+    sel = torch.stack([torch.randperm(6)[:2] for _ in range(5)])
+    w = torch.rand(5, 2, dtype=torch.float64)
+    with torch.no_grad():
+        got = dense_small_batch_experts(x, ex, sel, w, torch.float64)
+        ref = vectorized_sparse_dispatch(x, ex, sel, w, accumulation_dtype=torch.float64)
+    assert torch.allclose(got, ref, atol=1e-10, rtol=1e-9)

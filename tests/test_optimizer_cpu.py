@@ -138,3 +138,22 @@ def test_scheduler_matches_reference():
             assert abs(a["adamw_lr"] - b["adamw_lr"]) < 1e-15 and abs(a["muon_lr"] - b["muon_lr"]) < 1e-15
         s1.step()
         s2.step()
+
+
+def test_newton_schulz_reformulation_and_transposed_output():
+    """``(aI + bG + cG^2) X`` equals ``aX + (bG + cG^2) X`` (fp64), and ``transpose_out`` returns
+    the transpose of the plain result."""
+    import torch
+    from kimi_k3_b200.train.optimizer import NS_COEFFS, newton_schulz_iterations
+    torch.manual_seed(0)
+    x = torch.randn(3, 16, 40, dtype=torch.float64)
+    x = x / x.flatten(1).norm(dim=1)[:, None, None]
+    a, b, c = NS_COEFFS
+    w = x.clone()
+    for _ in range(5):
+        g = w @ w.transpose(-2, -1)
+        w = a * w + (b * g + c * g @ g) @ w
+    got = newton_schulz_iterations(x.clone(), 5)
+    assert torch.allclose(got, w, atol=1e-10, rtol=1e-10)
+    got_t = newton_schulz_iterations(x.clone(), 5, transpose_out=True)
+    assert got_t.is_contiguous() and torch.allclose(got_t, w.transpose(-2, -1), atol=1e-10, rtol=1e-10)
