@@ -93,6 +93,13 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                : "memory");
 }
 
+constexpr float kLog2e = 1.4426950408889634f;  // log2(e)
+__device__ __forceinline__ float exp2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kStagedThreads, 1) ce_rows_staged_kernel(T* __restrict__ logits, int64_t ld,
                                                                            int64_t rows, int vocab,
@@ -137,12 +144,15 @@ __global__ void __launch_bounds__(kStagedThreads, 1) ce_rows_staged_kernel(T* __
     }
     for (int i = nv * VN + tid; i < vocab; i += kStagedThreads) m = fmaxf(m, to_f<T>(sr[i]));
     const float gm = block_max(m, scratch);
+    // e^{x - m} as 2^{(x - m) log2 e} on the hardware exp2 (relative error near 2^-22): the row's
+    // two exponential passes are what bounds this kernel
+    const float gml = gm * kLog2e;
     float se = 0.f;
     for (int i = tid; i < nv; i += kStagedThreads) {
       Vec<T> a;
       a.load(sr + i * VN);
 #pragma unroll
-      for (int j = 0; j < VN; ++j) se += expf(a.f(j) - gm);
+      for (int j = 0; j < VN; ++j) se += exp2_approx(fmaf(a.f(j), kLog2e, -gml));
     }
     for (int i = nv * VN + tid; i < vocab; i += kStagedThreads) se += expf(to_f<T>(sr[i]) - gm);
     const float lse = gm + logf(block_sum(se, scratch));
@@ -150,6 +160,7 @@ __global__ void __launch_bounds__(kStagedThreads, 1) ce_rows_staged_kernel(T* __
     const int64_t tgt = ok ? targets[row] : -1;
     if (tid == 0) loss_rows[row] = (ok && tgt >= 0 && tgt < vocab) ? lse - to_f<T>(sr[tgt]) : 0.f;
     const float sc = ok ? grad_scale : 0.f;
+    const float lsel = lse * kLog2e;
     T* gr = logits + row * ld;
     for (int i = tid; i < nv; i += kStagedThreads) {
       Vec<T> a;
@@ -157,7 +168,7 @@ __global__ void __launch_bounds__(kStagedThreads, 1) ce_rows_staged_kernel(T* __
 #pragma unroll
       for (int j = 0; j < VN; ++j) {
         const int64_t col = (int64_t)i * VN + j;
-        a.set(j, sc * (expf(a.f(j) - lse) - (col == tgt ? 1.f : 0.f)));
+        a.set(j, sc * (exp2_approx(fmaf(a.f(j), kLog2e, -lsel)) - (col == tgt ? 1.f : 0.f)));
       }
       a.store(gr + i * VN);
     }
