@@ -381,7 +381,9 @@ cudaError_t rms_norm_bwd(int dtype, const void* dy, const void* x, const float* 
     if (dw && grid > 148 * 4) grid = 148 * 4;
     const int nvec = dim / Vec<T>::N;
     if (p == 1 && nvec <= 32 * 4) {
-      const int wgrid = (int)std::min<int64_t>((rows + 7) / 8, 148 * 8);
+      // with dw, every block ends with one global atomic per weight element: two blocks per SM keep
+      // those few hundred per element (eight per SM made the flush, not the rows, the cost)
+      const int wgrid = (int)std::min<int64_t>((rows + 7) / 8, dw ? 148 * 2 : 148 * 8);
       const size_t wsmem = dw ? (size_t)dim * sizeof(float) : 0;
       if (nvec <= 32)
         rms_bwd_warp_kernel<T, 1><<<wgrid, 256, wsmem, s>>>((const T*)dy, (const T*)x, w, rstd, (T*)dx, dw, rows, dim);
