@@ -3,6 +3,8 @@
 // and an fp32 weighted sum of the raw sources. One warp per token; each source tensor is
 // read through its own pointer (no stacked copy), once for the logits and once for the sum
 // (once in all when there are at most four sources).
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -296,7 +298,9 @@ static cudaError_t bwd_impl(const void* const* sources, int S, const float* q, c
   const int threads = 256;
   const int mv = maxv_for<T>(dim);
   KIMI_MAXV_SWITCH(mv, MV, {
-    attnres_bwd_kernel<T, MV><<<grid_tokens(tokens, threads / 32), threads, dim * sizeof(float), s>>>(
+    // every block ends with 2 * dim global atomics into dq / dw: two blocks per SM keep the number
+    // per element in the hundreds
+    attnres_bwd_kernel<T, MV><<<std::min(grid_tokens(tokens, threads / 32), 148 * 2), threads, dim * sizeof(float), s>>>(
         ptrs, S, q, w, (const T*)dout, probs, rstd, dptrs, dq, dw, tokens, dim);
   });
   return cudaGetLastError();
