@@ -6,6 +6,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "device_info.h"
 #include "kernels.h"
 
 namespace kimi {
@@ -24,7 +25,8 @@ struct DstPtrs {
 
 int grid_tokens(int64_t tokens, int warps_per_block) {
   int64_t g = (tokens + warps_per_block - 1) / warps_per_block;
-  if (g > 148 * 8) g = 148 * 8;
+  const int64_t cap = (int64_t)device_sms() * 8;
+  if (g > cap) g = cap;
   return (int)(g < 1 ? 1 : g);
 }
 
@@ -300,7 +302,7 @@ static cudaError_t bwd_impl(const void* const* sources, int S, const float* q, c
   KIMI_MAXV_SWITCH(mv, MV, {
     // every block ends with 2 * dim global atomics into dq / dw: two blocks per SM keep the number
     // per element in the hundreds
-    attnres_bwd_kernel<T, MV><<<std::min(grid_tokens(tokens, threads / 32), 148 * 2), threads, dim * sizeof(float), s>>>(
+    attnres_bwd_kernel<T, MV><<<std::min(grid_tokens(tokens, threads / 32), device_sms() * 2), threads, dim * sizeof(float), s>>>(
         ptrs, S, q, w, (const T*)dout, probs, rstd, dptrs, dq, dw, tokens, dim);
   });
   return cudaGetLastError();

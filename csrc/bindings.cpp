@@ -442,8 +442,12 @@ static void check_tma_matrix(const at::Tensor& t, const char* name) {
 
 // Dense GEMM out[M,N] = op(a) op(b)^T on the tcgen05 kernel. Operands may be row-strided views
 // (any M, N, K; row strides multiples of 8 elements): tiles past the logical edge read zeros.
+// `status` (int32 CUDA tensor) receives the code of the first bounded wait that gave up; without it
+// the device's default status word does (tc_gemm_status).  `spin_limit` > 0 shortens every
+// pipeline wait to that many polls (tests use it to make a wait run out on purpose).
 at::Tensor tc_gemm_dense(at::Tensor a, at::Tensor b, bool a_mn, bool b_mn, bool out_fp32, int64_t bn,
-                         c10::optional<at::Tensor> out_opt) {
+                         c10::optional<at::Tensor> out_opt, c10::optional<at::Tensor> status_opt,
+                         int64_t spin_limit) {
   check_tma_matrix(a, "a");
   check_tma_matrix(b, "b");
   const at::cuda::CUDAGuard gd(a.device());
@@ -480,6 +484,11 @@ at::Tensor tc_gemm_dense(at::Tensor a, at::Tensor b, bool a_mn, bool b_mn, bool 
   g.out = out.data_ptr();
   g.out_fp32 = out.scalar_type() == at::kFloat;
   g.ldc = out.stride(0);
+  if (status_opt.has_value() && status_opt->defined()) {
+    TORCH_CHECK(status_opt->is_cuda() && status_opt->scalar_type() == at::kInt, "status must be an int32 CUDA tensor");
+    g.status = status_opt->data_ptr<int>();
+  }
+  g.spin_limit = (uint32_t)std::max<int64_t>(0, std::min<int64_t>(spin_limit, 0x7fffffff));
   int dev = a.get_device();
   g.num_sms = at::cuda::getDeviceProperties(dev)->multiProcessorCount;
   check(kimi::tc_gemm(g, stream()), "tc_gemm_dense");
@@ -1075,7 +1084,25 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kda_bwd", &kda_bwd);
   m.def("fa_fwd", &fa_fwd);
   m.def("fa_bwd", &fa_bwd);
-  m.def("tc_gemm_dense", &tc_gemm_dense);
+  m.def("tc_gemm_dense", &tc_gemm_dense, py::arg("a"), py::arg("b"), py::arg("a_mn"), py::arg("b_mn"),
+        py::arg("out_fp32"), py::arg("bn"), py::arg("out") = py::none(), py::arg("status") = py::none(),
+        py::arg("spin_limit") = 0);
+  // Views of the current device's default status words of the GEMM and the KDA kernels (int32
+  // [1] each, not owned): a training step copies them to pinned host memory with its other
+  // per-step flags, so a bounded wait that gave up inside a kernel surfaces at the next step.
+  m.def("status_words", []() {
+    const int dev = c10::cuda::current_device();
+    auto opts = at::TensorOptions().dtype(at::kInt).device(at::kCUDA, dev);
+    int* g = kimi::tc_gemm_default_status();
+    int* k = kimi::kda_tc_default_status();
+    TORCH_CHECK(g && k, "status words unavailable on this device");
+    return std::vector<at::Tensor>{at::from_blob(g, {1}, opts), at::from_blob(k, {1}, opts)};
+  });
+  m.def("tc_gemm_status", [](bool clear) {
+    const int v = kimi::tc_gemm_status(clear);
+    TORCH_CHECK(v >= 0, "reading the GEMM status word failed");
+    return v;
+  });
   m.def("tc_gemm_grouped", &tc_gemm_grouped);
   m.def("tc_gemm_comm", &tc_gemm_comm);
   m.def("tc_gemm_tiles", [](int64_t m, int64_t n, int64_t bn) { return kimi::tc_gemm_tiles((int)m, (int)n, (int)bn); });

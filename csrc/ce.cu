@@ -9,6 +9,7 @@
 // an mbarrier; no multicast), so the max / sum / gradient passes read shared memory and HBM sees
 // each logit read once and written once.  Other rows use the two-pass kernel below.
 #include "common.cuh"
+#include "device_info.h"
 #include "kernels.h"
 #include "tc_common.cuh"
 
@@ -133,7 +134,7 @@ __global__ void __launch_bounds__(kStagedThreads, 1) ce_rows_staged_kernel(T* __
       tc::mbar_arrive_expect_tx(&bars[b ^ 1], row_bytes);
       bulk_g2s(buf[b ^ 1], logits + next * ld, row_bytes, &bars[b ^ 1]);
     }
-    tc::mbar_wait(&bars[b], (uint32_t)((it >> 1) & 1), nullptr, 0);
+    tc::mbar_wait_local(&bars[b], (uint32_t)((it >> 1) & 1), nullptr, 0);
     const T* sr = buf[b];
     float m = -INFINITY;
     for (int i = tid; i < nv; i += kStagedThreads) {
@@ -188,17 +189,13 @@ cudaError_t ce_rows_fwd_bwd(int dtype, void* logits, int64_t ld, int64_t rows, i
                          (int64_t)row_bytes <= ld * 2;
     if (aligned && row_bytes <= (uint32_t)kMaxStagedBytes && rows > 0) {
       const size_t smem = 2 * (size_t)row_bytes;
-      const int grid = (int)(rows < 148 ? rows : 148);
-      static bool configured[2] = {false, false};
-      if (!configured[dtype - 1]) {  // the attribute covers the largest staged row
-        const cudaError_t e = dtype == 1 ? cudaFuncSetAttribute(ce_rows_staged_kernel<__nv_bfloat16>,
-                                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                                2 * kMaxStagedBytes)
-                                         : cudaFuncSetAttribute(ce_rows_staged_kernel<__half>,
-                                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                                2 * kMaxStagedBytes);
+      const int sms = device_sms();
+      const int grid = (int)(rows < sms ? rows : sms);
+      {  // the attribute covers the largest staged row
+        const cudaError_t e = dtype == 1 ? ensure_dynamic_smem(ce_rows_staged_kernel<__nv_bfloat16>,
+                                                               2 * kMaxStagedBytes)
+                                         : ensure_dynamic_smem(ce_rows_staged_kernel<__half>, 2 * kMaxStagedBytes);
         if (e != cudaSuccess) return e;
-        configured[dtype - 1] = true;
       }
       if (dtype == 1) {
         ce_rows_staged_kernel<__nv_bfloat16><<<grid, kStagedThreads, smem, s>>>(
@@ -210,7 +207,8 @@ cudaError_t ce_rows_fwd_bwd(int dtype, void* logits, int64_t ld, int64_t rows, i
       return cudaGetLastError();
     }
   }
-  int64_t grid = rows < 148 * 8 ? rows : 148 * 8;
+  const int64_t cap = (int64_t)device_sms() * 8;
+  int64_t grid = rows < cap ? rows : cap;
   if (grid < 1) grid = 1;
   switch (dtype) {
     case 0: ce_rows_kernel<float><<<grid, 512, 0, s>>>((float*)logits, ld, rows, vocab, targets, valid, loss_rows,

@@ -18,6 +18,7 @@
 // weights) followed by SiLU and the per-head L2 normalisation of q and k in
 // `src/kda/projections.py:188-200` (reference).
 #include "common.cuh"
+#include "device_info.h"
 #include "kernels.h"
 #include "tc_common.cuh"
 
@@ -295,7 +296,7 @@ __global__ void __launch_bounds__(256) conv_fwd_s_kernel(const T* __restrict__ x
 #pragma unroll
     for (int j = 0; j < K; ++j) wr[e][j] = active ? w[(c0 + e) * K + j] : 0.f;
   __syncthreads();  // zero rows written
-  tc::mbar_wait(&bar, 0, nullptr, 0);
+  tc::mbar_wait_local(&bar, 0, nullptr, 0);
   const int64_t rowbase = (int64_t)b * tokens;
   for (int t = t0; t < t1; ++t) {
     float s[8], ss = 0.f;
@@ -356,7 +357,7 @@ __global__ void __launch_bounds__(256) conv_bwd_s_kernel(const T* __restrict__ d
       dwacc[e][j] = 0.f;
     }
   __syncthreads();
-  tc::mbar_wait(&bar, 0, nullptr, 0);
+  tc::mbar_wait_local(&bar, 0, nullptr, 0);
   const int64_t rowbase = (int64_t)b * tokens;
   float dph[K][8];  // dph[j] = dpre[t + j]; slot 0 is this step's
 #pragma unroll
@@ -453,10 +454,8 @@ cudaError_t launch_conv(bool fwd, const void* dy, const void* x, const float* w,
   case KK:                                                                                                          \
     if (staged) {                                                                                                   \
       if (ssm > 48 * 1024) {                                                                                        \
-        cudaError_t e = fwd ? cudaFuncSetAttribute(conv_fwd_s_kernel<T, KK>,                                        \
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kConvSmemCap)  \
-                            : cudaFuncSetAttribute(conv_bwd_s_kernel<T, KK>,                                        \
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kConvSmemCap); \
+        cudaError_t e = fwd ? ensure_dynamic_smem(conv_fwd_s_kernel<T, KK>, (int)kConvSmemCap)                       \
+                            : ensure_dynamic_smem(conv_bwd_s_kernel<T, KK>, (int)kConvSmemCap);                      \
         if (e != cudaSuccess) return e;                                                                             \
       }                                                                                                             \
       if (fwd)                                                                                                      \

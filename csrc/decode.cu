@@ -22,6 +22,7 @@
 #include <cstdint>
 
 #include "common.cuh"
+#include "device_info.h"
 #include "kernels.h"
 
 namespace kimi {
@@ -659,7 +660,7 @@ cudaError_t mla_decode(int dtype, const float* qlat, const void* latent, const i
   do {                                                                                                            \
     auto fn = mla_decode_kernel<TT, HM, CP>;                                                                      \
     if (sm > 48 * 1024) {                                                                                         \
-      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(200 * 1024));   \
+      cudaError_t e = ensure_dynamic_smem(fn, (int)(200 * 1024));                                                \
       if (e != cudaSuccess) return e;                                                                             \
     }                                                                                                             \
     fn<<<grid, kMlaThreads, sm, s>>>(qlat, (const TT*)latent, lengths, heads, ldim, tmax, rows_per_split,        \

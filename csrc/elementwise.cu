@@ -9,6 +9,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "device_info.h"
 #include "kernels.h"
 
 namespace kimi {
@@ -22,7 +23,7 @@ int pick_tpr(int nvec) {
 
 int grid_for(int64_t work_items, int per_block) {
   int64_t g = (work_items + per_block - 1) / per_block;
-  const int64_t cap = 148 * 16;
+  const int64_t cap = (int64_t)device_sms() * 16;
   if (g > cap) g = cap;
   if (g < 1) g = 1;
   return (int)g;
@@ -378,12 +379,12 @@ cudaError_t rms_norm_bwd(int dtype, const void* dy, const void* x, const float* 
     // The dw partials are flushed once per block: keep the grid near 4 blocks per SM so the
     // global atomics per weight element stay in the hundreds.
     int grid = grid_for(rows, threads / tpr);
-    if (dw && grid > 148 * 4) grid = 148 * 4;
+    if (dw && grid > device_sms() * 4) grid = device_sms() * 4;
     const int nvec = dim / Vec<T>::N;
     if (p == 1 && nvec <= 32 * 4) {
       // with dw, every block ends with one global atomic per weight element: two blocks per SM keep
       // those few hundred per element (eight per SM made the flush, not the rows, the cost)
-      const int wgrid = (int)std::min<int64_t>((rows + 7) / 8, dw ? 148 * 2 : 148 * 8);
+      const int wgrid = (int)std::min<int64_t>((rows + 7) / 8, dw ? device_sms() * 2 : device_sms() * 8);
       const size_t wsmem = dw ? (size_t)dim * sizeof(float) : 0;
       if (nvec <= 32)
         rms_bwd_warp_kernel<T, 1><<<wgrid, 256, wsmem, s>>>((const T*)dy, (const T*)x, w, rstd, (T*)dx, dw, rows, dim);
@@ -443,7 +444,7 @@ cudaError_t kda_decay_bwd(int dtype, const float* dg, const void* z, const float
   const int64_t n = rows * heads * kdim;
   if (kdim % 64) return cudaErrorInvalidValue;
   KIMI_DISPATCH(dtype, T, {
-    const int grid = (int)std::min<int64_t>(grid_for(n / 8, 256), 148 * 4);
+    const int grid = (int)std::min<int64_t>(grid_for(n / 8, 256), device_sms() * 4);
     decay_bwd_kernel<T><<<grid, 256, heads * sizeof(float), s>>>(dg, (const T*)z, a_log, (T*)dz, da_log, n, heads,
                                                                  kdim, g_min, ceps);
   });

@@ -36,6 +36,7 @@
 #include <cstdint>
 
 #include "common.cuh"
+#include "device_info.h"
 #include "kernels.h"
 
 namespace kimi {
@@ -291,7 +292,8 @@ __global__ void __launch_bounds__(256) ep_slot_sum_kernel(EpPeers p, const int64
 
 int grid_for(int64_t warps) {
   int64_t b = (warps + 7) / 8;
-  return (int)(b < 1 ? 1 : (b > 148 * 8 ? 148 * 8 : b));
+  const int64_t cap = (int64_t)device_sms() * 8;
+  return (int)(b < 1 ? 1 : (b > cap ? cap : b));
 }
 
 }  // namespace
@@ -303,7 +305,10 @@ cudaError_t ep_count(const int64_t* sel, int64_t n, int E, int* cnt, float* agg,
   if (cudaMemsetAsync(cnt, 0, sizeof(int) * E, s) != cudaSuccess) return cudaGetLastError();
   const int64_t work = n > agg_elems / 4 ? n : agg_elems / 4;
   int blocks = (int)((work + 255) / 256);
-  blocks = blocks < 1 ? 1 : (blocks > 148 * 8 ? 148 * 8 : blocks);
+  {
+    const int cap = device_sms() * 8;
+    blocks = blocks < 1 ? 1 : (blocks > cap ? cap : blocks);
+  }
   ep_count_kernel<<<blocks, 256, 0, s>>>(sel, n, E, cnt, agg, agg_elems);
   return cudaGetLastError();
 }

@@ -7,6 +7,7 @@
 // per-batch key lengths (padding) are applied on the score tile. Q, K, V, O are
 // [B, T, H, 64]; LSE is [B, H, T].
 #include "common.cuh"
+#include "device_info.h"
 #include "kernels.h"
 
 namespace kimi {
@@ -337,14 +338,10 @@ template <typename T>
 cudaError_t bwd_impl(const void* q, const void* k, const void* v, const void* o, const void* dout, const float* lse,
                      float* dq_acc, void* dk, void* dv, float* delta, int B, int tq, int tk, int H, bool causal,
                      const int* kl, float scale, cudaStream_t s) {
-  fa_delta_kernel<T><<<148 * 4, 256, 0, s>>>((const T*)o, (const T*)dout, delta, B, tq, H);
+  fa_delta_kernel<T><<<device_sms() * 4, 256, 0, s>>>((const T*)o, (const T*)dout, delta, B, tq, H);
   KIMI_CUDA_CHECK(cudaGetLastError());
   const size_t smem = (size_t)6 * 64 * LDS * sizeof(T);
-  static bool configured = false;
-  if (!configured) {
-    KIMI_CUDA_CHECK(cudaFuncSetAttribute(fa_bwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    configured = true;
-  }
+  KIMI_CUDA_CHECK(ensure_dynamic_smem(fa_bwd_kernel<T>, (int)smem));
   dim3 grid((tk + BN - 1) / BN, B * H);
   fa_bwd_kernel<T><<<grid, NTH, smem, s>>>((const T*)q, (const T*)k, (const T*)v, (const T*)dout, lse, delta, dq_acc,
                                            (T*)dk, (T*)dv, tq, tk, H, causal, kl, scale);

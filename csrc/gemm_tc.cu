@@ -32,7 +32,10 @@
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
 
+#include <mutex>
+
 #include "common.cuh"
+#include "device_info.h"
 #include "tc_common.cuh"
 #include "tc_gemm.h"
 
@@ -90,6 +93,7 @@ struct DevParams {
   float* agg_peer[8];
   int agg_tokens;
   int* status;
+  uint32_t spin_limit;  // polls per pipeline wait before it gives up (tests shorten it)
   CommParams cm;
 };
 
@@ -232,6 +236,16 @@ __device__ bool wait_geq(const uint32_t* flag, uint32_t target, int64_t timeout_
   return true;
 }
 __device__ __forceinline__ void comm_bar() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
+// Named-barrier OR vote over `threads` threads: true when any of them passes pred = true.
+__device__ __forceinline__ bool bar_red_or(int id, int threads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(threads)
+      : "memory");
+  return r != 0;
+}
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 __device__ __forceinline__ void add_bf16x8(float* acc, uint4 v) {
@@ -293,7 +307,8 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* drain = tempty + 2;  // MMA warp's exit barrier: every issued MMA has completed
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bnt = p.situ ? BN / 2 : BN;  // output columns per tile
 
@@ -306,6 +321,7 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
       tc::mbar_init(&tfull[b], 1);
       tc::mbar_init(&tempty[b], 256);
     }
+    tc::mbar_init(drain, 1);
     tc::fence_barrier_init();
     tc::fence_proxy_async();
   }
@@ -326,35 +342,52 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
 
   if (warp == 0) {
     if (lane == 0) {
+      // Roles leave their loops at the first failed wait (their own timeout, or another role's
+      // or CTA's recorded in the status word).  On the way out the producer waits for the TMA
+      // copies it has in flight, so no copy lands in shared memory after the CTA has exited.
       int s = 0;
       uint32_t ph = 0;
-      const uint32_t ag_target = CM == 3 ? *p.ag_epoch + 1u : 0u;
-      for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+      bool ok = true;
+      uint32_t inflight = 0, inflight_ph = 0;  // stages filled since their last consumption, and their phase
+      uint32_t ag_target = 0u;
+      if constexpr (CM == 3) ag_target = *p.ag_epoch + 1u;
+      for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
         const TileInfo ti = p.situ ? tile_info<BN / 2>(p, tile) : tile_info<BN>(p, tile);
         for (int kb = 0; kb < ti.num_kb; ++kb) {
-          tc::mbar_wait(&empty[s], ph ^ 1, p.status, tc::kTimeoutEmpty);
+          if (!tc::mbar_wait(&empty[s], ph ^ 1, p.status, tc::kTimeoutEmpty, p.spin_limit)) {
+            ok = false;
+            break;
+          }
+          inflight &= ~(1u << s);
           uint8_t* sa = smem + s * STAGE;
           uint8_t* sb = sa + A_BYTES;
-          tc::mbar_arrive_expect_tx(&full[s], STAGE);
           const int k = ti.k0 + kb * BK;
-          if (!A_MN) {
-            if (CM == 3 && kb == 0 && ti.m0 / p.ag_rows != p.ag_rank) {
-              // remote rows: wait until a comm warp has copied this block into the local buffer
-              const uint32_t* f = p.ag_flags + ti.m0 / BM;
-              const uint32_t target = ag_target;
-              const uint64_t t0 = global_ns();
-              uint32_t v;
-              while (true) {
-                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-                if (v >= target) break;
-                if ((int64_t)(global_ns() - t0) > (int64_t)10000000000LL) {
-                  atomicCAS(p.status, 0, kCommTimeout);
-                  break;
-                }
-                __nanosleep(64);
+          if constexpr (CM == 3 && !A_MN) {
+            if (kb == 0 && ti.m0 / p.ag_rows != p.ag_rank) {
+            // remote rows: wait until a comm warp has copied this block into the local buffer
+            const uint32_t* f = p.ag_flags + ti.m0 / BM;
+            const uint64_t t0 = global_ns();
+            uint32_t v;
+            while (true) {
+              asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+              if (v >= ag_target) break;
+              if (tc::status_peek(p.status) != 0) {
+                ok = false;
+                break;
               }
-              asm volatile("fence.proxy.async.global;" ::: "memory");
+              if ((int64_t)(global_ns() - t0) > (int64_t)10000000000LL) {
+                atomicCAS(p.status, 0, kCommTimeout);
+                ok = false;
+                break;
+              }
+              __nanosleep(64);
             }
+            if (!ok) break;
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            }
+          }
+          tc::mbar_arrive_expect_tx(&full[s], STAGE);
+          if (!A_MN) {
             tc::tma_load_2d(sa, &p.map_a, &full[s], k, ti.m0);
           } else {
             tc::tma_load_2d(sa, &p.map_a, &full[s], ti.m0, k);
@@ -377,27 +410,39 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
               tc::tma_load_3d(sb + q * (BK * 64 * 2), mb, &full[s], ti.n0 + q * 64, kb_coord,
                               p.mode == 2 ? 0 : ti.g);
           }
+          inflight |= 1u << s;
+          inflight_ph = (inflight_ph & ~(1u << s)) | (ph << s);
           if (++s == STAGES) {
             s = 0;
             ph ^= 1;
           }
         }
       }
+      if (!ok)
+        for (int q = 0; q < STAGES; ++q)
+          if (inflight & (1u << q)) tc::mbar_wait_local(&full[q], (inflight_ph >> q) & 1u, p.status, tc::kTimeoutDrain);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = tc::instr_desc_f16(BM, BN, true, A_MN, B_MN);
       int s = 0, it = 0;
       uint32_t ph = 0;
-      for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+      bool ok = true, issued = false;
+      for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x, ++it) {
         const TileInfo ti = p.situ ? tile_info<BN / 2>(p, tile) : tile_info<BN>(p, tile);
         const int buf = it & 1;
         const uint32_t tph = (it >> 1) & 1;
-        tc::mbar_wait(&tempty[buf], tph ^ 1, p.status, tc::kTimeoutTmemEmpty);
+        if (!tc::mbar_wait(&tempty[buf], tph ^ 1, p.status, tc::kTimeoutTmemEmpty, p.spin_limit)) {
+          ok = false;
+          break;
+        }
         tc::tc_fence_after();
         const uint32_t d = tmem_base + buf * BN;
         for (int kb = 0; kb < ti.num_kb; ++kb) {
-          tc::mbar_wait(&full[s], ph, p.status, tc::kTimeoutFull);
+          if (!tc::mbar_wait(&full[s], ph, p.status, tc::kTimeoutFull, p.spin_limit)) {
+            ok = false;
+            break;
+          }
           tc::tc_fence_after();
           const uint32_t base_a = tc::smem_u32(smem + s * STAGE);
           const uint32_t base_b = base_a + A_BYTES;
@@ -409,13 +454,20 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
                                      : tc::smem_desc_sw128(base_b + kk * 32, 16, 1024);
             tc::mma_f16(d, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
           }
+          issued = true;
           tc::mma_commit(&empty[s]);
           if (++s == STAGES) {
             s = 0;
             ph ^= 1;
           }
         }
+        if (!ok) break;
         tc::mma_commit(&tfull[buf]);
+      }
+      if (!ok && issued) {
+        // let every issued MMA finish before the CTA frees its TMEM and shared memory
+        tc::mma_commit(drain);
+        tc::mbar_wait_local(drain, 0, p.status, tc::kTimeoutDrain);
       }
     }
   } else if (warp < 10) {
@@ -428,7 +480,12 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
       const TileInfo ti = p.situ ? tile_info<BN / 2>(p, tile) : tile_info<BN>(p, tile);
       const int buf = it & 1;
       const uint32_t tph = (it >> 1) & 1;
-      tc::mbar_wait(&tfull[buf], tph, p.status, tc::kTimeoutTmemFull);
+      bool ok = tc::mbar_wait(&tfull[buf], tph, p.status, tc::kTimeoutTmemFull, p.spin_limit);
+      if constexpr (CM == 1 || CM == 2) {
+        // the comm epilogue meets at a named barrier per tile: leave together or not at all
+        ok = !bar_red_or(1, 256, !ok);
+      }
+      if (!ok) break;
       tc::tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + buf * BN;
       const int row = ti.c_row0 + r_local;
@@ -712,14 +769,11 @@ cudaError_t launch(const DevParams& dp, int num_sms, cudaStream_t s) {
   if (debug_on() && stale != cudaSuccess) fprintf(stderr, "tc_gemm: stale error before launch: %s\n", cudaGetErrorString(stale));
   constexpr int STAGES = BN == 256 ? 4 : 6;
   constexpr int STAGE = BM * BK * 2 + BN * BK * 2;
-  const size_t smem = 1024 + (size_t)STAGES * STAGE + (2 * STAGES + 4) * 8 + 16;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, AMN, BMN, CM>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const size_t smem = 1024 + (size_t)STAGES * STAGE + (2 * STAGES + 5) * 8 + 16;
+  {
+    cudaError_t e = ensure_dynamic_smem(gemm_tc_kernel<BN, AMN, BMN, CM>, (int)smem);
     if (debug_on() && e != cudaSuccess) fprintf(stderr, "tc_gemm: smem attribute failed: %s\n", cudaGetErrorString(e));
     if (e != cudaSuccess) return e;
-    configured = true;
   }
   gemm_tc_kernel<BN, AMN, BMN, CM><<<num_sms, CM ? 448 : 320, smem, s>>>(dp);
   const cudaError_t e = cudaGetLastError();
@@ -735,7 +789,40 @@ cudaError_t launch(const DevParams& dp, int num_sms, cudaStream_t s) {
   return e;
 }
 
+// Status word of launches that pass none (one per device): a failed bounded wait records its code
+// here, and every later launch on that device winds down at once until the host reads and clears
+// it with tc_gemm_status(true).
+__device__ int g_gemm_status = 0;
+
+constexpr int kMaxDevices = 64;
+std::mutex g_status_mutex;
+int* g_status_ptr[kMaxDevices] = {};
+
+int* default_status() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(g_status_mutex);
+  if (!g_status_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_gemm_status) != cudaSuccess) return nullptr;
+    g_status_ptr[dev] = static_cast<int*>(p);
+  }
+  return g_status_ptr[dev];
+}
+
 }  // namespace
+
+int tc_gemm_status(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_gemm_status, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_gemm_status, &zero, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
+}
+
+int* tc_gemm_default_status() { return default_status(); }
 
 cudaError_t tc_gemm(const TcGemmArgs& a, cudaStream_t stream) {
   // The driver's tensor-map encoder needs the device's context current on this host thread; a
@@ -782,7 +869,9 @@ cudaError_t tc_gemm(const TcGemmArgs& a, cudaStream_t stream) {
                          a.ag_rank < 0 || a.ag_rank >= a.ag_world || !a.ag_flags || !a.ag_epoch || !a.status ||
                          (a.a_ld * 2) % 16))
     return cudaErrorInvalidValue;
-  dp.status = a.status;
+  dp.status = a.status ? a.status : default_status();
+  if (!dp.status) return cudaErrorInvalidValue;
+  dp.spin_limit = a.spin_limit > 0 ? a.spin_limit : tc::kSpinLimit;
   const int bn = a.epi == 1 ? 256 : a.bn;
   if (bn != 128 && bn != 256) return cudaErrorInvalidValue;
   if (a.epi == 1 && (a.a_mn || a.b_mn || !a.b2)) return cudaErrorInvalidValue;
@@ -814,7 +903,7 @@ cudaError_t tc_gemm(const TcGemmArgs& a, cudaStream_t stream) {
       return cudaErrorInvalidValue;
     }
   }
-  int sms = a.num_sms > 0 ? a.num_sms : 148;
+  int sms = a.num_sms > 0 ? a.num_sms : device_sms();
   if (a.comm_mode != 0) {
     CommParams& c = dp.cm;
     c.mode = a.comm_mode;

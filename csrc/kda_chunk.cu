@@ -44,11 +44,12 @@ cudaError_t bwd_impl(const void* q, const void* k, const void* v, const float* g
 }  // namespace
 
 cudaError_t kda_chunk_fwd(int dtype, const void* q, const void* k, const void* v, const float* g, const float* beta,
-                          const float* h0, void* o, float* ht, KdaBuffers buf, int B, int Tp, int H, cudaStream_t s) {
+                          const float* h0, void* o, float* ht, KdaBuffers buf, int B, int Tp, int H, cudaStream_t s,
+                          int* status) {
   if (Tp % C || !buf.Araw || dtype < 0 || dtype > 2) return cudaErrorInvalidValue;
-  cudaError_t e = kda_intra_fwd_tc(dtype, q, k, v, g, beta, buf, B, Tp, H, nullptr, s);
+  cudaError_t e = kda_intra_fwd_tc(dtype, q, k, v, g, beta, buf, B, Tp, H, status, s);
   if (e != cudaSuccess) return e;
-  return kda_state_fwd_tc(dtype, buf, h0, o, ht, B, Tp, H, nullptr, s);
+  return kda_state_fwd_tc(dtype, buf, h0, o, ht, B, Tp, H, status, s);
 }
 
 cudaError_t kda_chunk_bwd(int dtype, const void* q, const void* k, const void* v, const float* g, const float* beta,

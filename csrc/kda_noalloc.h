@@ -27,6 +27,7 @@ extern "C" {
 #define KIMI_KDA_NOALLOC_OK 0
 #define KIMI_KDA_NOALLOC_TOO_LARGE 10001  // batch * heads * chunks exceeds the scratch array
 #define KIMI_KDA_NOALLOC_BAD_SHAPE 10002  // tokens_padded not a positive multiple of 64, or another bad argument
+#define KIMI_KDA_NOALLOC_WAIT_TIMEOUT 10003  // a kernel's bounded wait gave up (kimi_kda_noalloc_last_status)
 
 // Chunked KDA forward, o = KDA(q, k, v, g, beta; h0), with head dims of 64.
 //   dtype:        0 = float32, 1 = bfloat16, 2 = float16 (q, k, v and o)
@@ -56,6 +57,15 @@ extern "C" {
 int kimi_kda_chunk_fwd_noalloc(int dtype, const void* q, const void* k, const void* v, const float* g,
                                const float* beta, const float* h0, void* o, float* ht, int batch, int tokens_padded,
                                int heads, cudaStream_t stream);
+
+// Status of the kernels launched by the calls above on the current device since the last check.
+// The launch itself cannot report a wait that gives up inside a kernel (every wait in these kernels
+// is bounded, so a broken tensor-core pipeline ends the kernel instead of hanging the GPU); the
+// kernel records it in a status word that lives beside the scratch array.  Synchronize the stream
+// first, then call this: it returns KIMI_KDA_NOALLOC_OK, or KIMI_KDA_NOALLOC_WAIT_TIMEOUT (and
+// clears the word) when the outputs of those calls are not valid, or a cudaError_t value if the
+// word could not be read.  It allocates nothing.
+int kimi_kda_noalloc_last_status(void);
 
 // Human-readable text for a status code returned above.
 const char* kimi_kda_noalloc_status_string(int status);

@@ -21,10 +21,12 @@
 // Gradients of q and k accumulate in global fp32 (one writer per element per stage); dG
 // accumulates in shared memory and becomes dg by a reverse cumulative sum.  Every mbarrier wait
 // is bounded and reports through the status word.
+#include <mutex>
 #include <vector>
 
 #include "kernels.h"
 #include "tc_small.cuh"
+#include "device_info.h"
 
 namespace kimi {
 namespace {
@@ -582,15 +584,12 @@ size_t bwd_smem() {
 
 template <typename T>
 cudaError_t launch_bwd(const BwdArgs& args, cudaStream_t s) {
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kda_intra_bwd_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)bwd_smem<T>());
+  {
+    cudaError_t e = ensure_dynamic_smem(kda_intra_bwd_tc_kernel<T>, (int)bwd_smem<T>());
     if (e != cudaSuccess) return e;
-    configured = true;
   }
   const int total = args.B * args.H * args.NC;
-  int sms = 148;
+  const int sms = device_sms();
   const int grid = total < sms ? total : sms;
   kda_intra_bwd_tc_kernel<T><<<grid, NTB, bwd_smem<T>(), s>>>(args);
   return cudaGetLastError();
@@ -1086,16 +1085,9 @@ constexpr size_t kStateSmem = 1024 + 104 * KB + 16;  // backward: three R64 K128
 
 template <typename T>
 cudaError_t launch_state(bool fwd, const StateArgs& args, cudaStream_t s) {
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kda_state_fwd_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)kStateFwdSmem);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(kda_state_bwd_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)kStateSmem);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  cudaError_t e = ensure_dynamic_smem(kda_state_fwd_tc_kernel<T>, (int)kStateFwdSmem);
+  if (e == cudaSuccess) e = ensure_dynamic_smem(kda_state_bwd_tc_kernel<T>, (int)kStateSmem);
+  if (e != cudaSuccess) return e;
   if (fwd)
     kda_state_fwd_tc_kernel<T><<<args.B * args.H, NTH, kStateFwdSmem, s>>>(args);
   else
@@ -1107,11 +1099,20 @@ int* status_ptr(int* status);
 
 __device__ int g_kda_tc_status = 0;
 
+std::mutex g_status_mutex;
+int* g_status_addr[64] = {};  // device address of g_kda_tc_status, per device
+
 int* status_ptr(int* status) {
   if (status) return status;
-  void* p = nullptr;
-  if (cudaGetSymbolAddress(&p, g_kda_tc_status) != cudaSuccess) return nullptr;
-  return static_cast<int*>(p);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(g_status_mutex);
+  if (!g_status_addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_kda_tc_status) != cudaSuccess) return nullptr;
+    g_status_addr[dev] = static_cast<int*>(p);
+  }
+  return g_status_addr[dev];
 }
 
 }  // namespace
@@ -1123,6 +1124,8 @@ std::vector<long long> kda_phase_profile(bool enable) {
   cudaMemcpyToSymbol(g_kda_phase_on, &on, sizeof(int));
   return v;
 }
+
+int* kda_tc_default_status() { return status_ptr(nullptr); }
 
 int kda_tc_status(bool clear) {
   int v = 0;
@@ -1194,11 +1197,10 @@ cudaError_t kda_intra_fwd_tc(int dtype, const void* q, const void* k, const void
   if (!status) return cudaErrorInvalidValue;
   FwdArgs args{q, k, v, g, beta, buf, B, Tp, H, Tp / C, status};
   const int total = B * H * (Tp / C);
-  const int grid = total < 148 ? total : 148;
+  const int sms = device_sms();
+  const int grid = total < sms ? total : sms;
   auto go = [&](auto kernel) -> cudaError_t {
-    static bool configured = false;
-    (void)configured;
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFwdSmem);
+    cudaError_t e = ensure_dynamic_smem(kernel, (int)kFwdSmem);
     if (e != cudaSuccess) return e;
     kernel<<<grid, NTH, kFwdSmem, s>>>(args);
     return cudaGetLastError();

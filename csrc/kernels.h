@@ -64,7 +64,7 @@ struct KdaBuffers {
 };
 cudaError_t kda_chunk_fwd(int dtype, const void* q, const void* k, const void* v, const float* g, const float* beta,
                           const float* h0, void* o, float* ht, KdaBuffers buf, int batch, int tokens_padded,
-                          int heads, cudaStream_t s);
+                          int heads, cudaStream_t s, int* status = nullptr);
 cudaError_t kda_chunk_bwd(int dtype, const void* q, const void* k, const void* v, const float* g, const float* beta,
                           KdaBuffers buf, const void* dout, const float* dht, float* dVp, float* dSn, float* dq,
                           float* dk, float* dv, float* dg, float* dbeta, float* dh0, int batch, int tokens_padded,
@@ -91,6 +91,8 @@ cudaError_t kda_state_bwd_tc(int dtype, KdaBuffers buf, const void* dout, const 
 std::vector<long long> kda_phase_profile(bool enable);
 // Device status word shared by the tcgen05 KDA kernels (read and cleared by the host).
 int kda_tc_status(bool clear);
+// Device address of the current device's default KDA status word (for stream-ordered reads).
+int* kda_tc_default_status();
 
 // ---- flash attention (flash_attn.cu); q/k/v/o are [B,T,H,D] contiguous
 cudaError_t flash_attn_fwd(int dtype, const void* q, const void* k, const void* v, void* o, float* lse, int batch,

@@ -9,6 +9,7 @@
 //   situ_bwd_cat:    [dGate | dUp] of the SiTU-GLU into one [R, 2H] buffer
 // Buffers have R_max = M*k + E*128 rows so the launch shape never depends on the routing.
 #include "common.cuh"
+#include "device_info.h"
 #include "moe_route.h"
 
 namespace kimi {
@@ -187,7 +188,7 @@ __global__ void situ_bwd_cat_kernel(const T* __restrict__ dh, const T* __restric
 
 int grid_of(int64_t n, int threads) {
   int64_t g = (n + threads - 1) / threads;
-  if (g > 148 * 16) g = 148 * 16;
+  if (g > (int64_t)device_sms() * 16) g = (int64_t)device_sms() * 16;
   return (int)(g < 1 ? 1 : g);
 }
 

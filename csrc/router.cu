@@ -3,6 +3,7 @@
 // Selection is k rounds of a warp arg-max over the lanes' candidates; among equal biased
 // scores the lowest expert index wins.
 #include "common.cuh"
+#include "device_info.h"
 #include "kernels.h"
 
 namespace kimi {
@@ -100,7 +101,7 @@ cudaError_t router_topk(int dtype, const void* logits, const float* bias, int64_
   if (experts > 32 * kMaxPerLane || k < 1 || k + 1 > kMaxTopK || k > experts) return cudaErrorInvalidValue;
   const int threads = 256;
   int64_t grid = (rows + 7) / 8;
-  if (grid > 148 * 16) grid = 148 * 16;
+  if (grid > device_sms() * 16) grid = device_sms() * 16;
   if (grid < 1) grid = 1;
   switch (dtype) {
     case 0: router_kernel<float><<<grid, threads, 0, s>>>((const float*)logits, bias, rows, experts, k, need_cutoff,

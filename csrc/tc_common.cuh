@@ -9,7 +9,12 @@
 //
 // Every wait on an mbarrier is bounded: after kSpinLimit polls it records an error code in
 // the kernel's status word and returns, so a broken pipeline ends the kernel instead of
-// hanging the GPU (the host checks the status word).
+// hanging the GPU (the host checks the status word).  A pipeline wait (one role of a
+// warp-specialised kernel waiting on another) also gives up as soon as the status word shows
+// that another role or CTA has failed, so the whole kernel winds down within about one limit.
+// Waits for work this thread itself issued (a TMA copy, committed MMAs) use mbar_wait_local:
+// that work always completes, so those waits do not give up early on the status word; the
+// exit path uses them to let copies and MMAs in flight finish before TMEM is freed.
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -20,7 +25,9 @@ namespace tc {
 
 constexpr uint32_t kSpinLimit = 1u << 26;
 
-enum Status : int { kOk = 0, kTimeoutFull = 1, kTimeoutEmpty = 2, kTimeoutTmemFull = 3, kTimeoutTmemEmpty = 4 };
+enum Status : int {
+  kOk = 0, kTimeoutFull = 1, kTimeoutEmpty = 2, kTimeoutTmemFull = 3, kTimeoutTmemEmpty = 4, kTimeoutDrain = 6
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -52,8 +59,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return done != 0;
 }
-// Bounded wait; on timeout writes `code` to *status (first error wins) and returns false.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+__device__ __forceinline__ int status_peek(const int* status) {
+  return status ? *reinterpret_cast<const volatile int*>(status) : 0;
+}
+// Bounded pipeline wait: false after `limit` polls (records `code` in *status, first error
+// wins) or as soon as *status is non-zero (checked every 1024 polls).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code,
+                                          uint32_t limit = kSpinLimit) {
+  for (uint32_t i = 0; i < limit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 1023u) == 1023u && status_peek(status) != 0) return false;
+  }
+  if (status) atomicCAS(status, 0, code);
+  return false;
+}
+// Bounded wait for this thread's own copies / MMAs (always complete): ignores the status word.
+__device__ __forceinline__ bool mbar_wait_local(uint64_t* bar, uint32_t parity, int* status, int code) {
   for (uint32_t i = 0; i < kSpinLimit; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   if (status) atomicCAS(status, 0, code);
@@ -139,6 +160,74 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, float* v) {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ---------------------------------------------------------------- CTA pairs (cta_group::2)
+// Two CTAs of a cluster share one MMA: the even CTA issues tcgen05.mma.cta_group::2 with M = 256,
+// reading rows 0-127 of A (and the first half of B's rows) from its own shared memory and the rest
+// from the odd CTA's shared memory at the same offsets; each CTA's TMEM receives its 128 rows.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+  return r;
+}
+// Shared::cluster address of the object at `p` (this CTA's shared memory) in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+// Arrive (release, cluster scope) on an mbarrier given by its shared::cluster address.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];\n" ::"r"(bar_cluster) : "memory");
+}
+// TMA tile loads into this CTA's shared memory whose completion is counted on an mbarrier of either
+// CTA of the pair (`bar_cluster`: shared::cluster address).  No multicast: each CTA loads its own half.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];\n" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int x, int y,
+                                                 int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+      "%4}], [%5];\n" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar_cluster)
+      : "memory");
+}
+// Both CTAs of the pair execute these (same warp, same slot offset); the column address is shared.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D[tmem of both CTAs] (+)= A[smem of both CTAs] * B[smem of both CTAs]^T; issued by the even CTA.
+__device__ __forceinline__ void mma_f16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z)
+      : "memory");
+}
+// Arrive on the mbarrier at `bar_cluster` (either CTA of the pair) once every tcgen05.mma issued so
+// far by this thread has completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar_cluster)
+               : "memory");
 }
 
 // ---------------------------------------------------------------- descriptors

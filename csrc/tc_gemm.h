@@ -40,7 +40,8 @@ struct TcGemmArgs {
   int ag_world = 0, ag_rows = 0, ag_rank = 0;
   uint32_t* ag_flags = nullptr;
   const uint32_t* ag_epoch = nullptr;
-  int* status = nullptr;
+  int* status = nullptr;     // null: the device's default status word (tc_gemm_status)
+  uint32_t spin_limit = 0;   // polls per pipeline wait before giving up; 0 = the built-in limit
   int num_sms = 0;
   // Comm modes (dense, bf16 output, A K-major, N % 8 == 0): `out` / `ldc` must be this rank's
   // symmetric partial buffer [M, N] (ldc == N); the summed result goes to comm_out.
@@ -59,5 +60,12 @@ struct TcGemmArgs {
 inline int tc_gemm_tiles(int M, int N, int bn) { return ((M + 127) / 128) * ((N + bn - 1) / bn); }
 
 cudaError_t tc_gemm(const TcGemmArgs& args, cudaStream_t stream);
+
+// Read (and with clear, reset) the current device's default GEMM status word: 0 = every wait of
+// every launch that used it completed; otherwise the code of the first wait that gave up.
+// Synchronous (a device-to-host copy); -1 if the copy failed.
+int tc_gemm_status(bool clear);
+// Device address of the current device's default status word (for stream-ordered reads).
+int* tc_gemm_default_status();
 
 }  // namespace kimi

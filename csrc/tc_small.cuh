@@ -94,7 +94,7 @@ KIMI_D void operands_ready() {
 
 // Wait for the MMAs committed to `bar` (phase bit flips per use); bounded.
 KIMI_D bool mma_done(uint64_t* bar, uint32_t& phase, int* status, int code) {
-  const bool ok = tc::mbar_wait(bar, phase, status, code);
+  const bool ok = tc::mbar_wait_local(bar, phase, status, code);
   phase ^= 1u;
   tc::tc_fence_after();
   return ok;

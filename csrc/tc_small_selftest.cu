@@ -5,6 +5,7 @@
 //   mode 2: out[:, 16 J + c] = A B[16J + c, :]^T                     (four row offsets, N = 16 each)
 #include "kernels.h"
 #include "tc_small.cuh"
+#include "device_info.h"
 
 namespace kimi {
 namespace {
@@ -64,7 +65,7 @@ cudaError_t tcs_selftest(const float* A, const float* B, float* out, int K, int 
   if (mode != 0 && K != 64) return cudaErrorInvalidValue;
   const int nb = mode == 0 ? n : 64;
   const size_t smem = 1024 + (size_t)(128 + nb) * K * 4;
-  cudaError_t e = cudaFuncSetAttribute(tcs_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = ensure_dynamic_smem(tcs_selftest_kernel, (int)smem);
   if (e != cudaSuccess) return e;
   tcs_selftest_kernel<<<1, 128, smem, s>>>(A, B, out, K, n, mode, status);
   return cudaGetLastError();

@@ -25,6 +25,30 @@ from dataclasses import dataclass
 import torch
 
 
+class KernelWaitError(RuntimeError):
+    """A bounded wait inside one of the framework's kernels gave up during a training step."""
+
+
+def kernel_status_words(device):
+    """The device's default status words of the GEMM and KDA kernels (int32 views), or None."""
+    if device.type != "cuda":
+        return None
+    from ..ops import _loader
+    ext = _loader.load()
+    if ext is None or not hasattr(ext, "status_words"):
+        return None
+    with torch.cuda.device(device):
+        return ext.status_words()
+
+
+def clear_kernel_status(device) -> None:
+    from ..ops import _loader
+    ext = _loader.require()
+    with torch.cuda.device(device):
+        ext.tc_gemm_status(True)
+        ext.kda_tc_status(True)
+
+
 @dataclass
 class StepOutput:
     loss: torch.Tensor          # device scalar (total objective)
@@ -75,7 +99,8 @@ class TrainStepEngine:
         self._static_in = None
         self._static_out = None
         self._graph_steps = 0
-        self._pending = None  # (pinned found_inf copy, event) of the last replayed step
+        self._pending = None  # (pinned found_inf copy or None, pinned kernel status, event) of the last step
+        self._status_words = kernel_status_words(self.device)
 
     def _autocast(self, cache_enabled: bool = True):
         if self.amp_dtype is None or self.device.type != "cuda":
@@ -92,10 +117,9 @@ class TrainStepEngine:
     def step(self, batch: dict, *, mask_all_valid: bool | None = None) -> StepOutput:
         """One optimizer step. ``mask_all_valid`` tells the CUDA-graph path that the batch's
         attention mask is all True (otherwise it is checked, on the host copy when there is one)."""
-        if self.cuda_graph:
-            if self._graph_eligible(batch, mask_all_valid):
-                return self._graph_step(batch)
-            self._resolve_pending()
+        if self.cuda_graph and self._graph_eligible(batch, mask_all_valid):
+            return self._graph_step(batch)
+        self._resolve_pending()
         if batch["input_ids"].device != self.device:
             batch = move_batch(batch, self.device)
         self.model.train()
@@ -122,9 +146,37 @@ class TrainStepEngine:
         elif self.moe_controller is not None:
             self.moe_controller.discard()
         self.optimizer.zero_grad(set_to_none=True)
+        status = self._status_snapshot()
+        if status is not None:
+            self._pending = (None, *self._to_host(status))
         lo = out.loss_output
         return StepOutput(out.loss.detach(), lo.ntp.loss.detach(), None if lo.mtp is None else lo.mtp.loss.detach(),
                           gnorm, executed)
+
+    # ------------------------------------------------------------------ kernel status
+    def _status_snapshot(self):
+        """Stream-ordered copy of the kernels' status words (int32 [2]: GEMM, KDA) or None."""
+        if self._status_words is None:
+            return None
+        return torch.cat(self._status_words)
+
+    @staticmethod
+    def _to_host(t):
+        host = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+        host.copy_(t, non_blocking=True)
+        event = torch.cuda.Event()
+        event.record()
+        return host, event
+
+    def _check_status(self, status) -> None:
+        if status is None:
+            return
+        gemm, kda = (int(v) for v in status.tolist())
+        if gemm or kda:
+            clear_kernel_status(self.device)
+            raise KernelWaitError(
+                f"a bounded wait inside a kernel gave up (GEMM status {gemm}, KDA status {kda}); the results of "
+                "the last step are not valid. Codes: 1-4 GEMM pipeline roles, 5 peer flag, 6 drain, 11-31 KDA MMAs")
 
     # ------------------------------------------------------------------ CUDA graph
     @staticmethod
@@ -166,9 +218,12 @@ class TrainStepEngine:
         """Read the previous replay's skip flag; advance the scheduler only for executed steps."""
         if self._pending is None:
             return
-        flag, event = self._pending
+        flag, status, event = self._pending
         self._pending = None
         event.synchronize()
+        self._check_status(status)
+        if flag is None:
+            return
         if bool(flag.item()):
             if hasattr(self.optimizer, "undo_step_count"):
                 self.optimizer.undo_step_count()
@@ -204,21 +259,27 @@ class TrainStepEngine:
                 self.optimizer.zero_grad(set_to_none=True)
                 res = self._device_step_body(self._static_in, cache_enabled=False)
             torch.cuda.current_stream().wait_stream(side)
+            res = (*res, self._status_snapshot())
         else:
             if self._graph is None:
                 self.optimizer.zero_grad(set_to_none=True)
                 self._graph = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(self._graph):
-                    self._static_out = self._device_step_body(self._static_in, cache_enabled=False)
+                    body = self._device_step_body(self._static_in, cache_enabled=False)
+                    self._static_out = (*body, self._status_snapshot())
             self._graph.replay()
             res = self._static_out
         self._graph_steps += 1
-        loss, ntp, mtp, gnorm, found_inf = res
+        loss, ntp, mtp, gnorm, found_inf, status = res
         flag = torch.empty((), dtype=torch.bool, pin_memory=True)
         flag.copy_(found_inf, non_blocking=True)
+        host_status = None
+        if status is not None:
+            host_status = torch.empty(status.shape, dtype=status.dtype, pin_memory=True)
+            host_status.copy_(status, non_blocking=True)
         event = torch.cuda.Event()
         event.record()
-        self._pending = (flag, event)
+        self._pending = (flag, host_status, event)
         return StepOutput(loss, ntp, mtp, gnorm, True)
 
     def finish(self) -> None:

@@ -117,10 +117,17 @@ def child_timeout(port):
     fake_part = ws.peer_ptrs[0] + (ws.partial_bytes // 2)
     fake_flags = torch.zeros(2 * _TILES_CAP, dtype=torch.int32, device="cuda")
     out = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    torch.cuda.synchronize()
+    import time
+    t0 = time.perf_counter()
     C.tc_gemm_comm(x, w, False, 256, 1, 0, 2, part, [ws.peer_ptrs[0], fake_part], 0,
                    [ws.flag_ptrs[0], fake_flags.data_ptr()], _TILES_CAP, out, ws.status, int(0.2e9))
     torch.cuda.synchronize()
+    elapsed = time.perf_counter() - t0
     assert int(ws.status.item()) == 5, int(ws.status.item())  # the comm timeout code
+    # one time limit (0.2 s) for the whole kernel, not one per tile: every later wait sees the
+    # recorded failure and gives up at once
+    assert elapsed < 2.0, elapsed
     try:
         ws.check()
         raise AssertionError("check() did not raise")

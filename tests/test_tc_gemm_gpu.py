@@ -183,3 +183,29 @@ def test_dense_strided_ragged(cuda, a_mn, b_mn):
     assert (out[:, n:] == 7.0).all()  # nothing written past the logical edge
     out16 = _C().tc_gemm_dense(a, b, a_mn, b_mn, False, 256, None)
     _close(out16, ref)
+
+
+def test_pipeline_wait_gives_up_and_context_survives(cuda):
+    """A pipeline wait shortened to a single poll gives up inside the kernel: the launch reports the
+    failure through the status word, the kernel drains its copies and MMAs and exits, and the next
+    GEMM on the same context is correct."""
+    import time
+    C = _C()
+    torch.manual_seed(3)
+    a = torch.randn(512, 1024, device=cuda).to(torch.bfloat16)
+    b = torch.randn(384, 1024, device=cuda).to(torch.bfloat16)
+    ref = a.float() @ b.float().t()
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    C.tc_gemm_dense(a, b, False, False, False, 256, None, status=status, spin_limit=1)
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 5.0
+    assert int(status.item()) in (1, 2, 3, 4), int(status.item())
+    status.zero_()
+    out = C.tc_gemm_dense(a, b, False, False, False, 256, None, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    _close(out, ref)
+    # the default (per-device) status word saw nothing
+    assert C.tc_gemm_status(False) == 0
