@@ -445,9 +445,14 @@ static void check_tma_matrix(const at::Tensor& t, const char* name) {
 // `status` (int32 CUDA tensor) receives the code of the first bounded wait that gave up; without it
 // the device's default status word does (tc_gemm_status).  `spin_limit` > 0 shortens every
 // pipeline wait to that many polls (tests use it to make a wait run out on purpose).
+// `accumulate` adds the product into `out` (fp32, given) with vector atomics instead of storing it;
+// `ksplit` > 1 splits the K range over that many work units (needs `accumulate`).  `bias` (fp32 [N])
+// and `residual` (bf16 [M, N], row-major) are added in the store epilogue.  `pair`: 1 / 0 force or
+// forbid CTA-pair (cta_group::2) tiles, -1 uses them whenever M > 128.
 at::Tensor tc_gemm_dense(at::Tensor a, at::Tensor b, bool a_mn, bool b_mn, bool out_fp32, int64_t bn,
                          c10::optional<at::Tensor> out_opt, c10::optional<at::Tensor> status_opt,
-                         int64_t spin_limit) {
+                         int64_t spin_limit, bool accumulate, int64_t ksplit, c10::optional<at::Tensor> bias,
+                         c10::optional<at::Tensor> residual, int64_t pair) {
   check_tma_matrix(a, "a");
   check_tma_matrix(b, "b");
   const at::cuda::CUDAGuard gd(a.device());
@@ -463,7 +468,29 @@ at::Tensor tc_gemm_dense(at::Tensor a, at::Tensor b, bool a_mn, bool b_mn, bool 
   TORCH_CHECK(out.is_cuda() && out.dim() == 2 && out.size(0) == M && out.size(1) == N && out.stride(1) == 1 &&
                   out.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0,
               "out must be an [M,N] row-major matrix with a 16-byte aligned row stride");
+  TORCH_CHECK(!accumulate || (out_opt.has_value() && out_opt->defined() && out.scalar_type() == at::kFloat),
+              "accumulate needs a given fp32 out");
+  TORCH_CHECK(ksplit <= 1 || accumulate, "ksplit > 1 needs accumulate");
   kimi::TcGemmArgs g;
+  g.epi = accumulate ? 3 : 0;
+  g.ksplit = (int)std::max<int64_t>(1, ksplit);
+  g.pair = (int)pair;
+  at::Tensor bias_c, res_c;
+  if (bias.has_value() && bias->defined()) {
+    bias_c = bias->to(at::kFloat).contiguous();
+    TORCH_CHECK(bias_c.is_cuda() && bias_c.numel() == N, "bias must hold N values");
+    g.bias = bias_c.data_ptr<float>();
+  }
+  if (residual.has_value() && residual->defined()) {
+    res_c = *residual;
+    TORCH_CHECK(res_c.is_cuda() && res_c.scalar_type() == at::kBFloat16 && res_c.dim() == 2 && res_c.size(0) == M &&
+                    res_c.size(1) == N && res_c.stride(1) == 1 && res_c.stride(0) % 8 == 0 &&
+                    (reinterpret_cast<uintptr_t>(res_c.data_ptr()) & 15) == 0,
+                "residual must be a bf16 [M, N] row-major matrix with a 16-byte aligned row stride");
+    TORCH_CHECK(out.scalar_type() == at::kBFloat16, "a residual needs a bf16 output");
+    g.resid = res_c.data_ptr();
+    g.ldr = res_c.stride(0);
+  }
   g.mode = 0;
   g.bn = (int)bn;
   g.a_mn = a_mn;
@@ -1086,7 +1113,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fa_bwd", &fa_bwd);
   m.def("tc_gemm_dense", &tc_gemm_dense, py::arg("a"), py::arg("b"), py::arg("a_mn"), py::arg("b_mn"),
         py::arg("out_fp32"), py::arg("bn"), py::arg("out") = py::none(), py::arg("status") = py::none(),
-        py::arg("spin_limit") = 0);
+        py::arg("spin_limit") = 0, py::arg("accumulate") = false, py::arg("ksplit") = 1,
+        py::arg("bias") = py::none(), py::arg("residual") = py::none(), py::arg("pair") = -1);
   // Views of the current device's default status words of the GEMM and the KDA kernels (int32
   // [1] each, not owned): a training step copies them to pinned host memory with its other
   // per-step flags, so a bounded wait that gave up inside a kernel surfaces at the next step.

@@ -94,6 +94,10 @@ struct DevParams {
   int agg_tokens;
   int* status;
   uint32_t spin_limit;  // polls per pipeline wait before it gives up (tests shorten it)
+  int ksplit;           // dense mode: the K range is split into this many slices (epi 3 adds them up)
+  const float* bias;    // epi 0: fp32 [N] added to every row (or null)
+  const __nv_bfloat16* resid;  // epi 0, bf16 output: [M, ldr] added to the result (or null)
+  int64_t ldr;
   CommParams cm;
 };
 
@@ -111,10 +115,11 @@ __device__ __forceinline__ int tiles_n_of(const DevParams& p) {
   return (p.N + BNT - 1) / BNT;
 }
 
-template <int BNT>
+// Work units of a launch.  BMT is the output rows of a tile: 128 for one CTA, 256 for a CTA pair.
+template <int BNT, int BMT = BM>
 __device__ int total_tiles(const DevParams& p) {
   const int tn = tiles_n_of<BNT>(p);
-  if (p.mode == 0) return ((p.M + BM - 1) / BM) * tn;
+  if (p.mode == 0) return ((p.M + BMT - 1) / BMT) * tn * p.ksplit;
   if (p.mode == 1) {
     int t = 0;
     for (int g = 0; g < p.G; ++g) t += ((p.offsets[g + 1] - p.offsets[g]) / BM) * tn;
@@ -123,13 +128,20 @@ __device__ int total_tiles(const DevParams& p) {
   return p.G * ((p.M + BM - 1) / BM) * tn;
 }
 
-template <int BNT>
+template <int BNT, int BMT = BM>
 __device__ TileInfo tile_info(const DevParams& p, int tile) {
   const int tn = tiles_n_of<BNT>(p);
   TileInfo ti;
   if (p.mode == 0) {
-    const int tm = (p.M + BM - 1) / BM;
+    const int tm = (p.M + BMT - 1) / BMT;
     ti.g = 0;
+    const int total_kb = (p.K + BK - 1) / BK;
+    int split = 0, kb_per = total_kb;
+    if (p.ksplit > 1) {  // slices of the K range: every output tile of slice 0, then slice 1, ...
+      split = tile / (tm * tn);
+      tile -= split * tm * tn;
+      kb_per = (total_kb + p.ksplit - 1) / p.ksplit;
+    }
     if (p.ag_world > 0) {  // this rank's row blocks first (every column tile), then the remote ones
       const int bpr = p.ag_rows / BM, first = p.ag_rank * bpr, local = bpr * tn;
       if (tile < local) {
@@ -141,11 +153,12 @@ __device__ TileInfo tile_info(const DevParams& p, int tile) {
         ti.n0 = (t2 / rem) * BNT;
       }
     } else {
-      ti.m0 = (tile % tm) * BM;
+      ti.m0 = (tile % tm) * BMT;
       ti.n0 = (tile / tm) * BNT;
     }
-    ti.k0 = 0;
-    ti.num_kb = (p.K + BK - 1) / BK;
+    ti.k0 = split * kb_per * BK;
+    const int left = total_kb - split * kb_per;
+    ti.num_kb = left < kb_per ? (left > 0 ? left : 0) : kb_per;
     ti.c_row0 = ti.m0;
     return ti;
   }
@@ -177,7 +190,6 @@ __device__ TileInfo tile_info(const DevParams& p, int tile) {
   ti.c_row0 = ti.m0;
   return ti;
 }
-
 
 // ---------------------------------------------------------------- cross-rank helpers (comm modes)
 constexpr int kCommTimeout = 5;
@@ -294,13 +306,28 @@ template <int BN>
 __device__ void comm_loop(const DevParams& p, int total);
 __device__ void ag_copy_loop(const DevParams& p);
 
-template <int BN, bool A_MN, bool B_MN, int CM>
+// Shared-memory ring depth: about 192 KB of stages whatever the tile shape.
+template <int BN, bool PAIR>
+constexpr int ring_stages() {
+  return (192 * 1024) / (BM * BK * 2 + (PAIR ? BN / 2 : BN) * BK * 2);
+}
+
+template <int BN, bool A_MN, bool B_MN, int CM, bool PAIR>
 __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid_constant__ DevParams p) {
+  // PAIR: two CTAs of a cluster compute one 256 x BN tile with tcgen05.mma.cta_group::2, issued by
+  // the even CTA.  Each CTA loads its 128 rows of A and its BN / 2 rows of B into its own shared
+  // memory (counted on the even CTA's `full` barrier), owns 128 rows of the accumulator in its own
+  // TMEM and stores them.  Halving each SM's share of B halves the B traffic per MMA, which keeps
+  // the tensor pipe fed at N = 128 and takes a quarter off the L2 -> SMEM bytes at N = 256.
+  constexpr int CTAS = PAIR ? 2 : 1;
+  constexpr int BMT = BM * CTAS;           // output rows of a tile
+  constexpr int BNL = BN / CTAS;           // rows of the B tile held by this CTA
   constexpr int A_BYTES = BM * BK * 2;
-  constexpr int B_BYTES = BN * BK * 2;
+  constexpr int B_BYTES = BNL * BK * 2;
   constexpr int STAGE = A_BYTES + B_BYTES;
-  constexpr int STAGES = BN == 256 ? 4 : 6;
+  constexpr int STAGES = ring_stages<BN, PAIR>();
   constexpr int TMEM_COLS = 2 * BN;
+  static_assert(!PAIR || CM == 0, "CTA pairs run the plain (non-comm) kernel");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE);
@@ -311,6 +338,9 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
   uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bnt = p.situ ? BN / 2 : BN;  // output columns per tile
+  const uint32_t rank = PAIR ? tc::cluster_ctarank() : 0u;
+  const int first_unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int unit_stride = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -319,15 +349,20 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&tfull[b], 1);
-      tc::mbar_init(&tempty[b], 256);
+      tc::mbar_init(&tempty[b], 8 * CTAS);  // one arrival per epilogue warp of every CTA
     }
     tc::mbar_init(drain, 1);
     tc::fence_barrier_init();
     tc::fence_proxy_async();
   }
   if (warp == 1) {
-    tc::tmem_alloc(tslot, TMEM_COLS);
-    tc::tmem_relinquish();
+    if constexpr (PAIR) {
+      tc::tmem_alloc_pair(tslot, TMEM_COLS);
+      tc::tmem_relinquish_pair();
+    } else {
+      tc::tmem_alloc(tslot, TMEM_COLS);
+      tc::tmem_relinquish();
+    }
   }
   if (warp == 0 && lane == 0) {
     tc::tma_prefetch(&p.map_a);
@@ -336,9 +371,10 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
   }
   tc::tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) tc::cluster_sync();  // both CTAs' barriers are initialised before any remote use
   tc::tc_fence_after();
   const uint32_t tmem_base = *tslot;
-  const int total = p.situ ? total_tiles<BN / 2>(p) : total_tiles<BN>(p);
+  const int total = p.situ ? total_tiles<BN / 2, BMT>(p) : total_tiles<BN, BMT>(p);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -349,10 +385,11 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
       uint32_t ph = 0;
       bool ok = true;
       uint32_t inflight = 0, inflight_ph = 0;  // stages filled since their last consumption, and their phase
+      uint64_t last_issue_ns = 0;
       uint32_t ag_target = 0u;
       if constexpr (CM == 3) ag_target = *p.ag_epoch + 1u;
-      for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x) {
-        const TileInfo ti = p.situ ? tile_info<BN / 2>(p, tile) : tile_info<BN>(p, tile);
+      for (int tile = first_unit; ok && tile < total; tile += unit_stride) {
+        const TileInfo ti = p.situ ? tile_info<BN / 2, BMT>(p, tile) : tile_info<BN, BMT>(p, tile);
         for (int kb = 0; kb < ti.num_kb; ++kb) {
           if (!tc::mbar_wait(&empty[s], ph ^ 1, p.status, tc::kTimeoutEmpty, p.spin_limit)) {
             ok = false;
@@ -364,34 +401,27 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
           const int k = ti.k0 + kb * BK;
           if constexpr (CM == 3 && !A_MN) {
             if (kb == 0 && ti.m0 / p.ag_rows != p.ag_rank) {
-            // remote rows: wait until a comm warp has copied this block into the local buffer
-            const uint32_t* f = p.ag_flags + ti.m0 / BM;
-            const uint64_t t0 = global_ns();
-            uint32_t v;
-            while (true) {
-              asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-              if (v >= ag_target) break;
-              if (tc::status_peek(p.status) != 0) {
-                ok = false;
-                break;
+              // remote rows: wait until a comm warp has copied this block into the local buffer
+              const uint32_t* f = p.ag_flags + ti.m0 / BM;
+              const uint64_t t0 = global_ns();
+              uint32_t v;
+              while (true) {
+                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+                if (v >= ag_target) break;
+                if (tc::status_peek(p.status) != 0) {
+                  ok = false;
+                  break;
+                }
+                if ((int64_t)(global_ns() - t0) > (int64_t)10000000000LL) {
+                  atomicCAS(p.status, 0, kCommTimeout);
+                  ok = false;
+                  break;
+                }
+                __nanosleep(64);
               }
-              if ((int64_t)(global_ns() - t0) > (int64_t)10000000000LL) {
-                atomicCAS(p.status, 0, kCommTimeout);
-                ok = false;
-                break;
-              }
-              __nanosleep(64);
+              if (!ok) break;
+              asm volatile("fence.proxy.async.global;" ::: "memory");
             }
-            if (!ok) break;
-            asm volatile("fence.proxy.async.global;" ::: "memory");
-            }
-          }
-          tc::mbar_arrive_expect_tx(&full[s], STAGE);
-          if (!A_MN) {
-            tc::tma_load_2d(sa, &p.map_a, &full[s], k, ti.m0);
-          } else {
-            tc::tma_load_2d(sa, &p.map_a, &full[s], ti.m0, k);
-            tc::tma_load_2d(sa + A_BYTES / 2, &p.map_a, &full[s], ti.m0 + 64, k);
           }
           const CUtensorMap* mb = &p.map_b;
           int kb_coord = k;
@@ -399,16 +429,46 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
             mb = &p.map_b2;
             kb_coord = k - p.b2_k_split;
           }
-          if (p.situ) {
-            tc::tma_load_3d(sb, &p.map_b, &full[s], kb_coord, ti.n0, ti.g);
-            tc::tma_load_3d(sb + B_BYTES / 2, &p.map_b2, &full[s], kb_coord, ti.n0, ti.g);
-          } else if (!B_MN) {
-            tc::tma_load_3d(sb, mb, &full[s], kb_coord, ti.n0, p.mode == 2 ? 0 : ti.g);
-          } else {
+          const int arow = ti.m0 + (int)rank * BM;  // this CTA's rows of the tile
+          if constexpr (PAIR) {
+            // both CTAs' copies are counted on the even CTA's barrier, which expects them all
+            const uint32_t fb = tc::mapa_shared(&full[s], 0);
+            if (rank == 0) tc::mbar_arrive_expect_tx(&full[s], 2 * STAGE);
+            if (!A_MN) {
+              tc::tma_load_2d_pair(sa, &p.map_a, fb, k, arow);
+            } else {
+              tc::tma_load_2d_pair(sa, &p.map_a, fb, arow, k);
+              tc::tma_load_2d_pair(sa + A_BYTES / 2, &p.map_a, fb, arow + 64, k);
+            }
+            if (p.situ) {  // the even CTA holds the gate rows of the tile, the odd one the up rows
+              tc::tma_load_3d_pair(sb, rank == 0 ? &p.map_b : &p.map_b2, fb, kb_coord, ti.n0, ti.g);
+            } else if (!B_MN) {
+              tc::tma_load_3d_pair(sb, mb, fb, kb_coord, ti.n0 + (int)rank * BNL, 0);
+            } else {
 #pragma unroll
-            for (int q = 0; q < BN / 64; ++q)
-              tc::tma_load_3d(sb + q * (BK * 64 * 2), mb, &full[s], ti.n0 + q * 64, kb_coord,
-                              p.mode == 2 ? 0 : ti.g);
+              for (int q = 0; q < BNL / 64; ++q)
+                tc::tma_load_3d_pair(sb + q * (BK * 64 * 2), mb, fb, ti.n0 + (int)rank * BNL + q * 64, kb_coord, 0);
+            }
+            last_issue_ns = global_ns();
+          } else {
+            tc::mbar_arrive_expect_tx(&full[s], STAGE);
+            if (!A_MN) {
+              tc::tma_load_2d(sa, &p.map_a, &full[s], k, ti.m0);
+            } else {
+              tc::tma_load_2d(sa, &p.map_a, &full[s], ti.m0, k);
+              tc::tma_load_2d(sa + A_BYTES / 2, &p.map_a, &full[s], ti.m0 + 64, k);
+            }
+            if (p.situ) {
+              tc::tma_load_3d(sb, &p.map_b, &full[s], kb_coord, ti.n0, ti.g);
+              tc::tma_load_3d(sb + B_BYTES / 2, &p.map_b2, &full[s], kb_coord, ti.n0, ti.g);
+            } else if (!B_MN) {
+              tc::tma_load_3d(sb, mb, &full[s], kb_coord, ti.n0, p.mode == 2 ? 0 : ti.g);
+            } else {
+#pragma unroll
+              for (int q = 0; q < BN / 64; ++q)
+                tc::tma_load_3d(sb + q * (BK * 64 * 2), mb, &full[s], ti.n0 + q * 64, kb_coord,
+                                p.mode == 2 ? 0 : ti.g);
+            }
           }
           inflight |= 1u << s;
           inflight_ph = (inflight_ph & ~(1u << s)) | (ph << s);
@@ -418,18 +478,26 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
           }
         }
       }
-      if (!ok)
-        for (int q = 0; q < STAGES; ++q)
-          if (inflight & (1u << q)) tc::mbar_wait_local(&full[q], (inflight_ph >> q) & 1u, p.status, tc::kTimeoutDrain);
+      if (!ok) {
+        if (!PAIR || rank == 0) {
+          for (int q = 0; q < STAGES; ++q)
+            if (inflight & (1u << q))
+              tc::mbar_wait_local(&full[q], (inflight_ph >> q) & 1u, p.status, tc::kTimeoutDrain, tc::kDrainNs);
+        } else if (inflight) {
+          // the odd CTA's copies are counted on the even CTA's barrier, which it cannot poll: give
+          // them a fixed 200 us (a 16 KB tile lands in a few microseconds) before leaving
+          while (global_ns() - last_issue_ns < 200000ull) __nanosleep(1000);
+        }
+      }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      const uint32_t idesc = tc::instr_desc_f16(BM, BN, true, A_MN, B_MN);
+    if (lane == 0 && (!PAIR || rank == 0)) {
+      const uint32_t idesc = tc::instr_desc_f16(BMT, BN, true, A_MN, B_MN);
       int s = 0, it = 0;
       uint32_t ph = 0;
       bool ok = true, issued = false;
-      for (int tile = blockIdx.x; ok && tile < total; tile += gridDim.x, ++it) {
-        const TileInfo ti = p.situ ? tile_info<BN / 2>(p, tile) : tile_info<BN>(p, tile);
+      for (int tile = first_unit; ok && tile < total; tile += unit_stride, ++it) {
+        const TileInfo ti = p.situ ? tile_info<BN / 2, BMT>(p, tile) : tile_info<BN, BMT>(p, tile);
         const int buf = it & 1;
         const uint32_t tph = (it >> 1) & 1;
         if (!tc::mbar_wait(&tempty[buf], tph ^ 1, p.status, tc::kTimeoutTmemEmpty, p.spin_limit)) {
@@ -452,22 +520,38 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
                                      : tc::smem_desc_sw128(base_a + kk * 32, 16, 1024);
             const uint64_t bd = B_MN ? tc::smem_desc_sw128(base_b + kk * 2048, 8192, 1024)
                                      : tc::smem_desc_sw128(base_b + kk * 32, 16, 1024);
-            tc::mma_f16(d, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            if constexpr (PAIR)
+              tc::mma_f16_pair(d, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            else
+              tc::mma_f16(d, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
           }
           issued = true;
-          tc::mma_commit(&empty[s]);
+          if constexpr (PAIR) {  // the stage is free in both CTAs once these MMAs are done
+            tc::mma_commit_pair(tc::mapa_shared(&empty[s], 0));
+            tc::mma_commit_pair(tc::mapa_shared(&empty[s], 1));
+          } else {
+            tc::mma_commit(&empty[s]);
+          }
           if (++s == STAGES) {
             s = 0;
             ph ^= 1;
           }
         }
         if (!ok) break;
-        tc::mma_commit(&tfull[buf]);
+        if constexpr (PAIR) {
+          tc::mma_commit_pair(tc::mapa_shared(&tfull[buf], 0));
+          tc::mma_commit_pair(tc::mapa_shared(&tfull[buf], 1));
+        } else {
+          tc::mma_commit(&tfull[buf]);
+        }
       }
       if (!ok && issued) {
         // let every issued MMA finish before the CTA frees its TMEM and shared memory
-        tc::mma_commit(drain);
-        tc::mbar_wait_local(drain, 0, p.status, tc::kTimeoutDrain);
+        if constexpr (PAIR)
+          tc::mma_commit_pair(tc::mapa_shared(drain, 0));
+        else
+          tc::mma_commit(drain);
+        tc::mbar_wait_local(drain, 0, p.status, tc::kTimeoutDrain, tc::kDrainNs);
       }
     }
   } else if (warp < 10) {
@@ -475,9 +559,11 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
     const int r_local = sub * 32 + lane;
     const int chalf = (warp - 2) >> 2;  // column half of the tile handled by this warpgroup
     const float ibg = 1.f / p.bg, ibu = 1.f / p.bu;
+    const uint32_t tempty_c0_0 = PAIR ? tc::mapa_shared(&tempty[0], 0) : 0u;
+    const uint32_t tempty_c0_1 = PAIR ? tc::mapa_shared(&tempty[1], 0) : 0u;
     int it = 0;
-    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
-      const TileInfo ti = p.situ ? tile_info<BN / 2>(p, tile) : tile_info<BN>(p, tile);
+    for (int tile = first_unit; tile < total; tile += unit_stride, ++it) {
+      const TileInfo ti = p.situ ? tile_info<BN / 2, BMT>(p, tile) : tile_info<BN, BMT>(p, tile);
       const int buf = it & 1;
       const uint32_t tph = (it >> 1) & 1;
       bool ok = tc::mbar_wait(&tfull[buf], tph, p.status, tc::kTimeoutTmemFull, p.spin_limit);
@@ -488,7 +574,7 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
       if (!ok) break;
       tc::tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + buf * BN;
-      const int row = ti.c_row0 + r_local;
+      const int row = ti.c_row0 + (int)rank * BM + r_local;
       const bool row_ok = (p.mode == 1) ? true : row < p.M;
       for (int c0 = chalf * (bnt / 2); c0 < (chalf + 1) * (bnt / 2); c0 += 32) {
         float v[32];
@@ -556,8 +642,30 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
               }
             }
           }
+        } else if (p.epi == 3) {
+          // fp32 accumulation into `out` (split-K slices, or a gradient that already holds a value)
+          if (row_ok && ti.num_kb > 0) {
+            float* o = reinterpret_cast<float*>(p.out) + (int64_t)row * p.ldc;
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              if (col0 + i + 4 <= p.N) {
+                asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(o + col0 + i),
+                             "f"(v[i]), "f"(v[i + 1]), "f"(v[i + 2]), "f"(v[i + 3])
+                             : "memory");
+              } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                  if (col0 + i + j < p.N) atomicAdd(o + col0 + i + j, v[i + j]);
+              }
+            }
+          }
         } else if (row_ok) {
           const int64_t goff = p.mode == 2 ? (int64_t)ti.g * p.M * p.ldc : 0;
+          if (p.bias) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i < p.N) v[i] += __ldg(p.bias + col0 + i);
+          }
           if (p.out_fp32) {
             float* o = reinterpret_cast<float*>(p.out) + goff + (int64_t)row * p.ldc;
 #pragma unroll
@@ -572,24 +680,41 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
             }
           } else {
             __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + goff + (int64_t)row * p.ldc;
+            const __nv_bfloat16* rr = p.resid ? p.resid + (int64_t)row * p.ldr : nullptr;
 #pragma unroll
             for (int i = 0; i < 32; i += 8) {
               if (col0 + i + 8 <= p.N) {
                 Vec<__nv_bfloat16> vo;
+                if (rr) {
+                  Vec<__nv_bfloat16> vr;
+                  vr.load(rr + col0 + i);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) vo.v[j] = from_f<__nv_bfloat16>(v[i + j]);
+                  for (int j = 0; j < 8; ++j) vo.v[j] = from_f<__nv_bfloat16>(v[i + j] + vr.f(j));
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 8; ++j) vo.v[j] = from_f<__nv_bfloat16>(v[i + j]);
+                }
                 vo.store(o + col0 + i);
               } else {
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
-                  if (col0 + i + j < p.N) o[col0 + i + j] = from_f<__nv_bfloat16>(v[i + j]);
+                  if (col0 + i + j < p.N)
+                    o[col0 + i + j] =
+                        from_f<__nv_bfloat16>(v[i + j] + (rr ? to_f<__nv_bfloat16>(rr[col0 + i + j]) : 0.f));
               }
             }
           }
         }
       }
+      // this warp is done with the accumulator: one arrival per warp on the MMA issuer's barrier
       tc::tc_fence_before();
-      tc::mbar_arrive(&tempty[buf]);
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (PAIR)
+          tc::mbar_arrive_cluster(buf ? tempty_c0_1 : tempty_c0_0);
+        else
+          tc::mbar_arrive(&tempty[buf]);
+      }
       if constexpr (CM == 1 || CM == 2) {
         // this rank's partial tile is in the symmetric buffer: tell the tile's owner
         fence_sys();
@@ -608,8 +733,14 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
   }
   tc::tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) tc::cluster_sync();  // neither CTA leaves while the other may still touch its memory
   tc::tc_fence_after();
-  if (warp == 1) tc::tmem_dealloc(tmem_base, TMEM_COLS);
+  if (warp == 1) {
+    if constexpr (PAIR)
+      tc::tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else
+      tc::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
 }
 
 
@@ -762,29 +893,62 @@ bool debug_on() {
   return on;
 }
 
-template <int BN, bool AMN, bool BMN, int CM = 0>
+template <int BN, bool AMN, bool BMN, int CM = 0, bool PAIR = false>
 cudaError_t launch(const DevParams& dp, int num_sms, cudaStream_t s) {
   // an error left by an unrelated earlier call on this host thread is not this launch's
   const cudaError_t stale = cudaGetLastError();
   if (debug_on() && stale != cudaSuccess) fprintf(stderr, "tc_gemm: stale error before launch: %s\n", cudaGetErrorString(stale));
-  constexpr int STAGES = BN == 256 ? 4 : 6;
-  constexpr int STAGE = BM * BK * 2 + BN * BK * 2;
+  constexpr int STAGES = ring_stages<BN, PAIR>();
+  constexpr int STAGE = BM * BK * 2 + (PAIR ? BN / 2 : BN) * BK * 2;
   const size_t smem = 1024 + (size_t)STAGES * STAGE + (2 * STAGES + 5) * 8 + 16;
+  auto kern = gemm_tc_kernel<BN, AMN, BMN, CM, PAIR>;
+  constexpr int threads = CM ? 448 : 320;
   {
-    cudaError_t e = ensure_dynamic_smem(gemm_tc_kernel<BN, AMN, BMN, CM>, (int)smem);
+    cudaError_t e = ensure_dynamic_smem(kern, (int)smem);
     if (debug_on() && e != cudaSuccess) fprintf(stderr, "tc_gemm: smem attribute failed: %s\n", cudaGetErrorString(e));
     if (e != cudaSuccess) return e;
   }
-  gemm_tc_kernel<BN, AMN, BMN, CM><<<num_sms, CM ? 448 : 320, smem, s>>>(dp);
+  int grid = num_sms;
+  if constexpr (PAIR) {
+    // one CTA pair (a cluster of two) per pair of SMs, as many as can be resident at once
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    static int clusters[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && clusters[dev] == 0) {
+      int n = 0;
+      cfg.gridDim = dim3(num_sms & ~1);
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+        (void)cudaGetLastError();
+        n = num_sms / 2;
+      }
+      clusters[dev] = n < num_sms / 2 ? n : num_sms / 2;
+    }
+    grid = 2 * ((dev >= 0 && dev < 64) ? clusters[dev] : num_sms / 2);
+    cfg.gridDim = dim3(grid);
+    cudaLaunchKernelEx(&cfg, kern, dp);
+  } else {
+    kern<<<grid, threads, smem, s>>>(dp);
+  }
   const cudaError_t e = cudaGetLastError();
   if (debug_on() && e != cudaSuccess) {
     int dev = -1, maxs = -1;
     cudaGetDevice(&dev);
     cudaFuncAttributes fa{};
-    cudaFuncGetAttributes(&fa, gemm_tc_kernel<BN, AMN, BMN, CM>);
+    cudaFuncGetAttributes(&fa, kern);
     maxs = fa.maxDynamicSharedSizeBytes;
     fprintf(stderr, "tc_gemm: launch failed: %s (device %d, grid %d, smem %zu, max dynamic smem %d, params %zu)\n",
-            cudaGetErrorString(e), dev, num_sms, smem, maxs, sizeof(DevParams));
+            cudaGetErrorString(e), dev, grid, smem, maxs, sizeof(DevParams));
   }
   return e;
 }
@@ -875,6 +1039,18 @@ cudaError_t tc_gemm(const TcGemmArgs& a, cudaStream_t stream) {
   const int bn = a.epi == 1 ? 256 : a.bn;
   if (bn != 128 && bn != 256) return cudaErrorInvalidValue;
   if (a.epi == 1 && (a.a_mn || a.b_mn || !a.b2)) return cudaErrorInvalidValue;
+  dp.ksplit = a.ksplit > 1 ? a.ksplit : 1;
+  dp.bias = a.bias;
+  dp.resid = reinterpret_cast<const __nv_bfloat16*>(a.resid);
+  dp.ldr = a.ldr;
+  if (dp.ksplit > 1 && (a.mode != 0 || a.epi != 3 || a.comm_mode != 0 || a.ag_world > 0)) return cudaErrorInvalidValue;
+  if (a.epi == 3 && (!a.out_fp32 || a.mode != 0 || a.comm_mode != 0)) return cudaErrorInvalidValue;
+  if ((a.bias || a.resid) && (a.epi != 0 || a.mode != 0 || a.comm_mode != 0)) return cudaErrorInvalidValue;
+  if (a.resid && (a.out_fp32 || a.ldr % 8 || (reinterpret_cast<uintptr_t>(a.resid) & 15))) return cudaErrorInvalidValue;
+  // CTA pairs: dense non-comm launches of more than one 128-row block (pair = -1 picks this)
+  const bool pair_ok = a.mode == 0 && a.comm_mode == 0 && a.ag_world == 0 && a.epi != 2;
+  const bool pair = pair_ok && (a.pair > 0 || (a.pair < 0 && a.M > BM));
+  if (a.pair > 0 && !pair_ok) return cudaErrorInvalidValue;
   // A: K-major storage [a_rows, a_cols=K]; MN-major storage [a_rows=K, a_cols=M]
   if (!a.a_mn) {
     if (!make_map_2d(&dp.map_a, a.a, a.a_cols, a.a_rows, a.a_ld * 2, 64, 128)) {
@@ -885,7 +1061,7 @@ cudaError_t tc_gemm(const TcGemmArgs& a, cudaStream_t stream) {
     if (!make_map_2d(&dp.map_a, a.a, a.a_cols, a.a_rows, a.a_ld * 2, 64, 64)) return cudaErrorInvalidValue;
   }
   // B: K-major storage [G, N, K]; MN-major storage [G, K, N]
-  const uint32_t bbox_rows = a.epi == 1 ? 128 : (uint32_t)bn;
+  const uint32_t bbox_rows = a.epi == 1 ? 128 : (uint32_t)(pair ? bn / 2 : bn);
   const void* bptrs[2] = {a.b, a.b2};
   CUtensorMap* bmaps[2] = {&dp.map_b, &dp.map_b2};
   for (int i = 0; i < 2; ++i) {
@@ -938,6 +1114,19 @@ cudaError_t tc_gemm(const TcGemmArgs& a, cudaStream_t stream) {
     return (bn == 256 ? (a.b_mn ? launch<256, false, true, 3>(dp, sms, stream) : launch<256, false, false, 3>(dp, sms, stream))
                       : (a.b_mn ? launch<128, false, true, 3>(dp, sms, stream) : launch<128, false, false, 3>(dp, sms, stream)));
 #define KIMI_TC_LAUNCH(BN_, AM_, BM_) return launch<BN_, AM_, BM_>(dp, sms, stream)
+#define KIMI_TC_LAUNCH_PAIR(BN_, AM_, BM_) return launch<BN_, AM_, BM_, 0, true>(dp, sms, stream)
+  if (pair) {
+    if (bn == 256) {
+      if (!a.a_mn && !a.b_mn) KIMI_TC_LAUNCH_PAIR(256, false, false);
+      if (!a.a_mn && a.b_mn) KIMI_TC_LAUNCH_PAIR(256, false, true);
+      if (a.a_mn && !a.b_mn) KIMI_TC_LAUNCH_PAIR(256, true, false);
+      KIMI_TC_LAUNCH_PAIR(256, true, true);
+    }
+    if (!a.a_mn && !a.b_mn) KIMI_TC_LAUNCH_PAIR(128, false, false);
+    if (!a.a_mn && a.b_mn) KIMI_TC_LAUNCH_PAIR(128, false, true);
+    if (a.a_mn && !a.b_mn) KIMI_TC_LAUNCH_PAIR(128, true, false);
+    KIMI_TC_LAUNCH_PAIR(128, true, true);
+  }
   if (bn == 256) {
     if (!a.a_mn && !a.b_mn) KIMI_TC_LAUNCH(256, false, false);
     if (!a.a_mn && a.b_mn) KIMI_TC_LAUNCH(256, false, true);
@@ -949,6 +1138,7 @@ cudaError_t tc_gemm(const TcGemmArgs& a, cudaStream_t stream) {
   if (a.a_mn && !a.b_mn) KIMI_TC_LAUNCH(128, true, false);
   KIMI_TC_LAUNCH(128, true, true);
 #undef KIMI_TC_LAUNCH
+#undef KIMI_TC_LAUNCH_PAIR
 }
 
 }  // namespace kimi

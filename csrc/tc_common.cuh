@@ -7,7 +7,7 @@
 // at [61,64) (SWIZZLE_128B = 2); instruction: c_format [4,6), a_format [7,10), b_format
 // [10,13), a_major bit 15, b_major bit 16, N >> 3 at [17,23), M >> 4 at [24,29).
 //
-// Every wait on an mbarrier is bounded: after kSpinLimit polls it records an error code in
+// Every wait on an mbarrier is bounded: after a time limit (2 s) it records an error code in
 // the kernel's status word and returns, so a broken pipeline ends the kernel instead of
 // hanging the GPU (the host checks the status word).  A pipeline wait (one role of a
 // warp-specialised kernel waiting on another) also gives up as soon as the status word shows
@@ -23,7 +23,7 @@
 namespace kimi {
 namespace tc {
 
-constexpr uint32_t kSpinLimit = 1u << 26;
+constexpr uint32_t kSpinLimit = 0xFFFFFFFFu;  // polls: no limit by count, only by time
 
 enum Status : int {
   kOk = 0, kTimeoutFull = 1, kTimeoutEmpty = 2, kTimeoutTmemFull = 3, kTimeoutTmemEmpty = 4, kTimeoutDrain = 6
@@ -62,21 +62,47 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ int status_peek(const int* status) {
   return status ? *reinterpret_cast<const volatile int*>(status) : 0;
 }
-// Bounded pipeline wait: false after `limit` polls (records `code` in *status, first error
-// wins) or as soon as *status is non-zero (checked every 1024 polls).
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Time limits of the bounded waits.  Pipeline waits normally complete within microseconds; the
+// limits only end a kernel whose pipeline has broken.
+constexpr uint64_t kWaitNs = 2000000000ull;   // a pipeline or MMA-completion wait
+constexpr uint64_t kDrainNs = 200000000ull;   // the exit path waiting for copies / MMAs in flight
+
+// Bounded pipeline wait: false after `limit` polls or kWaitNs (records `code` in *status, first
+// error wins), or as soon as *status is non-zero.  The clock and the status word are read every
+// 1024 polls.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code,
                                           uint32_t limit = kSpinLimit) {
-  for (uint32_t i = 0; i < limit; ++i) {
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 1023u) == 1023u && status_peek(status) != 0) return false;
+    if (i + 1 >= limit) break;
+    if ((i & 1023u) == 1023u) {
+      if (status_peek(status) != 0) return false;
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) t0 = now;
+      else if (now - t0 > kWaitNs) break;
+    }
   }
   if (status) atomicCAS(status, 0, code);
   return false;
 }
 // Bounded wait for this thread's own copies / MMAs (always complete): ignores the status word.
-__device__ __forceinline__ bool mbar_wait_local(uint64_t* bar, uint32_t parity, int* status, int code) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
+__device__ __forceinline__ bool mbar_wait_local(uint64_t* bar, uint32_t parity, int* status, int code,
+                                                uint64_t limit_ns = kWaitNs) {
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 1023u) == 1023u) {
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) t0 = now;
+      else if (now - t0 > limit_ns) break;
+    }
+  }
   if (status) atomicCAS(status, 0, code);
   return false;
 }

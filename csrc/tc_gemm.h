@@ -21,7 +21,7 @@ struct TcGemmArgs {
   int b2_k_split = 0;
   int M = 0, N = 0, K = 0, G = 1;
   const int* offsets = nullptr;  // device [G+1]
-  int epi = 0;                   // 0 store, 1 SiTU, 2 weighted scatter-add (fp32)
+  int epi = 0;                   // 0 store, 1 SiTU, 2 weighted scatter-add (fp32), 3 fp32 add into out
   void* out = nullptr;
   bool out_fp32 = false;
   int64_t ldc = 0;
@@ -40,6 +40,14 @@ struct TcGemmArgs {
   int ag_world = 0, ag_rows = 0, ag_rank = 0;
   uint32_t* ag_flags = nullptr;
   const uint32_t* ag_epoch = nullptr;
+  // Dense mode only: split the K range into `ksplit` slices (epi 3 adds them into `out`); an fp32
+  // bias [N] or a bf16 residual [M, ldr] added in the store epilogue; CTA pairs (cta_group::2,
+  // 256-row tiles): 1 on, 0 off, -1 whenever M > 128.
+  int ksplit = 1;
+  const float* bias = nullptr;
+  const void* resid = nullptr;
+  int64_t ldr = 0;
+  int pair = -1;
   int* status = nullptr;     // null: the device's default status word (tc_gemm_status)
   uint32_t spin_limit = 0;   // polls per pipeline wait before giving up; 0 = the built-in limit
   int num_sms = 0;

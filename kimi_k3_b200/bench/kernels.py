@@ -66,6 +66,84 @@ def bench_gemm(args) -> list:
     return rows
 
 
+def bench_gemm_variants(args) -> list:
+    """Dense GEMM ``[m,k] x [n,k]^T``: every tile variant of the tcgen05 kernel (one CTA with 128 or 256
+    output columns, CTA pairs with 256-row tiles) against cuBLAS (``torch.mm``)."""
+    C, dev = _require_cuda()
+    torch.manual_seed(0)
+    m, n, k = args.m, args.n, args.k
+    a = torch.randn(m, k, device=dev).bfloat16()
+    b = torch.randn(n, k, device=dev).bfloat16()
+    out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    flops = 2.0 * m * n * k
+    rows = []
+    for pair in (0, 1):
+        for bn in (128, 256):
+            t = time_fn(lambda: C.tc_gemm_dense(a, b, False, False, False, bn, out, pair=pair), device=dev,
+                        warmup=args.warmup, repeats=args.repeats)
+            rows.append(_emit({"case": "gemm", "impl": f"tcgen05_bn{bn}_{'pair' if pair else 'single'}", "m": m,
+                               "n": n, "k": k, **t.as_dict(), **roofline(t.median_ms, flops=flops)}))
+    ref = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    t = time_fn(lambda: torch.mm(a, b.t(), out=ref), device=dev, warmup=args.warmup, repeats=args.repeats)
+    rows.append(_emit({"case": "gemm", "impl": "cublas", "m": m, "n": n, "k": k, **t.as_dict(),
+                       **roofline(t.median_ms, flops=flops)}))
+    C.tc_gemm_dense(a, b, False, False, False, 256, out, pair=1)
+    err = ((out.float() - ref.float()).norm() / ref.float().norm()).item()
+    rows.append(_emit({"case": "gemm", "check": "rel_err_vs_cublas", "value": err}))
+    return rows
+
+
+# (name, output features, input features) of the flagship model's dense projections
+PROJECTION_SHAPES = [
+    ("attn_640x640", 640, 640), ("qkv_fused", 1920, 640), ("shared_gate_up", 1920, 640),
+    ("shared_down", 640, 960), ("moe_down", 320, 640), ("moe_up", 640, 320), ("mtp_fusion", 640, 1280),
+]
+
+
+def bench_projections(args) -> list:
+    """Forward ``y = x W^T``, input gradient ``dX = dY W`` and weight gradient ``dW = dY^T X`` of every
+    projection shape of the flagship model at ``--tokens`` rows: the tcgen05 kernel (best tile variant,
+    split-K fp32 weight gradient) against cuBLAS (``torch.mm`` on bf16, bf16 output)."""
+    C, dev = _require_cuda()
+    torch.manual_seed(0)
+    t = args.tokens
+    rows = []
+    for name, n_out, k_in in PROJECTION_SHAPES:
+        x = torch.randn(t, k_in, device=dev).bfloat16()
+        w = (torch.randn(n_out, k_in, device=dev) / k_in ** 0.5).bfloat16()
+        dy = torch.randn(t, n_out, device=dev).bfloat16()
+        y = torch.empty(t, n_out, device=dev, dtype=torch.bfloat16)
+        dx = torch.empty(t, k_in, device=dev, dtype=torch.bfloat16)
+        dw = torch.zeros(n_out, k_in, device=dev)
+        flops = 2.0 * t * n_out * k_in
+        ksplit = max(1, min(16, (2 * 148) // max(1, ((n_out + 255) // 256) * ((k_in + 127) // 128))))
+        cases = {
+            "fwd": [(f"ours_bn{bn}_p{p}", (lambda bn=bn, p=p: C.tc_gemm_dense(x, w, False, False, False, bn, y, pair=p)))
+                    for bn in (128, 256) for p in (0, 1)],
+            "dgrad": [(f"ours_bn{bn}_p{p}", (lambda bn=bn, p=p: C.tc_gemm_dense(dy, w, False, True, False, bn, dx,
+                                                                                pair=p)))
+                      for bn in (128, 256) for p in (0, 1)],
+            "wgrad": [(f"ours_bn{bn}_p{p}_k{ks}", (lambda bn=bn, p=p, ks=ks: C.tc_gemm_dense(
+                dy, x, True, True, True, bn, dw, accumulate=True, ksplit=ks, pair=p)))
+                      for bn in (128, 256) for p in (0, 1) for ks in sorted({1, ksplit})],
+        }
+        ref = {"fwd": lambda: torch.mm(x, w.t(), out=y), "dgrad": lambda: torch.mm(dy, w, out=dx),
+               "wgrad": lambda: torch.mm(dy.t(), x)}
+        for kind, variants in cases.items():
+            best = None
+            for label, fn in variants:
+                tm = time_fn(fn, device=dev, warmup=args.warmup, repeats=args.repeats)
+                if best is None or tm.median_ms < best[1].median_ms:
+                    best = (label, tm)
+            tr = time_fn(ref[kind], device=dev, warmup=args.warmup, repeats=args.repeats)
+            rows.append(_emit({"case": "projection", "shape": name, "pass": kind, "tokens": t, "n_out": n_out,
+                               "k_in": k_in, "ours": best[0], "ours_ms": round(best[1].median_ms, 4),
+                               "cublas_ms": round(tr.median_ms, 4),
+                               "speedup": round(tr.median_ms / best[1].median_ms, 3),
+                               **roofline(best[1].median_ms, flops=flops)}))
+    return rows
+
+
 def bench_kda(args) -> list:
     from ..ops import kda_chunk
     _, dev = _require_cuda()
@@ -262,7 +340,8 @@ def bench_decode(args) -> list:
     return rows
 
 
-CASES = {"kda_phases": bench_kda_phases, "gemm": bench_gemm, "kda": bench_kda, "moe": bench_moe, "linear_ce": bench_linear_ce,
+CASES = {"kda_phases": bench_kda_phases, "gemm": bench_gemm, "gemm_variants": bench_gemm_variants,
+         "projections": bench_projections, "kda": bench_kda, "moe": bench_moe, "linear_ce": bench_linear_ce,
          "attention": bench_attention, "attnres": bench_attnres, "decode": bench_decode}
 
 
@@ -290,7 +369,7 @@ def build_parser(parser: argparse.ArgumentParser | None = None) -> argparse.Argu
 
 def main(argv=None) -> list:
     args = build_parser().parse_args(argv)
-    if args.case == "moe" and args.tokens == 1024:
+    if args.case in ("moe", "projections") and args.tokens == 1024:
         args.tokens = 16384  # one micro-batch of the flagship config
     return CASES[args.case](args)
 

@@ -209,3 +209,50 @@ def test_pipeline_wait_gives_up_and_context_survives(cuda):
     _close(out, ref)
     # the default (per-device) status word saw nothing
     assert C.tc_gemm_status(False) == 0
+
+
+@pytest.mark.parametrize("a_mn", [False, True])
+@pytest.mark.parametrize("b_mn", [False, True])
+@pytest.mark.parametrize("shape", [(512, 384, 512), (200, 136, 72), (1000, 640, 640), (384, 1920, 128)])
+@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("pair", [0, 1])
+def test_dense_cta_pair(cuda, a_mn, b_mn, shape, bn, pair):
+    """256-row tiles on CTA pairs (tcgen05.mma.cta_group::2) against the single-CTA kernel and fp32."""
+    m, n, k = shape
+    torch.manual_seed(m + 3 * n + k)
+    a = torch.randn(m, k, device=cuda).to(torch.bfloat16)
+    b = torch.randn(n, k, device=cuda).to(torch.bfloat16)
+    ref = a.float() @ b.float().t()
+    a_in = a.t().contiguous() if a_mn else a
+    b_in = b.t().contiguous() if b_mn else b
+    out = _C().tc_gemm_dense(a_in, b_in, a_mn, b_mn, True, bn, None, pair=pair)
+    _close(out, ref, 1e-3)
+    out16 = _C().tc_gemm_dense(a_in, b_in, a_mn, b_mn, False, bn, None, pair=pair)
+    _close(out16, ref)
+
+
+@pytest.mark.parametrize("pair", [0, 1])
+def test_dense_bias_residual_epilogue(cuda, pair):
+    torch.manual_seed(7)
+    m, n, k = 700, 640, 320
+    a = torch.randn(m, k, device=cuda).to(torch.bfloat16)
+    b = torch.randn(n, k, device=cuda).to(torch.bfloat16)
+    bias = torch.randn(n, device=cuda)
+    res = torch.randn(m, n, device=cuda).to(torch.bfloat16)
+    out = _C().tc_gemm_dense(a, b, False, False, False, 128, None, bias=bias, residual=res, pair=pair)
+    _close(out, a.float() @ b.float().t() + bias + res.float())
+
+
+@pytest.mark.parametrize("ksplit", [1, 3, 8])
+@pytest.mark.parametrize("pair", [0, 1])
+def test_dense_accumulate_split_k(cuda, ksplit, pair):
+    """Weight-gradient form dW += dY^T X (both operands MN-major) with the K range split over work units
+    whose fp32 partial tiles are added into the existing gradient."""
+    torch.manual_seed(11)
+    t, n_out, k_in = 4096, 640, 320
+    dy = torch.randn(t, n_out, device=cuda).to(torch.bfloat16)
+    x = torch.randn(t, k_in, device=cuda).to(torch.bfloat16)
+    g0 = torch.randn(n_out, k_in, device=cuda)
+    out = g0.clone()
+    _C().tc_gemm_dense(dy, x, True, True, True, 128, out, accumulate=True, ksplit=ksplit, pair=pair)
+    _close(out, g0 + dy.float().t() @ x.float(), 1e-3)
