@@ -337,6 +337,22 @@ std::vector<at::Tensor> kda_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Te
   return {dq, dk, dv, dg, dbeta, dh0};
 }
 
+// ---------------------------------------------------------------- bf16 weight mirrors
+// One launch: dst[t] = bf16(src[t]) for every tensor of a table.  `tables` is an int64 CUDA tensor
+// [4, T + 1]: rows 0-2 hold the source pointers, destination pointers and element counts (entry T
+// unused), row 3 the prefix sums of ceil(numel / 8); `total_vec` = tables[3][T].
+void cast_bf16_multi(at::Tensor tables, int64_t tensors, int64_t total_vec) {
+  TORCH_CHECK(tables.is_cuda() && tables.scalar_type() == at::kLong && tables.is_contiguous() && tables.dim() == 2 &&
+                  tables.size(0) == 4 && tables.size(1) == tensors + 1,
+              "tables must be a contiguous int64 CUDA tensor [4, tensors + 1]");
+  const at::cuda::CUDAGuard gd(tables.device());
+  const int64_t* t = tables.data_ptr<int64_t>();
+  const int64_t w = tensors + 1;
+  check(kimi::cast_bf16_multi(reinterpret_cast<const float* const*>(t), reinterpret_cast<void* const*>(t + w), t + 2 * w,
+                              t + 3 * w, (int)tensors, total_vec, stream()),
+        "cast_bf16_multi");
+}
+
 // ---------------------------------------------------------------- fused Muon passes
 void muon_momentum(at::Tensor g, at::Tensor mom, at::Tensor x, at::Tensor sumsq, double momentum, bool nesterov,
                    c10::optional<at::Tensor> skip) {
@@ -452,7 +468,7 @@ static void check_tma_matrix(const at::Tensor& t, const char* name) {
 at::Tensor tc_gemm_dense(at::Tensor a, at::Tensor b, bool a_mn, bool b_mn, bool out_fp32, int64_t bn,
                          c10::optional<at::Tensor> out_opt, c10::optional<at::Tensor> status_opt,
                          int64_t spin_limit, bool accumulate, int64_t ksplit, c10::optional<at::Tensor> bias,
-                         c10::optional<at::Tensor> residual, int64_t pair) {
+                         c10::optional<at::Tensor> residual, int64_t pair, int64_t debug) {
   check_tma_matrix(a, "a");
   check_tma_matrix(b, "b");
   const at::cuda::CUDAGuard gd(a.device());
@@ -475,6 +491,7 @@ at::Tensor tc_gemm_dense(at::Tensor a, at::Tensor b, bool a_mn, bool b_mn, bool 
   g.epi = accumulate ? 3 : 0;
   g.ksplit = (int)std::max<int64_t>(1, ksplit);
   g.pair = (int)pair;
+  g.debug = (int)debug;
   at::Tensor bias_c, res_c;
   if (bias.has_value() && bias->defined()) {
     bias_c = bias->to(at::kFloat).contiguous();
@@ -1103,6 +1120,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("router", &router);
   m.def("tcs_selftest", &tcs_selftest);
   m.def("muon_momentum", &muon_momentum);
+  m.def("cast_bf16_multi", &cast_bf16_multi);
   m.def("muon_normalize", &muon_normalize);
   m.def("muon_apply", &muon_apply);
   m.def("kda_phase_profile", &kimi::kda_phase_profile);
@@ -1114,7 +1132,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tc_gemm_dense", &tc_gemm_dense, py::arg("a"), py::arg("b"), py::arg("a_mn"), py::arg("b_mn"),
         py::arg("out_fp32"), py::arg("bn"), py::arg("out") = py::none(), py::arg("status") = py::none(),
         py::arg("spin_limit") = 0, py::arg("accumulate") = false, py::arg("ksplit") = 1,
-        py::arg("bias") = py::none(), py::arg("residual") = py::none(), py::arg("pair") = -1);
+        py::arg("bias") = py::none(), py::arg("residual") = py::none(), py::arg("pair") = -1, py::arg("debug") = 0);
   // Views of the current device's default status words of the GEMM and the KDA kernels (int32
   // [1] each, not owned): a training step copies them to pinned host memory with its other
   // per-step flags, so a bounded wait that gave up inside a kernel surfaces at the next step.

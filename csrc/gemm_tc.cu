@@ -95,6 +95,7 @@ struct DevParams {
   int* status;
   uint32_t spin_limit;  // polls per pipeline wait before it gives up (tests shorten it)
   int ksplit;           // dense mode: the K range is split into this many slices (epi 3 adds them up)
+  int debug;            // bit 0: skip the epilogue's global stores (timing experiments only)
   const float* bias;    // epi 0: fp32 [N] added to every row (or null)
   const __nv_bfloat16* resid;  // epi 0, bf16 output: [M, ldr] added to the result (or null)
   int64_t ldr;
@@ -659,7 +660,7 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
               }
             }
           }
-        } else if (row_ok) {
+        } else if (row_ok && !(p.debug & 1)) {
           const int64_t goff = p.mode == 2 ? (int64_t)ti.g * p.M * p.ldc : 0;
           if (p.bias) {
 #pragma unroll
@@ -1040,6 +1041,7 @@ cudaError_t tc_gemm(const TcGemmArgs& a, cudaStream_t stream) {
   if (bn != 128 && bn != 256) return cudaErrorInvalidValue;
   if (a.epi == 1 && (a.a_mn || a.b_mn || !a.b2)) return cudaErrorInvalidValue;
   dp.ksplit = a.ksplit > 1 ? a.ksplit : 1;
+  dp.debug = a.debug;
   dp.bias = a.bias;
   dp.resid = reinterpret_cast<const __nv_bfloat16*>(a.resid);
   dp.ldr = a.ldr;

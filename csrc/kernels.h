@@ -91,6 +91,11 @@ cudaError_t kda_state_bwd_tc(int dtype, KdaBuffers buf, const void* dout, const 
 std::vector<long long> kda_phase_profile(bool enable);
 // Device status word shared by the tcgen05 KDA kernels (read and cleared by the host).
 int kda_tc_status(bool clear);
+
+// ---- bf16 mirrors of fp32 tensors (optim.cu): device tables of source / destination pointers,
+// element counts and the prefix sums of ceil(numel / 8) (tensors + 1 entries); 16-byte aligned tensors.
+cudaError_t cast_bf16_multi(const float* const* src, void* const* dst, const int64_t* numel, const int64_t* vec_off,
+                            int tensors, int64_t total_vec, cudaStream_t s);
 // Device address of the current device's default KDA status word (for stream-ordered reads).
 int* kda_tc_default_status();
 

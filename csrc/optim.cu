@@ -13,6 +13,7 @@
 // Parity: the Muon update of `training/optimizer/muon.py` (reference) with the bucketed batching
 // of this framework's optimizer.
 #include "common.cuh"
+#include "device_info.h"
 #include "kernels.h"
 
 namespace kimi {
@@ -173,7 +174,50 @@ int blocks_per_matrix(int64_t mn) {
   return (int)(b < 1 ? 1 : (b > 64 ? 64 : b));
 }
 
+// bf16 mirrors of fp32 tensors (one launch for a whole table).  `vec_off[t]` is the first 8-element
+// vector of tensor t in a virtual concatenation (prefix sums of ceil(numel / 8)); a thread converts
+// one vector: 32 bytes read, 16 bytes written.
+__global__ void __launch_bounds__(kThreads) cast_bf16_multi_kernel(const float* const* __restrict__ src,
+                                                                   __nv_bfloat16* const* __restrict__ dst,
+                                                                   const int64_t* __restrict__ numel,
+                                                                   const int64_t* __restrict__ vec_off, int tensors) {
+  const int64_t total = vec_off[tensors];
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < total; v += (int64_t)gridDim.x * blockDim.x) {
+    int lo = 0, hi = tensors - 1;  // last t with vec_off[t] <= v
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (vec_off[mid] <= v) lo = mid;
+      else hi = mid - 1;
+    }
+    const int64_t e = (v - vec_off[lo]) * 8, n = numel[lo];
+    const float* sp = src[lo] + e;
+    __nv_bfloat16* dp = dst[lo] + e;
+    if (e + 8 <= n) {
+      const float4 a = reinterpret_cast<const float4*>(sp)[0], b = reinterpret_cast<const float4*>(sp)[1];
+      Vec<__nv_bfloat16> o;
+      o.v[0] = __float2bfloat16_rn(a.x); o.v[1] = __float2bfloat16_rn(a.y);
+      o.v[2] = __float2bfloat16_rn(a.z); o.v[3] = __float2bfloat16_rn(a.w);
+      o.v[4] = __float2bfloat16_rn(b.x); o.v[5] = __float2bfloat16_rn(b.y);
+      o.v[6] = __float2bfloat16_rn(b.z); o.v[7] = __float2bfloat16_rn(b.w);
+      o.store(dp);
+    } else {
+      for (int64_t i = 0; e + i < n; ++i) dp[i] = __float2bfloat16_rn(sp[i]);
+    }
+  }
+}
+
 }  // namespace
+
+cudaError_t cast_bf16_multi(const float* const* src, void* const* dst, const int64_t* numel, const int64_t* vec_off,
+                            int tensors, int64_t total_vec, cudaStream_t s) {
+  if (tensors <= 0 || total_vec <= 0) return cudaSuccess;
+  int64_t blocks = (total_vec + kThreads - 1) / kThreads;
+  const int64_t cap = (int64_t)device_sms() * 16;
+  if (blocks > cap) blocks = cap;
+  cast_bf16_multi_kernel<<<(int)blocks, kThreads, 0, s>>>(src, reinterpret_cast<__nv_bfloat16* const*>(dst), numel,
+                                                          vec_off, tensors);
+  return cudaGetLastError();
+}
 
 cudaError_t muon_momentum(const float* g, float* mom, void* x_bf16, float* sumsq, int count, int64_t mn,
                           float momentum, bool nesterov, const bool* skip, cudaStream_t s) {

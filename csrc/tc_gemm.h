@@ -48,6 +48,7 @@ struct TcGemmArgs {
   const void* resid = nullptr;
   int64_t ldr = 0;
   int pair = -1;
+  int debug = 0;  // bit 0: skip the store epilogue's global writes (timing experiments)
   int* status = nullptr;     // null: the device's default status word (tc_gemm_status)
   uint32_t spin_limit = 0;   // polls per pipeline wait before giving up; 0 = the built-in limit
   int num_sms = 0;

@@ -33,6 +33,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .. import ops as _ops
+from .linear import Linear
 from ..runtime import host_checks
 from .primitives import (CausalShortConv1D, FullRankOutputGate, HeadwiseRMSNorm, ShortConvState,
                          combine_heads)
@@ -340,15 +341,15 @@ class KDAProjections(nn.Module):
     def __init__(self, config: KDAConfig):
         super().__init__()
         self.config = c = config
-        self.q_proj = nn.Linear(c.d_model, c.key_width, bias=c.projection_bias)
-        self.k_proj = nn.Linear(c.d_model, c.key_width, bias=c.projection_bias)
-        self.v_proj = nn.Linear(c.d_model, c.value_width, bias=c.projection_bias)
+        self.q_proj = Linear(c.d_model, c.key_width, bias=c.projection_bias)
+        self.k_proj = Linear(c.d_model, c.key_width, bias=c.projection_bias)
+        self.v_proj = Linear(c.d_model, c.value_width, bias=c.projection_bias)
         self.q_conv = CausalShortConv1D(c.key_width, c.short_conv_kernel_size, bias=c.short_conv_bias)
         self.k_conv = CausalShortConv1D(c.key_width, c.short_conv_kernel_size, bias=c.short_conv_bias)
         self.v_conv = CausalShortConv1D(c.value_width, c.short_conv_kernel_size, bias=c.short_conv_bias)
-        self.beta_proj = nn.Linear(c.d_model, c.num_heads, bias=c.beta_bias)
-        self.alpha_down = nn.Linear(c.d_model, c.resolved_decay_rank, bias=False)
-        self.alpha_up = nn.Linear(c.resolved_decay_rank, c.key_width, bias=False)
+        self.beta_proj = Linear(c.d_model, c.num_heads, bias=c.beta_bias)
+        self.alpha_down = Linear(c.d_model, c.resolved_decay_rank, bias=False)
+        self.alpha_up = Linear(c.resolved_decay_rank, c.key_width, bias=False)
         self.b_alpha = nn.Parameter(torch.empty(c.num_heads, c.key_head_dim))
         self.reset_parameters()
 

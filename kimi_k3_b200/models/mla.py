@@ -26,6 +26,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .. import ops as _ops
+from .linear import Linear
 from .primitives import FullRankOutputGate, combine_heads
 
 
@@ -236,9 +237,9 @@ class LatentKVProjection(nn.Module):
     def __init__(self, config: GatedMLAConfig):
         super().__init__()
         self.config = c = config
-        self.compression = nn.Linear(c.d_model, c.kv_latent_dim, bias=c.projection_bias)
-        self.key_up = nn.Linear(c.kv_latent_dim, c.query_width, bias=c.projection_bias)
-        self.value_up = nn.Linear(c.kv_latent_dim, c.value_width, bias=c.projection_bias)
+        self.compression = Linear(c.d_model, c.kv_latent_dim, bias=c.projection_bias)
+        self.key_up = Linear(c.kv_latent_dim, c.query_width, bias=c.projection_bias)
+        self.value_up = Linear(c.kv_latent_dim, c.value_width, bias=c.projection_bias)
         for proj in (self.compression, self.key_up, self.value_up):
             nn.init.normal_(proj.weight, mean=0.0, std=c.init_std)
             if proj.bias is not None:
@@ -272,7 +273,7 @@ class MLAProjections(nn.Module):
     def __init__(self, config: GatedMLAConfig):
         super().__init__()
         self.config = config
-        self.query = nn.Linear(config.d_model, config.query_width, bias=config.projection_bias)
+        self.query = Linear(config.d_model, config.query_width, bias=config.projection_bias)
         self.latent_kv = LatentKVProjection(config)
         nn.init.normal_(self.query.weight, mean=0.0, std=config.init_std)
         if self.query.bias is not None:

@@ -21,6 +21,7 @@ import torch
 import torch.nn as nn
 
 from .. import ops as _ops
+from .linear import Linear
 from ..runtime import host_checks
 from .primitives import RMSNorm, SiTUGLU, situ_glu_activation
 
@@ -143,7 +144,7 @@ class TopKRouter(nn.Module):
     def __init__(self, config: StableLatentMoEConfig):
         super().__init__()
         self.config = config
-        self.projection = nn.Linear(config.d_model, config.num_routed_experts, bias=config.router_bias)
+        self.projection = Linear(config.d_model, config.num_routed_experts, bias=config.router_bias)
         self.register_buffer("routing_bias", torch.zeros(config.num_routed_experts))
         nn.init.normal_(self.projection.weight, mean=0.0, std=config.init_std)
         if self.projection.bias is not None:
@@ -401,14 +402,14 @@ class StableLatentMoE(nn.Module):
         self.shared_experts = nn.ModuleList(
             SharedExpert(c.d_model, c.shared_expert_hidden_dim, c.beta_gate, c.beta_up, c.expert_bias, c.init_std)
             for _ in range(c.num_shared_experts))
-        self.down_projection = nn.Linear(c.d_model, c.latent_dim, bias=c.projection_bias)
+        self.down_projection = Linear(c.d_model, c.latent_dim, bias=c.projection_bias)
         self.router = TopKRouter(c)
         if c.expert_bias:
             raise ValueError("biased routed experts are not supported by the grouped expert layout")
         self.routed_experts = GroupedRoutedExperts(c.num_routed_experts, c.latent_dim, c.routed_expert_hidden_dim,
                                                    c.beta_gate, c.beta_up, c.init_std)
         self.routed_aggregate_norm = RMSNorm(c.latent_dim, eps=c.norm_eps)
-        self.up_projection = nn.Linear(c.latent_dim, c.d_model, bias=c.projection_bias)
+        self.up_projection = Linear(c.latent_dim, c.d_model, bias=c.projection_bias)
         self.exact_balancer = (ExactQuantileBalancer(c.num_routed_experts, c.top_k)
                                if c.enable_quantile_balancing else None)
         self.histogram_balancer = (HistogramQuantileBalancer(c.num_routed_experts, c.top_k, c.histogram_num_bins,

@@ -23,6 +23,7 @@ from .attnres import AttentionResidualConfig
 from .backbone import (CANONICAL_ATTENTION_PATTERN, HybridAttentionBackbone, HybridBackboneConfig,
                        HybridBackboneOutput)
 from .kda import KDAConfig
+from .linear import Linear
 from .losses import MultiTokenPredictionLoss
 from .mla import GatedMLAConfig
 from .moe import StableLatentMoEConfig
@@ -166,7 +167,7 @@ class KimiMTPFusion(nn.Module):
         self.d_model = d_model
         self.hidden_norm = RMSNorm(d_model, eps=eps)
         self.future_embedding_norm = RMSNorm(d_model, eps=eps)
-        self.projection = nn.Linear(2 * d_model, d_model, bias=False)
+        self.projection = Linear(2 * d_model, d_model, bias=False)
         nn.init.normal_(self.projection.weight, mean=0.0, std=init_std)
 
     def forward(self, source_hidden, future_embeddings):

@@ -21,6 +21,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from .. import ops as _ops
+from .linear import Linear
 
 
 # --------------------------------------------------------------------------- states
@@ -204,9 +205,9 @@ class SiTUGLU(nn.Module):
         self.beta_gate, self.beta_up = float(beta_gate), float(beta_up)
         output_bias = bias if output_bias is None else output_bias
         kw = {"device": device, "dtype": dtype}
-        self.gate_proj = nn.Linear(d_model, hidden_dim, bias=bias, **kw)
-        self.up_proj = nn.Linear(d_model, hidden_dim, bias=bias, **kw)
-        self.down_proj = nn.Linear(hidden_dim, d_model, bias=output_bias, **kw)
+        self.gate_proj = Linear(d_model, hidden_dim, bias=bias, **kw)
+        self.up_proj = Linear(d_model, hidden_dim, bias=bias, **kw)
+        self.down_proj = Linear(hidden_dim, d_model, bias=output_bias, **kw)
         self.init_std = float(init_std)
         self.reset_parameters()
 
@@ -236,8 +237,8 @@ class FullRankOutputGate(nn.Module):
         # value_width < d_model only for a tensor-parallel shard owning a subset of the heads
         self.d_model, self.value_width, self.init_std = d_model, value_width, float(init_std)
         kw = {"device": device, "dtype": dtype}
-        self.gate_proj = nn.Linear(d_model, value_width, bias=bias, **kw)
-        self.output_proj = nn.Linear(value_width, d_model, bias=output_bias, **kw)
+        self.gate_proj = Linear(d_model, value_width, bias=bias, **kw)
+        self.output_proj = Linear(value_width, d_model, bias=output_bias, **kw)
         self.reset_parameters()
 
     def reset_parameters(self) -> None:

@@ -25,6 +25,88 @@ def _act_dtype(x: torch.Tensor) -> torch.dtype:
     return x.dtype
 
 
+# --------------------------------------------------------------------------- projections
+def _tma_rows(t: torch.Tensor) -> torch.Tensor:
+    """``t`` as a row-major matrix whose rows start on 16-byte boundaries (copy only when needed)."""
+    if t.stride(-1) != 1 or (t.stride(0) * t.element_size()) % 16 or t.data_ptr() % 16 or t.stride(0) < t.shape[1]:
+        t = t.contiguous()
+    return t
+
+
+def gemm_tiles(n: int) -> int:
+    """Output columns per tile for an ``n``-wide product: 256 when it divides the width well."""
+    return 256 if n >= 1280 or n % 256 == 0 else 128
+
+
+def wgrad_splits(rows: int, cols: int, k: int, bn: int, sms: int = 148) -> int:
+    """K slices of a weight-gradient product ``[rows, cols]`` with reduction length ``k``, so that
+    about two work units per SM exist while every slice keeps at least four 64-wide K blocks."""
+    tiles = -(-rows // 128) * -(-cols // bn)
+    want = max(1, -(-2 * sms // tiles))
+    return int(max(1, min(want, 16, max(1, (k // 64) // 4))))
+
+
+class _Linear(torch.autograd.Function):
+    """``y = x W^T (+ b)`` on the tcgen05 GEMM with bf16 operands and fp32 accumulation.
+
+    Forward reads the weight's persistent bf16 mirror (``ops.mirror``) and adds the bias in the
+    epilogue.  Backward: ``dX = dY W`` (the mirror read MN-major, no transpose copy) and
+    ``dW = dY^T X`` written in fp32 by split-K work units that add their slices into one zeroed
+    buffer, so the fp32 master's gradient needs no cast.  Reference: ``nn.Linear`` under bf16
+    autocast (``src/kda/projections.py:164-215``, ``src/mla/latent_kv.py:22-79``,
+    ``src/kimi_primitives/output_gate.py:9-74``, ``src/stable_latent_moe/module.py:198-230``).
+    """
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, wb):
+        shape = x.shape
+        k, n = shape[-1], wb.shape[0]
+        x2 = x.reshape(-1, k)
+        if x2.dtype != torch.bfloat16:
+            x2 = x2.to(torch.bfloat16)
+        x2 = _tma_rows(x2)
+        y = _C().tc_gemm_dense(x2, wb, False, False, False, gemm_tiles(n), None, bias=bias)
+        ctx.save_for_backward(x2, wb)
+        ctx.meta = (shape, x.dtype, bias is not None)
+        return y.view(*shape[:-1], n) if y.is_contiguous() else y.reshape(*shape[:-1], n)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, wb = ctx.saved_tensors
+        shape, xdt, has_bias = ctx.meta
+        n, k = wb.shape
+        dy2 = dy.reshape(-1, n)
+        if dy2.dtype != torch.bfloat16:
+            dy2 = dy2.to(torch.bfloat16)
+        dy2 = _tma_rows(dy2)
+        C = _C()
+        dx = dw = db = None
+        if ctx.needs_input_grad[0]:
+            dx = C.tc_gemm_dense(dy2, wb, False, True, xdt == torch.float32, gemm_tiles(k), None)
+            dx = dx.reshape(shape)
+        if ctx.needs_input_grad[1]:
+            bn = gemm_tiles(k)
+            dw = torch.zeros(n, k, device=dy.device, dtype=torch.float32)
+            C.tc_gemm_dense(dy2, x2, True, True, True, bn, dw, accumulate=True,
+                            ksplit=wgrad_splits(n, k, dy2.shape[0], bn))
+        if has_bias and ctx.needs_input_grad[2]:
+            db = dy2.float().sum(0)
+        return dx, dw, db, None
+
+
+def linear_supported(x: torch.Tensor, weight: torch.Tensor) -> bool:
+    """The tcgen05 path applies: bf16 compute (autocast or bf16 input), widths multiples of 8."""
+    if _act_dtype(x) != torch.bfloat16 or weight.ndim != 2:
+        return False
+    return x.shape[-1] % 8 == 0 and weight.shape[1] == x.shape[-1] and x.numel() > 0
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """``x @ weight^T + bias`` with bf16 operands on the tcgen05 GEMM (see :class:`_Linear`)."""
+    from .mirror import bf16_weight
+    return _Linear.apply(x, weight, bias, bf16_weight(weight))
+
+
 # --------------------------------------------------------------------------- RMSNorm
 class _RMSNorm(torch.autograd.Function):
     @staticmethod
@@ -351,7 +433,8 @@ class _MoEGrouped(torch.autograd.Function):
         r_max = m * k + e * 128
         bf = torch.bfloat16
         x = latent.to(bf).contiguous()
-        wg, wu, wd = (w.to(bf).contiguous() for w in (gate_w, up_w, down_w))
+        from .mirror import bf16_weight
+        wg, wu, wd = (bf16_weight(w).contiguous() for w in (gate_w, up_w, down_w))
         _, offsets, row_token, row_weight, row_of = C.moe_route(selected.contiguous(), weights.detach(), e, r_max)
         xs = C.moe_gather(x, row_token)
         hh, gg, uu = C.tc_gemm_grouped(1, xs, wg, wu, False, False, offsets, r_max, h, l, 1, None, False, bg, bu,
@@ -435,7 +518,8 @@ class _LinearCE(torch.autograd.Function):
     def forward(ctx, h, w, targets, valid, chunk_rows):
         n, d = h.shape
         v = w.shape[0]
-        wd = w.to(torch.bfloat16).contiguous()
+        from .mirror import bf16_weight
+        wd = bf16_weight(w).contiguous()
         vpad = (v + 63) // 64 * 64
         loss = torch.zeros((), device=h.device, dtype=torch.float32)
         dh = torch.empty_like(h)
@@ -473,7 +557,7 @@ def linear_cross_entropy(hidden, weight, targets, valid, chunk_rows: int = 16384
 
 
 __all__ = [
-    "rms_norm", "situ_glu", "sigmoid_mul", "kda_decay", "conv_silu_norm", "kda_chunk", "kda_decode_step",
+    "linear", "linear_supported", "gemm_tiles", "wgrad_splits", "rms_norm", "situ_glu", "sigmoid_mul", "kda_decay", "conv_silu_norm", "kda_chunk", "kda_decode_step",
     "conv_silu_norm_step", "mla_decode_supported", "sample_tokens", "mark_seen",
     "flash_attention", "mla_absorbed_decode", "router_topk", "qb_histogram", "moe_grouped_experts",
     "attnres_mix", "linear_cross_entropy",

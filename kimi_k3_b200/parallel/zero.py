@@ -130,6 +130,9 @@ class ZeroDataParallel:
             self._broadcast_updates()
         if qk is not None:
             qk.apply(self.optimizer.step_number, materialize=False)
+        refresh = getattr(self.optimizer, "refresh_weight_mirror", None)
+        if refresh is not None:
+            refresh()  # the broadcasts and QK-Clip rewrote masters after the optimizer's own refresh
         return report
 
     def state_dict(self) -> dict:

@@ -241,6 +241,11 @@ class TrainStepEngine:
     def _graph_step(self, batch) -> StepOutput:
         self._resolve_pending()
         self.model.train()
+        mirror = getattr(self.optimizer, "weight_mirror", None)
+        if mirror is not None:
+            # a master changed outside the optimizer since the last step (checkpoint load, EMA
+            # swap): the replay reads the bf16 mirrors, so bring them up to date first
+            mirror.refresh_if_stale()
         if self._static_in is None:
             if hasattr(self.optimizer, "use_device_lrs"):
                 self.optimizer.use_device_lrs()

@@ -759,8 +759,11 @@ def _all_finite(tensors) -> torch.Tensor:
 class KimiHybridOptimizer:
     """Muon (matrices) + AdamW (rest) + QK-Clip; a non-finite gradient skips the whole step."""
 
-    def __init__(self, muon, adamw, report, config, qk_clip):
+    def __init__(self, muon, adamw, report, config, qk_clip, mirror=None):
         self.muon, self.adamw, self.report, self.config, self.qk_clip = muon, adamw, report, config, qk_clip
+        # bf16 copies of the projection weights read by the tensor-core GEMMs; rewritten (one
+        # launch) at the end of every step, after Muon, AdamW and QK-Clip have written the masters
+        self.weight_mirror = mirror
         self.step_number = 0
         self.last_step_report: OptimizerStepReport | None = None
         self.last_skip: torch.Tensor | None = None
@@ -804,6 +807,7 @@ class KimiHybridOptimizer:
             self.step_number += 1
             if self.qk_clip is not None:
                 self.qk_clip.apply(self.step_number, materialize=False, skip=skip)
+            self.refresh_weight_mirror()
             self.last_skip = skip
             rep = OptimizerStepReport(True, self.adamw.param_groups[0]["lr"], self.muon.param_groups[0]["lr"], False,
                                       0, 0, {})
@@ -822,10 +826,18 @@ class KimiHybridOptimizer:
         self.step_number += 1
         if self.qk_clip is not None:
             self.qk_clip.apply(self.step_number, materialize=False)
+        self.refresh_weight_mirror()
         rep = OptimizerStepReport(True, self.adamw.param_groups[0]["lr"], self.muon.param_groups[0]["lr"], False, 0,
                                   0, {})
         self.last_step_report = rep
         return rep
+
+    def refresh_weight_mirror(self) -> None:
+        """Rewrite the bf16 weight mirrors from the fp32 masters (stream-ordered, one launch).  The
+        optimizer calls it after every update; sharded data parallelism calls it again after the
+        owners' broadcasts."""
+        if self.weight_mirror is not None:
+            self.weight_mirror.refresh()
 
     def restrict_to(self, param_ids) -> None:
         """Update only ``param_ids`` (sharded data parallelism): Muon keeps state for its owned
@@ -941,12 +953,32 @@ def build_kimi_optimizer(model, config: KimiOptimizerConfig | None = None):
                            every_steps=config.qk_clip_every_steps,
                            include_kda_experimental=config.qk_clip_kda_experimental)
           if config.qk_clip_enabled else None)
-    return KimiHybridOptimizer(muon, adamw, reg, config, qk), reg
+    return KimiHybridOptimizer(muon, adamw, reg, config, qk, mirror=build_weight_mirror(model)), reg
+
+
+def build_weight_mirror(model):
+    """bf16 mirrors of the model's projection weights (every ``nn.Linear`` weight and the stacked
+    routed-expert matrices) when they live on CUDA and the native kernels are enabled; else None."""
+    from .. import ops
+    from ..ops.mirror import WeightMirror
+    weights, seen = [], set()
+    for mod in model.modules():
+        cands = []
+        if isinstance(mod, nn.Linear):
+            cands.append(mod.weight)
+        cands.extend(p for _, p in mod.named_parameters(recurse=False) if p.ndim == 3)
+        for p in cands:
+            if id(p) not in seen and p.is_cuda and p.dtype == torch.float32:
+                seen.add(id(p))
+                weights.append(p)
+    if not weights or not ops.use_kernels(weights[0]):
+        return None
+    return WeightMirror(weights)
 
 
 __all__ = [
     "KimiOptimizerConfig", "zeropower_via_newton_schulz", "batched_newton_schulz", "match_update_rms",
     "HeadMatrixLayout", "split_head_matrix", "merge_head_matrix", "per_head_orthogonalize", "MatrixParameterSpec",
     "ParameterAssignmentReport", "build_parameter_registry", "KimiMuon", "QKClipReport", "QKClipController",
-    "OptimizerStepReport", "KimiHybridOptimizer", "build_kimi_optimizer",
+    "OptimizerStepReport", "KimiHybridOptimizer", "build_kimi_optimizer", "build_weight_mirror",
 ]
