@@ -19,10 +19,9 @@ from typing import Any
 
 import torch
 
-from .cache import cache_summary
 from .config import GenerationConfig
 from .sampling import sample_next_token
-from .tokenization import decode_token_ids, encode_prompt, tokenizer_token_id
+from .session import cache_summary, decode_token_ids, encode_prompt, tokenizer_token_id
 
 
 @dataclass

@@ -33,7 +33,7 @@ from ..models.kda import KDAState
 from ..models.mla import MLACache, StaticMLACache
 from ..models.primitives import ShortConvState
 from ..runtime import sync_free
-from .cache import cache_summary
+from .session import cache_summary
 from .config import GenerationConfig
 from .generation import GenerationOutput, last_prompt_logits
 from .sampling import sample_next_token

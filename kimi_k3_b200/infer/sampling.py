@@ -3,7 +3,9 @@
 Parity: ``inference/sampling.py:10-91`` (reference): repetition penalty (divide positive,
 multiply negative logits of seen tokens), top-k, top-p (keep the smallest prefix whose mass
 reaches p, always the top token), temperature, seeded multinomial, NaN-safe argmax; an
-all-invalid distribution falls back to argmax.
+all-invalid distribution falls back to argmax.  Both filters here cut at a per-row logit
+threshold, so tokens tied with the last kept one are all kept (as in the fused device sampler);
+the reference's cut among equal values depends on its sort order.
 
 The reference's repetition penalty loops over rows in Python with ``torch.unique``; here it
 is one scatter over a ``[B, V]`` seen-mask. The validity fallback is decided on the device
@@ -28,21 +30,28 @@ def apply_repetition_penalty(logits: torch.Tensor, token_ids: torch.Tensor, pena
 
 
 def top_k_filter(logits: torch.Tensor, top_k: int | None) -> torch.Tensor:
-    if top_k is None or top_k >= logits.shape[-1]:
+    """Keep the logits at or above each row's k-th largest value (ties with it are kept)."""
+    v = logits.shape[-1]
+    if top_k is None or top_k >= v:
         return logits
-    cutoff = torch.topk(logits, int(top_k), dim=-1).values[..., -1, None]
-    return logits.masked_fill(logits < cutoff, float("-inf"))
+    # the k-th largest is the (v - k + 1)-th smallest
+    threshold = torch.kthvalue(logits, v - int(top_k) + 1, dim=-1, keepdim=True).values
+    return torch.where(logits >= threshold, logits, torch.full_like(logits, float("-inf")))
 
 
 def top_p_filter(logits: torch.Tensor, top_p: float | None) -> torch.Tensor:
+    """Nucleus filter: a token survives when the probability mass strictly ahead of it (in
+    descending order) is at most ``top_p``, so the top token always survives and the kept set is
+    the shortest prefix whose mass reaches ``top_p``.  Applied as a per-row logit threshold (the
+    smallest surviving logit), which also keeps ties with the last surviving token."""
     if top_p is None or top_p >= 1:
         return logits
-    srt, idx = torch.sort(logits, descending=True, dim=-1)
-    cum = torch.softmax(srt, dim=-1).cumsum(dim=-1)
-    drop = cum > top_p
-    drop[..., 1:] = drop[..., :-1].clone()
-    drop[..., 0] = False
-    return torch.empty_like(logits).scatter(-1, idx, srt.masked_fill(drop, float("-inf")))
+    ordered = logits.sort(dim=-1, descending=True).values
+    p = torch.softmax(ordered, dim=-1)
+    mass_ahead = p.cumsum(dim=-1) - p
+    survivors = (mass_ahead <= top_p).sum(dim=-1, keepdim=True).clamp_min(1)
+    threshold = ordered.gather(-1, survivors - 1)
+    return torch.where(logits >= threshold, logits, torch.full_like(logits, float("-inf")))
 
 
 def safe_argmax(logits: torch.Tensor) -> torch.Tensor:
