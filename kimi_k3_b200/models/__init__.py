@@ -4,6 +4,7 @@ from .backbone import *  # noqa: F401,F403
 from .kda import *  # noqa: F401,F403
 from .kimi_k3 import *  # noqa: F401,F403
 from .losses import *  # noqa: F401,F403
+from .posttrain import *  # noqa: F401,F403
 from .mla import *  # noqa: F401,F403
 from .moe import *  # noqa: F401,F403
 from .mtp import *  # noqa: F401,F403

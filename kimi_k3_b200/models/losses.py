@@ -1,13 +1,12 @@
-"""Token losses: NTP, MTP, pretraining composite, SFT, Kimi policy loss, MOPD.
+"""Token losses: NTP, MTP and the pretraining composite, with the shared token helpers.
 
 Parity targets (reference paths):
   * ``src/loss/common/reduction.py:10-51``, ``common/validation.py:14-127``
   * ``src/loss/pretraining/cross_entropy.py:13-57``, ``next_token_loss.py``
   * ``src/loss/multi_token_prediction_loss.py:18-105``
   * ``src/loss/pretraining/composite.py:12-77``  (NTP + lambda * MTP, no router loss)
-  * ``src/loss/sft_loss.py:22-157``, ``policy_optimization_loss.py:17-176``,
-    ``mopd_loss.py:21-216``, ``rl/reward_processing.py``, ``distillation/components.py``
-  * ``src/loss/training_objective.py:66-118``, ``common/config.py``
+  (the post-training objectives -- SFT, the Kimi policy loss, MOPD, rewards and the per-phase
+  dispatcher -- live in ``posttrain.py``)
 
 Label alignment: the reference's datasets emit pre-shifted labels and its NTP
 loss applies a causal shift again, so logits[t] train against x[t+2].
@@ -459,422 +458,6 @@ class KimiPretrainingLoss(nn.Module):
                if mtp_hidden is not None else None)
         total = ntp.loss if mtp is None else ntp.loss + self.lambda_mtp * mtp.loss
         return KimiPretrainingLossOutput(total, ntp, mtp, self.lambda_mtp)
-
-
-# --------------------------------------------------------------------------- SFT / RL / MOPD
-class SFTTrajectoryCrossEntropyLoss(nn.Module):
-    """Assistant-token CE over trajectories (token- or sequence-mean)."""
-
-    def __init__(self, *, ignore_index=-100, alignment="causal_shift", reduction="token_mean",
-                 zero_valid_policy="raise"):
-        super().__init__()
-        if alignment not in ("causal_shift", "already_aligned") or reduction not in ("token_mean", "sequence_mean"):
-            raise ValueError("unsupported SFT alignment or reduction")
-        self.ignore_index, self.alignment, self.reduction = ignore_index, alignment, reduction
-        self.zero_valid_policy = validate_zero_policy(zero_valid_policy)
-
-    def forward(self, logits, labels, *, assistant_mask, attention_mask=None, component_ids=None,
-                component_weights=None, boundary_mask=None, sample_weights=None,
-                return_per_component=False) -> SFTLossOutput:
-        if assistant_mask.shape != labels.shape:
-            raise ValueError("assistant_mask must match labels")
-        amask = assistant_mask.to(torch.bool)
-        weights = torch.ones_like(labels, dtype=torch.float32)
-        if component_ids is not None:
-            if component_ids.shape != labels.shape:
-                raise ValueError("component_ids must match labels")
-            weights = resolve_component_weights(component_ids, component_weights)
-            amask = amask & component_ids.ne(0)
-        elif component_weights is not None:
-            raise ValueError("component_weights require component_ids")
-        sl, al, valid, aw = align_token_inputs(logits, labels, alignment=self.alignment,
-                                               attention_mask=attention_mask, loss_mask=amask,
-                                               boundary_mask=boundary_mask, token_weights=weights,
-                                               ignore_index=self.ignore_index)
-        validate_token_ids(al, valid, logits.shape[-1])
-        safe = al.masked_fill(~valid, 0).long()
-        per = F.cross_entropy(logits[:, sl].float().reshape(-1, logits.shape[-1]), safe.reshape(-1),
-                              reduction="none").reshape_as(al)
-        if torch.any(valid & ~torch.isfinite(per)):
-            raise FloatingPointError("SFT cross-entropy produced non-finite values")
-        tw = aw * valid.float()
-        weighted = torch.where(valid, per * aw, torch.zeros_like(per))
-        count = valid.sum().float()
-        ps, pdn = weighted.sum(-1), tw.sum(-1)
-        if sample_weights is None:
-            samples = torch.ones(logits.shape[0], dtype=torch.float32, device=logits.device)
-        else:
-            if tuple(sample_weights.shape) != (logits.shape[0],):
-                raise ValueError("sample_weights must have shape [B]")
-            samples = sample_weights.float().to(logits.device)
-            if not torch.isfinite(samples).all() or torch.any(samples < 0):
-                raise ValueError("sample_weights must be finite and non-negative")
-        if self.reduction == "token_mean":
-            loss_sum = (weighted * samples[:, None]).sum()
-            normalizer = (tw * samples[:, None]).sum()
-        else:
-            active = pdn > 0
-            loss_sum = (ps / pdn.clamp_min(1) * samples * active).sum()
-            normalizer = (samples * active).sum()
-        if normalizer.item() == 0:
-            if self.zero_valid_policy == "raise":
-                raise ValueError("SFT batch contains no assistant targets")
-            loss = loss_sum = connected_zero(logits)
-        else:
-            loss = loss_sum / normalizer
-        csum = ccnt = None
-        if return_per_component:
-            if component_ids is None:
-                raise ValueError("component diagnostics require component_ids")
-            ac = component_ids[:, 1:] if self.alignment == "causal_shift" else component_ids
-            csum, ccnt = {}, {}
-            for ident in torch.unique(ac[valid]).tolist():
-                sel = valid & ac.eq(ident)
-                csum[int(ident)] = per[sel].sum().detach()
-                ccnt[int(ident)] = sel.sum().detach()
-        return SFTLossOutput(loss, loss_sum, normalizer.detach(), count.detach(), None, ps.detach(),
-                             valid.sum(-1).detach(), csum, ccnt, self.reduction)
-
-
-class KimiPolicyOptimizationLoss(nn.Module):
-    """``-clip(exp(delta), a, b) * A + tau * delta^2`` token-normalised (no critic)."""
-
-    def __init__(self, *, ratio_clip_min, ratio_clip_max, log_ratio_l2_coef, normalize_advantages=False,
-                 require_complete_groups=True, zero_valid_policy="raise"):
-        super().__init__()
-        if not 0 < ratio_clip_min <= ratio_clip_max:
-            raise ValueError("ratio bounds must satisfy 0 < min <= max")
-        if log_ratio_l2_coef < 0:
-            raise ValueError("log_ratio_l2_coef must be >= 0")
-        self.ratio_clip_min, self.ratio_clip_max = float(ratio_clip_min), float(ratio_clip_max)
-        self.log_ratio_l2_coef = float(log_ratio_l2_coef)
-        self.normalize_advantages, self.require_complete_groups = normalize_advantages, require_complete_groups
-        self.zero_valid_policy = validate_zero_policy(zero_valid_policy)
-
-    def forward(self, *, current_logprobs, old_logprobs, action_mask, rewards=None, prompt_group_ids=None,
-                advantages=None, sample_weights=None, expected_group_size=None) -> PolicyOptimizationLossOutput:
-        if current_logprobs.ndim != 2 or old_logprobs.shape != current_logprobs.shape:
-            raise ValueError("current_logprobs and old_logprobs must have shape [B,T]")
-        b, t = current_logprobs.shape
-        valid = boolean_mask("action_mask", action_mask, (b, t), current_logprobs.device)
-        reward_mode = rewards is not None or prompt_group_ids is not None
-        if reward_mode == (advantages is not None):
-            raise ValueError("provide exactly rewards+prompt_group_ids or explicit advantages")
-        mean_reward = reward_std = None
-        if reward_mode:
-            if rewards is None or prompt_group_ids is None:
-                raise ValueError("rewards and prompt_group_ids are required together")
-            adv = group_mean_advantages(rewards, prompt_group_ids, expected_group_size=expected_group_size,
-                                        require_complete_groups=self.require_complete_groups)
-            mean_reward, reward_std = rewards.detach().float().mean(), rewards.detach().float().std(unbiased=False)
-            tok_adv = adv[:, None].expand(b, t)
-        else:
-            if advantages.shape not in ((b,), (b, t)):
-                raise ValueError("advantages must have shape [B] or [B,T]")
-            tok_adv = (advantages[:, None].expand(b, t) if advantages.ndim == 1 else advantages).detach().float()
-        if self.normalize_advantages:
-            sel = tok_adv[valid]
-            if sel.numel():
-                tok_adv = (tok_adv - sel.mean()) / sel.std(unbiased=False).clamp_min(1e-6)
-        if sample_weights is None:
-            w = torch.ones((b, 1), device=current_logprobs.device)
-        else:
-            if tuple(sample_weights.shape) != (b,):
-                raise ValueError("sample_weights must have shape [B]")
-            w = sample_weights.detach().float()[:, None]
-            if not torch.isfinite(w).all() or torch.any(w < 0):
-                raise ValueError("sample_weights must be finite and non-negative")
-        normalizer = (valid.float() * w).sum(dtype=torch.float32)
-        cur, old = current_logprobs.float(), old_logprobs.detach().float()
-        require_finite("current_logprobs", cur, valid)
-        require_finite("old_logprobs", old, valid)
-        require_finite("advantages", tok_adv, valid)
-        lr = cur - old
-        lo, hi = math.log(self.ratio_clip_min), math.log(self.ratio_clip_max)
-        pterm = torch.exp(lr.clamp(lo, hi)) * tok_adv
-        rterm = self.log_ratio_l2_coef * lr.square()
-        psum = torch.where(valid, pterm * w, torch.zeros_like(pterm)).sum()
-        rsum = torch.where(valid, rterm * w, torch.zeros_like(rterm)).sum()
-        loss_sum = -psum + rsum
-        if normalizer.item() == 0:
-            if self.zero_valid_policy == "raise":
-                raise ValueError("RL batch contains no action tokens")
-            loss = loss_sum = connected_zero(current_logprobs)
-        else:
-            loss = loss_sum / normalizer
-        sr, sa = lr[valid], tok_adv[valid]
-        zero = cur.detach().new_zeros(())
-        clipped = valid & ((lr < lo) | (lr > hi))
-        return PolicyOptimizationLossOutput(
-            loss, loss_sum, normalizer.detach(), valid.sum().float().detach(), psum.detach(), rsum.detach(),
-            sa.mean().detach() if sa.numel() else zero, sr.mean().detach() if sr.numel() else zero,
-            sr.abs().max().detach() if sr.numel() else zero,
-            clipped[valid].float().mean().detach() if torch.any(valid) else zero,
-            None if mean_reward is None else mean_reward.detach(), None if reward_std is None else reward_std.detach())
-
-
-def validate_teacher_ids(teacher_ids, batch_size, device):
-    if teacher_ids.device != device:
-        raise ValueError("teacher_ids must share the student device")
-    if teacher_ids.dtype not in (torch.int32, torch.int64):
-        raise TypeError("teacher_ids must use int32 or int64")
-    if tuple(teacher_ids.shape) == (batch_size,):
-        if torch.any((teacher_ids < 0) | (teacher_ids >= 9)):
-            raise ValueError("flat teacher IDs must be in [0, 9)")
-        return
-    if tuple(teacher_ids.shape) == (batch_size, 2):
-        if torch.any((teacher_ids < 0) | (teacher_ids >= 3)):
-            raise ValueError("domain/effort IDs must each be in [0, 3)")
-        return
-    raise ValueError("teacher_ids must have shape [B] or [B,2]")
-
-
-def clipped_teacher_student_reward(teacher_logprobs, student_reference_logprobs, reward_clip_max):
-    raw = teacher_logprobs.detach().float() - student_reference_logprobs.detach().float()
-    return raw.clamp(-reward_clip_max, reward_clip_max).detach(), raw.abs() > reward_clip_max
-
-
-def corrected_topk_reverse_kl(teacher_logprobs, student_logprobs):
-    t, s = teacher_logprobs.detach().float(), student_logprobs.float()
-    sp = s.exp()
-    return (sp * (s - t) - sp + t.exp()).sum(-1)
-
-
-class MultiTeacherOnPolicyDistillationLoss(nn.Module):
-    """Multi-teacher on-policy distillation: sampled-token PG, Kimi-regularised, or corrected Top-k RKL."""
-
-    MODES = ("sampled_token_pg", "kimi_rl_regularized", "topk_reverse_kl")
-
-    def __init__(self, *, reward_clip_max, mode="sampled_token_pg", policy_loss=None, zero_valid_policy="raise"):
-        super().__init__()
-        if reward_clip_max <= 0:
-            raise ValueError("reward_clip_max must be > 0")
-        if mode not in self.MODES:
-            raise ValueError("unsupported MOPD mode")
-        if mode == "kimi_rl_regularized" and policy_loss is None:
-            raise ValueError("regularized MOPD requires KimiPolicyOptimizationLoss")
-        self.reward_clip_max, self.mode, self.policy_loss = float(reward_clip_max), mode, policy_loss
-        self.zero_valid_policy = validate_zero_policy(zero_valid_policy)
-
-    def forward(self, *, current_student_logprobs, teacher_sampled_token_logprobs, action_mask, teacher_ids,
-                student_logprobs_for_reward=None, old_student_logprobs=None, teacher_topk_token_ids=None,
-                teacher_topk_logprobs=None, student_topk_logprobs=None, sampled_token_ids=None,
-                teacher_sampled_token_ids=None) -> MOPDLossOutput:
-        if current_student_logprobs.ndim != 2:
-            raise ValueError("current_student_logprobs must have shape [B,T]")
-        b, t = current_student_logprobs.shape
-        dev = current_student_logprobs.device
-        valid = boolean_mask("action_mask", action_mask, (b, t), dev)
-        validate_teacher_ids(teacher_ids, b, dev)
-        if (sampled_token_ids is None) != (teacher_sampled_token_ids is None):
-            raise ValueError("both sampled-token metadata tensors are required")
-        if sampled_token_ids is not None and (tuple(sampled_token_ids.shape) != (b, t)
-                                              or tuple(teacher_sampled_token_ids.shape) != (b, t)
-                                              or torch.any(sampled_token_ids[valid] != teacher_sampled_token_ids[valid])):
-            raise ValueError("teacher/student tokenization metadata mismatch")
-        normalizer = valid.sum().float()
-        if normalizer.item() == 0 and self.zero_valid_policy == "raise":
-            raise ValueError("MOPD batch contains no sampled action tokens")
-        cur = current_student_logprobs.float()
-        require_finite("current_student_logprobs", cur, valid)
-        policy_output = None
-        if self.mode == "topk_reverse_kl":
-            if any(v is None for v in (teacher_topk_token_ids, teacher_topk_logprobs, student_topk_logprobs)):
-                raise ValueError("Top-k mode requires token IDs and both logprobs")
-            if (teacher_topk_token_ids.shape[:2] != (b, t) or teacher_topk_logprobs.shape != teacher_topk_token_ids.shape
-                    or student_topk_logprobs.shape != teacher_topk_token_ids.shape):
-                raise ValueError("Top-k tensors must have shape [B,T,K]")
-            srt = teacher_topk_token_ids.sort(-1).values
-            if torch.any(srt[..., 1:] == srt[..., :-1]):
-                raise ValueError("teacher Top-k token IDs must be unique per token")
-            per = corrected_topk_reverse_kl(teacher_topk_logprobs, student_topk_logprobs)
-            require_finite("topk_reverse_kl", per, valid)
-            loss_sum = torch.where(valid, per, torch.zeros_like(per)).sum()
-            loss = loss_sum / normalizer if normalizer.item() else connected_zero(student_topk_logprobs)
-            tv, sv = teacher_topk_logprobs.detach().float(), student_topk_logprobs.detach().float()
-            reward, clipped = torch.zeros_like(cur), torch.zeros_like(valid)
-            ref = "topk_distribution"
-            mt = tv.mean(-1)[valid].mean() if torch.any(valid) else tv.new_zeros(())
-            ms = sv.mean(-1)[valid].mean() if torch.any(valid) else sv.new_zeros(())
-        else:
-            if teacher_sampled_token_logprobs is None or tuple(teacher_sampled_token_logprobs.shape) != (b, t):
-                raise ValueError("sampled MOPD requires teacher logprobs [B,T]")
-            tv = teacher_sampled_token_logprobs.detach().float()
-            require_finite("teacher_logprobs", tv, valid)
-            if student_logprobs_for_reward is None:
-                sv, ref = cur.detach(), "current_detached"
-            else:
-                if tuple(student_logprobs_for_reward.shape) != (b, t):
-                    raise ValueError("stored student logprobs must have shape [B,T]")
-                sv, ref = student_logprobs_for_reward.detach().float(), "rollout_stored"
-            require_finite("student_reward_reference", sv, valid)
-            reward, clipped = clipped_teacher_student_reward(tv, sv, self.reward_clip_max)
-            if self.mode == "sampled_token_pg":
-                loss_sum = -torch.where(valid, reward * cur, torch.zeros_like(cur)).sum()
-                loss = loss_sum / normalizer if normalizer.item() else connected_zero(current_student_logprobs)
-            else:
-                if old_student_logprobs is None:
-                    raise ValueError("regularized MOPD requires old_student_logprobs")
-                policy_output = self.policy_loss(current_logprobs=current_student_logprobs,
-                                                 old_logprobs=old_student_logprobs, action_mask=valid,
-                                                 advantages=reward)
-                loss, loss_sum = policy_output.loss, policy_output.loss_sum
-            mt = tv[valid].mean() if torch.any(valid) else tv.new_zeros(())
-            ms = sv[valid].mean() if torch.any(valid) else sv.new_zeros(())
-        zero = cur.detach().new_zeros(())
-        return MOPDLossOutput(loss, loss_sum, normalizer.detach(), normalizer.detach(),
-                              reward[valid].mean().detach() if torch.any(valid) else zero,
-                              clipped[valid].float().mean().detach() if torch.any(valid) else zero,
-                              mt.detach(), ms.detach(), (mt - ms).detach(), normalizer.detach(), self.mode, ref,
-                              policy_output)
-
-
-class KimiRewardComposer:
-    """Explicitly weighted, detached sum of verifier / generative / task rewards."""
-
-    def __call__(self, *, verifier_reward, generative_reward, task_specific_reward, weights: RewardWeights):
-        sources = (("verifier", verifier_reward, weights.verifier), ("generative", generative_reward, weights.generative),
-                   ("task_specific", task_specific_reward, weights.task_specific))
-        present = [s for s in sources if s[1] is not None]
-        if not present:
-            raise ValueError("at least one reward source is required")
-        shape = present[0][1].shape
-        if len(shape) != 1:
-            raise ValueError("reward sources must have shape [B]")
-        out = torch.zeros_like(present[0][1], dtype=torch.float32)
-        for name, value, weight in sources:
-            if value is None:
-                if weight is not None:
-                    raise ValueError(f"{name} weight was supplied without its reward")
-                continue
-            if weight is None:
-                raise ValueError(f"{name} reward requires an explicit weight")
-            if value.shape != shape:
-                raise ValueError("all reward sources must share shape and device")
-            if not torch.isfinite(value).all():
-                raise FloatingPointError(f"{name} reward contains non-finite values")
-            out = out + float(weight) * value.detach().float()
-        return out.detach()
-
-
-def apply_reasoning_budget_override(reward, used_tokens, base_budget, budget_multiplier, penalty_reward=-1.0):
-    if reward.ndim != 1 or used_tokens.shape != reward.shape or base_budget.shape != reward.shape:
-        raise ValueError("reward, used_tokens and base_budget must have shape [B]")
-    if budget_multiplier <= 0:
-        raise ValueError("budget_multiplier must be > 0")
-    if torch.any(used_tokens < 0) or torch.any(base_budget < 0):
-        raise ValueError("token counts and budgets must be non-negative")
-    exceeded = used_tokens.float() > float(budget_multiplier) * base_budget.float()
-    return torch.where(exceeded, torch.full_like(reward.float(), float(penalty_reward)), reward.detach().float()).detach()
-
-
-def apply_verbosity_binary_rule(wins, output_length, initial_verbosity, sigma):
-    if wins.dtype != torch.bool:
-        raise TypeError("wins must be boolean")
-    if output_length.shape != wins.shape or initial_verbosity.shape != wins.shape:
-        raise ValueError("verbosity inputs must share shape")
-    if sigma <= 0:
-        raise ValueError("sigma must be > 0")
-    return (wins & ~(output_length.float() > sigma * initial_verbosity.float())).detach()
-
-
-# --------------------------------------------------------------------------- objective
-@dataclass(frozen=True)
-class KimiLossConfig:
-    ignore_index: int = -100
-    label_smoothing: float = 0.0
-    lambda_mtp: float = 0.0
-    sft_reduction: str = "token_mean"
-    rl_ratio_clip_min: float | None = None
-    rl_ratio_clip_max: float | None = None
-    rl_log_ratio_l2_coef: float | None = None
-    rl_normalize_advantages: bool = False
-    mopd_reward_clip_max: float | None = None
-    mopd_mode: str = "sampled_token_pg"
-    compute_loss_in_fp32: bool = True
-
-    def __post_init__(self) -> None:
-        if self.ignore_index >= 0:
-            raise ValueError("ignore_index must be outside the non-negative vocabulary")
-        if not 0.0 <= self.label_smoothing < 1.0 or self.lambda_mtp < 0:
-            raise ValueError("invalid label_smoothing or lambda_mtp")
-        if self.sft_reduction not in ("token_mean", "sequence_mean"):
-            raise ValueError("unsupported SFT reduction")
-        if self.rl_log_ratio_l2_coef is not None and self.rl_log_ratio_l2_coef < 0:
-            raise ValueError("rl_log_ratio_l2_coef must be >= 0")
-        if self.mopd_reward_clip_max is not None and self.mopd_reward_clip_max <= 0:
-            raise ValueError("mopd_reward_clip_max must be > 0")
-        if (self.rl_ratio_clip_min is None) != (self.rl_ratio_clip_max is None):
-            raise ValueError("both RL ratio bounds must be provided together")
-        if self.rl_ratio_clip_min is not None and not 0 < self.rl_ratio_clip_min <= self.rl_ratio_clip_max:
-            raise ValueError("RL ratio bounds must satisfy 0 < min <= max")
-        if self.mopd_mode not in MultiTeacherOnPolicyDistillationLoss.MODES:
-            raise ValueError("unsupported MOPD mode")
-        if not self.compute_loss_in_fp32:
-            raise ValueError("losses are computed in fp32")
-
-    def require_posttraining_values(self) -> None:
-        if any(v is None for v in (self.rl_ratio_clip_min, self.rl_ratio_clip_max, self.rl_log_ratio_l2_coef,
-                                   self.mopd_reward_clip_max)):
-            raise ValueError("RL and MOPD values must be provided explicitly before building post-training objectives")
-
-    def to_dict(self) -> dict:
-        return asdict(self)
-
-    @classmethod
-    def from_dict(cls, values: dict) -> "KimiLossConfig":
-        return cls(**values)
-
-
-_PHASE_KEYS = {
-    KimiTrainingPhase.PRETRAIN: {"logits", "labels", "attention_mask", "loss_mask", "boundary_mask", "token_weights",
-                                 "mtp_logits", "mtp_labels", "mtp_loss_mask", "future_offsets", "moe_diagnostics"},
-    KimiTrainingPhase.SFT: {"logits", "labels", "assistant_mask", "attention_mask", "component_ids",
-                            "component_weights", "boundary_mask", "sample_weights", "return_per_component"},
-    KimiTrainingPhase.RL: {"current_logprobs", "old_logprobs", "action_mask", "rewards", "prompt_group_ids",
-                           "advantages", "sample_weights", "expected_group_size"},
-    KimiTrainingPhase.MOPD: {"current_student_logprobs", "teacher_sampled_token_logprobs", "action_mask",
-                             "teacher_ids", "student_logprobs_for_reward", "old_student_logprobs",
-                             "teacher_topk_token_ids", "teacher_topk_logprobs", "student_topk_logprobs",
-                             "sampled_token_ids", "teacher_sampled_token_ids"},
-}
-
-
-class KimiTrainingObjective(nn.Module):
-    """Strict per-phase dispatcher; unknown keys for a phase raise."""
-
-    def __init__(self, config: KimiLossConfig):
-        super().__init__()
-        self.config = config
-        self.pretrain = KimiPretrainingLoss(lambda_mtp=config.lambda_mtp, ignore_index=config.ignore_index,
-                                            label_smoothing=config.label_smoothing)
-        self.sft = SFTTrajectoryCrossEntropyLoss(ignore_index=config.ignore_index, reduction=config.sft_reduction)
-        self.rl = self.mopd = None
-        if config.rl_ratio_clip_min is not None and config.rl_log_ratio_l2_coef is not None:
-            self.rl = KimiPolicyOptimizationLoss(ratio_clip_min=config.rl_ratio_clip_min,
-                                                 ratio_clip_max=config.rl_ratio_clip_max,
-                                                 log_ratio_l2_coef=config.rl_log_ratio_l2_coef,
-                                                 normalize_advantages=config.rl_normalize_advantages)
-        if config.mopd_reward_clip_max is not None:
-            self.mopd = MultiTeacherOnPolicyDistillationLoss(reward_clip_max=config.mopd_reward_clip_max,
-                                                             mode=config.mopd_mode, policy_loss=self.rl)
-
-    def forward(self, phase, **inputs) -> KimiLossBundle:
-        phase = KimiTrainingPhase(phase)
-        unknown = set(inputs) - _PHASE_KEYS[phase]
-        if unknown:
-            raise ValueError(f"unexpected inputs for phase {phase.value}: {sorted(unknown)}")
-        module = {KimiTrainingPhase.PRETRAIN: self.pretrain, KimiTrainingPhase.SFT: self.sft,
-                  KimiTrainingPhase.RL: self.rl, KimiTrainingPhase.MOPD: self.mopd}[phase]
-        if module is None:
-            self.config.require_posttraining_values()
-        if phase == KimiTrainingPhase.SFT:
-            out = module(inputs.pop("logits"), inputs.pop("labels"), **inputs)
-        elif phase == KimiTrainingPhase.PRETRAIN:
-            out = module(**inputs)
-        else:
-            out = module(**inputs)
-        return KimiLossBundle(phase, out.loss, out)
 
 
 __all__ = [n for n in dir() if not n.startswith("_") and n not in ("annotations", "math", "torch", "nn", "F")]
