@@ -468,7 +468,8 @@ static void check_tma_matrix(const at::Tensor& t, const char* name) {
 at::Tensor tc_gemm_dense(at::Tensor a, at::Tensor b, bool a_mn, bool b_mn, bool out_fp32, int64_t bn,
                          c10::optional<at::Tensor> out_opt, c10::optional<at::Tensor> status_opt,
                          int64_t spin_limit, bool accumulate, int64_t ksplit, c10::optional<at::Tensor> bias,
-                         c10::optional<at::Tensor> residual, int64_t pair, int64_t debug) {
+                         c10::optional<at::Tensor> residual, int64_t pair, int64_t debug,
+                         c10::optional<at::Tensor> dbg) {
   check_tma_matrix(a, "a");
   check_tma_matrix(b, "b");
   const at::cuda::CUDAGuard gd(a.device());
@@ -492,6 +493,10 @@ at::Tensor tc_gemm_dense(at::Tensor a, at::Tensor b, bool a_mn, bool b_mn, bool 
   g.ksplit = (int)std::max<int64_t>(1, ksplit);
   g.pair = (int)pair;
   g.debug = (int)debug;
+  if (dbg.has_value() && dbg->defined()) {
+    TORCH_CHECK(dbg->is_cuda() && dbg->scalar_type() == at::kLong && dbg->numel() >= 16, "dbg: int64 CUDA [16]");
+    g.dbg = reinterpret_cast<unsigned long long*>(dbg->data_ptr<int64_t>());
+  }
   at::Tensor bias_c, res_c;
   if (bias.has_value() && bias->defined()) {
     bias_c = bias->to(at::kFloat).contiguous();
@@ -537,6 +542,107 @@ at::Tensor tc_gemm_dense(at::Tensor a, at::Tensor b, bool a_mn, bool b_mn, bool 
   g.num_sms = at::cuda::getDeviceProperties(dev)->multiProcessorCount;
   check(kimi::tc_gemm(g, stream()), "tc_gemm_dense");
   return out;
+}
+
+// Fused projection group: several weights that read one input, as one GEMM over their concatenated
+// bf16 weight W_cat [N_total, K] (rows of consecutive segments).
+//   kind 1 (forward):      segs[s] (bf16 [M, N_s] outputs) <- x [M, K] W_cat^T
+//   kind 2 (input grad):   out [M, K] = sum_s segs[s] ([M, N_s] output grads) W_cat[rows of s]
+//   kind 3 (weight grads): out [N_total, K] fp32 += concat_s(segs[s])^T x   (split over `ksplit` K slices)
+// Segment widths must be multiples of 32 (kind 1) or 64 (kinds 2, 3) except the last; rows of every
+// tensor start on 16-byte boundaries.
+void tc_gemm_group(int64_t kind, std::vector<at::Tensor> segs, at::Tensor x, at::Tensor w,
+                   c10::optional<at::Tensor> out_opt, int64_t bn, int64_t ksplit, int64_t pair) {
+  TORCH_CHECK(kind >= 1 && kind <= 3, "kind must be 1, 2 or 3");
+  TORCH_CHECK(!segs.empty() && segs.size() <= 8, "1 to 8 segments");
+  const at::cuda::CUDAGuard gd(x.device());
+  kimi::TcGemmArgs g;
+  g.mode = 0;
+  g.bn = (int)bn;
+  g.pair = (int)pair;
+  g.seg_kind = (int)kind;
+  g.nseg = (int)segs.size();
+  int64_t total = 0;
+  for (size_t s = 0; s < segs.size(); ++s) {
+    check_tma_matrix(segs[s], "segment");
+    g.seg_ptr[s] = segs[s].data_ptr();
+    g.seg_width[s] = segs[s].size(1);
+    g.seg_ld[s] = segs[s].stride(0);
+    total += segs[s].size(1);
+  }
+  if (kind == 1) {  // A = x [M, K] K-major, B = W_cat [N, K] K-major
+    check_tma_matrix(x, "x");
+    check_tma_matrix(w, "w");
+    TORCH_CHECK(w.size(0) == total && w.size(1) == x.size(1), "W_cat must be [sum of widths, K]");
+    for (auto& t : segs) TORCH_CHECK(t.size(0) == x.size(0), "outputs must have the rows of x");
+    g.a = x.data_ptr();
+    g.a_rows = x.size(0);
+    g.a_cols = x.size(1);
+    g.a_ld = x.stride(0);
+    g.b = w.data_ptr();
+    g.b_rows = w.size(0);
+    g.b_cols = w.size(1);
+    g.b_ld = w.stride(0);
+    g.b_gstride = w.stride(0) * w.size(0);
+    g.M = (int)x.size(0);
+    g.N = (int)total;
+    g.K = (int)x.size(1);
+  } else if (kind == 2) {  // A = segments (K-major), B = W_cat given MN-major [N_total (k), K_in (n)]
+    TORCH_CHECK(out_opt.has_value() && out_opt->defined(), "kind 2 needs out [M, K_in]");
+    check_tma_matrix(w, "w");
+    const at::Tensor& out = *out_opt;
+    const int64_t M = segs[0].size(0);
+    for (auto& t : segs) TORCH_CHECK(t.size(0) == M, "segments must share their rows");
+    TORCH_CHECK(out.is_cuda() && out.dim() == 2 && out.size(0) == M && out.size(1) == w.size(1) && out.stride(1) == 1,
+                "out must be [M, K_in]");
+    TORCH_CHECK(total >= w.size(0), "segments must cover every row of W_cat");
+    g.a = segs[0].data_ptr();
+    g.a_rows = M;
+    g.a_cols = segs[0].size(1);
+    g.a_ld = segs[0].stride(0);
+    g.b_mn = true;
+    g.b = w.data_ptr();
+    g.b_rows = w.size(0);
+    g.b_cols = w.size(1);
+    g.b_ld = w.stride(0);
+    g.b_gstride = w.stride(0) * w.size(0);
+    g.M = (int)M;
+    g.N = (int)w.size(1);
+    g.K = (int)total;
+    g.out = out.data_ptr();
+    g.out_fp32 = out.scalar_type() == at::kFloat;
+    g.ldc = out.stride(0);
+  } else {  // A = segments given MN-major [tokens, N_s], B = x given MN-major [tokens, K_in]
+    TORCH_CHECK(out_opt.has_value() && out_opt->defined(), "kind 3 needs an fp32 out [N_total, K_in]");
+    check_tma_matrix(x, "x");
+    const at::Tensor& out = *out_opt;
+    const int64_t T = x.size(0);
+    for (auto& t : segs) TORCH_CHECK(t.size(0) == T, "segments must share the token rows of x");
+    TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.dim() == 2 && out.size(1) == x.size(1) &&
+                    out.stride(1) == 1 && out.stride(0) % 4 == 0 && out.size(0) <= total,
+                "out must be an fp32 [N_total, K_in] matrix");
+    g.a_mn = true;
+    g.a = segs[0].data_ptr();
+    g.a_rows = T;
+    g.a_cols = segs[0].size(1);
+    g.a_ld = segs[0].stride(0);
+    g.b_mn = true;
+    g.b = x.data_ptr();
+    g.b_rows = T;
+    g.b_cols = x.size(1);
+    g.b_ld = x.stride(0);
+    g.b_gstride = x.stride(0) * T;
+    g.M = (int)out.size(0);
+    g.N = (int)x.size(1);
+    g.K = (int)T;
+    g.out = out.data_ptr();
+    g.out_fp32 = true;
+    g.ldc = out.stride(0);
+    g.epi = 3;
+    g.ksplit = (int)std::max<int64_t>(1, ksplit);
+  }
+  g.num_sms = at::cuda::getDeviceProperties(x.get_device())->multiProcessorCount;
+  check(kimi::tc_gemm(g, stream()), "tc_gemm_group");
 }
 
 // Fused GEMM + cross-rank reduction (tensor parallelism): every rank computes its partial
@@ -1132,7 +1238,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tc_gemm_dense", &tc_gemm_dense, py::arg("a"), py::arg("b"), py::arg("a_mn"), py::arg("b_mn"),
         py::arg("out_fp32"), py::arg("bn"), py::arg("out") = py::none(), py::arg("status") = py::none(),
         py::arg("spin_limit") = 0, py::arg("accumulate") = false, py::arg("ksplit") = 1,
-        py::arg("bias") = py::none(), py::arg("residual") = py::none(), py::arg("pair") = -1, py::arg("debug") = 0);
+        py::arg("bias") = py::none(), py::arg("residual") = py::none(), py::arg("pair") = -1, py::arg("debug") = 0,
+        py::arg("dbg") = py::none());
   // Views of the current device's default status words of the GEMM and the KDA kernels (int32
   // [1] each, not owned): a training step copies them to pinned host memory with its other
   // per-step flags, so a bounded wait that gave up inside a kernel surfaces at the next step.
@@ -1150,6 +1257,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     return v;
   });
   m.def("tc_gemm_grouped", &tc_gemm_grouped);
+  m.def("tc_gemm_group", &tc_gemm_group, py::arg("kind"), py::arg("segs"), py::arg("x"), py::arg("w"),
+        py::arg("out") = py::none(), py::arg("bn") = 256, py::arg("ksplit") = 1, py::arg("pair") = -1);
   m.def("tc_gemm_comm", &tc_gemm_comm);
   m.def("tc_gemm_tiles", [](int64_t m, int64_t n, int64_t bn) { return kimi::tc_gemm_tiles((int)m, (int)n, (int)bn); });
   m.def("moe_route", &moe_route);

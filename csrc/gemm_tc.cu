@@ -46,6 +46,7 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 
 constexpr int kMaxRanks = 8;
+constexpr int kMaxSegs = 8;
 
 struct CommParams {
   int mode;                     // 0 off, 1 all-reduce, 2 reduce-scatter
@@ -64,6 +65,16 @@ struct DevParams {
   CUtensorMap map_a;
   CUtensorMap map_b;
   CUtensorMap map_b2;
+  CUtensorMap map_c;  // the output [M, N] (bf16: 32 x 32 boxes; fp32: 16 x 32), 64-byte swizzle
+  // Segmented operands of fused projection groups (several weights sharing one input):
+  //   kind 1: the output's columns [start[s], start[s+1]) go to seg_map[s] (forward, N = sum of widths)
+  //   kind 2: A's K range [start[s], start[s+1]) comes from seg_map[s] (input gradient dX = sum_s dY_s W_s)
+  //   kind 3: A's rows [start[s], start[s+1]) come from seg_map[s], A MN-major (weight gradients dY_s^T X)
+  // Boundaries are multiples of 32 (kind 1) or 64 (kinds 2, 3) except the last.
+  CUtensorMap seg_map[kMaxSegs];
+  int nseg, seg_kind;
+  int seg_start[kMaxSegs + 1];
+  int tma_store;      // epi 0 stores through shared memory + TMA (see the epilogue)
   // All-gather fused into the A operand (dense mode, A K-major, comm warps): every rank holds an
   // [M, K] gather buffer (symmetric) whose rows [r * ag_rows, (r + 1) * ag_rows) rank r fills with its
   // shard.  The comm warps copy each remote 128-row block from its owner's buffer into this rank's
@@ -95,7 +106,9 @@ struct DevParams {
   int* status;
   uint32_t spin_limit;  // polls per pipeline wait before it gives up (tests shorten it)
   int ksplit;           // dense mode: the K range is split into this many slices (epi 3 adds them up)
-  int debug;            // bit 0: skip the epilogue's global stores (timing experiments only)
+  int debug;            // bit 0: skip the epilogue's global stores; bit 1: role wait counters (experiments)
+  unsigned long long* dbg;  // bit 1: [0] MMA waits on full, [1] MMA waits on tempty, [2] producer waits on
+                            // empty, [3] epilogue waits on tfull, [4] MMA loop, [5] epilogue loop (cycles)
   const float* bias;    // epi 0: fp32 [N] added to every row (or null)
   const __nv_bfloat16* resid;  // epi 0, bf16 output: [M, ldr] added to the result (or null)
   int64_t ldr;
@@ -307,18 +320,42 @@ template <int BN>
 __device__ void comm_loop(const DevParams& p, int total);
 __device__ void ag_copy_loop(const DevParams& p);
 
+// Output staging of the TMA-store epilogue: 8 warps x 2 buffers x (32 rows x 64 bytes).
+constexpr int kStagingBytes = 8 * 2 * 2048;
+
 // Shared-memory ring depth: about 192 KB of stages whatever the tile shape.
 template <int BN, bool PAIR>
 constexpr int ring_stages() {
   return (192 * 1024) / (BM * BK * 2 + (PAIR ? BN / 2 : BN) * BK * 2);
 }
 
+// Segment holding coordinate `c` (the last one for coordinates past the end: its map reads zeros there).
+__device__ __forceinline__ int seg_of(const DevParams& p, int c) {
+  int s = 0;
+  while (s + 1 < p.nseg && c >= p.seg_start[s + 1]) ++s;
+  return s;
+}
+
+// debug bit 2: launch timeline (globaltimer ns) into dbg[8..15]: [8] earliest CTA start (min),
+// [9] latest CTA start, [10] latest end of set-up, [11] latest first stage seen by an MMA issuer,
+// [12] latest MMA loop end, [13] latest epilogue end, [14] latest CTA exit
+__device__ __forceinline__ void dbg_stamp(const DevParams& p, int slot, bool as_min) {
+  if (!(p.debug & 4)) return;
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  if (as_min)
+    atomicMin(p.dbg + slot, (unsigned long long)t);
+  else
+    atomicMax(p.dbg + slot, (unsigned long long)t);
+}
+
 template <int BN, bool A_MN, bool B_MN, int CM, bool PAIR>
 __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid_constant__ DevParams p) {
   // PAIR: two CTAs of a cluster compute one 256 x BN tile with tcgen05.mma.cta_group::2, issued by
-  // the even CTA.  Each CTA loads its 128 rows of A and its BN / 2 rows of B into its own shared
-  // memory (counted on the even CTA's `full` barrier), owns 128 rows of the accumulator in its own
-  // TMEM and stores them.  Halving each SM's share of B halves the B traffic per MMA, which keeps
+  // the even CTA.  Each CTA's shared memory holds its 128 rows of A and its BN / 2 rows of B; the even
+  // CTA's producer issues all four copies of a stage (the odd CTA's through shared::cluster
+  // addresses) against its own `full` barrier, so one commit per K block frees the stage.  Each CTA
+  // owns 128 rows of the accumulator in its own TMEM and stores them.  Halving each SM's share of B halves the B traffic per MMA, which keeps
   // the tensor pipe fed at N = 128 and takes a quarter off the L2 -> SMEM bytes at N = 256.
   constexpr int CTAS = PAIR ? 2 : 1;
   constexpr int BMT = BM * CTAS;           // output rows of a tile
@@ -331,7 +368,9 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
   static_assert(!PAIR || CM == 0, "CTA pairs run the plain (non-comm) kernel");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE);
+  // TMA-store staging: two 2 KB buffers per epilogue warp after the ring
+  uint8_t* staging = smem + STAGES * STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + kStagingBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -340,6 +379,10 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bnt = p.situ ? BN / 2 : BN;  // output columns per tile
   const uint32_t rank = PAIR ? tc::cluster_ctarank() : 0u;
+  if (threadIdx.x == 0) {
+    dbg_stamp(p, 8, true);
+    dbg_stamp(p, 9, false);
+  }
   const int first_unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
   const int unit_stride = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
@@ -369,16 +412,18 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
     tc::tma_prefetch(&p.map_a);
     tc::tma_prefetch(&p.map_b);
     if (p.situ || p.b2_k_split) tc::tma_prefetch(&p.map_b2);
+    if (p.tma_store) tc::tma_prefetch(&p.map_c);
   }
   tc::tc_fence_before();
   __syncthreads();
   if constexpr (PAIR) tc::cluster_sync();  // both CTAs' barriers are initialised before any remote use
   tc::tc_fence_after();
   const uint32_t tmem_base = *tslot;
+  if (threadIdx.x == 0) dbg_stamp(p, 10, false);
   const int total = p.situ ? total_tiles<BN / 2, BMT>(p) : total_tiles<BN, BMT>(p);
 
   if (warp == 0) {
-    if (lane == 0) {
+    if (lane == 0 && (!PAIR || rank == 0)) {
       // Roles leave their loops at the first failed wait (their own timeout, or another role's
       // or CTA's recorded in the status word).  On the way out the producer waits for the TMA
       // copies it has in flight, so no copy lands in shared memory after the CTA has exited.
@@ -386,16 +431,17 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
       uint32_t ph = 0;
       bool ok = true;
       uint32_t inflight = 0, inflight_ph = 0;  // stages filled since their last consumption, and their phase
-      uint64_t last_issue_ns = 0;
       uint32_t ag_target = 0u;
       if constexpr (CM == 3) ag_target = *p.ag_epoch + 1u;
       for (int tile = first_unit; ok && tile < total; tile += unit_stride) {
         const TileInfo ti = p.situ ? tile_info<BN / 2, BMT>(p, tile) : tile_info<BN, BMT>(p, tile);
         for (int kb = 0; kb < ti.num_kb; ++kb) {
+          const long long w0 = (p.debug & 2) ? clock64() : 0;
           if (!tc::mbar_wait(&empty[s], ph ^ 1, p.status, tc::kTimeoutEmpty, p.spin_limit)) {
             ok = false;
             break;
           }
+          if (p.debug & 2) atomicAdd(p.dbg + 2, (unsigned long long)(clock64() - w0));
           inflight &= ~(1u << s);
           uint8_t* sa = smem + s * STAGE;
           uint8_t* sb = sa + A_BYTES;
@@ -430,31 +476,58 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
             mb = &p.map_b2;
             kb_coord = k - p.b2_k_split;
           }
-          const int arow = ti.m0 + (int)rank * BM;  // this CTA's rows of the tile
           if constexpr (PAIR) {
-            // both CTAs' copies are counted on the even CTA's barrier, which expects them all
-            const uint32_t fb = tc::mapa_shared(&full[s], 0);
-            if (rank == 0) tc::mbar_arrive_expect_tx(&full[s], 2 * STAGE);
-            if (!A_MN) {
-              tc::tma_load_2d_pair(sa, &p.map_a, fb, k, arow);
-            } else {
-              tc::tma_load_2d_pair(sa, &p.map_a, fb, arow, k);
-              tc::tma_load_2d_pair(sa + A_BYTES / 2, &p.map_a, fb, arow + 64, k);
-            }
-            if (p.situ) {  // the even CTA holds the gate rows of the tile, the odd one the up rows
-              tc::tma_load_3d_pair(sb, rank == 0 ? &p.map_b : &p.map_b2, fb, kb_coord, ti.n0, ti.g);
-            } else if (!B_MN) {
-              tc::tma_load_3d_pair(sb, mb, fb, kb_coord, ti.n0 + (int)rank * BNL, 0);
-            } else {
+            // the leader fills the stage in both CTAs (its own rows, then the peer's through its
+            // shared::cluster address); every copy is counted on the leader's barrier
+            const uint32_t fb = tc::smem_u32(&full[s]);
+            tc::mbar_arrive_expect_tx(&full[s], 2 * STAGE);
 #pragma unroll
-              for (int q = 0; q < BNL / 64; ++q)
-                tc::tma_load_3d_pair(sb + q * (BK * 64 * 2), mb, fb, ti.n0 + (int)rank * BNL + q * 64, kb_coord, 0);
+            for (int r = 0; r < 2; ++r) {
+              const uint32_t da = r == 0 ? tc::smem_u32(sa) : tc::mapa_shared(sa, 1);
+              const uint32_t db = da + A_BYTES;
+              const int arow = ti.m0 + r * BM;
+              if (!A_MN) {
+                if (p.seg_kind == 2) {
+                  const int sg = seg_of(p, k);
+                  tc::tma_load_2d_pair_to(da, &p.seg_map[sg], fb, k - p.seg_start[sg], arow);
+                } else {
+                  tc::tma_load_2d_pair_to(da, &p.map_a, fb, k, arow);
+                }
+              } else if (p.seg_kind == 3) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const int mm = arow + 64 * h, sg = seg_of(p, mm);
+                  tc::tma_load_2d_pair_to(da + h * (A_BYTES / 2), &p.seg_map[sg], fb, mm - p.seg_start[sg], k);
+                }
+              } else {
+                tc::tma_load_2d_pair_to(da, &p.map_a, fb, arow, k);
+                tc::tma_load_2d_pair_to(da + A_BYTES / 2, &p.map_a, fb, arow + 64, k);
+              }
+              if (p.situ) {  // the even CTA holds the gate rows of the tile, the odd one the up rows
+                tc::tma_load_3d_pair_to(db, r == 0 ? &p.map_b : &p.map_b2, fb, kb_coord, ti.n0, ti.g);
+              } else if (!B_MN) {
+                tc::tma_load_3d_pair_to(db, mb, fb, kb_coord, ti.n0 + r * BNL, 0);
+              } else {
+#pragma unroll
+                for (int q = 0; q < BNL / 64; ++q)
+                  tc::tma_load_3d_pair_to(db + q * (BK * 64 * 2), mb, fb, ti.n0 + r * BNL + q * 64, kb_coord, 0);
+              }
             }
-            last_issue_ns = global_ns();
           } else {
             tc::mbar_arrive_expect_tx(&full[s], STAGE);
             if (!A_MN) {
-              tc::tma_load_2d(sa, &p.map_a, &full[s], k, ti.m0);
+              if (p.seg_kind == 2) {
+                const int sg = seg_of(p, k);
+                tc::tma_load_2d(sa, &p.seg_map[sg], &full[s], k - p.seg_start[sg], ti.m0);
+              } else {
+                tc::tma_load_2d(sa, &p.map_a, &full[s], k, ti.m0);
+              }
+            } else if (p.seg_kind == 3) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int mm = ti.m0 + 64 * h, sg = seg_of(p, mm);
+                tc::tma_load_2d(sa + h * (A_BYTES / 2), &p.seg_map[sg], &full[s], mm - p.seg_start[sg], k);
+              }
             } else {
               tc::tma_load_2d(sa, &p.map_a, &full[s], ti.m0, k);
               tc::tma_load_2d(sa + A_BYTES / 2, &p.map_a, &full[s], ti.m0 + 64, k);
@@ -479,59 +552,68 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
           }
         }
       }
-      if (!ok) {
-        if (!PAIR || rank == 0) {
-          for (int q = 0; q < STAGES; ++q)
-            if (inflight & (1u << q))
-              tc::mbar_wait_local(&full[q], (inflight_ph >> q) & 1u, p.status, tc::kTimeoutDrain, tc::kDrainNs);
-        } else if (inflight) {
-          // the odd CTA's copies are counted on the even CTA's barrier, which it cannot poll: give
-          // them a fixed 200 us (a 16 KB tile lands in a few microseconds) before leaving
-          while (global_ns() - last_issue_ns < 200000ull) __nanosleep(1000);
-        }
-      }
+      if (!ok)
+        for (int q = 0; q < STAGES; ++q)
+          if (inflight & (1u << q))
+            tc::mbar_wait_local(&full[q], (inflight_ph >> q) & 1u, p.status, tc::kTimeoutDrain, tc::kDrainNs);
     }
   } else if (warp == 1) {
     if (lane == 0 && (!PAIR || rank == 0)) {
       const uint32_t idesc = tc::instr_desc_f16(BMT, BN, true, A_MN, B_MN);
+      // Descriptors of stage 0 at K offset 0; a stage / K step only moves the 14-bit start-address
+      // field (16-byte units), so the loop adds small constants to precomputed 64-bit values.
+      const uint32_t ring0 = tc::smem_u32(smem);
+      const uint64_t adesc0 = A_MN ? tc::smem_desc_sw128(ring0, 8192, 1024) : tc::smem_desc_sw128(ring0, 16, 1024);
+      const uint64_t bdesc0 = B_MN ? tc::smem_desc_sw128(ring0 + A_BYTES, 8192, 1024)
+                                   : tc::smem_desc_sw128(ring0 + A_BYTES, 16, 1024);
+      constexpr uint64_t A_KSTEP = (A_MN ? 2048 : 32) >> 4, B_KSTEP = (B_MN ? 2048 : 32) >> 4;
+      constexpr uint64_t STAGE16 = STAGE >> 4;
+      // commit target: the stage's `empty` barrier of the producer that refills it
+      const uint32_t empty_c0 = PAIR ? tc::mapa_shared(&empty[0], 0) : tc::smem_u32(&empty[0]);
       int s = 0, it = 0;
       uint32_t ph = 0;
       bool ok = true, issued = false;
+      const long long t_mma = (p.debug & 2) ? clock64() : 0;
       for (int tile = first_unit; ok && tile < total; tile += unit_stride, ++it) {
-        const TileInfo ti = p.situ ? tile_info<BN / 2, BMT>(p, tile) : tile_info<BN, BMT>(p, tile);
+        const int num_kb = p.situ ? tile_info<BN / 2, BMT>(p, tile).num_kb : tile_info<BN, BMT>(p, tile).num_kb;
         const int buf = it & 1;
         const uint32_t tph = (it >> 1) & 1;
+        const long long w1 = (p.debug & 2) ? clock64() : 0;
         if (!tc::mbar_wait(&tempty[buf], tph ^ 1, p.status, tc::kTimeoutTmemEmpty, p.spin_limit)) {
           ok = false;
           break;
         }
+        if (p.debug & 2) atomicAdd(p.dbg + 1, (unsigned long long)(clock64() - w1));
         tc::tc_fence_after();
         const uint32_t d = tmem_base + buf * BN;
-        for (int kb = 0; kb < ti.num_kb; ++kb) {
+        uint32_t acc = 0;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (p.debug & 2) {
+            const long long w2 = clock64();
+            while (!tc::mbar_try_wait(&full[s], ph)) {}
+            atomicAdd(p.dbg + 0, (unsigned long long)(clock64() - w2));
+          }
           if (!tc::mbar_wait(&full[s], ph, p.status, tc::kTimeoutFull, p.spin_limit)) {
             ok = false;
             break;
           }
           tc::tc_fence_after();
-          const uint32_t base_a = tc::smem_u32(smem + s * STAGE);
-          const uint32_t base_b = base_a + A_BYTES;
+          if (!issued) dbg_stamp(p, 11, false);
+          const uint64_t soff = (uint64_t)s * STAGE16;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t ad = A_MN ? tc::smem_desc_sw128(base_a + kk * 2048, 8192, 1024)
-                                     : tc::smem_desc_sw128(base_a + kk * 32, 16, 1024);
-            const uint64_t bd = B_MN ? tc::smem_desc_sw128(base_b + kk * 2048, 8192, 1024)
-                                     : tc::smem_desc_sw128(base_b + kk * 32, 16, 1024);
+            const uint64_t ad = adesc0 + soff + kk * A_KSTEP, bd = bdesc0 + soff + kk * B_KSTEP;
             if constexpr (PAIR)
-              tc::mma_f16_pair(d, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+              tc::mma_f16_pair(d, ad, bd, idesc, acc);
             else
-              tc::mma_f16(d, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+              tc::mma_f16(d, ad, bd, idesc, acc);
+            acc = 1u;
           }
           issued = true;
-          if constexpr (PAIR) {  // the stage is free in both CTAs once these MMAs are done
-            tc::mma_commit_pair(tc::mapa_shared(&empty[s], 0));
-            tc::mma_commit_pair(tc::mapa_shared(&empty[s], 1));
+          if constexpr (PAIR) {  // the leader's producer refills both CTAs' halves of the stage
+            tc::mma_commit_pair(empty_c0 + 8u * s);
           } else {
-            tc::mma_commit(&empty[s]);
+            tc::mma_commit_addr(empty_c0 + 8u * s);
           }
           if (++s == STAGES) {
             s = 0;
@@ -546,6 +628,8 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
           tc::mma_commit(&tfull[buf]);
         }
       }
+      if (p.debug & 2) atomicAdd(p.dbg + 4, (unsigned long long)(clock64() - t_mma));
+      dbg_stamp(p, 12, false);
       if (!ok && issued) {
         // let every issued MMA finish before the CTA frees its TMEM and shared memory
         if constexpr (PAIR)
@@ -562,12 +646,45 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
     const float ibg = 1.f / p.bg, ibu = 1.f / p.bu;
     const uint32_t tempty_c0_0 = PAIR ? tc::mapa_shared(&tempty[0], 0) : 0u;
     const uint32_t tempty_c0_1 = PAIR ? tc::mapa_shared(&tempty[1], 0) : 0u;
+    // TMA-store epilogue: this warp's two staging buffers (32 rows x 64 bytes each, 64-byte swizzle)
+    // alternate between chunks; a buffer is rewritten only after the store issued from it two
+    // chunks earlier has finished reading it.
+    uint8_t* my_stage = staging + (warp - 2) * 2 * 2048;
+    uint32_t stores = 0;
+    // one 32-row x 64-byte chunk: row `lane` writes its 16-byte pieces at their swizzled slots
+    auto stage_and_store = [&](const uint4* pieces, int x, int y, bool reduce_add) {
+      uint8_t* b = my_stage + (stores & 1) * 2048;
+      if (lane == 0) tc::bulk_wait_read<1>();
+      __syncwarp();
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4*>(b + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4)) = pieces[c];
+      tc::fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        const CUtensorMap* map = &p.map_c;
+        if (p.seg_kind == 1) {  // a fused projection group: this chunk's columns belong to one output
+          const int sg = seg_of(p, x);
+          map = &p.seg_map[sg];
+          x -= p.seg_start[sg];
+        }
+        if (reduce_add)
+          tc::tma_reduce_add_2d(map, b, x, y);
+        else
+          tc::tma_store_2d(map, b, x, y);
+        tc::bulk_commit();
+      }
+      ++stores;
+    };
     int it = 0;
+    const long long t_epi = (p.debug & 2) ? clock64() : 0;
     for (int tile = first_unit; tile < total; tile += unit_stride, ++it) {
       const TileInfo ti = p.situ ? tile_info<BN / 2, BMT>(p, tile) : tile_info<BN, BMT>(p, tile);
       const int buf = it & 1;
       const uint32_t tph = (it >> 1) & 1;
-      bool ok = tc::mbar_wait(&tfull[buf], tph, p.status, tc::kTimeoutTmemFull, p.spin_limit);
+      const long long w3 = (p.debug & 2) ? clock64() : 0;
+      bool ok = tc::mbar_wait(&tfull[buf], tph, p.status, tc::kTimeoutTmemFull, p.spin_limit, 128);
+      if ((p.debug & 2) && lane == 0 && warp == 2) atomicAdd(p.dbg + 3, (unsigned long long)(clock64() - w3));
       if constexpr (CM == 1 || CM == 2) {
         // the comm epilogue meets at a named barrier per tile: leave together or not at all
         ok = !bar_red_or(1, 256, !ok);
@@ -643,6 +760,20 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
               }
             }
           }
+        } else if (p.epi == 3 && p.tma_store) {
+          // fp32 accumulation through shared memory and TMA reduce-add (whole warp; an empty K slice adds nothing)
+          if (ti.num_kb > 0) {
+            const int y = ti.c_row0 + (int)rank * BM + sub * 32;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              uint4 pieces[4];
+#pragma unroll
+              for (int c = 0; c < 4; ++c)
+                pieces[c] = make_uint4(__float_as_uint(v[h * 16 + 4 * c]), __float_as_uint(v[h * 16 + 4 * c + 1]),
+                                       __float_as_uint(v[h * 16 + 4 * c + 2]), __float_as_uint(v[h * 16 + 4 * c + 3]));
+              stage_and_store(pieces, col0 + h * 16, y, true);
+            }
+          }
         } else if (p.epi == 3) {
           // fp32 accumulation into `out` (split-K slices, or a gradient that already holds a value)
           if (row_ok && ti.num_kb > 0) {
@@ -659,6 +790,50 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
                   if (col0 + i + j < p.N) atomicAdd(o + col0 + i + j, v[i + j]);
               }
             }
+          }
+        } else if (p.tma_store) {
+          // the whole warp takes part (rows past the end are clipped by the TMA store)
+          if (p.bias) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i < p.N) v[i] += __ldg(p.bias + col0 + i);
+          }
+          const int y = ti.c_row0 + (int)rank * BM + sub * 32;
+          if (p.out_fp32) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              uint4 pieces[4];
+#pragma unroll
+              for (int c = 0; c < 4; ++c)
+                pieces[c] = make_uint4(__float_as_uint(v[h * 16 + 4 * c]), __float_as_uint(v[h * 16 + 4 * c + 1]),
+                                       __float_as_uint(v[h * 16 + 4 * c + 2]), __float_as_uint(v[h * 16 + 4 * c + 3]));
+              stage_and_store(pieces, col0 + h * 16, y, false);
+            }
+          } else {
+            if (p.resid && row_ok) {
+              const __nv_bfloat16* rr = p.resid + (int64_t)row * p.ldr;
+#pragma unroll
+              for (int i = 0; i < 32; i += 8) {
+                if (col0 + i + 8 <= p.N) {
+                  Vec<__nv_bfloat16> vr;
+                  vr.load(rr + col0 + i);
+#pragma unroll
+                  for (int j = 0; j < 8; ++j) v[i + j] += vr.f(j);
+                } else {
+                  for (int j = 0; j < 8; ++j)
+                    if (col0 + i + j < p.N) v[i + j] += to_f<__nv_bfloat16>(rr[col0 + i + j]);
+                }
+              }
+            }
+            uint4 pieces[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              Vec<__nv_bfloat16> o;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) o.v[j] = from_f<__nv_bfloat16>(v[8 * c + j]);
+              pieces[c] = *reinterpret_cast<const uint4*>(o.v);
+            }
+            stage_and_store(pieces, col0, y, false);
           }
         } else if (row_ok && !(p.debug & 1)) {
           const int64_t goff = p.mode == 2 ? (int64_t)ti.g * p.M * p.ldc : 0;
@@ -726,6 +901,11 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
         }
       }
     }
+    // the staging buffers are shared memory of this CTA: its stores must have read them before it exits
+    if (lane == 0 && stores) tc::bulk_wait_read<0>();
+    if ((p.debug & 2) && lane == 0 && warp == 2) atomicAdd(p.dbg + 5, (unsigned long long)(clock64() - t_epi));
+    if (lane == 0) dbg_stamp(p, 13, false);
+    __syncwarp();
   } else {
     if constexpr (CM == 3)
       ag_copy_loop(p);
@@ -741,6 +921,7 @@ __global__ void __launch_bounds__(CM ? 448 : 320, 1) gemm_tc_kernel(const __grid
       tc::tmem_dealloc_pair(tmem_base, TMEM_COLS);
     else
       tc::tmem_dealloc(tmem_base, TMEM_COLS);
+    if (lane == 0) dbg_stamp(p, 14, false);
   }
 }
 
@@ -889,6 +1070,21 @@ bool make_map_2d(CUtensorMap* m, const void* ptr, uint64_t d0, uint64_t d1, uint
   return r == CUDA_SUCCESS;
 }
 
+// Output map of the TMA-store epilogue: [rows, cols] with a row pitch of ld_bytes, boxes of 32 rows x 64
+// bytes (32 bf16 or 16 fp32 columns), 64-byte swizzle (the layout the epilogue writes into shared memory).
+bool make_store_map(CUtensorMap* m, void* ptr, uint64_t cols, uint64_t rows, uint64_t ld_bytes, bool fp32) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld_bytes};
+  cuuint32_t box[2] = {fp32 ? 16u : 32u, 32u};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ptr, dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 bool debug_on() {
   static const bool on = getenv("KIMI_K3_DEBUG") != nullptr;
   return on;
@@ -901,7 +1097,7 @@ cudaError_t launch(const DevParams& dp, int num_sms, cudaStream_t s) {
   if (debug_on() && stale != cudaSuccess) fprintf(stderr, "tc_gemm: stale error before launch: %s\n", cudaGetErrorString(stale));
   constexpr int STAGES = ring_stages<BN, PAIR>();
   constexpr int STAGE = BM * BK * 2 + (PAIR ? BN / 2 : BN) * BK * 2;
-  const size_t smem = 1024 + (size_t)STAGES * STAGE + (2 * STAGES + 5) * 8 + 16;
+  const size_t smem = 1024 + (size_t)STAGES * STAGE + kStagingBytes + (2 * STAGES + 5) * 8 + 16;
   auto kern = gemm_tc_kernel<BN, AMN, BMN, CM, PAIR>;
   constexpr int threads = CM ? 448 : 320;
   {
@@ -1042,6 +1238,8 @@ cudaError_t tc_gemm(const TcGemmArgs& a, cudaStream_t stream) {
   if (a.epi == 1 && (a.a_mn || a.b_mn || !a.b2)) return cudaErrorInvalidValue;
   dp.ksplit = a.ksplit > 1 ? a.ksplit : 1;
   dp.debug = a.debug;
+  dp.dbg = a.dbg;
+  if ((a.debug & 6) && !a.dbg) return cudaErrorInvalidValue;
   dp.bias = a.bias;
   dp.resid = reinterpret_cast<const __nv_bfloat16*>(a.resid);
   dp.ldr = a.ldr;
@@ -1080,6 +1278,62 @@ cudaError_t tc_gemm(const TcGemmArgs& a, cudaStream_t stream) {
       if (debug_on()) fprintf(stderr, "tc_gemm: B tensor map %d failed\n", i);
       return cudaErrorInvalidValue;
     }
+  }
+  if (a.seg_kind != 0) {
+    // fused projection group: one map per segment; boundaries (prefix sums of the widths) must be
+    // multiples of 32 (output columns) or 64 (A's K blocks / row boxes) except the last
+    if (a.mode != 0 || a.comm_mode != 0 || a.ag_world != 0 || a.nseg < 1 || a.nseg > kMaxSegs || a.bias || a.resid ||
+        a.epi == 1 || a.epi == 2 || (a.seg_kind == 1 && (a.epi != 0 || a.out_fp32)) ||
+        (a.seg_kind == 2 && a.a_mn) || (a.seg_kind == 3 && !a.a_mn) || a.seg_kind > 3)
+      return cudaErrorInvalidValue;
+    const int align = a.seg_kind == 1 ? 32 : 64;
+    dp.seg_kind = a.seg_kind;
+    dp.nseg = a.nseg;
+    dp.seg_start[0] = 0;
+    for (int s = 0; s < a.nseg; ++s) {
+      if (a.seg_width[s] <= 0 || !a.seg_ptr[s] || (reinterpret_cast<uintptr_t>(a.seg_ptr[s]) & 15) ||
+          (a.seg_ld[s] * 2) % 16 || a.seg_ld[s] < a.seg_width[s])
+        return cudaErrorInvalidValue;
+      if (s + 1 < a.nseg && (dp.seg_start[s] + a.seg_width[s]) % align) return cudaErrorInvalidValue;
+      dp.seg_start[s + 1] = dp.seg_start[s] + (int)a.seg_width[s];
+      bool ok;
+      if (a.seg_kind == 1) {
+        // the TMA clips the right edge in 16-byte units: a ragged (last) segment writes its row padding
+        // up to the next 8 columns, which its row stride must hold (those columns get zeros)
+        const int64_t cols = (a.seg_width[s] + 7) / 8 * 8;
+        ok = cols <= a.seg_ld[s] && make_store_map(&dp.seg_map[s], a.seg_ptr[s], (uint64_t)cols, (uint64_t)a.M,
+                                                   (uint64_t)(a.seg_ld[s] * 2), false);
+      }
+      else if (a.seg_kind == 2)
+        ok = make_map_2d(&dp.seg_map[s], a.seg_ptr[s], (uint64_t)a.seg_width[s], (uint64_t)a.M,
+                         (uint64_t)(a.seg_ld[s] * 2), 64, 128);
+      else
+        ok = make_map_2d(&dp.seg_map[s], a.seg_ptr[s], (uint64_t)a.seg_width[s], (uint64_t)a.K,
+                         (uint64_t)(a.seg_ld[s] * 2), 64, 64);
+      if (!ok) return cudaErrorInvalidValue;
+    }
+    const int total_w = dp.seg_start[a.nseg];
+    if ((a.seg_kind == 1 && total_w != a.N) || (a.seg_kind == 2 && total_w < a.K) || (a.seg_kind == 3 && total_w < a.M))
+      return cudaErrorInvalidValue;
+    if (a.seg_kind != 1) dp.map_a = dp.seg_map[0];  // map_a is prefetched; keep it a valid descriptor
+    if (a.seg_kind == 1) {
+      dp.map_c = dp.seg_map[0];
+      dp.tma_store = 1;
+    }
+  }
+  // Plain stores of dense / grouped-M products go through shared memory and TMA (full 32-byte
+  // sectors, one instruction per 32 x 32 chunk); comm modes keep direct stores, which they fence
+  // before signalling peers.
+  {
+    const size_t elt = a.out_fp32 ? 4 : 2;
+    const int64_t out_rows = a.mode == 1 ? a.a_rows : a.M;
+    if ((a.epi == 0 || (a.epi == 3 && a.out_fp32)) && (a.mode == 0 || a.mode == 1) && a.comm_mode == 0 &&
+        a.ag_world == 0 && !(a.debug & 1) &&
+        a.out && (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && (a.ldc * elt) % 16 == 0 && a.ldc >= a.N &&
+        (a.N * elt) % 16 == 0 &&  // the TMA clips the right edge in 16-byte units, not elements
+        out_rows > 0 && make_store_map(&dp.map_c, a.out, (uint64_t)a.N, (uint64_t)out_rows, (uint64_t)(a.ldc * elt),
+                                       a.out_fp32))
+      dp.tma_store = 1;
   }
   int sms = a.num_sms > 0 ? a.num_sms : device_sms();
   if (a.comm_mode != 0) {

@@ -75,11 +75,15 @@ constexpr uint64_t kDrainNs = 200000000ull;   // the exit path waiting for copie
 // Bounded pipeline wait: false after `limit` polls or kWaitNs (records `code` in *status, first
 // error wins), or as soon as *status is non-zero.  The clock and the status word are read every
 // 1024 polls.
+// `sleep_ns` > 0 backs off between polls: for waiters off the critical path (an epilogue waiting for
+// the next accumulator), so their polling does not take issue slots from the MMA or TMA threads.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code,
-                                          uint32_t limit = kSpinLimit) {
+                                          uint32_t limit = kSpinLimit, uint32_t sleep_ns = 0) {
+  if (mbar_try_wait(bar, parity)) return true;  // fast path: already complete
   uint64_t t0 = 0;
   for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if (sleep_ns) __nanosleep(sleep_ns);
     if (i + 1 >= limit) break;
     if ((i & 1023u) == 1023u) {
       if (status_peek(status) != 0) return false;
@@ -126,6 +130,30 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// TMA tile store from shared memory (bulk-group completion); out-of-range rows / columns of the box
+// are not written.  The smem tile must follow the map's swizzle; writers fence the async proxy first.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];\n" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(smem_u32(src))
+               : "memory");
+}
+// TMA tile reduce-add from shared memory into global memory (fp32 add in L2); same rules as the store.
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%1, %2}], [%3];\n" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(smem_u32(src))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+// Wait until at most N committed store groups still read shared memory (their source may be reused).
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;\n" ::"n"(N) : "memory");
+}
+// Wait until every committed store group has completed (its writes are visible).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
+
 // ---------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(slot)),
@@ -152,6 +180,11 @@ __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+// tcgen05.commit (one CTA) to a barrier given by its 32-bit shared-memory address.
+__device__ __forceinline__ void mma_commit_addr(uint32_t bar_addr) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar_addr)
+               : "memory");
 }
 // Arrive on `bar` once every previously issued tcgen05.mma of this thread has completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -224,6 +257,24 @@ __device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* m
   asm volatile(
       "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
       "%4}], [%5];\n" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar_cluster)
+      : "memory");
+}
+// Same loads with the destination given as a shared::cluster address: the leader CTA of a pair fills
+// its peer's half of a stage (still a single destination, no multicast).
+__device__ __forceinline__ void tma_load_2d_pair_to(uint32_t dst_cluster, const CUtensorMap* map, uint32_t bar_cluster,
+                                                    int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];\n" ::"r"(dst_cluster),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_pair_to(uint32_t dst_cluster, const CUtensorMap* map, uint32_t bar_cluster,
+                                                    int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+      "%4}], [%5];\n" ::"r"(dst_cluster),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar_cluster)
       : "memory");
 }

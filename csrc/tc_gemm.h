@@ -48,7 +48,14 @@ struct TcGemmArgs {
   const void* resid = nullptr;
   int64_t ldr = 0;
   int pair = -1;
-  int debug = 0;  // bit 0: skip the store epilogue's global writes (timing experiments)
+  int debug = 0;  // bit 0: skip the store epilogue's global writes; bit 1: role wait counters into dbg
+  // Fused projection groups (dense mode): kind 1 splits the output's columns over seg_ptr (bf16
+  // [M, width] row-major outputs), kind 2 takes A's K range from K-major segments [M, width], kind 3
+  // takes A's rows from MN-major segments [K, width].  seg_width[s] > 0, seg_ld[s] in elements.
+  int seg_kind = 0, nseg = 0;
+  void* seg_ptr[8] = {};
+  int64_t seg_width[8] = {}, seg_ld[8] = {};
+  unsigned long long* dbg = nullptr;
   int* status = nullptr;     // null: the device's default status word (tc_gemm_status)
   uint32_t spin_limit = 0;   // polls per pipeline wait before giving up; 0 = the built-in limit
   int num_sms = 0;

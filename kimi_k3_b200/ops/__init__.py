@@ -15,7 +15,8 @@ import torch
 
 from . import _loader
 from .functional import (attnres_mix, conv_silu_norm, conv_silu_norm_step, flash_attention, kda_chunk, kda_decay,
-                         kda_decode_step, linear, linear_cross_entropy, linear_supported, mark_seen, mla_absorbed_decode, mla_decode_supported,
+                         kda_decode_step, linear, linear_cross_entropy, linear_group, linear_group_supported,
+                         linear_supported, mark_seen, mla_absorbed_decode, mla_decode_supported,
                          moe_grouped_experts, qb_histogram, rms_norm, router_topk, sample_tokens, sigmoid_mul,
                          situ_glu)
 
@@ -33,7 +34,7 @@ def use_kernels(x: torch.Tensor) -> bool:
 
 
 __all__ = [
-    "kernels_enabled", "use_kernels", "linear", "linear_supported", "rms_norm", "situ_glu", "sigmoid_mul", "kda_chunk", "kda_decode_step",
+    "kernels_enabled", "use_kernels", "linear", "linear_supported", "linear_group", "linear_group_supported", "rms_norm", "situ_glu", "sigmoid_mul", "kda_chunk", "kda_decode_step",
     "conv_silu_norm", "kda_decay", "flash_attention", "mla_absorbed_decode", "router_topk", "qb_histogram",
     "moe_grouped_experts", "attnres_mix", "linear_cross_entropy", "conv_silu_norm_step", "mla_decode_supported",
     "sample_tokens", "mark_seen",

@@ -34,8 +34,9 @@ def _tma_rows(t: torch.Tensor) -> torch.Tensor:
 
 
 def gemm_tiles(n: int) -> int:
-    """Output columns per tile for an ``n``-wide product: 256 when it divides the width well."""
-    return 256 if n >= 1280 or n % 256 == 0 else 128
+    """Output columns per tile for an ``n``-wide product: 256 (with CTA pairs, 256 x 256 tiles) unless
+    the width is so narrow that most of a 256-wide tile would be padding."""
+    return 256 if n >= 512 or n % 256 == 0 else 128
 
 
 def wgrad_splits(rows: int, cols: int, k: int, bn: int, sms: int = 148) -> int:
@@ -78,6 +79,13 @@ class _Linear(torch.autograd.Function):
         dy2 = dy.reshape(-1, n)
         if dy2.dtype != torch.bfloat16:
             dy2 = dy2.to(torch.bfloat16)
+        n8 = -(-n // 8) * 8
+        if n8 != n:
+            # a narrow projection (router, beta): dY is both the K-major A of dX and the MN-major A
+            # of dW, so its rows must be 16-byte aligned: pad the width with zero columns (and the
+            # weight with zero rows); the zeros add nothing to either product
+            dy2 = F.pad(dy2, (0, n8 - n))
+            wb = F.pad(wb, (0, 0, 0, n8 - n))
         dy2 = _tma_rows(dy2)
         C = _C()
         dx = dw = db = None
@@ -86,12 +94,93 @@ class _Linear(torch.autograd.Function):
             dx = dx.reshape(shape)
         if ctx.needs_input_grad[1]:
             bn = gemm_tiles(k)
-            dw = torch.zeros(n, k, device=dy.device, dtype=torch.float32)
+            dw = torch.zeros(n8, k, device=dy.device, dtype=torch.float32)
             C.tc_gemm_dense(dy2, x2, True, True, True, bn, dw, accumulate=True,
-                            ksplit=wgrad_splits(n, k, dy2.shape[0], bn))
+                            ksplit=wgrad_splits(n8, k, dy2.shape[0], bn))
+            dw = dw[:n]
         if has_bias and ctx.needs_input_grad[2]:
-            db = dy2.float().sum(0)
+            db = dy2[:, :n].float().sum(0)
         return dx, dw, db, None
+
+
+def _pad8(n: int) -> int:
+    return -(-n // 8) * 8
+
+
+class _LinearGroup(torch.autograd.Function):
+    """Several projections of one input as one GEMM per pass (forward, input gradient, weight
+    gradients) over the group's concatenated bf16 weight ``W_cat``.
+
+    Forward writes each projection's output straight into its own tensor (per-column-segment output
+    maps); backward reads every output gradient in place as one K-segmented operand, so
+    ``dX = sum_i dY_i W_i`` is a single product with no concatenation copy and no gradient adds,
+    and all weight gradients come out of one split-K product into one fp32 buffer whose row slices
+    are the parameters' gradients."""
+
+    @staticmethod
+    def forward(ctx, x, wcat, widths, *weights):
+        shape = x.shape
+        k = shape[-1]
+        x2 = x.reshape(-1, k)
+        if x2.dtype != torch.bfloat16:
+            x2 = x2.to(torch.bfloat16)
+        x2 = _tma_rows(x2)
+        m = x2.shape[0]
+        outs = [torch.empty(m, _pad8(w), device=x.device, dtype=torch.bfloat16)[:, :w] for w in widths]
+        _C().tc_gemm_group(1, outs, x2, wcat, None, 256, 1, -1)
+        ctx.save_for_backward(x2, wcat)
+        ctx.meta = (shape, x.dtype, tuple(widths))
+        return tuple(o.view(*shape[:-1], w) for o, w in zip(outs, widths))
+
+    @staticmethod
+    def backward(ctx, *grads):
+        x2, wcat = ctx.saved_tensors
+        shape, xdt, widths = ctx.meta
+        m, k = x2.shape
+        segs = []
+        for g, w in zip(grads, widths):
+            if g is None:
+                g2 = torch.zeros(m, _pad8(w), device=x2.device, dtype=torch.bfloat16)
+            else:
+                g2 = g.reshape(m, w)
+                if g2.dtype != torch.bfloat16:
+                    g2 = g2.to(torch.bfloat16)
+                if w % 8:
+                    g2 = F.pad(g2, (0, _pad8(w) - w))
+                g2 = _tma_rows(g2)
+            segs.append(g2)
+        C = _C()
+        dx = dws = None
+        if ctx.needs_input_grad[0]:
+            dx = torch.empty(m, k, device=x2.device, dtype=torch.float32 if xdt == torch.float32 else torch.bfloat16)
+            C.tc_gemm_group(2, segs, x2, wcat, dx, gemm_tiles(k), 1, -1)
+            dx = dx.view(shape)
+        if any(ctx.needs_input_grad[3:]):
+            n = wcat.shape[0]
+            dwcat = torch.zeros(n, k, device=x2.device, dtype=torch.float32)
+            bn = gemm_tiles(k)
+            C.tc_gemm_group(3, segs, x2, wcat, dwcat, bn, wgrad_splits(n, k, m, bn), 0)
+            dws, row = [], 0
+            for w in widths:
+                dws.append(dwcat[row:row + w])
+                row += w
+        return (dx, None, None, *(dws if dws is not None else [None] * len(widths)))
+
+
+def linear_group_supported(x: torch.Tensor, weights) -> bool:
+    """Every width but the last a multiple of 64, every weight reading the same ``K``, bf16 compute."""
+    if len(weights) < 2 or len(weights) > 8 or _act_dtype(x) != torch.bfloat16:
+        return False
+    k = x.shape[-1]
+    if k % 8 or any(w.ndim != 2 or w.shape[1] != k for w in weights):
+        return False
+    return all(w.shape[0] % 64 == 0 for w in weights[:-1])
+
+
+def linear_group(x: torch.Tensor, weights) -> tuple:
+    """``tuple(x @ W_i^T for W_i in weights)`` as one tcgen05 GEMM per pass (see :class:`_LinearGroup`)."""
+    from .mirror import group_weight
+    return _LinearGroup.apply(x, group_weight(weights), [int(w.shape[0]) for w in weights], *weights)
 
 
 def linear_supported(x: torch.Tensor, weight: torch.Tensor) -> bool:
@@ -557,7 +646,7 @@ def linear_cross_entropy(hidden, weight, targets, valid, chunk_rows: int = 16384
 
 
 __all__ = [
-    "linear", "linear_supported", "gemm_tiles", "wgrad_splits", "rms_norm", "situ_glu", "sigmoid_mul", "kda_decay", "conv_silu_norm", "kda_chunk", "kda_decode_step",
+    "linear", "linear_supported", "linear_group", "linear_group_supported", "gemm_tiles", "wgrad_splits", "rms_norm", "situ_glu", "sigmoid_mul", "kda_decay", "conv_silu_norm", "kda_chunk", "kda_decode_step",
     "conv_silu_norm_step", "mla_decode_supported", "sample_tokens", "mark_seen",
     "flash_attention", "mla_absorbed_decode", "router_topk", "qb_histogram", "moe_grouped_experts",
     "attnres_mix", "linear_cross_entropy",

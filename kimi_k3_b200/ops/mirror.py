@@ -23,6 +23,8 @@ import torch
 from . import _loader
 
 _REGISTRY: "weakref.WeakValueDictionary[int, _Entry]" = weakref.WeakValueDictionary()
+# projection groups: tuple of parameter ids -> the bf16 buffer their mirrors are row slices of
+_GROUPS: "dict[tuple, torch.Tensor]" = {}
 
 
 class _Entry:
@@ -42,7 +44,24 @@ class _Entry:
 class WeightMirror:
     """Persistent bf16 copies of a set of fp32 CUDA parameters."""
 
-    def __init__(self, params):
+    def __init__(self, params, groups=()):
+        """``groups``: lists of 2-D weights with equal column counts that one fused projection reads as
+        a single ``[sum of rows, cols]`` matrix; their mirrors become row slices of one buffer."""
+        params = list(params)
+        group_of = {}
+        for grp in groups:
+            grp = [p for p in grp]
+            if len(grp) < 2 or any(p.ndim != 2 or p.shape[1] != grp[0].shape[1] or not p.is_cuda
+                                   or p.dtype != torch.float32 for p in grp):
+                continue
+            buf = torch.empty(sum(p.shape[0] for p in grp), grp[0].shape[1], dtype=torch.bfloat16,
+                              device=grp[0].device)
+            row = 0
+            for p in grp:
+                group_of[id(p)] = buf[row:row + p.shape[0]]
+                row += p.shape[0]
+            _GROUPS[tuple(id(p) for p in grp)] = buf
+            params.extend(grp)
         seen, ps = set(), []
         for p in params:
             if id(p) in seen or not isinstance(p, torch.Tensor) or not p.is_cuda or p.dtype != torch.float32:
@@ -57,7 +76,10 @@ class WeightMirror:
         self._ptrs = []
         self._total_vec = 0
         for p in ps:
-            e = _Entry(p, torch.empty(p.shape, dtype=torch.bfloat16, device=p.device), self)
+            mirror = group_of.get(id(p))
+            if mirror is None:
+                mirror = torch.empty(p.shape, dtype=torch.bfloat16, device=p.device)
+            e = _Entry(p, mirror, self)
             self.entries.append(e)
             _REGISTRY[id(p)] = e
         self.refresh()
@@ -115,9 +137,29 @@ def bf16_weight(p: torch.Tensor) -> torch.Tensor:
     return e.mirror
 
 
+def group_weight(params) -> torch.Tensor:
+    """The concatenated bf16 ``[sum of rows, cols]`` operand of a projection group: the shared mirror
+    buffer when the group is registered (stale members re-cast first), else a fresh concatenation."""
+    buf = _GROUPS.get(tuple(id(p) for p in params))
+    if buf is not None:
+        views = [bf16_weight(p) for p in params]  # refreshes stale members in place
+        if all(v.data_ptr() == buf[0].data_ptr() + off * buf.stride(0) * buf.element_size()
+               for v, off in zip(views, _offsets(params))):
+            return buf
+    return torch.cat([bf16_weight(p) for p in params], 0)
+
+
+def _offsets(params):
+    out, row = [], 0
+    for p in params:
+        out.append(row)
+        row += p.shape[0]
+    return out
+
+
 def mirror_for(p: torch.Tensor):
     e = _REGISTRY.get(id(p))
     return None if e is None or e.param_ref() is not p else e.owner
 
 
-__all__ = ["WeightMirror", "bf16_weight", "mirror_for"]
+__all__ = ["WeightMirror", "bf16_weight", "group_weight", "mirror_for"]

@@ -75,3 +75,55 @@ def test_optimizer_step_keeps_mirrors_current(cuda):
     opt.step()  # bumps versions: bf16_weight re-casts on demand even without a refresh
     for m in (net[0], net[2]):
         assert torch.equal(bf16_weight(m.weight), m.weight.detach().bfloat16())
+
+
+def test_tc_gemm_group_three_kinds(cuda):
+    """Segmented products of one projection group against fp32 torch: per-segment outputs, the
+    K-segmented input gradient and the M-segmented weight gradients."""
+    from kimi_k3_b200.ops import _loader
+    C = _loader.require()
+    torch.manual_seed(9)
+    m, k = 1000, 640
+    widths = [640, 128, 64, 10]
+    w = [(torch.randn(n, k, device=cuda) / k ** 0.5).bfloat16() for n in widths]
+    wcat = torch.cat(w, 0)
+    x = torch.randn(m, k, device=cuda).bfloat16()
+    outs = [torch.empty(m, -(-n // 8) * 8, device=cuda, dtype=torch.bfloat16)[:, :n] for n in widths]
+    C.tc_gemm_group(1, outs, x, wcat, None, 256, 1, -1)
+    for o, wi in zip(outs, w):
+        ref = x.float() @ wi.float().t()
+        assert _rel(o, ref) < 1e-2
+    dys = [torch.randn(m, n, device=cuda).bfloat16() for n in widths]
+    segs = [d if n % 8 == 0 else F.pad(d, (0, -(-n // 8) * 8 - n)).contiguous() for d, n in zip(dys, widths)]
+    for pair in (0, 1):
+        dx = torch.empty(m, k, device=cuda, dtype=torch.bfloat16)
+        C.tc_gemm_group(2, segs, x, wcat, dx, 256, 1, pair)
+        ref = sum(d.float() @ wi.float() for d, wi in zip(dys, w))
+        assert _rel(dx, ref) < 1e-2
+        dw = torch.zeros(sum(widths), k, device=cuda)
+        C.tc_gemm_group(3, segs, x, wcat, dw, 256, 3, pair)
+        ref = torch.cat([d.float().t() @ x.float() for d in dys], 0)
+        assert _rel(dw, ref) < 1e-3
+
+
+def test_linear_group_matches_separate_projections(cuda):
+    from kimi_k3_b200.models.linear import Linear
+    from kimi_k3_b200.ops import linear_group
+    from kimi_k3_b200.ops.mirror import WeightMirror
+    torch.manual_seed(4)
+    lins = [Linear(640, n, bias=False).to(cuda) for n in (640, 640, 64, 10)]
+    mirror = WeightMirror([], groups=[[l.weight for l in lins]])
+    x = torch.randn(2, 300, 640, device=cuda, requires_grad=True)
+    dys = [torch.randn(2, 300, l.out_features, device=cuda) for l in lins]
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        ys = linear_group(x, [l.weight for l in lins])
+    sum((y.float() * d).sum() for y, d in zip(ys, dys)).backward()
+    xr = x.detach().bfloat16().float().requires_grad_()
+    ws = [l.weight.detach().bfloat16().float().requires_grad_() for l in lins]
+    sum((F.linear(xr, wr) * d).sum() for wr, d in zip(ws, dys)).backward()
+    for y, wr in zip(ys, ws):
+        assert _rel(y, F.linear(xr, wr)) < 1e-2
+    assert _rel(x.grad, xr.grad) < 1e-2
+    for l, wr in zip(lins, ws):
+        assert l.weight.grad.dtype == torch.float32 and _rel(l.weight.grad, wr.grad) < 1e-2
+    assert mirror.params  # the group's mirrors were registered
