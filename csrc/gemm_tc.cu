@@ -1247,9 +1247,11 @@ cudaError_t tc_gemm(const TcGemmArgs& a, cudaStream_t stream) {
   if (a.epi == 3 && (!a.out_fp32 || a.mode != 0 || a.comm_mode != 0)) return cudaErrorInvalidValue;
   if ((a.bias || a.resid) && (a.epi != 0 || a.mode != 0 || a.comm_mode != 0)) return cudaErrorInvalidValue;
   if (a.resid && (a.out_fp32 || a.ldr % 8 || (reinterpret_cast<uintptr_t>(a.resid) & 15))) return cudaErrorInvalidValue;
-  // CTA pairs: dense non-comm launches of more than one 128-row block (pair = -1 picks this)
+  // CTA pairs: dense non-comm launches of more than one 128-row block whose operands are both
+  // K-major (pair = -1 picks this; measured on B200, an MN-major operand makes the leader's
+  // per-stage copies small 64 x 64 boxes and the single-CTA 128 x 256 tile wins)
   const bool pair_ok = a.mode == 0 && a.comm_mode == 0 && a.ag_world == 0 && a.epi != 2;
-  const bool pair = pair_ok && (a.pair > 0 || (a.pair < 0 && a.M > BM));
+  const bool pair = pair_ok && (a.pair > 0 || (a.pair < 0 && a.M > BM && !a.a_mn && !a.b_mn));
   if (a.pair > 0 && !pair_ok) return cudaErrorInvalidValue;
   // A: K-major storage [a_rows, a_cols=K]; MN-major storage [a_rows=K, a_cols=M]
   if (!a.a_mn) {

@@ -383,7 +383,10 @@ class KDAProjections(nn.Module):
         return torch.cat(outs, 0), (ShortConvState(torch.cat(bufs, 0)) if return_state else None)
 
     def forward(self, hidden_states, *, q_conv_state=None, k_conv_state=None, v_conv_state=None,
-                attention_mask=None, output_final_state=False, inplace_state=False) -> KDAProjectionResult:
+                attention_mask=None, output_final_state=False, inplace_state=False,
+                projected=None) -> KDAProjectionResult:
+        """``projected``: the (q, k, v, alpha_down, beta) linear outputs when the caller computed them
+        in one fused group GEMM together with the output-gate logits."""
         c = self.config
         if hidden_states.ndim != 3 or hidden_states.shape[-1] != c.d_model:
             raise ValueError(f"hidden_states must have shape [B,T,{c.d_model}]")
@@ -393,11 +396,15 @@ class KDAProjections(nn.Module):
         validate_attention_mask(attention_mask, b, t)
         fused = (_ops.use_kernels(hidden_states) and not output_final_state and q_conv_state is None
                  and attention_mask is None and not c.short_conv_bias)
-        ql, kl, vl = self.q_proj(hidden_states), self.k_proj(hidden_states), self.v_proj(hidden_states)
-        beta = torch.sigmoid(self.beta_proj(hidden_states))
+        if projected is not None:
+            ql, kl, vl, adown, blog = projected
+        else:
+            ql, kl, vl = self.q_proj(hidden_states), self.k_proj(hidden_states), self.v_proj(hidden_states)
+            adown, blog = self.alpha_down(hidden_states), self.beta_proj(hidden_states)
+        beta = torch.sigmoid(blog)
         be = torch.finfo(beta.dtype).eps
         beta = beta.clamp(be, 1.0 - be)
-        decay_logits = self.alpha_up(self.alpha_down(hidden_states)).reshape(b, t, c.num_heads, c.key_head_dim)
+        decay_logits = self.alpha_up(adown).reshape(b, t, c.num_heads, c.key_head_dim)
         decay_logits = decay_logits + self.b_alpha[None, None]
         states = (q_conv_state, k_conv_state, v_conv_state)
         hl = c.key_head_dim // 8
@@ -469,6 +476,13 @@ class KimiDeltaAttention(nn.Module):
         self.output_gate = FullRankOutputGate(config.d_model, bias=config.output_gate_bias,
                                               output_bias=config.output_bias, init_std=config.init_std, value_width=config.value_width)
 
+    def projection_groups(self):
+        """Weights that read the block input and run as one fused GEMM on CUDA: q, k, v, the output
+        gate (widths multiples of 64), then the decay down-projection and beta (the ragged last)."""
+        p = self.projections
+        return [[p.q_proj.weight, p.k_proj.weight, p.v_proj.weight, self.output_gate.gate_proj.weight,
+                 p.alpha_down.weight, p.beta_proj.weight]]
+
     def _validate_state(self, x, state):
         if state is None:
             return
@@ -498,11 +512,18 @@ class KimiDeltaAttention(nn.Module):
         self._validate_state(hidden_states, state)
         return_state = output_final_state or mode == "decode"
         inplace = state is not None and state.inplace and mode == "decode"
+        projected = gate_logits = None
+        group = self.projection_groups()[0]
+        if (_ops.use_kernels(hidden_states) and self.projections.q_proj.bias is None
+                and self.projections.beta_proj.bias is None and self.output_gate.gate_proj.bias is None
+                and _ops.linear_group_supported(hidden_states, group)):
+            ql, kl, vl, gate_logits, adown, blog = _ops.linear_group(hidden_states, group)
+            projected = (ql, kl, vl, adown, blog)
         proj = self.projections(hidden_states, q_conv_state=state.q_conv_state if state else None,
                                 k_conv_state=state.k_conv_state if state else None,
                                 v_conv_state=state.v_conv_state if state else None,
                                 attention_mask=attention_mask, output_final_state=return_state,
-                                inplace_state=inplace)
+                                inplace_state=inplace, projected=projected)
         g, alpha = self.decay(proj.decay_logits)
         init = state.recurrent_state if state is not None else None
         kw = dict(initial_state=init, output_final_state=return_state or output_diagnostics,
@@ -519,7 +540,8 @@ class KimiDeltaAttention(nn.Module):
             core = kda_core(proj.q, proj.k, proj.v, g, proj.beta, chunk_size=c.chunk_size,
                             secondary_tile_size=c.secondary_tile_size, **kw)
         normalized = self.output_norm(core.hidden_states)
-        out, gate = self.output_gate(combine_heads(normalized), hidden_states, return_gate=True)
+        out, gate = self.output_gate(combine_heads(normalized), hidden_states, return_gate=True,
+                                     gate_logits=gate_logits)
         if attention_mask is not None:
             out = out * attention_mask[..., None].to(out.dtype)
         nxt = None

@@ -253,8 +253,13 @@ class LatentKVProjection(nn.Module):
         if latent_kv.ndim != 3 or latent_kv.shape[-1] != c.kv_latent_dim:
             raise ValueError(f"latent_kv must have shape [B,T,{c.kv_latent_dim}]")
         b, t, _ = latent_kv.shape
-        return (self.key_up(latent_kv).reshape(b, t, c.num_heads, c.q_head_dim),
-                self.value_up(latent_kv).reshape(b, t, c.num_heads, c.v_head_dim))
+        pair = [self.key_up.weight, self.value_up.weight]
+        if (_ops.use_kernels(latent_kv) and self.key_up.bias is None and self.value_up.bias is None
+                and _ops.linear_group_supported(latent_kv, pair)):
+            key, value = _ops.linear_group(latent_kv, pair)  # K and V from one read of the latent
+        else:
+            key, value = self.key_up(latent_kv), self.value_up(latent_kv)
+        return key.reshape(b, t, c.num_heads, c.q_head_dim), value.reshape(b, t, c.num_heads, c.v_head_dim)
 
     def forward(self, hidden_states) -> LatentKVOutput:
         latent = self.compress(hidden_states)
@@ -406,9 +411,17 @@ class GatedMLA(nn.Module):
         self.output_dropout = nn.Dropout(config.output_dropout)
         self.absorbed_decode = True
 
-    def _postprocess(self, attention_output, hidden_states):
+    def projection_groups(self):
+        """Weights that run as one fused GEMM each on CUDA: those reading the block input (query,
+        latent compression, output gate) and those reading the latent (key and value
+        reconstruction)."""
+        p = self.projections
+        return [[p.query.weight, p.latent_kv.compression.weight, self.output_gate.gate_proj.weight],
+                [p.latent_kv.key_up.weight, p.latent_kv.value_up.weight]]
+
+    def _postprocess(self, attention_output, hidden_states, gate_logits=None):
         combined = combine_heads(attention_output)
-        logits = self.output_gate.gate_proj(hidden_states)
+        logits = self.output_gate.gate_proj(hidden_states) if gate_logits is None else gate_logits
         gp = self.output_gate.output_proj
         if _ops.use_kernels(combined) and gp.bias is None:
             gated = _ops.sigmoid_mul(logits, combined.to(hidden_states.dtype))
@@ -437,8 +450,15 @@ class GatedMLA(nn.Module):
         b, t = hidden_states.shape[:2]
         validate_right_padding_mask(attention_mask, b, t)
         dev = hidden_states.device
-        query = self.projections.project_queries(hidden_states)
-        latent = self.projections.compress_kv(hidden_states)
+        gate_logits = None
+        group = self.projection_groups()[0]
+        if (_ops.use_kernels(hidden_states) and not c.projection_bias and self.output_gate.gate_proj.bias is None
+                and _ops.linear_group_supported(hidden_states, group)):
+            q_flat, latent, gate_logits = _ops.linear_group(hidden_states, group)
+            query = q_flat.reshape(b, t, c.num_heads, c.q_head_dim)
+        else:
+            query = self.projections.project_queries(hidden_states)
+            latent = self.projections.compress_kv(hidden_states)
         need_probs = output_attentions or output_diagnostics
         fast_full = (cache is None and not use_cache and not need_probs and attention_mask is None
                      and _ops.use_kernels(hidden_states) and c.attention_dropout == 0.0)
@@ -448,7 +468,7 @@ class GatedMLA(nn.Module):
             key, value = self.projections.reconstruct_kv(latent)
             self._record_qk_scale(query, key)
             raw = _ops.flash_attention(query, key, value, causal=True)
-            out, gate = self._postprocess(raw, hidden_states)
+            out, gate = self._postprocess(raw, hidden_states, gate_logits)
             return GatedMLAOutput(out, None, None, None)
         if cache is None and not use_cache and not need_probs and attention_mask is None and not output_diagnostics:
             # Full causal sequence without padding and without a cache to build: no mask at all.
@@ -457,7 +477,7 @@ class GatedMLA(nn.Module):
             raw = mla_attention(query, key, value, None, is_causal=True, dropout_p=c.attention_dropout,
                                 keep_output_fp32=c.keep_attention_output_fp32, backend=c.resolved_backend,
                                 training=self.training)
-            out, gate = self._postprocess(raw, hidden_states)
+            out, gate = self._postprocess(raw, hidden_states, gate_logits)
             return GatedMLAOutput(out, None, None, None)
         current_mask = torch.ones(b, t, dtype=torch.bool, device=dev) if attention_mask is None else attention_mask
         prev = torch.zeros(b, dtype=torch.long, device=dev) if cache is None else cache.sequence_offset
@@ -477,7 +497,7 @@ class GatedMLA(nn.Module):
                                          lengths=getattr(updated, "valid_lengths", None))
             if not c.keep_attention_output_fp32:
                 raw = raw.to(hidden_states.dtype)
-            out, gate = self._postprocess(raw, hidden_states)
+            out, gate = self._postprocess(raw, hidden_states, gate_logits)
             return GatedMLAOutput(out, updated if use_cache else None, None, None)
         key, value = self.projections.reconstruct_kv(updated.latent_kv)
         self._record_qk_scale(query, key)
@@ -488,7 +508,7 @@ class GatedMLA(nn.Module):
                                backend=c.resolved_backend, query_mask=current_mask, query_positions=qpos,
                                training=self.training, return_attentions=need_probs)
         raw, probs = (result if need_probs else (result, None))
-        out, gate = self._postprocess(raw, hidden_states)
+        out, gate = self._postprocess(raw, hidden_states, gate_logits)
         out = out * current_mask[..., None].to(out.dtype)
         diagnostics = None
         if output_diagnostics:

@@ -158,13 +158,15 @@ class TopKRouter(nn.Module):
             raise ValueError("next routing bias must be finite")
         self.routing_bias.copy_(next_bias.to(device=self.routing_bias.device, dtype=self.routing_bias.dtype))
 
-    def forward(self, inputs, *, need_qb_cutoff=False, return_full_scores=False) -> RouterOutput:
+    def forward(self, inputs, *, need_qb_cutoff=False, return_full_scores=False, logits=None) -> RouterOutput:
+        """``logits``: ``projection(inputs)`` already computed (by a fused projection group)."""
         c = self.config
         if inputs.ndim != 2 or inputs.shape[-1] != c.d_model:
             raise ValueError(f"router inputs must have shape [M,{c.d_model}]")
         if need_qb_cutoff and c.top_k >= c.num_routed_experts:
             raise ValueError("Top-(k+1) cutoff requires k < num_experts")
-        logits = self.projection(inputs)
+        if logits is None:
+            logits = self.projection(inputs)
         cd = policy_dtype(inputs.dtype, c.router_logits_dtype)
         wd = policy_dtype(inputs.dtype, c.routing_weights_dtype)
         if _ops.use_kernels(logits) and cd == torch.float32 and wd == torch.float32:
@@ -515,12 +517,36 @@ class StableLatentMoE(nn.Module):
         return fn(latent, self.routed_experts, ro.selected_experts, ro.selected_weights,
                   accumulation_dtype=accumulation_dtype)
 
-    def shared_forward(self, flat):
+    def shared_forward(self, flat, projected=None):
+        """``projected``: the experts' (gate, up) linear outputs from a fused projection group."""
         out = None
-        for expert in self.shared_experts:
-            y = expert(flat)
+        for i, expert in enumerate(self.shared_experts):
+            if projected is None:
+                y = expert(flat)
+            else:
+                t = expert.transform
+                g, u = projected[2 * i], projected[2 * i + 1]
+                y = t.down_proj(situ_glu_activation(g, u, t.beta_gate, t.beta_up))
             out = y if out is None else out + y
         return out
+
+    def projection_groups(self):
+        """Weights that read the block input and run as one fused GEMM on CUDA: every shared expert's
+        gate and up projections, the latent down-projection, then the router (the ragged last)."""
+        ws = []
+        for expert in self.shared_experts:
+            ws += [expert.transform.gate_proj.weight, expert.transform.up_proj.weight]
+        return [ws + [self.down_projection.weight, self.router.projection.weight]]
+
+    def _fused_projections(self, flat):
+        group = self.projection_groups()[0]
+        biases = [self.down_projection.bias, self.router.projection.bias]
+        for expert in self.shared_experts:
+            biases += [expert.transform.gate_proj.bias, expert.transform.up_proj.bias]
+        if (not _ops.use_kernels(flat) or any(b is not None for b in biases)
+                or not _ops.linear_group_supported(flat, group)):
+            return None
+        return _ops.linear_group(flat, group)
 
     def forward(self, inputs, *, update_routing_bias=False, return_router_diagnostics=False,
                 return_branch_outputs=False):
@@ -531,10 +557,16 @@ class StableLatentMoE(nn.Module):
             raise RuntimeError("routing bias cannot update during eval")
         shape = inputs.shape
         flat = inputs.reshape(-1, c.d_model)
-        shared = self.shared_forward(flat)
-        latent = self.down_projection(flat)
+        fused = self._fused_projections(flat)
+        if fused is None:
+            shared = self.shared_forward(flat)
+            latent = self.down_projection(flat)
+            router_logits = None
+        else:
+            shared = self.shared_forward(flat, fused[:-2])
+            latent, router_logits = fused[-2], fused[-1]
         need_balance = update_routing_bias or self._balance_accumulating
-        ro = self.router(flat, need_qb_cutoff=need_balance, return_full_scores=need_balance)
+        ro = self.router(flat, need_qb_cutoff=need_balance, return_full_scores=need_balance, logits=router_logits)
         acc = policy_dtype(latent.dtype, c.routed_accumulation_dtype)
         agg = self.routed_aggregate(latent, ro, acc)
         normalized = self.routed_aggregate_norm(agg).to(latent.dtype)

@@ -252,12 +252,14 @@ class FullRankOutputGate(nn.Module):
             raise ValueError(f"residual_input must have shape [B,T,{self.d_model}]")
         return torch.sigmoid(self.gate_proj(residual_input))
 
-    def forward(self, attention_output: torch.Tensor, residual_input: torch.Tensor, *, return_gate: bool = False):
+    def forward(self, attention_output: torch.Tensor, residual_input: torch.Tensor, *, return_gate: bool = False,
+                gate_logits: torch.Tensor | None = None):
+        """``gate_logits``: ``gate_proj(residual_input)`` already computed (by a fused projection group)."""
         if attention_output.ndim != 3 or attention_output.shape[-1] != self.value_width:
             raise ValueError(f"attention_output must have shape [B,T,{self.value_width}]")
         if attention_output.shape[:2] != residual_input.shape[:2] or residual_input.shape[-1] != self.d_model:
             raise ValueError("attention_output and residual_input must share [B,T] (residual width d_model)")
-        logits = self.gate_proj(residual_input)
+        logits = self.gate_proj(residual_input) if gate_logits is None else gate_logits
         if _ops.use_kernels(logits):
             gated = _ops.sigmoid_mul(logits, attention_output)
             gate = None

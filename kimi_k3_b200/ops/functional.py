@@ -36,15 +36,16 @@ def _tma_rows(t: torch.Tensor) -> torch.Tensor:
 def gemm_tiles(n: int) -> int:
     """Output columns per tile for an ``n``-wide product: 256 (with CTA pairs, 256 x 256 tiles) unless
     the width is so narrow that most of a 256-wide tile would be padding."""
-    return 256 if n >= 512 or n % 256 == 0 else 128
+    return 256 if n >= 320 or n % 256 == 0 else 128
 
 
 def wgrad_splits(rows: int, cols: int, k: int, bn: int, sms: int = 148) -> int:
-    """K slices of a weight-gradient product ``[rows, cols]`` with reduction length ``k``, so that
-    about two work units per SM exist while every slice keeps at least four 64-wide K blocks."""
+    """K slices of a weight-gradient product ``[rows, cols]`` with reduction length ``k``: about one
+    work unit per SM (every extra slice adds a tile of fp32 reduce-adds in L2), at most 8, and every
+    slice keeps at least four 64-wide K blocks (measured on B200 at the model's shapes)."""
     tiles = -(-rows // 128) * -(-cols // bn)
-    want = max(1, -(-2 * sms // tiles))
-    return int(max(1, min(want, 16, max(1, (k // 64) // 4))))
+    want = max(1, round(sms / tiles))
+    return int(max(1, min(want, 8, max(1, (k // 64) // 4))))
 
 
 class _Linear(torch.autograd.Function):
@@ -96,7 +97,7 @@ class _Linear(torch.autograd.Function):
             bn = gemm_tiles(k)
             dw = torch.zeros(n8, k, device=dy.device, dtype=torch.float32)
             C.tc_gemm_dense(dy2, x2, True, True, True, bn, dw, accumulate=True,
-                            ksplit=wgrad_splits(n8, k, dy2.shape[0], bn))
+                            ksplit=wgrad_splits(n8, k, dy2.shape[0], bn), pair=0)
             dw = dw[:n]
         if has_bias and ctx.needs_input_grad[2]:
             db = dy2[:, :n].float().sum(0)

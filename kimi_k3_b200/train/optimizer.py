@@ -958,7 +958,9 @@ def build_kimi_optimizer(model, config: KimiOptimizerConfig | None = None):
 
 def build_weight_mirror(model):
     """bf16 mirrors of the model's projection weights (every ``nn.Linear`` weight and the stacked
-    routed-expert matrices) when they live on CUDA and the native kernels are enabled; else None."""
+    routed-expert matrices) when they live on CUDA and the native kernels are enabled; else None.
+    Weights a module declares in ``projection_groups()`` share one buffer per group (the fused GEMM
+    reads them as one matrix)."""
     from .. import ops
     from ..ops.mirror import WeightMirror
     weights, seen = [], set()
@@ -973,7 +975,12 @@ def build_weight_mirror(model):
                 weights.append(p)
     if not weights or not ops.use_kernels(weights[0]):
         return None
-    return WeightMirror(weights)
+    groups = []
+    for mod in model.modules():
+        declare = getattr(mod, "projection_groups", None)
+        if callable(declare):
+            groups.extend(declare())
+    return WeightMirror(weights, groups=groups)
 
 
 __all__ = [
