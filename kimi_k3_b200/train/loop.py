@@ -278,7 +278,9 @@ def train_one_epoch(model, dataloader, optimizer, *, device="cpu", scheduler=Non
             if finite and grad_clip is not None and pre is not None:
                 coef = min(1.0, float(grad_clip) / (pre + 1e-6))
                 if coef < 1.0:
-                    torch._foreach_mul_([p.grad for p in params if p.grad is not None], coef)
+                    # sharded (DTensor) gradients are scaled through their local shards
+                    torch._foreach_mul_([p.grad.to_local() if hasattr(p.grad, "to_local") else p.grad
+                                         for p in params if p.grad is not None], coef)
             post = None if pre is None else (pre * min(1.0, float(grad_clip) / (pre + 1e-6)) if grad_clip else pre)
             opt_metrics = diagnostics.capture_before_optimizer_step() if diagnostics is not None else {}
             o0 = time.perf_counter()

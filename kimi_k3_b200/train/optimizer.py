@@ -491,6 +491,8 @@ class KimiMuon(torch.optim.Optimizer):
         if closure is not None:
             with torch.enable_grad():
                 closure()
+        if any(_is_dtensor(p) for g in self.param_groups for p in g["params"]):
+            return self._step_sharded(skip)
         if any(p.grad is None for g in self.param_groups for p in g["params"] if self._mine(p)):
             if skip is not None:
                 raise RuntimeError("device-flag Muon steps need a gradient for every parameter")
@@ -592,6 +594,63 @@ class KimiMuon(torch.optim.Optimizer):
         metrics["ratio"].append(lr_t * unorm / (pnorm.clamp_min(1e-30) / numel).clamp_min(group["eps"]) / numel)
 
     @torch.no_grad()
+    def _step_sharded(self, skip=None):
+        """Fully sharded parameters (DTensor shards along dim 0): momentum per local shard; the
+        momentum-updated matrix is all-gathered, orthogonalised whole (Newton-Schulz needs the full
+        matrix), and every rank applies its own rows of the update."""
+        from torch.distributed.tensor import DTensor
+        metrics = {"raw": [], "ortho": [], "scaled": [], "ratio": []}
+        for group in self.param_groups:
+            lr, mom, wd = group["lr"], group["momentum"], group["weight_decay"]
+            for p in group["params"]:
+                if p.grad is None:
+                    continue
+                sharded = isinstance(p, DTensor)
+                pl = p.to_local() if sharded else p
+                g = p.grad.to_local() if isinstance(p.grad, DTensor) else p.grad
+                st = self.state[p]
+                buf = st.get("momentum_buffer")
+                if buf is None:
+                    buf = st["momentum_buffer"] = torch.zeros_like(pl)
+                g = g.to(buf.dtype)
+                if skip is not None:
+                    g = torch.where(skip, torch.zeros((), device=g.device, dtype=g.dtype), g)
+                    buf.mul_(torch.where(skip, 1.0, mom).to(buf.dtype)).add_(g)
+                else:
+                    buf.mul_(mom).add_(g)
+                raw = g.add(buf, alpha=mom) if group["nesterov"] else buf
+                if sharded:
+                    raw_full = DTensor.from_local(raw, p.device_mesh, p.placements, shape=p.shape,
+                                                  stride=p.stride()).full_tensor()
+                else:
+                    raw_full = raw
+                slot = self._slots[id(p)]
+                blocks = slot.to_blocks(raw_full).float()
+                ortho = batched_newton_schulz(blocks, steps=group["ns_steps"], eps=group["eps"],
+                                              dtype=self._resolved_ns_dtype(p.device))
+                scale = max(slot.rows, slot.cols) ** 0.5 if group["update_rms_scaling"] else 1.0
+                metrics["raw"].append(blocks.flatten(1).square().mean(1).sqrt())
+                metrics["ortho"].append(ortho.flatten(1).square().mean(1).sqrt())
+                metrics["scaled"].append(metrics["ortho"][-1] * scale)
+                upd = slot.from_blocks(ortho).to(pl.dtype).mul_(scale)
+                if sharded:
+                    mesh = p.device_mesh
+                    upd = torch.chunk(upd, mesh.size(), dim=0)[mesh.get_local_rank()]
+                lr_eff = torch.where(skip, 0.0, lr) if skip is not None else lr
+                if wd:
+                    pl.mul_(1.0 - lr_eff * wd)
+                if torch.is_tensor(lr_eff):
+                    pl.add_(upd * (-lr_eff).to(upd.dtype))
+                else:
+                    pl.add_(upd, alpha=-lr_eff)
+                prms = pl.float().square().mean().sqrt().clamp_min(group["eps"])  # this rank's rows
+                lr_v = lr if torch.is_tensor(lr) else torch.tensor(float(lr), device=prms.device)
+                metrics["ratio"].append((lr_v * metrics["scaled"][-1].mean() / prms)[None])
+        self._metric_tensors = {k: torch.cat(v) for k, v in metrics.items() if v}
+        self.last_update_metrics = {}
+        return self._metric_tensors
+
+    @torch.no_grad()
     def _step_sparse(self):
         """Parameters without gradients this step keep their momentum untouched (reference
         behaviour); the others are processed matrix by matrix."""
@@ -634,6 +693,14 @@ class KimiMuon(torch.optim.Optimizer):
                                     "muon/scaled_update_rms": scaled, "muon/ns_gain": scaled / max(raw, 1e-12),
                                     "muon/update_to_parameter_ratio": ratio}
         return self.last_update_metrics
+
+
+def _is_dtensor(p) -> bool:
+    try:
+        from torch.distributed.tensor import DTensor
+    except ImportError:  # pragma: no cover
+        return False
+    return isinstance(p, DTensor)
 
 
 # --------------------------------------------------------------------------- QK-Clip
@@ -683,6 +750,7 @@ class QKClipController:
         self.total_events = 0
         self.consecutive_steps_active = 0
         self._pending = None
+        self.replica_group = None  # data-parallel group: scales are MAX-reduced over it as well
 
     @torch.no_grad()
     def apply(self, step: int, *, materialize: bool = True, skip: torch.Tensor | None = None):
@@ -695,14 +763,17 @@ class QKClipController:
         group = getattr(active[0][0], "_kimi_qk_group", None)
         if group is not None and torch.distributed.is_initialized() and torch.distributed.get_world_size(group) > 1:
             torch.distributed.all_reduce(scales, op=torch.distributed.ReduceOp.MAX, group=group)
+        # replicas (data parallel) and shards (fully sharded) of one matrix must take the same factor
+        if self.replica_group is not None and torch.distributed.get_world_size(self.replica_group) > 1:
+            torch.distributed.all_reduce(scales, op=torch.distributed.ReduceOp.MAX, group=self.replica_group)
         corr = torch.where(scales > self.threshold, self.threshold / scales.clamp_min(self.eps),
                            torch.ones_like(scales)).clamp(max=1.0)
         if skip is not None:  # the optimizer step was suppressed on the device: no clipping either
             corr = torch.where(skip, torch.ones_like(corr), corr)
         sym = corr.sqrt()
         for i, (_, wq, wk) in enumerate(active):
-            wq.mul_(sym[i].to(wq.dtype))
-            wk.mul_(sym[i].to(wk.dtype))
+            for w in (wq, wk):
+                (w.to_local() if _is_dtensor(w) else w).mul_(sym[i].to(w.dtype))
         self._pending = (scales, corr, len(self.layers))
         return self.report() if materialize else None
 
@@ -751,6 +822,7 @@ def _all_finite(tensors) -> torch.Tensor:
     """Single device boolean: every tensor is finite."""
     if not tensors:
         return torch.ones((), dtype=torch.bool)
+    tensors = [t.to_local() if _is_dtensor(t) else t for t in tensors]  # a shard is finite iff its rows are
     norms = torch._foreach_norm([t.float() if t.dtype not in (torch.float32, torch.float64) else t
                                  for t in tensors], 2.0)
     return torch.isfinite(torch.stack(norms)).all()
@@ -933,7 +1005,7 @@ def build_kimi_optimizer(model, config: KimiOptimizerConfig | None = None):
     reg = build_parameter_registry(model, kind=config.kind, strict=config.fail_on_unclassified_matrix)
     decay = [s.parameter for s in reg.specs if s.optimizer_family == "adamw_decay"]
     no_decay = [s.parameter for s in reg.specs if s.optimizer_family == "adamw_no_decay"]
-    fused = bool(decay + no_decay) and all(p.is_cuda for p in decay + no_decay)
+    fused = bool(decay + no_decay) and all(p.is_cuda and not _is_dtensor(p) for p in decay + no_decay)
     groups = [{"params": decay, "weight_decay": config.weight_decay, "group_name": "adamw_decay"},
               {"params": no_decay, "weight_decay": 0.0, "group_name": "adamw_no_decay"}]
     if config.kind == "adamw":
@@ -963,6 +1035,8 @@ def build_weight_mirror(model):
     reads them as one matrix)."""
     from .. import ops
     from ..ops.mirror import WeightMirror
+    if any(_is_dtensor(p) for p in model.parameters()):
+        return None  # fully sharded: weights exist whole only while their unit runs
     weights, seen = [], set()
     for mod in model.modules():
         cands = []

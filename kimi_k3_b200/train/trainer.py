@@ -129,8 +129,11 @@ def train_kimiK3(*, model, train_loader=None, train_loader_factory=None, val_loa
         model.to(dev)
         if dcfg.data_parallel.mode == "fsdp" and (use_ema or ema is not None):
             raise ValueError("EMA is unsupported with the sharded (fsdp) data-parallel mode")
-        if dcfg.data_parallel.mode != "fsdp":
-            plan.broadcast_parameters()
+        plan.broadcast_parameters()
+        if dcfg.data_parallel.mode == "fsdp":
+            # parameters, gradients and optimizer state sharded over the data-parallel group
+            from ..parallel.fsdp import shard_kimi_model
+            shard_kimi_model(model, dcfg, ctx)
     raw_cfg = getattr(model, "config", None)
     if train_loader is not None and train_loader_factory is not None:
         raise ValueError("pass train_loader or train_loader_factory, not both")
@@ -161,17 +164,20 @@ def train_kimiK3(*, model, train_loader=None, train_loader_factory=None, val_loa
     if plan is not None:
         grad_sync, grad_norm = plan.sync_gradients, plan.grad_norm
     if dcfg.enabled and dcfg.data_parallel.mode == "fsdp":
-        from ..parallel.zero import ZeroDataParallel
-        zero = ZeroDataParallel(model, optimizer, ctx.dp_group, bucket_mb=dcfg.data_parallel.bucket_mb)
-        zero.broadcast_parameters()
-        step_optimizer, grad_norm = zero, zero.grad_norm
+        from ..parallel.fsdp import sharded_grad_norm
         reducers = list(plan.reducers) if plan is not None else []
+        params_all = [p for p in model.parameters() if p.requires_grad]
 
-        def grad_sync():  # experts / TP-partial reducers of the plan, then the owner reduction
+        def grad_sync():  # the sharded gradients were reduce-scattered in backward; other groups here
             for r in reducers:
                 if r.group is not ctx.dp_group:
                     r.all_reduce_gradients()
-            zero.reduce_gradients()
+
+        def grad_norm():
+            return sharded_grad_norm(params_all)
+        qk = getattr(optimizer, "qk_clip", None)
+        if qk is not None:
+            qk.replica_group = ctx.dp_group
     if total_steps is None:
         per_epoch = math.ceil(_loader_batches(train_loader, tc.max_batches_per_epoch) / tc.gradient_accumulation_steps)
         total_steps = max(per_epoch * tc.epochs, 1)

@@ -38,13 +38,14 @@ def _train(model, batch, kind, *, context=None, plan=None, steps=1, zero=False):
     # a large AdamW epsilon keeps the update linear in tiny gradients, whose float32 rounding
     # (the vocabulary-parallel logits) would otherwise be amplified to full-size updates
     opt, _ = build_kimi_optimizer(model, KimiOptimizerConfig(kind=kind, adamw_lr=1e-3, muon_lr=1e-2, adamw_eps=1e-2))
-    if zero:
+    if zero:  # fully sharded: gradients were reduce-scattered in backward
         from kimi_k3_b200.parallel.data_parallel import QBReducer
-        from kimi_k3_b200.parallel.zero import ZeroDataParallel
-        zdp = ZeroDataParallel(model, opt, context.dp_group)
-        zdp.broadcast_parameters()
+        from kimi_k3_b200.parallel.fsdp import sharded_grad_norm
+        params = [p for p in model.parameters() if p.requires_grad]
         ctl = MoEController(model, reducer=QBReducer(context.dp_group))
-        opt, sync, norm = zdp, zdp.reduce_gradients, zdp.grad_norm
+        if getattr(opt, "qk_clip", None) is not None:
+            opt.qk_clip.replica_group = context.dp_group
+        sync, norm = None, (lambda: sharded_grad_norm(params))
     else:
         ctl = MoEController(model, reducer=None if plan is None else plan.qb_reducer())
         sync = None if plan is None else plan.sync_gradients
@@ -84,9 +85,15 @@ def _rank(rank, world, layout, kind, qb):
     ctx = setup_distributed(dcfg)
     model = _model(qb)
     plan = None
+    shard_bytes = None
     if layout != "fsdp":
         plan = parallelize_kimi_model(model, dcfg, ctx)
         plan.broadcast_parameters()
+    else:
+        from kimi_k3_b200.parallel.fsdp import local_shard_bytes, shard_kimi_model
+        full_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
+        shard_kimi_model(model, dcfg, ctx)
+        shard_bytes = local_shard_bytes(model) / full_bytes
     full = _global_batch(world)
     data_replicas = world if layout in ("dp", "ep", "fsdp") else 1
     if data_replicas > 1:
@@ -94,8 +101,11 @@ def _rank(rank, world, layout, kind, qb):
     else:
         batch = full
     res = _train(model, batch, kind, context=ctx, plan=plan, steps=2, zero=layout == "fsdp")
-    out = {n: p.detach().clone() for n, p in model.named_parameters()
+    out = {n: (p.full_tensor() if hasattr(p, "full_tensor") else p).detach().clone()
+           for n, p in model.named_parameters()
            if not getattr(p, "_kimi_tp_shard", False) and not getattr(p, "_kimi_local_expert", False)}
+    if shard_bytes is not None:
+        out["__shard_fraction__"] = torch.tensor(shard_bytes)
     experts = {n: p.detach().clone() for n, p in model.named_parameters() if getattr(p, "_kimi_local_expert", False)}
     ctx.close()
     return res["loss"], out, experts
@@ -123,6 +133,9 @@ def test_parallel_layout_matches_single_process(layout, kind):
     for loss, params, experts in results:
         # the single-process CPU loss is reduced in float32 (its logits are float32)
         assert abs(loss - ref_loss) < max(tol, 1e-6), (layout, loss, ref_loss)
+        if layout == "fsdp":  # each rank holds about 1/world of the parameters
+            frac = float(params.pop("__shard_fraction__"))
+            assert frac < 0.6, frac
         assert _compare(ref_params, params, tol) < tol, layout
     if layout in ("ep", "tp_ep_overlay"):
         # each rank's local experts equal the matching slice of the single-process experts
