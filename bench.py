@@ -18,10 +18,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import statistics
-import subprocess
 import sys
-import threading
 import time
 
 import torch
@@ -34,103 +31,9 @@ METRIC = "train_tokens_per_s"
 
 
 # --------------------------------------------------------------------------- helpers
-class ClockSampler:
-    """Samples SM clocks and throttle reasons with nvidia-smi while the timed region runs."""
-
-    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
-
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.lines: list[str] = []
-        self.thread = None
-
-    def start(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except (FileNotFoundError, OSError):
-            self.proc = None
-            return
-        self.thread = threading.Thread(target=self._read, daemon=True)
-        self.thread.start()
-
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
-    def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        if self.thread is not None:
-            self.thread.join(timeout=2)
-        sm, mx, reasons = [], [], set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 7:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                mx.append(float(parts[1]))
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[3:7]):
-                if val.lower().startswith("active"):
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
-
-
-def dist_env():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return world, rank, local
-
-
-def init_dist(world, local):
-    torch.cuda.set_device(local)
-    if world > 1 and not torch.distributed.is_initialized():
-        from datetime import timedelta
-        torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=600),
-                                             device_id=torch.device("cuda", local))
-
-
-def max_over_ranks(value: float) -> float:
-    if torch.distributed.is_initialized():
-        t = torch.tensor([value], device="cuda", dtype=torch.float64)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        return float(t.item())
-    return value
-
-
-def barrier():
-    if torch.distributed.is_initialized():
-        torch.distributed.barrier()
-
-
-def make_batches(n, batch, seq, vocab, seed, device=None, pin=False):
-    g = torch.Generator().manual_seed(seed)
-    out = []
-    for _ in range(n):
-        ids = torch.randint(0, vocab, (batch, seq + 1), generator=g)
-        b = {"input_ids": ids[:, :-1].contiguous(), "labels": ids[:, 1:].contiguous(),
-             "attention_mask": torch.ones(batch, seq, dtype=torch.bool)}
-        if pin:
-            b = {k: v.pin_memory() for k, v in b.items()}
-        if device is not None:
-            b = {k: v.to(device) for k, v in b.items()}
-        out.append(b)
-    return out
+sys.path.insert(0, ROOT)
+from kimi_k3_b200.bench.harness import (ClockSampler, barrier, dist_env, init_dist,  # noqa: E402
+                                        make_batches, max_over_ranks)
 
 
 def optimizer_settings():
@@ -303,6 +206,23 @@ def run_reference(args, world, rank, local, amp=True):
     return ms, e2e_ms, clocks, h2d, None, None, None
 
 
+# --------------------------------------------------------------------------- other configurations
+def run_suite_config(args, world, rank, local):
+    from kimi_k3_b200.bench.suite import run_config
+    try:
+        line = run_config(args, world, rank, local)
+    except Exception as exc:
+        if args.impl != "reference":
+            raise
+        line = {"impl": "reference", "bench_config": args.config,
+                "unavailable": f"{type(exc).__name__}: {exc}"[:300]}
+        if torch.distributed.is_initialized():
+            torch.distributed.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+    return 0
+
+
 # --------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
@@ -312,12 +232,18 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--batch-per-gpu", type=int, default=16)
     ap.add_argument("--no-graph", action="store_true", help="eager steps instead of one CUDA graph per step")
+    ap.add_argument("--config", default="t4", choices=("t4", "cpu_smoke", "gpu24_tp_ep", "gpu48_fsdp", "gpu80_infer"),
+                    help="t4 (default): the flagship t4_wikitext-shaped training step; the others are described in "
+                         "kimi_k3_b200/bench/suite.py")
+    ap.add_argument("--decode-steps", type=int, default=512, help="gpu80_infer: greedy decode steps per generation")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     world, rank, local = dist_env()
-    if world != args.gpus:
+    if world != args.gpus and args.config != "cpu_smoke":
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torch.distributed.run")
+    if args.config != "t4":
+        return run_suite_config(args, world, rank, local)
     base = {"metric": METRIC, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "dtype": "bf16",
             "data": "synthetic uniform token ids (seeded), random-init weights",

@@ -66,8 +66,13 @@ def cmd_train(args) -> int:
 
 
 def cmd_infer(args) -> int:
-    import torch
-    from .infer import GenerationConfig, inference_autoregressive, load_generation_config, load_kimi_checkpoint
+    """Generate from a checkpoint.  An inference YAML with ``distributed.enabled`` shards the model
+    over the torchrun ranks (TP / EP) before generating; every rank generates, rank 0 prints."""
+    from dataclasses import replace
+    from .infer import GenerationConfig, load_inference_yaml_config
+    from .infer.distributed import run_distributed_generation
+    from .infer.yaml_config import InferenceYamlConfig
+    from .parallel.config import DistributedConfig
     model_p = Path(args.model_config) if args.model_config else _profile_paths(args.profile).model
     tok = None
     if args.data_config or args.profile:
@@ -77,17 +82,25 @@ def cmd_infer(args) -> int:
                                                 else _profile_paths(args.profile).data)
         except FileNotFoundError:
             tok = None
-    loaded = load_kimi_checkpoint(model_p, args.checkpoint, tokenizer=tok)
-    gen = load_generation_config(args.inference_config) if args.inference_config else GenerationConfig(
-        max_new_tokens=args.max_new_tokens)
+    if args.inference_config:
+        iy = load_inference_yaml_config(args.inference_config)
+    else:
+        iy = InferenceYamlConfig(GenerationConfig(max_new_tokens=32), DistributedConfig(), None)
+    if args.max_new_tokens is not None:
+        iy = replace(iy, generation=replace(iy.generation, max_new_tokens=args.max_new_tokens))
     prompt = args.prompt
     if tok is None:
         prompt = [int(x) for x in prompt.split()]
-    with torch.inference_mode():
-        out = inference_autoregressive(loaded.model, prompt, tokenizer=tok, generation_config=gen)
-    print(out.text if out.text is not None else out.sequences.tolist())
-    print(json.dumps({"prefill_seconds": out.prefill_seconds, "decode_seconds": out.decode_seconds,
-                      "tokens_per_second": out.tokens_per_second, "finish_reason": out.finish_reason}))
+    out, ctx = run_distributed_generation(model_p, args.checkpoint, prompt, iy, tokenizer=tok,
+                                          precision=args.precision, use_graph=args.graph)
+    try:
+        if ctx.is_global_zero:
+            print(out.text if out.text is not None else out.sequences.tolist())
+            print(json.dumps({"prefill_seconds": out.prefill_seconds, "decode_seconds": out.decode_seconds,
+                              "tokens_per_second": out.tokens_per_second, "finish_reason": out.finish_reason,
+                              "world_size": ctx.world_size}))
+    finally:
+        ctx.close()
     return 0
 
 
@@ -162,7 +175,11 @@ def build_parser() -> argparse.ArgumentParser:
             p.add_argument("--checkpoint", required=True)
             p.add_argument("--prompt", required=True)
             p.add_argument("--inference-config")
-            p.add_argument("--max-new-tokens", type=int, default=32)
+            p.add_argument("--max-new-tokens", type=int, default=None,
+                           help="overrides the inference YAML (default 32 without one)")
+            p.add_argument("--precision", choices=("model", "fp32", "bf16", "fp16"), default="model")
+            p.add_argument("--graph", action="store_true",
+                           help="serve the decode loop from one captured CUDA graph per token")
     sub.add_parser("smoke")
     pp = sub.add_parser("profiles")
     pp.add_argument("--output", default="configs/kimi_full_pipeline")

@@ -39,13 +39,27 @@ from .generation import GenerationOutput, last_prompt_logits
 from .sampling import sample_next_token
 
 
-def serving_copy(model: nn.Module, dtype: torch.dtype) -> nn.Module:
-    """A copy of ``model`` whose projection matrices (every ``nn.Linear`` weight and the stacked
-    routed-expert weights) are stored in ``dtype``, so decode steps under autocast read them
-    without a per-step cast.  Embeddings, norms, conv and decay parameters keep their dtype; a
-    LM head tied to the embedding gets its own ``dtype`` copy."""
+def _shared_handles(model: nn.Module) -> dict:
+    """Deep-copy memo that keeps process groups and symmetric-memory workspaces shared: they are
+    process-wide rendezvous objects (a copy of a sharded model talks to the same peers)."""
+    import torch.distributed as dist
+    memo = {}
+    kinds = (dist.ProcessGroup,) if dist.is_available() else ()
+    for mod in model.modules():
+        for value in vars(mod).values():
+            if (kinds and isinstance(value, kinds)) or getattr(value, "_kimi_rendezvous", False):
+                memo[id(value)] = value
+    return memo
+
+
+def serving_copy(model: nn.Module, dtype: torch.dtype, *, inplace: bool = False) -> nn.Module:
+    """``model`` (or a copy of it, unless ``inplace``) with its projection matrices (every
+    ``nn.Linear`` weight and the stacked routed-expert weights) stored in ``dtype``, so decode
+    steps under autocast read them without a per-step cast.  Embeddings, norms, conv and decay
+    parameters keep their dtype; a LM head tied to the embedding gets its own ``dtype`` copy.
+    Process groups and peer-memory workspaces of a sharded model are shared, not copied."""
     from ..models.moe import GroupedRoutedExperts
-    m = copy.deepcopy(model)
+    m = model if inplace else copy.deepcopy(model, _shared_handles(model))
     for mod in m.modules():
         if isinstance(mod, nn.Linear):
             mod.weight = nn.Parameter(mod.weight.detach().to(dtype), requires_grad=False)
@@ -86,17 +100,20 @@ class GraphDecoder:
     ``max_length`` bounds prompt + generated tokens (the MLA latent buffers are sized for it).
     ``autocast_dtype`` (bf16 by default on CUDA, None to disable) is the compute dtype of the
     prefill and of every decode step; with it the decoder serves from :func:`serving_copy` of the
-    model (projection matrices stored in that dtype)."""
+    model (projection matrices stored in that dtype; ``copy_model=False`` converts the model itself
+    instead of a copy, for a model loaded only to serve)."""
 
     def __init__(self, model, *, max_length: int, generation_config: GenerationConfig | None = None,
-                 use_graph: bool | None = None, autocast_dtype: torch.dtype | None = torch.bfloat16):
+                 use_graph: bool | None = None, autocast_dtype: torch.dtype | None = torch.bfloat16,
+                 copy_model: bool = True):
         self.max_length = int(max_length)
         self.cfg = generation_config or GenerationConfig()
         dev = next(model.parameters()).device
         self.device = dev
         self.use_graph = (dev.type == "cuda") if use_graph is None else bool(use_graph and dev.type == "cuda")
         self.autocast_dtype = autocast_dtype if dev.type == "cuda" else None
-        self.model = serving_copy(model, self.autocast_dtype) if self.autocast_dtype is not None else model
+        self.model = (serving_copy(model, self.autocast_dtype, inplace=not copy_model)
+                      if self.autocast_dtype is not None else model)
         self.graph = None
         self.replays = 0
 

@@ -34,6 +34,8 @@ def _align(n: int) -> int:
 class EPWorkspace:
     """Symmetric buffers of one expert-parallel MoE layer (collective construction)."""
 
+    _kimi_rendezvous = True  # one per process and peer set: model copies share it, never copy it
+
     def __init__(self, group, device, *, tokens: int, top_k: int, latent: int, num_experts: int,
                  timeout_s: float = 10.0):
         import torch.distributed._symmetric_memory as symm_mem

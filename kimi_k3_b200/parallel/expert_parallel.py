@@ -25,6 +25,10 @@ from .data_parallel import QBReducer
 from .tensor_parallel import group_rank, group_size
 
 
+# inference-time fused-exchange workspaces shared by all MoE layers of one shape
+_SHARED_WORKSPACES: dict = {}
+
+
 def expert_range(num_experts: int, group) -> tuple:
     size, rank = group_size(group), group_rank(group)
     if num_experts % size:
@@ -117,6 +121,7 @@ class ExpertParallelMoE(StableLatentMoE):
         # CUDA ranks: device-initiated NVLink exchange (``ep_fused``) instead of NCCL all-to-alls
         self.fused_comm = bool(fused_comm)
         self._ep_workspace = None
+        self._token_block = None
         # EP overlaid on TP: the group shares one token stream, so each rank takes a block of
         # the tokens, and the replicated MoE weights see only that block (sum over the group).
         self.token_split = bool(token_split)
@@ -134,7 +139,11 @@ class ExpertParallelMoE(StableLatentMoE):
         blk = -(-m // n)
         s, e = min(r * blk, m), min((r + 1) * blk, m)
         local = _TakeRows.apply(flat, self.group, s, e, blk * n)
-        out = super().forward(local, **kw)
+        self._token_block = blk  # equal on every rank: the fused exchange's row capacity
+        try:
+            out = super().forward(local, **kw)
+        finally:
+            self._token_block = None
         hidden = out if torch.is_tensor(out) else out.hidden_states
         full = _GatherRows.apply(hidden, self.group, m, blk * n).reshape(shape)
         if torch.is_tensor(out):
@@ -160,26 +169,59 @@ class ExpertParallelMoE(StableLatentMoE):
                 return scores, cutoffs
         return super().finalize_and_commit_balance(_Chain(self._qb_reducer, reducer), keep_old=keep_old)
 
+    @property
+    def device_exchange(self) -> bool:
+        """True when routed rows move through the device-initiated NVLink exchange: no host
+        synchronisation, so the layer can run inside a captured CUDA graph."""
+        c = self.config
+        return (self.fused_comm and self.routed_experts.gate_proj.is_cuda and c.latent_dim % 64 == 0
+                and c.routed_expert_hidden_dim % 128 == 0 and c.routed_accumulation_dtype == "float32")
+
     def _fused_workspace(self, tokens: int, top_k: int, latent: int):
+        """The symmetric buffers of the fused exchange for ``tokens`` rows per rank.  Training keeps
+        one per layer (backward reads the rows its forward dispatched); without autograd every layer
+        of the same shape shares one from a process-wide pool, since layers run one after another."""
         from .ep_fused import EPWorkspace
-        ws = self._ep_workspace
+        key = (id(self.group), tokens, top_k, latent, self.config.num_routed_experts)
+        shared = not torch.is_grad_enabled()
+        ws = _SHARED_WORKSPACES.get(key) if shared else self._ep_workspace
         if ws is None or ws.tokens != tokens or ws.top_k != top_k or ws.latent != latent:
             if torch.cuda.is_current_stream_capturing():
                 raise RuntimeError("the expert-parallel workspace must exist before CUDA-graph capture")
             ws = EPWorkspace(self.group, torch.device("cuda", torch.cuda.current_device()), tokens=tokens, top_k=top_k,
                              latent=latent, num_experts=self.config.num_routed_experts)
-            self._ep_workspace = ws
+            if shared:
+                _SHARED_WORKSPACES[key] = ws
+            else:
+                self._ep_workspace = ws
         return ws
+
+    def _fused_routed(self, latent, ro):
+        """The fused exchange over a row count that is the same on every rank (the exchange encodes
+        source rows as ``rank * rows + row``): with the token split, rows are padded to the block
+        size with zero-weight assignments whose results are dropped."""
+        from .ep_fused import fused_ep_experts
+        m, l = latent.shape
+        sel, w = ro.selected_experts, ro.selected_weights
+        k = sel.shape[1]
+        cap = self._token_block if self._token_block is not None else m
+        if cap > m:
+            pad = cap - m
+            e = self.config.num_routed_experts
+            latent = torch.cat((latent, latent.new_zeros(pad, l)), 0)
+            fill = (torch.arange(pad * k, device=sel.device) % e).view(pad, k).to(sel.dtype)
+            sel = torch.cat((sel, fill), 0)
+            w = torch.cat((w, w.new_zeros(pad, k)), 0)
+        ws = self._fused_workspace(cap, k, l)
+        out = fused_ep_experts(latent, sel, w, self.routed_experts, ws, self.config.beta_gate, self.config.beta_up)
+        return out[:m] if cap > m else out
 
     def routed_aggregate(self, latent, ro, accumulation_dtype):
         m, l = latent.shape
         k = ro.selected_experts.shape[1]
         if (self.fused_comm and _ops.use_kernels(latent) and accumulation_dtype == torch.float32 and l % 64 == 0
                 and self.config.routed_expert_hidden_dim % 128 == 0):
-            from .ep_fused import fused_ep_experts
-            ws = self._fused_workspace(m, k, l)
-            return fused_ep_experts(latent, ro.selected_experts, ro.selected_weights, self.routed_experts, ws,
-                                    self.config.beta_gate, self.config.beta_up)
+            return self._fused_routed(latent, ro)
         group, world = self.group, group_size(self.group)
         per = self.expert_end - self.expert_start
         flat_e = ro.selected_experts.reshape(-1).long()

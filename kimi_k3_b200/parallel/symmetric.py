@@ -37,6 +37,8 @@ class SymmetricWorkspace:
     Construction and :meth:`grow` are collective over the group (every rank must call them with
     the same sizes, in the same order)."""
 
+    _kimi_rendezvous = True  # one per process and peer set: model copies share it, never copy it
+
     def __init__(self, group=None, device=None, partial_bytes: int = 1 << 24, *, use_multicast: bool = True):
         self.group = group if group is not None else dist.group.WORLD
         self.device = torch.device(device if device is not None else "cuda", torch.cuda.current_device()) \
@@ -189,6 +191,8 @@ class FusedRowParallelOutput(torch.nn.Module):
 class AllGatherWorkspace:
     """Symmetric ``[row shard | flags]`` buffer for :func:`fused_allgather_matmul` (collective
     construction): each rank's bf16 shard ``[rows, cols]`` is read by every rank's GEMM."""
+
+    _kimi_rendezvous = True  # one per process and peer set: model copies share it, never copy it
 
     _FLAGS = 1 << 12
 

@@ -82,7 +82,7 @@ class TrainStepEngine:
 
     def __init__(self, model, optimizer, *, scheduler=None, grad_clip: float | None = 1.0,
                  amp_dtype: torch.dtype | None = torch.bfloat16, use_mtp: bool = True, moe_controller=None,
-                 grad_hook=None, cuda_graph: bool = False, graph_warmup: int = 2):
+                 grad_hook=None, cuda_graph: bool = False, graph_warmup: int = 2, grad_norm_fn=None):
         self.model = model
         self.optimizer = optimizer
         self.scheduler = scheduler
@@ -91,6 +91,9 @@ class TrainStepEngine:
         self.use_mtp = use_mtp
         self.moe_controller = moe_controller
         self.grad_hook = grad_hook  # called after backward (gradient reduction in data parallel)
+        # global gradient norm of a parallel plan (tensor / expert shards counted once, FSDP shards
+        # all-reduced); None: the norm of this process's gradients
+        self.grad_norm_fn = grad_norm_fn
         self.device = next(model.parameters()).device
         self._params = [p for p in model.parameters() if p.requires_grad]
         self.cuda_graph = bool(cuda_graph) and self.device.type == "cuda"
@@ -130,7 +133,7 @@ class TrainStepEngine:
             out.loss.backward()
             if self.grad_hook is not None:
                 self.grad_hook()
-            gnorm = clip_grad_norm_device(self._params, self.grad_clip)
+            gnorm = self._clip()
             report = self.optimizer.step()
             executed = bool(getattr(report, "executed", True))
         except BaseException:
@@ -152,6 +155,17 @@ class TrainStepEngine:
         lo = out.loss_output
         return StepOutput(out.loss.detach(), lo.ntp.loss.detach(), None if lo.mtp is None else lo.mtp.loss.detach(),
                           gnorm, executed)
+
+    def _clip(self) -> torch.Tensor:
+        if self.grad_norm_fn is None:
+            return clip_grad_norm_device(self._params, self.grad_clip)
+        total = self.grad_norm_fn()
+        if self.grad_clip is not None:
+            grads = [p.grad.to_local() if hasattr(p.grad, "to_local") else p.grad
+                     for p in self._params if p.grad is not None]
+            if grads:
+                torch._foreach_mul_(grads, (self.grad_clip / (total + 1e-6)).clamp(max=1.0))
+        return total
 
     # ------------------------------------------------------------------ kernel status
     def _status_snapshot(self):
@@ -205,7 +219,7 @@ class TrainStepEngine:
             out.loss.backward()
             if self.grad_hook is not None:
                 self.grad_hook()
-            gnorm = clip_grad_norm_device(self._params, self.grad_clip)
+            gnorm = self._clip()
             found_inf = ~torch.isfinite(gnorm)
             self.optimizer.step(found_inf=found_inf)
             if self.moe_controller is not None:
