@@ -353,6 +353,19 @@ void cast_bf16_multi(at::Tensor tables, int64_t tensors, int64_t total_vec) {
         "cast_bf16_multi");
 }
 
+// Newton-Schulz polynomial P = c * G2 + b * G + a * I of stacked [m, m] Gram matrices (bf16 [rows, m]).
+at::Tensor ns_poly(at::Tensor g, at::Tensor g2, double a, double b, double c) {
+  TORCH_CHECK(g.is_cuda() && g.scalar_type() == at::kBFloat16 && g.dim() == 2 && g.is_contiguous() &&
+                  g2.sizes() == g.sizes() && g2.scalar_type() == at::kBFloat16 && g2.is_contiguous(),
+              "ns_poly: contiguous bf16 [rows, m] Gram matrices");
+  const at::cuda::CUDAGuard gd(g.device());
+  at::Tensor out = at::empty_like(g);
+  check(kimi::ns_poly(g.data_ptr(), g2.data_ptr(), out.data_ptr(), g.size(0), (int)g.size(1), (float)a, (float)b,
+                      (float)c, stream()),
+        "ns_poly");
+  return out;
+}
+
 // ---------------------------------------------------------------- fused Muon passes
 void muon_momentum(at::Tensor g, at::Tensor mom, at::Tensor x, at::Tensor sumsq, double momentum, bool nesterov,
                    c10::optional<at::Tensor> skip) {
@@ -1227,6 +1240,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tcs_selftest", &tcs_selftest);
   m.def("muon_momentum", &muon_momentum);
   m.def("cast_bf16_multi", &cast_bf16_multi);
+  m.def("ns_poly", &ns_poly);
   m.def("muon_normalize", &muon_normalize);
   m.def("muon_apply", &muon_apply);
   m.def("kda_phase_profile", &kimi::kda_phase_profile);

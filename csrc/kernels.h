@@ -96,6 +96,10 @@ int kda_tc_status(bool clear);
 // element counts and the prefix sums of ceil(numel / 8) (tensors + 1 entries); 16-byte aligned tensors.
 cudaError_t cast_bf16_multi(const float* const* src, void* const* dst, const int64_t* numel, const int64_t* vec_off,
                             int tensors, int64_t total_vec, cudaStream_t s);
+// Newton-Schulz polynomial c * G2 + b * G + a * I over a batch of [m, m] matrices stacked as
+// [rows, m] (bf16, m a multiple of 8, 16-byte aligned).
+cudaError_t ns_poly(const void* g, const void* g2, void* out, int64_t rows, int m, float a, float b, float c,
+                    cudaStream_t s);
 // Device address of the current device's default KDA status word (for stream-ordered reads).
 int* kda_tc_default_status();
 

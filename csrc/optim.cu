@@ -206,7 +206,47 @@ __global__ void __launch_bounds__(kThreads) cast_bf16_multi_kernel(const float* 
   }
 }
 
+// Newton-Schulz polynomial of a batch of Gram matrices: P = c * G2 + b * G + a * I (bf16 in and out,
+// fp32 arithmetic, one rounding).  G and G2 are [batch * m, m] row-major; one thread per 8 columns.
+__global__ void __launch_bounds__(kThreads) ns_poly_kernel(const __nv_bfloat16* __restrict__ g,
+                                                           const __nv_bfloat16* __restrict__ g2,
+                                                           __nv_bfloat16* __restrict__ out, int64_t rows, int m,
+                                                           float a, float b, float c) {
+  const int per_row = m >> 3;
+  const int64_t total = rows * per_row;
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < total; v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = v / per_row;
+    const int c0 = (int)(v - r * per_row) * 8;
+    const int diag = (int)(r % m);
+    Vec<__nv_bfloat16> x, y, o;
+    x.load(g + r * m + c0);
+    y.load(g2 + r * m + c0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float val = c * __bfloat162float(y.v[i]) + b * __bfloat162float(x.v[i]);
+      if (c0 + i == diag) val += a;
+      o.v[i] = __float2bfloat16_rn(val);
+    }
+    o.store(out + r * m + c0);
+  }
+}
+
 }  // namespace
+
+cudaError_t ns_poly(const void* g, const void* g2, void* out, int64_t rows, int m, float a, float b, float c,
+                    cudaStream_t s) {
+  if (rows <= 0 || m <= 0) return cudaSuccess;
+  if ((m & 7) || (reinterpret_cast<uintptr_t>(g) & 15) || (reinterpret_cast<uintptr_t>(g2) & 15) ||
+      (reinterpret_cast<uintptr_t>(out) & 15))
+    return cudaErrorInvalidValue;
+  int64_t blocks = (rows * (m >> 3) + kThreads - 1) / kThreads;
+  const int64_t cap = (int64_t)device_sms() * 16;
+  if (blocks > cap) blocks = cap;
+  ns_poly_kernel<<<(int)blocks, kThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(g),
+                                                  static_cast<const __nv_bfloat16*>(g2),
+                                                  static_cast<__nv_bfloat16*>(out), rows, m, a, b, c);
+  return cudaGetLastError();
+}
 
 cudaError_t cast_bf16_multi(const float* const* src, void* const* dst, const int64_t* numel, const int64_t* vec_off,
                             int tensors, int64_t total_vec, cudaStream_t s) {

@@ -133,6 +133,8 @@ def newton_schulz_iterations(w: torch.Tensor, steps: int, *, transpose_out: bool
     takes the ``a I`` term on its diagonal, so the big product is a plain batched GEMM (no copy of
     X into the output as ``a X + P X`` would need).  ``transpose_out`` returns ``X^T`` [N, n, m]
     contiguous, computed by the last step as ``X^T P`` (P is symmetric) instead of a transpose copy."""
+    if _ns_on_tensor_cores(w):
+        return _ns_iterations_tc(w, steps, transpose_out)
     a, b, c = NS_COEFFS
     for i in range(steps):
         gram = w @ w.transpose(-2, -1)
@@ -142,6 +144,48 @@ def newton_schulz_iterations(w: torch.Tensor, steps: int, *, transpose_out: bool
             return torch.bmm(w.transpose(-2, -1), poly)
         w = torch.bmm(poly, w)
     return w.transpose(-2, -1).contiguous() if transpose_out else w
+
+
+def _ns_on_tensor_cores(w: torch.Tensor) -> bool:
+    from .. import ops
+    return (w.is_cuda and w.dtype == torch.bfloat16 and w.ndim == 3 and w.shape[-1] % 8 == 0 and w.numel() > 0
+            and ops.use_kernels(w))
+
+
+_NS_OFFSETS: dict = {}
+
+
+def _ns_iterations_tc(w: torch.Tensor, steps: int, transpose_out: bool) -> torch.Tensor:
+    """The quintic iterations on this package's grouped tcgen05 GEMM (bf16 operands, fp32
+    accumulation).  Each matrix of the batch is one row segment of the grouped product, padded to
+    a multiple of 128 rows with zeros; the padding stays zero through every step (its rows of
+    ``P = a I + b G + c G^2`` are ``a e_i`` and meet zero rows of X).  Per step: ``G = X X^T`` and
+    ``G2 = G G^T`` (G is symmetric) with both operands K-major, the polynomial in one elementwise
+    kernel, and ``X <- P X`` with X as the MN-major operand."""
+    from ..ops import _loader
+    C = _loader.require()
+    e, m, n = w.shape
+    mp = -(-m // 128) * 128
+    x = torch.zeros(e, mp, n, dtype=torch.bfloat16, device=w.device)
+    x[:, :m].copy_(w)
+    key = (e, mp, w.device)
+    offs = _NS_OFFSETS.get(key)
+    if offs is None:
+        offs = _NS_OFFSETS[key] = (torch.arange(e + 1, dtype=torch.int32) * mp).to(w.device)
+    a, b, c = NS_COEFFS
+    bn_g = 256 if (mp >= 320 or mp % 256 == 0) else 128
+    bn_x = 256 if (n >= 320 or n % 256 == 0) else 128
+    rows = e * mp
+    for _ in range(steps):
+        g = C.tc_gemm_grouped(1, x.view(rows, n), x, None, False, False, offs, rows, mp, n, 0, None, False, 0.0,
+                              0.0, None, None, 0, bn_g)[0]
+        g2 = C.tc_gemm_grouped(1, g, g.view(e, mp, mp), None, False, False, offs, rows, mp, mp, 0, None, False, 0.0,
+                               0.0, None, None, 0, bn_g)[0]
+        poly = C.ns_poly(g, g2, a, b, c)
+        x = C.tc_gemm_grouped(1, poly, x, None, False, True, offs, rows, n, mp, 0, None, False, 0.0, 0.0, None, None,
+                              0, bn_x)[0].view(e, mp, n)
+    out = x[:, :m]
+    return out.transpose(-2, -1) if transpose_out else out
 
 
 @torch.no_grad()

@@ -8,7 +8,8 @@ schedule, EMA, Quantile-Balancing windows, diagnostics, resume from a single or 
 checkpoint, per-epoch evaluation / preview / atomic checkpoints with pruning.
 
 B200 specifics: ``data_parallel.mode`` ``ddp`` uses the overlapped bucketed reducer and
-``fsdp`` the whole-tensor-owner sharded optimizer; the EMA shadow stays on the GPU.
+``fsdp`` shards parameters, gradients and optimizer state per token mixer / FFN unit
+(``parallel/fsdp.py``); the EMA shadow stays on the GPU.
 """
 from __future__ import annotations
 

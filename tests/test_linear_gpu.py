@@ -127,3 +127,37 @@ def test_linear_group_matches_separate_projections(cuda):
     for l, wr in zip(lins, ws):
         assert l.weight.grad.dtype == torch.float32 and _rel(l.weight.grad, wr.grad) < 1e-2
     assert mirror.params  # the group's mirrors were registered
+
+
+def _ns_fp32(w, steps):
+    """The quintic Newton-Schulz iterations in fp32 PyTorch (``a X + (b G + c G^2) X``)."""
+    from kimi_k3_b200.train.optimizer import NS_COEFFS
+    a, b, c = NS_COEFFS
+    x = w.float()
+    for _ in range(steps):
+        g = x @ x.transpose(-2, -1)
+        x = a * x + (b * g + c * g @ g) @ x
+    return x
+
+
+@pytest.mark.parametrize("e,m,n,transposed", [(3, 64, 640, False), (2, 640, 960, False), (4, 320, 640, True),
+                                               (1, 128, 2560, False)])
+def test_newton_schulz_on_tensor_cores(cuda, e, m, n, transposed):
+    """The grouped tcgen05 Newton-Schulz (padded segments, K-major Gram products, MN-major update)
+    against fp32 PyTorch on the same bf16-normalised input; ``transpose_out`` returns X^T."""
+    from kimi_k3_b200.train.optimizer import _ns_on_tensor_cores, newton_schulz_iterations
+    torch.manual_seed(3)
+    raw = torch.randn(e, n, m, device=cuda) if transposed else torch.randn(e, m, n, device=cuda)
+    w = raw.transpose(-2, -1) if transposed else raw
+    w = (w / w.flatten(1).norm(dim=1)[:, None, None]).to(torch.bfloat16)
+    assert _ns_on_tensor_cores(w)
+    got = newton_schulz_iterations(w, 5, transpose_out=transposed).float()
+    want = _ns_fp32(w, 5)
+    if transposed:
+        want = want.transpose(-2, -1)
+    assert got.shape == want.shape
+    err = (got - want).norm() / want.norm()
+    assert err < 3e-2, float(err)
+    # the result is near-orthogonal: singular values inside the quintic's band
+    sv = torch.linalg.svdvals(got.transpose(-2, -1) if transposed else got)
+    assert float(sv.max()) < 1.3 and float(sv.min()) > 0.5
