@@ -731,7 +731,8 @@ std::vector<at::Tensor> tc_gemm_grouped(int64_t mode, at::Tensor a, at::Tensor b
                                         bool a_mn, bool b_mn, at::Tensor offsets, int64_t M, int64_t N, int64_t K,
                                         int64_t epi, c10::optional<at::Tensor> out_opt, bool out_fp32, double bg,
                                         double bu, c10::optional<at::Tensor> row_token,
-                                        c10::optional<at::Tensor> row_weight, int64_t b2_k_split, int64_t bn) {
+                                        c10::optional<at::Tensor> row_weight, int64_t b2_k_split, int64_t bn,
+                                        int64_t uniform_rows) {
   TORCH_CHECK(a.is_cuda() && a.dim() == 2 && a.stride(1) == 1 && a.stride(0) % 8 == 0,
               "a must be a row-major CUDA matrix with a 16-byte aligned row stride");
   CHECK_CUDA_CONTIG(b);
@@ -772,6 +773,9 @@ std::vector<at::Tensor> tc_gemm_grouped(int64_t mode, at::Tensor a, at::Tensor b
   g.K = (int)K;
   g.G = G;
   g.offsets = offsets.data_ptr<int>();
+  TORCH_CHECK(uniform_rows == 0 || (mode == 1 && uniform_rows % 128 == 0 && uniform_rows * G == a.size(0)),
+              "uniform_rows: mode 1 segments of a multiple of 128 rows covering a");
+  g.uniform_rows = (int)uniform_rows;
   g.epi = (int)epi;
   g.bg = (float)bg;
   g.bu = (float)bu;
@@ -1270,7 +1274,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     TORCH_CHECK(v >= 0, "reading the GEMM status word failed");
     return v;
   });
-  m.def("tc_gemm_grouped", &tc_gemm_grouped);
+  m.def("tc_gemm_grouped", &tc_gemm_grouped, py::arg("mode"), py::arg("a"), py::arg("b"), py::arg("b2"),
+        py::arg("a_mn"), py::arg("b_mn"), py::arg("offsets"), py::arg("M"), py::arg("N"), py::arg("K"), py::arg("epi"),
+        py::arg("out"), py::arg("out_fp32"), py::arg("bg"), py::arg("bu"), py::arg("row_token"), py::arg("row_weight"),
+        py::arg("b2_k_split"), py::arg("bn"), py::arg("uniform_rows") = 0);
   m.def("tc_gemm_group", &tc_gemm_group, py::arg("kind"), py::arg("segs"), py::arg("x"), py::arg("w"),
         py::arg("out") = py::none(), py::arg("bn") = 256, py::arg("ksplit") = 1, py::arg("pair") = -1);
   m.def("tc_gemm_comm", &tc_gemm_comm);

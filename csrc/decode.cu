@@ -138,24 +138,27 @@ __global__ void __launch_bounds__(256) kda_decode_kernel(const T* __restrict__ q
 }
 
 // ---------------------------------------------------------------- MLA latent flash decode
-// CTA (split, b): rows [split * rows_per_split, ...) of sequence b, in sub-chunks of 32 rows.
-// Scores: each warp takes 4 rows; a lane accumulates the dot products of its latent columns for
-// every head and the warp reduces.  Context: thread owns latent columns tid, tid + 256, ... and
-// keeps one running accumulator per (head, column).
-constexpr int kMlaRows = 32, kMlaThreads = 256;
+// CTA (split, b): rows [split * rows_per_split, ...) of sequence b, in sub-chunks of ROWS rows kept
+// in shared memory in the cache's own dtype (the chunk is read from HBM once, 16-byte vectors).
+// Scores: each warp takes ROWS / 8 rows; a lane accumulates the dot products of its latent columns
+// for every head and the warp reduces.  Context: thread owns latent columns tid, tid + 256, ... (CPT
+// of them) and keeps one running accumulator per (head, column).  Instances: HMAX heads padded to
+// 4 / 8 / 16 / 32, CPT = ceil(L / 256) rounded to 2 / 4 / 6 / 8, ROWS 32 (L <= 1024) or 16.
+constexpr int kMlaThreads = 256;
 
-template <typename T, int HMAX, int CPT>
+template <typename T, int HMAX, int CPT, int ROWS>
 __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(const float* __restrict__ qlat,
                                                                  const T* __restrict__ latent,
                                                                  const int32_t* __restrict__ lengths, int heads,
                                                                  int ldim, int64_t tmax, int rows_per_split,
                                                                  float* __restrict__ part_acc,
                                                                  float* __restrict__ part_ml) {
+  constexpr int RPW = ROWS / 8;  // rows per warp in the score phase
   extern __shared__ __align__(16) float smem[];
-  float* sq = smem;                                      // [heads][ldim]
-  float* sx = sq + heads * ldim;                         // [kMlaRows][ldim]
-  float* sp = sx + kMlaRows * ldim;                      // [kMlaRows][HMAX] scores, then weights
-  float* sstat = sp + kMlaRows * HMAX;                   // [HMAX] running max, [HMAX] sum, [HMAX] scale
+  float* sq = smem;                                            // [heads][ldim] fp32
+  T* sx = reinterpret_cast<T*>(sq + heads * ldim);            // [ROWS][ldim] cache dtype
+  float* sp = reinterpret_cast<float*>(sx + ROWS * ldim);     // [ROWS][HMAX] scores, then weights
+  float* sstat = sp + ROWS * HMAX;                             // [HMAX] running max, [HMAX] sum, [HMAX] scale
   const int split = blockIdx.x, b = blockIdx.y, nsplit = gridDim.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int len = (int)min((int64_t)lengths[b], tmax);
@@ -177,45 +180,39 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(const float* __
 #pragma unroll
     for (int h = 0; h < HMAX; ++h) acc[c][h] = 0.f;
   const T* xb = latent + (int64_t)b * tmax * ldim;
-  for (int c0 = r0; c0 < r1; c0 += kMlaRows) {
-    const int nr = min(kMlaRows, r1 - c0);
+  for (int c0 = r0; c0 < r1; c0 += ROWS) {
+    const int nr = min(ROWS, r1 - c0);
     __syncthreads();  // previous sub-chunk fully consumed
     {
-      constexpr int VN = 16 / sizeof(T);
-      const T* src = xb + (int64_t)c0 * ldim;
-      const int nv = nr * ldim / VN;
+      const int4* src = reinterpret_cast<const int4*>(xb + (int64_t)c0 * ldim);
+      int4* dst = reinterpret_cast<int4*>(sx);
+      const int nv = nr * ldim * (int)sizeof(T) / 16;
 #pragma unroll 4
-      for (int i = tid; i < nv; i += kMlaThreads) {
-        Vec<T> v;
-        v.load(src + i * VN);
-#pragma unroll
-        for (int e = 0; e < VN; ++e) sx[i * VN + e] = v.f(e);
-      }
+      for (int i = tid; i < nv; i += kMlaThreads) dst[i] = src[i];
     }
     __syncthreads();
-    // scores of rows warp*4 .. +4
     {
-      float dot[4][HMAX];
+      float dot[RPW][HMAX];
 #pragma unroll
-      for (int r = 0; r < 4; ++r)
+      for (int r = 0; r < RPW; ++r)
 #pragma unroll
         for (int h = 0; h < HMAX; ++h) dot[r][h] = 0.f;
-      const int rb = warp * 4;
+      const int rb = warp * RPW;
       for (int l = lane; l < ldim; l += 32) {
-        float xv[4];
+        float xv[RPW];
 #pragma unroll
-        for (int r = 0; r < 4; ++r) xv[r] = rb + r < nr ? sx[(rb + r) * ldim + l] : 0.f;
+        for (int r = 0; r < RPW; ++r) xv[r] = rb + r < nr ? to_f<T>(sx[(rb + r) * ldim + l]) : 0.f;
 #pragma unroll
         for (int h = 0; h < HMAX; ++h) {
           if (h < heads) {
             const float qv = sq[h * ldim + l];
 #pragma unroll
-            for (int r = 0; r < 4; ++r) dot[r][h] += qv * xv[r];
+            for (int r = 0; r < RPW; ++r) dot[r][h] += qv * xv[r];
           }
         }
       }
 #pragma unroll
-      for (int r = 0; r < 4; ++r)
+      for (int r = 0; r < RPW; ++r)
 #pragma unroll
         for (int h = 0; h < HMAX; ++h) {
           const float d = warp_sum(dot[r][h]);
@@ -246,7 +243,7 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(const float* __
 #pragma unroll
       for (int h = 0; h < HMAX; ++h) acc[c][h] *= h < heads ? sstat[2 * HMAX + h] : 0.f;
       for (int r = 0; r < nr; ++r) {
-        const float xv = sx[r * ldim + l];
+        const float xv = to_f<T>(sx[r * ldim + l]);
 #pragma unroll
         for (int h = 0; h < HMAX; ++h) acc[c][h] += sp[r * HMAX + h] * xv;
       }
@@ -624,27 +621,38 @@ cudaError_t kda_decode(int dtype, const void* q, const void* k, const void* v, c
 }
 
 namespace {
-template <int HMAX, int CPT>
-bool mla_fits(int heads, int ldim) { return heads <= HMAX && ldim <= CPT * kMlaThreads; }
-size_t mla_smem(int heads, int ldim, int hmax) {
-  return sizeof(float) * ((size_t)heads * ldim + (size_t)kMlaRows * ldim + (size_t)kMlaRows * hmax + 3 * hmax);
+// Instance choice: heads padded to 4 / 8 / 16 / 32, columns per thread rounded up to 2 / 4 / 6 / 8,
+// at most 96 running accumulators per thread (HMAX * CPT), 16 rows per chunk above L = 1024.
+struct MlaShape {
+  int hmax, cpt, rows;
+};
+MlaShape mla_shape(int heads, int ldim) {
+  MlaShape s{heads <= 4 ? 4 : heads <= 8 ? 8 : heads <= 16 ? 16 : heads <= 32 ? 32 : 0, 0, ldim <= 1024 ? 32 : 16};
+  const int need = (ldim + kMlaThreads - 1) / kMlaThreads;
+  s.cpt = need <= 2 ? 2 : need <= 4 ? 4 : need <= 6 ? 6 : need <= 8 ? 8 : 0;
+  return s;
+}
+size_t mla_smem(int heads, int ldim, const MlaShape& s, size_t elt) {
+  return sizeof(float) * (size_t)heads * ldim + elt * (size_t)s.rows * ldim +
+         sizeof(float) * ((size_t)s.rows * s.hmax + 3 * (size_t)s.hmax);
 }
 }  // namespace
 
 bool mla_decode_supported(int heads, int ldim) {
-  if (ldim % 8) return false;
-  const int hmax = heads <= 16 ? 16 : heads <= 32 ? 32 : 0;
-  if (!hmax || !(hmax == 16 ? mla_fits<16, 4>(heads, ldim) : mla_fits<32, 2>(heads, ldim))) return false;
-  return mla_smem(heads, ldim, hmax) <= 200 * 1024;
+  if (ldim % 8 || heads <= 0) return false;
+  const MlaShape s = mla_shape(heads, ldim);
+  if (!s.hmax || !s.cpt || s.hmax * s.cpt > 96) return false;
+  return mla_smem(heads, ldim, s, sizeof(float)) <= 200 * 1024;  // fits every cache dtype
 }
 
 int mla_decode_splits(int batch, int64_t tmax, int* rows_per_split) {
   int splits = (296 + batch - 1) / batch;
-  const int64_t max_splits = (tmax + kMlaRows - 1) / kMlaRows;
+  constexpr int kMlaSplitRows = 32;  // a multiple of every instance's chunk rows
+  const int64_t max_splits = (tmax + kMlaSplitRows - 1) / kMlaSplitRows;
   if (splits > max_splits) splits = (int)max_splits;
   if (splits < 1) splits = 1;
   int64_t rps = (tmax + splits - 1) / splits;
-  rps = (rps + kMlaRows - 1) / kMlaRows * kMlaRows;
+  rps = (rps + kMlaSplitRows - 1) / kMlaSplitRows * kMlaSplitRows;
   *rows_per_split = (int)rps;
   return (int)((tmax + rps - 1) / rps);
 }
@@ -652,33 +660,54 @@ int mla_decode_splits(int batch, int64_t tmax, int* rows_per_split) {
 cudaError_t mla_decode(int dtype, const float* qlat, const void* latent, const int32_t* lengths, int batch,
                        int heads, int ldim, int64_t tmax, float* part_acc, float* part_ml, int splits,
                        int rows_per_split, float* ctx, cudaStream_t s) {
-  if (!mla_decode_supported(heads, ldim) || tmax <= 0) return cudaErrorInvalidValue;
-  const int hmax = heads <= 16 ? 16 : 32;
-  const size_t sm = mla_smem(heads, ldim, hmax);
+  if (!mla_decode_supported(heads, ldim) || tmax <= 0 || dtype < 0 || dtype > 2) return cudaErrorInvalidValue;
+  const MlaShape shp = mla_shape(heads, ldim);
+  const size_t sm = mla_smem(heads, ldim, shp, dtype == 0 ? sizeof(float) : 2);
+  if (sm > 200 * 1024) return cudaErrorInvalidValue;
+  if (rows_per_split % shp.rows) return cudaErrorInvalidValue;
   const dim3 grid(splits, batch);
-#define KIMI_MLA(TT, HM, CP)                                                                                      \
-  do {                                                                                                            \
-    auto fn = mla_decode_kernel<TT, HM, CP>;                                                                      \
-    if (sm > 48 * 1024) {                                                                                         \
-      cudaError_t e = ensure_dynamic_smem(fn, (int)(200 * 1024));                                                \
-      if (e != cudaSuccess) return e;                                                                             \
-    }                                                                                                             \
-    fn<<<grid, kMlaThreads, sm, s>>>(qlat, (const TT*)latent, lengths, heads, ldim, tmax, rows_per_split,        \
-                                     part_acc, part_ml);                                                          \
+  cudaError_t err = cudaErrorInvalidValue;
+#define KIMI_MLA(TT, HM, CP, RW)                                                                               \
+  do {                                                                                                         \
+    auto fn = mla_decode_kernel<TT, HM, CP, RW>;                                                               \
+    if (sm > 48 * 1024) {                                                                                      \
+      cudaError_t e = ensure_dynamic_smem(fn, (int)(200 * 1024));                                             \
+      if (e != cudaSuccess) return e;                                                                          \
+    }                                                                                                          \
+    fn<<<grid, kMlaThreads, sm, s>>>(qlat, (const TT*)latent, lengths, heads, ldim, tmax, rows_per_split,     \
+                                     part_acc, part_ml);                                                       \
+    err = cudaSuccess;                                                                                         \
   } while (0)
-#define KIMI_MLA_H(TT)            \
-  if (hmax == 16)                 \
-    KIMI_MLA(TT, 16, 4);          \
-  else                            \
-    KIMI_MLA(TT, 32, 2);
-  switch (dtype) {
-    case 0: KIMI_MLA_H(float); break;
-    case 1: KIMI_MLA_H(__nv_bfloat16); break;
-    case 2: KIMI_MLA_H(__half); break;
-    default: return cudaErrorInvalidValue;
+#define KIMI_MLA_R(TT, HM, CP)              \
+  if (shp.rows == 32)                       \
+    KIMI_MLA(TT, HM, CP, 32);               \
+  else                                      \
+    KIMI_MLA(TT, HM, CP, 16);
+#define KIMI_MLA_T(TT)                                                   \
+  switch (shp.hmax * 16 + shp.cpt) {                                     \
+    case 4 * 16 + 2: KIMI_MLA_R(TT, 4, 2); break;                        \
+    case 4 * 16 + 4: KIMI_MLA_R(TT, 4, 4); break;                        \
+    case 4 * 16 + 6: KIMI_MLA_R(TT, 4, 6); break;                        \
+    case 4 * 16 + 8: KIMI_MLA_R(TT, 4, 8); break;                        \
+    case 8 * 16 + 2: KIMI_MLA_R(TT, 8, 2); break;                        \
+    case 8 * 16 + 4: KIMI_MLA_R(TT, 8, 4); break;                        \
+    case 8 * 16 + 6: KIMI_MLA_R(TT, 8, 6); break;                        \
+    case 8 * 16 + 8: KIMI_MLA_R(TT, 8, 8); break;                        \
+    case 16 * 16 + 2: KIMI_MLA_R(TT, 16, 2); break;                      \
+    case 16 * 16 + 4: KIMI_MLA_R(TT, 16, 4); break;                      \
+    case 16 * 16 + 6: KIMI_MLA_R(TT, 16, 6); break;                      \
+    case 32 * 16 + 2: KIMI_MLA_R(TT, 32, 2); break;                      \
+    default: return cudaErrorInvalidValue;                               \
   }
-#undef KIMI_MLA_H
+  switch (dtype) {
+    case 0: KIMI_MLA_T(float); break;
+    case 1: KIMI_MLA_T(__nv_bfloat16); break;
+    case 2: KIMI_MLA_T(__half); break;
+  }
+#undef KIMI_MLA_T
+#undef KIMI_MLA_R
 #undef KIMI_MLA
+  if (err != cudaSuccess) return err;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   mla_decode_combine_kernel<<<dim3(heads, batch), 256, 0, s>>>(part_acc, part_ml, splits, heads, ldim, ctx);

@@ -88,6 +88,7 @@ struct DevParams {
   int64_t ag_ld;             // row stride of the gather buffers in bytes
   int mode, M, N, K, G;
   const int* offsets;
+  int uniform_rows;  // mode 1 with equal segments: tile -> segment by division, no offset scan
   int b2_k_split;  // k-blocks at k >= split read map_b2 at (k - split); 0 = off
   int situ;        // B tile = [gate 128 rows | up 128 rows] from map_b / map_b2
   int epi;
@@ -135,6 +136,7 @@ __device__ int total_tiles(const DevParams& p) {
   const int tn = tiles_n_of<BNT>(p);
   if (p.mode == 0) return ((p.M + BMT - 1) / BMT) * tn * p.ksplit;
   if (p.mode == 1) {
+    if (p.uniform_rows > 0) return p.G * (p.uniform_rows / BM) * tn;
     int t = 0;
     for (int g = 0; g < p.G; ++g) t += ((p.offsets[g + 1] - p.offsets[g]) / BM) * tn;
     return t;
@@ -173,6 +175,17 @@ __device__ TileInfo tile_info(const DevParams& p, int tile) {
     ti.k0 = split * kb_per * BK;
     const int left = total_kb - split * kb_per;
     ti.num_kb = left < kb_per ? (left > 0 ? left : 0) : kb_per;
+    ti.c_row0 = ti.m0;
+    return ti;
+  }
+  if (p.mode == 1 && p.uniform_rows > 0) {
+    const int tm = p.uniform_rows / BM, per = tm * tn;
+    const int g = tile / per, local = tile - g * per;
+    ti.g = g;
+    ti.m0 = g * p.uniform_rows + (local % tm) * BM;
+    ti.n0 = (local / tm) * BNT;
+    ti.k0 = 0;
+    ti.num_kb = (p.K + BK - 1) / BK;
     ti.c_row0 = ti.m0;
     return ti;
   }
@@ -1201,6 +1214,7 @@ cudaError_t tc_gemm(const TcGemmArgs& a, cudaStream_t stream) {
   dp.K = a.K;
   dp.G = a.G;
   dp.offsets = a.offsets;
+  dp.uniform_rows = a.mode == 1 ? a.uniform_rows : 0;
   dp.b2_k_split = a.b2_k_split;
   dp.situ = a.epi == 1 ? 1 : 0;
   dp.epi = a.epi;

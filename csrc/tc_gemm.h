@@ -21,6 +21,7 @@ struct TcGemmArgs {
   int b2_k_split = 0;
   int M = 0, N = 0, K = 0, G = 1;
   const int* offsets = nullptr;  // device [G+1]
+  int uniform_rows = 0;          // mode 1: every segment has this many rows (offsets[g] = g * rows)
   int epi = 0;                   // 0 store, 1 SiTU, 2 weighted scatter-add (fp32), 3 fp32 add into out
   void* out = nullptr;
   bool out_fp32 = false;

@@ -82,6 +82,26 @@ def _static_layer(lc: HybridLayerCache, max_length: int) -> HybridLayerCache:
     raise TypeError(f"unsupported layer cache {type(s).__name__}")
 
 
+def _load_static_layer(static: HybridLayerCache, lc: HybridLayerCache) -> None:
+    """Refill a serving layer cache in place from a prefill cache (the captured step keeps
+    reading the same tensors)."""
+    s, src = static.state, lc.state
+    if isinstance(s, KDAState):
+        s.recurrent_state.copy_(src.recurrent_state)
+        for dst, new in ((s.q_conv_state, src.q_conv_state), (s.k_conv_state, src.k_conv_state),
+                         (s.v_conv_state, src.v_conv_state)):
+            dst.buffer.copy_(new.buffer)
+        s.sequence_offset.copy_(src.sequence_offset)
+        return
+    t = src.latent_kv.shape[1]
+    if t > s.latent_kv.shape[1]:
+        raise ValueError(f"prompt of {t} tokens exceeds the serving cache ({s.latent_kv.shape[1]})")
+    s.latent_kv[:, :t].copy_(src.latent_kv)
+    if src.attention_mask is not None:
+        s.latent_kv[:, :t].mul_(src.attention_mask[..., None].to(s.latent_kv.dtype))
+    s.sequence_offset.copy_(src.sequence_offset)
+
+
 def _state_tensors(cache: HybridBackboneCache) -> list:
     out = []
     for lc in cache.layer_caches:
@@ -116,6 +136,7 @@ class GraphDecoder:
                       if self.autocast_dtype is not None else model)
         self.graph = None
         self.replays = 0
+        self._key = None
 
     # ------------------------------------------------------------------ helpers
     def _autocast(self):
@@ -190,21 +211,40 @@ class GraphDecoder:
                 pre = model(input_ids=input_ids, attention_mask=attention_mask, use_cache=True, return_dict=True)
             logits = last_prompt_logits(pre.logits, attention_mask)
             self.vocab = int(logits.shape[-1])
-            self.cache = HybridBackboneCache(tuple(_static_layer(lc, self.max_length)
-                                                   for lc in pre.cache.layer_caches), pre.cache.sequence_length)
-            self.tok = torch.zeros(b, 1, dtype=torch.long, device=dev)
-            self.out = torch.zeros(b, max(steps, 1), dtype=torch.long, device=dev)
-            self.step = torch.zeros((), dtype=torch.long, device=dev)
-            self.finished = torch.zeros(b, dtype=torch.bool, device=dev)
             pen = cfg.repetition_penalty not in (None, 1)
+            # the captured step bakes in the batch shape and the sampling / EOS settings
+            key = (b, self.vocab, pen, cfg.do_sample, cfg.temperature, cfg.top_k, cfg.top_p, cfg.repetition_penalty,
+                   cfg.eos_token_id, cfg.pad_token_id)
+            if self.graph is not None and self._key == key:
+                # same batch shape as the captured step: refill its buffers in place, replay it
+                for static, lc in zip(self.cache.layer_caches, pre.cache.layer_caches):
+                    _load_static_layer(static, lc)
+                self.cache = HybridBackboneCache(self.cache.layer_caches, pre.cache.sequence_length)
+                for t in (self.tok, self.out, self.step, self.finished):
+                    t.zero_()
+            else:
+                self.release()
+                self._key = key
+                self.cache = HybridBackboneCache(tuple(_static_layer(lc, self.max_length)
+                                                       for lc in pre.cache.layer_caches), pre.cache.sequence_length)
+                self.tok = torch.zeros(b, 1, dtype=torch.long, device=dev)
+                self.out = torch.zeros(b, self.max_length, dtype=torch.long, device=dev)
+                self.step = torch.zeros((), dtype=torch.long, device=dev)
+                self.finished = torch.zeros(b, dtype=torch.bool, device=dev)
+                self.seen = self.seed_offset = None
             if dev.type == "cuda":
                 from .. import ops
-                self.seen = (torch.zeros(b, (self.vocab + 31) // 32, dtype=torch.int32, device=dev)
-                             if pen else None)
-                if self.seen is not None:
+                if pen:
+                    if self.seen is None:
+                        self.seen = torch.zeros(b, (self.vocab + 31) // 32, dtype=torch.int32, device=dev)
+                    self.seen.zero_()
                     ops.mark_seen(self.seen, input_ids, self.vocab)
                 seed = cfg.seed if cfg.seed is not None else int(torch.randint(0, 2 ** 62, ()).item())
-                self.seed_offset = torch.tensor([seed, 0], dtype=torch.long, device=dev)
+                seed_offset = torch.tensor([seed, 0], dtype=torch.long)
+                if self.seed_offset is None:
+                    self.seed_offset = seed_offset.to(dev)
+                else:
+                    self.seed_offset.copy_(seed_offset)
             else:
                 self.seen = None
                 self.history = input_ids.clone()
@@ -216,7 +256,7 @@ class GraphDecoder:
             if steps > 0:
                 self._emit(self._sample(logits))
                 n = 1
-                if self.use_graph and steps > 1:
+                if self.use_graph and steps > 1 and self.graph is None:
                     self._capture()
                 check = max(int(cfg.eos_check_every), 1)
                 while n < steps:
@@ -267,7 +307,9 @@ class GraphDecoder:
         torch.cuda.synchronize(self.device)
 
     def release(self) -> None:
+        """Drop the captured step (required before destroying a process group it uses)."""
         self.graph = None
+        self._key = None
 
 
 def graph_generate(model, input_ids, *, max_length: int | None = None,

@@ -155,6 +155,11 @@ def _ns_on_tensor_cores(w: torch.Tensor) -> bool:
 _NS_OFFSETS: dict = {}
 
 
+def _ns_tile_n(n: int) -> int:
+    """Output tile width with the least padding (256 on a tie: fewer tiles)."""
+    return 256 if (-n) % 256 <= (-n) % 128 else 128
+
+
 def _ns_iterations_tc(w: torch.Tensor, steps: int, transpose_out: bool) -> torch.Tensor:
     """The quintic iterations on this package's grouped tcgen05 GEMM (bf16 operands, fp32
     accumulation).  Each matrix of the batch is one row segment of the grouped product, padded to
@@ -173,17 +178,16 @@ def _ns_iterations_tc(w: torch.Tensor, steps: int, transpose_out: bool) -> torch
     if offs is None:
         offs = _NS_OFFSETS[key] = (torch.arange(e + 1, dtype=torch.int32) * mp).to(w.device)
     a, b, c = NS_COEFFS
-    bn_g = 256 if (mp >= 320 or mp % 256 == 0) else 128
-    bn_x = 256 if (n >= 320 or n % 256 == 0) else 128
+    bn_g, bn_x = _ns_tile_n(mp), _ns_tile_n(n)
     rows = e * mp
     for _ in range(steps):
         g = C.tc_gemm_grouped(1, x.view(rows, n), x, None, False, False, offs, rows, mp, n, 0, None, False, 0.0,
-                              0.0, None, None, 0, bn_g)[0]
+                              0.0, None, None, 0, bn_g, uniform_rows=mp)[0]
         g2 = C.tc_gemm_grouped(1, g, g.view(e, mp, mp), None, False, False, offs, rows, mp, mp, 0, None, False, 0.0,
-                               0.0, None, None, 0, bn_g)[0]
+                               0.0, None, None, 0, bn_g, uniform_rows=mp)[0]
         poly = C.ns_poly(g, g2, a, b, c)
         x = C.tc_gemm_grouped(1, poly, x, None, False, True, offs, rows, n, mp, 0, None, False, 0.0, 0.0, None, None,
-                              0, bn_x)[0].view(e, mp, n)
+                              0, bn_x, uniform_rows=mp)[0].view(e, mp, n)
     out = x[:, :m]
     return out.transpose(-2, -1) if transpose_out else out
 

@@ -70,7 +70,9 @@ def test_kda_decode_step(cuda, inplace):
 
 
 @pytest.mark.parametrize("heads,ldim,dtype", [(10, 640, torch.bfloat16), (12, 768, torch.bfloat16),
-                                               (24, 512, torch.float32), (16, 1024, torch.bfloat16)])
+                                               (24, 512, torch.float32), (16, 1024, torch.bfloat16),
+                                               (3, 1536, torch.bfloat16), (12, 1536, torch.bfloat16),
+                                               (6, 1536, torch.float32), (2, 64, torch.bfloat16)])
 def test_mla_absorbed_decode(cuda, heads, ldim, dtype):
     from kimi_k3_b200 import ops
     torch.manual_seed(2)
@@ -178,3 +180,10 @@ def test_graph_decoder(cuda):
     out = dec.generate(ids, mask)
     assert dec.replays == 7
     assert torch.equal(out.generated_ids, ref_out.generated_ids), (out.generated_ids, ref_out.generated_ids)
+    # a second generation with the same batch shape refills the buffers and replays the same graph
+    graph = dec.graph
+    ids2 = torch.randint(5, 1000, (4, 30), device=cuda)
+    again = dec.generate(ids2)
+    assert dec.graph is graph and dec.replays == 14
+    fresh = GraphDecoder(model, max_length=64, generation_config=cfg, autocast_dtype=None).generate(ids2)
+    assert torch.equal(again.generated_ids, fresh.generated_ids)
