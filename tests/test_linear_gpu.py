@@ -151,7 +151,7 @@ def test_newton_schulz_on_tensor_cores(cuda, e, m, n, transposed):
     w = raw.transpose(-2, -1) if transposed else raw
     w = (w / w.flatten(1).norm(dim=1)[:, None, None]).to(torch.bfloat16)
     assert _ns_on_tensor_cores(w)
-    got = newton_schulz_iterations(w, 5, transpose_out=transposed).float()
+    got = newton_schulz_iterations(w, 5, transpose_out=transposed, tensor_cores=True).float()
     want = _ns_fp32(w, 5)
     if transposed:
         want = want.transpose(-2, -1)
