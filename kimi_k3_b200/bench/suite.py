@@ -120,6 +120,44 @@ class _ReferenceTimer:
         return self.ev0.elapsed_time(self.ev1) / self.steps, (self.t1 - self.t0) * 1e3 / self.steps, clocks
 
 
+def _reference_train(ref_train, model, opt, make_batches, args, local, **kw):
+    """Time the reference's ``train_one_epoch`` over ``warmup + steps`` optimizer steps.
+
+    Falls back, in this order and saying so in the returned note, to what the reference itself
+    offers: fp32 when its bf16 autocast path raises (its AttnRes rejects mixed depth-source dtypes),
+    and gradient accumulation over 2, 4 or 8 micro-batches (its ``grad_accum_steps``) when the full
+    per-replica batch runs out of device memory.  ``make_batches(n, micro)`` returns ``n`` batches of
+    ``1 / micro`` of the per-replica batch.  Returns (device ms, host ms, clocks, note)."""
+    notes, amp = [], True
+    for micro in (1, 2, 4, 8):
+        batches = make_batches((args.warmup + args.steps) * micro, micro)
+        while True:
+            timer = _ReferenceTimer(args.warmup, args.steps, local)
+            oom = False
+            try:
+                ref_train(model, batches, opt, amp_enabled=amp, amp_dtype="bf16", grad_accum_steps=micro,
+                          max_batches=len(batches), on_optimizer_step=timer, **kw)
+                if micro > 1:
+                    notes.append(f"the full batch exceeds device memory in the reference; {micro} accumulated "
+                                 "micro-batches per step")
+                ms, host, clocks = timer.result()
+                return ms, host, clocks, "; ".join(notes) or None
+            except TypeError as exc:
+                if not amp:
+                    raise
+                amp = False
+                notes.append(f"reference bf16 autocast fails ({str(exc)[:100]}); measured in fp32")
+            except torch.OutOfMemoryError:
+                oom = True
+            if oom:  # outside the handler, so the failed step's frames are gone before the cache is freed
+                if timer.sampler is not None:
+                    timer.sampler.stop()
+                opt.zero_grad(set_to_none=True)
+                torch.cuda.empty_cache()
+                break
+    raise torch.OutOfMemoryError("the reference runs out of device memory even with 8 micro-batches per step")
+
+
 def _time_engine(engine, dev_batches, host_batches, warmup, steps, local):
     """Device-timed steps, then the same count end to end (pinned inputs in, loss out)."""
     for i in range(warmup):
@@ -295,28 +333,18 @@ def run_gpu24_tp_ep(args, world, rank, local, impl):
         raw = model.module if hasattr(model, "module") else model
         opt, _ = ref_build_optimizer(raw, RefOptConfig(**optimizer_settings()))
         vocab = raw.config.vocab_size
-        batches = _token_batches(args.warmup + args.steps, per_replica, GPU24_SEQ, vocab, 1000 + ctx.ep_rank)
-        timer = _ReferenceTimer(args.warmup, args.steps, local)
-        amp = True
-        try:
-            ref_train(model, batches, opt, device=dev, amp_enabled=True, amp_dtype="bf16", grad_clip=1.0,
-                      max_batches=len(batches), use_mtp=True, moe_controller=RefMoEController(model),
-                      on_optimizer_step=timer, distributed_context=ctx)
-        except TypeError as exc:  # the reference's AttnRes rejects bf16 autocast outputs: run its fp32 path
-            amp, note = False, f"reference bf16 autocast fails ({exc}); measured in fp32"
-            timer = _ReferenceTimer(args.warmup, args.steps, local)
-            ref_train(model, batches, opt, device=dev, amp_enabled=False, grad_clip=1.0, max_batches=len(batches),
-                      use_mtp=True, moe_controller=RefMoEController(model), on_optimizer_step=timer,
-                      distributed_context=ctx)
-        ms, e2e, clocks = timer.result()
+
+        def make(n, micro):
+            return _token_batches(n, per_replica // micro, GPU24_SEQ, vocab, 1000 + ctx.ep_rank)
+        ms, e2e, clocks, note = _reference_train(ref_train, model, opt, make, args, local, device=dev, grad_clip=1.0,
+                                                 use_mtp=True, moe_controller=RefMoEController(model),
+                                                 distributed_context=ctx)
         loss = None
-        if not amp:
-            note = note or "fp32"
     ms, e2e = max_over_ranks(ms), max_over_ranks(e2e)
     tokens = GPU24_GLOBAL_BATCH * GPU24_SEQ
     h2d = per_replica * GPU24_SEQ * (8 + 8 + 1)
     line = {"metric": "train_tokens_per_s", "unit": "tokens/s", "value": round(tokens / (ms / 1e3), 1),
-            "ms_per_step": round(ms, 3), "n_gpus": world, "dtype": "bf16" if note is None else "fp32",
+            "ms_per_step": round(ms, 3), "n_gpus": world, "dtype": "fp32" if note and "fp32" in note else "bf16",
             "scaling": "strong", "higher_is_better": True, "clocks": clocks,
             "e2e": {"value": round(tokens / (e2e / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(e2e, 3),
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
@@ -408,23 +436,15 @@ def run_gpu48_fsdp(args, world, rank, local, impl):
             note = f"reference Muon rejects FSDP parameter shards ({exc}); measured with AdamW only"
             opt, _ = ref_build_optimizer(model, RefOptConfig(**optimizer_settings(kind="adamw")))
         vocab = raw.config.vocab_size
-        amp = True
         for si, (seq, bpg) in enumerate(GPU48_STAGES):
-            batches = _token_batches(args.warmup + args.steps, bpg, seq, vocab, 1000 + 10 * rank + si)
-            timer = _ReferenceTimer(args.warmup, args.steps, local)
-            kw = dict(device=dev, grad_clip=1.0, max_batches=len(batches), use_mtp=True,
-                      moe_controller=RefMoEController(model), on_optimizer_step=timer, distributed_context=ctx)
-            try:
-                ref_train(model, batches, opt, amp_enabled=amp, amp_dtype="bf16", **kw)
-            except TypeError as exc:
-                if not amp:
-                    raise
-                amp = False
-                note = "; ".join(x for x in (note, f"reference bf16 autocast fails ({exc}); measured in fp32") if x)
-                timer = _ReferenceTimer(args.warmup, args.steps, local)
-                kw["on_optimizer_step"] = timer
-                ref_train(model, batches, opt, amp_enabled=False, **kw)
-            ms, e2e, clocks = timer.result()
+            def make(n, micro, seq=seq, bpg=bpg, si=si):
+                return _token_batches(n, max(bpg // micro, 1), seq, vocab, 1000 + 10 * rank + si)
+            ms, e2e, clocks, stage_note = _reference_train(ref_train, model, opt, make, args, local, device=dev,
+                                                           grad_clip=1.0, use_mtp=True,
+                                                           moe_controller=RefMoEController(model),
+                                                           distributed_context=ctx)
+            if stage_note:
+                note = "; ".join(x for x in (note, f"stage {seq}: {stage_note}") if x)
             stage_ms.append(max_over_ranks(ms))
             stage_e2e.append(max_over_ranks(e2e))
             clocks_all.append(clocks)
