@@ -146,6 +146,11 @@ __global__ void __launch_bounds__(256) kda_decode_kernel(const T* __restrict__ q
 // 4 / 8 / 16 / 32, CPT = ceil(L / 256) rounded to 2 / 4 / 6 / 8, ROWS 32 (L <= 1024) or 16.
 constexpr int kMlaThreads = 256;
 
+// Two adjacent elements as floats (one 4- or 8-byte shared-memory load).
+KIMI_D float2 mla_pair(const float* p) { return *reinterpret_cast<const float2*>(p); }
+KIMI_D float2 mla_pair(const __nv_bfloat16* p) { return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p)); }
+KIMI_D float2 mla_pair(const __half* p) { return __half22float2(*reinterpret_cast<const __half2*>(p)); }
+
 template <typename T, int HMAX, int CPT, int ROWS>
 __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(const float* __restrict__ qlat,
                                                                  const T* __restrict__ latent,
@@ -198,16 +203,16 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(const float* __
 #pragma unroll
         for (int h = 0; h < HMAX; ++h) dot[r][h] = 0.f;
       const int rb = warp * RPW;
-      for (int l = lane; l < ldim; l += 32) {
-        float xv[RPW];
+      for (int l = 2 * lane; l < ldim; l += 64) {  // two adjacent columns per lane (ldim is even)
+        float2 xv[RPW];
 #pragma unroll
-        for (int r = 0; r < RPW; ++r) xv[r] = rb + r < nr ? to_f<T>(sx[(rb + r) * ldim + l]) : 0.f;
+        for (int r = 0; r < RPW; ++r) xv[r] = rb + r < nr ? mla_pair(sx + (rb + r) * ldim + l) : make_float2(0.f, 0.f);
 #pragma unroll
         for (int h = 0; h < HMAX; ++h) {
           if (h < heads) {
-            const float qv = sq[h * ldim + l];
+            const float2 qv = *reinterpret_cast<const float2*>(sq + h * ldim + l);
 #pragma unroll
-            for (int r = 0; r < RPW; ++r) dot[r][h] += qv * xv[r];
+            for (int r = 0; r < RPW; ++r) dot[r][h] += qv.x * xv[r].x + qv.y * xv[r].y;
           }
         }
       }
@@ -236,16 +241,34 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(const float* __
       sstat[2 * HMAX + tid] = scale;
     }
     __syncthreads();
+    {  // rescale, then add this chunk: one row's HMAX weights are read once (float4) for all CPT columns
+      float scale[HMAX];
 #pragma unroll
-    for (int c = 0; c < CPT; ++c) {
-      const int l = tid + c * kMlaThreads;
-      if (l >= ldim) break;
+      for (int h = 0; h < HMAX; ++h) scale[h] = h < heads ? sstat[2 * HMAX + h] : 0.f;
 #pragma unroll
-      for (int h = 0; h < HMAX; ++h) acc[c][h] *= h < heads ? sstat[2 * HMAX + h] : 0.f;
+      for (int c = 0; c < CPT; ++c)
+#pragma unroll
+        for (int h = 0; h < HMAX; ++h) acc[c][h] *= scale[h];
       for (int r = 0; r < nr; ++r) {
-        const float xv = to_f<T>(sx[r * ldim + l]);
+        float w[HMAX];
+        const float4* wr = reinterpret_cast<const float4*>(sp + r * HMAX);
 #pragma unroll
-        for (int h = 0; h < HMAX; ++h) acc[c][h] += sp[r * HMAX + h] * xv;
+        for (int q = 0; q < HMAX / 4; ++q) {
+          const float4 v = wr[q];
+          w[4 * q] = v.x;
+          w[4 * q + 1] = v.y;
+          w[4 * q + 2] = v.z;
+          w[4 * q + 3] = v.w;
+        }
+#pragma unroll
+        for (int c = 0; c < CPT; ++c) {
+          const int l = tid + c * kMlaThreads;
+          if (l < ldim) {
+            const float xv = to_f<T>(sx[r * ldim + l]);
+#pragma unroll
+            for (int h = 0; h < HMAX; ++h) acc[c][h] += w[h] * xv;
+          }
+        }
       }
     }
   }
