@@ -159,6 +159,7 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(const float* __
                                                                  float* __restrict__ part_acc,
                                                                  float* __restrict__ part_ml) {
   constexpr int RPW = ROWS / 8;  // rows per warp in the score phase
+  static_assert(ROWS <= 32 && ROWS % 8 == 0, "one lane per chunk row in the softmax phase");
   extern __shared__ __align__(16) float smem[];
   float* sq = smem;                                            // [heads][ldim] fp32
   T* sx = reinterpret_cast<T*>(sq + heads * ldim);            // [ROWS][ldim] cache dtype
@@ -225,20 +226,19 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(const float* __
         }
     }
     __syncthreads();
-    // running softmax statistics per head (one thread per head)
-    if (tid < heads) {
-      float m = sstat[tid];
-      for (int r = 0; r < nr; ++r) m = fmaxf(m, sp[r * HMAX + tid]);
-      const float scale = expf(sstat[tid] - m);  // exp(-inf) = 0 on the first chunk
-      float sum = sstat[HMAX + tid] * scale;
-      for (int r = 0; r < nr; ++r) {
-        const float p = expf(sp[r * HMAX + tid] - m);
-        sp[r * HMAX + tid] = p;
-        sum += p;
+    // running softmax statistics: one warp per head, one lane per row of the chunk (ROWS <= 32)
+    for (int h = warp; h < heads; h += kMlaThreads / 32) {
+      const float v = lane < nr ? sp[lane * HMAX + h] : -INFINITY;
+      const float m = fmaxf(sstat[h], warp_max(v));
+      const float scale = expf(sstat[h] - m);  // exp(-inf) = 0 on the first chunk
+      const float p = lane < nr ? expf(v - m) : 0.f;
+      if (lane < ROWS) sp[lane * HMAX + h] = p;
+      const float sum = warp_sum(p);
+      if (lane == 0) {
+        sstat[h] = m;
+        sstat[HMAX + h] = sstat[HMAX + h] * scale + sum;
+        sstat[2 * HMAX + h] = scale;
       }
-      sstat[tid] = m;
-      sstat[HMAX + tid] = sum;
-      sstat[2 * HMAX + tid] = scale;
     }
     __syncthreads();
     {  // rescale, then add this chunk: one row's HMAX weights are read once (float4) for all CPT columns
@@ -669,7 +669,10 @@ bool mla_decode_supported(int heads, int ldim) {
 }
 
 int mla_decode_splits(int batch, int64_t tmax, int* rows_per_split) {
-  int splits = (296 + batch - 1) / batch;
+  // about six CTAs per SM over the grid (several resident per SM keep more cache rows in flight),
+  // each with at least one 32-row block
+  const int target = device_sms() * 6;
+  int splits = (target + batch - 1) / batch;
   constexpr int kMlaSplitRows = 32;  // a multiple of every instance's chunk rows
   const int64_t max_splits = (tmax + kMlaSplitRows - 1) / kMlaSplitRows;
   if (splits > max_splits) splits = (int)max_splits;

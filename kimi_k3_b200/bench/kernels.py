@@ -340,9 +340,36 @@ def bench_decode(args) -> list:
     return rows
 
 
+def bench_newton_schulz(args) -> list:
+    """Five Newton-Schulz iterations per Muon bucket of the t4_wikitext model (vocab 50,257): the
+    batched library GEMMs (the training default) against the grouped tcgen05 path."""
+    from ..config.profiles import profile_model_config
+    from ..models import KimiK3
+    from ..train import optimizer as O
+    C, dev = _require_cuda()
+    del C
+    model = KimiK3(profile_model_config("t4_wikitext", vocab_size=50257))
+    opt, _ = O.build_kimi_optimizer(model, O.KimiOptimizerConfig(kind="per_head_muon_adamw", per_head_qkv=True))
+    rows = []
+    for (_, r, c, _, mom, _) in opt.muon._ensure_buckets():
+        e = mom.shape[0]
+        x = torch.randn(e, r, c, device=dev).to(torch.bfloat16)
+        tr = r > c
+        w = x.transpose(-2, -1) if tr else x
+        for name, tc in (("batched_gemm", False), ("tcgen05_grouped", True)):
+            tm = time_fn(lambda: O.newton_schulz_iterations(w, 5, transpose_out=tr, tensor_cores=tc), device=dev,
+                         warmup=args.warmup, repeats=args.repeats)
+            m, n = min(r, c), max(r, c)
+            flops = 5 * e * (2 * m * m * n * 2 + 2 * m * m * m)
+            rows.append(_emit({"case": "ns", "path": name, "matrices": e, "rows": r, "cols": c, **tm.as_dict(),
+                               **roofline(tm.median_ms, flops=flops)}))
+    return rows
+
+
 CASES = {"kda_phases": bench_kda_phases, "gemm": bench_gemm, "gemm_variants": bench_gemm_variants,
          "projections": bench_projections, "kda": bench_kda, "moe": bench_moe, "linear_ce": bench_linear_ce,
-         "attention": bench_attention, "attnres": bench_attnres, "decode": bench_decode}
+         "attention": bench_attention, "attnres": bench_attnres, "decode": bench_decode,
+         "ns": bench_newton_schulz}
 
 
 def build_parser(parser: argparse.ArgumentParser | None = None) -> argparse.ArgumentParser:
