@@ -289,6 +289,213 @@ __global__ void __launch_bounds__(kMlaThreads) mla_decode_kernel(const float* __
   }
 }
 
+// ---------------------------------------------------------------- MLA flash decode on tensor cores
+// bf16 caches with latent L = 64 * NT (512 / 768 / 1024 / 1536) and at most 16 heads.  Per chunk of 16
+// cache rows:  S = Q C^T  (M = 16 heads, N = 16 rows, K = L; warp w takes the K steps w, w + 8, ...)
+// and O += P C  (M = 16 heads, N = L, K = 16 rows; warp w owns L / 8 output columns), both with
+// mma.sync m16n8k16 (bf16 in, fp32 accumulate).  Q and P enter as bf16 high + low parts (two MMAs
+// each), so the products keep about 16 mantissa bits.  Chunks stream through two shared-memory
+// buffers with cp.async (the next chunk loads while this one computes); rows past the valid prefix
+// are zero-filled.  Shared-memory rows are padded by 8 elements so fragment loads are conflict-free.
+KIMI_D void mla_cp_async16(void* smem, const void* gmem, int src_bytes) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(src_bytes) : "memory");
+}
+KIMI_D void mla_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+KIMI_D void mla_cp_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+KIMI_D uint32_t mla_ld32(const __nv_bfloat16* p) { return *reinterpret_cast<const uint32_t*>(p); }
+KIMI_D void mla_mma(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+KIMI_D void mla_ldmatrix_x4_trans(uint32_t* r, const __nv_bfloat16* p) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(s));
+}
+KIMI_D void mla_split_bf16(float v, __nv_bfloat16* hi, __nv_bfloat16* lo) {
+  const __nv_bfloat16 h = __float2bfloat16_rn(v);
+  *hi = h;
+  *lo = __float2bfloat16_rn(v - __bfloat162float(h));
+}
+
+constexpr int kMmaRows = 16;
+
+size_t mla_mma_smem(int ldim) {
+  const size_t ld = (size_t)ldim + 8;
+  return 4 * 16 * ld * 2 + 8 * 16 * kMmaRows * sizeof(float) + 2 * 16 * kMmaRows * 2 + 48 * sizeof(float);
+}
+
+template <int NT>
+__global__ void __launch_bounds__(256, 1) mla_decode_mma_kernel(const float* __restrict__ qlat,
+                                                                const __nv_bfloat16* __restrict__ latent,
+                                                                const int32_t* __restrict__ lengths, int heads,
+                                                                int64_t tmax, int rows_per_split,
+                                                                float* __restrict__ part_acc,
+                                                                float* __restrict__ part_ml) {
+  constexpr int L = 64 * NT, LD = L + 8, KSTEPS = L / 16, R = kMmaRows, V = L / 8;
+  extern __shared__ __align__(16) unsigned char mla_smem_raw[];
+  __nv_bfloat16* sqh = reinterpret_cast<__nv_bfloat16*>(mla_smem_raw);  // [16][LD] query, high parts
+  __nv_bfloat16* sql = sqh + 16 * LD;                                    // [16][LD] query, low parts
+  __nv_bfloat16* sx0 = sql + 16 * LD;                                    // 2 x [R][LD] cache chunks
+  float* ss = reinterpret_cast<float*>(sx0 + 2 * R * LD);                // [8 warps][16][R] partial scores
+  __nv_bfloat16* sph = reinterpret_cast<__nv_bfloat16*>(ss + 8 * 16 * R);  // [16][R] weights, high
+  __nv_bfloat16* spl = sph + 16 * R;                                       // [16][R] weights, low
+  float* sstat = reinterpret_cast<float*>(spl + 16 * R);                   // max [16], sum [16], scale [16]
+  const int split = blockIdx.x, b = blockIdx.y, nsplit = gridDim.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, tg = lane & 3;
+  const int len = (int)min((int64_t)lengths[b], tmax);
+  const int r0 = split * rows_per_split, r1 = min(r0 + rows_per_split, len);
+  const __nv_bfloat16* xb = latent + (int64_t)b * tmax * L;
+
+  auto load_chunk = [&](int c0, __nv_bfloat16* dst) {
+    const int nr = min(R, r1 - c0);
+    for (int i = tid; i < R * V; i += 256) {
+      const int r = i / V, v = i - r * V;
+      const bool ok = r < nr;
+      mla_cp_async16(dst + r * LD + v * 8, ok ? xb + (int64_t)(c0 + r) * L + v * 8 : xb, ok ? 16 : 0);
+    }
+    mla_cp_commit();
+  };
+  if (r0 < r1) load_chunk(r0, sx0);
+  {  // query -> bf16 high / low parts, heads padded to 16 with zeros
+    const float* qb = qlat + (int64_t)b * heads * L;
+    for (int i = tid; i < 16 * L; i += 256) {
+      const int h = i / L, l = i - h * L;
+      mla_split_bf16(h < heads ? qb[(int64_t)h * L + l] : 0.f, sqh + h * LD + l, sql + h * LD + l);
+    }
+  }
+  if (tid < 16) {
+    sstat[tid] = -INFINITY;
+    sstat[16 + tid] = 0.f;
+    sstat[32 + tid] = 0.f;
+  }
+  float acc[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+  int buf = 0;
+  for (int c0 = r0; c0 < r1; c0 += R) {
+    const int nr = min(R, r1 - c0);
+    const __nv_bfloat16* sx = sx0 + buf * R * LD;
+    if (c0 + R < r1) {
+      load_chunk(c0 + R, sx0 + (buf ^ 1) * R * LD);
+      mla_cp_wait<1>();
+    } else {
+      mla_cp_wait<0>();
+    }
+    __syncthreads();  // this chunk (and, on the first pass, the query and statistics) visible to all
+    {  // partial scores of this warp's K steps
+      float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      for (int ks = warp; ks < KSTEPS; ks += 8) {
+        const int k0 = ks * 16 + tg * 2;
+        uint32_t ah[4], al[4];
+        ah[0] = mla_ld32(sqh + g * LD + k0);
+        ah[1] = mla_ld32(sqh + (g + 8) * LD + k0);
+        ah[2] = mla_ld32(sqh + g * LD + k0 + 8);
+        ah[3] = mla_ld32(sqh + (g + 8) * LD + k0 + 8);
+        al[0] = mla_ld32(sql + g * LD + k0);
+        al[1] = mla_ld32(sql + (g + 8) * LD + k0);
+        al[2] = mla_ld32(sql + g * LD + k0 + 8);
+        al[3] = mla_ld32(sql + (g + 8) * LD + k0 + 8);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const __nv_bfloat16* xr = sx + (nt * 8 + g) * LD + k0;
+          const uint32_t b0 = mla_ld32(xr), b1 = mla_ld32(xr + 8);
+          mla_mma(sc[nt], ah, b0, b1);
+          mla_mma(sc[nt], al, b0, b1);
+        }
+      }
+      float* sw = ss + warp * 16 * R;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const int c = nt * 8 + tg * 2;
+        sw[g * R + c] = sc[nt][0];
+        sw[g * R + c + 1] = sc[nt][1];
+        sw[(g + 8) * R + c] = sc[nt][2];
+        sw[(g + 8) * R + c + 1] = sc[nt][3];
+      }
+    }
+    __syncthreads();
+    // online softmax: one warp per head, one lane per chunk row
+    for (int h = warp; h < 16; h += 8) {
+      float v = -INFINITY;
+      if (h < heads && lane < nr) {
+        v = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) v += ss[w * 16 * R + h * R + lane];
+      }
+      float p = 0.f, scale = 0.f, m = -INFINITY;
+      if (h < heads) {  // nr >= 1: the maximum is finite
+        m = fmaxf(sstat[h], warp_max(v));
+        scale = expf(sstat[h] - m);  // exp(-inf) = 0 on the first chunk
+        p = lane < nr ? expf(v - m) : 0.f;
+      }
+      if (lane < R) mla_split_bf16(p, sph + h * R + lane, spl + h * R + lane);
+      const float sum = warp_sum(p);
+      if (lane == 0) {
+        if (h < heads) {
+          sstat[h] = m;
+          sstat[16 + h] = sstat[16 + h] * scale + sum;
+        }
+        sstat[32 + h] = scale;
+      }
+    }
+    __syncthreads();
+    {  // rescale the running context, then add P C for this warp's columns
+      const float s0 = sstat[32 + g], s1 = sstat[32 + g + 8];
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        acc[j][0] *= s0;
+        acc[j][1] *= s0;
+        acc[j][2] *= s1;
+        acc[j][3] *= s1;
+      }
+      uint32_t ph[4], pl[4];
+      ph[0] = mla_ld32(sph + g * R + tg * 2);
+      ph[1] = mla_ld32(sph + (g + 8) * R + tg * 2);
+      ph[2] = mla_ld32(sph + g * R + tg * 2 + 8);
+      ph[3] = mla_ld32(sph + (g + 8) * R + tg * 2 + 8);
+      pl[0] = mla_ld32(spl + g * R + tg * 2);
+      pl[1] = mla_ld32(spl + (g + 8) * R + tg * 2);
+      pl[2] = mla_ld32(spl + g * R + tg * 2 + 8);
+      pl[3] = mla_ld32(spl + (g + 8) * R + tg * 2 + 8);
+      const __nv_bfloat16* xrow = sx + ((lane & 7) + ((lane >> 3) & 1) * 8) * LD + (lane >> 4) * 8;
+#pragma unroll
+      for (int j = 0; j < NT; j += 2) {
+        uint32_t bq[4];
+        mla_ldmatrix_x4_trans(bq, xrow + warp * NT * 8 + j * 8);
+        mla_mma(acc[j], ph, bq[0], bq[1]);
+        mla_mma(acc[j], pl, bq[0], bq[1]);
+        mla_mma(acc[j + 1], ph, bq[2], bq[3]);
+        mla_mma(acc[j + 1], pl, bq[2], bq[3]);
+      }
+    }
+    buf ^= 1;
+    __syncthreads();  // the chunk buffer and the weights are rewritten next pass
+  }
+  __syncthreads();
+  const int64_t pb = ((int64_t)b * nsplit + split) * heads;
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    const int col = warp * NT * 8 + j * 8 + tg * 2;
+    if (g < heads)
+      *reinterpret_cast<float2*>(part_acc + (pb + g) * L + col) = make_float2(acc[j][0], acc[j][1]);
+    if (g + 8 < heads)
+      *reinterpret_cast<float2*>(part_acc + (pb + g + 8) * L + col) = make_float2(acc[j][2], acc[j][3]);
+  }
+  if (tid < heads) {
+    part_ml[(pb + tid) * 2] = sstat[tid];
+    part_ml[(pb + tid) * 2 + 1] = sstat[16 + tid];
+  }
+}
+
 __global__ void __launch_bounds__(256) mla_decode_combine_kernel(const float* __restrict__ part_acc,
                                                                  const float* __restrict__ part_ml, int nsplit,
                                                                  int heads, int ldim, float* __restrict__ ctx) {
@@ -687,6 +894,29 @@ cudaError_t mla_decode(int dtype, const float* qlat, const void* latent, const i
                        int heads, int ldim, int64_t tmax, float* part_acc, float* part_ml, int splits,
                        int rows_per_split, float* ctx, cudaStream_t s) {
   if (!mla_decode_supported(heads, ldim) || tmax <= 0 || dtype < 0 || dtype > 2) return cudaErrorInvalidValue;
+  if (dtype == 1 && heads <= 16 && rows_per_split % kMmaRows == 0 &&
+      (ldim == 512 || ldim == 768 || ldim == 1024 || ldim == 1536)) {
+    const size_t msm = mla_mma_smem(ldim);
+    const dim3 mgrid(splits, batch);
+#define KIMI_MLA_MMA(NT)                                                                                     \
+  do {                                                                                                       \
+    cudaError_t e = ensure_dynamic_smem(mla_decode_mma_kernel<NT>, (int)msm);                                \
+    if (e != cudaSuccess) return e;                                                                          \
+    mla_decode_mma_kernel<NT><<<mgrid, 256, msm, s>>>(qlat, static_cast<const __nv_bfloat16*>(latent), lengths, \
+                                                      heads, tmax, rows_per_split, part_acc, part_ml);        \
+  } while (0)
+    switch (ldim) {
+      case 512: KIMI_MLA_MMA(8); break;
+      case 768: KIMI_MLA_MMA(12); break;
+      case 1024: KIMI_MLA_MMA(16); break;
+      default: KIMI_MLA_MMA(24); break;
+    }
+#undef KIMI_MLA_MMA
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    mla_decode_combine_kernel<<<dim3(heads, batch), 256, 0, s>>>(part_acc, part_ml, splits, heads, ldim, ctx);
+    return cudaGetLastError();
+  }
   const MlaShape shp = mla_shape(heads, ldim);
   const size_t sm = mla_smem(heads, ldim, shp, dtype == 0 ? sizeof(float) : 2);
   if (sm > 200 * 1024) return cudaErrorInvalidValue;

@@ -72,7 +72,8 @@ def test_kda_decode_step(cuda, inplace):
 @pytest.mark.parametrize("heads,ldim,dtype", [(10, 640, torch.bfloat16), (12, 768, torch.bfloat16),
                                                (24, 512, torch.float32), (16, 1024, torch.bfloat16),
                                                (3, 1536, torch.bfloat16), (12, 1536, torch.bfloat16),
-                                               (6, 1536, torch.float32), (2, 64, torch.bfloat16)])
+                                               (6, 1536, torch.float32), (2, 64, torch.bfloat16),
+                                               (16, 512, torch.bfloat16), (1, 768, torch.bfloat16)])
 def test_mla_absorbed_decode(cuda, heads, ldim, dtype):
     from kimi_k3_b200 import ops
     torch.manual_seed(2)
