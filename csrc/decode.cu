@@ -404,13 +404,14 @@ __global__ void __launch_bounds__(256, 1) mla_decode_mma_kernel(const float* __r
         al[1] = mla_ld32(sql + (g + 8) * LD + k0);
         al[2] = mla_ld32(sql + g * LD + k0 + 8);
         al[3] = mla_ld32(sql + (g + 8) * LD + k0 + 8);
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          const __nv_bfloat16* xr = sx + (nt * 8 + g) * LD + k0;
-          const uint32_t b0 = mla_ld32(xr), b1 = mla_ld32(xr + 8);
-          mla_mma(sc[nt], ah, b0, b1);
-          mla_mma(sc[nt], al, b0, b1);
-        }
+        const __nv_bfloat16* xr0 = sx + g * LD + k0;
+        const __nv_bfloat16* xr1 = xr0 + 8 * LD;
+        const uint32_t b00 = mla_ld32(xr0), b01 = mla_ld32(xr0 + 8), b10 = mla_ld32(xr1), b11 = mla_ld32(xr1 + 8);
+        // the four products interleave two accumulators (no back-to-back dependence)
+        mla_mma(sc[0], ah, b00, b01);
+        mla_mma(sc[1], ah, b10, b11);
+        mla_mma(sc[0], al, b00, b01);
+        mla_mma(sc[1], al, b10, b11);
       }
       float* sw = ss + warp * 16 * R;
 #pragma unroll
@@ -472,8 +473,8 @@ __global__ void __launch_bounds__(256, 1) mla_decode_mma_kernel(const float* __r
         uint32_t bq[4];
         mla_ldmatrix_x4_trans(bq, xrow + warp * NT * 8 + j * 8);
         mla_mma(acc[j], ph, bq[0], bq[1]);
-        mla_mma(acc[j], pl, bq[0], bq[1]);
         mla_mma(acc[j + 1], ph, bq[2], bq[3]);
+        mla_mma(acc[j], pl, bq[0], bq[1]);
         mla_mma(acc[j + 1], pl, bq[2], bq[3]);
       }
     }
