@@ -48,6 +48,35 @@ def wgrad_splits(rows: int, cols: int, k: int, bn: int, sms: int = 148) -> int:
     return int(max(1, min(want, 8, max(1, (k // 64) // 4))))
 
 
+_SMALL_M = 128  # rows up to one tile: decode steps and short prompts
+_SM_COUNT: dict = {}
+
+
+def _sm_count(device) -> int:
+    n = _SM_COUNT.get(device)
+    if n is None:
+        n = _SM_COUNT[device] = torch.cuda.get_device_properties(device).multi_processor_count
+    return n
+
+
+def _split_k_product(x2: torch.Tensor, w: torch.Tensor):
+    """``x2 @ w^T`` in fp32 for at most one tile of rows, or None when one pass already fills the GPU.
+
+    With a handful of rows a product has only ``ceil(n / 128)`` output tiles, so a plain launch keeps
+    a few SMs busy streaming the whole weight.  Here the reduction is split so that about one work
+    unit runs per SM (at most 8 slices, each at least four 64-wide K blocks) and the slices add into
+    one zeroed fp32 buffer with TMA reduce-adds."""
+    m, k = x2.shape
+    n = w.shape[0]
+    tiles = -(-n // 128)
+    splits = int(min(_sm_count(x2.device) // tiles, 8, k // 256))
+    if splits < 2 or n % 4:
+        return None
+    acc = torch.zeros(m, n, device=x2.device, dtype=torch.float32)
+    _C().tc_gemm_dense(x2, w, False, False, True, 128, acc, accumulate=True, ksplit=splits)
+    return acc
+
+
 class _Linear(torch.autograd.Function):
     """``y = x W^T (+ b)`` on the tcgen05 GEMM with bf16 operands and fp32 accumulation.
 
@@ -67,7 +96,13 @@ class _Linear(torch.autograd.Function):
         if x2.dtype != torch.bfloat16:
             x2 = x2.to(torch.bfloat16)
         x2 = _tma_rows(x2)
-        y = _C().tc_gemm_dense(x2, wb, False, False, False, gemm_tiles(n), None, bias=bias)
+        acc = _split_k_product(x2, wb) if x2.shape[0] <= _SMALL_M else None
+        if acc is not None:
+            if bias is not None:
+                acc.add_(bias)
+            y = acc.to(torch.bfloat16)
+        else:
+            y = _C().tc_gemm_dense(x2, wb, False, False, False, gemm_tiles(n), None, bias=bias)
         ctx.save_for_backward(x2, wb)
         ctx.meta = (shape, x.dtype, bias is not None)
         return y.view(*shape[:-1], n) if y.is_contiguous() else y.reshape(*shape[:-1], n)
@@ -127,8 +162,16 @@ class _LinearGroup(torch.autograd.Function):
             x2 = x2.to(torch.bfloat16)
         x2 = _tma_rows(x2)
         m = x2.shape[0]
-        outs = [torch.empty(m, _pad8(w), device=x.device, dtype=torch.bfloat16)[:, :w] for w in widths]
-        _C().tc_gemm_group(1, outs, x2, wcat, None, 256, 1, -1)
+        acc = _split_k_product(x2, wcat) if m <= _SMALL_M else None
+        if acc is not None:  # few rows: one split-K product over W_cat, outputs are column slices
+            y = acc.to(torch.bfloat16)
+            offs = [0]
+            for w in widths:
+                offs.append(offs[-1] + w)
+            outs = [y[:, a:b] for a, b in zip(offs[:-1], offs[1:])]
+        else:
+            outs = [torch.empty(m, _pad8(w), device=x.device, dtype=torch.bfloat16)[:, :w] for w in widths]
+            _C().tc_gemm_group(1, outs, x2, wcat, None, 256, 1, -1)
         ctx.save_for_backward(x2, wcat)
         ctx.meta = (shape, x.dtype, tuple(widths))
         return tuple(o.view(*shape[:-1], w) for o, w in zip(outs, widths))

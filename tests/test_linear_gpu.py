@@ -11,7 +11,8 @@ def _rel(a, b):
     return ((a - b).norm() / b.norm().clamp_min(1e-12)).item()
 
 
-@pytest.mark.parametrize("shape", [(4, 333, 640, 640), (2, 1024, 1920, 640), (3, 100, 12, 640), (1, 512, 640, 64)])
+@pytest.mark.parametrize("shape", [(4, 333, 640, 640), (2, 1024, 1920, 640), (3, 100, 12, 640), (1, 512, 640, 64),
+                                   (64, 1, 1536, 1536), (2, 16, 768, 2048)])
 @pytest.mark.parametrize("bias", [False, True])
 def test_linear_forward_backward(cuda, shape, bias):
     from kimi_k3_b200.models.linear import Linear
@@ -106,15 +107,17 @@ def test_tc_gemm_group_three_kinds(cuda):
         assert _rel(dw, ref) < 1e-3
 
 
-def test_linear_group_matches_separate_projections(cuda):
+# 32 rows with a total width that is a multiple of 4: the split-K path for few rows (decode)
+@pytest.mark.parametrize("rows,last", [(300, 10), (32, 12)])
+def test_linear_group_matches_separate_projections(cuda, rows, last):
     from kimi_k3_b200.models.linear import Linear
     from kimi_k3_b200.ops import linear_group
     from kimi_k3_b200.ops.mirror import WeightMirror
     torch.manual_seed(4)
-    lins = [Linear(640, n, bias=False).to(cuda) for n in (640, 640, 64, 10)]
+    lins = [Linear(640, n, bias=False).to(cuda) for n in (640, 640, 64, last)]
     mirror = WeightMirror([], groups=[[l.weight for l in lins]])
-    x = torch.randn(2, 300, 640, device=cuda, requires_grad=True)
-    dys = [torch.randn(2, 300, l.out_features, device=cuda) for l in lins]
+    x = torch.randn(2, rows, 640, device=cuda, requires_grad=True)
+    dys = [torch.randn(2, rows, l.out_features, device=cuda) for l in lins]
     with torch.autocast("cuda", dtype=torch.bfloat16):
         ys = linear_group(x, [l.weight for l in lins])
     sum((y.float() * d).sum() for y, d in zip(ys, dys)).backward()
