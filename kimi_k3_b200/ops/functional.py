@@ -72,7 +72,7 @@ def _split_k_product(x2: torch.Tensor, w: torch.Tensor):
     splits = int(min(_sm_count(x2.device) // tiles, 8, k // 256))
     if splits < 2 or n % 4:
         return None
-    acc = torch.zeros(m, n, device=x2.device, dtype=torch.float32)
+    acc = torch.zeros(m, _pad8(n), device=x2.device, dtype=torch.float32)[:, :n]  # row stride: 8 elements
     _C().tc_gemm_dense(x2, w, False, False, True, 128, acc, accumulate=True, ksplit=splits)
     return acc
 
