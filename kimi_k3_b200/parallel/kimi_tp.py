@@ -57,6 +57,16 @@ def _copy(dst: torch.Tensor, src: torch.Tensor) -> None:
     dst.copy_(src)
 
 
+def _tag_shards(inner: nn.Module, shard_dims: dict, group) -> None:
+    """Record on each sharded parameter the dimension it is split along and the group that holds
+    the other pieces: optimizers that need whole matrices (Muon) gather over that group."""
+    params = dict(inner.named_parameters())
+    for name, dim in shard_dims.items():
+        if dim is not None and name in params:
+            params[name]._kimi_tp_dim = dim
+            params[name]._kimi_tp_group = group
+
+
 def _install_fused_output(inner: nn.Module, group, enabled: bool) -> bool:
     """Swap the shard's output projection for the fused GEMM + all-reduce (one tcgen05 kernel
     over symmetric memory, ``parallel/symmetric.py``); the wrapper then skips its own reduce."""
@@ -112,6 +122,7 @@ class TensorParallelKDA(nn.Module):
                            "projections.alpha_up.weight": 0, "projections.b_alpha": 0, "decay.A_log": 0,
                            "output_norm.weight": 0 if module.output_norm.per_head_affine else None,
                            "output_gate.gate_proj.weight": 0, "output_gate.output_proj.weight": 1}
+        _tag_shards(self.inner, self.shard_dims, group)
         self.fused_output = _install_fused_output(self.inner, group, fused_output)
 
     def forward(self, hidden_states, attention_mask=None, state=None, mode="chunkwise", output_final_state=False,
@@ -150,6 +161,7 @@ class TensorParallelMLA(nn.Module):
         self.shard_dims = {"projections.query.weight": 0, "projections.latent_kv.compression.weight": None,
                            "projections.latent_kv.key_up.weight": 0, "projections.latent_kv.value_up.weight": 0,
                            "output_gate.gate_proj.weight": 0, "output_gate.output_proj.weight": 1}
+        _tag_shards(self.inner, self.shard_dims, group)
         self.fused_output = _install_fused_output(self.inner, group, fused_output)
         self.inner._kimi_qk_group = group  # QK-Clip takes the MAX scale over the heads of all ranks
         for attr in ("absorbed_decode",):

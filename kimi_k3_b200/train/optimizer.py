@@ -454,6 +454,7 @@ class _MatrixSlot:
     cols: int
     to_blocks: callable  # tensor shaped like param -> [count, rows, cols]
     from_blocks: callable
+    per_head: bool = False  # head blocks along dim 0 (Per-Head Muon)
 
 
 class KimiMuon(torch.optim.Optimizer):
@@ -484,7 +485,7 @@ class KimiMuon(torch.optim.Optimizer):
             hl = spec.head_layout
             return _MatrixSlot(p, hl.num_heads, hl.head_dim, p.shape[1],
                                lambda t, hl=hl: t.reshape(hl.num_heads, hl.head_dim, t.shape[-1]),
-                               lambda b, p=p: b.reshape(p.shape))
+                               lambda b, p=p: b.reshape(p.shape), per_head=True)
         if p.ndim == 3:
             return _MatrixSlot(p, p.shape[0], p.shape[1], p.shape[2], lambda t: t, lambda b: b)
         return _MatrixSlot(p, 1, p.shape[0], p.shape[1], lambda t: t[None], lambda b: b[0])
@@ -504,6 +505,60 @@ class KimiMuon(torch.optim.Optimizer):
         owned = getattr(self, "_owned", None)
         return owned is None or id(p) in owned
 
+    def _tp_gathered(self, p) -> bool:
+        """A tensor-parallel shard whose Newton-Schulz needs the whole matrix: split over a group of
+        more than one rank, and not a per-head slot whose heads all live on this rank."""
+        group = getattr(p, "_kimi_tp_group", None)
+        if group is None or not torch.distributed.is_initialized() or torch.distributed.get_world_size(group) < 2:
+            return False
+        slot = self._slots[id(p)]
+        return not (slot.per_head and getattr(p, "_kimi_tp_dim", 0) == 0)
+
+    @torch.no_grad()
+    def _step_tp_gathered(self, skip, metrics) -> None:
+        """Momentum stays per shard; the momentum-updated shard is all-gathered along its split
+        dimension, orthogonalised as the whole matrix (the same update as one process computes) and
+        each rank applies its own slice."""
+        import torch.distributed as dist
+        for group in self.param_groups:
+            lr, mom, wd = group["lr"], group["momentum"], group["weight_decay"]
+            for p in group["params"]:
+                if p.grad is None or not self._mine(p) or not self._tp_gathered(p):
+                    continue
+                st = self.state[p]
+                buf = st.get("momentum_buffer")
+                if buf is None:
+                    buf = st["momentum_buffer"] = torch.zeros_like(p)
+                g = p.grad.to(buf.dtype)
+                if skip is not None:
+                    g = torch.where(skip, torch.zeros((), device=g.device, dtype=g.dtype), g)
+                    buf.mul_(torch.where(skip, 1.0, mom).to(buf.dtype)).add_(g)
+                else:
+                    buf.mul_(mom).add_(g)
+                raw = (g.add(buf, alpha=mom) if group["nesterov"] else buf).contiguous()
+                tp, dim = p._kimi_tp_group, p._kimi_tp_dim
+                world, rank = dist.get_world_size(tp), dist.get_rank(tp)
+                parts = [torch.empty_like(raw) for _ in range(world)]
+                dist.all_gather(parts, raw, group=tp)
+                full = torch.cat(parts, dim)
+                ortho = batched_newton_schulz(full.float()[None], steps=group["ns_steps"], eps=group["eps"],
+                                              dtype=self._resolved_ns_dtype(p.device))[0]
+                scale = max(full.shape) ** 0.5 if group["update_rms_scaling"] else 1.0
+                metrics["raw"].append(full.float().square().mean().sqrt()[None])
+                metrics["ortho"].append(ortho.square().mean().sqrt()[None])
+                metrics["scaled"].append(metrics["ortho"][-1] * scale)
+                upd = torch.chunk(ortho, world, dim=dim)[rank].to(p.dtype).mul_(scale)
+                lr_eff = torch.where(skip, 0.0, lr) if skip is not None else lr
+                if wd:
+                    p.mul_(1.0 - lr_eff * wd)
+                if torch.is_tensor(lr_eff):
+                    p.add_(upd * (-lr_eff).to(upd.dtype))
+                else:
+                    p.add_(upd, alpha=-lr_eff)
+                prms = p.float().square().mean().sqrt().clamp_min(group["eps"])
+                lr_v = lr if torch.is_tensor(lr) else torch.tensor(float(lr), device=prms.device)
+                metrics["ratio"].append((lr_v * metrics["scaled"][-1].mean() / prms)[None])
+
     # ---- bucketed state: one momentum tensor [count, rows, cols] per (group, matrix shape)
     def _ensure_buckets(self) -> list:
         """Per-parameter momentum buffers become views into one tensor per bucket, so a step
@@ -513,7 +568,7 @@ class KimiMuon(torch.optim.Optimizer):
         keyed: dict = {}
         for gi, group in enumerate(self.param_groups):
             for p in group["params"]:
-                if not self._mine(p):
+                if not self._mine(p) or self._tp_gathered(p):
                     continue
                 slot = self._slots[id(p)]
                 keyed.setdefault((gi, slot.rows, slot.cols, p.device, p.dtype), []).append(p)
@@ -589,6 +644,7 @@ class KimiMuon(torch.optim.Optimizer):
                 torch._foreach_add_(ps, views)
             else:
                 torch._foreach_add_(ps, views, alpha=-lr_eff)
+        self._step_tp_gathered(skip, metrics)
         self._metric_tensors = {k: torch.cat(v) for k, v in metrics.items() if v}
         self.last_update_metrics = {}
         return self._metric_tensors
@@ -714,7 +770,7 @@ class KimiMuon(torch.optim.Optimizer):
         for group in self.param_groups:
             lr, mom, wd = group["lr"], group["momentum"], group["weight_decay"]
             for p in group["params"]:
-                if p.grad is None or not self._mine(p):
+                if p.grad is None or not self._mine(p) or self._tp_gathered(p):
                     continue
                 slot = self._slots[id(p)]
                 buf = self.state[p]["momentum_buffer"]
@@ -733,6 +789,7 @@ class KimiMuon(torch.optim.Optimizer):
                 if wd:
                     p.mul_(1.0 - lr * wd)
                 p.add_(upd, alpha=-lr)
+        self._step_tp_gathered(None, metrics)
         self._metric_tensors = {k: torch.cat(v) for k, v in metrics.items() if v}
         self.last_update_metrics = {}
         return self._metric_tensors

@@ -107,6 +107,10 @@ def _rank(rank, world, layout, kind, qb):
     if shard_bytes is not None:
         out["__shard_fraction__"] = torch.tensor(shard_bytes)
     experts = {n: p.detach().clone() for n, p in model.named_parameters() if getattr(p, "_kimi_local_expert", False)}
+    # tensor-parallel shards with the dimension they split (compared against slices of the full matrices)
+    shards = {n: (p._kimi_tp_dim, ctx.tp_rank, p.detach().clone()) for n, p in model.named_parameters()
+              if getattr(p, "_kimi_tp_dim", None) is not None}
+    experts["__tp_shards__"] = shards
     ctx.close()
     return res["loss"], out, experts
 
@@ -120,7 +124,8 @@ def _compare(ref_params, got, tol):
     return worst
 
 
-@pytest.mark.parametrize("layout,kind", [("dp", "per_head_muon_adamw"), ("tp", "adamw"), ("tp_fused_output", "adamw"),
+@pytest.mark.parametrize("layout,kind", [("dp", "per_head_muon_adamw"), ("tp", "adamw"), ("tp", "per_head_muon_adamw"),
+                                         ("tp_fused_output", "adamw"),
                                          ("ep", "per_head_muon_adamw"),
                                          ("tp_ep_overlay", "adamw"), ("fsdp", "per_head_muon_adamw")])
 def test_parallel_layout_matches_single_process(layout, kind):
@@ -137,6 +142,13 @@ def test_parallel_layout_matches_single_process(layout, kind):
             frac = float(params.pop("__shard_fraction__"))
             assert frac < 0.6, frac
         assert _compare(ref_params, params, tol) < tol, layout
+    for _, _, experts in results:
+        # every tensor-parallel shard equals its slice of the single-process matrix (Muon orthogonalises
+        # the gathered whole matrix, so sharded and unsharded runs take the same step)
+        for n, (dim, tp_rank, v) in experts.pop("__tp_shards__").items():
+            full = ref_params[n.replace(".inner.", ".")]
+            want = full.chunk(world, dim)[tp_rank]
+            assert (want - v).abs().max().item() < tol, (layout, n)
     if layout in ("ep", "tp_ep_overlay"):
         # each rank's local experts equal the matching slice of the single-process experts
         for rank, (_, _, experts) in enumerate(results):
