@@ -293,6 +293,8 @@ class MoonViTEncoder(nn.Module):
             if at is not None:
                 at.append(w)
         x = self.final_norm(x)
+        if hs is not None:
+            hs[-1] = x  # the last entry is the encoder's (normalised) output itself
         return VisionEncoderOutput(x, grid, tuple(hs) if hs is not None else None,
                                    tuple(at) if at is not None else None)
 

@@ -196,9 +196,12 @@ class WindowSelfAttention(nn.Module):
         if self.relative_position_bias is not None:
             bias = self.relative_position_bias[self.relative_position_index.reshape(-1)]
             scores = scores + bias.reshape(n, n, self.num_heads).permute(2, 0, 1).unsqueeze(0)
+        scores32 = scores.float()
         if attention_mask is not None:
-            scores = scores.masked_fill(~attention_mask[:, None], torch.finfo(scores.dtype).min)
-        p = F.softmax(scores.float(), dim=-1).to(scores.dtype)
+            # the fill is float32's lowest value: a float64 lowest value would become -inf in the fp32
+            # softmax, and a fully padded window row would turn into NaN (and NaN weight gradients)
+            scores32 = scores32.masked_fill(~attention_mask[:, None], torch.finfo(torch.float32).min)
+        p = F.softmax(scores32, dim=-1).to(scores.dtype)
         if attention_mask is not None:
             p = p * attention_mask[:, None].to(p.dtype)
             p = p / p.sum(-1, keepdim=True).clamp_min(torch.finfo(p.dtype).tiny)
@@ -340,6 +343,8 @@ class SwinMoonViTEncoder(nn.Module):
                     at.append(w)
             if si < len(self.mergers):
                 x, grid, padding_mask = self.mergers[si](x, grid, padding_mask)
+                if hs is not None:
+                    hs.append(x)  # the merged tokens open the next stage
         x = self.final_norm(x)
         if hs is not None:
             hs[-1] = x
