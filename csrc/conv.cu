@@ -239,7 +239,10 @@ __global__ void __launch_bounds__(256) dw_reduce_kernel(const float* __restrict_
 // The block's token rows (and their K - 1 halo rows) are contiguous in [B, T, C]: one TMA bulk
 // copy per tensor brings them into shared memory (mbarrier completion), then each thread walks
 // its 8 channels over the tile reading shared memory, so DRAM latency is paid once per block.
-constexpr int kSTile = 32;
+// Tokens per block: 32 forward; 16 backward, whose two staged tensors and larger register state would
+// otherwise leave two 3-warp blocks per SM (the walk over the tile is a dependent chain, so the
+// backward is latency-bound and wants more resident blocks more than it minds the K - 1 halo).
+constexpr int kSTileFwd = 32, kSTileBwd = 16;
 
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
@@ -278,7 +281,7 @@ __global__ void __launch_bounds__(256) conv_fwd_s_kernel(const T* __restrict__ x
   const int ch = threadIdx.x;
   const bool active = ch * 8 < channels;
   const int c0 = active ? ch * 8 : 0;
-  const int b = blockIdx.y, t0 = blockIdx.x * kSTile, t1 = min(t0 + kSTile, tokens);
+  const int b = blockIdx.y, t0 = blockIdx.x * kSTileFwd, t1 = min(t0 + kSTileFwd, tokens);
   const int r0 = t0 - (K - 1);
   if (threadIdx.x == 0) {
     tc::mbar_init(&bar, 1);
@@ -331,12 +334,12 @@ __global__ void __launch_bounds__(256) conv_bwd_s_kernel(const T* __restrict__ d
   const int ch = threadIdx.x;
   const bool active = ch * 8 < channels;
   const int c0 = active ? ch * 8 : 0;
-  const int b = blockIdx.y, t0 = blockIdx.x * kSTile, t1 = min(t0 + kSTile, tokens);
+  const int b = blockIdx.y, t0 = blockIdx.x * kSTileBwd, t1 = min(t0 + kSTileBwd, tokens);
   const int tstart = min(t1 + K - 2, tokens - 1);
   const int xr0 = t0 - (K - 1), xr1 = tstart + 1;  // x rows needed
   const int dr0 = t0, dr1 = tstart + 1;            // dy rows needed
   T* sx = reinterpret_cast<T*>(smem);
-  T* sd = sx + (int64_t)(kSTile + 2 * K - 2) * channels;
+  T* sd = sx + (int64_t)(kSTileBwd + 2 * K - 2) * channels;
   if (threadIdx.x == 0) {
     tc::mbar_init(&bar, 1);
     tc::fence_barrier_init();
@@ -425,9 +428,9 @@ __global__ void __launch_bounds__(256) conv_bwd_s_kernel(const T* __restrict__ d
   }
 }
 
-size_t conv_fwd_s_smem(int channels, int ksize, size_t es) { return (size_t)(kSTile + ksize - 1) * channels * es; }
+size_t conv_fwd_s_smem(int channels, int ksize, size_t es) { return (size_t)(kSTileFwd + ksize - 1) * channels * es; }
 size_t conv_bwd_s_smem(int channels, int ksize, size_t es) {
-  return (size_t)((kSTile + 2 * ksize - 2) + (kSTile + ksize - 1)) * channels * es;
+  return (size_t)((kSTileBwd + 2 * ksize - 2) + (kSTileBwd + ksize - 1)) * channels * es;
 }
 constexpr size_t kConvSmemCap = 200 * 1024;
 
@@ -446,7 +449,7 @@ cudaError_t launch_conv(bool fwd, const void* dy, const void* x, const float* w,
     return cudaErrorInvalidValue;
   const bool staged = (fwd ? conv_fwd_s_smem(channels, ksize, sizeof(T))
                            : conv_bwd_s_smem(channels, ksize, sizeof(T))) <= kConvSmemCap;
-  const int tile = staged ? kSTile : kTile;
+  const int tile = staged ? (fwd ? kSTileFwd : kSTileBwd) : kTile;
   const dim3 grid((tokens + tile - 1) / tile, batch);
   const int hl = head_dim / 8;
   const size_t ssm = fwd ? conv_fwd_s_smem(channels, ksize, sizeof(T)) : conv_bwd_s_smem(channels, ksize, sizeof(T));
@@ -490,7 +493,9 @@ cudaError_t launch_conv(bool fwd, const void* dy, const void* x, const float* w,
 
 }  // namespace
 
-int conv_bwd_partial_rows(int batch, int tokens) { return batch * ((tokens + kTile - 1) / kTile); }  // >= staged rows
+// >= the staged rows (kSTileBwd >= kTile)
+int conv_bwd_partial_rows(int batch, int tokens) { return batch * ((tokens + kTile - 1) / kTile); }
+static_assert(kSTileBwd >= kTile, "the partial-sum buffer is sized for kTile-token tiles");
 
 cudaError_t conv_silu_norm_fwd(int dtype, const void* x, const float* w, void* y, int batch, int tokens,
                                int channels, int ksize, int head_dim, float eps, bool normalize, cudaStream_t s) {
@@ -520,7 +525,7 @@ cudaError_t conv_silu_norm_bwd(int dtype, const void* dy, const void* x, const f
   if (e != cudaSuccess) return e;
   const int n = channels * ksize;
   const size_t es = dtype == 0 ? 4 : 2;
-  const int tile = conv_bwd_s_smem(channels, ksize, es) <= kConvSmemCap ? kSTile : kTile;
+  const int tile = conv_bwd_s_smem(channels, ksize, es) <= kConvSmemCap ? kSTileBwd : kTile;
   const int rows = batch * ((tokens + tile - 1) / tile);
   const dim3 rgrid((n + 31) / 32, rows >= 64 * 8 ? 8 : 1);
   if (cudaMemsetAsync(dw, 0, sizeof(float) * n, s) != cudaSuccess) return cudaGetLastError();
