@@ -19,6 +19,7 @@ from typing import Literal
 import torch
 import torch.nn as nn
 
+from ..debug import nvtx
 from ..runtime import host_checks, mask_all_valid
 from .attnres import (AttentionResidualBackboneOutput, AttentionResidualConfig, AttentionResidualSite,
                       BlockAttentionResidualController, DepthSiteMetadata, FullAttentionResidualController,
@@ -429,8 +430,9 @@ class HybridAttentionGroup(nn.Module):
         caches, states, diags = [], [], []
         out = hidden_states
         for i, layer in enumerate(self.layers):
-            lo = layer(out, attention_mask, None if cache is None else cache[i], use_cache=use_cache, mode=mode,
-                       output_diagnostics=output_diagnostics, update_routing_bias=update_routing_bias)
+            with nvtx(f"layer {i} {layer.attention_type}"):
+                lo = layer(out, attention_mask, None if cache is None else cache[i], use_cache=use_cache, mode=mode,
+                           output_diagnostics=output_diagnostics, update_routing_bias=update_routing_bias)
             out = lo.hidden_states
             if use_cache:
                 caches.append(lo.cache)
@@ -622,11 +624,13 @@ class HybridAttentionBackbone(nn.Module):
         legacy = [x] if output_hidden_states else []
         pre_a, a_out, pre_f, f_out = [], [], [], []
         for i, layer in enumerate(self.layers):
-            lo, mixes = layer.forward_attnres(ctrl, state, layer_mask, None if cache is None else cache.layer_caches[i],
-                                              depth_block_sites=block_sites, use_cache=use_cache, mode=mode,
-                                              output_depth_weights=rw, output_depth_stats=rs,
-                                              output_diagnostics=output_diagnostics,
-                                              update_routing_bias=update_routing_bias)
+            with nvtx(f"layer {i} {layer.attention_label}"):
+                lo, mixes = layer.forward_attnres(ctrl, state, layer_mask,
+                                                  None if cache is None else cache.layer_caches[i],
+                                                  depth_block_sites=block_sites, use_cache=use_cache, mode=mode,
+                                                  output_depth_weights=rw, output_depth_stats=rs,
+                                                  output_diagnostics=output_diagnostics,
+                                                  update_routing_bias=update_routing_bias)
             if use_cache:
                 caches.append(lo.cache)
             if output_diagnostics:

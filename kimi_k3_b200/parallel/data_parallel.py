@@ -13,6 +13,8 @@ import torch
 import torch.distributed as dist
 from torch._utils import _flatten_dense_tensors, _unflatten_dense_tensors
 
+from ..debug import nvtx
+
 
 class QBReducer:
     """Global Quantile-Balancing statistics over the data/expert-parallel group."""
@@ -126,9 +128,10 @@ class GradientAllReducer:
             return
         bucket = self._buckets[bi]
         grads = [p.grad if p.grad is not None else torch.zeros_like(p) for p in bucket]
-        flat = _flatten_dense_tensors(grads)
-        flat.mul_(self.scale if self.scale is not None else 1.0 / self.world_size)
-        self._pending[bi] = (grads, flat, dist.all_reduce(flat, group=self.group, async_op=True))
+        with nvtx(f"dp all-reduce bucket {bi}"):
+            flat = _flatten_dense_tensors(grads)
+            flat.mul_(self.scale if self.scale is not None else 1.0 / self.world_size)
+            self._pending[bi] = (grads, flat, dist.all_reduce(flat, group=self.group, async_op=True))
 
     def _grad_ready(self, bi: int) -> None:
         if not self.armed:  # an earlier micro-batch of an accumulation window

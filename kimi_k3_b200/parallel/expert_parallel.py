@@ -21,6 +21,7 @@ import torch.nn as nn
 
 from ..models.moe import GroupedRoutedExperts, StableLatentMoE, vectorized_sparse_dispatch
 from .. import ops as _ops
+from ..debug import nvtx
 from .data_parallel import QBReducer
 from .tensor_parallel import group_rank, group_size
 
@@ -217,6 +218,10 @@ class ExpertParallelMoE(StableLatentMoE):
         return out[:m] if cap > m else out
 
     def routed_aggregate(self, latent, ro, accumulation_dtype):
+        with nvtx("expert exchange"):
+            return self._routed_aggregate(latent, ro, accumulation_dtype)
+
+    def _routed_aggregate(self, latent, ro, accumulation_dtype):
         m, l = latent.shape
         k = ro.selected_experts.shape[1]
         if (self.fused_comm and _ops.use_kernels(latent) and accumulation_dtype == torch.float32 and l % 64 == 0

@@ -20,6 +20,8 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as dist
 import torch.nn as nn
+
+from ..debug import nvtx
 import torch.nn.functional as F
 
 
@@ -97,11 +99,13 @@ def copy_to_tensor_parallel_region(x, group=None):
 
 
 def reduce_from_tensor_parallel_region(x, group=None):
-    return _ReduceFromRegion.apply(x, group)
+    with nvtx("tp all-reduce"):
+        return _ReduceFromRegion.apply(x, group)
 
 
 def gather_from_tensor_parallel_region(x, group=None):
-    return _GatherLastDim.apply(x, group)
+    with nvtx("tp all-gather"):
+        return _GatherLastDim.apply(x, group)
 
 
 class ColumnParallelLinear(nn.Module):

@@ -24,6 +24,8 @@ from dataclasses import dataclass
 
 import torch
 
+from ..debug import nvtx
+
 
 class KernelWaitError(RuntimeError):
     """A bounded wait inside one of the framework's kernels gave up during a training step."""
@@ -129,12 +131,16 @@ class TrainStepEngine:
         if self.moe_controller is not None:
             self.moe_controller.begin()
         try:
-            out = self.forward_loss(batch)
-            out.loss.backward()
+            with nvtx("forward"):
+                out = self.forward_loss(batch)
+            with nvtx("backward"):
+                out.loss.backward()
             if self.grad_hook is not None:
-                self.grad_hook()
-            gnorm = self._clip()
-            report = self.optimizer.step()
+                with nvtx("gradient sync"):
+                    self.grad_hook()
+            with nvtx("optimizer"):
+                gnorm = self._clip()
+                report = self.optimizer.step()
             executed = bool(getattr(report, "executed", True))
         except BaseException:
             if self.moe_controller is not None:
@@ -215,13 +221,17 @@ class TrainStepEngine:
         with sync_free(all_valid_mask=True):
             if self.moe_controller is not None:
                 self.moe_controller.begin()
-            out = self.forward_loss(batch, cache_enabled=cache_enabled)
-            out.loss.backward()
+            with nvtx("forward"):
+                out = self.forward_loss(batch, cache_enabled=cache_enabled)
+            with nvtx("backward"):
+                out.loss.backward()
             if self.grad_hook is not None:
-                self.grad_hook()
-            gnorm = self._clip()
-            found_inf = ~torch.isfinite(gnorm)
-            self.optimizer.step(found_inf=found_inf)
+                with nvtx("gradient sync"):
+                    self.grad_hook()
+            with nvtx("optimizer"):
+                gnorm = self._clip()
+                found_inf = ~torch.isfinite(gnorm)
+                self.optimizer.step(found_inf=found_inf)
             if self.moe_controller is not None:
                 self.moe_controller.commit(keep_old=found_inf)
         lo = out.loss_output
