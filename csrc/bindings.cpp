@@ -563,7 +563,9 @@ at::Tensor tc_gemm_dense(at::Tensor a, at::Tensor b, bool a_mn, bool b_mn, bool 
 //   kind 2 (input grad):   out [M, K] = sum_s segs[s] ([M, N_s] output grads) W_cat[rows of s]
 //   kind 3 (weight grads): out [N_total, K] fp32 += concat_s(segs[s])^T x   (split over `ksplit` K slices)
 // Segment widths must be multiples of 32 (kind 1) or 64 (kinds 2, 3) except the last; rows of every
-// tensor start on 16-byte boundaries.
+// tensor start on 16-byte boundaries.  Kind 1 stores whole 16-byte units: a segment whose width is
+// not a multiple of 8 also gets its columns [width, round_up(width, 8)) written (zeros), so its row
+// stride must leave room for them (such an output is a view into a row-padded buffer).
 void tc_gemm_group(int64_t kind, std::vector<at::Tensor> segs, at::Tensor x, at::Tensor w,
                    c10::optional<at::Tensor> out_opt, int64_t bn, int64_t ksplit, int64_t pair) {
   TORCH_CHECK(kind >= 1 && kind <= 3, "kind must be 1, 2 or 3");
@@ -584,6 +586,9 @@ void tc_gemm_group(int64_t kind, std::vector<at::Tensor> segs, at::Tensor x, at:
     total += segs[s].size(1);
   }
   if (kind == 1) {  // A = x [M, K] K-major, B = W_cat [N, K] K-major
+    for (auto& t : segs)
+      TORCH_CHECK(t.stride(0) >= (t.size(1) + 7) / 8 * 8,
+                  "a kind-1 segment's row stride must cover its width rounded up to 8 columns");
     check_tma_matrix(x, "x");
     check_tma_matrix(w, "w");
     TORCH_CHECK(w.size(0) == total && w.size(1) == x.size(1), "W_cat must be [sum of widths, K]");

@@ -175,6 +175,7 @@ def _time_engine(engine, dev_batches, host_batches, warmup, steps, local):
     ev1.record()
     torch.cuda.synchronize()
     barrier()
+    clocks = sampler.stop()  # device-timed loop only (its polls would slow the synchronising loop below)
     ms = ev0.elapsed_time(ev1) / steps
     torch.cuda.synchronize()
     barrier()
@@ -186,7 +187,6 @@ def _time_engine(engine, dev_batches, host_batches, warmup, steps, local):
     engine.finish()
     torch.cuda.synchronize()
     barrier()
-    clocks = sampler.stop()  # sampled through both timed loops
     e2e = (time.perf_counter() - t0) * 1e3 / steps
     return ms, e2e, clocks, loss
 
