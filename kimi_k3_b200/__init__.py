@@ -2,8 +2,10 @@
 
 Public API (mirrors the reference project's entry points):
   * models:   ``KimiK3``, ``KimiK3Config``, ``build_model_from_yaml``, ``load_model_config``
-  * training: ``train_kimiK3``, ``train_kimi_from_yaml``, ``build_kimi_optimizer``
+  * training: ``train_kimiK3``, ``train_kimi_from_yaml``, ``train_one_epoch``, ``build_kimi_optimizer``,
+    ``build_muon_adamw_optimizer``, ``build_adamw_optimizer``
   * inference: ``inference_autoregressive``, ``generate_tokens``, ``load_kimi_checkpoint``
+  * distributed: ``parallelize_kimi_model``, ``setup_distributed``
 """
 from .models import (KimiK3, KimiK3Config, KimiK3Output, kimi_k3_canonical_config,  # noqa: F401
                      kimi_k3_cpu_tiny_config)
@@ -21,6 +23,18 @@ def __getattr__(name):  # lazy access to the heavier subsystems
     if name == "build_kimi_optimizer":
         from .train.optimizer import build_kimi_optimizer
         return build_kimi_optimizer
+    if name == "train_one_epoch":
+        from .train.loop import train_one_epoch
+        return train_one_epoch
+    if name in ("build_muon_adamw_optimizer", "build_adamw_optimizer"):
+        from .train import legacy
+        return getattr(legacy, name)
+    if name == "parallelize_kimi_model":
+        from .parallel.parallelize import parallelize_kimi_model
+        return parallelize_kimi_model
+    if name == "setup_distributed":
+        from .parallel.environment import setup_distributed
+        return setup_distributed
     if name in ("inference_autoregressive", "generate_tokens", "load_kimi_checkpoint"):
         from . import infer
         return getattr(infer, name)
