@@ -58,7 +58,8 @@ KIMI_D void load_group(Vec<T> (&xb)[Group<MAXV>::n][MAXV], const SrcPtrs<T>& src
 }
 
 template <typename T, int MAXV>
-__global__ void attnres_fwd_kernel(SrcPtrs<T> src, int S, const float* __restrict__ q, const float* __restrict__ w,
+__global__ void attnres_fwd_kernel(const __grid_constant__ SrcPtrs<T> src, int S, const float* __restrict__ q,
+                                   const float* __restrict__ w,
                                    T* __restrict__ out, float* __restrict__ probs, float* __restrict__ rstd,
                                    int64_t tokens, int dim, float eps) {
   constexpr int VN = Vec<T>::N;
@@ -142,9 +143,10 @@ __global__ void attnres_fwd_kernel(SrcPtrs<T> src, int S, const float* __restric
 }
 
 template <typename T, int MAXV>
-__global__ void attnres_bwd_kernel(SrcPtrs<T> src, int S, const float* __restrict__ q, const float* __restrict__ w,
-                                   const T* __restrict__ dout, const float* __restrict__ probs,
-                                   const float* __restrict__ rstd, DstPtrs<T> dsrc, float* __restrict__ dq,
+__global__ void attnres_bwd_kernel(const __grid_constant__ SrcPtrs<T> src, int S, const float* __restrict__ q,
+                                   const float* __restrict__ w, const T* __restrict__ dout,
+                                   const float* __restrict__ probs, const float* __restrict__ rstd,
+                                   const __grid_constant__ DstPtrs<T> dsrc, float* __restrict__ dq,
                                    float* __restrict__ dw, int64_t tokens, int dim) {
   constexpr int VN = Vec<T>::N;
   constexpr int kGroup = Group<MAXV>::n;
@@ -255,7 +257,9 @@ int maxv_for(int dim) {
   const int per_lane = (nvec + 31) / 32;
   if (per_lane <= 1) return 1;
   if (per_lane <= 2) return 2;
+  if (per_lane <= 3) return 3;  // d_model 640 / 768 in bf16: no idle vector slot per lane
   if (per_lane <= 4) return 4;
+  if (per_lane <= 6) return 6;
   if (per_lane <= 8) return 8;
   return -1;
 }
@@ -266,7 +270,9 @@ int maxv_for(int dim) {
   switch (mv) {                                  \
     case 1: { constexpr int MV = 1; __VA_ARGS__; break; } \
     case 2: { constexpr int MV = 2; __VA_ARGS__; break; } \
+    case 3: { constexpr int MV = 3; __VA_ARGS__; break; } \
     case 4: { constexpr int MV = 4; __VA_ARGS__; break; } \
+    case 6: { constexpr int MV = 6; __VA_ARGS__; break; } \
     case 8: { constexpr int MV = 8; __VA_ARGS__; break; } \
     default: return cudaErrorInvalidValue;       \
   }
@@ -277,7 +283,9 @@ static cudaError_t fwd_impl(const void* const* sources, int S, const float* q, c
   if (S < 1 || S > kMaxSources || dim % Vec<T>::N) return cudaErrorInvalidValue;
   SrcPtrs<T> ptrs{};
   for (int i = 0; i < S; ++i) ptrs.p[i] = (const T*)sources[i];
-  const int threads = 256;
+  // 4-warp blocks: the kernels hold well over 128 registers per thread, so occupancy comes in block
+  // steps; smaller blocks let three or four of them share an SM instead of one 8-warp block
+  const int threads = 128;
   const int mv = maxv_for<T>(dim);
   KIMI_MAXV_SWITCH(mv, MV, {
     attnres_fwd_kernel<T, MV><<<grid_tokens(tokens, threads / 32), threads, 0, s>>>(ptrs, S, q, w, (T*)out, probs,
@@ -297,12 +305,12 @@ static cudaError_t bwd_impl(const void* const* sources, int S, const float* q, c
     ptrs.p[i] = (const T*)sources[i];
     dptrs.p[i] = (T*)dsources[i];
   }
-  const int threads = 256;
+  const int threads = 128;
   const int mv = maxv_for<T>(dim);
   KIMI_MAXV_SWITCH(mv, MV, {
-    // every block ends with 2 * dim global atomics into dq / dw: two blocks per SM keep the number
-    // per element in the hundreds
-    attnres_bwd_kernel<T, MV><<<std::min(grid_tokens(tokens, threads / 32), device_sms() * 2), threads, dim * sizeof(float), s>>>(
+    // every block ends with 2 * dim global atomics into dq / dw: four 4-warp blocks per SM keep the
+    // number per element in the hundreds
+    attnres_bwd_kernel<T, MV><<<std::min(grid_tokens(tokens, threads / 32), device_sms() * 4), threads, dim * sizeof(float), s>>>(
         ptrs, S, q, w, (const T*)dout, probs, rstd, dptrs, dq, dw, tokens, dim);
   });
   return cudaGetLastError();
