@@ -233,18 +233,18 @@ def test_router_topk(cuda):
     _close(g1, logits.grad, 1e-5)
 
 
-@pytest.mark.parametrize("nsrc", [1, 3, 6])
-def test_attnres_mix(cuda, nsrc):
+@pytest.mark.parametrize("nsrc,dim", [(1, 640), (3, 640), (6, 640), (5, 1536), (2, 1024)])
+def test_attnres_mix(cuda, nsrc, dim):
     from kimi_k3_b200 import ops
     from kimi_k3_b200.models.attnres import depth_softmax_mix_reference
     from kimi_k3_b200.models.primitives import RMSNorm
     torch.manual_seed(8)
-    srcs = [torch.randn(2, 37, 640, device=cuda, dtype=torch.bfloat16).requires_grad_() for _ in range(nsrc)]
-    q = (0.3 * torch.randn(640, device=cuda)).requires_grad_()
-    norm = RMSNorm(640).to(cuda)
+    srcs = [torch.randn(2, 37, dim, device=cuda, dtype=torch.bfloat16).requires_grad_() for _ in range(nsrc)]
+    q = (0.3 * torch.randn(dim, device=cuda)).requires_grad_()
+    norm = RMSNorm(dim).to(cuda)
     with torch.no_grad():
-        norm.weight.add_(0.1 * torch.randn(640, device=cuda))
-    go = torch.randn(2, 37, 640, device=cuda, dtype=torch.bfloat16)
+        norm.weight.add_(0.1 * torch.randn(dim, device=cuda))
+    go = torch.randn(2, 37, dim, device=cuda, dtype=torch.bfloat16)
     y1 = ops.attnres_mix(srcs, q, norm.weight, 1e-6)
     y1.backward(go)
     g1 = [s.grad.clone() for s in srcs] + [q.grad.clone(), norm.weight.grad.clone()]
