@@ -382,16 +382,20 @@ cudaError_t rms_norm_bwd(int dtype, const void* dy, const void* x, const float* 
     if (dw && grid > device_sms() * 4) grid = device_sms() * 4;
     const int nvec = dim / Vec<T>::N;
     if (p == 1 && nvec <= 32 * 4) {
-      // with dw, every block ends with one global atomic per weight element: two blocks per SM keep
-      // those few hundred per element (eight per SM made the flush, not the rows, the cost)
-      const int wgrid = (int)std::min<int64_t>((rows + 7) / 8, dw ? device_sms() * 2 : device_sms() * 8);
+      // 4-warp blocks (the wide instances hold well over 128 registers per thread, so occupancy comes
+      // in block steps).  With dw, every block ends with one global atomic per weight element: four
+      // such blocks per SM keep those few hundred per element (32 warps per SM made the flush, not
+      // the rows, the cost)
+      const int wgrid = (int)std::min<int64_t>((rows + 3) / 4, dw ? device_sms() * 4 : device_sms() * 16);
       const size_t wsmem = dw ? (size_t)dim * sizeof(float) : 0;
       if (nvec <= 32)
-        rms_bwd_warp_kernel<T, 1><<<wgrid, 256, wsmem, s>>>((const T*)dy, (const T*)x, w, rstd, (T*)dx, dw, rows, dim);
+        rms_bwd_warp_kernel<T, 1><<<wgrid, 128, wsmem, s>>>((const T*)dy, (const T*)x, w, rstd, (T*)dx, dw, rows, dim);
       else if (nvec <= 64)
-        rms_bwd_warp_kernel<T, 2><<<wgrid, 256, wsmem, s>>>((const T*)dy, (const T*)x, w, rstd, (T*)dx, dw, rows, dim);
+        rms_bwd_warp_kernel<T, 2><<<wgrid, 128, wsmem, s>>>((const T*)dy, (const T*)x, w, rstd, (T*)dx, dw, rows, dim);
+      else if (nvec <= 96)  // d_model 640 / 768 in bf16: no idle vector slot per lane
+        rms_bwd_warp_kernel<T, 3><<<wgrid, 128, wsmem, s>>>((const T*)dy, (const T*)x, w, rstd, (T*)dx, dw, rows, dim);
       else
-        rms_bwd_warp_kernel<T, 4><<<wgrid, 256, wsmem, s>>>((const T*)dy, (const T*)x, w, rstd, (T*)dx, dw, rows, dim);
+        rms_bwd_warp_kernel<T, 4><<<wgrid, 128, wsmem, s>>>((const T*)dy, (const T*)x, w, rstd, (T*)dx, dw, rows, dim);
       break;
     }
     rms_bwd_kernel<T><<<grid, threads, smem, s>>>(
