@@ -24,7 +24,7 @@ def _grads(fn, inputs, gout):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("shape,period", [((64, 37, 640), 1), ((8, 50, 10, 64), 10)])
+@pytest.mark.parametrize("shape,period", [((64, 37, 640), 1), ((4, 33, 1024), 1), ((4, 33, 256), 1), ((8, 50, 10, 64), 10)])
 def test_rms_norm(cuda, dtype, shape, period):
     from kimi_k3_b200 import ops
     from kimi_k3_b200.models.primitives import rms_norm_reference
