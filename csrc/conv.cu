@@ -271,17 +271,23 @@ __device__ void copy_inside(T* dst, const T* src_batch, int r0, int r1, int toke
              (uint32_t)((int64_t)(v1 - v0) * channels * sizeof(T)), bar);
 }
 
+// Forward tokens are independent: kFwdGroups groups of whole warps split the block's tile (each
+// group walks kSTileFwd / kFwdGroups tokens over the same staged rows).
+constexpr int kFwdGroups = 2;
+
 template <typename T, int K>
-__global__ void __launch_bounds__(256) conv_fwd_s_kernel(const T* __restrict__ x, const float* __restrict__ w,
+__global__ void __launch_bounds__(512) conv_fwd_s_kernel(const T* __restrict__ x, const float* __restrict__ w,
                                                          T* __restrict__ y, int tokens, int channels, int head_lanes,
                                                          float eps, bool normalize) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   T* sx = reinterpret_cast<T*>(smem);
-  const int ch = threadIdx.x;
+  const int per = blockDim.x / kFwdGroups;  // threads of one token group (whole warps)
+  const int grp = threadIdx.x / per, ch = threadIdx.x - grp * per;
   const bool active = ch * 8 < channels;
   const int c0 = active ? ch * 8 : 0;
   const int b = blockIdx.y, t0 = blockIdx.x * kSTileFwd, t1 = min(t0 + kSTileFwd, tokens);
+  const int tg0 = t0 + grp * (kSTileFwd / kFwdGroups), tg1 = min(tg0 + kSTileFwd / kFwdGroups, t1);
   const int r0 = t0 - (K - 1);
   if (threadIdx.x == 0) {
     tc::mbar_init(&bar, 1);
@@ -301,7 +307,7 @@ __global__ void __launch_bounds__(256) conv_fwd_s_kernel(const T* __restrict__ x
   __syncthreads();  // zero rows written
   tc::mbar_wait_local(&bar, 0, nullptr, 0);
   const int64_t rowbase = (int64_t)b * tokens;
-  for (int t = t0; t < t1; ++t) {
+  for (int t = tg0; t < tg1; ++t) {
     float s[8], ss = 0.f;
     float xv[K][8];
 #pragma unroll
@@ -462,8 +468,8 @@ cudaError_t launch_conv(bool fwd, const void* dy, const void* x, const float* w,
         if (e != cudaSuccess) return e;                                                                             \
       }                                                                                                             \
       if (fwd)                                                                                                      \
-        conv_fwd_s_kernel<T, KK><<<grid, threads, ssm, s>>>((const T*)x, w, (T*)out, tokens, channels, hl, eps,     \
-                                                            normalize);                                             \
+        conv_fwd_s_kernel<T, KK><<<grid, threads * kFwdGroups, ssm, s>>>((const T*)x, w, (T*)out, tokens, channels, \
+                                                                         hl, eps, normalize);                       \
       else                                                                                                          \
         conv_bwd_s_kernel<T, KK><<<grid, threads, ssm, s>>>((const T*)dy, (const T*)x, w, (T*)out, dw, tokens,      \
                                                             channels, hl, eps, normalize);                          \
