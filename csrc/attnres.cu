@@ -40,12 +40,12 @@ struct Group {
   static constexpr int n = MAXV >= 8 ? 2 : 4;  // fewer rows in flight for wide rows (register budget)
 };
 
-template <typename T, int MAXV>
-KIMI_D void load_group(Vec<T> (&xb)[Group<MAXV>::n][MAXV], const SrcPtrs<T>& src, int s0, int S, int64_t tok,
+template <typename T, int MAXV, int NG = Group<MAXV>::n>
+KIMI_D void load_group(Vec<T> (&xb)[NG][MAXV], const SrcPtrs<T>& src, int s0, int S, int64_t tok,
                        int dim, int lane, int nvec) {
   constexpr int VN = Vec<T>::N;
 #pragma unroll
-  for (int u = 0; u < Group<MAXV>::n; ++u) {
+  for (int u = 0; u < NG; ++u) {
     if (s0 + u < S) {
       const T* row = src.p[s0 + u] + tok * dim;
 #pragma unroll
@@ -149,7 +149,9 @@ __global__ void attnres_bwd_kernel(const __grid_constant__ SrcPtrs<T> src, int S
                                    const __grid_constant__ DstPtrs<T> dsrc, float* __restrict__ dq,
                                    float* __restrict__ dw, int64_t tokens, int dim) {
   constexpr int VN = Vec<T>::N;
-  constexpr int kGroup = Group<MAXV>::n;
+  // two source rows in flight in the backward (it also holds the output-gradient row and the
+  // dq / dw accumulators): fewer registers, one more resident block per SM
+  constexpr int kGroup = MAXV >= 3 ? 2 : Group<MAXV>::n;
   const int lane = threadIdx.x & 31;
   const int wpb = blockDim.x >> 5;
   const int nvec = dim / VN;
@@ -178,7 +180,7 @@ __global__ void attnres_bwd_kernel(const __grid_constant__ SrcPtrs<T> src, int S
     float my_dp = 0.f, my_a = 0.f;
     Vec<T> xb[kGroup][MAXV];
     for (int s0 = 0; s0 < S; s0 += kGroup) {
-      load_group<T, MAXV>(xb, src, s0, S, tok, dim, lane, nvec);
+      load_group<T, MAXV, kGroup>(xb, src, s0, S, tok, dim, lane, nvec);
 #pragma unroll
       for (int u = 0; u < kGroup; ++u) {
         float d0 = 0.f, a0 = 0.f;
@@ -205,7 +207,7 @@ __global__ void attnres_bwd_kernel(const __grid_constant__ SrcPtrs<T> src, int S
     }
     const float pdp = warp_sum(lane < S ? my_p * my_dp : 0.f);
     for (int s0 = 0; s0 < S; s0 += kGroup) {
-      if (S > kGroup) load_group<T, MAXV>(xb, src, s0, S, tok, dim, lane, nvec);
+      if (S > kGroup) load_group<T, MAXV, kGroup>(xb, src, s0, S, tok, dim, lane, nvec);
 #pragma unroll
       for (int u = 0; u < kGroup; ++u) {
         if (s0 + u < S) {
