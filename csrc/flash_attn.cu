@@ -95,6 +95,24 @@ KIMI_D void load_tile(T* s, const T* g, int64_t ld, int valid) {
   }
 }
 
+// The same copy with cp.async (16-byte units, zero-filled rows >= valid); the caller commits and waits.
+template <typename T>
+KIMI_D void load_tile_async(T* s, const T* g, int64_t ld, int valid) {
+  for (int idx = threadIdx.x; idx < 64 * 8; idx += blockDim.x) {
+    const int row = idx >> 3, ch = idx & 7;
+    const bool ok = row < valid;
+    const uint32_t dst = smem_u32(s + row * LDS + ch * 8);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(ok ? g + row * ld + ch * 8 : g),
+                 "r"(ok ? 16 : 0)
+                 : "memory");
+  }
+}
+KIMI_D void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+KIMI_D void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Accumulator element (n-tile nt, reg e) -> (row, col) inside the warp's 16 x 64 tile.
 KIMI_D int acc_row(int e) { return ((threadIdx.x & 31) >> 2) + (e >= 2 ? 8 : 0); }
 KIMI_D int acc_col(int nt, int e) { return nt * 8 + ((threadIdx.x & 3) << 1) + (e & 1); }
@@ -104,10 +122,11 @@ __global__ void __launch_bounds__(NTH) fa_fwd_kernel(const T* __restrict__ q, co
                                                      const T* __restrict__ v, T* __restrict__ o,
                                                      float* __restrict__ lse, int tq, int tk, int H, bool causal,
                                                      const int* __restrict__ key_lengths, float scale) {
-  __shared__ __align__(16) T sQ[BM * LDS];
-  __shared__ __align__(16) T sK[BN * LDS];
-  __shared__ __align__(16) T sV[BN * LDS];
-  __shared__ __align__(16) T sP[BM * LDS];
+  // K / V tiles are double-buffered: the next tile streams in (cp.async) while this one is used
+  extern __shared__ __align__(16) uint8_t fa_smem[];
+  T* sQ = reinterpret_cast<T*>(fa_smem);
+  T* sP = sQ + BM * LDS;
+  T* sKV = sP + BM * LDS;  // [2 buffers][K | V][BN * LDS]
   const int mt = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh % H;
   const int warp = threadIdx.x >> 5;
   const int q0 = mt * BM;
@@ -126,11 +145,27 @@ __global__ void __launch_bounds__(NTH) fa_fwd_kernel(const T* __restrict__ q, co
   const float sl2 = scale * 1.4426950408889634f;  // log2(e) * scale
   int kend = klen;
   if (causal) kend = min(kend, q0 + BM + (tk - tq));
+  if (kend > 0) {
+    load_tile_async(sKV, kb, ld, min(BN, tk));
+    load_tile_async(sKV + BN * LDS, vb, ld, min(BN, tk));
+    cp_async_commit();
+  }
+  int buf = 0;
   for (int k0 = 0; k0 < kend; k0 += BN) {
-    __syncthreads();
-    load_tile(sK, kb + k0 * ld, ld, min(BN, tk - k0));
-    load_tile(sV, vb + k0 * ld, ld, min(BN, tk - k0));
-    __syncthreads();
+    __syncthreads();  // every warp is done with the other buffer (the previous tile)
+    if (k0 + BN < kend) {
+      T* nxt = sKV + (buf ^ 1) * 2 * BN * LDS;
+      load_tile_async(nxt, kb + (k0 + BN) * ld, ld, min(BN, tk - k0 - BN));
+      load_tile_async(nxt + BN * LDS, vb + (k0 + BN) * ld, ld, min(BN, tk - k0 - BN));
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();  // this tile landed for every thread
+    const T* sK = sKV + buf * 2 * BN * LDS;
+    const T* sV = sK + BN * LDS;
+    buf ^= 1;
     float s[8][4];
 #pragma unroll
     for (int n = 0; n < 8; ++n)
@@ -329,8 +364,10 @@ template <typename T>
 cudaError_t fwd_impl(const void* q, const void* k, const void* v, void* o, float* lse, int B, int tq, int tk, int H,
                      bool causal, const int* kl, float scale, cudaStream_t s) {
   dim3 grid((tq + BM - 1) / BM, B * H);
-  fa_fwd_kernel<T><<<grid, NTH, 0, s>>>((const T*)q, (const T*)k, (const T*)v, (T*)o, lse, tq, tk, H, causal, kl,
-                                        scale);
+  const size_t smem = (size_t)6 * 64 * LDS * sizeof(T);  // Q, P and two K / V pairs
+  KIMI_CUDA_CHECK(ensure_dynamic_smem(fa_fwd_kernel<T>, (int)smem));
+  fa_fwd_kernel<T><<<grid, NTH, smem, s>>>((const T*)q, (const T*)k, (const T*)v, (T*)o, lse, tq, tk, H, causal, kl,
+                                           scale);
   return cudaGetLastError();
 }
 
