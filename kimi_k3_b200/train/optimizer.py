@@ -516,50 +516,59 @@ class KimiMuon(torch.optim.Optimizer):
 
     @torch.no_grad()
     def _step_tp_gathered(self, skip, metrics) -> None:
-        """Momentum stays per shard; the momentum-updated shard is all-gathered along its split
-        dimension, orthogonalised as the whole matrix (the same update as one process computes) and
-        each rank applies its own slice."""
+        """Momentum stays per shard; the momentum-updated shards are all-gathered along their split
+        dimension, orthogonalised as whole matrices (the same update as one process computes) and
+        each rank applies its own slice.  Shards of equal shape, split dimension and group move as
+        one batch: one all-gather and one batched Newton-Schulz per batch."""
         import torch.distributed as dist
         for group in self.param_groups:
             lr, mom, wd = group["lr"], group["momentum"], group["weight_decay"]
+            batches: dict = {}
             for p in group["params"]:
                 if p.grad is None or not self._mine(p) or not self._tp_gathered(p):
                     continue
-                st = self.state[p]
-                buf = st.get("momentum_buffer")
-                if buf is None:
-                    buf = st["momentum_buffer"] = torch.zeros_like(p)
-                g = p.grad.to(buf.dtype)
-                if skip is not None:
-                    g = torch.where(skip, torch.zeros((), device=g.device, dtype=g.dtype), g)
-                    buf.mul_(torch.where(skip, 1.0, mom).to(buf.dtype)).add_(g)
-                else:
-                    buf.mul_(mom).add_(g)
-                raw = (g.add(buf, alpha=mom) if group["nesterov"] else buf).contiguous()
-                tp, dim = p._kimi_tp_group, p._kimi_tp_dim
+                key = (id(p._kimi_tp_group), p._kimi_tp_dim, tuple(p.shape), p.dtype, p.device)
+                batches.setdefault(key, []).append(p)
+            for ps in batches.values():
+                tp, dim = ps[0]._kimi_tp_group, ps[0]._kimi_tp_dim
                 world, rank = dist.get_world_size(tp), dist.get_rank(tp)
-                parts = [torch.empty_like(raw) for _ in range(world)]
-                dist.all_gather(parts, raw, group=tp)
-                full = torch.cat(parts, dim)
-                ortho = batched_newton_schulz(full.float()[None], steps=group["ns_steps"], eps=group["eps"],
-                                              dtype=self._resolved_ns_dtype(p.device))[0]
-                scale = max(full.shape) ** 0.5 if group["update_rms_scaling"] else 1.0
-                metrics["raw"].append(full.float().square().mean().sqrt()[None])
-                metrics["ortho"].append(ortho.square().mean().sqrt()[None])
+                raws = []
+                for p in ps:
+                    st = self.state[p]
+                    buf = st.get("momentum_buffer")
+                    if buf is None:
+                        buf = st["momentum_buffer"] = torch.zeros_like(p)
+                    g = p.grad.to(buf.dtype)
+                    if skip is not None:
+                        g = torch.where(skip, torch.zeros((), device=g.device, dtype=g.dtype), g)
+                        buf.mul_(torch.where(skip, 1.0, mom).to(buf.dtype)).add_(g)
+                    else:
+                        buf.mul_(mom).add_(g)
+                    raws.append(g.add(buf, alpha=mom) if group["nesterov"] else buf)
+                local = torch.stack(raws)                               # [n, r, c]
+                n = local.shape[0]
+                parts = torch.empty((world * n,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+                dist.all_gather_into_tensor(parts, local.contiguous(), group=tp)  # rank-major blocks of n
+                full = torch.cat(parts.view((world,) + tuple(local.shape)).unbind(0), dim + 1)  # [n, R, C]
+                ortho = batched_newton_schulz(full.float(), steps=group["ns_steps"], eps=group["eps"],
+                                              dtype=self._resolved_ns_dtype(local.device))
+                scale = max(full.shape[1:]) ** 0.5 if group["update_rms_scaling"] else 1.0
+                metrics["raw"].append(full.float().flatten(1).square().mean(1).sqrt())
+                metrics["ortho"].append(ortho.flatten(1).square().mean(1).sqrt())
                 metrics["scaled"].append(metrics["ortho"][-1] * scale)
-                upd = torch.chunk(ortho, world, dim=dim)[rank].to(p.dtype).mul_(scale)
+                upd = torch.chunk(ortho, world, dim=dim + 1)[rank].to(ps[0].dtype).mul_(scale)
                 lr_eff = torch.where(skip, 0.0, lr) if skip is not None else lr
                 if wd:
-                    p.mul_(1.0 - lr_eff * wd)
+                    torch._foreach_mul_(ps, 1.0 - lr_eff * wd)
                 if torch.is_tensor(lr_eff):
-                    p.add_(upd * (-lr_eff).to(upd.dtype))
+                    upd.mul_((-lr_eff).to(upd.dtype))
+                    torch._foreach_add_(ps, list(upd.unbind(0)))
                 else:
-                    p.add_(upd, alpha=-lr_eff)
-                prms = p.float().square().mean().sqrt().clamp_min(group["eps"])
-                lr_v = lr if torch.is_tensor(lr) else torch.tensor(float(lr), device=prms.device)
-                metrics["ratio"].append((lr_v * metrics["scaled"][-1].mean() / prms)[None])
+                    torch._foreach_add_(ps, list(upd.unbind(0)), alpha=-lr_eff)
+                pn = torch.stack(torch._foreach_norm(ps)).float() / (ps[0].numel() ** 0.5)
+                lr_v = lr if torch.is_tensor(lr) else torch.tensor(float(lr), device=pn.device)
+                metrics["ratio"].append(lr_v * metrics["scaled"][-1] / pn.clamp_min(group["eps"]))
 
-    # ---- bucketed state: one momentum tensor [count, rows, cols] per (group, matrix shape)
     def _ensure_buckets(self) -> list:
         """Per-parameter momentum buffers become views into one tensor per bucket, so a step
         is a handful of launches per bucket instead of a dozen per parameter."""
