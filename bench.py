@@ -140,7 +140,7 @@ def count_launches(engine, batch):
 
 
 # --------------------------------------------------------------------------- reference arm
-def run_reference(args, world, rank, local, amp=True):
+def run_reference(args, world, rank, local, amp=True, weights_bf16=False):
     ref = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref, "src")):
         raise FileNotFoundError("baseline/_ref is not installed")
@@ -160,6 +160,8 @@ def run_reference(args, world, rank, local, amp=True):
     mapping["model"]["vocab_size"] = VOCAB
     torch.manual_seed(1337)
     model = RefKimiK3(ref_build(mapping)).to(dev)
+    if weights_bf16:  # the second reference arm: its stock path on bf16 weights, autocast off
+        model = model.to(torch.bfloat16)
     context = None
     if world > 1:
         from training.distributed.config import DataParallelConfig, DistributedConfig
@@ -238,6 +240,9 @@ def main():
                     help="t4 (default): the flagship t4_wikitext-shaped training step; the others are described in "
                          "kimi_k3_b200/bench/suite.py")
     ap.add_argument("--decode-steps", type=int, default=512, help="gpu80_infer: greedy decode steps per generation")
+    ap.add_argument("--ref-dtype", choices=("auto", "bf16"), default="auto",
+                    help="reference arm: auto = bf16 autocast, else its fp32 path (the anchor); bf16 = the "
+                         "reference model cast to bf16 weights with autocast off")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -259,7 +264,11 @@ def main():
         if not torch.cuda.is_available():
             raise RuntimeError("no CUDA device")
         init_dist(world, local)
-        if args.impl == "reference":
+        if args.impl == "reference" and args.ref_dtype == "bf16":
+            base["note"] = "reference model cast to bf16 weights (model.to(torch.bfloat16)), autocast off"
+            ms, e2e_ms, clocks, h2d, d2h, launches, last_loss = run_reference(args, world, rank, local, amp=False,
+                                                                              weights_bf16=True)
+        elif args.impl == "reference":
             try:
                 ms, e2e_ms, clocks, h2d, d2h, launches, last_loss = run_reference(args, world, rank, local, amp=True)
             except TypeError as exc:
