@@ -111,3 +111,20 @@ def test_inference_yaml_distributed_section(tmp_path):
     for seq, world_size in run_ranks(_yaml_rank, 2, str(tmp_path)):
         assert world_size == 2
         assert torch.equal(seq, ref)
+
+
+def test_cli_infer_single_process(tmp_path, capsys):
+    """``python -m kimi_k3_b200 infer`` without a distributed section: token-id prompt, greedy."""
+    from kimi_k3_b200.cli import main
+    from kimi_k3_b200.config.model_yaml import build_model_from_yaml
+    from kimi_k3_b200.config.profiles import write_pipeline
+    write_pipeline("cpu_smoke", tmp_path)
+    model = build_model_from_yaml(tmp_path / "model.yaml")
+    torch.save({"model_state_dict": model.state_dict(), "format_version": 1}, tmp_path / "ckpt.pt")
+    assert main(["infer", "--model-config", str(tmp_path / "model.yaml"), "--checkpoint", str(tmp_path / "ckpt.pt"),
+                 "--prompt", "5 17 9 33", "--max-new-tokens", "3"]) == 0
+    out = capsys.readouterr().out.splitlines()
+    import json
+    stats = json.loads(out[-1])
+    assert stats["world_size"] == 1 and stats["finish_reason"] in ("length", "eos")
+    assert out[0].startswith("[[5, 17, 9, 33")
