@@ -569,7 +569,9 @@ def run_gpu80_infer(args, world, rank, local, impl):
         generated = int(toks.shape[1])
     clocks = sampler.stop()
     if impl == "ours":
+        from ..parallel.expert_parallel import release_shared_workspaces
         decoder.release()  # the captured step holds NCCL calls: drop it before the process group
+        release_shared_workspaces()
     dec = statistics.median(decode_s)
     batch_tps = GPU80_PROMPTS * generated / dec if dec > 0 else 0.0
     line = {"metric": "decode_tokens_per_s", "unit": "tokens/s", "value": round(batch_tps, 1),

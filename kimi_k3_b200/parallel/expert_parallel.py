@@ -26,8 +26,14 @@ from .data_parallel import QBReducer
 from .tensor_parallel import group_rank, group_size
 
 
-# inference-time fused-exchange workspaces shared by all MoE layers of one shape
+# inference-time fused-exchange workspaces shared by all MoE layers of one shape:
+# key -> (process group, workspace)
 _SHARED_WORKSPACES: dict = {}
+
+
+def release_shared_workspaces() -> None:
+    """Drop the inference-time exchange workspaces (before destroying their process groups)."""
+    _SHARED_WORKSPACES.clear()
 
 
 def expert_range(num_experts: int, group) -> tuple:
@@ -185,14 +191,19 @@ class ExpertParallelMoE(StableLatentMoE):
         from .ep_fused import EPWorkspace
         key = (id(self.group), tokens, top_k, latent, self.config.num_routed_experts)
         shared = not torch.is_grad_enabled()
-        ws = _SHARED_WORKSPACES.get(key) if shared else self._ep_workspace
+        if shared:
+            hit = _SHARED_WORKSPACES.get(key)
+            # the entry keeps its group alive, so a recycled id cannot alias another group
+            ws = hit[1] if hit is not None and hit[0] is self.group else None
+        else:
+            ws = self._ep_workspace
         if ws is None or ws.tokens != tokens or ws.top_k != top_k or ws.latent != latent:
             if torch.cuda.is_current_stream_capturing():
                 raise RuntimeError("the expert-parallel workspace must exist before CUDA-graph capture")
             ws = EPWorkspace(self.group, torch.device("cuda", torch.cuda.current_device()), tokens=tokens, top_k=top_k,
                              latent=latent, num_experts=self.config.num_routed_experts)
             if shared:
-                _SHARED_WORKSPACES[key] = ws
+                _SHARED_WORKSPACES[key] = (self.group, ws)
             else:
                 self._ep_workspace = ws
         return ws
@@ -288,5 +299,5 @@ def scale_local_expert_gradients(model: nn.Module, *, group=None) -> None:
         torch._foreach_mul_(grads, 1.0 / n)
 
 
-__all__ = ["ExpertParallelMoE", "shard_kimi_experts", "expert_range", "exchange_counts",
+__all__ = ["ExpertParallelMoE", "shard_kimi_experts", "expert_range", "exchange_counts", "release_shared_workspaces",
            "local_expert_parameter_ids", "scale_local_expert_gradients"]
