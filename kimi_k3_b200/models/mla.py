@@ -158,7 +158,11 @@ class MLACache:
         if latent_kv.dtype != self.latent_kv.dtype:
             raise TypeError("new latent_kv and cache must share dtype")
         dev = latent_kv.device
+        if dev != self.latent_kv.device:
+            raise ValueError("new latent_kv and cache must share device")
         new_mask = torch.ones(b, t, dtype=torch.bool, device=dev) if attention_mask is None else attention_mask
+        if tuple(new_mask.shape) != (b, t) or new_mask.dtype != torch.bool:
+            raise ValueError("new attention_mask must be boolean with shape [B,T]")
         old_mask = (torch.ones(b, self.cache_length, dtype=torch.bool, device=dev)
                     if self.attention_mask is None else self.attention_mask)
         values = torch.cat((self.latent_kv, latent_kv), dim=1)
