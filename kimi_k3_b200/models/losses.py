@@ -296,13 +296,24 @@ def compute_aligned_cross_entropy(logits, labels, *, alignment, ignore_index, la
 
 class NextTokenCrossEntropyLoss(nn.Module):
     def __init__(self, *, ignore_index=-100, label_smoothing=0.0, zero_valid_policy="raise",
-                 label_alignment="causal_shift"):
+                 label_alignment="causal_shift", alignment=None):
+        """``alignment`` is the reference's name for ``label_alignment`` and may be used instead."""
         super().__init__()
+        if alignment is not None:
+            if label_alignment not in ("causal_shift", alignment):
+                raise ValueError("alignment and label_alignment disagree")
+            label_alignment = alignment
         if label_alignment not in ("causal_shift", "already_aligned"):
             raise ValueError("label_alignment must be 'causal_shift' or 'already_aligned'")
+        if not 0.0 <= float(label_smoothing) < 1.0:
+            raise ValueError("label_smoothing must be in [0, 1)")
         self.ignore_index, self.label_smoothing = ignore_index, float(label_smoothing)
         self.zero_valid_policy = validate_zero_policy(zero_valid_policy)
         self.label_alignment = label_alignment
+
+    @property
+    def alignment(self) -> str:
+        return self.label_alignment
 
     def forward(self, logits, labels, *, attention_mask=None, loss_mask=None, boundary_mask=None,
                 token_weights=None, return_per_token=False) -> TokenCrossEntropyOutput:
