@@ -361,6 +361,8 @@ class VisualPlaceholderComposer(nn.Module):
             return torch.ones(batch_size, dtype=torch.long, device=device)
         if tuple(counts.shape) != (batch_size,) or counts.dtype not in (torch.int32, torch.int64):
             raise ValueError(f"{name} must be an integer tensor of shape {(batch_size,)}")
+        if torch.device(counts.device) != torch.device(device):
+            raise ValueError(f"{name} must be on the text device")
         if torch.any(counts < 0) or int(counts.sum().item()) != item_count:
             raise ValueError(f"{name} must be non-negative and sum to {item_count}")
         return counts
@@ -375,6 +377,8 @@ class VisualPlaceholderComposer(nn.Module):
             return None, None
         if projected.ndim != 3 or projected.shape[-1] != self.d_model:
             raise ValueError(f"{modality} projection must have shape [M,N,{self.d_model}]")
+        if counts is None:
+            raise ValueError(f"{modality}_counts must be resolved before composition")
         cursor, positions, per_sample = 0, [], []
         for bi, n_items in enumerate(counts.tolist()):
             items = [projected[cursor + j][pmask[cursor + j]] for j in range(n_items)]
