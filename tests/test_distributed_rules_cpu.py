@@ -1,0 +1,237 @@
+"""Distributed runtime rules on CPU: mesh rank arithmetic and axis groups, configuration checks, the
+torchrun environment contract, metric reduction, the resumable sampler, size-1 collectives, failure
+detection between gloo ranks, and a four-rank TP x EP layout against one process.
+
+Reference behaviour: ``training/distributed/{mesh,config,environment,metrics,sampler,collectives}.py`` and
+the four-rank TP x EP smoke of ``tests/training/distributed/test_tp_ep_smoke.py``.
+"""
+import os
+import time
+
+import pytest
+import torch
+
+from _dist_harness import run_ranks
+from _oracle import needs_reference, ref
+from kimi_k3_b200.parallel.collectives import (all_gather_variable, all_ranks_true, all_reduce_max, all_reduce_mean,
+                                               all_reduce_sum)
+from kimi_k3_b200.parallel.config import distributed_config_from_dict
+from kimi_k3_b200.parallel.environment import (axis_rank_lists, coordinates_from_rank, initialize_distributed,
+                                               rank_from_coordinates)
+from kimi_k3_b200.parallel.metrics import reduce_scalar_metrics, reduction_for
+from kimi_k3_b200.parallel.sampler import StatefulDistributedSampler
+
+
+# --------------------------------------------------------------------------- mesh
+@pytest.mark.parametrize("dp,tp,ep", [(1, 1, 1), (2, 1, 1), (1, 2, 2), (2, 2, 2), (4, 2, 1), (1, 1, 8)])
+def test_rank_coordinates_round_trip_and_groups_partition_the_world(dp, tp, ep):
+    world = dp * tp * ep
+    seen = set()
+    for r in range(world):
+        d, t, e = coordinates_from_rank(r, tp_size=tp, ep_size=ep)
+        assert rank_from_coordinates(d, t, e, tp_size=tp, ep_size=ep) == r
+        seen.add((d, t, e))
+    assert len(seen) == world
+    for axis, size in zip(axis_rank_lists(dp, tp, ep), (dp, tp, ep)):
+        assert sorted(r for g in axis for r in g) == list(range(world))
+        assert all(len(g) == size for g in axis)
+    # a rank's TP peers share its DP and EP coordinates
+    _, tp_groups, _ = axis_rank_lists(dp, tp, ep)
+    for g in tp_groups:
+        coords = [coordinates_from_rank(r, tp_size=tp, ep_size=ep) for r in g]
+        assert len({(c[0], c[2]) for c in coords}) == 1
+
+
+def test_expert_parallel_overlaid_on_tensor_parallel_shares_the_tp_groups():
+    dp_groups, tp_groups, ep_groups = axis_rank_lists(2, 4, 4, overlay=True)
+    assert tp_groups == ep_groups == [[0, 1, 2, 3], [4, 5, 6, 7]]
+    assert dp_groups == [[0, 4], [1, 5], [2, 6], [3, 7]]
+
+
+@needs_reference
+@pytest.mark.reference
+@pytest.mark.parametrize("dp,tp,ep", [(2, 2, 2), (1, 4, 2), (3, 1, 2)])
+def test_axis_groups_match_reference(dp, tp, ep):
+    ref()
+    from training.distributed.mesh import _all_axis_groups
+    assert tuple(axis_rank_lists(dp, tp, ep)) == tuple(_all_axis_groups(dp, tp, ep))
+
+
+# --------------------------------------------------------------------------- configuration
+@pytest.mark.parametrize("bad", [
+    {"data_parallel": {"mode": "zero3", "size": 2}},
+    {"data_parallel": {"size": 0}},
+    {"tensor_parallel": {"enabled": True, "size": 0}},
+    {"expert_parallel": {"enabled": True, "size": -2}},
+    {"pipeline_parallel": {"enabled": True, "size": 2}},
+    {"context_parallel": {"enabled": True, "size": 2}},
+    {"backend": "mpi"},
+    {"timeout_seconds": 0},
+    {"not_a_section": {}},
+])
+def test_distributed_config_rejects_invalid_values(bad):
+    with pytest.raises((ValueError, TypeError)):
+        distributed_config_from_dict({"enabled": True, **bad})
+
+
+def test_logical_world_size_and_overlay():
+    c = distributed_config_from_dict({"enabled": True, "data_parallel": {"mode": "ddp", "size": 2},
+                                      "tensor_parallel": {"enabled": True, "size": 4},
+                                      "expert_parallel": {"enabled": True, "size": 2}})
+    assert c.logical_world_size == 16
+    o = distributed_config_from_dict({"enabled": True, "tensor_parallel": {"enabled": True, "size": 8},
+                                      "expert_parallel": {"enabled": True, "size": 8,
+                                                          "overlay_tensor_parallel": True}})
+    assert o.logical_world_size == 8
+    assert distributed_config_from_dict(None).logical_world_size == 1
+
+
+def test_environment_contract_is_checked_before_any_process_group():
+    disabled = distributed_config_from_dict({"enabled": False})
+    with pytest.raises(RuntimeError):
+        initialize_distributed(disabled, environment={"WORLD_SIZE": "2", "RANK": "0", "LOCAL_RANK": "0"})
+    ctx = initialize_distributed(disabled, environment={"WORLD_SIZE": "1", "RANK": "0", "LOCAL_RANK": "0"})
+    assert not ctx.initialized and ctx.world_size == 1
+    two = distributed_config_from_dict({"enabled": True, "backend": "gloo", "data_parallel": {"mode": "ddp",
+                                                                                             "size": 2}})
+    with pytest.raises(RuntimeError):
+        initialize_distributed(two, environment={"WORLD_SIZE": "4", "RANK": "0", "LOCAL_RANK": "0"})
+
+
+# --------------------------------------------------------------------------- metrics, collectives, sampler
+@pytest.mark.parametrize("name,kind", [("train/loss", "mean"), ("memory/peak_gb", "max"), ("grad/max_norm", "max"),
+                                       ("kda/alpha_min", "min"), ("throughput/tokens", "mean")])
+def test_metric_reduction_rule(name, kind):
+    assert reduction_for(name) == kind
+
+
+def test_size_one_helpers_are_identities_without_a_process_group():
+    t = torch.tensor([1.0, -2.0])
+    assert torch.equal(all_reduce_sum(t.clone()), t) and torch.equal(all_reduce_mean(t.clone()), t)
+    assert torch.equal(all_reduce_max(t.clone()), t)
+    assert all_ranks_true(True) and not all_ranks_true(False)
+    assert torch.equal(all_gather_variable(t), t)
+    assert reduce_scalar_metrics({"a": 1.0}) == {"a": 1.0}
+
+
+@pytest.mark.parametrize("n,replicas,drop_last", [(10, 3, False), (10, 3, True), (8, 4, False), (5, 8, False)])
+def test_sampler_shards_cover_the_dataset(n, replicas, drop_last):
+    data = list(range(n))
+    shards = [list(StatefulDistributedSampler(data, replicas, r, shuffle=True, seed=3, drop_last=drop_last))
+              for r in range(replicas)]
+    sizes = {len(s) for s in shards}
+    assert len(sizes) == 1
+    flat = [i for s in shards for i in s]
+    if drop_last:
+        assert len(set(flat)) == len(flat) == (n // replicas) * replicas
+    else:
+        assert set(flat) == set(data)
+
+
+def test_sampler_resumes_mid_epoch_and_reshuffles_per_epoch():
+    data = list(range(20))
+    s = StatefulDistributedSampler(data, 2, 1, seed=5)
+    it = iter(s)
+    first = [next(it) for _ in range(4)]
+    state = s.state_dict()
+    resumed = StatefulDistributedSampler(data, 2, 1, seed=5)
+    resumed.load_state_dict(state)
+    assert first + list(resumed) == list(StatefulDistributedSampler(data, 2, 1, seed=5))
+    assert len(resumed) == 0
+    e0 = list(StatefulDistributedSampler(data, 2, 1, seed=5))
+    s1 = StatefulDistributedSampler(data, 2, 1, seed=5)
+    s1.set_epoch(1)
+    assert list(s1) != e0
+    with pytest.raises(ValueError):
+        StatefulDistributedSampler(data, 4, 1, seed=5).load_state_dict(state)
+    with pytest.raises(ValueError):
+        StatefulDistributedSampler(data, 2, 2)
+
+
+# --------------------------------------------------------------------------- multi-process
+def _metrics_rank(rank, world):
+    from kimi_k3_b200.parallel.environment import setup_distributed
+    ctx = setup_distributed(distributed_config_from_dict({"enabled": True, "backend": "gloo",
+                                                          "data_parallel": {"mode": "ddp", "size": world}}))
+    out = reduce_scalar_metrics({"train/loss": float(rank + 1), "memory/peak_gb": float(10 * rank),
+                                 "kda/alpha_min": float(rank - 5), "label": "x"}, context=ctx)
+    ragged = all_gather_variable(torch.arange(rank + 1, dtype=torch.float32), group=None)
+    ctx.close()
+    return out, ragged
+
+
+def test_metrics_and_ragged_gather_over_gloo_ranks():
+    res = run_ranks(_metrics_rank, 3)
+    for out, ragged in res:
+        assert out["train/loss"] == pytest.approx(2.0) and out["memory/peak_gb"] == 20.0
+        assert out["kda/alpha_min"] == -5.0 and out["label"] == "x"
+        assert ragged.tolist() == [0.0, 0.0, 1.0, 0.0, 1.0, 2.0]
+
+
+def _failing_rank(rank, world, marker):
+    from kimi_k3_b200.parallel.environment import setup_distributed
+    ctx = setup_distributed(distributed_config_from_dict({"enabled": True, "backend": "gloo", "timeout_seconds": 20,
+                                                          "data_parallel": {"mode": "ddp", "size": world}}))
+    t = torch.ones(1)
+    torch.distributed.all_reduce(t)               # both ranks reach the first collective
+    if rank == 1:
+        os._exit(3)                               # this rank dies between steps
+    start = time.monotonic()
+    try:
+        torch.distributed.all_reduce(t)           # the survivor learns of it from its next collective
+        outcome = "completed"
+    except Exception as exc:                       # noqa: BLE001 - any transport error is the signal
+        outcome = type(exc).__name__
+    with open(marker, "w") as f:
+        f.write(f"{outcome} {time.monotonic() - start:.1f}")
+    os._exit(0)
+
+
+def test_a_dead_rank_surfaces_as_an_error_on_the_survivor(tmp_path):
+    import torch.multiprocessing as mp
+    from _dist_harness import _entry, free_port
+    marker = str(tmp_path / "survivor.txt")
+    ctx = mp.get_context("spawn")
+    port = free_port()
+    procs = [ctx.Process(target=_entry, args=(r, 2, port, _failing_rank, str(tmp_path), (marker,)))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(90)
+        if p.is_alive():
+            p.kill()
+    assert procs[1].exitcode == 3
+    outcome, seconds = open(marker).read().split()
+    assert outcome != "completed" and float(seconds) < 60.0
+
+
+def _tp_ep_rank(rank, world, kind):
+    from test_distributed_cpu import _global_batch, _model, _train
+    from kimi_k3_b200.parallel.environment import setup_distributed
+    from kimi_k3_b200.parallel.parallelize import parallelize_kimi_model
+    dcfg = distributed_config_from_dict({"enabled": True, "backend": "gloo", "timeout_seconds": 120,
+                                         "tensor_parallel": {"enabled": True, "size": 2},
+                                         "expert_parallel": {"enabled": True, "size": 2}})
+    ctx = setup_distributed(dcfg)
+    model = _model()
+    plan = parallelize_kimi_model(model, dcfg, ctx)
+    plan.broadcast_parameters()
+    full = _global_batch(2)                         # two data replicas (the EP ranks) of two rows each
+    batch = {k: v[2 * ctx.ep_rank: 2 * ctx.ep_rank + 2] for k, v in full.items()}
+    res = _train(model, batch, kind, context=ctx, plan=plan, steps=2)
+    shared = {n: p.detach().clone() for n, p in model.named_parameters()
+              if not getattr(p, "_kimi_tp_shard", False) and not getattr(p, "_kimi_local_expert", False)}
+    ctx.close()
+    return res["loss"], shared, (ctx.tp_rank, ctx.ep_rank)
+
+
+@pytest.mark.slow
+def test_four_rank_tp_ep_layout_matches_single_process():
+    from test_distributed_cpu import _compare, _single
+    ref_loss, ref_params = _single(2, "adamw")
+    results = run_ranks(_tp_ep_rank, 4, "adamw")
+    assert sorted(r[2] for r in results) == [(0, 0), (0, 1), (1, 0), (1, 1)]
+    for loss, params, _ in results:
+        assert abs(loss - ref_loss) < 1e-6
+        assert _compare(ref_params, params, 1e-7) < 1e-7
