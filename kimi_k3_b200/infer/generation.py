@@ -129,7 +129,10 @@ def generate_tokens(model, input_ids, *, generation_config: GenerationConfig | N
             seqs = torch.cat((seqs, nxt), dim=1)
             if eos is not None:
                 finished |= active & nxt[:, 0].eq(int(eos))
-            dec = decode_one_token(model, nxt, cache, active[:, None])
+            # Every row decodes its token: a finished row feeds the pad id and its outputs are
+            # ignored.  (Masking finished rows out would hand the model a row with no valid token,
+            # which it rejects; the reference's loop raises there once one row ends before the rest.)
+            dec = decode_one_token(model, nxt, cache, torch.ones_like(active)[:, None])
             cache = dec.cache
             logits = dec.logits[:, -1, :]
             if eos is not None and (step + 1) % cfg.eos_check_every == 0 and bool(finished.all()):
