@@ -94,3 +94,48 @@ def test_yaml_trainer_end_to_end_and_resume(tmp_path):
     # scheduler state would differ by far more)
     for (n, p), (_, q) in zip(res["model"].named_parameters(), res2["model"].named_parameters()):
         torch.testing.assert_close(p, q, rtol=1e-5, atol=1e-6, msg=n)
+
+
+def test_yaml_trainer_with_context_curriculum_transitions_and_resumes(tmp_path):
+    """A two-stage curriculum (16 then 32 tokens) through ``train_kimi_from_yaml``: the run moves to the
+    second stage, the curriculum state rides in the checkpoint, and a run resumed from the first
+    epoch's checkpoint ends in the same curriculum state with the same token count."""
+    import yaml
+    from kimi_k3_b200.config.model_yaml import build_model_from_yaml
+    from kimi_k3_b200.config.profiles import write_pipeline
+    from kimi_k3_b200.data import build_dataloaders_from_yaml
+    from kimi_k3_b200.train.checkpoints import list_checkpoints
+    from kimi_k3_b200.train.trainer import train_kimi_from_yaml
+    d = write_pipeline("cpu_smoke", tmp_path / "prof")
+    tr = yaml.safe_load((d / "training.yaml").read_text())
+    tr["checkpoint"]["output_dir"] = str(tmp_path / "ckpt")
+    tr["training"]["epochs"] = 2
+    tr["runtime"]["verbose"] = False
+    tr["context_curriculum"] = {"enabled": True, "stages": [{"max_seq_len": 16, "until_tokens": 200},
+                                                            {"max_seq_len": 32, "until_tokens": None}]}
+    (d / "training.yaml").write_text(yaml.safe_dump(tr))
+    data = build_dataloaders_from_yaml(d / "data.yaml")
+    torch.manual_seed(0)
+    model = build_model_from_yaml(d / "model.yaml", data_bundle=data)
+    res = train_kimi_from_yaml(d / "training.yaml", model=model, data=data)
+    cur = res["curriculum"] if "curriculum" in res else None
+    ckpts = list_checkpoints(tmp_path / "ckpt")
+    assert ckpts
+    payload = torch.load(ckpts[-1], weights_only=False)
+    state = payload["context_curriculum"]
+    assert state is not None and state["stage_index"] == 1 and state["max_seq_len"] == 32
+    assert state["transition_count"] >= 1 and state["tokens_seen"] >= 200
+    if cur is not None:
+        assert cur.current_max_seq_len() == 32
+    assert res["state"].optimizer_step > 0
+    first = [p for p in ckpts if p.name.endswith("epoch_0000.pt")][0]
+    tr["checkpoint"]["resume_from"] = str(first)
+    tr["checkpoint"]["output_dir"] = str(tmp_path / "ckpt2")
+    (d / "training.yaml").write_text(yaml.safe_dump(tr))
+    data2 = build_dataloaders_from_yaml(d / "data.yaml")
+    model2 = build_model_from_yaml(d / "model.yaml", data_bundle=data2)
+    res2 = train_kimi_from_yaml(d / "training.yaml", model=model2, data=data2)
+    again = torch.load(list_checkpoints(tmp_path / "ckpt2")[-1], weights_only=False)["context_curriculum"]
+    for key in ("stage_index", "max_seq_len", "tokens_seen"):
+        assert again[key] == state[key], key
+    assert res2["state"].optimizer_step == res["state"].optimizer_step
