@@ -156,3 +156,17 @@ def test_left_to_right_ragged_prompts_use_each_rows_last_valid_token(model):
     assert torch.equal(out.generated_ids[1], alone.generated_ids[0])
     with pytest.raises(TypeError):
         generate_tokens(model, padded, attention_mask=mask.long())
+
+
+def test_image_prompt_generation_matches_the_full_multimodal_forward():
+    torch.manual_seed(0)
+    cfg = kimi_k3_cpu_tiny_config()
+    m = KimiK3(cfg).double().eval()
+    ids = torch.randint(5, 128, (1, 10))
+    ids[0, 2:6] = cfg.image_token_id              # a 16x16 image gives 4 tokens after the 2x2 shuffle
+    img = torch.randn(1, 3, 16, 16, dtype=torch.float64)
+    out = generate_tokens(m, ids, generation_config=GenerationConfig(max_new_tokens=4),
+                          prefill_kwargs={"pixel_values": img})
+    with torch.no_grad():
+        full = m(input_ids=torch.cat((ids, out.generated_ids[:, :3]), 1), pixel_values=img).logits
+    assert torch.equal(full[:, -4:].argmax(-1), out.generated_ids)
