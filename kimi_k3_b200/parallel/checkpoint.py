@@ -6,10 +6,14 @@ sha256 fingerprints of the model / data / training configs and the optimizer par
 registry) and a ``SUCCESS`` marker, then renames the directory into place; loading requires
 the marker and the same topology. The on-disk layout is kept identical.
 
+Sharded data parallelism (``data_parallel.mode: fsdp``): every rank's file holds its own shards
+(:class:`LocalShard`) of the DTensor parameters and optimizer states; loading rebuilds the DTensors
+around the live parameters' meshes, so a sharded run resumes on the same topology.
+
 Addition: :func:`export_rank0_full_checkpoint` also un-shards tensor-parallel heads,
 vocabulary shards and expert-parallel experts (all-gathers along the recorded shard
-dimensions), so a TP/EP run exports an ordinary single-process checkpoint; the reference
-supports data parallelism only.
+dimensions) and gathers fully sharded parameters, so a TP / EP / FSDP run exports an ordinary
+single-process checkpoint; the reference supports data parallelism only.
 """
 from __future__ import annotations
 
@@ -25,6 +29,7 @@ import torch.distributed as dist
 import torch.nn as nn
 
 from ..train.checkpoints import restore_rng_state, rng_state, save_checkpoint, to_host
+from .fsdp import reshard_all
 
 FORMAT_VERSION = 1
 SUCCESS_MARKER = "SUCCESS"
@@ -41,6 +46,71 @@ def _barrier(context) -> None:
 
 def _unwrap(model):
     return model.module if hasattr(model, "module") else model
+
+
+# --------------------------------------------------------------------------- sharded (FSDP) values
+class LocalShard:
+    """This rank's shard of a sharded (DTensor) value, as stored in its per-rank file.  Loading
+    rebuilds the DTensor around it with the mesh and placements of the live parameter."""
+
+    __slots__ = ("tensor",)
+
+    def __init__(self, tensor: torch.Tensor):
+        self.tensor = tensor
+
+    def __reduce__(self):
+        return (LocalShard, (self.tensor,))
+
+
+def _dtensor_type():
+    try:
+        from torch.distributed.tensor import DTensor
+    except ImportError:  # pragma: no cover - every supported torch has it
+        return None
+    return DTensor
+
+
+def _to_local_shards(obj):
+    dt = _dtensor_type()
+    if dt is not None and isinstance(obj, dt):
+        return LocalShard(obj.to_local().detach().cpu())
+    if isinstance(obj, dict):
+        return {k: _to_local_shards(v) for k, v in obj.items()}
+    if isinstance(obj, list):
+        return [_to_local_shards(v) for v in obj]
+    if isinstance(obj, tuple):
+        return tuple(_to_local_shards(v) for v in obj)
+    return obj
+
+
+def _as_dtensor(local: torch.Tensor, like, dtype=None):
+    dt = _dtensor_type()
+    return dt.from_local(local.to(device=like.device, dtype=dtype or local.dtype), like.device_mesh, like.placements,
+                         shape=like.shape, stride=like.stride(), run_check=False)
+
+
+def _model_state_for_load(model: nn.Module, saved: dict) -> dict:
+    """Rebuild the DTensor entries of a saved model state around the live parameters' meshes."""
+    dt = _dtensor_type()
+    live = model.state_dict()
+    out = dict(saved)
+    for k, v in saved.items():
+        if isinstance(v, LocalShard):
+            cur = live.get(k)
+            if dt is None or not isinstance(cur, dt):
+                raise ValueError(f"checkpoint holds a shard of {k}, but the model's {k} is not sharded")
+            out[k] = _as_dtensor(v.tensor, cur, dtype=cur.dtype)
+    return out
+
+
+def _restore_optimizer_shards(optimizer) -> None:
+    """After ``load_state_dict``: optimizer states saved as shards become DTensors of their parameter."""
+    inner = [o for o in (getattr(optimizer, "muon", None), getattr(optimizer, "adamw", None)) if o is not None]
+    for opt in inner or [optimizer]:
+        for p, st in getattr(opt, "state", {}).items():
+            for key, val in list(st.items()):
+                if isinstance(val, LocalShard):
+                    st[key] = _as_dtensor(val.tensor, p)
 
 
 def checkpoint_metadata(context, *, step: int, model_config=None, data_config=None, training_config=None,
@@ -72,8 +142,9 @@ def save_distributed_checkpoint(path, *, model: nn.Module, context, step: int, o
     _barrier(context)
 
     def st(obj):
-        return None if obj is None else to_host(obj.state_dict())
-    payload = {"model": to_host(_unwrap(model).state_dict()), "optimizer": st(optimizer), "scheduler": st(scheduler),
+        return None if obj is None else to_host(_to_local_shards(obj.state_dict()))
+    reshard_all(_unwrap(model))
+    payload = {"model": st(_unwrap(model)), "optimizer": st(optimizer), "scheduler": st(scheduler),
                "scaler": st(scaler), "ema": st(ema), "trainer_state": st(trainer_state), "curriculum": st(curriculum),
                "diagnostics": st(diagnostics), "sampler": st(sampler), "rng": rng_state() if save_rng else None,
                "extra": extra or {}}
@@ -102,9 +173,11 @@ def load_distributed_checkpoint(path, *, model: nn.Module, context, optimizer=No
     if actual != expected:
         raise ValueError(f"distributed checkpoint topology change is unsupported: saved={actual}, current={expected}")
     payload = torch.load(src / f"rank_{context.global_rank:05d}.pt", map_location="cpu", weights_only=False)
-    incompatible = _unwrap(model).load_state_dict(payload["model"], strict=strict)
+    raw = _unwrap(model)
+    incompatible = raw.load_state_dict(_model_state_for_load(raw, payload["model"]), strict=strict)
     if optimizer is not None and payload.get("optimizer") is not None:
         optimizer.load_state_dict(payload["optimizer"])
+        _restore_optimizer_shards(optimizer)
     for owner, key in ((scheduler, "scheduler"), (scaler, "scaler"), (ema, "ema"), (trainer_state, "trainer_state"),
                        (curriculum, "curriculum"), (diagnostics, "diagnostics"), (sampler, "sampler")):
         if owner is not None and payload.get(key) is not None:
@@ -130,7 +203,11 @@ def full_state_dict(model: nn.Module, context) -> dict:
     from .kimi_tp import TensorParallelKDA, TensorParallelMLA
     from .tensor_parallel import VocabParallelEmbedding, VocabParallelLMHead
     raw = _unwrap(model)
+    reshard_all(raw)
     sd = raw.state_dict(keep_vars=False)
+    dt = _dtensor_type()
+    if dt is not None:  # sharded data parallelism: gather every shard (same key order on all ranks)
+        sd = {k: (v.full_tensor() if isinstance(v, dt) else v) for k, v in sd.items()}
     out = {}
     handled = set()
     for name, mod in raw.named_modules():
@@ -182,5 +259,5 @@ def export_rank0_full_checkpoint(path, *, model: nn.Module, context, model_confi
     return target
 
 
-__all__ = ["FORMAT_VERSION", "SUCCESS_MARKER", "fingerprint", "checkpoint_metadata", "save_distributed_checkpoint",
+__all__ = ["FORMAT_VERSION", "SUCCESS_MARKER", "LocalShard", "fingerprint", "checkpoint_metadata", "save_distributed_checkpoint",
            "load_distributed_checkpoint", "full_state_dict", "export_rank0_full_checkpoint"]

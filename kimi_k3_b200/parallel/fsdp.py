@@ -107,6 +107,20 @@ def shard_kimi_model(model: nn.Module, config, context) -> nn.Module:
     return model
 
 
+def reshard_all(model: nn.Module) -> None:
+    """Put every sharded unit back on its shards.  The root unit keeps its gathered parameters
+    registered after a forward (backward reuses them), so a parameter list or state dict read
+    after an evaluation forward would otherwise hold the gathered root tensors instead of the
+    DTensor shards that receive the reduce-scattered gradients.  A no-op without sharding."""
+    try:
+        from torch.distributed.fsdp import FSDPModule
+    except ImportError:  # pragma: no cover - every supported torch has it
+        return
+    for m in model.modules():
+        if isinstance(m, FSDPModule):
+            m.reshard()
+
+
 def is_sharded(p: torch.Tensor) -> bool:
     from torch.distributed.tensor import DTensor
     return isinstance(p, DTensor)

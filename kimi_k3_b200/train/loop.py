@@ -147,6 +147,8 @@ def train_one_epoch(model, dataloader, optimizer, *, device="cpu", scheduler=Non
     if max_batches is not None and max_batches < 0:
         raise ValueError("max_batches must be None or non-negative")
     device = torch.device(device)
+    from ..parallel.fsdp import reshard_all
+    reshard_all(model)  # after an evaluation forward the sharded root would list gathered tensors
     model.to(device).train()
     state = TrainerState() if state is None else state
     raw = _unwrap(model)

@@ -235,3 +235,105 @@ def test_four_rank_tp_ep_layout_matches_single_process():
     for loss, params, _ in results:
         assert abs(loss - ref_loss) < 1e-6
         assert _compare(ref_params, params, 1e-7) < 1e-7
+
+
+def _fsdp_ckpt_rank(rank, world, path):
+    from test_distributed_cpu import _global_batch, _model, _train
+    from kimi_k3_b200.parallel.checkpoint import (export_rank0_full_checkpoint, load_distributed_checkpoint,
+                                                  save_distributed_checkpoint)
+    from kimi_k3_b200.parallel.environment import setup_distributed
+    from kimi_k3_b200.parallel.fsdp import shard_kimi_model
+    from kimi_k3_b200.train.optimizer import KimiOptimizerConfig, build_kimi_optimizer
+    dcfg = distributed_config_from_dict({"enabled": True, "backend": "gloo", "timeout_seconds": 120,
+                                         "data_parallel": {"mode": "fsdp", "size": world}})
+    ctx = setup_distributed(dcfg)
+    full = _global_batch(world)
+    batch = {k: v[2 * rank: 2 * rank + 2] for k, v in full.items()}
+
+    def build():
+        m = _model()
+        shard_kimi_model(m, dcfg, ctx)
+        m._test_params = [p for p in m.parameters() if p.requires_grad]   # the shards, as the trainer keeps
+        opt, _ = build_kimi_optimizer(m, KimiOptimizerConfig(kind="adamw", adamw_lr=1e-3, adamw_eps=1e-2))
+        return m, opt
+
+    def step(m, opt):
+        from kimi_k3_b200.train.loop import train_one_epoch
+        from kimi_k3_b200.parallel.fsdp import sharded_grad_norm
+        train_one_epoch(m, [batch], opt, grad_clip=0.5, use_mtp=True, distributed_context=ctx,
+                        grad_norm_fn=lambda: sharded_grad_norm(m._test_params))
+
+    a, oa = build()
+    step(a, oa)                                            # optimizer state exists before the save
+    a.eval()
+    with torch.no_grad():
+        ref = a(input_ids=full["input_ids"][:2], attention_mask=full["attention_mask"][:2]).logits
+    a.train()
+    save_distributed_checkpoint(os.path.join(path, "step_1"), model=a, context=ctx, step=1, optimizer=oa)
+    export_rank0_full_checkpoint(os.path.join(path, "full.pt"), model=a, context=ctx)
+    b, ob = build()
+    load_distributed_checkpoint(os.path.join(path, "step_1"), model=b, context=ctx, optimizer=ob)
+    b.eval()
+    with torch.no_grad():
+        got = b(input_ids=full["input_ids"][:2], attention_mask=full["attention_mask"][:2]).logits
+    b.train()
+    step(a, oa)                                            # one more step on both: same parameters
+    step(b, ob)
+    worst = max((pa.full_tensor() - pb.full_tensor()).abs().max().item()
+                for pa, pb in zip(a.parameters(), b.parameters()))
+    ctx.close()
+    return (ref - got).abs().max().item(), worst, ref
+
+
+def test_fully_sharded_checkpoint_round_trip_and_full_export(tmp_path):
+    from test_distributed_cpu import _model
+    from kimi_k3_b200.train.checkpoints import load_checkpoint
+    res = run_ranks(_fsdp_ckpt_rank, 2, str(tmp_path))
+    for logits_diff, param_diff, _ in res:
+        assert logits_diff == 0.0 and param_diff == 0.0
+    single = _model()
+    info = load_checkpoint(tmp_path / "full.pt", single)
+    assert not info["missing_keys"] and not info["unexpected_keys"]
+    single.eval()
+    from test_distributed_cpu import _global_batch
+    b = _global_batch(2)
+    with torch.no_grad():
+        out = single(input_ids=b["input_ids"][:2], attention_mask=b["attention_mask"][:2]).logits
+    assert (out - res[0][2]).abs().max().item() < 1e-12
+
+
+def _fsdp_eval_between_steps_rank(rank, world, with_eval):
+    from test_distributed_cpu import _global_batch, _model
+    from kimi_k3_b200.parallel.environment import setup_distributed
+    from kimi_k3_b200.parallel.fsdp import shard_kimi_model, sharded_grad_norm
+    from kimi_k3_b200.train.loop import eval_one_epoch, train_one_epoch
+    from kimi_k3_b200.train.optimizer import KimiOptimizerConfig, build_kimi_optimizer
+    dcfg = distributed_config_from_dict({"enabled": True, "backend": "gloo", "timeout_seconds": 120,
+                                         "data_parallel": {"mode": "fsdp", "size": world}})
+    ctx = setup_distributed(dcfg)
+    full = _global_batch(world)
+    batch = {k: v[2 * rank: 2 * rank + 2] for k, v in full.items()}
+    m = _model()
+    shard_kimi_model(m, dcfg, ctx)
+    shards = [p for p in m.parameters() if p.requires_grad]
+    opt, _ = build_kimi_optimizer(m, KimiOptimizerConfig(kind="adamw", adamw_lr=1e-3, adamw_eps=1e-2))
+    norms = []
+    for _ in range(2):
+        res = train_one_epoch(m, [batch], opt, grad_clip=0.5, use_mtp=True, distributed_context=ctx,
+                              grad_norm_fn=lambda: sharded_grad_norm(shards))
+        norms.append(res["grad_norm_pre_clip"])
+        if with_eval:  # an evaluation pass between epochs, as the trainer runs one
+            eval_one_epoch(m, [batch], use_mtp=True, distributed_context=ctx)
+    from kimi_k3_b200.parallel.fsdp import reshard_all
+    reshard_all(m)
+    out = {n: p.full_tensor().clone() for n, p in m.named_parameters()}
+    ctx.close()
+    return norms, out
+
+
+def test_an_evaluation_pass_between_sharded_epochs_changes_no_update():
+    plain = run_ranks(_fsdp_eval_between_steps_rank, 2, False)
+    with_eval = run_ranks(_fsdp_eval_between_steps_rank, 2, True)
+    for (na, pa), (nb, pb) in zip(plain, with_eval):
+        assert na == pytest.approx(nb, rel=1e-9)
+        assert max((pa[n] - pb[n]).abs().max().item() for n in pa) == 0.0
