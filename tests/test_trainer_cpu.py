@@ -139,3 +139,39 @@ def test_yaml_trainer_with_context_curriculum_transitions_and_resumes(tmp_path):
     for key in ("stage_index", "max_seq_len", "tokens_seen"):
         assert again[key] == state[key], key
     assert res2["state"].optimizer_step == res["state"].optimizer_step
+
+
+def test_single_threaded_resume_is_bit_identical(tmp_path):
+    """With one CPU thread (a fixed reduction order) a run resumed from its first epoch's checkpoint
+    ends with exactly the weights of the uninterrupted run: model, optimizer, scheduler, RNG and
+    sampler state all round-trip."""
+    import yaml
+    from kimi_k3_b200.config.model_yaml import build_model_from_yaml
+    from kimi_k3_b200.config.profiles import write_pipeline
+    from kimi_k3_b200.data import build_dataloaders_from_yaml
+    from kimi_k3_b200.train.trainer import train_kimi_from_yaml
+    threads = torch.get_num_threads()
+    torch.set_num_threads(1)
+    try:
+        d = write_pipeline("cpu_smoke", tmp_path / "prof")
+        tr = yaml.safe_load((d / "training.yaml").read_text())
+        tr["checkpoint"]["output_dir"] = str(tmp_path / "ckpt")
+        tr["training"]["epochs"] = 2
+        tr["runtime"]["verbose"] = False
+        (d / "training.yaml").write_text(yaml.safe_dump(tr))
+        data = build_dataloaders_from_yaml(d / "data.yaml")
+        torch.manual_seed(0)
+        res = train_kimi_from_yaml(d / "training.yaml", model=build_model_from_yaml(d / "model.yaml", data_bundle=data),
+                                   data=data)
+        tr["checkpoint"]["resume_from"] = str(tmp_path / "ckpt" / "kimi_k3_cpu_smoke_epoch_0000.pt")
+        tr["checkpoint"]["output_dir"] = str(tmp_path / "ckpt2")
+        (d / "training.yaml").write_text(yaml.safe_dump(tr))
+        data2 = build_dataloaders_from_yaml(d / "data.yaml")
+        res2 = train_kimi_from_yaml(d / "training.yaml",
+                                    model=build_model_from_yaml(d / "model.yaml", data_bundle=data2), data=data2)
+    finally:
+        torch.set_num_threads(threads)
+    for (n, p), (_, q) in zip(res["model"].named_parameters(), res2["model"].named_parameters()):
+        assert torch.equal(p, q), n
+    for (n, b), (_, c) in zip(res["model"].named_buffers(), res2["model"].named_buffers()):
+        assert torch.equal(b, c), n
