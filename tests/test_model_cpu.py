@@ -229,3 +229,28 @@ def test_mtp_gradients_reach_shared_embeddings_and_backbone():
     det.mtp.config = type(det.mtp.config).from_dict({**det.mtp.config.to_dict(), "detach_backbone_hidden": True})
     det(input_ids=ids, use_mtp=True).mtp_logits.square().mean().backward()
     assert all(p.grad is None or p.grad.abs().sum() == 0 for p in det.backbone.parameters())
+
+
+@needs_reference
+@pytest.mark.reference
+@pytest.mark.parametrize("vision,mtp", [(True, True), (False, True), (False, False)])
+def test_parameter_report_and_backbone_counts_match_reference(vision, mtp):
+    ref()
+    import dataclasses
+    from src.kimi_k3.config import kimi_k3_cpu_tiny_config as rcfg
+    from src.kimi_k3_mini import KimiK3 as RK
+    from kimi_k3_b200.models.diagnostics import parameter_counts
+    torch.manual_seed(0)
+    ours = KimiK3(kimi_k3_cpu_tiny_config(enable_vision=vision, enable_mtp=mtp))
+    theirs = RK(rcfg(enable_vision=vision, enable_mtp=mtp))
+    assert dataclasses.asdict(ours.parameter_report()) == dataclasses.asdict(theirs.parameter_report())
+    assert ours.num_parameters() == theirs.num_parameters()
+    assert ours.num_parameters(only_trainable=True) == theirs.num_parameters(only_trainable=True)
+    rb = theirs.backbone
+    from src.hybrid_backbone.diagnostics import parameter_counts as rcounts
+    inner = rb.backbone if hasattr(rb, "backbone") else rb
+    want = rcounts(inner.groups, inner.final_global_layer, inner.final_norm,
+                   getattr(inner, "final_output_attnres", None))
+    got = parameter_counts(ours.backbone.backbone if hasattr(ours.backbone, "backbone") else ours.backbone)
+    for key, value in want.items():
+        assert got[key] == value, key
