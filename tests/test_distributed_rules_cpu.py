@@ -337,3 +337,14 @@ def test_an_evaluation_pass_between_sharded_epochs_changes_no_update():
     for (na, pa), (nb, pb) in zip(plain, with_eval):
         assert na == pytest.approx(nb, rel=1e-9)
         assert max((pa[n] - pb[n]).abs().max().item() for n in pa) == 0.0
+
+
+def test_expert_parallel_with_histogram_balancing_matches_single_process():
+    """EP reduces the Quantile-Balancing histograms over the expert group (one all-reduce of the
+    counts); the routing biases and parameters then follow the single-process run."""
+    from test_distributed_cpu import _compare, _rank, _single
+    ref_loss, ref_params = _single(2, "adamw", qb="histogram")
+    results = run_ranks(_rank, 2, "ep", "adamw", "histogram")
+    for loss, params, _ in results:
+        assert abs(loss - ref_loss) < 1e-6
+        assert _compare(ref_params, params, 1e-7) < 1e-7
