@@ -348,3 +348,53 @@ def test_expert_parallel_with_histogram_balancing_matches_single_process():
     for loss, params, _ in results:
         assert abs(loss - ref_loss) < 1e-6
         assert _compare(ref_params, params, 1e-7) < 1e-7
+
+
+def _dp_accum_rank(rank, world, micro):
+    from test_distributed_cpu import _model
+    from kimi_k3_b200.parallel.environment import setup_distributed
+    from kimi_k3_b200.parallel.parallelize import parallelize_kimi_model
+    from kimi_k3_b200.train.engine import MoEController
+    from kimi_k3_b200.train.loop import train_one_epoch
+    from kimi_k3_b200.train.optimizer import KimiOptimizerConfig, build_kimi_optimizer
+    dcfg = distributed_config_from_dict({"enabled": True, "backend": "gloo", "timeout_seconds": 120,
+                                         "data_parallel": {"mode": "ddp", "size": world}})
+    ctx = setup_distributed(dcfg)
+    model = _model()
+    plan = parallelize_kimi_model(model, dcfg, ctx)
+    plan.broadcast_parameters()
+    opt, _ = build_kimi_optimizer(model, KimiOptimizerConfig(kind="adamw", adamw_lr=1e-3, adamw_eps=1e-2))
+    mine = micro[rank::world]
+    res = train_one_epoch(model, mine, opt, grad_accum_steps=len(mine), grad_clip=0.5, use_mtp=True,
+                          moe_controller=MoEController(model, reducer=plan.qb_reducer()), distributed_context=ctx,
+                          grad_reducer=plan.sync_gradients, grad_norm_fn=plan.grad_norm)
+    out = {n: p.detach().clone() for n, p in model.named_parameters()}
+    ctx.close()
+    return res["loss"], out
+
+
+def _uneven_micro_batches(n=4):
+    g = torch.Generator().manual_seed(11)
+    out = []
+    for i in range(n):
+        ids = torch.randint(5, 128, (2, 16), generator=g)
+        mask = torch.ones(2, 16, dtype=torch.bool)
+        mask[1, 4 + 3 * i:] = False                     # each micro-batch has a different token count
+        out.append({"input_ids": ids, "labels": ids.clone(), "attention_mask": mask})
+    return out
+
+
+def test_data_parallel_accumulation_windows_are_token_exact():
+    from test_distributed_cpu import _compare, _model
+    from kimi_k3_b200.train.engine import MoEController
+    from kimi_k3_b200.train.loop import train_one_epoch
+    from kimi_k3_b200.train.optimizer import KimiOptimizerConfig, build_kimi_optimizer
+    micro = _uneven_micro_batches(4)
+    single = _model()
+    opt, _ = build_kimi_optimizer(single, KimiOptimizerConfig(kind="adamw", adamw_lr=1e-3, adamw_eps=1e-2))
+    ref_res = train_one_epoch(single, micro, opt, grad_accum_steps=4, grad_clip=0.5, use_mtp=True,
+                              moe_controller=MoEController(single))
+    ref_params = {n: p.detach().clone() for n, p in single.named_parameters()}
+    for loss, params in run_ranks(_dp_accum_rank, 2, micro):
+        assert abs(loss - ref_res["loss"]) < 1e-6
+        assert _compare(ref_params, params, 1e-7) < 1e-7
