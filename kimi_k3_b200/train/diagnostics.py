@@ -84,6 +84,15 @@ class MetricBatch:
         self.values.update(other.values if isinstance(other, MetricBatch) else other)
 
     def materialize(self) -> dict:
+        """Under sharded data parallelism a metric computed from a DTensor parameter is a DTensor;
+        it is completed with its collective here, in insertion order, which every rank shares."""
+        try:
+            from torch.distributed.tensor import DTensor
+        except ImportError:  # pragma: no cover
+            DTensor = ()
+        for k, v in list(self.values.items()):
+            if isinstance(v, DTensor):
+                self.values[k] = v.full_tensor()
         dev_names = [k for k, v in self.values.items() if torch.is_tensor(v)]
         out = {k: float(v) for k, v in self.values.items() if not torch.is_tensor(v)}
         if dev_names:

@@ -398,3 +398,54 @@ def test_data_parallel_accumulation_windows_are_token_exact():
     for loss, params in run_ranks(_dp_accum_rank, 2, micro):
         assert abs(loss - ref_res["loss"]) < 1e-6
         assert _compare(ref_params, params, 1e-7) < 1e-7
+
+
+def _fsdp_trainer_rank(rank, world, root, resume):
+    import yaml
+    from pathlib import Path
+    from kimi_k3_b200.config.model_yaml import build_model_from_yaml
+    from kimi_k3_b200.data import build_dataloaders_from_yaml
+    from kimi_k3_b200.parallel.config import distributed_config_from_dict
+    from kimi_k3_b200.parallel.environment import setup_distributed
+    from kimi_k3_b200.train.trainer import train_kimi_from_yaml
+    d = Path(root) / "prof"
+    tr = yaml.safe_load((d / "training.yaml").read_text())
+    tr["checkpoint"]["output_dir"] = str(Path(root) / ("resumed" if resume else "ckpt"))
+    if resume:
+        tr["checkpoint"]["resume_from"] = str(Path(root) / "ckpt" / "kimi_k3_cpu_smoke_epoch_0000")
+    path = d / f"training_{rank}_{int(resume)}.yaml"
+    path.write_text(yaml.safe_dump(tr))
+    ctx = setup_distributed(distributed_config_from_dict(tr["distributed"]))
+    data = build_dataloaders_from_yaml(d / "data.yaml", distributed_context=ctx)
+    torch.manual_seed(0)
+    model = build_model_from_yaml(d / "model.yaml", data_bundle=data)
+    res = train_kimi_from_yaml(path, model=model, data=data, distributed_context=ctx)
+    from kimi_k3_b200.parallel.checkpoint import full_state_dict
+    full = {k: v.clone() for k, v in full_state_dict(res["model"], ctx).items()}
+    steps = res["state"].optimizer_step
+    ctx.close()
+    return steps, full
+
+
+@pytest.mark.slow
+def test_fully_sharded_yaml_trainer_checkpoints_every_epoch_and_resumes(tmp_path):
+    """The YAML trainer on two gloo ranks with ``data_parallel.mode: fsdp``: an evaluation pass and a
+    sharded checkpoint after each epoch, then a run resumed from the first epoch's checkpoint ends with
+    the weights of the uninterrupted run."""
+    import yaml
+    from kimi_k3_b200.config.profiles import write_pipeline
+    d = write_pipeline("cpu_smoke", tmp_path / "prof")
+    tr = yaml.safe_load((d / "training.yaml").read_text())
+    tr["training"]["epochs"] = 2
+    tr["training"]["max_batches_per_epoch"] = 2
+    tr["runtime"]["verbose"] = False
+    tr["distributed"] = {"enabled": True, "backend": "gloo", "timeout_seconds": 120,
+                         "data_parallel": {"mode": "fsdp", "size": 2}}
+    (d / "training.yaml").write_text(yaml.safe_dump(tr))
+    first = run_ranks(_fsdp_trainer_rank, 2, str(tmp_path), False)
+    assert (tmp_path / "ckpt" / "kimi_k3_cpu_smoke_epoch_0001" / "SUCCESS").is_file()
+    assert (tmp_path / "ckpt" / "kimi_k3_cpu_smoke_epoch_0000" / "rank_00001.pt").is_file()
+    again = run_ranks(_fsdp_trainer_rank, 2, str(tmp_path), True)
+    assert first[0][0] == again[0][0] == 4
+    for k, v in first[0][1].items():
+        torch.testing.assert_close(again[0][1][k], v, rtol=1e-5, atol=1e-6, msg=k)
