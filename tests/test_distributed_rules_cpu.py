@@ -427,11 +427,22 @@ def _fsdp_trainer_rank(rank, world, root, resume):
     return steps, full
 
 
+YAML_LAYOUTS = {
+    "fsdp": {"data_parallel": {"mode": "fsdp", "size": 2}},
+    "ddp": {"data_parallel": {"mode": "ddp", "size": 2}},
+    "tp": {"tensor_parallel": {"enabled": True, "size": 2}},
+    "ep": {"expert_parallel": {"enabled": True, "size": 2}},
+    "tp_ep_overlay": {"tensor_parallel": {"enabled": True, "size": 2},
+                      "expert_parallel": {"enabled": True, "size": 2, "overlay_tensor_parallel": True}},
+}
+
+
 @pytest.mark.slow
-def test_fully_sharded_yaml_trainer_checkpoints_every_epoch_and_resumes(tmp_path):
-    """The YAML trainer on two gloo ranks with ``data_parallel.mode: fsdp``: an evaluation pass and a
-    sharded checkpoint after each epoch, then a run resumed from the first epoch's checkpoint ends with
-    the weights of the uninterrupted run."""
+@pytest.mark.parametrize("layout", sorted(YAML_LAYOUTS))
+def test_distributed_yaml_trainer_checkpoints_every_epoch_and_resumes(tmp_path, layout):
+    """The YAML trainer on two gloo ranks for every parallel layout: diagnostics, an evaluation pass and a
+    distributed checkpoint after each epoch, then a run resumed from the first epoch's checkpoint ends
+    with the weights of the uninterrupted run."""
     import yaml
     from kimi_k3_b200.config.profiles import write_pipeline
     d = write_pipeline("cpu_smoke", tmp_path / "prof")
@@ -439,8 +450,7 @@ def test_fully_sharded_yaml_trainer_checkpoints_every_epoch_and_resumes(tmp_path
     tr["training"]["epochs"] = 2
     tr["training"]["max_batches_per_epoch"] = 2
     tr["runtime"]["verbose"] = False
-    tr["distributed"] = {"enabled": True, "backend": "gloo", "timeout_seconds": 120,
-                         "data_parallel": {"mode": "fsdp", "size": 2}}
+    tr["distributed"] = {"enabled": True, "backend": "gloo", "timeout_seconds": 120, **YAML_LAYOUTS[layout]}
     (d / "training.yaml").write_text(yaml.safe_dump(tr))
     first = run_ranks(_fsdp_trainer_rank, 2, str(tmp_path), False)
     assert (tmp_path / "ckpt" / "kimi_k3_cpu_smoke_epoch_0001" / "SUCCESS").is_file()
