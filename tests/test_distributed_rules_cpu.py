@@ -400,7 +400,7 @@ def test_data_parallel_accumulation_windows_are_token_exact():
         assert _compare(ref_params, params, 1e-7) < 1e-7
 
 
-def _fsdp_trainer_rank(rank, world, root, resume):
+def _fsdp_trainer_rank(rank, world, root, resume, overrides=None):
     import yaml
     from pathlib import Path
     from kimi_k3_b200.config.model_yaml import build_model_from_yaml
@@ -410,6 +410,8 @@ def _fsdp_trainer_rank(rank, world, root, resume):
     from kimi_k3_b200.train.trainer import train_kimi_from_yaml
     d = Path(root) / "prof"
     tr = yaml.safe_load((d / "training.yaml").read_text())
+    for section, values in (overrides or {}).items():
+        tr[section] = {**tr.get(section, {}), **values} if isinstance(values, dict) else values
     tr["checkpoint"]["output_dir"] = str(Path(root) / ("resumed" if resume else "ckpt"))
     if resume:
         tr["checkpoint"]["resume_from"] = str(Path(root) / "ckpt" / "kimi_k3_cpu_smoke_epoch_0000")
@@ -457,5 +459,29 @@ def test_distributed_yaml_trainer_checkpoints_every_epoch_and_resumes(tmp_path, 
     assert (tmp_path / "ckpt" / "kimi_k3_cpu_smoke_epoch_0000" / "rank_00001.pt").is_file()
     again = run_ranks(_fsdp_trainer_rank, 2, str(tmp_path), True)
     assert first[0][0] == again[0][0] == 4
+    for k, v in first[0][1].items():
+        torch.testing.assert_close(again[0][1][k], v, rtol=1e-5, atol=1e-6, msg=k)
+
+
+@pytest.mark.slow
+def test_data_parallel_trainer_with_curriculum_ema_and_accumulation_resumes(tmp_path):
+    """DDP over two gloo ranks with a two-stage context curriculum (loader rebuilt on the transition
+    with its distributed sampler), EMA and two-micro-batch windows: checkpoints and resumes."""
+    import yaml
+    from kimi_k3_b200.config.profiles import write_pipeline
+    d = write_pipeline("cpu_smoke", tmp_path / "prof")
+    tr = yaml.safe_load((d / "training.yaml").read_text())
+    tr["training"]["epochs"] = 2
+    tr["training"]["gradient_accumulation_steps"] = 2
+    tr["runtime"]["verbose"] = False
+    tr["runtime"]["use_ema"] = True
+    tr["context_curriculum"] = {"enabled": True, "stages": [{"max_seq_len": 16, "until_tokens": 300},
+                                                            {"max_seq_len": 32, "until_tokens": None}]}
+    tr["distributed"] = {"enabled": True, "backend": "gloo", "timeout_seconds": 120,
+                         "data_parallel": {"mode": "ddp", "size": 2}}
+    (d / "training.yaml").write_text(yaml.safe_dump(tr))
+    first = run_ranks(_fsdp_trainer_rank, 2, str(tmp_path), False)
+    again = run_ranks(_fsdp_trainer_rank, 2, str(tmp_path), True)
+    assert first[0][0] == again[0][0] > 0
     for k, v in first[0][1].items():
         torch.testing.assert_close(again[0][1][k], v, rtol=1e-5, atol=1e-6, msg=k)
