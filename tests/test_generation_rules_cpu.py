@@ -170,3 +170,19 @@ def test_image_prompt_generation_matches_the_full_multimodal_forward():
     with torch.no_grad():
         full = m(input_ids=torch.cat((ids, out.generated_ids[:, :3]), 1), pixel_values=img).logits
     assert torch.equal(full[:, -4:].argmax(-1), out.generated_ids)
+
+
+def test_graph_decoder_and_generate_agree_when_one_row_finishes_first(model):
+    from kimi_k3_b200.infer import GraphDecoder
+    torch.manual_seed(5)
+    ids = torch.randint(5, 128, (2, 7))
+    greedy = generate_tokens(model, ids, generation_config=GenerationConfig(max_new_tokens=5))
+    eos = int(greedy.generated_ids[0, 0])
+    if eos in greedy.generated_ids[1].tolist():
+        pytest.skip("both rows emit the chosen token")
+    cfg = GenerationConfig(max_new_tokens=5, eos_token_id=eos, pad_token_id=0)
+    a = generate_tokens(model, ids, generation_config=cfg)
+    b = GraphDecoder(model, max_length=16, generation_config=cfg).generate(ids)
+    assert torch.equal(a.generated_ids, b.generated_ids)
+    assert a.generated_ids[0].tolist() == [eos] + [0] * 4
+    assert torch.equal(a.generated_ids[1], greedy.generated_ids[1])
