@@ -13,7 +13,7 @@ import pytest
 import torch
 import torch.nn.functional as F
 
-from _oracle import max_diff
+from _oracle import max_diff, needs_reference, ref
 from kimi_k3_b200.models.vision import (DropPath, LearnedAbsolutePositionEmbedding, MoonViTEncoder,
                                         SpatialTokenPixelShuffle, VisionEncoderConfig, VisionPatchEmbedding,
                                         VisionProjector, VisionSelfAttention, VisualPlaceholderComposer,
@@ -196,3 +196,43 @@ def test_window_partition_and_merge_round_trip(h, w, ws):
     assert torch.equal(window_merge(win, ws, meta), x)
     # the first window holds the top-left ws x ws block, row by row
     assert torch.equal(win[0].reshape(ws, ws, 5)[:min(ws, h), :min(ws, w)], x[0, :ws, :ws])
+
+
+@needs_reference
+@pytest.mark.reference
+@pytest.mark.parametrize("kind", ["hierarchical", "swin"])
+def test_kimi_k3_with_ablation_encoders_matches_reference(kind):
+    """The full model with the hierarchical or Swin encoder as its vision tower: logits, loss and a
+    backward pass, against the reference model holding the same weights; the config round-trips."""
+    import dataclasses
+    ref()
+    import src.vision.hierarchical_encoder as rh
+    import src.vision.swin_encoder as rs
+    from src.kimi_k3.config import kimi_k3_cpu_tiny_config as rcfg
+    from src.kimi_k3_mini import KimiK3 as RK
+    from kimi_k3_b200 import KimiK3, kimi_k3_cpu_tiny_config
+    from kimi_k3_b200.models.kimi_k3 import KimiK3Config, VisionProjectorConfig
+    from kimi_k3_b200.models.vision_ablations import HierarchicalVisionConfig, SwinVisionConfig
+    kw = dict(image_size=32, patch_size=4, embed_dims=(8, 16), num_heads=(2, 4))
+    if kind == "hierarchical":
+        ours_v, theirs_v = (HierarchicalVisionConfig(depths=(1, 1), **kw),
+                            rh.HierarchicalVisionConfig(depths=(1, 1), **kw))
+    else:
+        ours_v = SwinVisionConfig(depths=(2, 2), window_size=2, **kw)
+        theirs_v = rs.SwinVisionConfig(depths=(2, 2), window_size=2, **kw)
+    base, rbase = kimi_k3_cpu_tiny_config(), rcfg()
+    cfg = dataclasses.replace(base, vision=ours_v, vision_projector=VisionProjectorConfig(64, 32, 16))
+    rc = dataclasses.replace(rbase, vision=theirs_v,
+                             vision_projector=dataclasses.replace(rbase.vision_projector, input_dim=64))
+    assert KimiK3Config.from_dict(cfg.to_dict()) == cfg
+    torch.manual_seed(0)
+    ours, theirs = KimiK3(cfg).double(), RK(rc).double()
+    theirs.load_state_dict(ours.state_dict())
+    img = torch.randn(1, 3, 32, 32, dtype=F64)
+    ids = torch.randint(5, 128, (1, 12))
+    ids[0, 2:6] = cfg.image_token_id          # 8x8 patches, one 2x pooling / merge, 2x2 shuffle -> 4 tokens
+    a = ours(input_ids=ids, pixel_values=img, labels=ids, use_mtp=True)
+    b = theirs(input_ids=ids, pixel_values=img, labels=ids, use_mtp=True)
+    assert max_diff(a.logits, b.logits) < 1e-12 and abs(a.loss.item() - b.loss.item()) < 1e-12
+    a.loss.backward()
+    assert all(p.grad is not None for n, p in ours.named_parameters() if n.startswith("vision_encoder"))
