@@ -137,3 +137,24 @@ def test_reference_loaders_read_the_generated_model_and_data_yaml(generated, nam
     assert ref_model(d / "model.yaml").to_dict() == load_model_config(d / "model.yaml").to_dict()
     theirs, ours = ref_data(d / "data.yaml"), load_data_config(d / "data.yaml")
     assert theirs.name == ours.name
+
+
+@needs_reference
+@pytest.mark.reference
+@pytest.mark.parametrize("vision_type,extra", [
+    ("moonvit", dict(image_size=16, patch_size=4, embed_dim=16, depth=1, num_heads=4)),
+    ("hierarchical", dict(image_size=32, patch_size=4, embed_dims=[8, 16], depths=[1, 1], num_heads=[2, 4])),
+    ("swin", dict(image_size=32, patch_size=4, embed_dims=[8, 16], depths=[2, 2], num_heads=[2, 4], window_size=2)),
+])
+def test_model_yaml_vision_types_match_reference(generated, vision_type, extra):
+    import copy
+    ref()
+    from src.kimi_k3.yaml_config import build_model_config_from_mapping as rbuild
+    values = yaml.safe_load((generated / "cpu_smoke" / "model.yaml").read_text())
+    values["model"]["vision"] = {"enabled": True, "type": vision_type, **extra, "projector": {"hidden_dim": 32}}
+    ours = build_model_config_from_mapping(copy.deepcopy(values))
+    assert ours.to_dict() == rbuild(copy.deepcopy(values)).to_dict()
+    bad = copy.deepcopy(values)
+    bad["model"]["vision"]["type"] = "convnext"
+    with pytest.raises((ConfigError, ValueError)):
+        build_model_config_from_mapping(bad)
