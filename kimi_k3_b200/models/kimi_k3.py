@@ -407,7 +407,9 @@ class KimiK3(nn.Module):
 
         emb = self.embed_tokens(input_ids) if input_ids is not None else inputs_embeds
         vis_out = meta = None
-        if input_ids is not None:
+        # Decode steps carry generated tokens only: a generated id that equals a visual placeholder
+        # is an ordinary token there (the visual inputs were consumed by the prefill).
+        if input_ids is not None and mode != "decode":
             emb, vis_out, meta = prepare_multimodal_embeddings(
                 config=c, input_ids=input_ids, text_embeddings=emb, attention_mask=attention_mask,
                 pixel_values=pixel_values, video_values=video_values, vision_attention_mask=vision_attention_mask,

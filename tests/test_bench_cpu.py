@@ -93,3 +93,29 @@ def test_mtp_parameter_counts_match_reference():
     assert ours["shared_embedding_lm_overlap"] == ours["shared_lm_head"]  # tied weights
     out, lines = _run(bench_mtp, ["--device", "cpu", "--iterations", "2"])
     assert lines[-1] == f"unique_mtp_parameters={ours['unique_mtp_total']}"
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("impl", ["ours", "reference"])
+def test_bench_cpu_smoke_prints_one_json_line(impl):
+    """``bench.py --config cpu_smoke`` (both arms) prints a single JSON result line with the metric,
+    its value and unit, the step time and the decode figures."""
+    import json
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    if impl == "reference":
+        from conftest import reference_available
+        if not reference_available():
+            pytest.skip("reference package not installed")
+    proc = subprocess.run([sys.executable, "bench.py", "--config", "cpu_smoke", "--steps", "2", "--warmup", "3",
+                           "--impl", impl], cwd=root, capture_output=True, text=True, timeout=600)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    lines = [ln for ln in proc.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1
+    out = json.loads(lines[0])
+    assert out["metric"] == "train_tokens_per_s" and out["unit"] == "tokens/s" and out["value"] > 0
+    assert out["steps"] == 2 and out["warmup"] == 3 and out["higher_is_better"] is True
+    assert out["decode"]["generated_tokens"] == 8
+    assert (out.get("impl") == "reference") == (impl == "reference")

@@ -186,3 +186,19 @@ def test_graph_decoder_and_generate_agree_when_one_row_finishes_first(model):
     assert torch.equal(a.generated_ids, b.generated_ids)
     assert a.generated_ids[0].tolist() == [eos] + [0] * 4
     assert torch.equal(a.generated_ids[1], greedy.generated_ids[1])
+
+
+def test_a_generated_placeholder_id_decodes_as_an_ordinary_token():
+    """A vision model may emit its image or video placeholder id; the next decode step embeds it as a
+    token (the visual inputs were consumed by the prefill) instead of failing the placeholder check."""
+    torch.manual_seed(0)
+    cfg = kimi_k3_cpu_tiny_config()
+    m = KimiK3(cfg).double().eval()
+    ids = torch.randint(5, 128, (2, 6))
+    with torch.no_grad():
+        pre = m.prefill(ids)
+        for placeholder in (cfg.image_token_id, cfg.video_token_id):
+            st = m.decode_step(torch.full((2, 1), placeholder), pre.cache.clone())
+            assert torch.isfinite(st.logits).all()
+        with pytest.raises(ValueError):   # in a prompt, a placeholder still needs its image
+            m.prefill(torch.tensor([[5, cfg.image_token_id, 6]]))
