@@ -111,3 +111,30 @@ def test_batch_limit_scheduler_and_ema_hooks():
         train_one_epoch(m, _batches(1), opt, grad_accum_steps=0)
     with pytest.raises(ValueError):
         train_one_epoch(m, _batches(1), opt, max_batches=-1)
+
+
+def test_image_batches_train_and_evaluate_through_the_loop():
+    """Batches carrying ``pixel_values`` (four placeholder tokens per image) pass through the training and
+    evaluation loops; a video of two frames composes into its placeholders too."""
+    from kimi_k3_b200.train.loop import eval_one_epoch
+    torch.manual_seed(0)
+    cfg = kimi_k3_cpu_tiny_config()
+    m = KimiK3(cfg)
+    opt = build_kimi_optimizer(m, KimiOptimizerConfig(muon_lr=0.01))[0]
+    batches = []
+    for _ in range(3):
+        ids = torch.randint(5, 128, (2, 16))
+        ids[:, 2:6] = cfg.image_token_id
+        batches.append({"input_ids": ids, "labels": ids.masked_fill(ids == cfg.image_token_id, -100),
+                        "attention_mask": torch.ones(2, 16, dtype=torch.bool),
+                        "pixel_values": torch.randn(2, 3, 16, 16)})
+    vision_before = {n: p.detach().clone() for n, p in m.named_parameters() if n.startswith("vision_")}
+    res = train_one_epoch(m, batches, opt, use_mtp=True, moe_controller=MoEController(m), grad_clip=1.0)
+    assert res["optimizer_steps"] == 3 and math.isfinite(res["loss"])
+    moved = [n for n, p in m.named_parameters() if n in vision_before and not torch.equal(p, vision_before[n])]
+    assert moved                                    # the vision tower trains as well
+    assert math.isfinite(eval_one_epoch(m, batches, use_mtp=True)["loss"])
+    vids = torch.randint(5, 128, (1, 20))
+    vids[0, 3:11] = cfg.video_token_id              # two frames of four tokens each
+    out = m(input_ids=vids, video_values=torch.randn(1, 2, 3, 16, 16), labels=vids, use_mtp=True)
+    assert math.isfinite(out.loss.item())
