@@ -160,6 +160,24 @@ def _metrics_rank(rank, world):
     return out, ragged
 
 
+def _uneven_metrics_rank(rank, world):
+    from kimi_k3_b200.parallel.environment import setup_distributed
+    ctx = setup_distributed(distributed_config_from_dict({"enabled": True, "backend": "gloo",
+                                                          "data_parallel": {"mode": "ddp", "size": world}}))
+    mine = {"train/loss": float(rank + 1)}
+    if rank == 1:   # optional metrics that only this rank logged
+        mine.update({"diag/rms": 4.0, "memory/peak_gb": 7.0, "kda/alpha_min": -1.0})
+    out = reduce_scalar_metrics(mine, context=ctx)
+    ctx.close()
+    return out
+
+
+def test_metric_reduction_tolerates_ranks_that_log_different_metrics():
+    for out in run_ranks(_uneven_metrics_rank, 2):
+        assert out["train/loss"] == pytest.approx(1.5)
+        assert out["diag/rms"] == 4.0 and out["memory/peak_gb"] == 7.0 and out["kda/alpha_min"] == -1.0
+
+
 def test_metrics_and_ragged_gather_over_gloo_ranks():
     res = run_ranks(_metrics_rank, 3)
     for out, ragged in res:
@@ -452,6 +470,8 @@ def test_distributed_yaml_trainer_checkpoints_every_epoch_and_resumes(tmp_path, 
     tr["training"]["epochs"] = 2
     tr["training"]["max_batches_per_epoch"] = 2
     tr["runtime"]["verbose"] = False
+    tr["diagnostics"]["standard_every_steps"] = 1   # every diagnostics tier runs (ranks may degrade apart)
+    tr["diagnostics"]["deep_every_steps"] = 2
     tr["distributed"] = {"enabled": True, "backend": "gloo", "timeout_seconds": 120, **YAML_LAYOUTS[layout]}
     (d / "training.yaml").write_text(yaml.safe_dump(tr))
     first = run_ranks(_fsdp_trainer_rank, 2, str(tmp_path), False)
