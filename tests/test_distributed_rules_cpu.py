@@ -320,43 +320,6 @@ def test_fully_sharded_checkpoint_round_trip_and_full_export(tmp_path):
     assert (out - res[0][2]).abs().max().item() < 1e-12
 
 
-def _fsdp_eval_between_steps_rank(rank, world, with_eval):
-    from test_distributed_cpu import _global_batch, _model
-    from kimi_k3_b200.parallel.environment import setup_distributed
-    from kimi_k3_b200.parallel.fsdp import shard_kimi_model, sharded_grad_norm
-    from kimi_k3_b200.train.loop import eval_one_epoch, train_one_epoch
-    from kimi_k3_b200.train.optimizer import KimiOptimizerConfig, build_kimi_optimizer
-    dcfg = distributed_config_from_dict({"enabled": True, "backend": "gloo", "timeout_seconds": 120,
-                                         "data_parallel": {"mode": "fsdp", "size": world}})
-    ctx = setup_distributed(dcfg)
-    full = _global_batch(world)
-    batch = {k: v[2 * rank: 2 * rank + 2] for k, v in full.items()}
-    m = _model()
-    shard_kimi_model(m, dcfg, ctx)
-    shards = [p for p in m.parameters() if p.requires_grad]
-    opt, _ = build_kimi_optimizer(m, KimiOptimizerConfig(kind="adamw", adamw_lr=1e-3, adamw_eps=1e-2))
-    norms = []
-    for _ in range(2):
-        res = train_one_epoch(m, [batch], opt, grad_clip=0.5, use_mtp=True, distributed_context=ctx,
-                              grad_norm_fn=lambda: sharded_grad_norm(shards))
-        norms.append(res["grad_norm_pre_clip"])
-        if with_eval:  # an evaluation pass between epochs, as the trainer runs one
-            eval_one_epoch(m, [batch], use_mtp=True, distributed_context=ctx)
-    from kimi_k3_b200.parallel.fsdp import reshard_all
-    reshard_all(m)
-    out = {n: p.full_tensor().clone() for n, p in m.named_parameters()}
-    ctx.close()
-    return norms, out
-
-
-def test_an_evaluation_pass_between_sharded_epochs_changes_no_update():
-    plain = run_ranks(_fsdp_eval_between_steps_rank, 2, False)
-    with_eval = run_ranks(_fsdp_eval_between_steps_rank, 2, True)
-    for (na, pa), (nb, pb) in zip(plain, with_eval):
-        assert na == pytest.approx(nb, rel=1e-9)
-        assert max((pa[n] - pb[n]).abs().max().item() for n in pa) == 0.0
-
-
 def test_expert_parallel_with_histogram_balancing_matches_single_process():
     """EP reduces the Quantile-Balancing histograms over the expert group (one all-reduce of the
     counts); the routing biases and parameters then follow the single-process run."""
@@ -468,7 +431,7 @@ def test_distributed_yaml_trainer_checkpoints_every_epoch_and_resumes(tmp_path, 
     d = write_pipeline("cpu_smoke", tmp_path / "prof")
     tr = yaml.safe_load((d / "training.yaml").read_text())
     tr["training"]["epochs"] = 2
-    tr["training"]["max_batches_per_epoch"] = 2
+    tr["training"]["max_batches_per_epoch"] = 1
     tr["runtime"]["verbose"] = False
     tr["diagnostics"]["standard_every_steps"] = 1   # every diagnostics tier runs (ranks may degrade apart)
     tr["diagnostics"]["deep_every_steps"] = 2
@@ -478,7 +441,7 @@ def test_distributed_yaml_trainer_checkpoints_every_epoch_and_resumes(tmp_path, 
     assert (tmp_path / "ckpt" / "kimi_k3_cpu_smoke_epoch_0001" / "SUCCESS").is_file()
     assert (tmp_path / "ckpt" / "kimi_k3_cpu_smoke_epoch_0000" / "rank_00001.pt").is_file()
     again = run_ranks(_fsdp_trainer_rank, 2, str(tmp_path), True)
-    assert first[0][0] == again[0][0] == 4
+    assert first[0][0] == again[0][0] == 2
     for k, v in first[0][1].items():
         torch.testing.assert_close(again[0][1][k], v, rtol=1e-5, atol=1e-6, msg=k)
 
