@@ -185,7 +185,10 @@ class GraphDecoder:
 
     # ------------------------------------------------------------------ API
     @torch.inference_mode()
-    def generate(self, input_ids: torch.Tensor, attention_mask: torch.Tensor | None = None) -> GenerationOutput:
+    def generate(self, input_ids: torch.Tensor, attention_mask: torch.Tensor | None = None, *,
+                 prefill_kwargs: dict | None = None) -> GenerationOutput:
+        """``prefill_kwargs`` go to the prompt's forward only (``pixel_values``, ``video_values``, their
+        counts and masks): the visual inputs are consumed by the prefill, decode steps are text."""
         cfg, model, dev = self.cfg, self.model, self.device
         input_ids = input_ids.to(device=dev, dtype=torch.long)
         if input_ids.ndim != 2 or input_ids.shape[1] == 0:
@@ -208,7 +211,8 @@ class GraphDecoder:
             sync()
             t0 = time.perf_counter()
             with self._autocast():
-                pre = model(input_ids=input_ids, attention_mask=attention_mask, use_cache=True, return_dict=True)
+                pre = model(input_ids=input_ids, attention_mask=attention_mask, use_cache=True, return_dict=True,
+                            **(prefill_kwargs or {}))
             logits = last_prompt_logits(pre.logits, attention_mask)
             self.vocab = int(logits.shape[-1])
             pen = cfg.repetition_penalty not in (None, 1)
@@ -314,12 +318,12 @@ class GraphDecoder:
 
 def graph_generate(model, input_ids, *, max_length: int | None = None,
                    generation_config: GenerationConfig | None = None, attention_mask=None,
-                   use_graph: bool | None = None) -> GenerationOutput:
+                   use_graph: bool | None = None, prefill_kwargs: dict | None = None) -> GenerationOutput:
     """One-call form of :class:`GraphDecoder` (``max_length`` defaults to prompt + new tokens)."""
     cfg = generation_config or GenerationConfig()
     ml = max_length if max_length is not None else int(input_ids.shape[1]) + cfg.max_new_tokens
     return GraphDecoder(model, max_length=ml, generation_config=cfg, use_graph=use_graph).generate(
-        input_ids, attention_mask)
+        input_ids, attention_mask, prefill_kwargs=prefill_kwargs)
 
 
 __all__ = ["GraphDecoder", "graph_generate", "serving_copy"]

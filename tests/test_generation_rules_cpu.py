@@ -202,3 +202,19 @@ def test_a_generated_placeholder_id_decodes_as_an_ordinary_token():
             assert torch.isfinite(st.logits).all()
         with pytest.raises(ValueError):   # in a prompt, a placeholder still needs its image
             m.prefill(torch.tensor([[5, cfg.image_token_id, 6]]))
+
+
+def test_graph_decoder_serves_image_prompts():
+    from kimi_k3_b200.infer import GraphDecoder
+    torch.manual_seed(0)
+    cfg = kimi_k3_cpu_tiny_config()
+    m = KimiK3(cfg).double().eval()
+    ids = torch.randint(5, 128, (1, 10))
+    ids[0, 2:6] = cfg.image_token_id
+    img = torch.randn(1, 3, 16, 16, dtype=torch.float64)
+    gcfg = GenerationConfig(max_new_tokens=4)
+    eager = generate_tokens(m, ids, generation_config=gcfg, prefill_kwargs={"pixel_values": img})
+    served = GraphDecoder(m, max_length=16, generation_config=gcfg).generate(ids, prefill_kwargs={"pixel_values": img})
+    assert torch.equal(eager.generated_ids, served.generated_ids)
+    with pytest.raises(ValueError):     # the placeholders need their image
+        GraphDecoder(m, max_length=16, generation_config=gcfg).generate(ids)
