@@ -175,3 +175,31 @@ def test_objective_dispatch():
     out = full("rl", current_logprobs=torch.zeros(1, 2, requires_grad=True), old_logprobs=torch.zeros(1, 2),
                action_mask=torch.ones(1, 2, dtype=torch.bool), advantages=torch.ones(1))
     assert out.phase.value == "rl" and torch.isfinite(out.loss)
+
+
+def test_sft_phase_trains_the_model_through_the_objective():
+    """Three optimizer steps on the SFT objective (assistant tokens only) lower its loss; the RL phase
+    refuses to run until its unpublished coefficients are configured."""
+    from kimi_k3_b200 import KimiK3, kimi_k3_cpu_tiny_config
+    from kimi_k3_b200.models.posttrain import KimiLossConfig, KimiTrainingObjective
+    from kimi_k3_b200.train.optimizer import KimiOptimizerConfig, build_kimi_optimizer
+    torch.manual_seed(0)
+    m = KimiK3(kimi_k3_cpu_tiny_config(enable_vision=False))
+    opt, _ = build_kimi_optimizer(m, KimiOptimizerConfig(muon_lr=0.01))
+    objective = KimiTrainingObjective(KimiLossConfig())
+    ids = torch.randint(5, 128, (2, 12))
+    assistant = torch.zeros(2, 12, dtype=torch.bool)
+    assistant[:, 6:] = True
+    losses = []
+    for _ in range(3):
+        bundle = objective("sft", logits=m(input_ids=ids).logits, labels=ids, assistant_mask=assistant)
+        opt.zero_grad()
+        bundle.loss.backward()
+        opt.step()
+        losses.append(bundle.loss.item())
+    assert losses[2] < losses[0]
+    with pytest.raises(ValueError):
+        objective("rl", current_logprobs=torch.zeros(2, 4), old_logprobs=torch.zeros(2, 4),
+                  action_mask=torch.ones(2, 4, dtype=torch.bool), rewards=torch.ones(2))
+    with pytest.raises(ValueError):
+        objective("sft", logits=m(input_ids=ids).logits, labels=ids, rewards=torch.ones(2))
