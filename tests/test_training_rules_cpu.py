@@ -230,3 +230,37 @@ def test_jsonl_and_memory_loggers(tmp_path):
     mem = MemoryLogger()
     mem.log(3, {"x": 1})
     assert mem.records == [{"step": 3, "x": 1}]
+
+
+@needs_reference
+@pytest.mark.reference
+def test_checkpoints_move_between_the_implementations(tmp_path):
+    """A format-v2 checkpoint written by the reference loads into this package's model (and the
+    reverse) with identical logits afterwards."""
+    ref()
+    from src.kimi_k3.config import kimi_k3_cpu_tiny_config as rcfg
+    from src.kimi_k3_mini import KimiK3 as RK
+    from training.checkpoints import load_checkpoint as ref_load
+    from training.checkpoints import save_checkpoint as ref_save
+    from kimi_k3_b200 import KimiK3, kimi_k3_cpu_tiny_config
+    from kimi_k3_b200.train.checkpoints import load_checkpoint, save_checkpoint
+    torch.manual_seed(0)
+    theirs = RK(rcfg(enable_vision=False))
+    ours = KimiK3(kimi_k3_cpu_tiny_config(enable_vision=False))
+    with torch.no_grad():
+        for p in theirs.parameters():
+            p.add_(0.01 * torch.randn_like(p))
+    ref_save(tmp_path / "ref.pt", theirs, epoch=1, global_step=7)
+    load_checkpoint(tmp_path / "ref.pt", ours)
+    ids = torch.randint(5, 128, (2, 9))
+    theirs.eval()
+    ours.eval()
+    with torch.no_grad():
+        assert torch.equal(ours(input_ids=ids).logits, theirs(input_ids=ids).logits)
+        for p in ours.parameters():
+            p.mul_(0.5)
+    save_checkpoint(tmp_path / "ours.pt", ours, epoch=2, global_step=9)
+    back = RK(rcfg(enable_vision=False)).eval()
+    ref_load(tmp_path / "ours.pt", back)
+    with torch.no_grad():
+        assert torch.equal(back(input_ids=ids).logits, ours(input_ids=ids).logits)
