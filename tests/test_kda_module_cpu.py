@@ -359,3 +359,23 @@ def test_bf16_forward_is_bitwise_equal_to_reference():
     a = ours.to(torch.bfloat16)(x).hidden_states
     b = theirs.to(torch.bfloat16)(x).hidden_states
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("g_scale", [-5.0, -0.01])
+def test_fp32_chunkwise_is_stable_under_extreme_decay(g_scale):
+    """Full 64-token chunks at the strongest (g near g_min = -5) and weakest decays: the fp32 chunk form
+    stays finite and within fp32 round-off of the fp64 recurrence (no exp(+|cumulative decay|) blow-up)."""
+    from kimi_k3_b200.models.kda import chunkwise_kda, recurrent_kda
+    import torch.nn.functional as F
+    torch.manual_seed(0)
+    b, t, h, k, v = 1, 256, 2, 16, 16
+    q = F.normalize(torch.randn(b, t, h, k), dim=-1)
+    kk = F.normalize(torch.randn(b, t, h, k), dim=-1)
+    vv = torch.randn(b, t, h, v)
+    g = g_scale * torch.rand(b, t, h, k).clamp_min(0.5)
+    beta = torch.rand(b, t, h)
+    want = recurrent_kda(q.double(), kk.double(), vv.double(), g.double(), beta.double(), None, True)
+    got = chunkwise_kda(q, kk, vv, g, beta, None, True, chunk_size=64)
+    assert torch.isfinite(got.hidden_states).all() and torch.isfinite(got.final_state).all()
+    assert max_diff(got.hidden_states, want.hidden_states) < 1e-5
+    assert max_diff(got.final_state, want.final_state) < 1e-5
