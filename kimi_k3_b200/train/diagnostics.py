@@ -562,6 +562,10 @@ class KimiDiagnosticCollector:
         self.previous_state_rms: dict = {}
         self.active_level: str | None = None
         self._pending = MetricBatch()
+        # Distributed runs: the budget decision is MAX-reduced over this group (on this device) so that
+        # every rank degrades on the same steps and runs the same diagnostics (and their collectives).
+        self.budget_group = None
+        self.budget_device = None
 
     def level_for_step(self, step: int) -> str | None:
         level = self.config.level_for_step(step)
@@ -679,6 +683,11 @@ class KimiDiagnosticCollector:
             metrics["diagnostics/time_fraction"] = metrics["train/diagnostics_time_fraction"] = frac
         over = (metrics.get("diagnostics/time_fraction", 0.0) > self.config.max_diagnostic_time_fraction or
                 metrics.get("diagnostics/persistent_gpu_bytes", 0.0) > self.config.max_persistent_gpu_bytes)
+        if self.budget_device is not None and torch.distributed.is_available() and torch.distributed.is_initialized() \
+                and torch.distributed.get_world_size(self.budget_group) > 1:
+            flag = torch.tensor([float(over)], device=self.budget_device)
+            torch.distributed.all_reduce(flag, op=torch.distributed.ReduceOp.MAX, group=self.budget_group)
+            over = bool(flag.item() > 0)
         if over:
             self.degrade_until_step = max(self.degrade_until_step, step + self.config.standard_every_steps)
         metrics["diagnostics/budget_exceeded"] = float(over)

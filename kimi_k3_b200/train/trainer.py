@@ -197,6 +197,8 @@ def train_kimiK3(*, model, train_loader=None, train_loader_factory=None, val_loa
     qb_reducer = plan.qb_reducer() if plan is not None else None
     moe_ctl = MoEController(model, reducer=qb_reducer)
     collector = KimiDiagnosticCollector(model, diagnostics_config, parameter_specs=registry.specs)
+    if dcfg.enabled and ctx.initialized and ctx.world_size > 1:
+        collector.budget_device = ctx.device   # every rank degrades diagnostics on the same steps
     log_rank = dcfg.diagnostics.log_rank
     is_log = ctx.global_rank == log_rank
     printer = KimiTrainingPrinter() if verbose and is_log else None

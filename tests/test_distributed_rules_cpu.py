@@ -468,3 +468,30 @@ def test_data_parallel_trainer_with_curriculum_ema_and_accumulation_resumes(tmp_
     assert first[0][0] == again[0][0] > 0
     for k, v in first[0][1].items():
         torch.testing.assert_close(again[0][1][k], v, rtol=1e-5, atol=1e-6, msg=k)
+
+
+def _budget_rank(rank, world):
+    from test_distributed_cpu import _model
+    from kimi_k3_b200.parallel.environment import setup_distributed
+    from kimi_k3_b200.train.diagnostics import DiagnosticsConfig, KimiDiagnosticCollector
+    from kimi_k3_b200.train.loop import train_one_epoch
+    from kimi_k3_b200.train.optimizer import KimiOptimizerConfig, build_kimi_optimizer
+    ctx = setup_distributed(distributed_config_from_dict({"enabled": True, "backend": "gloo",
+                                                          "data_parallel": {"mode": "ddp", "size": world}}))
+    model = _model()
+    opt, registry = build_kimi_optimizer(model, KimiOptimizerConfig(kind="adamw"))
+    # only rank 0 has a budget it is sure to exceed
+    cfg = DiagnosticsConfig(standard_every_steps=1, deep_every_steps=4,
+                            max_diagnostic_time_fraction=1e-9 if rank == 0 else 1.0)
+    collector = KimiDiagnosticCollector(model, cfg, parameter_specs=registry.specs)
+    collector.budget_device = ctx.device
+    ids = torch.randint(5, 128, (2, 12), generator=torch.Generator().manual_seed(rank))
+    batch = {"input_ids": ids, "labels": ids.clone(), "attention_mask": torch.ones(2, 12, dtype=torch.bool)}
+    train_one_epoch(model, [batch], opt, use_mtp=True, diagnostics=collector, distributed_context=ctx)
+    ctx.close()
+    return collector.degrade_until_step, [collector.level_for_step(s) for s in range(2, 5)]
+
+
+def test_diagnostics_degrade_on_the_same_steps_on_every_rank():
+    a, b = run_ranks(_budget_rank, 2)
+    assert a == b and a[0] > 0 and a[1][0] == "cheap"
