@@ -495,3 +495,26 @@ def _budget_rank(rank, world):
 def test_diagnostics_degrade_on_the_same_steps_on_every_rank():
     a, b = run_ranks(_budget_rank, 2)
     assert a == b and a[0] > 0 and a[1][0] == "cheap"
+
+
+@pytest.mark.slow
+def test_tp_ep_overlay_trainer_with_bf16_accumulation_curriculum_and_all_diagnostics(tmp_path):
+    """The most composed layout (EP on the TP ranks) under bf16 autocast, two-micro-batch windows, a
+    two-stage context curriculum and every diagnostics tier trains through the YAML trainer."""
+    import yaml
+    from kimi_k3_b200.config.profiles import write_pipeline
+    d = write_pipeline("cpu_smoke", tmp_path / "prof")
+    tr = yaml.safe_load((d / "training.yaml").read_text())
+    tr["training"].update(epochs=1, max_batches_per_epoch=4, gradient_accumulation_steps=2, precision="bf16")
+    tr["runtime"]["verbose"] = False
+    tr["diagnostics"].update(standard_every_steps=1, deep_every_steps=2)
+    tr["context_curriculum"] = {"enabled": True, "stages": [{"max_seq_len": 16, "until_tokens": 200},
+                                                            {"max_seq_len": 32, "until_tokens": None}]}
+    tr["distributed"] = {"enabled": True, "backend": "gloo", "timeout_seconds": 120,
+                         **YAML_LAYOUTS["tp_ep_overlay"]}
+    (d / "training.yaml").write_text(yaml.safe_dump(tr))
+    res = run_ranks(_fsdp_trainer_rank, 2, str(tmp_path), False)
+    assert res[0][0] == res[1][0] == 2
+    for k, v in res[0][1].items():
+        assert torch.isfinite(v).all(), k
+        assert torch.equal(v, res[1][1][k]), k      # both ranks export the same full weights
